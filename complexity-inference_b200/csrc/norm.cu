@@ -1,0 +1,341 @@
+// Row-wise kernels on the f32 residual stream: embedding lookup, fused
+// partial-sum reduction + residual add + RMSNorm (+ mu_clamp at each of the
+// reference's clamp sites), final-norm row gather, and the INL dynamics step
+// of DeepForCausalLM with its post-attention norm and mu-guided routing.
+//
+// One CTA per token row; the row is staged in shared memory (hidden <= 16384)
+// so the norm needs a single HBM read of every input.  These kernels are
+// HBM-bound: per row they move (num_partials + 2)·4·H bytes in and 6·H out.
+#include <math.h>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace muk {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxHidden = 16384;
+
+struct ClampArgs {
+  float mu, cmin, cmax;
+};
+
+__host__ __device__ inline ClampParams make_clamp(int enabled, float mu, float cmin, float cmax) {
+  ClampParams p;
+  p.enabled = enabled;
+  p.mu = mu;
+  p.center = (cmax + cmin) * 0.5f;
+  p.range = (cmax - cmin) * 0.5f;
+  p.inv_range = p.range > 0.f ? 1.f / p.range : 0.f;
+  return p;
+}
+
+// Sum of `v` over the CTA; `red` is >= 32 floats of shared scratch.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (warp == 0) {
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                             int64_t table_stride, float* __restrict__ resid, int hidden, int vocab,
+                             ClampParams cp) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  float* out = resid + (int64_t)t * hidden;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_device_error(kDevBadIndex);
+    for (int j = threadIdx.x; j < hidden; j += blockDim.x) out[j] = 0.f;
+    return;
+  }
+  const __nv_bfloat16* row = table + (int64_t)id * table_stride;
+  for (int j = threadIdx.x * 2; j < hidden; j += blockDim.x * 2) {
+    float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row + j));
+    out[j] = mu_clamp(v.x, cp);
+    out[j + 1] = mu_clamp(v.y, cp);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const float* __restrict__ partials,
+                                        int64_t partial_stride, int64_t partial_row_stride,
+                                        int num_partials, const int32_t* __restrict__ delta_rows,
+                                        const float* __restrict__ norm_w, float eps,
+                                        __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                                        int hidden, int clamp_delta, int clamp_sum,
+                                        ClampParams cp_norm, ClampParams cp) {
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int src = delta_rows ? delta_rows[t] : t;
+  float* rrow = resid + (int64_t)t * hidden;
+  float ss = 0.f;
+  for (int j = threadIdx.x * 4; j < hidden; j += blockDim.x * 4) {
+    float4 r = *reinterpret_cast<const float4*>(rrow + j);
+    if (num_partials > 0) {
+      float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < num_partials; ++p) {
+        float4 x = *reinterpret_cast<const float4*>(partials + p * partial_stride +
+                                                    (int64_t)src * partial_row_stride + j);
+        d.x += x.x;
+        d.y += x.y;
+        d.z += x.z;
+        d.w += x.w;
+      }
+      if (clamp_delta) {
+        d.x = mu_clamp(d.x, cp);
+        d.y = mu_clamp(d.y, cp);
+        d.z = mu_clamp(d.z, cp);
+        d.w = mu_clamp(d.w, cp);
+      }
+      r.x += d.x;
+      r.y += d.y;
+      r.z += d.z;
+      r.w += d.w;
+      if (clamp_sum) {
+        r.x = mu_clamp(r.x, cp);
+        r.y = mu_clamp(r.y, cp);
+        r.z = mu_clamp(r.z, cp);
+        r.w = mu_clamp(r.w, cp);
+      }
+      *reinterpret_cast<float4*>(rrow + j) = r;
+    }
+    *reinterpret_cast<float4*>(srow + j) = r;
+    ss += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
+  }
+  if (out == nullptr) return;
+  const float total = block_sum(ss, red);
+  const float inv = rsqrtf(total / (float)hidden + eps);
+  __nv_bfloat16* orow = out + (int64_t)t * out_stride;
+  for (int j = threadIdx.x * 2; j < hidden; j += blockDim.x * 2) {
+    float a = mu_clamp(norm_w[j] * (srow[j] * inv), cp_norm);
+    float b = mu_clamp(norm_w[j + 1] * (srow[j + 1] * inv), cp_norm);
+    *reinterpret_cast<uint32_t*>(orow + j) = pack_bf16x2(a, b);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ resid, const int32_t* __restrict__ rows,
+                                    const float* __restrict__ norm_w, float eps,
+                                    __nv_bfloat16* __restrict__ out, int64_t out_stride, int hidden,
+                                    ClampParams cp) {
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  const float* rrow = resid + (int64_t)rows[i] * hidden;
+  float ss = 0.f;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) ss += rrow[j] * rrow[j];
+  const float inv = rsqrtf(block_sum(ss, red) / (float)hidden + eps);
+  __nv_bfloat16* orow = out + (int64_t)i * out_stride;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x)
+    orow[j] = f_to_bf16(mu_clamp(norm_w[j] * (rrow[j] * inv), cp));
+}
+
+// ---------------------------------------------------------------------------
+__global__ void reduce_clamp_kernel(const float* __restrict__ partials, int64_t partial_stride,
+                                    int num_partials, float* __restrict__ dst,
+                                    __nv_bfloat16* __restrict__ dst_bf16, int64_t dst_bf16_stride,
+                                    int hidden, int64_t total, ClampParams cp) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int p = 0; p < num_partials; ++p) s += partials[p * partial_stride + i];
+    s = mu_clamp(s, cp);
+    dst[i] = s;
+    if (dst_bf16) {
+      const int64_t t = i / hidden, j = i - t * hidden;
+      dst_bf16[t * dst_bf16_stride + j] = f_to_bf16(s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
+// torch.nn.functional.softplus with beta=1, threshold=20.
+__device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+constexpr int kMaxExperts = 16;
+
+__global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __restrict__ ctrl_raw,
+                                    const float* __restrict__ ctrl_bias,
+                                    const float* __restrict__ muproj,
+                                    const float* __restrict__ mu_param, float dt, float* __restrict__ v,
+                                    __nv_bfloat16* __restrict__ v_bf16, int64_t v_bf16_stride,
+                                    float* __restrict__ resid, __nv_bfloat16* __restrict__ mu_out,
+                                    int64_t mu_out_stride, const float* __restrict__ norm_w, float eps,
+                                    __nv_bfloat16* __restrict__ norm_out, int64_t norm_out_stride,
+                                    const int32_t* __restrict__ token_ids,
+                                    const __nv_bfloat16* __restrict__ router_w, int num_experts,
+                                    int vocab, int32_t* __restrict__ expert_ids, int hidden,
+                                    ClampParams cp_norm) {
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  __shared__ float dots[kMaxExperts];
+  const int t = blockIdx.x;
+  const int64_t base = (int64_t)t * hidden;
+  const float* crow = ctrl_raw + (int64_t)t * 3 * hidden;
+  float ss = 0.f;
+  float edot[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) edot[e] = 0.f;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
+    const float a = sigmoidf_(crow[j] + ctrl_bias[j]);
+    const float b = fminf(softplusf_(crow[hidden + j] + ctrl_bias[hidden + j]), 2.f);
+    const float g = sigmoidf_(crow[2 * hidden + j] + ctrl_bias[2 * hidden + j]);
+    const float mu_c = mu_param[j] + muproj[base + j];
+    const float hj = h[base + j];
+    float vn = a * v[base + j] - b * (hj - mu_c);
+    vn = fminf(fmaxf(vn, -10.f), 10.f);
+    const float hn = hj + dt * g * vn;
+    const float r = resid[base + j] + hn;
+    resid[base + j] = r;
+    v[base + j] = vn;
+    if (v_bf16) v_bf16[(int64_t)t * v_bf16_stride + j] = f_to_bf16(vn);
+    if (mu_out) mu_out[(int64_t)t * mu_out_stride + j] = f_to_bf16(mu_c);
+    srow[j] = r;
+    ss += r * r;
+    if (router_w) {
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e)
+        if (e < num_experts) edot[e] += mu_c * bf16_to_f(router_w[(int64_t)e * hidden + j]);
+    }
+  }
+  const float total = block_sum(ss, red);
+  if (router_w) {
+    for (int e = 0; e < num_experts; ++e) {
+      const float d = block_sum(edot[e], red);
+      if (threadIdx.x == 0) dots[e] = d;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int id = token_ids[t];
+      id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+      const int base_e = id % num_experts;
+      int best = 0;
+      float bestv = -INFINITY;
+      for (int e = 0; e < num_experts; ++e) {
+        const float s = (e == base_e ? 10.f : 0.f) + dots[e];
+        if (s > bestv) {
+          bestv = s;
+          best = e;
+        }
+      }
+      expert_ids[t] = best;
+    }
+  }
+  if (norm_out) {
+    const float inv = rsqrtf(total / (float)hidden + eps);
+    __nv_bfloat16* orow = norm_out + (int64_t)t * norm_out_stride;
+    for (int j = threadIdx.x; j < hidden; j += blockDim.x)
+      orow[j] = f_to_bf16(mu_clamp(norm_w[j] * (srow[j] * inv), cp_norm));
+  }
+}
+
+}  // namespace muk
+
+using namespace muk;
+
+extern "C" int muk_embed(const int32_t* ids, const void* table, int64_t table_stride, float* resid,
+                         int num_tokens, int hidden, int vocab, int clamp, float mu, float clamp_min,
+                         float clamp_max, void* stream) {
+  MUK_REQUIRE(num_tokens >= 0 && hidden > 0 && (hidden % 2) == 0 && vocab > 0,
+              "muk_embed: bad shape T=%d H=%d V=%d", num_tokens, hidden, vocab);
+  MUK_REQUIRE(ids && table && resid, "muk_embed: null pointer");
+  MUK_REQUIRE(table_stride >= hidden && (table_stride % 2) == 0, "muk_embed: bad table stride");
+  if (num_tokens == 0) return MUK_OK;
+  embed_kernel<<<num_tokens, kRowThreads, 0, as_stream(stream)>>>(
+      ids, reinterpret_cast<const __nv_bfloat16*>(table), table_stride, resid, hidden, vocab,
+      make_clamp(clamp, mu, clamp_min, clamp_max));
+  return check_launch("muk_embed");
+}
+
+extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t partial_stride,
+                                    int64_t partial_row_stride, int num_partials,
+                                    const int32_t* delta_rows, const float* norm_w, float eps,
+                                    void* out, int64_t out_stride, int num_tokens, int hidden,
+                                    int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                                    float clamp_min, float clamp_max, void* stream) {
+  MUK_REQUIRE(num_tokens >= 0 && hidden > 0 && hidden % 4 == 0 && hidden <= kMaxHidden,
+              "muk_residual_rmsnorm: hidden=%d must be a multiple of 4 and <= %d", hidden,
+              kMaxHidden);
+  MUK_REQUIRE(resid != nullptr && MUK_ALIGNED16(resid), "muk_residual_rmsnorm: resid");
+  MUK_REQUIRE(num_partials >= 0 && (num_partials == 0 || (partials && MUK_ALIGNED16(partials) &&
+                                                          partial_row_stride % 4 == 0 &&
+                                                          partial_stride % 4 == 0)),
+              "muk_residual_rmsnorm: partials must be 16-byte aligned rows");
+  MUK_REQUIRE(out == nullptr || (norm_w && out_stride >= hidden && out_stride % 2 == 0),
+              "muk_residual_rmsnorm: out needs norm_w and an even stride >= hidden");
+  if (num_tokens == 0) return MUK_OK;
+  ClampParams cp = make_clamp(1, mu, clamp_min, clamp_max);
+  residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), as_stream(stream)>>>(
+      resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps,
+      reinterpret_cast<__nv_bfloat16*>(out), out_stride, hidden, clamp_delta, clamp_sum,
+      make_clamp(clamp_norm, mu, clamp_min, clamp_max), cp);
+  return check_launch("muk_residual_rmsnorm");
+}
+
+extern "C" int muk_rmsnorm_rows(const float* resid, const int32_t* rows, int num_rows,
+                                const float* norm_w, float eps, void* out, int64_t out_stride,
+                                int hidden, int clamp, float mu, float clamp_min, float clamp_max,
+                                void* stream) {
+  MUK_REQUIRE(resid && rows && norm_w && out && hidden > 0 && out_stride >= hidden,
+              "muk_rmsnorm_rows: bad arguments");
+  if (num_rows <= 0) return MUK_OK;
+  rmsnorm_rows_kernel<<<num_rows, kRowThreads, 0, as_stream(stream)>>>(
+      resid, rows, norm_w, eps, reinterpret_cast<__nv_bfloat16*>(out), out_stride, hidden,
+      make_clamp(clamp, mu, clamp_min, clamp_max));
+  return check_launch("muk_rmsnorm_rows");
+}
+
+extern "C" int muk_reduce_clamp(const float* partials, int64_t partial_stride, int num_partials,
+                                float* dst_f32, void* dst_bf16, int64_t dst_bf16_stride,
+                                int num_tokens, int hidden, int clamp, float mu, float clamp_min,
+                                float clamp_max, void* stream) {
+  MUK_REQUIRE(partials && dst_f32 && num_partials >= 1 && hidden > 0,
+              "muk_reduce_clamp: bad arguments");
+  MUK_REQUIRE(dst_bf16 == nullptr || dst_bf16_stride >= hidden, "muk_reduce_clamp: bad stride");
+  const int64_t total = (int64_t)num_tokens * hidden;
+  if (total == 0) return MUK_OK;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  reduce_clamp_kernel<<<blocks, 256, 0, as_stream(stream)>>>(
+      partials, partial_stride, num_partials, dst_f32, reinterpret_cast<__nv_bfloat16*>(dst_bf16),
+      dst_bf16_stride, hidden, total, make_clamp(clamp, mu, clamp_min, clamp_max));
+  return check_launch("muk_reduce_clamp");
+}
+
+extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bias,
+                                const float* muproj, const float* mu_param, float dt, float* v,
+                                void* v_bf16, int64_t v_bf16_stride, float* resid, void* mu_out,
+                                int64_t mu_out_stride, const float* norm_w, float eps,
+                                void* norm_out, int64_t norm_out_stride, const int32_t* token_ids,
+                                const void* router_w, int num_experts, int vocab,
+                                int32_t* expert_ids, int num_tokens, int hidden, int clamp_norm,
+                                float mu, float clamp_min, float clamp_max, void* stream) {
+  MUK_REQUIRE(h && ctrl_raw && ctrl_bias && muproj && mu_param && v && resid,
+              "muk_inl_dynamics: null pointer");
+  MUK_REQUIRE(hidden > 0 && hidden <= kMaxHidden, "muk_inl_dynamics: hidden=%d", hidden);
+  MUK_REQUIRE(norm_out == nullptr || norm_w, "muk_inl_dynamics: norm_out needs norm_w");
+  MUK_REQUIRE(router_w == nullptr ||
+                  (token_ids && expert_ids && num_experts >= 1 && num_experts <= kMaxExperts &&
+                   vocab > 0),
+              "muk_inl_dynamics: routing needs token_ids, expert_ids and 1..%d experts",
+              kMaxExperts);
+  if (num_tokens == 0) return MUK_OK;
+  inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), as_stream(stream)>>>(
+      h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, reinterpret_cast<__nv_bfloat16*>(v_bf16),
+      v_bf16_stride, resid, reinterpret_cast<__nv_bfloat16*>(mu_out), mu_out_stride, norm_w, eps,
+      reinterpret_cast<__nv_bfloat16*>(norm_out), norm_out_stride, token_ids,
+      reinterpret_cast<const __nv_bfloat16*>(router_w), num_experts, vocab, expert_ids, hidden,
+      make_clamp(clamp_norm, mu, clamp_min, clamp_max));
+  return check_launch("muk_inl_dynamics");
+}

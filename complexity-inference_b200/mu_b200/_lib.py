@@ -1,0 +1,116 @@
+"""ctypes binding of libmuk.so (declared in include/muk.h).
+
+The library is loaded from this package directory.  There is no fallback:
+if the shared object is missing or does not load, every kernel entry point
+raises, so a GPU run can never silently fall back to another code path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libmuk.so")
+
+MUK_OK = 0
+MUK_ERR_INVALID_ARG = -1
+MUK_ERR_UNSUPPORTED = -2
+MUK_ERR_WORKSPACE = -3
+MUK_ERR_CUDA = -4
+MUK_ERR_DEVICE = -5
+
+MUK_EPI_BF16 = 0
+MUK_EPI_F32 = 1
+MUK_EPI_SWIGLU = 2
+MUK_EPI_BIAS_SILU = 3
+
+_P = c_void_p
+_I32P = c_void_p  # device pointers are passed as integers
+
+# name -> (restype, argtypes); mirrors include/muk.h
+SIGNATURES = {
+    "muk_version": (c_int, []),
+    "muk_last_error": (c_char_p, []),
+    "muk_device_error": (c_int, [POINTER(c_int)]),
+    "muk_embed": (c_int, [_P, _P, c_int64, _P, c_int, c_int, c_int, c_int, c_float, c_float,
+                          c_float, _P]),
+    "muk_residual_rmsnorm": (c_int, [_P, _P, c_int64, c_int64, c_int, _P, _P, c_float, _P,
+                                     c_int64, c_int, c_int, c_int, c_int, c_int, c_float,
+                                     c_float, c_float, _P]),
+    "muk_rmsnorm_rows": (c_int, [_P, _P, c_int, _P, c_float, _P, c_int64, c_int, c_int, c_float,
+                                 c_float, c_float, _P]),
+    "muk_rope_kv_append": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
+                                   _P, _P, c_float, _P, _P, c_int, c_int, _P]),
+    "muk_decode_attn_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "muk_paged_decode_attn": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P, c_int,
+                                      c_int, c_int, c_int, c_int, c_int, c_float, c_int, _P,
+                                      c_size_t, _P]),
+    "muk_paged_prefill_attn": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P, _P, c_int,
+                                       c_int, c_int, c_int, c_int, c_int, c_int, c_float, _P]),
+    "muk_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, c_int, c_int,
+                              c_int, _P, _P]),
+    "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
+    "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
+    "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
+                                      c_int, c_int, c_int, _P]),
+    "muk_inl_dynamics": (c_int, [_P, _P, _P, _P, _P, c_float, _P, _P, c_int64, _P, _P, c_int64,
+                                 _P, c_float, _P, c_int64, _P, _P, c_int, c_int, _P, c_int, c_int,
+                                 c_int, c_float, c_float, c_float, _P]),
+    "muk_reduce_clamp": (c_int, [_P, c_int64, c_int, _P, _P, c_int64, c_int, c_int, c_int,
+                                 c_float, c_float, c_float, _P]),
+    "muk_sample": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P, _P, _P,
+                           _P]),
+    "muk_mark_seen": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+class MukError(RuntimeError):
+    """A libmuk entry point returned a non-zero status."""
+
+    def __init__(self, name: str, code: int, message: str):
+        super().__init__(f"{name} failed ({code}): {message}")
+        self.code = code
+
+
+def load() -> ctypes.CDLL:
+    """Load libmuk.so once and bind every signature; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise MukError("load", MUK_ERR_UNSUPPORTED,
+                       f"{LIB_PATH} is missing: build it with complexity-inference_b200/build.py")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().muk_last_error()
+    return msg.decode() if msg else ""
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise MukError on failure."""
+    fn = getattr(load(), name)
+    rc = fn(*args)
+    if rc != MUK_OK:
+        raise MukError(name, rc, last_error())
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (synchronises the device)."""
+    code = c_int(0)
+    call("muk_device_error", ctypes.byref(code))
+    return code.value
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)

@@ -1,0 +1,233 @@
+/*
+ * muk.h — C ABI of libmuk.so, the sm_100a kernels behind mu_b200.
+ *
+ * Plain pointers and sizes only: every device buffer is allocated by the
+ * caller (PyTorch on the Python side) and passed as a raw device pointer.
+ * Streams are passed as `void*` holding a cudaStream_t.  Except for
+ * muk_last_error/muk_version, every entry point returns MUK_OK (0) or a
+ * negative MUK_ERR_* code; the message of the last failure on the calling
+ * thread is available from muk_last_error().  No entry point allocates or
+ * frees device memory: kernels that need scratch take a caller-provided
+ * workspace whose size comes from the matching *_workspace_size query.
+ *
+ * Each entry point replaces one piece of the reference's PyTorch forward
+ * step (Complexity-ML/complexity-inference, package mu_inference); the
+ * citation on each declaration names the reference code it stands in for.
+ *
+ * Conventions
+ *   bf16      = IEEE bfloat16 stored as uint16
+ *   KV cache  = per layer two arrays [num_blocks][num_kv_heads][block_size][head_dim]
+ *               (K and V), bf16.  Token slot s lives in block s / block_size
+ *               at offset s % block_size.
+ *   positions = absolute token positions (the reference takes them from the
+ *               past-KV length, mu_inference/models/layers.py:682-694).
+ */
+#ifndef MUK_H_
+#define MUK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define MUK_OK 0
+#define MUK_ERR_INVALID_ARG -1   /* a shape, stride, pointer or flag outside the contract */
+#define MUK_ERR_UNSUPPORTED -2   /* legal request this build does not implement         */
+#define MUK_ERR_WORKSPACE -3     /* workspace missing or smaller than the size query    */
+#define MUK_ERR_CUDA -4          /* a CUDA runtime/driver call failed                   */
+#define MUK_ERR_DEVICE -5        /* a kernel reported a device-side error (time-out, bad index) */
+
+/* ---- GEMM epilogues ------------------------------------------------------ */
+#define MUK_EPI_BF16 0        /* C = bf16(A·Bᵀ)                                           */
+#define MUK_EPI_F32 1         /* C = f32(A·Bᵀ); with split_k > 1, C is [split_k][M][ldc]  */
+#define MUK_EPI_SWIGLU 2      /* B rows interleaved in 64-row gate/up groups; C[:, j] =
+                                 bf16(silu(g_j)·u_j), N/2 output columns                   */
+#define MUK_EPI_BIAS_SILU 3   /* C = bf16(silu(A·Bᵀ + bias))                               */
+
+/* ---- housekeeping -------------------------------------------------------- */
+int muk_version(void);
+const char* muk_last_error(void);
+/* Reads and clears the device-side error word of the current device.
+ * *code receives 0 (none) or a kernel error code (1-3 time-out, 4 shape,
+ * 5 index).  Synchronises the device. */
+int muk_device_error(int* code);
+
+/* ---- K6: embedding, RMSNorm, residual reduction -------------------------- */
+
+/* resid[t,:] = mu_clamp?(table[ids[t],:])  (f32 out, bf16 table).
+ * Replaces embed_tokens + mu_clamp, mu_inference/models/llama.py:196-205,
+ * mu_inference/models/deep.py:256-265.  Token ids outside [0, vocab) are an
+ * error (recorded on the device, row written as zeros). */
+int muk_embed(const int32_t* ids, const void* table, int64_t table_stride, float* resid,
+              int num_tokens, int hidden, int vocab, int clamp, float mu, float clamp_min,
+              float clamp_max, void* stream);
+
+/* One fused row pass over the f32 residual stream:
+ *   d      = Σ_{p<num_partials} partials[p][src_row(t)][:]      (src_row = delta_rows ? delta_rows[t] : t)
+ *   d      = clamp_delta ? mu_clamp(d) : d
+ *   r      = resid[t] + d ;  r = clamp_sum ? mu_clamp(r) : r ;  resid[t] = r
+ *   out[t] = bf16( mu_clamp?( norm_w * r * rsqrt(mean(r²) + eps) ) )   (if out != NULL)
+ * num_partials may be 0 (pure RMSNorm).  Replaces the residual adds and
+ * MuRMSNorm.forward of mu_inference/models/layers.py:149-164 plus the
+ * mu_clamp sites at mu_inference/models/layers.py:416-422 / 733-739 and
+ * mu_inference/models/llama.py:111-126 (MuAttention/MuMLP outputs and the
+ * layer output). */
+int muk_residual_rmsnorm(float* resid, const float* partials, int64_t partial_stride,
+                         int64_t partial_row_stride, int num_partials, const int32_t* delta_rows,
+                         const float* norm_w, float eps, void* out, int64_t out_stride,
+                         int num_tokens, int hidden, int clamp_delta, int clamp_sum,
+                         int clamp_norm, float mu, float clamp_min, float clamp_max,
+                         void* stream);
+
+/* out[i,:] = bf16(mu_clamp?(RMSNorm(resid[rows[i],:]))) — the final norm on the
+ * last token of each sequence before the LM head
+ * (mu_inference/models/llama.py:233-237, mu_inference/models/deep.py:318-322). */
+int muk_rmsnorm_rows(const float* resid, const int32_t* rows, int num_rows, const float* norm_w,
+                     float eps, void* out, int64_t out_stride, int hidden, int clamp, float mu,
+                     float clamp_min, float clamp_max, void* stream);
+
+/* ---- K1: RoPE (+ optional QK-norm) and paged-KV append -------------------- */
+
+/* qkv is [num_tokens][qkv_stride] bf16 holding q | k | v heads.  For every
+ * token: optional per-head RMSNorm of q and k (q_norm_w/k_norm_w, NULL = off),
+ * rotate-half RoPE of q (in place) and k using the f32 tables
+ * rope_cos/rope_sin [max_pos][head_dim/2], then scatter k and v into the
+ * paged cache at slot_mapping[t] (slots < 0 are skipped).
+ * Replaces mu_inference/models/layers.py:671-702 (reshape, QK-norm, RoPE,
+ * torch.cat of past KV) and MuPagedCache.append,
+ * mu_inference/core/cache.py:322-375. */
+int muk_rope_kv_append(void* qkv, int64_t qkv_stride, const int32_t* positions,
+                       const int32_t* slot_mapping, const float* rope_cos, const float* rope_sin,
+                       int max_pos, int num_tokens, int num_q_heads, int num_kv_heads,
+                       int head_dim, const float* q_norm_w, const float* k_norm_w, float qk_eps,
+                       void* k_cache, void* v_cache, int num_blocks, int block_size,
+                       void* stream);
+
+/* ---- K2a: paged-attention decode (one query token per sequence) ---------- */
+
+/* Scratch bytes muk_paged_decode_attn needs for this shape (0 if none). */
+size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, int head_dim,
+                                      int max_seq_len, int block_size);
+
+/* out[b, h, :] = softmax(q·Kᵀ·scale)·V over the sequence's first seq_lens[b]
+ * cached tokens (GQA: q head h reads kv head h / (Hq/Hkv)).  Split-K over
+ * blocks with a merge pass.  Replaces the decode branch of MuAttention
+ * (torch.cat + repeat_interleave + SDPA, is_causal=False),
+ * mu_inference/models/layers.py:700-723. */
+int muk_paged_decode_attn(const void* q, int64_t q_stride, void* out, int64_t out_stride,
+                          const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                          int block_table_stride, const int32_t* seq_lens, int num_seqs,
+                          int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                          int num_blocks, float scale, int max_seq_len, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ---- K2b: varlen causal prefill over the paged cache --------------------- */
+
+/* Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of q/out.
+ * Its context is seq_lens[b] cached tokens whose last q_len are the new ones;
+ * query i sits at absolute position seq_lens[b] - q_len + i and attends keys
+ * 0..that position.  Replaces the prefill branch of MuAttention
+ * (SDPA is_causal=True when q_len == k_len), mu_inference/models/layers.py:707-723. */
+int muk_paged_prefill_attn(const void* q, int64_t q_stride, void* out, int64_t out_stride,
+                           const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                           int block_table_stride, const int32_t* seq_lens,
+                           const int32_t* cu_seqlens_q, int num_seqs, int max_q_len,
+                           int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                           int num_blocks, float scale, void* stream);
+
+/* ---- K3: dense GEMM on tcgen05 / TMEM ------------------------------------ */
+
+/* C[M,N] = epilogue(A[M,K] · B[N,K]ᵀ); A and B are bf16, K-major (row-major
+ * with leading dimensions lda/ldb in elements, multiples of 8, 16-byte
+ * aligned bases).  split_k > 1 requires MUK_EPI_F32 and writes split_k
+ * partial products [split_k][M][ldc].  bias (f32 [N]) is used by
+ * MUK_EPI_BIAS_SILU only.  Replaces nn.Linear / torch.bmm on the forward
+ * step: q/k/v/o and mu_to_* projections (mu_inference/models/layers.py:661-669,
+ * 730), MuMLP (layers.py:410-424), the INL controller and mu_proj
+ * (layers.py:103-116) and the LM head (mu_inference/models/llama.py:237). */
+int muk_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                  int M, int N, int K, int epilogue, int split_k, const float* bias,
+                  void* stream);
+
+/* ---- K4: token-routed experts -------------------------------------------- */
+
+/* Stable counting sort of tokens by expert id.  expert_offsets[E+1] (prefix
+ * of per-expert counts), perm[i] = token at expert-sorted position i,
+ * inv_perm[t] = sorted position of token t.  Replaces the per-token weight
+ * gather of MuTokenRoutedMLP, mu_inference/models/layers.py:530-536. */
+int muk_route_permute(const int32_t* expert_ids, int num_tokens, int num_experts,
+                      int32_t* expert_offsets, int32_t* perm, int32_t* inv_perm, void* stream);
+
+/* dst[i,:] = src[rows[i],:] for bf16 rows of `width` elements. */
+int muk_gather_rows_bf16(const void* src, int64_t src_stride, const int32_t* rows, int num_rows,
+                         void* dst, int64_t dst_stride, int width, void* stream);
+
+/* Grouped GEMM: rows [expert_offsets[e], expert_offsets[e+1]) of A are
+ * multiplied by expert e's weight, rows [e*N, (e+1)*N) of B ([E*N][K],
+ * K-major).  epilogue is MUK_EPI_SWIGLU (C has N/2 columns), MUK_EPI_BF16 or
+ * MUK_EPI_F32.  max_rows bounds expert_offsets[E] (grid sizing).  Replaces
+ * the torch.bmm pair of MuTokenRoutedMLP, mu_inference/models/layers.py:538-547. */
+int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
+                          int64_t ldc, const int32_t* expert_offsets, int num_experts,
+                          int max_rows, int N, int K, int epilogue, void* stream);
+
+/* ---- K5: INL dynamics, post-attention norm and mu-guided routing --------- */
+
+/* Per token t (row-wise, all f32 unless noted):
+ *   ctrl = ctrl_raw[t] + ctrl_bias                    (3H: alpha | beta | gate)
+ *   mu_c = mu_param + muproj[t]
+ *   v'   = clamp(sigmoid(a)·v[t] − min(softplus(b),2)·(h[t] − mu_c), −10, 10)
+ *   h'   = h[t] + dt·sigmoid(g)·v'
+ *   resid[t] += h' ;  v[t] = v'
+ *   v_bf16[t] = bf16(v')            (A-operand copy for the next controller GEMM)
+ *   mu_out[t] = bf16(mu_c)          (A-operand copy for the next layer's mu_to_q/k/v)
+ *   norm_out[t] = bf16(mu_clamp?(RMSNorm(resid[t])·norm_w))
+ *   expert_ids[t] = argmax_e(10·[e == ids[t] mod E] + mu_c·router_w[e])  (if router_w)
+ * h is the clamped attention output (f32).  Replaces INLDynamics.forward
+ * (mu_inference/models/layers.py:81-127), the residual add and
+ * post_attention_layernorm of DeepDecoderLayer (mu_inference/models/deep.py:152-158)
+ * and the routing of MuTokenRoutedMLP (layers.py:510-528). */
+int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bias,
+                     const float* muproj, const float* mu_param, float dt, float* v,
+                     void* v_bf16, int64_t v_bf16_stride, float* resid, void* mu_out,
+                     int64_t mu_out_stride, const float* norm_w, float eps, void* norm_out,
+                     int64_t norm_out_stride, const int32_t* token_ids, const void* router_w,
+                     int num_experts, int vocab, int32_t* expert_ids, int num_tokens, int hidden,
+                     int clamp_norm, float mu, float clamp_min, float clamp_max, void* stream);
+
+/* f32 row pass used around the INL GEMMs: dst_f32[t] = mu_clamp?(Σ_p partials[p][t]),
+ * dst_bf16[t] = bf16(dst_f32[t]). */
+int muk_reduce_clamp(const float* partials, int64_t partial_stride, int num_partials,
+                     float* dst_f32, void* dst_bf16, int64_t dst_bf16_stride, int num_tokens,
+                     int hidden, int clamp, float mu, float clamp_min, float clamp_max,
+                     void* stream);
+
+/* ---- K7: batched sampler ------------------------------------------------- */
+
+/* One token per row of logits [B][ld] (f32).  Per row b: repetition penalty
+ * over the tokens set in seen_bits[b] (bitmap of prompt + generated ids,
+ * divide if > 0 else multiply), temperature (0 => argmax), top-k (ties at the
+ * k-th value kept), top-p (smallest descending prefix whose mass exceeds
+ * top_p), then an exact categorical draw (Gumbel-max on counter-based
+ * Philox4x32-10 noise keyed by seeds[b] and offsets[b]).  Replaces
+ * prepare_logits + sample_token, mu_inference/utils/sampling.py:20-120.
+ * tokens_out[b] receives the id; probs are not materialised. */
+int muk_sample(const float* logits, int64_t ld, int num_rows, int vocab,
+               const float* temperature, const int32_t* top_k, const float* top_p,
+               const float* rep_penalty, const uint32_t* seen_bits, int64_t seen_stride,
+               const uint64_t* seeds, const uint64_t* offsets, int32_t* tokens_out,
+               void* stream);
+
+/* Sets bit tokens[b] in seen_bits[rows[b]] for b < n (keeps the repetition
+ * bitmaps current after each step without a host round trip). */
+int muk_mark_seen(uint32_t* seen_bits, int64_t seen_stride, const int32_t* rows,
+                  const int32_t* tokens, int n, int vocab, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUK_H_ */
