@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kSampThreads)
                   const float* __restrict__ temperature, const int32_t* __restrict__ top_k,
                   const float* __restrict__ top_p, const float* __restrict__ rep_penalty,
                   const uint32_t* __restrict__ seen_bits, int64_t seen_stride,
-                  const uint64_t* __restrict__ seeds, const uint64_t* __restrict__ offsets,
+                  const int32_t* __restrict__ seen_rows, const uint64_t* __restrict__ seeds, const uint64_t* __restrict__ offsets,
                   int32_t* __restrict__ out) {
   __shared__ float redv[32];
   __shared__ int redi[32];
@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(kSampThreads)
   RowParams p;
   p.x = logits + (int64_t)row * ld;
   p.rp = rep_penalty ? rep_penalty[row] : 1.f;
-  p.seen = (seen_bits != nullptr && p.rp != 1.f) ? seen_bits + (int64_t)row * seen_stride : nullptr;
+  const int srow = seen_rows ? seen_rows[row] : row;
+  p.seen = (seen_bits != nullptr && p.rp != 1.f) ? seen_bits + (int64_t)srow * seen_stride : nullptr;
   p.temp = temperature ? temperature[row] : 1.f;
   const int tid = threadIdx.x;
 
@@ -363,13 +364,13 @@ using namespace muk;
 extern "C" int muk_sample(const float* logits, int64_t ld, int num_rows, int vocab,
                           const float* temperature, const int32_t* top_k, const float* top_p,
                           const float* rep_penalty, const uint32_t* seen_bits, int64_t seen_stride,
-                          const uint64_t* seeds, const uint64_t* offsets, int32_t* tokens_out,
-                          void* stream) {
+                          const int32_t* seen_rows, const uint64_t* seeds, const uint64_t* offsets,
+                          int32_t* tokens_out, void* stream) {
   MUK_REQUIRE(logits && tokens_out && vocab > 0 && ld >= vocab, "muk_sample: bad arguments");
   MUK_REQUIRE(seen_bits == nullptr || seen_stride * 32 >= vocab, "muk_sample: seen_stride");
   if (num_rows <= 0) return MUK_OK;
   sample_kernel<<<num_rows, kSampThreads, 0, as_stream(stream)>>>(
-      logits, ld, vocab, temperature, top_k, top_p, rep_penalty, seen_bits, seen_stride, seeds,
-      offsets, tokens_out);
+      logits, ld, vocab, temperature, top_k, top_p, rep_penalty, seen_bits, seen_stride, seen_rows,
+      seeds, offsets, tokens_out);
   return check_launch("muk_sample");
 }

@@ -60,7 +60,7 @@ SIGNATURES = {
     "muk_reduce_clamp": (c_int, [_P, c_int64, c_int, _P, _P, c_int64, c_int, c_int, c_int,
                                  c_float, c_float, c_float, _P]),
     "muk_sample": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P, _P, _P,
-                           _P]),
+                           _P, _P]),
     "muk_mark_seen": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P]),
 }
 

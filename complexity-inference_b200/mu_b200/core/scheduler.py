@@ -1,0 +1,226 @@
+"""Request scheduler with the MuScheduler interface (mu_inference/core/scheduler.py).
+
+Same request lifecycle, policies, token budgets and preemption bookkeeping
+as the reference (scheduler.py:135-379): running DECODE requests first, then
+new requests from the waiting queue (FCFS, or a heap for "priority") while
+the batch and prefill token budgets allow, preemption of the most advanced
+decodes when over budget.  The engine turns each SchedulerOutput into one
+flat GPU step (decode requests first, then prefills) — see
+``mu_b200.serving.step``.
+"""
+
+from __future__ import annotations
+
+import heapq
+import time
+import uuid
+from collections import deque
+from dataclasses import dataclass, field
+from enum import Enum
+from typing import Callable, Deque, Dict, List, Optional
+
+from .config import SamplingParams, SchedulerConfig
+from .mu import MuDynamics, soft_clamp
+
+
+class RequestStatus(str, Enum):
+    PENDING = "pending"
+    PREFILL = "prefill"
+    DECODE = "decode"
+    PREEMPTED = "preempted"
+    FINISHED = "finished"
+    FAILED = "failed"
+
+
+@dataclass
+class Request:
+    request_id: str = field(default_factory=lambda: uuid.uuid4().hex[:16])
+    prompt: str = ""
+    prompt_token_ids: List[int] = field(default_factory=list)
+    output_token_ids: List[int] = field(default_factory=list)
+    output_text: str = ""
+    sampling_params: SamplingParams = field(default_factory=SamplingParams)
+    status: RequestStatus = RequestStatus.PENDING
+    arrival_time: float = field(default_factory=time.time)
+    start_time: Optional[float] = None
+    finish_time: Optional[float] = None
+    priority: float = 0.0
+    num_prompt_tokens: int = 0
+    num_generated_tokens: int = 0
+    max_tokens: int = 512
+    num_preemptions: int = 0
+    on_token: Optional[Callable[[int, str], None]] = None
+    on_finish: Optional[Callable[["Request"], None]] = None
+
+    def __lt__(self, other: "Request") -> bool:
+        return self.priority < other.priority
+
+    @property
+    def is_finished(self) -> bool:
+        return self.status in (RequestStatus.FINISHED, RequestStatus.FAILED)
+
+    @property
+    def total_tokens(self) -> int:
+        return self.num_prompt_tokens + self.num_generated_tokens
+
+    @property
+    def latency(self) -> Optional[float]:
+        if self.finish_time and self.start_time:
+            return self.finish_time - self.start_time
+        return None
+
+    @property
+    def tokens_per_second(self) -> Optional[float]:
+        lat = self.latency
+        return self.num_generated_tokens / lat if lat and lat > 0 else None
+
+
+@dataclass
+class SchedulerOutput:
+    prefill_requests: List[Request] = field(default_factory=list)
+    decode_requests: List[Request] = field(default_factory=list)
+    preempted_requests: List[Request] = field(default_factory=list)
+    num_prefill_tokens: int = 0
+    num_decode_tokens: int = 0
+
+    @property
+    def total_tokens(self) -> int:
+        return self.num_prefill_tokens + self.num_decode_tokens
+
+    @property
+    def is_empty(self) -> bool:
+        return not self.prefill_requests and not self.decode_requests
+
+
+class MuScheduler:
+    def __init__(self, config: SchedulerConfig):
+        self.config = config
+        self.waiting: Deque[Request] = deque()
+        self.running: Dict[str, Request] = {}
+        self.finished: Dict[str, Request] = {}
+        self.priority_queue: List[Request] = []
+        self.priority_dynamics = MuDynamics(mu=0.0, clamp_min=-10.0, clamp_max=10.0, ema_alpha=0.3)
+        self.batch_dynamics = MuDynamics(mu=config.max_batch_size / 2, clamp_min=1,
+                                         clamp_max=config.max_batch_size, ema_alpha=0.2)
+        self._num_processed = 0
+        self._total_tokens = 0
+
+    def add_request(self, request: Request) -> str:
+        request.status = RequestStatus.PENDING
+        request.arrival_time = time.time()
+        if self.config.policy == "priority":
+            request.priority = self.priority_dynamics.update(request.priority)
+            heapq.heappush(self.priority_queue, request)
+        else:
+            self.waiting.append(request)
+        return request.request_id
+
+    def schedule(self) -> SchedulerOutput:
+        out = SchedulerOutput()
+        decode_budget = self.config.max_num_batched_tokens
+        for req in list(self.running.values()):
+            if req.status == RequestStatus.DECODE:
+                out.decode_requests.append(req)
+                out.num_decode_tokens += 1
+                decode_budget -= 1
+        slots = self.config.max_batch_size - len(out.decode_requests)
+        prefill_budget = min(self.config.max_prefill_tokens, decode_budget)
+        for req in self._get_next_requests(slots):
+            need = req.num_prompt_tokens
+            if self.config.enable_chunked_prefill:
+                need = min(need, prefill_budget)
+            if need <= prefill_budget:
+                req.status = RequestStatus.PREFILL
+                req.start_time = time.time()
+                self.running[req.request_id] = req
+                out.prefill_requests.append(req)
+                out.num_prefill_tokens += need
+                prefill_budget -= need
+        if self._should_preempt(out):
+            out.preempted_requests = self._preempt_requests(out)
+        return out
+
+    def _get_next_requests(self, max_count: int) -> List[Request]:
+        got: List[Request] = []
+        if self.config.policy == "priority":
+            while self.priority_queue and len(got) < max_count:
+                got.append(heapq.heappop(self.priority_queue))
+        else:  # fcfs; "fair" is FCFS in the reference too
+            while self.waiting and len(got) < max_count:
+                got.append(self.waiting.popleft())
+        return got
+
+    def _should_preempt(self, out: SchedulerOutput) -> bool:
+        return self.config.enable_preemption and out.total_tokens > self.config.max_num_batched_tokens
+
+    def _preempt_requests(self, out: SchedulerOutput) -> List[Request]:
+        preempted: List[Request] = []
+        cands = sorted(out.decode_requests, key=lambda r: r.num_generated_tokens, reverse=True)
+        to_free = out.total_tokens - self.config.max_num_batched_tokens
+        for req in cands:
+            if to_free <= 0:
+                break
+            req.status = RequestStatus.PREEMPTED
+            req.num_preemptions += 1
+            out.decode_requests.remove(req)
+            if self.config.policy == "priority":
+                req.priority = soft_clamp(req.priority - 1.0, -10.0, 10.0)
+                heapq.heappush(self.priority_queue, req)
+            else:
+                self.waiting.appendleft(req)
+            preempted.append(req)
+            to_free -= 1
+        return preempted
+
+    def finish_request(self, request_id: str, success: bool = True) -> None:
+        req = self.running.pop(request_id, None)
+        if req:
+            req.status = RequestStatus.FINISHED if success else RequestStatus.FAILED
+            req.finish_time = time.time()
+            self.finished[request_id] = req
+            self._num_processed += 1
+            self._total_tokens += req.total_tokens
+            if req.on_finish:
+                req.on_finish(req)
+
+    def update_request(self, request_id: str, token_id: int, token_text: str = "") -> None:
+        req = self.running.get(request_id)
+        if req:
+            req.output_token_ids.append(token_id)
+            req.output_text += token_text
+            req.num_generated_tokens += 1
+            req.status = RequestStatus.DECODE
+            if req.on_token:
+                req.on_token(token_id, token_text)
+
+    def get_request(self, request_id: str) -> Optional[Request]:
+        return self.running.get(request_id) or self.finished.get(request_id)
+
+    def abort_request(self, request_id: str) -> None:
+        if request_id in self.running:
+            req = self.running.pop(request_id)
+            req.status = RequestStatus.FAILED
+            self.finished[request_id] = req
+            return
+        self.waiting = deque(r for r in self.waiting if r.request_id != request_id)
+        self.priority_queue = [r for r in self.priority_queue if r.request_id != request_id]
+        heapq.heapify(self.priority_queue)
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.priority_queue or self.running)
+
+    def get_stats(self) -> dict:
+        return {
+            "waiting": len(self.waiting) + len(self.priority_queue),
+            "running": len(self.running),
+            "finished": len(self.finished),
+            "total_processed": self._num_processed,
+            "total_tokens": self._total_tokens,
+            "policy": self.config.policy,
+            "batch_dynamics": self.batch_dynamics.get_stats(),
+        }
+
+    def clear_finished(self, max_age: float = 300.0) -> None:
+        cutoff = time.time() - max_age
+        self.finished = {k: v for k, v in self.finished.items()
+                         if v.finish_time and v.finish_time > cutoff}

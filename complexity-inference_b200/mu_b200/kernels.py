@@ -230,13 +230,15 @@ def inl_dynamics(h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_bf16, resid,
 
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
            top_p: torch.Tensor, rep_penalty: torch.Tensor, seen_bits: torch.Tensor | None,
-           seeds: torch.Tensor, offsets: torch.Tensor, out: torch.Tensor, num_rows: int | None = None):
+           seeds: torch.Tensor, offsets: torch.Tensor, out: torch.Tensor, num_rows: int | None = None,
+           seen_rows: torch.Tensor | None = None):
+    """One token per logits row; bitmap row of row b is seen_bits[seen_rows[b]] (or b)."""
     _check(logits, torch.float32, "logits")
     B = logits.shape[0] if num_rows is None else num_rows
     V = logits.shape[1]
     call("muk_sample", _p(logits), _row_stride(logits, "logits"), B, V, _p(temperature), _p(top_k),
          _p(top_p), _p(rep_penalty), _p(seen_bits), 0 if seen_bits is None else seen_bits.stride(0),
-         _p(seeds), _p(offsets), _p(out), _stream())
+         _p(seen_rows), _p(seeds), _p(offsets), _p(out), _stream())
 
 
 def mark_seen(seen_bits: torch.Tensor, rows: torch.Tensor, tokens: torch.Tensor, vocab: int,

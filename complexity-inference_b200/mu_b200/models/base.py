@@ -1,0 +1,201 @@
+"""Model base: the flat-batch forward step shared by the Llama and Deep models.
+
+The reference runs one ``model.forward(input_ids[1, S], past_key_values)``
+per request (mu_inference/models/base.py:107-129, serving/worker.py:249-331).
+Here a whole continuous-batching step runs as one pass over a flat token
+stream ``[T, H]`` (decode tokens first, then prefill tokens) with the KV
+cache in the paged pool; :meth:`MuModelBase.forward_step` returns the f32
+logits of each sequence's last token, ``[B, vocab]``.
+
+Numerics: weights and GEMM operands are bf16 with f32 accumulation; the
+residual stream, norms and INL dynamics stay f32; RoPE uses the f32 cos/sin
+table built exactly as RotaryEmbeddingCompat builds it (layers.py:286-299).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import kernels as K
+from ..core.config import ModelConfig, MuConfig
+from ..kernels import Clamp
+
+PAD_MULT = 64  # SwiGLU weights are interleaved in 64-row gate/up groups
+
+
+@dataclass
+class MuModelOutput:
+    """Output record with the reference's fields (mu_inference/models/base.py:22-47)."""
+
+    logits: torch.Tensor
+    hidden_states: Optional[torch.Tensor] = None
+    attentions: Optional[Dict[int, torch.Tensor]] = None
+    router_logits: Optional[Dict[int, torch.Tensor]] = None
+    mu_stats: Optional[Dict[str, float]] = None
+
+
+def pad_to(n: int, m: int) -> int:
+    return (n + m - 1) // m * m
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, pad: int) -> torch.Tensor:
+    """[I, K] gate and up -> [2*pad, K] in 64-row groups g0 u0 g1 u1 ... (zero rows past I)."""
+    I, Kd = gate.shape
+    g = torch.zeros(pad, Kd, dtype=gate.dtype, device=gate.device)
+    u = torch.zeros_like(g)
+    g[:I] = gate
+    u[:I] = up
+    return torch.stack([g.view(pad // PAD_MULT, PAD_MULT, Kd), u.view(pad // PAD_MULT, PAD_MULT, Kd)],
+                       1).reshape(2 * pad, Kd).contiguous()
+
+
+def pad_cols(w: torch.Tensor, cols: int) -> torch.Tensor:
+    if w.shape[1] == cols:
+        return w.contiguous()
+    out = torch.zeros(w.shape[0], cols, dtype=w.dtype, device=w.device)
+    out[:, : w.shape[1]] = w
+    return out
+
+
+def choose_split(M: int, N: int, K: int, max_rows: int, sms: int = 148) -> int:
+    """Split-K factor that fills the SMs when M x N has few 128x128 tiles."""
+    tiles = ((M + 127) // 128) * ((N + 127) // 128)
+    if tiles >= sms * 0.8:
+        return 1
+    s = min(-(-sms // tiles), max(1, ((K + 63) // 64) // 4), 16)
+    while s > 1 and s * M > max_rows:
+        s -= 1
+    return max(1, s)
+
+
+class Workspace:
+    """Activation buffers sized for ``max_tokens`` tokens / ``max_seqs`` sequences.
+
+    Buffer addresses stay fixed for the life of the workspace, which is what
+    lets a decode step be captured in a CUDA graph and replayed."""
+
+    def __init__(self, model: "MuModelBase", max_tokens: int, max_seqs: int, max_seq_len: int):
+        cfg = model.config
+        dev = model.device
+        H, D = cfg.hidden_size, cfg.head_dim
+        Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        T = max_tokens
+        self.max_tokens, self.max_seqs, self.max_seq_len = T, max_seqs, max_seq_len
+        bf, f32 = torch.bfloat16, torch.float32
+        self.resid = torch.empty(T, H, device=dev, dtype=f32)
+        self.x = torch.zeros(T, 2 * H, device=dev, dtype=bf)  # [x | mu_prev] for Deep
+        self.qkv = torch.empty(T, (Hq + 2 * Hkv) * D, device=dev, dtype=bf)
+        self.attn = torch.empty(T, Hq * D, device=dev, dtype=bf)
+        self.part_rows = max(T, 2048)
+        self.part = torch.empty(self.part_rows * model.max_part_width(), device=dev, dtype=f32)
+        self.act = torch.empty(T, model.act_width(), device=dev, dtype=bf)
+        self.xl = torch.empty(max_seqs, H, device=dev, dtype=bf)
+        self.logits = torch.empty(max_seqs, cfg.vocab_size, device=dev, dtype=f32)
+        nbytes = K.decode_attn_workspace_size(max_seqs, Hq, D, max_seq_len)
+        self.attn_ws = torch.empty(max(nbytes // 4, 4), device=dev, dtype=f32)
+        model.extra_workspace(self, T)
+
+    def part_view(self, splits: int, rows: int, cols: int) -> torch.Tensor:
+        return self.part[: splits * rows * cols].view(splits, rows, cols)
+
+
+class MuModelBase:
+    """Common state and the attention / LM-head pieces of the step."""
+
+    arch = "base"
+
+    def __init__(self, config: ModelConfig, mu_config: Optional[MuConfig] = None,
+                 device: str = "cuda"):
+        self.config = config
+        self.mu_config = mu_config or MuConfig()
+        self.clamp = Clamp.from_mu_config(self.mu_config)
+        self.device = torch.device(device)
+        self.dtype = torch.bfloat16
+        self.ws: Optional[Workspace] = None
+        self.rope_cos: Optional[torch.Tensor] = None
+        self.rope_sin: Optional[torch.Tensor] = None
+        self._rope_len = 0
+        self.ensure_rope(max(config.max_position_embeddings, 16))
+
+    # ---- overridable sizes ---------------------------------------------------
+    def act_width(self) -> int:
+        raise NotImplementedError
+
+    def max_part_width(self) -> int:
+        return self.config.hidden_size
+
+    def extra_workspace(self, ws: Workspace, T: int) -> None:
+        pass
+
+    # ---- setup -----------------------------------------------------------------
+    def ensure_rope(self, n: int) -> None:
+        """f32 cos/sin [n, head_dim/2], built like RotaryEmbeddingCompat._build_cache."""
+        if n <= self._rope_len:
+            return
+        D = self.config.head_dim
+        inv = 1.0 / (self.config.rope_theta ** (torch.arange(0, D, 2).float() / D))
+        t = torch.arange(n).float()
+        f = torch.outer(t, inv)
+        self.rope_cos = f.cos().to(self.device).contiguous()
+        self.rope_sin = f.sin().to(self.device).contiguous()
+        self._rope_len = n
+
+    def ensure_workspace(self, max_tokens: int, max_seqs: int, max_seq_len: int) -> bool:
+        """(Re)allocate buffers if a step needs more room; True if reallocated."""
+        ws = self.ws
+        if (ws is not None and ws.max_tokens >= max_tokens and ws.max_seqs >= max_seqs
+                and ws.max_seq_len >= max_seq_len):
+            return False
+        if ws is not None:
+            max_tokens = max(max_tokens, ws.max_tokens)
+            max_seqs = max(max_seqs, ws.max_seqs)
+            max_seq_len = max(max_seq_len, ws.max_seq_len)
+        self.ws = None
+        self.ws = Workspace(self, max_tokens, max_seqs, max_seq_len)
+        self.ensure_rope(max_seq_len + 1)
+        return True
+
+    # ---- shared pieces of the step ---------------------------------------------
+    def attention(self, layer: int, batch, cache, q_norm_w=None, k_norm_w=None) -> torch.Tensor:
+        """RoPE + KV append, then paged decode / varlen prefill attention -> ws.attn."""
+        cfg, ws = self.config, self.ws
+        T, Hq, Hkv, D = batch.num_tokens, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        kc, vc = cache.k_cache(layer), cache.v_cache(layer)
+        K.rope_kv_append(ws.qkv, batch.positions, batch.slot_mapping, self.rope_cos, self.rope_sin,
+                         Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, num_tokens=T)
+        nd, B = batch.num_decode, batch.num_seqs
+        bt = batch.block_tables
+        if nd > 0:
+            bound = min(batch.decode_len_bound, bt.shape[1] * 16)
+            K.decode_attn(ws.qkv[:, : Hq * D], ws.attn, kc, vc, bt, batch.seq_lens, Hq, Hkv, D,
+                          bound, workspace=ws.attn_ws, num_seqs=nd)
+        if B > nd:
+            # decode sequences own exactly one token each, so prefill rows start at nd
+            K.prefill_attn(ws.qkv[nd:, : Hq * D], ws.attn[nd:], kc, vc, bt[nd:],
+                           batch.seq_lens[nd:], batch.prefill_cu, batch.max_q_len, Hq, Hkv, D,
+                           num_seqs=B - nd)
+        return ws.attn
+
+    def lm_head(self, batch, final_norm_w: torch.Tensor, lm_w: torch.Tensor) -> torch.Tensor:
+        ws, B = self.ws, batch.num_seqs
+        K.rmsnorm_rows(ws.resid, batch.last_token_idx[:B], final_norm_w, self.config.rms_norm_eps,
+                       ws.xl, self.clamp)
+        K.gemm(ws.xl, lm_w, ws.logits, K.MUK_EPI_F32, M=B)
+        return ws.logits[:B]
+
+    def forward_step(self, batch, cache) -> torch.Tensor:
+        raise NotImplementedError
+
+    # ---- reference-style helpers ------------------------------------------------
+    def get_memory_footprint(self) -> Dict[str, float]:
+        tot = sum(t.numel() * t.element_size() for t in self.weight_tensors())
+        return {"total_mb": tot / 2**20}
+
+    def weight_tensors(self) -> List[torch.Tensor]:
+        return []
+
+    def num_parameters(self) -> int:
+        return sum(t.numel() for t in self.weight_tensors())

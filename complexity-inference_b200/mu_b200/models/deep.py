@@ -1,0 +1,175 @@
+"""DeepForCausalLM (Pacific-Prime) on libmuk: mu-guided attention, INL
+dynamics and the token-routed MLP as one flat-batch step.
+
+Restates mu_inference/models/deep.py:36-333 with layers.py:21-127 (INL),
+427-559 (token-routed MLP) and 562-741 (mu-guided attention):
+
+    x|mu_prev ─▶ fused [q|k|v ; mu_to_q|k|v] GEMM (K = 2H; H on layer 0)
+             ─▶ QK-norm + RoPE + append ─▶ attention ─▶ O GEMM ─▶ clamp
+             ─▶ controller_in GEMM (bias+SiLU epilogue) ─▶ controller_out GEMM
+             ─▶ mu_proj GEMM ─▶ INL kernel (v', h', residual, mu_c, post-norm,
+                mu-guided routing) ─▶ stable sort by expert ─▶ row gather
+             ─▶ grouped gate|up GEMM (SwiGLU) ─▶ grouped down GEMM
+             ─▶ un-permute + clamp + residual + clamp + next norm
+
+The reference gathers a private copy of the expert weights per token
+(layers.py:534-536); here tokens are bucketed per expert so each expert's
+weights stream once per step.  Expert weights are transposed at load to
+K-major ([E·2I, H] interleaved gate/up, [E·H, I]).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import kernels as K
+from ..core.config import ModelConfig, MuConfig
+from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
+from .registry import register_model
+from .weights import expert_intermediate, is_routed
+
+
+@register_model("deep")
+class DeepForCausalLM(MuModelBase):
+    arch = "deep"
+
+    def __init__(self, config: ModelConfig, mu_config: Optional[MuConfig] = None,
+                 device: str = "cuda"):
+        super().__init__(config, mu_config, device)
+        self.routed = is_routed("deep", config)
+        inner = expert_intermediate(config) if self.routed else config.intermediate_size
+        self.i_pad = pad_to(inner, PAD_MULT)
+        self.layers: List[Dict[str, torch.Tensor]] = []
+        self.embed = self.norm_w = self.lm_w = None
+
+    def act_width(self) -> int:
+        return self.i_pad
+
+    def extra_workspace(self, ws, T: int) -> None:
+        cfg, dev = self.config, self.device
+        H, C = cfg.hidden_size, cfg.dynamics_controller_hidden
+        ws.h = torch.empty(T, H, device=dev, dtype=torch.float32)
+        ws.hv = torch.zeros(T, 2 * H, device=dev, dtype=torch.bfloat16)
+        ws.v = torch.zeros(T, H, device=dev, dtype=torch.float32)
+        ws.ch = torch.empty(T, C, device=dev, dtype=torch.bfloat16)
+        ws.ctrl = torch.empty(T, 3 * H, device=dev, dtype=torch.float32)
+        ws.mp = torch.empty(T, H, device=dev, dtype=torch.float32)
+        ws.x2 = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        ws.xs = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        ws.dpart = torch.empty(T, H, device=dev, dtype=torch.float32)
+        ws.eids = torch.zeros(T, device=dev, dtype=torch.int32)
+        ws.offs = torch.zeros(max(cfg.num_experts, 1) + 1, device=dev, dtype=torch.int32)
+        ws.perm = torch.arange(T, device=dev, dtype=torch.int32)
+        ws.inv = torch.arange(T, device=dev, dtype=torch.int32)
+
+    # ---- weights -------------------------------------------------------------
+    @classmethod
+    def from_state_dict(cls, config: ModelConfig, sd: Dict[str, torch.Tensor],
+                        mu_config: Optional[MuConfig] = None, device: str = "cuda"):
+        m = cls(config, mu_config, device)
+        dev, bf = m.device, torch.bfloat16
+
+        def w(name):
+            return sd[name].to(dev, bf).contiguous()
+
+        def f(name):
+            return sd[name].to(dev, torch.float32).contiguous()
+
+        m.embed = w("embed_tokens.weight")
+        for l in range(config.num_hidden_layers):
+            p = f"layers.{l}."
+            a = p + "self_attn."
+            d = p + "dynamics."
+            wx = torch.cat([w(a + "q_proj.weight"), w(a + "k_proj.weight"), w(a + "v_proj.weight")], 0)
+            wm = torch.cat([w(a + "mu_to_q.weight"), w(a + "mu_to_k.weight"),
+                            w(a + "mu_to_v.weight")], 0)
+            L = {
+                "w_in": f(p + "input_layernorm.weight"),
+                "wcat": torch.cat([wx, wm], 1).contiguous(),  # [(Hq+2Hkv)D, 2H]
+                "wo": w(a + "o_proj.weight"),
+                "w_post": f(p + "post_attention_layernorm.weight"),
+                "wci": w(d + "controller_in.weight"),
+                "bci": f(d + "controller_in.bias"),
+                "wco": w(d + "controller_out.weight"),
+                "bco": f(d + "controller_out.bias"),
+                "wmu": w(d + "mu_proj.weight"),
+                "mu": f(d + "mu"),
+            }
+            if config.use_qk_norm:
+                L["qn"] = f(a + "q_norm.weight")
+                L["kn"] = f(a + "k_norm.weight")
+            if m.routed:
+                E = config.num_experts
+                gu = sd[p + "mlp.gate_up_proj"].to(dev, bf)   # [E, H, 2I]
+                dn = sd[p + "mlp.down_proj"].to(dev, bf)      # [E, I, H]
+                Ie = gu.shape[2] // 2
+                L["wgu"] = torch.cat([interleave_gate_up(gu[e, :, :Ie].t(), gu[e, :, Ie:].t(), m.i_pad)
+                                      for e in range(E)], 0).contiguous()
+                L["wd"] = torch.cat([pad_cols(dn[e].t(), m.i_pad) for e in range(E)], 0).contiguous()
+                L["router"] = w(p + "mlp.mu_router.weight")
+            else:
+                L["wgu"] = interleave_gate_up(w(p + "mlp.gate_proj.weight"),
+                                              w(p + "mlp.up_proj.weight"), m.i_pad)
+                L["wd"] = pad_cols(w(p + "mlp.down_proj.weight"), m.i_pad)
+            m.layers.append(L)
+        m.norm_w = f("norm.weight")
+        tied = config.tie_word_embeddings or "lm_head.weight" not in sd
+        m.lm_w = m.embed if tied else w("lm_head.weight")
+        return m
+
+    def weight_tensors(self):
+        ts = [self.embed, self.norm_w] + ([] if self.lm_w is self.embed else [self.lm_w])
+        for L in self.layers:
+            ts.extend(L.values())
+        return ts
+
+    # ---- step ------------------------------------------------------------------
+    def forward_step(self, batch, cache) -> torch.Tensor:
+        cfg, ws, cl = self.config, self.ws, self.clamp
+        T, H, eps = batch.num_tokens, cfg.hidden_size, cfg.rms_norm_eps
+        E, V = cfg.num_experts, cfg.vocab_size
+        resid = ws.resid[:T]
+        xcat = ws.x[:T]             # [x | mu_prev]
+        K.embed(batch.input_ids, self.embed, resid, cl)
+        ws.v[:T].zero_()            # velocity starts at zero (layers.py:99-100)
+        ws.hv[:T, H:].zero_()
+        K.residual_rmsnorm(resid, None, self.layers[0]["w_in"], eps, xcat[:, :H], clamp=cl,
+                           clamp_norm=True)
+        nl = len(self.layers)
+        for l, L in enumerate(self.layers):
+            kdim = H if l == 0 else 2 * H  # layer 0 has no mu_prev (deep.py:296)
+            K.gemm(xcat[:, :kdim], L["wcat"][:, :kdim], ws.qkv, K.MUK_EPI_BF16, M=T)
+            attn = self.attention(l, batch, cache, L.get("qn"), L.get("kn"))
+            s = choose_split(T, H, attn.shape[1], ws.part_rows)
+            part = ws.part_view(s, T, H)
+            K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)
+            K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)   # h = clamp(o_proj)
+            K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
+            K.gemm(ws.ch, L["wco"], ws.ctrl, K.MUK_EPI_F32, M=T)
+            K.gemm(ws.hv[:, :H], L["wmu"], ws.mp, K.MUK_EPI_F32, M=T)
+            K.inl_dynamics(ws.h, ws.ctrl, L["bco"], ws.mp, L["mu"], cfg.dynamics_dt, ws.v,
+                           ws.hv[:, H:], ws.resid, ws.x[:, H:], L["w_post"], eps, ws.x2,
+                           batch.input_ids, L.get("router"), E if self.routed else 0, V,
+                           ws.eids, cl, num_tokens=T)
+            last = l + 1 == nl
+            nxt_w = None if last else self.layers[l + 1]["w_in"]
+            nxt_out = None if last else xcat[:, :H]
+            if self.routed:
+                K.route_permute(ws.eids, E, ws.offs, ws.perm, ws.inv, num_tokens=T)
+                K.gather_rows(ws.x2, ws.perm, ws.xs, num_rows=T)
+                K.grouped_gemm(ws.xs, L["wgu"], ws.act, ws.offs, E, 2 * self.i_pad,
+                               K.MUK_EPI_SWIGLU, max_rows=T)
+                K.grouped_gemm(ws.act, L["wd"], ws.dpart, ws.offs, E, H, K.MUK_EPI_F32, max_rows=T)
+                K.residual_rmsnorm(resid, ws.dpart[:T], nxt_w, eps, nxt_out, clamp=cl,
+                                   clamp_delta=True, clamp_sum=True, clamp_norm=True,
+                                   delta_rows=ws.inv)
+            else:
+                K.gemm(ws.x2, L["wgu"], ws.act, K.MUK_EPI_SWIGLU, M=T)
+                s = choose_split(T, H, self.i_pad, ws.part_rows)
+                part = ws.part_view(s, T, H)
+                K.gemm(ws.act, L["wd"], part, K.MUK_EPI_F32, split_k=s, M=T)
+                K.residual_rmsnorm(resid, part, nxt_w, eps, nxt_out, clamp=cl, clamp_delta=True,
+                                   clamp_sum=True, clamp_norm=True)
+        return self.lm_head(batch, self.norm_w, self.lm_w)

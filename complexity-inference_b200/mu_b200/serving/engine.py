@@ -1,0 +1,415 @@
+"""Engines with the reference API (mu_inference/serving/engine.py).
+
+``StepEngine`` is the synchronous continuous-batching core: each ``step()``
+asks MuScheduler for a SchedulerOutput, runs it as one flat GPU step through
+MuWorker, samples every sequence on the GPU (BatchSampler) and applies the
+reference's stop rules (EOS of the tokenizer, stop_token_ids, max_tokens;
+engine.py:231-237 / 651-660).  New requests join while others decode;
+finished ones leave and free their blocks at once.
+
+``MuEngine`` keeps the reference's sequential API (initialize / generate /
+generate_stream / get_stats / shutdown, engine.py:58-426).
+``MuBatchEngine`` keeps the reference's continuous-batching API
+(engine.py:448-858), whose own loop cannot run (its sampling call raises
+TypeError); here it drives StepEngine from a background asyncio task.
+
+Prompts may be strings (a tokenizer is loaded from the model dir when
+available) or lists of token ids.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import logging
+import time
+import uuid
+from dataclasses import dataclass
+from typing import AsyncIterator, Dict, List, Optional, Sequence, Union
+
+import numpy as np
+import torch
+
+from ..core.config import EngineConfig, SamplingParams
+from ..core.scheduler import MuScheduler, Request, RequestStatus
+from ..utils.sampling import BatchSampler
+from ..utils.tokenizer import load_tokenizer
+from .worker import MuWorker
+
+logger = logging.getLogger(__name__)
+
+Prompt = Union[str, Sequence[int]]
+
+
+@dataclass
+class GenerationOutput:
+    request_id: str
+    text: str
+    token_ids: List[int]
+    finished: bool
+    finish_reason: Optional[str] = None
+    usage: Optional[Dict[str, int]] = None
+
+
+@dataclass
+class StreamOutput:
+    request_id: str
+    text: str
+    token_id: int
+    finished: bool
+    finish_reason: Optional[str] = None
+
+
+@dataclass
+class StepOutput:
+    request_id: str
+    token_id: int
+    finished: bool
+    finish_reason: Optional[str] = None
+
+
+class StepEngine:
+    """Scheduler + worker + sampler; one ``step()`` = one GPU forward step."""
+
+    def __init__(self, worker: MuWorker, config: EngineConfig, eos_token_id: Optional[int] = None):
+        self.worker = worker
+        self.config = config
+        self.scheduler = MuScheduler(config.scheduler)
+        self.sampler = BatchSampler(worker.model.config.vocab_size,
+                                    max(config.cache.max_num_seqs, config.scheduler.max_batch_size),
+                                    worker.device)
+        self.eos_token_id = eos_token_id
+        self.requests: Dict[str, Request] = {}
+        self._rows_host = torch.zeros(1024, dtype=torch.int32, pin_memory=torch.cuda.is_available())
+        self._rows_dev = torch.zeros(1024, dtype=torch.int32, device=worker.device)
+        self.num_steps = 0
+
+    # ---- requests ------------------------------------------------------------
+    def add_request(self, prompt_token_ids: Sequence[int], sampling_params: SamplingParams,
+                    request_id: Optional[str] = None) -> str:
+        rid = request_id or uuid.uuid4().hex[:16]
+        req = Request(request_id=rid, prompt_token_ids=list(prompt_token_ids),
+                      sampling_params=sampling_params, num_prompt_tokens=len(prompt_token_ids),
+                      max_tokens=sampling_params.max_tokens)
+        self.requests[rid] = req
+        self.scheduler.add_request(req)
+        return rid
+
+    def abort_request(self, request_id: str) -> None:
+        self._release(request_id)
+        self.scheduler.abort_request(request_id)
+        self.requests.pop(request_id, None)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    def _release(self, rid: str) -> None:
+        if rid in self.worker.active_requests:
+            self.worker.free_request(rid)
+        self.sampler.remove(rid)
+
+    def _finish(self, req: Request, reason: str, success: bool = True) -> None:
+        self._release(req.request_id)
+        self.scheduler.finish_request(req.request_id, success)
+        req.finish_reason = reason  # type: ignore[attr-defined]
+
+    # ---- one step ----------------------------------------------------------------
+    @torch.inference_mode()
+    def step(self) -> List[StepOutput]:
+        out = self.scheduler.schedule()
+        results: List[StepOutput] = []
+        for req in out.preempted_requests:  # recompute preemption: drop KV, re-prefill later
+            self._release(req.request_id)
+        prefills: List[Request] = []
+        for req in out.prefill_requests:
+            if req.request_id not in self.worker.active_requests:
+                if not self.worker.allocate_request(req.request_id):
+                    req.status = RequestStatus.PENDING
+                    self.scheduler.running.pop(req.request_id, None)
+                    self.scheduler.waiting.appendleft(req)
+                    continue
+            self.sampler.add(req.request_id)
+            prefills.append(req)
+        decodes = out.decode_requests
+        if not decodes and not prefills:
+            return results
+        work = [(r.request_id, np.asarray(r.output_token_ids[-1:], dtype=np.int32)) for r in decodes]
+        work += [(r.request_id, np.asarray(r.prompt_token_ids + r.output_token_ids, dtype=np.int32))
+                 for r in prefills]
+        seqs, errors = self.worker.prepare(work, len(decodes))
+        for rid, err in errors:
+            req = self.requests[rid]
+            logger.error("request %s: %s", rid, err)
+            self._finish(req, "error", success=False)
+            results.append(StepOutput(rid, -1, True, "error"))
+        if not seqs:
+            return results
+        ok = {s.request_id for s in seqs}
+        nd = sum(1 for r in decodes if r.request_id in ok)
+        logits, batch = self.worker.run_step(seqs, nd)
+        # repetition bitmaps: mark this step's input tokens in their request rows
+        T = sum(len(s.token_ids) for s in seqs)
+        if T > self._rows_host.numel():
+            n = 2 * T
+            self._rows_host = torch.zeros(n, dtype=torch.int32, pin_memory=torch.cuda.is_available())
+            self._rows_dev = torch.zeros(n, dtype=torch.int32, device=self.worker.device)
+        rh = self._rows_host.numpy()
+        rows = np.fromiter((self.sampler.row_of[s.request_id] for s in seqs), dtype=np.int32,
+                           count=len(seqs))
+        rh[:T] = np.repeat(rows, [len(s.token_ids) for s in seqs])
+        self._rows_dev[:T].copy_(self._rows_host[:T], non_blocking=True)
+        self.sampler.mark_inputs(self._rows_dev, batch.input_ids, T)
+        reqs = [self.requests[s.request_id] for s in seqs]
+        toks = self.sampler.sample(logits, [s.request_id for s in seqs],
+                                   [r.sampling_params for r in reqs],
+                                   [r.num_generated_tokens for r in reqs]).tolist()
+        self.num_steps += 1
+        for req, tok in zip(reqs, toks):
+            self.scheduler.update_request(req.request_id, tok)
+            sp = req.sampling_params
+            reason = None
+            if self.eos_token_id is not None and tok == self.eos_token_id:
+                reason = "stop"
+            elif sp.stop_token_ids and tok in sp.stop_token_ids:
+                reason = "stop"
+            elif req.num_generated_tokens >= sp.max_tokens:
+                reason = "length"
+            if reason:
+                self._finish(req, reason)
+            results.append(StepOutput(req.request_id, tok, reason is not None, reason))
+        return results
+
+    def run_to_completion(self) -> Dict[str, Request]:
+        while self.has_unfinished():
+            self.step()
+        return self.requests
+
+
+def _encode(tokenizer, prompt: Prompt) -> List[int]:
+    if isinstance(prompt, str):
+        if tokenizer is None:
+            raise ValueError("string prompts need a tokenizer in the model directory; "
+                             "pass token ids instead")
+        return list(tokenizer.encode(prompt))
+    return [int(t) for t in prompt]
+
+
+def _decode(tokenizer, ids: List[int]) -> str:
+    if tokenizer is None:
+        return ""
+    return tokenizer.decode(ids, skip_special_tokens=True)
+
+
+class MuEngine:
+    """Reference-compatible engine (engine.py:58-426): one request at a time."""
+
+    def __init__(self, config: Optional[EngineConfig] = None, model_path: Optional[str] = None):
+        self.config = config or EngineConfig()
+        self.model_path = model_path
+        self.worker: Optional[MuWorker] = None
+        self.tokenizer = None
+        self.core: Optional[StepEngine] = None
+        self.scheduler = None
+        self._initialized = False
+        self._lock = asyncio.Lock()
+        self.stats = {"total_requests": 0, "total_tokens_generated": 0, "start_time": None}
+
+    async def initialize(self, model_path: Optional[str] = None) -> None:
+        if self._initialized:
+            return
+        model_path = model_path or self.model_path
+        if model_path is None:
+            raise ValueError("model_path is required")
+        self.tokenizer = load_tokenizer(model_path)
+        self.worker = MuWorker(self.config, self.config.device)
+        self.worker.load_model(model_path)
+        self._make_core()
+
+    def initialize_from_worker(self, worker: MuWorker, tokenizer=None) -> None:
+        """Use an already loaded worker (random weights, tests, benchmarks)."""
+        self.worker = worker
+        self.tokenizer = tokenizer
+        self._make_core()
+
+    def _make_core(self) -> None:
+        eos = getattr(self.tokenizer, "eos_token_id", None) if self.tokenizer else None
+        self.core = StepEngine(self.worker, self.config, eos)
+        self.scheduler = self.core.scheduler
+        self._initialized = True
+        self.stats["start_time"] = time.time()
+
+    def _check(self) -> None:
+        if not self._initialized:
+            raise RuntimeError("Engine not initialized. Call initialize() first.")
+
+    def generate_sync(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
+                      request_id: Optional[str] = None) -> GenerationOutput:
+        return asyncio.get_event_loop().run_until_complete(
+            self.generate(prompt, sampling_params, request_id))
+
+    async def generate(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
+                       request_id: Optional[str] = None) -> GenerationOutput:
+        out = None
+        async for out in self._run(prompt, sampling_params, request_id, stream=False):
+            pass
+        return out
+
+    async def generate_stream(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
+                              request_id: Optional[str] = None) -> AsyncIterator[StreamOutput]:
+        async for item in self._run(prompt, sampling_params, request_id, stream=True):
+            yield item
+
+    async def _run(self, prompt, sampling_params, request_id, stream: bool):
+        self._check()
+        sp = sampling_params or SamplingParams()
+        ids = _encode(self.tokenizer, prompt)
+        async with self._lock:
+            rid = self.core.add_request(ids, sp, request_id)
+            req = self.core.requests[rid]
+            reason = None
+            while reason is None:
+                for o in self.core.step():
+                    if o.request_id != rid:
+                        continue
+                    if o.finished:
+                        reason = o.finish_reason
+                    if stream and o.token_id >= 0:
+                        yield StreamOutput(rid, _decode(self.tokenizer, [o.token_id]), o.token_id,
+                                           o.finished, o.finish_reason)
+                await asyncio.sleep(0)
+            self.core.requests.pop(rid, None)
+            gen = list(req.output_token_ids)
+            self.stats["total_requests"] += 1
+            self.stats["total_tokens_generated"] += len(gen)
+            if not stream:
+                yield GenerationOutput(rid, _decode(self.tokenizer, gen), gen, True, reason,
+                                       {"prompt_tokens": len(ids), "completion_tokens": len(gen),
+                                        "total_tokens": len(ids) + len(gen)})
+
+    def get_stats(self) -> Dict:
+        up = time.time() - self.stats["start_time"] if self.stats["start_time"] else 0
+        return {
+            "total_requests": self.stats["total_requests"],
+            "total_tokens_generated": self.stats["total_tokens_generated"],
+            "uptime_seconds": up,
+            "tokens_per_second": self.stats["total_tokens_generated"] / up if up > 0 else 0,
+            "worker": self.worker.get_stats() if self.worker else {},
+            "mu_config": {"enabled": self.config.mu.enabled, "mu": self.config.mu.mu,
+                          "clamp_min": self.config.mu.clamp_min,
+                          "clamp_max": self.config.mu.clamp_max},
+        }
+
+    def clear_cache(self) -> None:
+        if self.worker and self.worker.cache:
+            self.worker.cache.clear()
+
+    async def shutdown(self) -> None:
+        self.clear_cache()
+        self._initialized = False
+
+
+class MuBatchEngine(MuEngine):
+    """Continuous batching behind the reference's MuBatchEngine API (engine.py:448-858)."""
+
+    def __init__(self, config: Optional[EngineConfig] = None, model_path: Optional[str] = None):
+        super().__init__(config, model_path)
+        self._futures: Dict[str, asyncio.Future] = {}
+        self._queues: Dict[str, asyncio.Queue] = {}
+        self._prompt_len: Dict[str, int] = {}
+        self._task: Optional[asyncio.Task] = None
+        self._running = False
+        self.stats.update({"batches_processed": 0, "avg_batch_size": 0.0})
+
+    def _make_core(self) -> None:
+        super()._make_core()
+        self._running = True
+        try:
+            self._task = asyncio.get_event_loop().create_task(self._loop())
+        except RuntimeError:
+            self._task = None
+
+    async def _loop(self) -> None:
+        while self._running:
+            if not self.core.has_unfinished():
+                await asyncio.sleep(self.config.scheduler.batch_wait_time_ms / 1000.0)
+                continue
+            try:
+                outs = self.core.step()
+            except Exception as e:  # keep serving other requests
+                logger.error("batch step failed: %s", e)
+                await asyncio.sleep(0.01)
+                continue
+            n = self.stats["batches_processed"] = self.stats["batches_processed"] + 1
+            self.stats["avg_batch_size"] += (len(outs) - self.stats["avg_batch_size"]) / n
+            for o in outs:
+                q = self._queues.get(o.request_id)
+                if q is not None and o.token_id >= 0:
+                    await q.put(StreamOutput(o.request_id, _decode(self.tokenizer, [o.token_id]),
+                                             o.token_id, False))
+                if o.finished:
+                    await self._complete(o.request_id, o.finish_reason)
+            await asyncio.sleep(0)
+
+    async def _complete(self, rid: str, reason: Optional[str]) -> None:
+        req = self.core.requests.pop(rid, None)
+        gen = list(req.output_token_ids) if req else []
+        self.stats["total_requests"] += 1
+        self.stats["total_tokens_generated"] += len(gen)
+        fut = self._futures.pop(rid, None)
+        pl = self._prompt_len.pop(rid, 0)
+        if fut is not None and not fut.done():
+            fut.set_result(GenerationOutput(rid, _decode(self.tokenizer, gen), gen, True, reason,
+                                            {"prompt_tokens": pl, "completion_tokens": len(gen),
+                                             "total_tokens": pl + len(gen)}))
+        q = self._queues.pop(rid, None)
+        if q is not None:
+            await q.put(StreamOutput(rid, "", -1, True, reason))
+
+    async def generate(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
+                       request_id: Optional[str] = None) -> GenerationOutput:
+        self._check()
+        if self._task is None:
+            self._task = asyncio.get_event_loop().create_task(self._loop())
+        ids = _encode(self.tokenizer, prompt)
+        rid = self.core.add_request(ids, sampling_params or SamplingParams(), request_id)
+        fut = asyncio.get_event_loop().create_future()
+        self._futures[rid] = fut
+        self._prompt_len[rid] = len(ids)
+        return await fut
+
+    async def generate_stream(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
+                              request_id: Optional[str] = None) -> AsyncIterator[StreamOutput]:
+        self._check()
+        if self._task is None:
+            self._task = asyncio.get_event_loop().create_task(self._loop())
+        ids = _encode(self.tokenizer, prompt)
+        q: asyncio.Queue = asyncio.Queue()
+        rid = self.core.add_request(ids, sampling_params or SamplingParams(), request_id)
+        self._queues[rid] = q
+        self._prompt_len[rid] = len(ids)
+        while True:
+            item = await q.get()
+            yield item
+            if item.finished:
+                break
+
+    def get_stats(self) -> Dict:
+        s = super().get_stats()
+        s.update({"engine_type": "continuous_batching",
+                  "batches_processed": self.stats["batches_processed"],
+                  "avg_batch_size": round(self.stats["avg_batch_size"], 2),
+                  "scheduler": self.core.scheduler.get_stats() if self.core else {}})
+        return s
+
+    async def shutdown(self) -> None:
+        self._running = False
+        if self._task is not None:
+            self._task.cancel()
+            try:
+                await self._task
+            except (asyncio.CancelledError, Exception):
+                pass
+        for rid, fut in list(self._futures.items()):
+            if not fut.done():
+                fut.set_exception(RuntimeError("Engine shutdown"))
+        self._futures.clear()
+        await super().shutdown()

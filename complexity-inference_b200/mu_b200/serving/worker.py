@@ -1,0 +1,230 @@
+"""MuWorker: the drop-in step boundary (mu_inference/serving/worker.py).
+
+``execute(List[WorkerRequest]) -> List[WorkerOutput]`` keeps the reference
+signature, request/response types, order-preserving output and per-request
+error mapping (worker.py:150-209).  The difference is underneath: the
+reference runs one batch-1 forward per request with private contiguous KV
+tensors; here all requests of the call form ONE flat step — decode requests
+first, then prefills — over the paged KV pool, and the logits of all
+sequences come out of a single LM-head GEMM.
+
+``run_step`` is the batched entry used by the engines: it takes
+(request id, new token ids) pairs, returns the [B, vocab] f32 logits on the
+device and never copies logits to the host.  Pure-decode steps are replayed
+from CUDA graphs captured per batch-size bucket (padded with inert
+sequences: slot -1, one cached token), which removes the per-kernel launch
+cost of the Python layer loop.
+"""
+
+from __future__ import annotations
+
+import logging
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from ..core.cache import PagedKVCache
+from ..core.config import EngineConfig, ModelConfig
+from ..models.loader import build_model, config_from_dict, detect_architecture, load_config
+from ..models.weights import load_state_dict
+from .step import SeqWork, StepBatch, StepPacker
+
+logger = logging.getLogger(__name__)
+
+GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 96, 128, 192, 256, 384, 512)
+
+
+@dataclass
+class WorkerRequest:
+    """Request for the worker (worker.py:28-34)."""
+
+    request_id: str
+    input_ids: torch.Tensor  # [1, seq_len]
+    position_ids: Optional[torch.Tensor] = None
+    is_prefill: bool = True
+
+
+@dataclass
+class WorkerOutput:
+    """Output of the worker (worker.py:37-43)."""
+
+    request_id: str
+    logits: torch.Tensor  # [1, vocab_size]
+    finished: bool = False
+    error: Optional[str] = None
+
+
+class MuWorker:
+    def __init__(self, config: EngineConfig, device: str = "cuda"):
+        self.config = config
+        self.device = torch.device(device)
+        self.model = None
+        self.cache: Optional[PagedKVCache] = None
+        self.packer: Optional[StepPacker] = None
+        self.active_requests: Dict[str, Dict] = {}
+        self.stats = {"requests_processed": 0, "tokens_generated": 0, "prefill_tokens": 0}
+        self.use_graphs = True
+        self._graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, int]] = {}
+        self._graph_key = None
+
+    # ---- loading ---------------------------------------------------------------
+    def load_model(self, model_path: str) -> None:
+        """Load a local model dir (config.json + weights) and size the cache."""
+        cfg_dict = load_config(model_path)
+        arch = detect_architecture(cfg_dict)
+        mcfg = self.config.model
+        if mcfg is None or mcfg.hidden_size != cfg_dict.get("hidden_size", mcfg.hidden_size):
+            mcfg = config_from_dict(cfg_dict)
+            self.config.model = mcfg
+        self.load_state_dict(arch, mcfg, load_state_dict(model_path))
+
+    def load_state_dict(self, arch: str, model_config: ModelConfig, sd) -> None:
+        self.config.model = model_config
+        self.model = build_model(arch, model_config, sd, self.config.mu, str(self.device))
+        self._init_cache()
+
+    def _init_cache(self) -> None:
+        mc, cc, sc = self.config.model, self.config.cache, self.config.scheduler
+        nblocks = cc.num_gpu_blocks or cc.max_num_blocks
+        self.cache = PagedKVCache(mc.num_hidden_layers, mc.num_key_value_heads, mc.head_dim,
+                                  cc.block_size, nblocks, torch.bfloat16, str(self.device),
+                                  self.config.mu)
+        max_len = self.config.max_seq_len_hint or cc.max_seq_len
+        max_blocks = (max_len + cc.block_size - 1) // cc.block_size + 1
+        max_seqs = max(cc.max_num_seqs, sc.max_batch_size)
+        max_tokens = max(sc.max_num_batched_tokens, max_seqs)
+        self.packer = StepPacker(self.device, max_tokens, max_seqs, max_blocks)
+        self.model.ensure_workspace(max_tokens, max_seqs, max_blocks * cc.block_size)
+        self._graphs.clear()
+
+    # ---- request lifetime -------------------------------------------------------
+    def allocate_request(self, request_id: str) -> bool:
+        if not self.cache.allocate(request_id):
+            return False
+        self.active_requests[request_id] = {"seq_len": 0}
+        return True
+
+    def free_request(self, request_id: str) -> None:
+        self.cache.free(request_id)
+        self.active_requests.pop(request_id, None)
+
+    # ---- batched step -----------------------------------------------------------
+    def prepare(self, work: Sequence[Tuple[str, np.ndarray]], num_decode: int
+                ) -> Tuple[List[SeqWork], List[Tuple[str, str]]]:
+        """Reserve cache slots; returns the packable sequences and (id, error) pairs."""
+        seqs, errors = [], []
+        for rid, toks in work:
+            st = self.active_requests.get(rid)
+            if st is None:
+                errors.append((rid, f"Request {rid} not allocated"))
+                continue
+            toks = np.asarray(toks, dtype=np.int32).reshape(-1)
+            start = self.cache.get_seq_len(rid)
+            slots = self.cache.reserve(rid, len(toks))
+            if slots is None:
+                errors.append((rid, "KV cache out of blocks"))
+                continue
+            st["seq_len"] = start + len(toks)
+            seqs.append(SeqWork(rid, toks, start, slots, self.cache.block_table(rid)))
+        return seqs, errors
+
+    def run_step(self, seqs: List[SeqWork], num_decode: int) -> Tuple[torch.Tensor, StepBatch]:
+        """Pack and run one step; returns ([B, V] f32 logits on device, batch)."""
+        model = self.model
+        T = sum(len(s.token_ids) for s in seqs)
+        B = len(seqs)
+        grew = self.packer.ensure(T, B, max((len(s.block_table) for s in seqs), default=1))
+        # decode scratch is sized for the packer's block-table width (the graph bound)
+        grew |= model.ensure_workspace(max(T, self.packer.cap_b), self.packer.cap_b,
+                                       self._decode_bound())
+        if grew:
+            self._graphs.clear()
+        pure_decode = num_decode == B and B > 0
+        if pure_decode and self.use_graphs:
+            return self._run_decode_graph(seqs)
+        batch = self.packer.pack(seqs, num_decode)
+        logits = model.forward_step(batch, self.cache)
+        return logits, batch
+
+    def _decode_bound(self) -> int:
+        return self.packer.cap_mb * self.config.cache.block_size
+
+    def _run_decode_graph(self, seqs: List[SeqWork]) -> Tuple[torch.Tensor, StepBatch]:
+        B = len(seqs)
+        bucket = next((b for b in GRAPH_BUCKETS if b >= B), None)
+        cap_b = self.packer.cap_b
+        if bucket is None or bucket > cap_b or bucket > self.model.ws.max_seqs:
+            bucket = B
+        pad = [SeqWork("", np.zeros(1, np.int32), 0, np.full(1, -1, np.int32), [0])
+               for _ in range(bucket - B)]
+        allseq = list(seqs) + pad
+        T, Bb, _, qlens, ctx = self.packer.fill_host(allseq, bucket)
+        end = self.packer.off["bt"] + Bb * self.packer.cap_mb
+        self.packer.dev[:end].copy_(self.packer.host[:end], non_blocking=True)
+        key = (self.packer.generation, id(self.model.ws))
+        if self._graph_key != key:
+            self._graphs.clear()
+            self._graph_key = key
+        batch = self.packer.batch_view(T, Bb, bucket, qlens, ctx, self._decode_bound(),
+                                       [s.request_id for s in allseq])
+        g = self._graphs.get(bucket)
+        if g is None:
+            # warm-up on a side stream, then capture (all buffers are static)
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                self.model.forward_step(batch, self.cache)
+            torch.cuda.current_stream().wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.model.forward_step(batch, self.cache)
+            self._graphs[bucket] = (graph, bucket)
+            g = self._graphs[bucket]
+        g[0].replay()
+        return self.model.ws.logits[:B], batch
+
+    # ---- reference entry point ---------------------------------------------------
+    @torch.inference_mode()
+    def execute(self, requests: List[WorkerRequest]) -> List[WorkerOutput]:
+        """One flat step for all requests; outputs in request order."""
+        if not requests:
+            return []
+        V = self.model.config.vocab_size
+        dec = [r for r in requests if not r.is_prefill]
+        pre = [r for r in requests if r.is_prefill]
+        work = [(r.request_id, r.input_ids.reshape(-1).cpu().numpy()) for r in dec + pre]
+        out: Dict[str, WorkerOutput] = {}
+        try:
+            seqs, errors = self.prepare(work, len(dec))
+            for rid, err in errors:
+                out[rid] = WorkerOutput(rid, torch.zeros(1, V), finished=True, error=err)
+            ok_ids = {s.request_id for s in seqs}
+            nd = sum(1 for r in dec if r.request_id in ok_ids)
+            if seqs:
+                logits, _ = self.run_step(seqs, nd)
+                logits = logits.clone()
+                for i, s in enumerate(seqs):
+                    out[s.request_id] = WorkerOutput(s.request_id, logits[i:i + 1])
+                self.stats["tokens_generated"] += nd
+                self.stats["prefill_tokens"] += sum(len(s.token_ids) for s in seqs[nd:])
+        except Exception as e:  # per-request error mapping as in worker.py:179-206
+            logger.error("step failed: %s", e)
+            for r in requests:
+                if r.request_id not in out or out[r.request_id].error is None:
+                    out[r.request_id] = WorkerOutput(r.request_id, torch.zeros(1, V), True, str(e))
+        return [out[r.request_id] for r in requests]
+
+    def get_stats(self) -> Dict:
+        return {
+            **self.stats,
+            "active_requests": len(self.active_requests),
+            "cache": self.cache.get_stats() if self.cache else {},
+            "device": str(self.device),
+            "model_memory_mb": self.model.get_memory_footprint()["total_mb"] if self.model else 0,
+            "cuda_graphs": sorted(self._graphs),
+        }
+
+    def reset_stats(self) -> None:
+        self.stats = {"requests_processed": 0, "tokens_generated": 0, "prefill_tokens": 0}

@@ -214,12 +214,13 @@ int muk_reduce_clamp(const float* partials, int64_t partial_stride, int num_part
  * top_p), then an exact categorical draw (Gumbel-max on counter-based
  * Philox4x32-10 noise keyed by seeds[b] and offsets[b]).  Replaces
  * prepare_logits + sample_token, mu_inference/utils/sampling.py:20-120.
- * tokens_out[b] receives the id; probs are not materialised. */
+ * Row b's bitmap is seen_bits[seen_rows ? seen_rows[b] : b].  tokens_out[b]
+ * receives the id; probabilities are not materialised. */
 int muk_sample(const float* logits, int64_t ld, int num_rows, int vocab,
                const float* temperature, const int32_t* top_k, const float* top_p,
                const float* rep_penalty, const uint32_t* seen_bits, int64_t seen_stride,
-               const uint64_t* seeds, const uint64_t* offsets, int32_t* tokens_out,
-               void* stream);
+               const int32_t* seen_rows, const uint64_t* seeds, const uint64_t* offsets,
+               int32_t* tokens_out, void* stream);
 
 /* Sets bit tokens[b] in seen_bits[rows[b]] for b < n (keeps the repetition
  * bitmaps current after each step without a host round trip). */
