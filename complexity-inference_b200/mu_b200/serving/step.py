@@ -119,9 +119,12 @@ class StepPacker:
         T, B, maxb, qlens, ctx = self.fill_host(seqs, num_decode)
         # one copy covering the used prefix of every segment (block tables last)
         end = self.off["bt"] + B * self.cap_mb
-        st = stream or torch.cuda.current_stream()
-        with torch.cuda.stream(st):
-            self.dev[:end].copy_(self.host[:end], non_blocking=True)
+        if self.device.type == "cuda":
+            st = stream or torch.cuda.current_stream()
+            with torch.cuda.stream(st):
+                self.dev[:end].copy_(self.host[:end], non_blocking=True)
+        else:
+            self.dev[:end].copy_(self.host[:end])
         return self.batch_view(T, B, num_decode, qlens, ctx, decode_len_bound,
                                [s.request_id for s in seqs])
 
