@@ -1,0 +1,544 @@
+#!/usr/bin/env python
+"""Decode throughput of the continuous-batching forward step on B200.
+
+Workload (Llama-3-8B shape, random-init bf16 weights, seed 2): hidden 4096,
+32 layers, 32 query / 8 KV heads, head_dim 128, SwiGLU 14336, vocab 128256,
+RoPE theta 5e5, untied LM head.  256 concurrent requests per GPU, prompt
+lengths lognormal(median 512, sigma 0.8) clipped to [32, 4096], token ids
+uniform, 256 greedy output tokens each, a new request arriving as soon as
+one finishes.  The engine starts in steady state: each initial request has a
+random share (0..255) of its 256 tokens already generated, so finishes and
+arrivals are spread over the steps.
+
+A "step" is one scheduler step of the engine: all running requests decode
+one token and newly arrived requests are prefilled in the same flat batch.
+The metric counts generated tokens (one per scheduled sequence per step).
+
+  value     device throughput: the timed steps, recorded once, replayed with
+            their packed arrays already in HBM (no host work between steps)
+  e2e       the same steps through the public StepEngine.step() API: host
+            scheduling, packing, host->device copy of each step's arrays and
+            device->host read of the sampled ids inside the timed region
+  roofline  paged decode attention of the running batch (HBM-bound) and the
+            decode GEMMs (tensor-bound), timed in isolation with CUDA events
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun every rank serves its own 256 requests (replicas; no
+collective on the data path); value is the sum over ranks / max time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "complexity-inference_b200"))
+
+METRIC = "decode tokens/s @256 ragged reqs; paged-attn HBM GB/s vs 8 TB/s roofline"
+WORKLOAD = ("Llama-3-8B-shape (H4096 L32 32/8 heads D128 I14336 V128256 theta5e5), "
+            "256 concurrent ragged requests, steady-state continuous batching, greedy")
+C3 = dict(hidden=4096, layers=32, heads=32, kv=8, head_dim=128, inter=14336, vocab=128256,
+          theta=500000.0, seed=2)
+CONCURRENCY = 256
+OUT_TOKENS = 256
+PROMPT_MEDIAN, PROMPT_SIGMA, PROMPT_MIN, PROMPT_MAX = 512, 0.8, 32, 4096
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def model_config():
+    from mu_b200.core.config import ModelConfig
+
+    return ModelConfig(vocab_size=C3["vocab"], hidden_size=C3["hidden"],
+                       intermediate_size=C3["inter"], num_hidden_layers=C3["layers"],
+                       num_attention_heads=C3["heads"], num_key_value_heads=C3["kv"],
+                       head_dim=C3["head_dim"], max_position_embeddings=8192,
+                       rope_theta=C3["theta"], rms_norm_eps=1e-5, tie_word_embeddings=False)
+
+
+class Arrivals:
+    def __init__(self, seed: int, vocab: int):
+        self.rng = np.random.default_rng(seed)
+        self.vocab = vocab
+        self.n = 0
+
+    def prompt(self):
+        L = int(np.clip(np.round(self.rng.lognormal(math.log(PROMPT_MEDIAN), PROMPT_SIGMA)),
+                        PROMPT_MIN, PROMPT_MAX))
+        return self.rng.integers(0, self.vocab, L).tolist()
+
+    def new_request(self, engine, params_cls, already=0):
+        prompt = self.prompt()
+        if already:
+            prompt = prompt + self.rng.integers(0, self.vocab, already).tolist()
+        self.n += 1
+        sp = params_cls(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0,
+                        max_tokens=OUT_TOKENS - already)
+        return engine.add_request(prompt, sp, f"q{self.n}")
+
+
+def build(rank: int):
+    from mu_b200.core.config import CacheConfig, EngineConfig, SchedulerConfig
+    from mu_b200.models.weights import random_state_dict
+    from mu_b200.serving.engine import StepEngine
+    from mu_b200.serving.worker import MuWorker
+
+    cfg = model_config()
+    max_len = PROMPT_MAX + OUT_TOKENS + 16
+    # expected KV ~ 256 x ~830 tokens; keep 3x headroom for bursts of long prompts
+    blocks = 45000
+    ec = EngineConfig(model=cfg, dtype="bfloat16",
+                      cache=CacheConfig(max_seq_len=max_len, block_size=16, max_num_blocks=blocks,
+                                        max_num_seqs=CONCURRENCY),
+                      scheduler=SchedulerConfig(max_batch_size=CONCURRENCY,
+                                                max_num_batched_tokens=8192,
+                                                max_prefill_tokens=8192))
+    sd = random_state_dict(cfg, "llama", C3["seed"], device="cuda", dtype=torch.bfloat16,
+                           include_unused=False)
+    worker = MuWorker(ec, "cuda")
+    worker.load_state_dict("llama", cfg, sd)
+    del sd
+    torch.cuda.empty_cache()
+    engine = StepEngine(worker, ec)
+    return engine, worker, ec
+
+
+class Recorder:
+    """Wraps worker.run_step to keep each step's packed arrays for the replay."""
+
+    def __init__(self, worker):
+        self.worker = worker
+        self.orig = worker.run_step
+        self.steps = []
+        self.on = False
+        worker.run_step = self.run_step
+
+    def run_step(self, seqs, num_decode):
+        if self.on:
+            st = self.worker.stage(seqs, num_decode)
+            buf = self.worker.packer.host[:st.end].to(self.worker.device, non_blocking=True)
+            self.steps.append((st, buf))
+            self.worker.packer.dev[:st.end].copy_(buf)
+            return self.worker.run_staged(st)
+        return self.orig(seqs, num_decode)
+
+
+def steady_state_step(engine, arrivals, params_cls):
+    outs = engine.step()
+    produced = sum(1 for o in outs if o.token_id >= 0)
+    for o in outs:
+        if o.finished:
+            arrivals.new_request(engine, params_cls)
+    return produced
+
+
+def time_attention(worker, reps=10):
+    """Decode attention of the current running batch, layer 0, timed alone."""
+    from mu_b200 import kernels as K
+
+    cache = worker.cache
+    rids = [r for r in worker.active_requests]
+    lens = np.array([cache.get_seq_len(r) for r in rids], dtype=np.int32)
+    maxb = max(len(cache.block_table(r)) for r in rids)
+    bt = np.zeros((len(rids), maxb), np.int32)
+    for i, r in enumerate(rids):
+        b = cache.block_table(r)
+        bt[i, :len(b)] = b
+    cfg = worker.model.config
+    Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    B = len(rids)
+    q = torch.randn(B, Hq * D, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    btd = torch.from_numpy(bt).cuda()
+    sl = torch.from_numpy(lens).cuda()
+    mx = int(lens.max())
+    ws = torch.empty(K.decode_attn_workspace_size(B, Hq, D, mx) // 4 + 4, device="cuda")
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for layer in range(3):
+        K.decode_attn(q, out, cache.k_cache(layer), cache.v_cache(layer), btd, sl, Hq, Hkv, D, mx,
+                      workspace=ws)
+    torch.cuda.synchronize()
+    s.record()
+    for i in range(reps):  # rotate layers so each launch streams fresh KV (>> L2)
+        layer = i % cfg.num_hidden_layers
+        K.decode_attn(q, out, cache.k_cache(layer), cache.v_cache(layer), btd, sl, Hq, Hkv, D, mx,
+                      workspace=ws)
+    e.record()
+    torch.cuda.synchronize()
+    t = s.elapsed_time(e) / reps * 1e-3
+    byts = float(lens.sum()) * Hkv * D * 2 * 2
+    return byts, t, B, int(lens.sum())
+
+
+def time_gemms(worker, M=256, reps=10):
+    """The decode-shape GEMMs of one layer (QKV, O, gate|up, down), back to back."""
+    from mu_b200 import kernels as K
+    from mu_b200.models.base import choose_split
+
+    m = worker.model
+    ws = m.ws
+    H = m.config.hidden_size
+    x = torch.randn(M, 2 * H, device="cuda").bfloat16()[:, :H]
+    flops = 0
+    Ls = [m.layers[i % len(m.layers)] for i in range(reps)]
+
+    def run(L):
+        K.gemm(x, L["wqkv"], ws.qkv, K.MUK_EPI_BF16, M=M)
+        s = choose_split(M, H, ws.attn.shape[1], ws.part_rows)
+        K.gemm(ws.attn, L["wo"], ws.part_view(s, M, H), K.MUK_EPI_F32, split_k=s, M=M)
+        K.gemm(x, L["wgu"], ws.act, K.MUK_EPI_SWIGLU, M=M)
+        s = choose_split(M, H, m.i_pad, ws.part_rows)
+        K.gemm(ws.act, L["wd"], ws.part_view(s, M, H), K.MUK_EPI_F32, split_k=s, M=M)
+
+    L0 = m.layers[0]
+    for w in (L0["wqkv"], L0["wo"], L0["wgu"], L0["wd"]):
+        flops += 2 * M * w.shape[0] * w.shape[1]
+    run(L0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for L in Ls:
+        run(L)
+    e.record()
+    torch.cuda.synchronize()
+    t = s.elapsed_time(e) / reps * 1e-3
+    wbytes = sum(L0[k].numel() * 2 for k in ("wqkv", "wo", "wgu", "wd"))
+    return flops, t, wbytes
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (numpy restatement of the reference path)
+# ---------------------------------------------------------------------------
+class CpuBaseline:
+    """The reference algorithm on the host cores, via the oracle (numpy port).
+
+    The reference decodes one request at a time (batch-1 forwards with a
+    dense per-request KV cache).  Sample: one Llama-3-8B-shape layer (random
+    f32 weights) decoding one token at context ``ctx`` per step, plus one
+    LM-head matvec; the per-token time is scaled to 32 layers."""
+
+    def __init__(self, ctx=830, seed=0):
+        sys.path.insert(0, str(ROOT))
+        import oracle as O
+
+        H, Hq, Hkv, D, I, V = (C3["hidden"], C3["heads"], C3["kv"], C3["head_dim"], C3["inter"],
+                               C3["vocab"])
+        rng = np.random.default_rng(seed)
+
+        def w(*s):
+            return rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
+
+        p = {"embed_tokens.weight": w(64, H), "norm.weight": np.ones(H, np.float32),
+             "layers.0.input_layernorm.weight": np.ones(H, np.float32),
+             "layers.0.post_attention_layernorm.weight": np.ones(H, np.float32),
+             "layers.0.self_attn.q_proj.weight": w(Hq * D, H),
+             "layers.0.self_attn.k_proj.weight": w(Hkv * D, H),
+             "layers.0.self_attn.v_proj.weight": w(Hkv * D, H),
+             "layers.0.self_attn.o_proj.weight": w(H, Hq * D),
+             "layers.0.mlp.gate_proj.weight": w(I, H), "layers.0.mlp.up_proj.weight": w(I, H),
+             "layers.0.mlp.down_proj.weight": w(H, I)}
+        shape = O.ModelShape("llama", H, 1, Hq, Hkv, D, 64, 1e-5, C3["theta"], tie=True,
+                             max_pos=ctx + 4096)
+        self.model = O.OracleModel(shape, p, O.MuCfg(False))
+        self.past = [(rng.standard_normal((Hkv, ctx, D), dtype=np.float32),
+                      rng.standard_normal((Hkv, ctx, D), dtype=np.float32))]
+        self.lm = w(V, H)
+        self.x = rng.standard_normal(H, dtype=np.float32)
+        self.ctx = ctx
+        self.sample = (f"1 of 32 layers x 1 decode token at ctx {ctx} + 1 LM-head matvec "
+                       f"(numpy f32) per step, scaled to 32 layers")
+        self.step()  # warm
+
+    def step(self) -> float:
+        """Seconds per generated token (one layer timed, scaled to the model)."""
+        t0 = time.perf_counter()
+        self.model.forward([3], self.past)  # cache not grown: every step at the same context
+        layer_t = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        _ = self.lm @ self.x
+        lm_t = time.perf_counter() - t0
+        return layer_t * C3["layers"] + lm_t
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    cb = CpuBaseline()
+    per_tok = []
+    for i in range(args.warmup + args.steps):
+        t = cb.step()
+        if i >= args.warmup:
+            per_tok.append(t)
+    sample = cb.sample
+    tps = 1.0 / float(np.mean(per_tok))
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": float(np.mean(per_tok)) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "cpu_path": "oracle port of the reference "
+                       "(per-request batch-1 decode, dense KV), numpy f32"},
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cpu_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch.distributed as dist
+    from mu_b200 import _lib
+    from mu_b200 import kernels as K
+    from mu_b200.core.config import SamplingParams
+
+    torch.cuda.set_device(local_rank)
+    engine, worker, ec = build(rank)
+    arrivals = Arrivals(1000 + rank, C3["vocab"])
+    rng = np.random.default_rng(7 + rank)
+    for _ in range(CONCURRENCY):
+        arrivals.new_request(engine, SamplingParams, already=int(rng.integers(0, OUT_TOKENS)))
+    # initial fill: prefill every starting request (untimed)
+    fill_steps = 0
+    while engine.scheduler.waiting:
+        steady_state_step(engine, arrivals, SamplingParams)
+        fill_steps += 1
+    for _ in range(args.warmup):
+        steady_state_step(engine, arrivals, SamplingParams)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---- e2e: the public step API, host work and copies included ----------
+    rec = Recorder(worker)
+    rec.on = True
+    h2d0 = 0
+    n_tok = 0
+    launches0 = _lib.launch_count
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            n_tok += steady_state_step(engine, arrivals, SamplingParams)
+        end.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    launches = _lib.launch_count - launches0
+    rec.on = False
+    e2e_t = start.elapsed_time(end) * 1e-3
+    h2d = sum(st.end * 4 for st, _ in rec.steps) / max(1, len(rec.steps))
+    steps_meta = [(st.B, st.T, st.num_decode) for st, _ in rec.steps]
+
+    # ---- value: same steps, arrays resident in HBM, no host work in between ----
+    sampler = engine.sampler
+    greedy_t = torch.zeros(CONCURRENCY * 2, device="cuda")
+    zeros_i = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int32)
+    ones_f = torch.ones(CONCURRENCY * 2, device="cuda")
+    seeds = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int64)
+    toks = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int32)
+
+    def replay():
+        for st, buf in rec.steps:
+            worker.packer.dev[:st.end].copy_(buf, non_blocking=True)
+            logits, _ = worker.run_staged(st)
+            K.sample(logits, greedy_t, zeros_i, ones_f, ones_f, None, seeds, seeds, toks,
+                     num_rows=st.B)
+
+    replay()  # graphs for every bucket exist already; this warms the replay path
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    replay()
+    e2.record()
+    torch.cuda.synchronize()
+    dev_t = s2.elapsed_time(e2) * 1e-3
+
+    # ---- roofline pieces ------------------------------------------------------
+    hbm, tflops, peak_kind = peaks()
+    att_bytes, att_t, att_b, att_tok = time_attention(worker)
+    g_flops, g_t, g_wbytes = time_gemms(worker)
+
+    # ---- reduce over ranks ------------------------------------------------------
+    vals = torch.tensor([n_tok, dev_t, e2e_t, wall], device="cuda", dtype=torch.float64)
+    if world > 1:
+        tot = vals.clone()
+        dist.all_reduce(tot[:1], op=dist.ReduceOp.SUM)
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        n_all, dev_max, e2e_max, wall_max = float(tot[0]), float(mx[1]), float(mx[2]), float(mx[3])
+    else:
+        n_all, dev_max, e2e_max, wall_max = n_tok, dev_t, e2e_t, wall
+    if rank != 0:
+        return 0
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cb = CpuBaseline()
+        per_tok = float(np.mean([cb.step() for _ in range(5)]))
+        sample = cb.sample + ", mean of 5 steps"
+        cpu = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": sample}
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC,
+        "value": n_all / dev_max,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_max / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 2), lognormal prompts, uniform ids",
+        "config": {
+            "workload": WORKLOAD,
+            "model": "llama-3-8b-shape",
+            "global_batch": CONCURRENCY * world,
+            "seq_len": f"prompt lognormal(512, 0.8) in [32, 4096] + {OUT_TOKENS} generated",
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": "no flush needed: each step streams ~15 GB of weights and ~28 GB of KV (L2 126 MB)",
+            "tokens_timed": int(n_all),
+            "steps_pure_decode": sum(1 for b, t, d in steps_meta if d == b),
+            "mean_tokens_per_step": float(np.mean([t for _, t, _ in steps_meta])),
+            "initial_fill_steps": fill_steps,
+        },
+        "e2e": {"value": n_all / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(4 * CONCURRENCY), "wall_s": wall_max,
+                "api": "mu_b200.serving.engine.StepEngine.step"},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "muk_paged_decode_attn (layer, running batch)", "bound": "hbm",
+                     "achieved": att_bytes / att_t / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": att_bytes / att_t / 1e9 / hbm, "traffic": None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes": att_bytes, "seqs": att_b, "context_tokens": att_tok},
+        "roofline_gemm": {"kernel": "muk_gemm_bf16 decode layer (QKV+O+gate|up+down, M=256)",
+                          "bound": "tensor", "achieved": g_flops / g_t / 1e12, "peak": tflops,
+                          "unit": "TFLOP/s", "frac": g_flops / g_t / 1e12 / tflops,
+                          "weight_GBps": g_wbytes / g_t / 1e9, "peak_source": peak_kind},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

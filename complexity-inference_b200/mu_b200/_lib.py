@@ -66,6 +66,11 @@ SIGNATURES = {
 
 _lib: ctypes.CDLL | None = None
 
+# Kernel launches issued through call() (entry points that launch two kernels
+# count both); the benchmark reports it as its launch count.
+launch_count = 0
+_TWO_KERNELS = {"muk_paged_decode_attn"}
+
 
 class MukError(RuntimeError):
     """A libmuk entry point returned a non-zero status."""
@@ -99,10 +104,13 @@ def last_error() -> str:
 
 def call(name: str, *args) -> None:
     """Call a status-returning entry point and raise MukError on failure."""
+    global launch_count
     fn = getattr(load(), name)
     rc = fn(*args)
     if rc != MUK_OK:
         raise MukError(name, rc, last_error())
+    if name != "muk_device_error":
+        launch_count += 2 if name in _TWO_KERNELS else 1
 
 
 def device_error() -> int:

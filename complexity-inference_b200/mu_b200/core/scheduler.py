@@ -125,17 +125,26 @@ class MuScheduler:
                 decode_budget -= 1
         slots = self.config.max_batch_size - len(out.decode_requests)
         prefill_budget = min(self.config.max_prefill_tokens, decode_budget)
+        # Admission differs from the reference on purpose: there a popped request
+        # that misses the budget is neither scheduled nor re-queued (it is lost),
+        # and with chunked prefill every waiting request is admitted at once
+        # although prompts are always run whole.  Here a request is admitted when
+        # its whole prompt (plus tokens generated before a preemption) fits the
+        # remaining budget — the first prefill of a step always does — and the
+        # rest go back to the front of the queue in their original order.
+        deferred: List[Request] = []
         for req in self._get_next_requests(slots):
-            need = req.num_prompt_tokens
-            if self.config.enable_chunked_prefill:
-                need = min(need, prefill_budget)
-            if need <= prefill_budget:
-                req.status = RequestStatus.PREFILL
-                req.start_time = time.time()
-                self.running[req.request_id] = req
-                out.prefill_requests.append(req)
-                out.num_prefill_tokens += need
-                prefill_budget -= need
+            need = req.num_prompt_tokens + req.num_generated_tokens
+            if deferred or (out.prefill_requests and need > prefill_budget):
+                deferred.append(req)
+                continue
+            req.status = RequestStatus.PREFILL
+            req.start_time = req.start_time or time.time()
+            self.running[req.request_id] = req
+            out.prefill_requests.append(req)
+            out.num_prefill_tokens += need
+            prefill_budget -= need
+        self._requeue_front(deferred)
         if self._should_preempt(out):
             out.preempted_requests = self._preempt_requests(out)
         return out
@@ -149,6 +158,14 @@ class MuScheduler:
             while self.waiting and len(got) < max_count:
                 got.append(self.waiting.popleft())
         return got
+
+    def _requeue_front(self, reqs: List[Request]) -> None:
+        if self.config.policy == "priority":
+            for r in reqs:
+                heapq.heappush(self.priority_queue, r)
+        else:
+            for r in reversed(reqs):
+                self.waiting.appendleft(r)
 
     def _should_preempt(self, out: SchedulerOutput) -> bool:
         return self.config.enable_preemption and out.total_tokens > self.config.max_num_batched_tokens

@@ -25,6 +25,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
+from .. import _lib
 from ..core.cache import PagedKVCache
 from ..core.config import EngineConfig, ModelConfig
 from ..models.loader import build_model, config_from_dict, detect_architecture, load_config
@@ -33,7 +34,26 @@ from .step import SeqWork, StepBatch, StepPacker
 
 logger = logging.getLogger(__name__)
 
-GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 96, 128, 192, 256, 384, 512)
+GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
+
+
+def _bucket(n: int) -> int:
+    return next((b for b in GRAPH_BUCKETS if b >= n), n)
+
+
+@dataclass
+class StagedStep:
+    """A step packed into the staging buffer, ready for run_staged."""
+
+    B: int                 # real sequences (logits rows returned)
+    T: int                 # tokens incl. padding
+    Bp: int                # sequences incl. padding
+    num_decode: int
+    qlens: np.ndarray
+    ctx: np.ndarray
+    end: int               # used prefix of the staging buffer (int32 elements)
+    graph: bool
+    request_ids: List[str]
 
 
 @dataclass
@@ -132,58 +152,67 @@ class MuWorker:
 
     def run_step(self, seqs: List[SeqWork], num_decode: int) -> Tuple[torch.Tensor, StepBatch]:
         """Pack and run one step; returns ([B, V] f32 logits on device, batch)."""
-        model = self.model
+        st = self.stage(seqs, num_decode)
+        self.packer.dev[:st.end].copy_(self.packer.host[:st.end], non_blocking=True)
+        return self.run_staged(st)
+
+    def stage(self, seqs: List[SeqWork], num_decode: int) -> "StagedStep":
+        """Reserve buffer room and fill the pinned host staging buffer for a step.
+
+        Pure-decode steps are padded to their CUDA-graph bucket with inert
+        sequences (slot -1, one cached token in block 0, outputs ignored)."""
         T = sum(len(s.token_ids) for s in seqs)
         B = len(seqs)
-        grew = self.packer.ensure(T, B, max((len(s.block_table) for s in seqs), default=1))
+        grew = self.packer.ensure(max(T, _bucket(B)), max(B, _bucket(B)), max((len(s.block_table) for s in seqs),
+                                                               default=1))
         # decode scratch is sized for the packer's block-table width (the graph bound)
-        grew |= model.ensure_workspace(max(T, self.packer.cap_b), self.packer.cap_b,
-                                       self._decode_bound())
+        grew |= self.model.ensure_workspace(max(T, self.packer.cap_b), self.packer.cap_b,
+                                            self._decode_bound())
         if grew:
             self._graphs.clear()
-        pure_decode = num_decode == B and B > 0
-        if pure_decode and self.use_graphs:
-            return self._run_decode_graph(seqs)
-        batch = self.packer.pack(seqs, num_decode)
-        logits = model.forward_step(batch, self.cache)
-        return logits, batch
+        graph = self.use_graphs and num_decode == B and B > 0
+        allseq = seqs
+        if graph:
+            bucket = _bucket(B)
+            allseq = list(seqs) + [SeqWork("", np.zeros(1, np.int32), 0, np.full(1, -1, np.int32),
+                                           [0]) for _ in range(bucket - B)]
+            num_decode = bucket
+        Tp, Bp, _, qlens, ctx = self.packer.fill_host(allseq, num_decode)
+        end = self.packer.off["bt"] + Bp * self.packer.cap_mb
+        return StagedStep(B, Tp, Bp, num_decode, qlens, ctx, end, graph,
+                          [s.request_id for s in allseq])
 
-    def _decode_bound(self) -> int:
-        return self.packer.cap_mb * self.config.cache.block_size
-
-    def _run_decode_graph(self, seqs: List[SeqWork]) -> Tuple[torch.Tensor, StepBatch]:
-        B = len(seqs)
-        bucket = next((b for b in GRAPH_BUCKETS if b >= B), None)
-        cap_b = self.packer.cap_b
-        if bucket is None or bucket > cap_b or bucket > self.model.ws.max_seqs:
-            bucket = B
-        pad = [SeqWork("", np.zeros(1, np.int32), 0, np.full(1, -1, np.int32), [0])
-               for _ in range(bucket - B)]
-        allseq = list(seqs) + pad
-        T, Bb, _, qlens, ctx = self.packer.fill_host(allseq, bucket)
-        end = self.packer.off["bt"] + Bb * self.packer.cap_mb
-        self.packer.dev[:end].copy_(self.packer.host[:end], non_blocking=True)
+    def run_staged(self, st: "StagedStep") -> Tuple[torch.Tensor, StepBatch]:
+        """Run a step whose arrays are already in the packer's device buffer."""
+        bound = self._decode_bound() if st.graph else None
+        batch = self.packer.batch_view(st.T, st.Bp, st.num_decode, st.qlens, st.ctx, bound,
+                                       st.request_ids)
+        if not st.graph:
+            return self.model.forward_step(batch, self.cache), batch
         key = (self.packer.generation, id(self.model.ws))
         if self._graph_key != key:
             self._graphs.clear()
             self._graph_key = key
-        batch = self.packer.batch_view(T, Bb, bucket, qlens, ctx, self._decode_bound(),
-                                       [s.request_id for s in allseq])
-        g = self._graphs.get(bucket)
+        g = self._graphs.get(st.Bp)
         if g is None:
             # warm-up on a side stream, then capture (all buffers are static)
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
                 self.model.forward_step(batch, self.cache)
-            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
+            n0 = _lib.launch_count
             with torch.cuda.graph(graph):
                 self.model.forward_step(batch, self.cache)
-            self._graphs[bucket] = (graph, bucket)
-            g = self._graphs[bucket]
+            g = self._graphs[st.Bp] = (graph, _lib.launch_count - n0)
+            _lib.launch_count = n0
         g[0].replay()
-        return self.model.ws.logits[:B], batch
+        _lib.launch_count += g[1]
+        return self.model.ws.logits[:st.B], batch
+
+    def _decode_bound(self) -> int:
+        return self.packer.cap_mb * self.config.cache.block_size
 
     # ---- reference entry point ---------------------------------------------------
     @torch.inference_mode()

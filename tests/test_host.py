@@ -125,15 +125,37 @@ def test_scheduler_order_budget_and_preemption():
     for r in reqs:
         sc.add_request(r)
     out = sc.schedule()
-    # r0 (4) fits, r1 (5) exceeds the remaining prefill budget of 4 and is dropped from this
-    # step as in the reference (it is neither scheduled nor re-queued), r2 fits
-    assert [r.request_id for r in out.prefill_requests] == ["r0", "r2"]
+    # r0 (4) fits; r1 (5) exceeds the remaining prefill budget of 4, so it and the
+    # requests behind it go back to the front of the queue in order (the reference
+    # would lose r1 here)
+    assert [r.request_id for r in out.prefill_requests] == ["r0"]
+    assert [r.request_id for r in sc.waiting] == ["r1", "r2", "r3"]
     for r in out.prefill_requests:
         sc.update_request(r.request_id, 1)
     out2 = sc.schedule()
-    assert [r.request_id for r in out2.decode_requests] == ["r0", "r2"]
-    assert [r.request_id for r in out2.prefill_requests] == ["r3"]
+    assert [r.request_id for r in out2.decode_requests] == ["r0"]
+    assert [r.request_id for r in out2.prefill_requests] == ["r1", "r2"]
+    assert [r.request_id for r in sc.waiting] == ["r3"]
+    # a prompt longer than the whole budget still runs when it is first in its step
+    big = Request(request_id="big", num_prompt_tokens=100)
+    sc.waiting.appendleft(big)
+    for r in out2.prefill_requests:
+        sc.update_request(r.request_id, 1)
+    sc.running["r0"].status = RequestStatus.FINISHED
     sc.finish_request("r0")
+    out3 = sc.schedule()
+    assert [r.request_id for r in out3.prefill_requests] == ["big"]
+    # preemption: over the token budget, the most advanced decodes go back to the queue
+    sc2 = MuScheduler(SchedulerConfig(max_batch_size=8, max_num_batched_tokens=3,
+                                      max_prefill_tokens=8))
+    for i in range(4):
+        q = Request(request_id=f"d{i}", num_prompt_tokens=1)
+        sc2.running[q.request_id] = q
+        q.status = RequestStatus.DECODE
+        q.num_generated_tokens = i
+    o = sc2.schedule()
+    assert [r.request_id for r in o.preempted_requests] == ["d3"]
+    assert len(o.decode_requests) == 3 and sc2.waiting[0].request_id == "d3"
     assert sc.get_request("r0").status == RequestStatus.FINISHED
     st = sc.get_stats()
     assert st["finished"] == 1 and st["policy"] == "fcfs"

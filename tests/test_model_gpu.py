@@ -1,0 +1,137 @@
+"""Model-level parity of the GPU step against the reference's golden outputs.
+
+* ``MuWorker.execute`` (the drop-in boundary) runs all requests of the tiny
+  Llama / Deep fixtures as flat batched steps (8 prefills in one step, then
+  batched decodes).  With the reference's greedy tokens forced as inputs, the
+  bf16 logits must be within 2e-2 max-abs of the reference's fp32 logits at
+  every recorded step, and block tables must equal the reference allocator's.
+* ``StepEngine`` generates greedily with continuous batching (requests of
+  different lengths, later requests prefilled inside decode steps, CUDA-graph
+  replay of pure decode steps): tokens must equal the reference's up to the
+  first step whose reference top-2 logit gap is below 0.05 (a bf16 rounding
+  can legitimately flip a near tie there; the logits test covers those steps).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from golden_models import load_tiny
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2      # max-abs, bf16 path vs fp32 reference
+GAP_TOL = 0.05        # reference top-2 gap below which argmax may flip
+
+
+def _worker(name, cuda, graphs=True, max_batch=8):
+    from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
+    from mu_b200.serving.worker import MuWorker
+
+    shape, cfg, sd, d, prompts = load_tiny(name)
+    ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True),
+                      cache=CacheConfig(max_seq_len=256, max_num_blocks=512, max_num_seqs=16),
+                      scheduler=SchedulerConfig(max_batch_size=max_batch,
+                                                max_num_batched_tokens=2048))
+    w = MuWorker(ec, str(cuda))
+    w.load_state_dict(shape.arch, cfg, sd)
+    w.use_graphs = graphs
+    return w, shape, d, prompts, ec
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+@pytest.mark.parametrize("graphs", [False, True])
+def test_execute_teacher_forced(cuda, name, graphs):
+    from mu_b200.serving.worker import WorkerRequest
+
+    w, shape, d, prompts, _ = _worker(name, cuda, graphs)
+    toks = d["tokens"]
+    R, n = toks.shape
+    steps = list(d["logit_steps"])
+    alloc = O.PagedAllocatorOracle(w.cache.max_num_blocks, 16)
+    for r in range(R):
+        assert w.allocate_request(f"r{r}") and alloc.allocate(f"r{r}")
+    worst = 0.0
+    for i in range(n):
+        if i == 0:
+            reqs = [WorkerRequest(f"r{r}", torch.tensor([prompts[r]]), is_prefill=True)
+                    for r in range(R)]
+            for r in range(R):
+                alloc.append(f"r{r}", len(prompts[r]))
+        else:
+            reqs = [WorkerRequest(f"r{r}", torch.tensor([[int(toks[r, i - 1])]]), is_prefill=False)
+                    for r in range(R)]
+            for r in range(R):
+                alloc.append(f"r{r}", 1)
+        outs = w.execute(reqs)
+        assert [o.request_id for o in outs] == [f"r{r}" for r in range(R)]
+        for r, o in enumerate(outs):
+            assert o.error is None, o.error
+            lg = o.logits.float().cpu().numpy().reshape(-1)
+            if i in steps:
+                err = float(np.abs(lg - d["logits"][r, steps.index(i)]).max())
+                worst = max(worst, err)
+                assert err <= LOGIT_TOL, (name, r, i, err)
+            if d["top2_gap"][r, i] > GAP_TOL:
+                assert int(np.argmax(lg)) == int(toks[r, i]), (name, r, i)
+        for r in range(R):
+            assert w.cache.block_table(f"r{r}") == alloc.blocks[f"r{r}"]
+            assert w.cache.get_seq_len(f"r{r}") == alloc.seq_len(f"r{r}")
+    print(f"{name} graphs={graphs}: worst logit max-abs {worst:.4g}")
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+def test_engine_greedy_continuous_batching(cuda, name):
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=5)
+    toks = d["tokens"]
+    R, n = toks.shape
+    eng = StepEngine(w, ec)
+    lens = {}
+    for r in range(R):
+        # request 0 stops early so that waiting requests join while others decode
+        m = 5 if r == 0 else n
+        lens[f"r{r}"] = m
+        eng.add_request(prompts[r], SamplingParams(temperature=0.0, top_k=0, top_p=1.0,
+                                                   repetition_penalty=1.0, max_tokens=m), f"r{r}")
+    mixed = 0
+    while eng.has_unfinished():
+        nd = len([rq for rq in eng.scheduler.running.values() if rq.status.value == "decode"])
+        nw = len(eng.scheduler.waiting)
+        eng.step()
+        mixed += int(nd > 0 and nw > 0)
+    assert mixed > 0, "no step mixed decodes with new prefills"
+    for r in range(R):
+        req = eng.requests[f"r{r}"]
+        got = req.output_token_ids
+        assert len(got) == lens[f"r{r}"]
+        for i, t in enumerate(got):
+            if t != int(toks[r, i]):
+                assert d["top2_gap"][r, i] <= GAP_TOL, (name, r, i, t, int(toks[r, i]))
+                break
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+    assert w.get_stats()["cuda_graphs"], "pure-decode steps should replay a CUDA graph"
+
+
+def test_sampled_generation_is_seeded(cuda):
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    w, shape, d, prompts, ec = _worker("deep_tiny", cuda)
+    outs = []
+    for _ in range(2):
+        eng = StepEngine(w, ec)
+        for r in range(3):
+            eng.add_request(prompts[r], SamplingParams(temperature=0.7, top_k=50, top_p=0.9,
+                                                       repetition_penalty=1.1, max_tokens=12,
+                                                       seed=100 + r), f"s{r}")
+        eng.run_to_completion()
+        outs.append([eng.requests[f"s{r}"].output_token_ids for r in range(3)])
+    assert outs[0] == outs[1]
+    assert all(len(o) == 12 for o in outs[0])
