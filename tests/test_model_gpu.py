@@ -89,9 +89,10 @@ def test_engine_greedy_continuous_batching(cuda, name):
     from mu_b200.core.config import SamplingParams
     from mu_b200.serving.engine import StepEngine
 
-    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=5)
-    toks = d["tokens"]
+    toks = np.load(__import__("golden_models").G / f"{name}.npz")["tokens"]
     R, n = toks.shape
+    # fewer batch slots than requests: the last ones wait and join mid-generation
+    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=R - 1)
     eng = StepEngine(w, ec)
     lens = {}
     for r in range(R):
