@@ -20,6 +20,7 @@
 // 1/sqrt(head_dim); decode attends every cached token (is_causal=False with
 // q_len=1), prefill is causal with the queries at the end of the context.
 #include <math.h>
+#include <mutex>
 
 #include "abi_util.h"
 #include "common.cuh"
@@ -646,4 +647,80 @@ extern "C" int muk_paged_prefill_attn(const void* q, int64_t q_stride, void* out
                               num_q_heads, num_kv_heads, num_blocks, scale, s);
   set_last_error("muk_paged_prefill_attn: head_dim %d not built (64, 128)", head_dim);
   return MUK_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention without caller-provided scratch.
+//
+// For callers that cannot allocate device memory themselves: a process whose
+// HBM is reserved up front by another allocator (a framework's caching
+// allocator that a plain C caller cannot reach), or a latency-critical serving
+// loop that must not call cudaMalloc/cudaFree because they can synchronise
+// the device.  The split-K partial results live in this file-scope array
+// instead: every GPU that loads the library holds it until the process exits.
+// ---------------------------------------------------------------------------
+namespace muk {
+
+constexpr size_t kStaticDecodeScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) float g_decode_scratch[kStaticDecodeScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+static void* g_scratch_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_scratch_mu;
+
+// Device address of g_decode_scratch on the current device, resolved once per
+// device.  In host code the array's name is only a stand-in; the address must
+// come from cudaGetSymbolAddress with that device current.
+static int static_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_last_error("muk_paged_decode_attn_static: no usable current device (%s)",
+                   cudaGetErrorString(e));
+    return MUK_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_last_error("muk_paged_decode_attn_static: cudaGetSymbolAddress failed on device %d: %s",
+                     dev, cudaGetErrorString(e));
+      return MUK_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return MUK_OK;
+}
+
+}  // namespace muk
+
+extern "C" size_t muk_decode_attn_static_scratch_bytes(void) {
+  return muk::kStaticDecodeScratchBytes;
+}
+
+extern "C" int muk_paged_decode_attn_static(const void* q, int64_t q_stride, void* out,
+                                            int64_t out_stride, const void* k_cache,
+                                            const void* v_cache, const int32_t* block_tables,
+                                            int block_table_stride, const int32_t* seq_lens,
+                                            int num_seqs, int num_q_heads, int num_kv_heads,
+                                            int head_dim, int block_size, int num_blocks,
+                                            float scale, int max_seq_len, void* stream) {
+  const size_t need =
+      muk_decode_attn_workspace_size(num_seqs, num_q_heads, head_dim, max_seq_len, block_size);
+  if (need > muk::kStaticDecodeScratchBytes) {
+    muk::set_last_error(
+        "muk_paged_decode_attn_static: this shape needs %zu bytes of split-K scratch, more than "
+        "the library's static %zu-byte array; use muk_paged_decode_attn with a workspace",
+        need, muk::kStaticDecodeScratchBytes);
+    return MUK_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  int rc = muk::static_scratch(&scratch);
+  if (rc != MUK_OK) return rc;
+  return muk_paged_decode_attn(q, q_stride, out, out_stride, k_cache, v_cache, block_tables,
+                               block_table_stride, seq_lens, num_seqs, num_q_heads, num_kv_heads,
+                               head_dim, block_size, num_blocks, scale, max_seq_len, scratch,
+                               muk::kStaticDecodeScratchBytes, stream);
 }

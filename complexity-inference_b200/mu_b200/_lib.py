@@ -46,6 +46,10 @@ SIGNATURES = {
     "muk_paged_decode_attn": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P, c_int,
                                       c_int, c_int, c_int, c_int, c_int, c_float, c_int, _P,
                                       c_size_t, _P]),
+    "muk_decode_attn_static_scratch_bytes": (c_size_t, []),
+    "muk_paged_decode_attn_static": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P,
+                                             c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                             c_int, _P]),
     "muk_paged_prefill_attn": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P, _P, c_int,
                                        c_int, c_int, c_int, c_int, c_int, c_int, c_float, _P]),
     "muk_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, c_int, c_int,
@@ -69,7 +73,7 @@ _lib: ctypes.CDLL | None = None
 # Kernel launches issued through call() (entry points that launch two kernels
 # count both); the benchmark reports it as its launch count.
 launch_count = 0
-_TWO_KERNELS = {"muk_paged_decode_attn"}
+_TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static"}
 
 
 class MukError(RuntimeError):

@@ -124,6 +124,28 @@ int muk_paged_decode_attn(const void* q, int64_t q_stride, void* out, int64_t ou
                           int num_blocks, float scale, int max_seq_len, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Same computation as muk_paged_decode_attn, for callers that cannot allocate
+ * device memory: a process whose HBM is reserved up front by an allocator the
+ * caller cannot reach (e.g. a framework's caching allocator seen from plain
+ * C), or a serving loop that must not call cudaMalloc/cudaFree because they
+ * can synchronise the device.  No counterpart in the reference (it has no
+ * kernels).  The split-K scratch is a file-scope device array of
+ * muk_decode_attn_static_scratch_bytes() (16 MiB) that every GPU loading the
+ * library keeps until exit; shapes whose muk_decode_attn_workspace_size
+ * exceeds it are rejected with MUK_ERR_WORKSPACE.  The first call on a device
+ * resolves that array's device address (cudaGetSymbolAddress): make it
+ * before any stream capture on that device.  All calls share the one array,
+ * so calls that overlap on the GPU (different streams, concurrent threads)
+ * race; nothing in it needs to start at zero, since every entry the merge
+ * pass reads is written earlier by the same call.  Allocates nothing. */
+size_t muk_decode_attn_static_scratch_bytes(void);
+int muk_paged_decode_attn_static(const void* q, int64_t q_stride, void* out, int64_t out_stride,
+                                 const void* k_cache, const void* v_cache,
+                                 const int32_t* block_tables, int block_table_stride,
+                                 const int32_t* seq_lens, int num_seqs, int num_q_heads,
+                                 int num_kv_heads, int head_dim, int block_size, int num_blocks,
+                                 float scale, int max_seq_len, void* stream);
+
 /* ---- K2b: varlen causal prefill over the paged cache --------------------- */
 
 /* Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of q/out.
