@@ -402,11 +402,13 @@ def run_ours(args, rank, world, local_rank):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")
         start.record()
         t0 = time.perf_counter()
         for _ in range(args.steps):
             n_tok += steady_state_step(engine, arrivals, SamplingParams)
         end.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     launches = _lib.launch_count - launches0
@@ -511,6 +513,67 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_micro(args):
+    """Single-kernel cases sized for ncu captures (a few GB on the device)."""
+    from mu_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    res = {"micro": args.micro}
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.micro == "decode_attn":
+        Hq, Hkv, D = 32, 8, 128
+        rng = np.random.default_rng(3)
+        ctx = rng.integers(args.ctx_min, args.ctx_max + 1, args.seqs)
+        nblk = (ctx + 15) // 16
+        NB = int(nblk.sum()) + 8
+        kc = torch.randn(NB, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+        vc = torch.randn(NB, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+        perm = rng.permutation(NB)
+        bt = np.zeros((args.seqs, int(nblk.max())), np.int32)
+        i = 0
+        for b, n in enumerate(nblk):
+            bt[b, :n] = perm[i:i + n]
+            i += n
+        btd = torch.from_numpy(bt).cuda()
+        sl = torch.from_numpy(ctx.astype(np.int32)).cuda()
+        q = torch.randn(args.seqs, Hq * D, device="cuda", generator=g).bfloat16()
+        out = torch.empty_like(q)
+        mx = int(ctx.max())
+        ws = torch.empty(K.decode_attn_workspace_size(args.seqs, Hq, D, mx) // 4 + 4, device="cuda")
+
+        def fn():
+            K.decode_attn(q, out, kc, vc, btd, sl, Hq, Hkv, D, mx, workspace=ws)
+        byts = float(ctx.sum()) * Hkv * D * 4
+        res.update(seqs=args.seqs, ctx_sum=int(ctx.sum()), algorithmic_bytes=byts)
+    else:
+        M, N, Kd = args.m, args.n, args.k
+        A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
+        B = (torch.randn(N, Kd, device="cuda", generator=g) * 0.02).bfloat16()
+        C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+        def fn():
+            K.gemm(A, B, C, K.MUK_EPI_BF16)
+        byts = 2.0 * M * N * Kd
+        res.update(M=M, N=N, K=Kd, flops=byts)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(args.reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    t = s.elapsed_time(e) / args.reps * 1e-3
+    res["us_per_launch"] = t * 1e6
+    if args.micro == "decode_attn":
+        res["GBps"] = byts / t / 1e9
+    else:
+        res["TFLOPs"] = byts / t / 1e12
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,7 +581,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["decode_attn", "gemm"], default=None,
+                    help="time one kernel on a small case (for ncu captures)")
+    ap.add_argument("--seqs", type=int, default=64)
+    ap.add_argument("--ctx-min", type=int, default=256)
+    ap.add_argument("--ctx-max", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=256)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--reps", type=int, default=20)
     args = ap.parse_args()
+    if args.micro:
+        return run_micro(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
