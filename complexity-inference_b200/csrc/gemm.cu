@@ -3,23 +3,28 @@
 //   C[M, N] = epilogue(A[M, K] · B[N, K]ᵀ)     A = activations, B = weights,
 //                                             both K-major bf16, f32 accumulate.
 //
-// One CTA computes a 128 x BN output tile (split-K optional) with three
-// warp roles:
-//   warp 0      TMA producer: 2-D tiled loads (128-byte swizzle, no multicast)
-//               of the A and B k-tiles into a STAGES-deep shared-memory ring,
-//               completion signalled on the stage's `full` mbarrier;
-//   warp 1      allocates the TMEM accumulator (BN columns x 128 lanes) and
-//               has one thread issue tcgen05.mma (M=128, N=BN, K=16) per 16
-//               columns of each k-tile; tcgen05.commit releases the stage to
-//               the producer (`empty`) and finally signals `accum`;
-//   warps 2-5   epilogue: tcgen05.ld 32x32b (TMEM lane quarter = warp % 4),
-//               apply the fused epilogue, store to global memory.
-// Every mbarrier wait is bounded (see common.cuh); a time-out records a
-// device error and the CTA unwinds, freeing its TMEM.
+// Persistent, warp-specialised kernel: one CTA per SM walks a static list of
+// output tiles (128 x BN, optionally split along K), so the epilogue of one
+// tile overlaps the main loop of the next and short grids do not lose a
+// partial wave per launch.
+//   warp 0      TMA producer: 2-D tiled loads (128-byte swizzle, no
+//               multicast) of A/B k-tiles into a STAGES-deep shared-memory
+//               ring; completion on the stage's `full` mbarrier.
+//   warp 1      allocates TMEM (two BN-column accumulators, 128 lanes) and
+//               has one thread issue tcgen05.mma (M=128, N=BN, K=16); a
+//               tcgen05.commit frees each ring stage (`empty`) and, per tile,
+//               signals the accumulator (`acc_full[a]`).
+//   warps 2-5   epilogue: wait `acc_full[a]`, tcgen05.ld 32x32b (TMEM lane
+//               quarter = warp % 4), fused epilogue, store, release the
+//               accumulator (`acc_empty[a]`) for the tile after next.
+// Tiles are ordered M-fastest so that the CTAs working on the row tiles of
+// one weight tile run at the same time and the weights stream from HBM once.
+// Every mbarrier wait is bounded (common.cuh); a time-out records a device
+// error and the CTA unwinds, freeing its TMEM.
 //
-// Grouped mode (token-routed experts): grid.x enumerates (expert, 128-row
-// tile) pairs from the device-side expert offsets, B rows are offset by
-// expert * N, and stores are masked at the expert's last row.
+// Grouped mode (token-routed experts): the tile index enumerates (expert,
+// 128-row tile) pairs from the device-side expert offsets; B rows are offset
+// by expert * N; stores stop at the expert's last row.
 //
 // Replaces the nn.Linear / torch.bmm contractions of the reference forward
 // step (mu_inference/models/layers.py:410-424, 538-547, 661-669, 730, the
@@ -37,6 +42,7 @@ namespace muk {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
+constexpr int kNumSMs = 148;
 
 template <int BN, int STAGES>
 struct GemmLayout {
@@ -44,13 +50,64 @@ struct GemmLayout {
   static constexpr int kB = BN * kBK * 2;
   static constexpr int kStage = kA + kB;
   static constexpr int kBarOff = STAGES * kStage;
-  static constexpr int kBytes = kBarOff + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr int kBytes = kBarOff + (2 * STAGES + 4) * 8 + 16 + 1024;
 };
+
+struct TileArgs {
+  int M, N, K;
+  int m_tiles, n_tiles, splits, kt_per_split, total;
+  int64_t ldc, split_stride;
+  const float* bias;
+  const int32_t* offsets;  // grouped mode
+  int num_experts;
+};
+
+struct Tile {
+  int row0, row_end, brow0, n0, split, kt0, nk;
+  bool valid;
+};
+
+template <int BN, bool GROUPED>
+__device__ __forceinline__ Tile decode_tile(const TileArgs& a, int t) {
+  Tile r;
+  const int mt = t % a.m_tiles;
+  const int rest = t / a.m_tiles;
+  const int nt = rest % a.n_tiles;
+  r.split = rest / a.n_tiles;
+  r.n0 = nt * BN;
+  r.valid = true;
+  if (!GROUPED) {
+    r.row0 = mt * kBM;
+    r.row_end = a.M;
+    r.brow0 = r.n0;
+  } else {
+    int e = -1, acc = 0;
+    r.row0 = 0;
+    r.row_end = 0;
+    for (int i = 0; i < a.num_experts; ++i) {
+      const int lo = a.offsets[i], hi = a.offsets[i + 1];
+      const int tt = (hi - lo + kBM - 1) / kBM;
+      if (mt < acc + tt) {
+        e = i;
+        r.row0 = lo + (mt - acc) * kBM;
+        r.row_end = hi;
+        break;
+      }
+      acc += tt;
+    }
+    r.valid = e >= 0;
+    r.brow0 = (e < 0 ? 0 : e) * a.N + r.n0;
+  }
+  const int k_tiles = (a.K + kBK - 1) / kBK;
+  r.kt0 = r.split * a.kt_per_split;
+  r.nk = max(0, min(k_tiles, r.kt0 + a.kt_per_split) - r.kt0);
+  return r;
+}
 
 template <int EPI>
 __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_off, int row,
-                                            int row_end, int col, int ncols, const uint32_t (&v)[32],
-                                            const float* bias) {
+                                            int row_end, int col, int ncols,
+                                            const uint32_t (&v)[32], const float* bias) {
   if (row >= row_end) return;
   if (EPI == MUK_EPI_F32) {
     float* dst = reinterpret_cast<float*>(C) + split_off + (int64_t)row * ldc + col;
@@ -92,10 +149,9 @@ __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_
 
 template <int BN, int STAGES, int EPI, bool GROUPED>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   void* __restrict__ C, int64_t ldc, int M, int N, int K, int kt_per_split,
-                   int64_t split_stride, const float* __restrict__ bias,
-                   const int32_t* __restrict__ expert_offsets, int num_experts) {
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
+                           const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
+                           const TileArgs args) {
   using L = GemmLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -103,48 +159,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* basep = smem_raw + (base - raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(basep + L::kBarOff);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- tile coordinates -------------------------------------------------
-  int row0, row_end, brow0;
-  if (!GROUPED) {
-    row0 = blockIdx.x * kBM;
-    row_end = M;
-    brow0 = blockIdx.y * BN;
-  } else {
-    int e = -1, acc = 0;
-    row0 = 0;
-    row_end = 0;
-    for (int i = 0; i < num_experts; ++i) {
-      const int lo = expert_offsets[i], hi = expert_offsets[i + 1];
-      const int t = (hi - lo + kBM - 1) / kBM;
-      if ((int)blockIdx.x < acc + t) {
-        e = i;
-        row0 = lo + ((int)blockIdx.x - acc) * kBM;
-        row_end = hi;
-        break;
-      }
-      acc += t;
-    }
-    if (e < 0) return;  // whole CTA: no tile for this index
-    brow0 = e * N + blockIdx.y * BN;
-  }
-  const int n0 = blockIdx.y * BN;
-  const int k_tiles = (K + kBK - 1) / kBK;
-  const int kt0 = blockIdx.z * kt_per_split;
-  const int nk = max(0, min(k_tiles, kt0 + kt_per_split) - kt0);
-
-  // ---- setup ------------------------------------------------------------
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -152,7 +182,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -163,56 +193,88 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ---- TMA producer ----
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)L::kStage);
-        const uint32_t sa = base + (uint32_t)(s * L::kStage);
-        tma_load_2d(sa, &tmA, &full[s], (kt0 + i) * kBK, row0);
-        tma_load_2d(sa + L::kA, &tmB, &full[s], (kt0 + i) * kBK, brow0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.total && ok; t += gridDim.x) {
+        const Tile tl = decode_tile<BN, GROUPED>(args, t);
+        if (!tl.valid) continue;
+        for (int i = 0; i < tl.nk; ++i, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], (uint32_t)L::kStage);
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
+          tma_load_2d(sa, &tmA, &full[s], (tl.kt0 + i) * kBK, tl.row0);
+          tma_load_2d(sa + L::kA, &tmB, &full[s], (tl.kt0 + i) * kBK, tl.brow0);
+        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---- MMA issuer ----
-    if (lane == 0 && nk > 0) {
+    if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      uint32_t it = 0, use = 0;
       bool ok = true;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, kDevTimeoutFull)) {
-          ok = false;
-          break;
-        }
+      for (int t = blockIdx.x; t < args.total && ok; t += gridDim.x) {
+        const Tile tl = decode_tile<BN, GROUPED>(args, t);
+        if (!tl.valid) continue;
+        const int a = use & 1;
+        const uint32_t aph = (use >> 1) & 1u;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1u, kDevTimeoutAccum)) break;
         tc_fence_after();
-        const uint32_t sa = base + (uint32_t)(s * L::kStage);
+        const uint32_t dacc = tmem + (uint32_t)(a * BN);
+        for (int i = 0; i < tl.nk; ++i, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t ad = umma_desc_sw128(sa + k * 32);
-          const uint64_t bd = umma_desc_sw128(sa + L::kA + k * 32);
-          tc_mma_f16(tmem, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(sa + k * 32);
+            const uint64_t bd = umma_desc_sw128(sa + L::kA + k * 32);
+            tc_mma_f16(dacc, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        if (!ok) break;
+        tc_commit(&acc_full[a]);
+        ++use;
       }
-      if (ok) tc_commit(accum);
     }
     __syncwarp();
   } else {
     // ---- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----
     const int quarter = warp & 3;
-    const int row = row0 + quarter * 32 + lane;
-    const int64_t split_off = (int64_t)blockIdx.z * split_stride;
-    bool ok = true;
-    if (nk > 0) {
-      ok = mbar_wait(accum, 0, kDevTimeoutAccum);
+    uint32_t use = 0;
+    for (int t = blockIdx.x; t < args.total; t += gridDim.x) {
+      const Tile tl = decode_tile<BN, GROUPED>(args, t);
+      if (!tl.valid) continue;
+      const int a = use & 1;
+      const uint32_t aph = (use >> 1) & 1u;
+      if (!mbar_wait(&acc_full[a], aph, kDevTimeoutAccum)) break;
       tc_fence_after();
-    }
-    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    if (ok && nk > 0) {
-      if (EPI == MUK_EPI_SWIGLU) {
-        const int nout = N >> 1;
+      const int row = tl.row0 + quarter * 32 + lane;
+      const int64_t split_off = (int64_t)tl.split * args.split_stride;
+      const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * BN);
+      if (tl.nk == 0) {
+        if (EPI == MUK_EPI_F32) {  // empty split-K slice: its partial is zero
+          uint32_t z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0u;
+          for (int c = 0; c < BN / 32; ++c)
+            store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, tl.row_end, tl.n0 + c * 32,
+                                     args.N, z, nullptr);
+        }
+      } else if (EPI == MUK_EPI_SWIGLU) {
+        const int nout = args.N >> 1;
 #pragma unroll 1
         for (int grp = 0; grp < BN / 128; ++grp) {
 #pragma unroll 1
@@ -224,8 +286,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
-            store_chunk<MUK_EPI_BF16>(C, ldc, 0, row, row_end, (n0 >> 1) + grp * 64 + c * 32, nout,
-                                      gv, nullptr);
+            store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, tl.row_end,
+                                      (tl.n0 >> 1) + grp * 64 + c * 32, nout, gv, nullptr);
           }
         }
       } else {
@@ -234,16 +296,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(lane_addr + c * 32, v);
           tmem_ld_wait();
-          store_chunk<EPI>(C, ldc, split_off, row, row_end, n0 + c * 32, N, v, bias);
+          store_chunk<EPI>(C, args.ldc, split_off, row, tl.row_end, tl.n0 + c * 32, args.N, v,
+                           args.bias);
         }
       }
-    } else if (nk == 0 && EPI == MUK_EPI_F32) {
-      // Empty split-K slice: its partial is zero.
-      uint32_t z[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) z[j] = 0u;
-      for (int c = 0; c < BN / 32; ++c)
-        store_chunk<MUK_EPI_F32>(C, ldc, split_off, row, row_end, n0 + c * 32, N, z, nullptr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      ++use;
     }
   }
 
@@ -251,12 +311,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Host side: tensor maps and launch
+// Host side: tensor maps, tile shape choice and launch
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
@@ -296,16 +356,31 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t ld, int K, int ro
   return MUK_OK;
 }
 
-constexpr int kBN = 128;
-constexpr int kStages = 6;
+// SM count of the current device (cached per device).
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kNumSMs;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = kNumSMs;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
 
-template <int EPI, bool GROUPED>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int64_t ldc, int M,
-                       int N, int K, int split_k, int kt_per_split, int64_t split_stride,
-                       const float* bias, const int32_t* offsets, int num_experts, dim3 grid,
-                       cudaStream_t stream) {
-  using L = GemmLayout<kBN, kStages>;
-  auto kern = gemm_tc_kernel<kBN, kStages, EPI, GROUPED>;
+// Fraction of the last wave that does useful work, for `tiles` tiles on `sms` SMs.
+static double wave_eff(long tiles, int sms) {
+  const long waves = (tiles + sms - 1) / sms;
+  return (double)tiles / (double)(waves * sms);
+}
+
+template <int BN, int STAGES, int EPI, bool GROUPED>
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
+                  int sms, cudaStream_t stream) {
+  using L = GemmLayout<BN, STAGES>;
+  auto kern = gemm_persistent_kernel<BN, STAGES, EPI, GROUPED>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e =
@@ -316,34 +391,69 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, void* C, in
     }
     attr = true;
   }
-  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, ldc, M, N, K, kt_per_split,
-                                                   split_stride, bias, offsets, num_experts);
+  const int grid = a.total < sms ? a.total : sms;
+  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, a);
   return check_launch(GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16");
 }
 
-template <bool GROUPED>
+template <int BN, bool GROUPED>
 static int dispatch(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, void* C,
-                    int64_t ldc, int M, int N, int K, int split_k, int kt_per_split,
-                    int64_t split_stride, const float* bias, const int32_t* offsets,
-                    int num_experts, dim3 grid, cudaStream_t s) {
+                    const TileArgs& a, int sms, cudaStream_t s) {
+  constexpr int S = BN == 256 ? 4 : 6;
   switch (epilogue) {
     case MUK_EPI_BF16:
-      return launch_gemm<MUK_EPI_BF16, GROUPED>(ma, mb, C, ldc, M, N, K, split_k, kt_per_split,
-                                                split_stride, bias, offsets, num_experts, grid, s);
+      return launch<BN, S, MUK_EPI_BF16, GROUPED>(ma, mb, C, a, sms, s);
     case MUK_EPI_F32:
-      return launch_gemm<MUK_EPI_F32, GROUPED>(ma, mb, C, ldc, M, N, K, split_k, kt_per_split,
-                                               split_stride, bias, offsets, num_experts, grid, s);
+      return launch<BN, S, MUK_EPI_F32, GROUPED>(ma, mb, C, a, sms, s);
     case MUK_EPI_SWIGLU:
-      return launch_gemm<MUK_EPI_SWIGLU, GROUPED>(ma, mb, C, ldc, M, N, K, split_k, kt_per_split,
-                                                  split_stride, bias, offsets, num_experts, grid,
-                                                  s);
+      return launch<BN, S, MUK_EPI_SWIGLU, GROUPED>(ma, mb, C, a, sms, s);
     case MUK_EPI_BIAS_SILU:
-      return launch_gemm<MUK_EPI_BIAS_SILU, GROUPED>(ma, mb, C, ldc, M, N, K, split_k,
-                                                     kt_per_split, split_stride, bias, offsets,
-                                                     num_experts, grid, s);
+      return launch<BN, S, MUK_EPI_BIAS_SILU, GROUPED>(ma, mb, C, a, sms, s);
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
+}
+
+// BN = 256 halves the A traffic per flop; BN = 128 when N is small or when it
+// balances the last wave clearly better.
+static int pick_bn(long m_tiles, int N, int splits, int sms) {
+  if (N <= 128) return 128;
+  const long t256 = m_tiles * ((N + 255) / 256) * splits;
+  const long t128 = m_tiles * ((N + 127) / 128) * splits;
+  return wave_eff(t128, sms) > wave_eff(t256, sms) + 0.15 ? 128 : 256;
+}
+
+static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
+                    int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
+                    const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream) {
+  int rc = get_encode();
+  if (rc) return rc;
+  const int sms = sm_count();
+  const int bn = epilogue == MUK_EPI_SWIGLU ? (N % 256 == 0 ? 256 : 128)
+                                            : pick_bn(m_tiles, N, split_k, sms);
+  CUtensorMap ma, mb;
+  if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
+  if ((rc = make_map(&mb, B, ldb, K, grouped ? num_experts * N : N, bn))) return rc;
+  TileArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = m_tiles;
+  a.n_tiles = (N + bn - 1) / bn;
+  a.splits = split_k;
+  const int k_tiles = (K + kBK - 1) / kBK;
+  a.kt_per_split = (k_tiles + split_k - 1) / split_k;
+  a.total = a.m_tiles * a.n_tiles * split_k;
+  a.ldc = ldc;
+  a.split_stride = (int64_t)M * ldc;
+  a.bias = bias;
+  a.offsets = offsets;
+  a.num_experts = num_experts;
+  if (bn == 256)
+    return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
+                   : dispatch<256, false>(epilogue, ma, mb, C, a, sms, stream);
+  return grouped ? dispatch<128, true>(epilogue, ma, mb, C, a, sms, stream)
+                 : dispatch<128, false>(epilogue, ma, mb, C, a, sms, stream);
 }
 
 }  // namespace muk
@@ -367,16 +477,8 @@ extern "C" int muk_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t 
   const int nout = epilogue == MUK_EPI_SWIGLU ? N / 2 : N;
   MUK_REQUIRE(ldc >= nout, "muk_gemm_bf16: ldc=%lld < %d", (long long)ldc, nout);
   if (M == 0) return MUK_OK;
-  int rc = get_encode();
-  if (rc) return rc;
-  CUtensorMap ma, mb;
-  if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
-  if ((rc = make_map(&mb, B, ldb, K, N, kBN))) return rc;
-  const int k_tiles = (K + kBK - 1) / kBK;
-  const int kps = (k_tiles + split_k - 1) / split_k;
-  dim3 grid((M + kBM - 1) / kBM, (N + kBN - 1) / kBN, split_k);
-  return dispatch<false>(epilogue, ma, mb, C, ldc, M, N, K, split_k, kps, (int64_t)M * ldc, bias,
-                         nullptr, 0, grid, as_stream(stream));
+  return run_gemm(false, A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, bias, nullptr, 0,
+                  (M + kBM - 1) / kBM, as_stream(stream));
 }
 
 extern "C" int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
@@ -384,7 +486,7 @@ extern "C" int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, 
                                      int num_experts, int max_rows, int N, int K, int epilogue,
                                      void* stream) {
   MUK_REQUIRE(A && B && C && expert_offsets, "muk_grouped_gemm_bf16: null pointer");
-  MUK_REQUIRE(num_experts >= 1 && N > 0 && K > 0 && max_rows >= 0,
+  MUK_REQUIRE(num_experts >= 1 && num_experts <= 64 && N > 0 && K > 0 && max_rows >= 0,
               "muk_grouped_gemm_bf16: bad shape E=%d N=%d K=%d", num_experts, N, K);
   MUK_REQUIRE(lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 && MUK_ALIGNED16(A) &&
                   MUK_ALIGNED16(B),
@@ -393,15 +495,8 @@ extern "C" int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, 
               "muk_grouped_gemm_bf16: epilogue %d", epilogue);
   MUK_REQUIRE(epilogue != MUK_EPI_SWIGLU || N % 128 == 0, "muk_grouped_gemm_bf16: SWIGLU N%%128");
   if (max_rows == 0) return MUK_OK;
-  int rc = get_encode();
-  if (rc) return rc;
-  CUtensorMap ma, mb;
-  if ((rc = make_map(&ma, A, lda, K, max_rows, kBM))) return rc;
-  if ((rc = make_map(&mb, B, ldb, K, num_experts * N, kBN))) return rc;
-  const int k_tiles = (K + kBK - 1) / kBK;
   // Upper bound on (expert, row-tile) pairs: each expert adds at most one partial tile.
-  const int tiles = (max_rows + kBM - 1) / kBM + num_experts;
-  dim3 grid(tiles, (N + kBN - 1) / kBN, 1);
-  return dispatch<true>(epilogue, ma, mb, C, ldc, max_rows, N, K, 1, k_tiles, 0, nullptr,
-                        expert_offsets, num_experts, grid, as_stream(stream));
+  const int m_tiles = (max_rows + kBM - 1) / kBM + num_experts;
+  return run_gemm(true, A, lda, B, ldb, C, ldc, max_rows, N, K, epilogue, 1, nullptr,
+                  expert_offsets, num_experts, m_tiles, as_stream(stream));
 }

@@ -21,7 +21,8 @@ def _kern():
 
 
 # ----------------------------------------------------------------------------- GEMM
-@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (77, 300, 200), (256, 1024, 4096), (300, 256, 136)])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (77, 300, 200), (256, 1024, 4096), (300, 256, 136),
+                                   (1024, 8192, 512), (2000, 1152, 256)])
 def test_gemm_bf16_and_f32(cuda, M, N, K):
     k = _kern()
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
@@ -50,9 +51,10 @@ def test_gemm_split_k(cuda, split):
     torch.testing.assert_close(P.sum(0), ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
 
 
-def test_gemm_swiglu_and_bias_silu(cuda):
+@pytest.mark.parametrize("I", [256, 192, 1408])
+def test_gemm_swiglu_and_bias_silu(cuda, I):
     k = _kern()
-    M, I, K = 130, 256, 320
+    M, K = 130, 320
     g = torch.Generator(device="cuda").manual_seed(5)
     A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
     Wg = (torch.randn(I, K, device=cuda, generator=g) * 0.05).bfloat16()
@@ -306,6 +308,32 @@ def test_inl_dynamics_and_routing(cuda):
     top2 = logits.topk(2, -1).values
     clear = (top2[:, 0] - top2[:, 1]) > 1e-3
     assert torch.equal(eids[clear], ref_e[clear])
+
+
+def test_grouped_gemm_swiglu(cuda):
+    k = _kern()
+    E, I, K = 4, 192, 256
+    counts = [3, 150, 0, 40]
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + c)
+    R = offs[-1]
+    g = torch.Generator(device="cuda").manual_seed(12)
+    A = torch.randn(R, K, device=cuda, generator=g).bfloat16()
+    Wg = (torch.randn(E, I, K, device=cuda, generator=g) * 0.05).bfloat16()
+    Wu = (torch.randn(E, I, K, device=cuda, generator=g) * 0.05).bfloat16()
+    W = torch.cat([torch.stack([Wg[e].view(I // 64, 64, K), Wu[e].view(I // 64, 64, K)], 1)
+                   .reshape(2 * I, K) for e in range(E)], 0)
+    C = torch.zeros(R, I, device=cuda, dtype=torch.bfloat16)
+    k.grouped_gemm(A, W, C, torch.tensor(offs, device=cuda, dtype=torch.int32), E, 2 * I,
+                   k.MUK_EPI_SWIGLU)
+    for e in range(E):
+        lo, hi = offs[e], offs[e + 1]
+        if hi > lo:
+            ref = (torch.nn.functional.silu(A[lo:hi].float() @ Wg[e].float().t())
+                   * (A[lo:hi].float() @ Wu[e].float().t()))
+            torch.testing.assert_close(C[lo:hi].float(), ref, rtol=2e-2,
+                                       atol=2e-2 * ref.abs().max().item())
 
 
 def test_route_permute_and_gather(cuda):
