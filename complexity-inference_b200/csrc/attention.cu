@@ -27,10 +27,28 @@
 
 namespace muk {
 
-constexpr int kBlockSize = 16;       // tokens per paged block (the only supported size)
-constexpr int kDecWarps = 4;
-constexpr int kDecStages = 3;        // cp.async ring depth per warp
-constexpr int kMinSplitBlocks = 16;  // >= 256 tokens per decode split
+#ifndef MUK_DEC_WARPS
+#define MUK_DEC_WARPS 4
+#endif
+#ifndef MUK_DEC_STAGES
+#define MUK_DEC_STAGES 3
+#endif
+#ifndef MUK_DEC_MIN_SPLIT
+#define MUK_DEC_MIN_SPLIT 16
+#endif
+#ifndef MUK_DEC_MAX_SPLIT
+#define MUK_DEC_MAX_SPLIT 64
+#endif
+#ifndef MUK_DEC_SPLIT_DIV
+#define MUK_DEC_SPLIT_DIV 64
+#endif
+
+constexpr int kBlockSize = 16;                        // tokens per paged block (only size)
+constexpr int kDecWarps = MUK_DEC_WARPS;              // warps per CTA
+constexpr int kDecStages = MUK_DEC_STAGES;            // cp.async ring depth per warp
+constexpr int kMinSplitBlocks = MUK_DEC_MIN_SPLIT;    // blocks per split, lower bound
+constexpr int kMaxSplitBlocks = MUK_DEC_MAX_SPLIT;    // ... and upper bound
+constexpr int kSplitDiv = MUK_DEC_SPLIT_DIV;          // batch blocks per split-size unit
 constexpr int kMaxSplits = 128;
 
 // Byte offset of 16-byte chunk `c` of row `r` in a [rows][D] bf16 tile with
@@ -486,9 +504,15 @@ struct DecodeSplit {
   int max_splits;
 };
 
-static DecodeSplit decode_split_policy(int max_seq_len) {
+// Blocks per split grow with the batch (num_seqs x max_blocks): large batches
+// already fill the GPU, so longer splits cut the per-split fixed cost and the
+// merge traffic; small batches keep short splits for parallelism.
+static DecodeSplit decode_split_policy(int max_seq_len, int num_seqs) {
   const int max_blocks = (max_seq_len + kBlockSize - 1) / kBlockSize;
+  long want = ((long)num_seqs * max_blocks) / kSplitDiv;
+  if (want > kMaxSplitBlocks) want = kMaxSplitBlocks;
   int bps = (max_blocks + kMaxSplits - 1) / kMaxSplits;
+  if (bps < want) bps = (int)want;
   if (bps < kMinSplitBlocks) bps = kMinSplitBlocks;
   DecodeSplit p;
   p.blocks_per_split = bps;
@@ -515,7 +539,7 @@ using namespace muk;
 extern "C" size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, int head_dim,
                                                  int max_seq_len, int block_size) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || block_size != kBlockSize) return 0;
-  DecodeSplit p = decode_split_policy(max_seq_len);
+  DecodeSplit p = decode_split_policy(max_seq_len, num_seqs);
   if (p.max_splits <= 1) return 0;
   const size_t rows = (size_t)num_seqs * num_q_heads * p.max_splits;
   return rows * ((size_t)head_dim + 2) * sizeof(float);
@@ -527,7 +551,7 @@ static int launch_decode(const void* q, int64_t q_stride, void* out, int64_t out
                          int bt_stride, const int32_t* seq_lens, int num_seqs, int num_q_heads,
                          int num_kv_heads, int num_blocks, float scale, int max_seq_len,
                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const DecodeSplit p = decode_split_policy(max_seq_len);
+  const DecodeSplit p = decode_split_policy(max_seq_len, num_seqs);
   float* part_o = nullptr;
   float* part_ml = nullptr;
   if (p.max_splits > 1) {
