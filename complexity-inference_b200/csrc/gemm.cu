@@ -43,6 +43,11 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
 constexpr int kNumSMs = 148;
+#ifdef MUK_NO_PAIR
+static bool g_pair_enabled = false;
+#else
+static bool g_pair_enabled = true;
+#endif
 
 template <int BN, int STAGES>
 struct GemmLayout {
@@ -315,6 +320,211 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (dense only): a cluster of 2 CTAs computes 256 x 256 output
+// tiles with tcgen05.mma.cta_group::2 (M = 256).  Each CTA stages its own 128
+// rows of A and its half (128 rows) of the B tile, so per CTA a k-tile moves
+// 32 KB instead of 48 KB for a 128 x 256 tile: a third less L2 traffic per
+// flop.  The even CTA issues the MMAs; both CTAs' TMA loads complete on its
+// `full` barriers (loads carry .cta_group::2, no multicast); its commits arrive
+// on the `empty` / `acc_full` barriers of both CTAs; both epilogues release the
+// accumulator on its `acc_empty`.  Each CTA's TMEM holds its 128 rows.
+// ---------------------------------------------------------------------------
+constexpr int kPairBN = 256;
+constexpr int kPairStages = 6;
+
+struct PairLayout {
+  static constexpr int kA = kBM * kBK * 2;             // 16 KB: this CTA's 128 rows of A
+  static constexpr int kB = (kPairBN / 2) * kBK * 2;   // 16 KB: this CTA's half of B
+  static constexpr int kStage = kA + kB;
+  static constexpr int kBarOff = kPairStages * kStage;
+  static constexpr int kBytes = kBarOff + (2 * kPairStages + 4) * 8 + 16 + 1024;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
+                     const TileArgs args) {
+  using L = PairLayout;
+  constexpr int BN = kPairBN;
+  constexpr int S = kPairStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* basep = smem_raw + (base - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(basep + L::kBarOff);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;    // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2], used in the leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < args.total && ok; t += npairs) {
+        const int mt = t % args.m_tiles, rest = t / args.m_tiles;
+        const int nt = rest % args.n_tiles, split = rest / args.n_tiles;
+        const int k_tiles = (args.K + kBK - 1) / kBK;
+        const int kt0 = split * args.kt_per_split;
+        const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
+        const int arow = mt * 256 + (int)rank * kBM;
+        const int brow = nt * BN + (int)rank * (BN / 2);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)L::kStage);
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
+          tma_load_2d_pair(sa, &tmA, &full[s], (kt0 + i) * kBK, arow);
+          tma_load_2d_pair(sa + L::kA, &tmB, &full[s], (kt0 + i) * kBK, brow);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
+      uint32_t it = 0, use = 0;
+      bool ok = true;
+      for (int t = pair; t < args.total && ok; t += npairs) {
+        const int rest = t / args.m_tiles;
+        const int split = rest / args.n_tiles;
+        const int k_tiles = (args.K + kBK - 1) / kBK;
+        const int kt0 = split * args.kt_per_split;
+        const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
+        const int a = use & 1;
+        const uint32_t aph = (use >> 1) & 1u;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1u, kDevTimeoutAccum)) break;
+        tc_fence_after();
+        const uint32_t dacc = tmem + (uint32_t)(a * BN);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(sa + k * 32);
+            const uint64_t bd = umma_desc_sw128(sa + L::kA + k * 32);
+            tc_mma_f16_pair(dacc, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit_pair(&acc_full[a]);
+        ++use;
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    uint32_t use = 0;
+    for (int t = pair; t < args.total; t += npairs) {
+      const int mt = t % args.m_tiles, rest = t / args.m_tiles;
+      const int nt = rest % args.n_tiles, split = rest / args.n_tiles;
+      const int k_tiles = (args.K + kBK - 1) / kBK;
+      const int kt0 = split * args.kt_per_split;
+      const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
+      const int a = use & 1;
+      const uint32_t aph = (use >> 1) & 1u;
+      if (!mbar_wait(&acc_full[a], aph, kDevTimeoutAccum)) break;
+      tc_fence_after();
+      const int row = mt * 256 + (int)rank * kBM + quarter * 32 + lane;
+      const int n0 = nt * BN;
+      const int64_t split_off = (int64_t)split * args.split_stride;
+      const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * BN);
+      if (nk == 0) {
+        if (EPI == MUK_EPI_F32) {
+          uint32_t z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0u;
+          for (int c = 0; c < BN / 32; ++c)
+            store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, args.M, n0 + c * 32, args.N, z,
+                                     nullptr);
+        }
+      } else if (EPI == MUK_EPI_SWIGLU) {
+        const int nout = args.N >> 1;
+#pragma unroll 1
+        for (int grp = 0; grp < BN / 128; ++grp) {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t gv[32], uv[32];
+            tmem_ld_32x32b_x32(lane_addr + grp * 128 + c * 32, gv);
+            tmem_ld_32x32b_x32(lane_addr + grp * 128 + 64 + c * 32, uv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
+            store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, args.M, (n0 >> 1) + grp * 64 + c * 32,
+                                      nout, gv, nullptr);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+          tmem_ld_wait();
+          store_chunk<EPI>(C, args.ldc, split_off, row, args.M, n0 + c * 32, args.N, v, args.bias);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&acc_empty[a]);
+      ++use;
+    }
+  }
+
+  // Neither CTA may leave while its peer can still touch its shared memory
+  // (MMA operand reads, remote arrivals) or its TMEM.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * BN);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side: tensor maps, tile shape choice and launch
 // ---------------------------------------------------------------------------
@@ -376,6 +586,66 @@ static double wave_eff(long tiles, int sms) {
   return (double)tiles / (double)(waves * sms);
 }
 
+
+// ---------------------------------------------------------------------------
+// Shape planner: pick the kernel (single CTA with BN 128/256, or CTA pair with
+// 256 x 256 tiles) and the split-K factor with the shortest estimated
+// makespan: ceil(tiles / workers) x (k-tiles per tile + pipeline fill) x the
+// per-k-tile cost of that tile shape on one SM.  Each extra split pays for
+// writing and re-reading an M x N f32 partial, which relative to the GEMM's
+// tensor time is about 860 / K (HBM ~6.5 TB/s vs ~1.4 PFLOP/s).
+// ---------------------------------------------------------------------------
+struct GemmPlan {
+  int kind;   // 0: single CTA, 1: CTA pair
+  int bn;     // 128 or 256
+  int split;
+};
+
+static double plan_cost(int kind, int bn, int split, int M, int N, int K, int sms) {
+  const int k_tiles = (K + kBK - 1) / kBK;
+  const int kps = (k_tiles + split - 1) / split;
+  long tiles;
+  int workers;
+  double per_k;
+  if (kind == 1) {
+    tiles = (long)((M + 255) / 256) * ((N + 255) / 256) * split;
+    workers = sms / 2;
+    per_k = 0.88;  // measured: pair tiles run ~1.13x faster per SM than 128 x 256
+  } else {
+    tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn) * split;
+    workers = sms;
+    per_k = bn == 256 ? 1.0 : 0.70;  // measured: a 128 x 128 tile costs ~0.7 of 128 x 256
+  }
+  const long rounds = (tiles + workers - 1) / workers;
+  return (double)rounds * (kps + 3) * per_k * (1.0 + (0.03 + 860.0 / K) * (split - 1));
+}
+
+static GemmPlan plan_gemm(int M, int N, int K, int epilogue, int max_split, int sms) {
+  GemmPlan best = {0, 256, 1};
+  double best_cost = 1e300;
+  const bool swiglu = epilogue == MUK_EPI_SWIGLU;
+  const int smax = epilogue == MUK_EPI_F32 ? max_split : 1;
+  for (int split = 1; split <= smax; ++split) {
+    for (int bn : {256, 128}) {
+      if (bn == 256 && swiglu && N % 256 != 0) continue;
+      if (bn == 256 && N <= 128) continue;
+      const double c = plan_cost(0, bn, split, M, N, K, sms);
+      if (c < best_cost * 0.999) {
+        best_cost = c;
+        best = {0, bn, split};
+      }
+    }
+    if (g_pair_enabled && M > 128 && N >= 256 && !(swiglu && N % 256 != 0)) {
+      const double c = plan_cost(1, 256, split, M, N, K, sms);
+      if (c < best_cost * 0.999) {
+        best_cost = c;
+        best = {1, 256, split};
+      }
+    }
+  }
+  return best;
+}
+
 template <int BN, int STAGES, int EPI, bool GROUPED>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
                   int sms, cudaStream_t stream) {
@@ -423,14 +693,115 @@ static int pick_bn(long m_tiles, int N, int splits, int sms) {
   return wave_eff(t128, sms) > wave_eff(t256, sms) + 0.15 ? 128 : 256;
 }
 
+template <int EPI>
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
+                       int sms, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<EPI>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PairLayout::kBytes);
+    if (e != cudaSuccess) {
+      set_last_error("gemm(pair): cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return MUK_ERR_CUDA;
+    }
+    attr = true;
+  }
+  int pairs = sms / 2;
+  if (a.total < pairs) pairs = a.total;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairLayout::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, C, a);
+  if (e != cudaSuccess) {
+    set_last_error("muk_gemm_bf16(pair): launch failed: %s", cudaGetErrorString(e));
+    return MUK_ERR_CUDA;
+  }
+  return check_launch("muk_gemm_bf16(pair)");
+}
+
+static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
+                         int64_t ldc, int M, int N, int K, int epilogue, int split_k,
+                         const float* bias, int sms, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
+  if ((rc = make_map(&mb, B, ldb, K, N, kPairBN / 2))) return rc;
+  TileArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = (M + 255) / 256;
+  a.n_tiles = (N + kPairBN - 1) / kPairBN;
+  a.splits = split_k;
+  const int k_tiles = (K + kBK - 1) / kBK;
+  a.kt_per_split = (k_tiles + split_k - 1) / split_k;
+  a.total = a.m_tiles * a.n_tiles * split_k;
+  a.ldc = ldc;
+  a.split_stride = (int64_t)M * ldc;
+  a.bias = bias;
+  a.offsets = nullptr;
+  a.num_experts = 0;
+  switch (epilogue) {
+    case MUK_EPI_BF16:
+      return launch_pair<MUK_EPI_BF16>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_F32:
+      return launch_pair<MUK_EPI_F32>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_SWIGLU:
+      return launch_pair<MUK_EPI_SWIGLU>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_BIAS_SILU:
+      return launch_pair<MUK_EPI_BIAS_SILU>(ma, mb, C, a, sms, stream);
+  }
+  set_last_error("gemm: unknown epilogue %d", epilogue);
+  return MUK_ERR_INVALID_ARG;
+}
+
+// Pairs pay off once both CTAs of a pair have rows to work on and N fills
+// 256-wide tiles (SwiGLU needs N % 256 for its 128-row gate/up groups).
+static bool use_pair(int M, int N, int epilogue) {
+  if (M <= 128 || N < 256) return false;
+  if (epilogue == MUK_EPI_SWIGLU && N % 256 != 0) return false;
+  return true;
+}
+
 static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
                     const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream) {
   int rc = get_encode();
   if (rc) return rc;
   const int sms = sm_count();
-  const int bn = epilogue == MUK_EPI_SWIGLU ? (N % 256 == 0 ? 256 : 128)
-                                            : pick_bn(m_tiles, N, split_k, sms);
+  int bn;
+  if (!grouped) {
+    // the caller fixed split_k; choose the kernel and tile width for it
+    GemmPlan best = {0, 256, split_k};
+    double best_cost = 1e300;
+    for (int kind = 0; kind < 2; ++kind)
+      for (int b : {256, 128}) {
+        if (kind == 1 && (b != 256 || !g_pair_enabled || !use_pair(M, N, epilogue))) continue;
+        if (kind == 0 && b == 256 && ((epilogue == MUK_EPI_SWIGLU && N % 256) || N <= 128))
+          continue;
+        const double c = plan_cost(kind, b, split_k, M, N, K, sms);
+        if (c < best_cost * 0.999) {
+          best_cost = c;
+          best = {kind, b, split_k};
+        }
+      }
+    if (best.kind == 1)
+      return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, bias, sms, stream);
+    bn = best.bn;
+  } else {
+    bn = epilogue == MUK_EPI_SWIGLU ? (N % 256 == 0 ? 256 : 128)
+                                    : pick_bn(m_tiles, N, split_k, sms);
+  }
   CUtensorMap ma, mb;
   if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
   if ((rc = make_map(&mb, B, ldb, K, grouped ? num_experts * N : N, bn))) return rc;
@@ -499,4 +870,9 @@ extern "C" int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, 
   const int m_tiles = (max_rows + kBM - 1) / kBM + num_experts;
   return run_gemm(true, A, lda, B, ldb, C, ldc, max_rows, N, K, epilogue, 1, nullptr,
                   expert_offsets, num_experts, m_tiles, as_stream(stream));
+}
+
+extern "C" int muk_gemm_plan_split(int M, int N, int K, int epilogue, int max_split) {
+  if (M <= 0 || N <= 0 || K <= 0 || max_split < 1) return 1;
+  return plan_gemm(M, N, K, epilogue, max_split, sm_count()).split;
 }

@@ -60,15 +60,14 @@ def pad_cols(w: torch.Tensor, cols: int) -> torch.Tensor:
     return out
 
 
-def choose_split(M: int, N: int, K: int, max_rows: int, sms: int = 148) -> int:
-    """Split-K factor that fills the SMs when M x N has few 128x128 tiles."""
-    tiles = ((M + 127) // 128) * ((N + 127) // 128)
-    if tiles >= sms * 0.8:
-        return 1
-    s = min(-(-sms // tiles), max(1, ((K + 63) // 64) // 4), 16)
-    while s > 1 and s * M > max_rows:
-        s -= 1
-    return max(1, s)
+def choose_split(M: int, N: int, K: int, max_rows: int) -> int:
+    """Split-K factor for an f32-partial GEMM, from libmuk's shape planner
+    (the same model the launcher uses to pick tile shapes), bounded so the
+    partials fit ``max_rows`` rows of the workspace."""
+    from .. import _lib
+
+    max_s = max(1, min(16, max_rows // max(M, 1)))
+    return int(_lib.load().muk_gemm_plan_split(M, N, K, _lib.MUK_EPI_F32, max_s))
 
 
 class Workspace:

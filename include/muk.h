@@ -174,6 +174,12 @@ int muk_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
                   int M, int N, int K, int epilogue, int split_k, const float* bias,
                   void* stream);
 
+/* Split-K factor (1..max_split) that muk_gemm_bf16 runs fastest for this
+ * shape with MUK_EPI_F32 (1 for other epilogues): the same makespan model the
+ * launcher uses to choose between 128/256-wide single-CTA tiles and CTA-pair
+ * 256 x 256 tiles.  Callers size their partial buffers from it. */
+int muk_gemm_plan_split(int M, int N, int K, int epilogue, int max_split);
+
 /* ---- K4: token-routed experts -------------------------------------------- */
 
 /* Stable counting sort of tokens by expert id.  expert_offsets[E+1] (prefix
