@@ -117,6 +117,7 @@ class MuModelBase:
         self.rope_cos: Optional[torch.Tensor] = None
         self.rope_sin: Optional[torch.Tensor] = None
         self._rope_len = 0
+        self.tp_group = None   # torch.distributed group when tensor-parallel
         self.ensure_rope(max(config.max_position_embeddings, 16))
 
     # ---- overridable sizes ---------------------------------------------------
@@ -158,6 +159,13 @@ class MuModelBase:
         return True
 
     # ---- shared pieces of the step ---------------------------------------------
+    def reduce_partials(self, part: torch.Tensor) -> None:
+        """Sum a row-parallel projection's partial output over the TP ranks (NCCL)."""
+        if self.tp_group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(part, group=self.tp_group)
+
     def attention(self, layer: int, batch, cache, q_norm_w=None, k_norm_w=None) -> torch.Tensor:
         """RoPE + KV append, then paged decode / varlen prefill attention -> ws.attn."""
         cfg, ws = self.config, self.ws

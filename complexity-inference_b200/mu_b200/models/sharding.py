@@ -1,0 +1,84 @@
+"""Tensor-parallel sharding of the reference state dict.
+
+Rank r of P keeps:
+* attention: query heads [r·Hq/P, (r+1)·Hq/P) and KV heads [r·Hkv/P, ...)
+  — rows of q/k/v_proj and mu_to_q/k/v (column-parallel), the matching
+  input columns of o_proj (row-parallel); QK-norm weights are per head-dim
+  and replicated;
+* MLP: rows [r·I/P, (r+1)·I/P) of gate/up (column-parallel) and those
+  columns of down (row-parallel); for token-routed experts the same split is
+  applied inside every expert ([E, H, 2I] / [E, I, H] keep E whole);
+* everything else (embeddings, norms, LM head, INL dynamics, router) whole.
+
+After a row-parallel projection each rank holds a partial sum of the full
+[T, H] output; one all-reduce per projection (two per layer) restores it, so
+all ranks carry identical residual streams and sample identical tokens.
+The shard has the same names as the full dict and a ModelConfig whose head
+and intermediate counts are the local ones.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Dict, Tuple
+
+import torch
+
+from ..core.config import ModelConfig
+from .weights import expert_intermediate, is_routed
+
+
+def local_config(cfg: ModelConfig, arch: str, tp: int) -> ModelConfig:
+    Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    if Hq % tp or Hkv % tp:
+        raise ValueError(f"tensor_parallel_size {tp} must divide heads {Hq}/{Hkv}")
+    if is_routed(arch, cfg):
+        ie = expert_intermediate(cfg)
+        if ie % tp:
+            raise ValueError(f"tensor_parallel_size {tp} must divide the expert width {ie}")
+        inter = cfg.intermediate_size // tp
+    else:
+        if cfg.intermediate_size % tp:
+            raise ValueError(f"tensor_parallel_size {tp} must divide {cfg.intermediate_size}")
+        inter = cfg.intermediate_size // tp
+    return dataclasses.replace(cfg, num_attention_heads=Hq // tp, num_key_value_heads=Hkv // tp,
+                               intermediate_size=inter, head_dim=cfg.head_dim)
+
+
+def shard_state_dict(sd: Dict[str, torch.Tensor], cfg: ModelConfig, arch: str, rank: int,
+                     tp: int) -> Tuple[Dict[str, torch.Tensor], ModelConfig]:
+    """The rank's shard of a full state dict plus its local ModelConfig."""
+    if tp == 1:
+        return dict(sd), cfg
+    D = cfg.head_dim
+    hq = cfg.num_attention_heads // tp
+    hkv = cfg.num_key_value_heads // tp
+    q0, k0 = rank * hq * D, rank * hkv * D
+    out: Dict[str, torch.Tensor] = {}
+    routed = is_routed(arch, cfg)
+    if routed:
+        ie = expert_intermediate(cfg)
+        il = ie // tp
+    else:
+        il = cfg.intermediate_size // tp
+    i0 = rank * il
+    for name, t in sd.items():
+        leaf = name.split(".", 2)[-1] if name.startswith("layers.") else name
+        if leaf in ("self_attn.q_proj.weight", "self_attn.mu_to_q.weight"):
+            out[name] = t[q0:q0 + hq * D]
+        elif leaf in ("self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                      "self_attn.mu_to_k.weight", "self_attn.mu_to_v.weight"):
+            out[name] = t[k0:k0 + hkv * D]
+        elif leaf == "self_attn.o_proj.weight":
+            out[name] = t[:, q0:q0 + hq * D]
+        elif leaf in ("mlp.gate_proj.weight", "mlp.up_proj.weight"):
+            out[name] = t[i0:i0 + il]
+        elif leaf == "mlp.down_proj.weight" and not routed:
+            out[name] = t[:, i0:i0 + il]
+        elif leaf == "mlp.gate_up_proj":   # [E, H, 2I]: gate cols [0, I), up cols [I, 2I)
+            out[name] = torch.cat([t[:, :, i0:i0 + il], t[:, :, ie + i0:ie + i0 + il]], 2)
+        elif leaf == "mlp.down_proj" and routed:   # [E, I, H]
+            out[name] = t[:, i0:i0 + il, :]
+        else:
+            out[name] = t
+    return {k: v.contiguous() for k, v in out.items()}, local_config(cfg, arch, tp)

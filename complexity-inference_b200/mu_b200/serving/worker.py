@@ -77,8 +77,11 @@ class WorkerOutput:
 
 
 class MuWorker:
-    def __init__(self, config: EngineConfig, device: str = "cuda"):
+    def __init__(self, config: EngineConfig, device: str = "cuda", tp_group=None):
+        """``tp_group``: torch.distributed group of the tensor-parallel ranks
+        (defaults to the world group when config.tensor_parallel_size > 1)."""
         self.config = config
+        self.tp_group = tp_group
         self.device = torch.device(device)
         self.model = None
         self.cache: Optional[PagedKVCache] = None
@@ -101,12 +104,31 @@ class MuWorker:
         self.load_state_dict(arch, mcfg, load_state_dict(model_path))
 
     def load_state_dict(self, arch: str, model_config: ModelConfig, sd) -> None:
+        """Build the model from a full state dict (sharded here when tensor-parallel)."""
         self.config.model = model_config
-        self.model = build_model(arch, model_config, sd, self.config.mu, str(self.device))
+        tp = int(self.config.tensor_parallel_size or 1)
+        local = model_config
+        if tp > 1:
+            import torch.distributed as dist
+
+            from ..models.sharding import shard_state_dict
+
+            if not dist.is_initialized():
+                raise RuntimeError("tensor_parallel_size > 1 needs torch.distributed initialised")
+            group = self.tp_group
+            if dist.get_world_size(group) != tp:
+                raise RuntimeError(f"tensor_parallel_size {tp} != group size "
+                                   f"{dist.get_world_size(group)}")
+            sd, local = shard_state_dict(sd, model_config, arch, dist.get_rank(group), tp)
+        self.model = build_model(arch, local, sd, self.config.mu, str(self.device))
+        if tp > 1:
+            import torch.distributed as dist
+
+            self.model.tp_group = self.tp_group or dist.group.WORLD
         self._init_cache()
 
     def _init_cache(self) -> None:
-        mc, cc, sc = self.config.model, self.config.cache, self.config.scheduler
+        mc, cc, sc = self.model.config, self.config.cache, self.config.scheduler
         nblocks = cc.num_gpu_blocks or cc.max_num_blocks
         self.cache = PagedKVCache(mc.num_hidden_layers, mc.num_key_value_heads, mc.head_dim,
                                   cc.block_size, nblocks, torch.bfloat16, str(self.device),

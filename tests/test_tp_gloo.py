@@ -1,0 +1,160 @@
+"""Tensor-parallel sharding on CPU: gloo ranks, oracle math.
+
+Two processes each take their shard of the tiny fixtures' weights
+(mu_b200.models.sharding) and run the oracle's layer math on it; after each
+row-parallel projection (O and down) they all-reduce the partial outputs
+over gloo, exactly where the GPU model calls NCCL.  The result must equal the
+unsharded oracle forward, and the shards must recombine to the full weights.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import mu_oracle as O
+from golden_models import load_tiny
+from mu_b200.models.sharding import shard_state_dict
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _allreduce(x):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    dist.all_reduce(t)
+    return t.numpy()
+
+
+def _tp_forward(model: O.OracleModel, ids):
+    """Prefill-only forward of a sharded OracleModel with all-reduces."""
+    s, p, mu = model.s, model.p, model.mu
+    ids = np.asarray(ids)
+    h = O._clamp(p["embed_tokens.weight"][ids].astype(np.float32), mu)
+    v_state, mu_prev = None, None
+    for l in range(s.layers):
+        pre = f"layers.{l}."
+        res = h
+        x = O.rmsnorm(h, p[pre + "input_layernorm.weight"], s.eps, mu)
+        # attention on the local heads; o_proj gives a partial sum
+        a = pre + "self_attn."
+        S = x.shape[0]
+        q = x @ p[a + "q_proj.weight"].T
+        k = x @ p[a + "k_proj.weight"].T
+        v = x @ p[a + "v_proj.weight"].T
+        if s.arch == "deep" and mu_prev is not None:
+            q = q + mu_prev @ p[a + "mu_to_q.weight"].T
+            k = k + mu_prev @ p[a + "mu_to_k.weight"].T
+            v = v + mu_prev @ p[a + "mu_to_v.weight"].T
+        q = q.reshape(S, s.heads, s.head_dim).astype(np.float32)
+        k = k.reshape(S, s.kv_heads, s.head_dim).astype(np.float32)
+        v = v.reshape(S, s.kv_heads, s.head_dim).astype(np.float32)
+        if s.qk_norm:
+            q = O.rmsnorm(q, p[a + "q_norm.weight"], 1e-6)
+            k = O.rmsnorm(k, p[a + "k_norm.weight"], 1e-6)
+        pos = np.arange(S)
+        q = O.apply_rope(q, model.cos, model.sin, pos)
+        k = O.apply_rope(k, model.cos, model.sin, pos)
+        o = O.sdpa(q.transpose(1, 0, 2), k.transpose(1, 0, 2), v.transpose(1, 0, 2), True)
+        o = o.transpose(1, 0, 2).reshape(S, -1)
+        attn = O._clamp(_allreduce(o @ p[a + "o_proj.weight"].T), mu)
+        if s.arch == "deep":
+            h_next, v_state, mu_cur = O.inl_dynamics(attn, v_state, p, pre + "dynamics.", s.dt)
+            h = res + h_next
+            res = h
+            x2 = O.rmsnorm(h, p[pre + "post_attention_layernorm.weight"], s.eps, mu)
+            e = O.route_experts(ids, mu_cur, p[pre + "mlp.mu_router.weight"], s.experts, s.vocab)
+            gu, dn = p[pre + "mlp.gate_up_proj"], p[pre + "mlp.down_proj"]
+            I = dn.shape[1]
+            part = np.stack([(O._silu(x2[t] @ gu[e[t]][:, :I]) * (x2[t] @ gu[e[t]][:, I:])) @ dn[e[t]]
+                             for t in range(S)])
+            h = O._clamp(res + O._clamp(_allreduce(part), mu), mu)
+            mu_prev = mu_cur
+        else:
+            h = res + attn
+            res = h
+            x2 = O.rmsnorm(h, p[pre + "post_attention_layernorm.weight"], s.eps, mu)
+            m = pre + "mlp."
+            part = (O._silu(x2 @ p[m + "gate_proj.weight"].T) * (x2 @ p[m + "up_proj.weight"].T)
+                    ) @ p[m + "down_proj.weight"].T
+            h = O._clamp(res + O._clamp(_allreduce(part), mu), mu)
+    hn = O.rmsnorm(h, p["norm.weight"], s.eps, mu)
+    return (hn[-1] @ p["lm_head.weight"].T).astype(np.float32)
+
+
+def _worker(rank, world, port, name, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, f"init failed: {e!r}"))
+        return
+    try:
+        shape, cfg, sd, d, prompts = load_tiny(name)
+        shard, local = shard_state_dict(sd, cfg, shape.arch, rank, world)
+        lshape = O.ModelShape(shape.arch, shape.hidden, shape.layers, local.num_attention_heads,
+                              local.num_key_value_heads, shape.head_dim, shape.vocab,
+                              experts=shape.experts, qk_norm=shape.qk_norm)
+        model = O.OracleModel(lshape, {k: v.numpy() for k, v in shard.items()}, O.MuCfg(True))
+        logits = _tp_forward(model, prompts[0])
+        q.put((rank, logits))
+    except Exception as e:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+def test_tp2_matches_unsharded(name):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for r in range(world):
+        assert not isinstance(got[r], str), got[r]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    shape, cfg, sd, d, prompts = load_tiny(name)
+    full = O.OracleModel(shape, {k: v.numpy() for k, v in sd.items()}, O.MuCfg(True))
+    ref, _ = full.forward(prompts[0])
+    for r in range(world):
+        np.testing.assert_allclose(got[r], ref, rtol=1e-4, atol=1e-4)
+    assert np.array_equal(got[0], got[1])  # every rank holds the same logits
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+def test_shards_recombine(name):
+    shape, cfg, sd, d, prompts = load_tiny(name)
+    tp = 2
+    shards = [shard_state_dict(sd, cfg, shape.arch, r, tp)[0] for r in range(tp)]
+    a = "layers.0.self_attn."
+    assert torch.equal(torch.cat([s[a + "q_proj.weight"] for s in shards]), sd[a + "q_proj.weight"])
+    assert torch.equal(torch.cat([s[a + "o_proj.weight"] for s in shards], 1), sd[a + "o_proj.weight"])
+    if shape.arch == "deep":
+        gu = sd["layers.0.mlp.gate_up_proj"]
+        I = gu.shape[2] // 2
+        g = torch.cat([s["layers.0.mlp.gate_up_proj"][:, :, : I // tp] for s in shards], 2)
+        assert torch.equal(g, gu[:, :, :I])
+        dn = torch.cat([s["layers.0.mlp.down_proj"] for s in shards], 1)
+        assert torch.equal(dn, sd["layers.0.mlp.down_proj"])
+    else:
+        dn = torch.cat([s["layers.0.mlp.down_proj.weight"] for s in shards], 1)
+        assert torch.equal(dn, sd["layers.0.mlp.down_proj.weight"])
+    assert torch.equal(shards[1]["embed_tokens.weight"], sd["embed_tokens.weight"])
