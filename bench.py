@@ -154,7 +154,7 @@ class Arrivals:
         return engine.add_request(prompt, sp, f"q{self.n}")
 
 
-def build(rank: int):
+def build(rank: int, tp: int = 1):
     from mu_b200.core.config import CacheConfig, EngineConfig, SchedulerConfig
     from mu_b200.models.weights import random_state_dict
     from mu_b200.serving.engine import StepEngine
@@ -164,7 +164,7 @@ def build(rank: int):
     max_len = PROMPT_MAX + OUT_TOKENS + 16
     # expected KV ~ 256 x ~830 tokens; keep 3x headroom for bursts of long prompts
     blocks = 45000
-    ec = EngineConfig(model=cfg, dtype="bfloat16",
+    ec = EngineConfig(model=cfg, dtype="bfloat16", tensor_parallel_size=tp,
                       cache=CacheConfig(max_seq_len=max_len, block_size=16, max_num_blocks=blocks,
                                         max_num_seqs=CONCURRENCY),
                       scheduler=SchedulerConfig(max_batch_size=CONCURRENCY,
@@ -370,6 +370,15 @@ def run_reference_arm(args, rank, world):
     return 0
 
 
+def release(worker):
+    """Drop captured CUDA graphs (they may hold NCCL calls) before the process group goes."""
+    import gc
+
+    worker._graphs.clear()
+    gc.collect()
+    torch.cuda.synchronize()
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     from mu_b200 import _lib
@@ -377,9 +386,12 @@ def run_ours(args, rank, world, local_rank):
     from mu_b200.core.config import SamplingParams
 
     torch.cuda.set_device(local_rank)
-    engine, worker, ec = build(rank)
-    arrivals = Arrivals(1000 + rank, C3["vocab"])
-    rng = np.random.default_rng(7 + rank)
+    tp = world if args.parallel == "tp" else 1
+    engine, worker, ec = build(rank, tp)
+    # tensor-parallel ranks serve the same requests; replicas serve their own
+    seed_rank = 0 if tp > 1 else rank
+    arrivals = Arrivals(1000 + seed_rank, C3["vocab"])
+    rng = np.random.default_rng(7 + seed_rank)
     for _ in range(CONCURRENCY):
         arrivals.new_request(engine, SamplingParams, already=int(rng.integers(0, OUT_TOKENS)))
     # initial fill: prefill every starting request (untimed)
@@ -452,12 +464,14 @@ def run_ours(args, rank, world, local_rank):
     vals = torch.tensor([n_tok, dev_t, e2e_t, wall], device="cuda", dtype=torch.float64)
     if world > 1:
         tot = vals.clone()
-        dist.all_reduce(tot[:1], op=dist.ReduceOp.SUM)
+        if tp == 1:  # replicas: tokens add up; tensor-parallel ranks produce the same tokens
+            dist.all_reduce(tot[:1], op=dist.ReduceOp.SUM)
         mx = vals.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         n_all, dev_max, e2e_max, wall_max = float(tot[0]), float(mx[1]), float(mx[2]), float(mx[3])
     else:
         n_all, dev_max, e2e_max, wall_max = n_tok, dev_t, e2e_t, wall
+    release(worker)
     if rank != 0:
         return 0
     cpu = None
@@ -477,16 +491,16 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": dev_max / args.steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: random-init bf16 weights (seed 2), lognormal prompts, uniform ids",
         "config": {
             "workload": WORKLOAD,
             "model": "llama-3-8b-shape",
-            "global_batch": CONCURRENCY * world,
+            "global_batch": CONCURRENCY * (world // tp),
             "seq_len": f"prompt lognormal(512, 0.8) in [32, 4096] + {OUT_TOKENS} generated",
-            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "parallelism": (f"tp{tp}" if tp > 1 else f"replicas{world}") if world > 1 else "single",
             "l2": "no flush needed: each step streams ~15 GB of weights and ~28 GB of KV (L2 126 MB)",
             "tokens_timed": int(n_all),
             "steps_pure_decode": sum(1 for b, t, d in steps_meta if d == b),
@@ -581,6 +595,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", choices=["replicas", "tp"], default="replicas",
+                    help="N>1: independent replicas (default) or one tensor-parallel engine")
     ap.add_argument("--micro", choices=["decode_attn", "gemm"], default=None,
                     help="time one kernel on a small case (for ncu captures)")
     ap.add_argument("--seqs", type=int, default=64)
@@ -604,7 +620,7 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
     try:
         return run_ours(args, rank, world, local_rank)
     finally:

@@ -192,7 +192,9 @@ class MuWorker:
                                             self._decode_bound())
         if grew:
             self._graphs.clear()
-        graph = self.use_graphs and num_decode == B and B > 0
+        # Tensor-parallel steps run eagerly: replaying graphs that captured the
+        # torch NCCL all-reduce gave wrong results after the first replays.
+        graph = self.use_graphs and self.model.tp_group is None and num_decode == B and B > 0
         allseq = seqs
         if graph:
             bucket = _bucket(B)
