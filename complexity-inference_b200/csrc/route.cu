@@ -100,6 +100,16 @@ __global__ void mark_seen_kernel(uint32_t* __restrict__ seen, int64_t stride,
   atomicOr(seen + (int64_t)rows[b] * stride + (tok >> 5), 1u << (tok & 31));
 }
 
+// Decode inputs that are the previous step's samples: ids[j] = sampled[src[j]]
+// where src[j] >= 0 (src[j] < 0 keeps the id the host wrote).
+__global__ void fill_decode_inputs_kernel(int32_t* __restrict__ ids, const int32_t* __restrict__ src,
+                                          const int32_t* __restrict__ sampled, int n) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const int s = src[j];
+  if (s >= 0) ids[j] = sampled[s];
+}
+
 }  // namespace muk
 
 using namespace muk;
@@ -140,4 +150,13 @@ extern "C" int muk_mark_seen(uint32_t* seen_bits, int64_t seen_stride, const int
   mark_seen_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(seen_bits, seen_stride, rows,
                                                                    tokens, n, vocab);
   return check_launch("muk_mark_seen");
+}
+
+extern "C" int muk_fill_decode_inputs(int32_t* input_ids, const int32_t* src,
+                                      const int32_t* sampled, int n, void* stream) {
+  MUK_REQUIRE(input_ids && src && sampled && n >= 0, "muk_fill_decode_inputs: bad arguments");
+  if (n == 0) return MUK_OK;
+  fill_decode_inputs_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(input_ids, src,
+                                                                            sampled, n);
+  return check_launch("muk_fill_decode_inputs");
 }

@@ -67,6 +67,7 @@ SIGNATURES = {
     "muk_sample": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P, _P, _P,
                            _P, _P]),
     "muk_mark_seen": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P]),
+    "muk_fill_decode_inputs": (c_int, [_P, _P, _P, c_int, _P]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -17,7 +17,7 @@ import uuid
 from collections import deque
 from dataclasses import dataclass, field
 from enum import Enum
-from typing import Callable, Deque, Dict, List, Optional
+from typing import Callable, Deque, Dict, List, Optional, Set
 
 from .config import SamplingParams, SchedulerConfig
 from .mu import MuDynamics, soft_clamp
@@ -115,11 +115,14 @@ class MuScheduler:
             self.waiting.append(request)
         return request.request_id
 
-    def schedule(self) -> SchedulerOutput:
+    def schedule(self, hold: Optional[Set[str]] = None) -> SchedulerOutput:
+        """Next step's work.  ``hold``: running requests to leave out of this
+        step (an engine that has their last token in flight already knows
+        they finish); they take no decode slot or budget."""
         out = SchedulerOutput()
         decode_budget = self.config.max_num_batched_tokens
         for req in list(self.running.values()):
-            if req.status == RequestStatus.DECODE:
+            if req.status == RequestStatus.DECODE and not (hold and req.request_id in hold):
                 out.decode_requests.append(req)
                 out.num_decode_tokens += 1
                 decode_budget -= 1
@@ -191,6 +194,13 @@ class MuScheduler:
 
     def finish_request(self, request_id: str, success: bool = True) -> None:
         req = self.running.pop(request_id, None)
+        if req is None:  # finished while re-queued after a preemption
+            req = next((r for r in list(self.waiting) + self.priority_queue
+                        if r.request_id == request_id), None)
+            if req is not None:
+                self.waiting = deque(r for r in self.waiting if r is not req)
+                self.priority_queue = [r for r in self.priority_queue if r is not req]
+                heapq.heapify(self.priority_queue)
         if req:
             req.status = RequestStatus.FINISHED if success else RequestStatus.FAILED
             req.finish_time = time.time()

@@ -20,7 +20,7 @@ __all__ = [
     "Clamp", "MUK_EPI_BF16", "MUK_EPI_F32", "MUK_EPI_SWIGLU", "MUK_EPI_BIAS_SILU",
     "embed", "residual_rmsnorm", "rmsnorm_rows", "rope_kv_append", "decode_attn_workspace_size",
     "decode_attn", "prefill_attn", "gemm", "grouped_gemm", "route_permute", "gather_rows",
-    "inl_dynamics", "reduce_clamp", "sample", "mark_seen",
+    "inl_dynamics", "reduce_clamp", "sample", "mark_seen", "fill_decode_inputs",
 ]
 
 
@@ -246,3 +246,10 @@ def mark_seen(seen_bits: torch.Tensor, rows: torch.Tensor, tokens: torch.Tensor,
     n = tokens.numel() if n is None else n
     call("muk_mark_seen", _p(seen_bits), seen_bits.stride(0), _p(rows), _p(tokens), n, vocab,
          _stream())
+
+
+def fill_decode_inputs(input_ids: torch.Tensor, src: torch.Tensor, sampled: torch.Tensor, n: int):
+    """input_ids[j] = sampled[src[j]] where src[j] >= 0, for j < n (int32 tensors)."""
+    for t, name in ((input_ids, "input_ids"), (src, "src"), (sampled, "sampled")):
+        _check(t, torch.int32, name)
+    call("muk_fill_decode_inputs", _p(input_ids), _p(src), _p(sampled), n, _stream())

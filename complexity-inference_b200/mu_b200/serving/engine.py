@@ -31,7 +31,7 @@ import torch
 
 from ..core.config import EngineConfig, SamplingParams
 from ..core.scheduler import MuScheduler, Request, RequestStatus
-from ..utils.sampling import BatchSampler
+from ..utils.sampling import BatchSampler, SampleHandle
 from ..utils.tokenizer import load_tokenizer
 from .worker import MuWorker
 
@@ -67,21 +67,50 @@ class StepOutput:
     finish_reason: Optional[str] = None
 
 
-class StepEngine:
-    """Scheduler + worker + sampler; one ``step()`` = one GPU forward step."""
+@dataclass
+class _Launched:
+    """A step whose sampled tokens have not been read back yet."""
 
-    def __init__(self, worker: MuWorker, config: EngineConfig, eos_token_id: Optional[int] = None):
+    reqs: List[Request]           # one per logits row
+    idx: List[int]                # position of the pending token in output_token_ids
+    row_of: Dict[str, int]        # request id -> row of its token in handle.dev
+    handle: SampleHandle
+
+
+class StepEngine:
+    """Scheduler + worker + sampler; one ``step()`` = one GPU forward step.
+
+    With ``overlap`` (the default) the host never waits for the GPU between
+    steps: ``step()`` packs and launches step i+1 first — decode inputs that
+    are step i's samples are read on the device (``muk_fill_decode_inputs``)
+    — and only then waits for step i's tokens and applies them.  So
+    ``step()`` returns the outputs of the previous launch, and the
+    scheduling, slot reservation and packing of a step run while the GPU
+    executes the one before.  A request whose length limit is reached is
+    left out of the next launch; one that stops on a stop token was already
+    launched once more: that extra token is dropped (its KV slot is freed
+    with the request), so the generated tokens are exactly those of the
+    non-overlapped engine.  ``overlap=False`` runs each step to completion
+    (the reference's order, engine.py:560-680).
+    """
+
+    def __init__(self, worker: MuWorker, config: EngineConfig, eos_token_id: Optional[int] = None,
+                 overlap: bool = True):
         self.worker = worker
         self.config = config
         self.scheduler = MuScheduler(config.scheduler)
+        # requests whose last token is still in flight keep their bitmap row
+        # while new ones are admitted: room for twice the batch
         self.sampler = BatchSampler(worker.model.config.vocab_size,
-                                    max(config.cache.max_num_seqs, config.scheduler.max_batch_size),
+                                    2 * max(config.cache.max_num_seqs,
+                                            config.scheduler.max_batch_size),
                                     worker.device)
         self.eos_token_id = eos_token_id
+        self.overlap = overlap
         self.requests: Dict[str, Request] = {}
-        self._rows_host = torch.zeros(1024, dtype=torch.int32, pin_memory=torch.cuda.is_available())
-        self._rows_dev = torch.zeros(1024, dtype=torch.int32, device=worker.device)
         self.num_steps = 0
+        self._inflight: Optional[_Launched] = None
+        self._closing: set = set()   # last token in flight and length limit reached
 
     # ---- requests ------------------------------------------------------------
     def add_request(self, prompt_token_ids: Sequence[int], sampling_params: SamplingParams,
@@ -100,12 +129,13 @@ class StepEngine:
         self.requests.pop(request_id, None)
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_unfinished()
+        return self.scheduler.has_unfinished() or self._inflight is not None
 
     def _release(self, rid: str) -> None:
         if rid in self.worker.active_requests:
             self.worker.free_request(rid)
         self.sampler.remove(rid)
+        self._closing.discard(rid)
 
     def _finish(self, req: Request, reason: str, success: bool = True) -> None:
         self._release(req.request_id)
@@ -115,8 +145,24 @@ class StepEngine:
     # ---- one step ----------------------------------------------------------------
     @torch.inference_mode()
     def step(self) -> List[StepOutput]:
-        out = self.scheduler.schedule()
         results: List[StepOutput] = []
+        launched = self._launch(results)
+        if not self.overlap:
+            if launched is not None:
+                results += self._complete(launched)
+            return results
+        prev, self._inflight = self._inflight, launched
+        if prev is not None:
+            results += self._complete(prev)
+        return results
+
+    def flush(self) -> List[StepOutput]:
+        """Wait for the step in flight, if any, and return its outputs."""
+        prev, self._inflight = self._inflight, None
+        return self._complete(prev) if prev is not None else []
+
+    def _launch(self, results: List[StepOutput]) -> Optional[_Launched]:
+        out = self.scheduler.schedule(self._closing)
         for req in out.preempted_requests:  # recompute preemption: drop KV, re-prefill later
             self._release(req.request_id)
         prefills: List[Request] = []
@@ -131,10 +177,18 @@ class StepEngine:
             prefills.append(req)
         decodes = out.decode_requests
         if not decodes and not prefills:
-            return results
-        work = [(r.request_id, np.asarray(r.output_token_ids[-1:], dtype=np.int32)) for r in decodes]
-        work += [(r.request_id, np.asarray(r.prompt_token_ids + r.output_token_ids, dtype=np.int32))
-                 for r in prefills]
+            return None
+        prev = self._inflight
+        prev_rows = prev.row_of if prev is not None else {}
+        row_of = self.sampler.row_of
+        work = []
+        for r in decodes:
+            rid = r.request_id
+            src = prev_rows.get(rid, -1)
+            toks = _ZERO if src >= 0 else np.asarray(r.output_token_ids[-1:], dtype=np.int32)
+            work.append((rid, toks, src, row_of[rid]))
+        work += [(r.request_id, np.asarray(r.prompt_token_ids + r.output_token_ids, dtype=np.int32),
+                  -1, row_of[r.request_id]) for r in prefills]
         seqs, errors = self.worker.prepare(work, len(decodes))
         for rid, err in errors:
             req = self.requests[rid]
@@ -142,38 +196,48 @@ class StepEngine:
             self._finish(req, "error", success=False)
             results.append(StepOutput(rid, -1, True, "error"))
         if not seqs:
-            return results
+            return None
         ok = {s.request_id for s in seqs}
         nd = sum(1 for r in decodes if r.request_id in ok)
-        logits, batch = self.worker.run_step(seqs, nd)
-        # repetition bitmaps: mark this step's input tokens in their request rows
+        logits, batch = self.worker.run_step(seqs, nd, prev.handle.dev if prev is not None else None)
         T = sum(len(s.token_ids) for s in seqs)
-        if T > self._rows_host.numel():
-            n = 2 * T
-            self._rows_host = torch.zeros(n, dtype=torch.int32, pin_memory=torch.cuda.is_available())
-            self._rows_dev = torch.zeros(n, dtype=torch.int32, device=self.worker.device)
-        rh = self._rows_host.numpy()
-        rows = np.fromiter((self.sampler.row_of[s.request_id] for s in seqs), dtype=np.int32,
-                           count=len(seqs))
-        rh[:T] = np.repeat(rows, [len(s.token_ids) for s in seqs])
-        self._rows_dev[:T].copy_(self._rows_host[:T], non_blocking=True)
-        self.sampler.mark_inputs(self._rows_dev, batch.input_ids, T)
         reqs = [self.requests[s.request_id] for s in seqs]
-        toks = self.sampler.sample(logits, [s.request_id for s in seqs],
-                                   [r.sampling_params for r in reqs],
-                                   [r.num_generated_tokens for r in reqs]).tolist()
+        ids = [s.request_id for s in seqs]
+        handle = self.sampler.launch(logits, ids, [r.sampling_params for r in reqs],
+                                     [r.num_generated_tokens for r in reqs],
+                                     batch.token_rows, batch.input_ids, T)
         self.num_steps += 1
-        for req, tok in zip(reqs, toks):
-            self.scheduler.update_request(req.request_id, tok)
+        idx = []
+        for req in reqs:  # the pending token takes its place now; its value comes later
+            idx.append(len(req.output_token_ids))
+            req.output_token_ids.append(-1)
+            req.num_generated_tokens += 1
+            req.status = RequestStatus.DECODE
+            if req.num_generated_tokens >= req.sampling_params.max_tokens:
+                self._closing.add(req.request_id)
+        return _Launched(reqs, idx, {rid: i for i, rid in enumerate(ids)}, handle)
+
+    def _complete(self, launched: _Launched) -> List[StepOutput]:
+        toks = launched.handle.wait()
+        results: List[StepOutput] = []
+        eos = self.eos_token_id
+        for req, i, tok in zip(launched.reqs, launched.idx, toks):
+            if req.is_finished or self.requests.get(req.request_id) is not req:
+                continue  # stopped on the step before, or aborted
+            req.output_token_ids[i] = tok
+            if req.on_token:
+                req.on_token(tok, "")
             sp = req.sampling_params
             reason = None
-            if self.eos_token_id is not None and tok == self.eos_token_id:
+            if eos is not None and tok == eos:
                 reason = "stop"
             elif sp.stop_token_ids and tok in sp.stop_token_ids:
                 reason = "stop"
-            elif req.num_generated_tokens >= sp.max_tokens:
+            elif i + 1 >= sp.max_tokens:
                 reason = "length"
             if reason:
+                del req.output_token_ids[i + 1:]   # a token launched after this one is dropped
+                req.num_generated_tokens = i + 1
                 self._finish(req, reason)
             results.append(StepOutput(req.request_id, tok, reason is not None, reason))
         return results
@@ -182,6 +246,9 @@ class StepEngine:
         while self.has_unfinished():
             self.step()
         return self.requests
+
+
+_ZERO = np.zeros(1, dtype=np.int32)
 
 
 def _encode(tokenizer, prompt: Prompt) -> List[int]:

@@ -26,6 +26,7 @@ import numpy as np
 import torch
 
 from .. import _lib
+from .. import kernels as K
 from ..core.cache import PagedKVCache
 from ..core.config import EngineConfig, ModelConfig
 from ..models.loader import build_model, config_from_dict, detect_architecture, load_config
@@ -54,6 +55,8 @@ class StagedStep:
     end: int               # used prefix of the staging buffer (int32 elements)
     graph: bool
     request_ids: List[str]
+    patch: int = 0         # leading decode rows whose input comes from the previous samples
+    real_tokens: int = 0   # tokens of the real sequences (padding excluded)
 
 
 @dataclass
@@ -153,30 +156,43 @@ class MuWorker:
         self.active_requests.pop(request_id, None)
 
     # ---- batched step -----------------------------------------------------------
-    def prepare(self, work: Sequence[Tuple[str, np.ndarray]], num_decode: int
+    def prepare(self, work: Sequence[Tuple], num_decode: int
                 ) -> Tuple[List[SeqWork], List[Tuple[str, str]]]:
-        """Reserve cache slots; returns the packable sequences and (id, error) pairs."""
+        """Reserve cache slots; returns the packable sequences and (id, error) pairs.
+
+        ``work`` items are ``(request_id, new_token_ids)`` with optional
+        ``src`` (index of the decode input among the previous step's sampled
+        tokens on the device, -1 when the ids are given) and ``row``
+        (repetition-bitmap row) appended."""
         seqs, errors = [], []
-        for rid, toks in work:
+        cache = self.cache
+        for item in work:
+            rid, toks = item[0], item[1]
             st = self.active_requests.get(rid)
             if st is None:
                 errors.append((rid, f"Request {rid} not allocated"))
                 continue
             toks = np.asarray(toks, dtype=np.int32).reshape(-1)
-            start = self.cache.get_seq_len(rid)
-            slots = self.cache.reserve(rid, len(toks))
+            start = cache.get_seq_len(rid)
+            slots = cache.reserve(rid, len(toks))
             if slots is None:
                 errors.append((rid, "KV cache out of blocks"))
                 continue
             st["seq_len"] = start + len(toks)
-            seqs.append(SeqWork(rid, toks, start, slots, self.cache.block_table(rid)))
+            seqs.append(SeqWork(rid, toks, start, slots, cache.block_table(rid),
+                                item[2] if len(item) > 2 else -1,
+                                item[3] if len(item) > 3 else 0))
         return seqs, errors
 
-    def run_step(self, seqs: List[SeqWork], num_decode: int) -> Tuple[torch.Tensor, StepBatch]:
-        """Pack and run one step; returns ([B, V] f32 logits on device, batch)."""
+    def run_step(self, seqs: List[SeqWork], num_decode: int,
+                 sampled: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, StepBatch]:
+        """Pack and run one step; returns ([B, V] f32 logits on device, batch).
+
+        ``sampled``: the previous step's sampled tokens on the device, read by
+        decode sequences whose ``src`` is set."""
         st = self.stage(seqs, num_decode)
-        self.packer.dev[:st.end].copy_(self.packer.host[:st.end], non_blocking=True)
-        return self.run_staged(st)
+        self.packer.upload(st.end)
+        return self.run_staged(st, sampled)
 
     def stage(self, seqs: List[SeqWork], num_decode: int) -> "StagedStep":
         """Reserve buffer room and fill the pinned host staging buffer for a step.
@@ -203,14 +219,20 @@ class MuWorker:
             num_decode = bucket
         Tp, Bp, _, qlens, ctx = self.packer.fill_host(allseq, num_decode)
         end = self.packer.off["bt"] + Bp * self.packer.cap_mb
+        patch = max((i + 1 for i, s in enumerate(seqs) if s.src >= 0), default=0)
         return StagedStep(B, Tp, Bp, num_decode, qlens, ctx, end, graph,
-                          [s.request_id for s in allseq])
+                          [s.request_id for s in allseq], patch, T)
 
-    def run_staged(self, st: "StagedStep") -> Tuple[torch.Tensor, StepBatch]:
+    def run_staged(self, st: "StagedStep", sampled: Optional[torch.Tensor] = None
+                   ) -> Tuple[torch.Tensor, StepBatch]:
         """Run a step whose arrays are already in the packer's device buffer."""
         bound = self._decode_bound() if st.graph else None
         batch = self.packer.batch_view(st.T, st.Bp, st.num_decode, st.qlens, st.ctx, bound,
                                        st.request_ids)
+        if st.patch:
+            if sampled is None:
+                raise ValueError("step has decode inputs from the previous samples; pass sampled")
+            K.fill_decode_inputs(batch.input_ids, batch.decode_src, sampled, st.patch)
         if not st.graph:
             return self.model.forward_step(batch, self.cache), batch
         key = (self.packer.generation, id(self.model.ws))

@@ -24,7 +24,27 @@ from .. import kernels as K
 from ..core.config import SamplingParams
 
 
+class SampleHandle:
+    """Tokens of one launched sampling step: ``dev`` (int32 on the device,
+    valid for the next step's inputs) and a pinned host copy that is ready
+    once ``event`` has completed."""
+
+    __slots__ = ("dev", "host", "event")
+
+    def __init__(self, dev: torch.Tensor, host: torch.Tensor, event):
+        self.dev, self.host, self.event = dev, host, event
+
+    def wait(self) -> List[int]:
+        if self.event is not None:
+            self.event.synchronize()
+        return self.host.tolist()
+
+
 class BatchSampler:
+    # per row in the parameter blob (int32 words): temperature, top_p,
+    # repetition_penalty (f32), top_k, bitmap row (i32), seed, offset (i64)
+    _WORDS = 9
+
     def __init__(self, vocab_size: int, max_rows: int, device="cuda"):
         self.vocab = vocab_size
         self.words = (vocab_size + 31) // 32
@@ -32,22 +52,31 @@ class BatchSampler:
         self.seen = torch.zeros(max_rows, self.words, dtype=torch.int32, device=self.device)
         self.free_rows: List[int] = list(range(max_rows - 1, -1, -1))
         self.row_of: Dict[str, int] = {}
+        self._seed_of: Dict[str, int] = {}
         self._cap = 0
         self._alloc(256)
 
     def _alloc(self, n: int) -> None:
+        if self._cap and self.device.type == "cuda":  # queued copies still use the old buffers
+            torch.cuda.current_stream(self.device).synchronize()
+        n = (n + 3) // 4 * 4
         self._cap = n
         pin = torch.cuda.is_available()
-        # host staging: temp f32, top_p f32, rep f32, top_k i32, rows i32, seeds i64, offsets i64
-        self.h_f = torch.zeros(3, n, dtype=torch.float32, pin_memory=pin)
-        self.h_i = torch.zeros(2, n, dtype=torch.int32, pin_memory=pin)
-        self.h_l = torch.zeros(2, n, dtype=torch.int64, pin_memory=pin)
-        self.d_f = torch.zeros(3, n, dtype=torch.float32, device=self.device)
-        self.d_i = torch.zeros(2, n, dtype=torch.int32, device=self.device)
-        self.d_l = torch.zeros(2, n, dtype=torch.int64, device=self.device)
+        # two pinned parameter blobs and token buffers, used alternately: the
+        # host stages step i+1 while step i's copies may still be queued
+        self._blob_h = [torch.zeros(self._WORDS * n, dtype=torch.int32, pin_memory=pin)
+                        for _ in range(2)]
+        self._blob_ev: List[Optional[torch.cuda.Event]] = [None, None]
+        self._out_h = [torch.zeros(n, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._cur = 0
+        self._blob_d = torch.zeros(self._WORDS * n, dtype=torch.int32, device=self.device)
+        d = self._blob_d
+        self.d_temp, self.d_topp, self.d_rep = (d[i * n:(i + 1) * n].view(torch.float32)
+                                                for i in range(3))
+        self.d_topk, self.d_rows = d[3 * n:4 * n], d[4 * n:5 * n]
+        self.d_seed = d[5 * n:7 * n].view(torch.int64)
+        self.d_off = d[7 * n:9 * n].view(torch.int64)
         self.d_out = torch.zeros(n, dtype=torch.int32, device=self.device)
-        self.h_out = torch.zeros(n, dtype=torch.int32, pin_memory=pin)
-        self.d_seen_seq = torch.zeros(n, dtype=torch.int32, device=self.device)
 
     # ---- request rows -------------------------------------------------------
     def add(self, request_id: str) -> int:
@@ -64,6 +93,7 @@ class BatchSampler:
 
     def remove(self, request_id: str) -> None:
         row = self.row_of.pop(request_id, None)
+        self._seed_of.pop(request_id, None)
         if row is not None:
             self.free_rows.append(row)
 
@@ -72,32 +102,64 @@ class BatchSampler:
         """Set the bits of this step's input tokens in their requests' rows."""
         K.mark_seen(self.seen, token_rows, input_ids, self.vocab, n=n)
 
+    def _seed(self, rid: str, p: SamplingParams) -> int:
+        if p.seed is not None:
+            return p.seed
+        s = self._seed_of.get(rid)
+        if s is None:
+            s = self._seed_of[rid] = zlib.crc32(rid.encode())
+        return s
+
+    def launch(self, logits: torch.Tensor, request_ids: Sequence[str],
+               params: Sequence[SamplingParams], steps: Sequence[int],
+               token_rows: Optional[torch.Tensor] = None, input_ids: Optional[torch.Tensor] = None,
+               num_tokens: int = 0) -> SampleHandle:
+        """Enqueue (optional) bitmap marking of the step's input tokens, one
+        sampling launch and the copy of the chosen ids to pinned host memory;
+        returns without waiting."""
+        B = len(request_ids)
+        if B > self._cap:
+            self._alloc(max(B, 2 * self._cap))
+        n, k = self._cap, self._cur
+        ev = self._blob_ev[k]
+        if ev is not None:  # the copy that last read this blob must have run
+            ev.synchronize()
+        blob = self._blob_h[k].numpy()
+        f = blob[:3 * n].view(np.float32)
+        l = blob[5 * n:].view(np.int64)
+        f[:B] = [p.temperature for p in params]
+        f[n:n + B] = [p.top_p for p in params]
+        f[2 * n:2 * n + B] = [p.repetition_penalty for p in params]
+        blob[3 * n:3 * n + B] = [p.top_k for p in params]
+        row_of = self.row_of
+        blob[4 * n:4 * n + B] = [row_of[r] for r in request_ids]
+        l[:B] = [self._seed(r, p) for r, p in zip(request_ids, params)]
+        l[n:n + B] = steps
+        stream = torch.cuda.current_stream(self.device)
+        self._blob_d.copy_(self._blob_h[k], non_blocking=True)
+        ev = self._blob_ev[k] or torch.cuda.Event()
+        ev.record(stream)
+        self._blob_ev[k] = ev
+        if token_rows is not None and num_tokens > 0:
+            self.mark_inputs(token_rows, input_ids, num_tokens)
+        K.sample(logits, self.d_temp, self.d_topk, self.d_topp, self.d_rep, self.seen,
+                 self.d_seed, self.d_off, self.d_out, num_rows=B, seen_rows=self.d_rows)
+        host = self._out_h[k][:B]
+        host.copy_(self.d_out[:B], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        self._cur ^= 1
+        return SampleHandle(self.d_out[:B], host, done)
+
     def sample(self, logits: torch.Tensor, request_ids: Sequence[str],
                params: Sequence[SamplingParams], steps: Sequence[int],
                copy_to_host: bool = True) -> torch.Tensor:
         """One token per logits row; returns a host (pinned) or device int32 tensor."""
-        B = len(request_ids)
-        if B > self._cap:
-            self._alloc(max(B, 2 * self._cap))
-        hf, hi, hl = self.h_f.numpy(), self.h_i.numpy(), self.h_l.numpy()
-        for b, (rid, p, st) in enumerate(zip(request_ids, params, steps)):
-            hf[0, b] = p.temperature
-            hf[1, b] = p.top_p
-            hf[2, b] = p.repetition_penalty
-            hi[0, b] = p.top_k
-            hi[1, b] = self.row_of[rid]
-            hl[0, b] = p.seed if p.seed is not None else zlib.crc32(rid.encode())
-            hl[1, b] = st
-        self.d_f[:, :B].copy_(self.h_f[:, :B], non_blocking=True)
-        self.d_i[:, :B].copy_(self.h_i[:, :B], non_blocking=True)
-        self.d_l[:, :B].copy_(self.h_l[:, :B], non_blocking=True)
-        K.sample(logits, self.d_f[0], self.d_i[0], self.d_f[1], self.d_f[2], self.seen,
-                 self.d_l[0], self.d_l[1], self.d_out, num_rows=B, seen_rows=self.d_i[1])
+        h = self.launch(logits, request_ids, params, steps)
         if not copy_to_host:
-            return self.d_out[:B]
-        self.h_out[:B].copy_(self.d_out[:B], non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return self.h_out[:B]
+            return h.dev
+        h.event.synchronize()
+        return h.host
 
 
 # ---- reference single-row API ------------------------------------------------

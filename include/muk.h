@@ -255,6 +255,14 @@ int muk_sample(const float* logits, int64_t ld, int num_rows, int vocab,
 int muk_mark_seen(uint32_t* seen_bits, int64_t seen_stride, const int32_t* rows,
                   const int32_t* tokens, int n, int vocab, void* stream);
 
+/* input_ids[j] = sampled[src[j]] for j < n with src[j] >= 0; other entries
+ * are left as written.  Lets a decode step take the previous step's sampled
+ * tokens straight from device memory, so the host can pack and launch the
+ * next step before those tokens have been copied back.  The reference feeds
+ * each decode token from the host (mu_inference/serving/engine.py:594-602). */
+int muk_fill_decode_inputs(int32_t* input_ids, const int32_t* src, const int32_t* sampled, int n,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,156 @@
+"""StepEngine bookkeeping on CPU: the overlapped engine (step i+1 launched
+before step i's tokens are read back) must generate exactly what the
+step-by-step engine generates, stop on the same tokens and free every
+block and bitmap row.
+
+The GPU parts are replaced by a deterministic stand-in: the "model" maps
+(last input token, its position) to the next token, and decode inputs whose
+``src`` is set are read from the previous step's sampled tokens, as
+``muk_fill_decode_inputs`` does on the device.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from mu_b200.core.cache import PagedKVCache
+from mu_b200.core.config import CacheConfig, EngineConfig, ModelConfig, SamplingParams, SchedulerConfig
+from mu_b200.serving import engine as E
+from mu_b200.serving.worker import MuWorker
+
+V = 97
+
+
+def next_token(last: int, pos: int) -> int:
+    return (last * 31 + pos * 7 + 3) % V
+
+
+class _Handle:
+    def __init__(self, toks):
+        self.dev = torch.tensor(toks, dtype=torch.int32)
+
+    def wait(self):
+        return self.dev.tolist()
+
+
+class FakeSampler:
+    def __init__(self, vocab, rows, device):
+        self.row_of, self.free = {}, list(range(rows))
+
+    def add(self, rid):
+        if rid not in self.row_of:
+            if not self.free:  # grows like BatchSampler
+                n = len(self.row_of)
+                self.free = list(range(n, 2 * n))
+            self.row_of[rid] = self.free.pop()
+
+    def remove(self, rid):
+        r = self.row_of.pop(rid, None)
+        if r is not None:
+            self.free.append(r)
+
+    def launch(self, logits, ids, params, steps, token_rows=None, input_ids=None, num_tokens=0):
+        return _Handle(logits)
+
+
+class _Model:
+    config = ModelConfig(vocab_size=V)
+
+
+class FakeWorker:
+    """MuWorker's host bookkeeping (prepare) over a CPU cache, fake compute."""
+
+    prepare = MuWorker.prepare
+    allocate_request = MuWorker.allocate_request
+    free_request = MuWorker.free_request
+
+    def __init__(self, blocks=64):
+        self.model = _Model()
+        self.device = torch.device("cpu")
+        self.cache = PagedKVCache(1, 1, 2, 4, blocks, torch.float32, "cpu")
+        self.active_requests = {}
+        self.steps = []
+
+    def run_step(self, seqs, nd, sampled=None):
+        out = []
+        for s in seqs:
+            if s.src >= 0:
+                assert sampled is not None
+                last = int(sampled[s.src])
+            else:
+                last = int(s.token_ids[-1])
+            out.append(next_token(last, s.start_pos + len(s.token_ids) - 1))
+        self.steps.append((len(seqs), nd))
+        return out, type("B", (), {"token_rows": None, "input_ids": None})()
+
+
+def expected(prompt, max_tokens, stop):
+    toks, gen = list(prompt), []
+    while len(gen) < max_tokens:
+        t = next_token(toks[-1], len(toks) - 1)
+        gen.append(t)
+        toks.append(t)
+        if t in stop:
+            break
+    return gen
+
+
+def run(overlap, prompts, limits, stop, max_batch, abort=None, monkeypatch=None):
+    monkeypatch.setattr(E, "BatchSampler", FakeSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=max_batch),
+                      scheduler=SchedulerConfig(max_batch_size=max_batch, max_num_batched_tokens=64,
+                                                max_prefill_tokens=64))
+    w = FakeWorker()
+    eng = E.StepEngine(w, ec, overlap=overlap)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=m, stop_token_ids=stop),
+                        f"r{i}")
+    reported = {f"r{i}": [] for i in range(len(prompts))}
+    n = 0
+    while eng.has_unfinished():
+        for o in eng.step():
+            assert o.token_id >= 0
+            reported[o.request_id].append(o.token_id)
+        n += 1
+        if abort and n == abort[1]:
+            eng.abort_request(abort[0])
+        assert n < 500
+    return eng, w, reported
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_overlapped_engine_matches_sequential_generation(overlap, monkeypatch):
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in rng.integers(1, 11, 9)]
+    limits = [int(m) for m in rng.integers(1, 14, 9)]
+    stop = [5, 11]
+    eng, w, reported = run(overlap, prompts, limits, stop, max_batch=4, monkeypatch=monkeypatch)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        req = eng.requests[f"r{i}"]
+        want = expected(p, m, stop)
+        assert req.output_token_ids == want, (i, overlap)
+        assert req.num_generated_tokens == len(want)
+        assert reported[f"r{i}"] == want  # each token reported once, in order
+        assert req.finish_reason == ("stop" if want[-1] in stop else "length")
+    assert any(eng.requests[f"r{i}"].finish_reason == "stop" for i in range(len(prompts)))
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+    assert not eng.sampler.row_of and eng._inflight is None and not eng._closing
+    # continuous batching really mixed decodes with new prefills
+    assert any(0 < nd < b for b, nd in w.steps)
+
+
+def test_overlap_launches_no_more_steps_than_needed(monkeypatch):
+    """Length limits are known at launch: no step runs past max_tokens."""
+    prompts = [[1, 2, 3], [4, 5], [6]]
+    _, w1, _ = run(False, prompts, [4, 6, 2], [], 8, monkeypatch=monkeypatch)
+    _, w2, _ = run(True, prompts, [4, 6, 2], [], 8, monkeypatch=monkeypatch)
+    assert w1.steps == w2.steps
+
+
+def test_abort_while_in_flight(monkeypatch):
+    prompts = [[1, 2, 3], [4, 5, 6, 7]]
+    eng, w, reported = run(True, prompts, [20, 6], [], 4, abort=("r0", 3),
+                           monkeypatch=monkeypatch)
+    assert "r0" not in eng.requests
+    assert eng.requests["r1"].output_token_ids == expected(prompts[1], 6, [])
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks

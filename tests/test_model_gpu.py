@@ -136,3 +136,37 @@ def test_sampled_generation_is_seeded(cuda):
         outs.append([eng.requests[f"s{r}"].output_token_ids for r in range(3)])
     assert outs[0] == outs[1]
     assert all(len(o) == 12 for o in outs[0])
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_engine_stops_on_eos_with_overlap(cuda, overlap):
+    """A request stopping on the EOS token: with the overlapped engine its
+    next step was already launched; that token must be dropped and the
+    request's blocks and bitmap row freed."""
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    name = "llama_tiny"
+    toks = np.load(__import__("golden_models").G / f"{name}.npz")["tokens"]
+    R, n = toks.shape
+    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=R)
+    # EOS = request 1's 4th reference token; trust only the prefix before a near tie
+    eos = int(toks[1, 3])
+    eng = StepEngine(w, ec, eos_token_id=eos, overlap=overlap)
+    for r in range(R):
+        eng.add_request(prompts[r], SamplingParams(temperature=0.0, top_k=0, top_p=1.0,
+                                                   repetition_penalty=1.0, max_tokens=n), f"r{r}")
+    eng.run_to_completion()
+    for r in range(R):
+        got = eng.requests[f"r{r}"].output_token_ids
+        ref = [int(t) for t in toks[r]]
+        stop = next((i for i, t in enumerate(ref) if t == eos), None)
+        want = ref if stop is None else ref[:stop + 1]
+        m = min(len(got), len(want))
+        first = next((i for i in range(m) if got[i] != want[i]), m)
+        if first < m or len(got) != len(want):  # only after a reference near tie
+            assert d["top2_gap"][r, :min(first, n - 1) + 1].min() <= GAP_TOL, (r, got, want)
+        if eos in got:
+            assert got.index(eos) == len(got) - 1 and eng.requests[f"r{r}"].finish_reason == "stop"
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+    assert not eng.sampler.row_of
