@@ -19,6 +19,18 @@
 //               accumulator (`acc_empty[a]`) for the tile after next.
 // Tiles are ordered M-fastest so that the CTAs working on the row tiles of
 // one weight tile run at the same time and the weights stream from HBM once.
+//
+// Optional stream-K schedule (dense, split_k = 1; off unless enabled, see
+// streamk_enabled): when the tile count is not a multiple of the workers
+// (SMs, or SM pairs), whole waves of tiles run
+// data-parallel and the last one or two waves' k-iterations are divided
+// evenly over all workers, so no worker idles through a partial wave.  A tile
+// shared by several workers is finished by the last one to get there: each
+// other contributor writes its f32 accumulator to an in-library slot and
+// takes a ticket (threadfence + atomicAdd on the tile's counter); the worker
+// whose ticket completes the count sums all contributions in a fixed order
+// (bit-identical whoever arrives last) and runs the real epilogue.  Nothing
+// ever waits on another CTA, so there is no co-residency requirement.
 // Every mbarrier wait is bounded (common.cuh); a time-out records a device
 // error and the CTA unwinds, freeing its TMEM.
 //
@@ -32,6 +44,7 @@
 // mu_inference/models/llama.py:237).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "abi_util.h"
@@ -65,7 +78,115 @@ struct TileArgs {
   const float* bias;
   const int32_t* offsets;  // grouped mode
   int num_experts;
+  // schedule: units [0, dp_tiles) data-parallel (tile x split order), then
+  // tiles [dp_tiles, dp_tiles + sk_tiles) stream-K over `workers` workers
+  int dp_tiles, sk_tiles, k_tiles, workers;
 };
+
+// Stream-K partial slots: (worker, which of its two split units, CTA rank)
+// -> 128 rows x 256 columns f32, stored [column chunk][float4 j][row] so a
+// warp's 32 rows move as 512 contiguous bytes.
+constexpr int kSkMaxWorkers = kNumSMs;
+constexpr int kSkSlotFloats = kBM * 256;
+constexpr int kSkSlots = kSkMaxWorkers * 2;  // x ranks: pairs have half the workers
+constexpr int kSkMaxCounters = 4096;
+static __device__ __align__(256) float g_sk_ws[(size_t)kSkSlots * kSkSlotFloats];
+static __device__ uint32_t g_sk_cnt[kSkMaxCounters];  // zero between launches
+
+// One piece of a worker's work: k-tiles [kt0, kt0 + nk) of tile t.
+struct Unit {
+  int t, kt0, nk;
+  int part;  // -1: the whole tile; 0 / 1: stream-K share (first / last unit of the worker)
+  int sk;    // stream-K tile index (counter), when part >= 0
+};
+
+__device__ __forceinline__ long long sk_begin(const TileArgs& a, int w) {
+  return (long long)w * ((long long)a.sk_tiles * a.k_tiles) / a.workers;
+}
+
+__device__ __forceinline__ int sk_worker_of(const TileArgs& a, long long i) {
+  const long long I = (long long)a.sk_tiles * a.k_tiles;
+  return (int)(((i + 1) * a.workers - 1) / I);
+}
+
+// The idx-th unit of worker w; false past the last.  For DP units kt0/nk come
+// from the split decode (kt0 = -1 here).
+__device__ __forceinline__ bool get_unit(const TileArgs& a, int w, int idx, Unit& u) {
+  const int P = a.workers;
+  const int ndp = w < a.dp_tiles ? (a.dp_tiles - 1 - w) / P + 1 : 0;
+  if (idx < ndp) {
+    u.t = w + idx * P;
+    u.kt0 = -1;
+    u.nk = 0;
+    u.part = -1;
+    u.sk = -1;
+    return true;
+  }
+  if (a.sk_tiles == 0) return false;
+  const long long b = sk_begin(a, w), e = sk_begin(a, w + 1);
+  const int j = idx - ndp;
+  const long long s = b / a.k_tiles + j;
+  const long long tb = s * a.k_tiles;
+  const long long lo = b > tb ? b : tb;
+  const long long hi = e < tb + a.k_tiles ? e : tb + a.k_tiles;
+  if (lo >= hi) return false;
+  u.t = a.dp_tiles + (int)s;
+  u.kt0 = (int)(lo - tb);
+  u.nk = (int)(hi - lo);
+  u.sk = (int)s;
+  u.part = (u.kt0 == 0 && u.nk == a.k_tiles) ? -1 : (j == 0 ? 0 : 1);
+  return true;
+}
+
+__device__ __forceinline__ float4* sk_slot(int w, int which, int rank, int ranks) {
+  return reinterpret_cast<float4*>(g_sk_ws) +
+         (size_t)((w * 2 + which) * ranks + rank) * (kSkSlotFloats / 4);
+}
+
+// Stream-K share of a tile, epilogue side (one warp: 32 rows of this CTA's
+// 128).  Returns true when this warp holds the last share; then `acc_fn`
+// must be used to read accumulator chunks (own TMEM + the other shares).
+struct SkFix {
+  int wf, wl, self, rank, ranks, row_local;
+  long long tile_begin;
+  const TileArgs* a;
+};
+
+__device__ __forceinline__ void sk_store_chunk(const SkFix& f, int which, int chunk,
+                                               const uint32_t (&v)[32]) {
+  float4* p = sk_slot(f.self, which, f.rank, f.ranks) + (size_t)(chunk * 8) * kBM + f.row_local;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    __stcg(p + (size_t)j * kBM, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                            __uint_as_float(v[4 * j + 2]),
+                                            __uint_as_float(v[4 * j + 3])));
+}
+
+// v: this worker's accumulator chunk in, the fixed-order sum over all shares out.
+__device__ __forceinline__ void sk_sum_chunk(const SkFix& f, int chunk, uint32_t (&v)[32]) {
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+  for (int c = f.wf; c <= f.wl; ++c) {
+    if (c == f.self) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(v[j]);
+    } else {
+      const int which = sk_begin(*f.a, c) >= f.tile_begin ? 0 : 1;
+      const float4* p = sk_slot(c, which, f.rank, f.ranks) + (size_t)(chunk * 8) * kBM + f.row_local;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = __ldcg(p + (size_t)j * kBM);
+        acc[4 * j] += x.x;
+        acc[4 * j + 1] += x.y;
+        acc[4 * j + 2] += x.z;
+        acc[4 * j + 3] += x.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(acc[j]);
+}
 
 struct Tile {
   int row0, row_end, brow0, n0, split, kt0, nk;
@@ -152,6 +273,104 @@ __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_
   }
 }
 
+// Epilogue of one accumulator (this warp's 32 rows): TMEM -> registers ->
+// fused epilogue -> global.  With `fix`, each chunk is first replaced by the
+// sum of all stream-K shares of the tile.
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int row, int row_end,
+                                              int n0, int64_t split_off, uint32_t lane_addr,
+                                              const SkFix* fix) {
+  if (EPI == MUK_EPI_SWIGLU) {
+    const int nout = args.N >> 1;
+#pragma unroll 1
+    for (int grp = 0; grp < BN / 128; ++grp) {
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t gv[32], uv[32];
+        tmem_ld_32x32b_x32(lane_addr + grp * 128 + c * 32, gv);
+        tmem_ld_32x32b_x32(lane_addr + grp * 128 + 64 + c * 32, uv);
+        tmem_ld_wait();
+        if (fix) {
+          sk_sum_chunk(*fix, grp * 4 + c, gv);
+          sk_sum_chunk(*fix, grp * 4 + 2 + c, uv);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
+        store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, row_end, (n0 >> 1) + grp * 64 + c * 32,
+                                  nout, gv, nullptr);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+      tmem_ld_wait();
+      if (fix) sk_sum_chunk(*fix, c, v);
+      store_chunk<EPI>(C, args.ldc, split_off, row, row_end, n0 + c * 32, args.N, v, args.bias);
+    }
+  }
+}
+
+// Stream-K share, epilogue side: publish this warp's rows of the share unless
+// every other share is in already; true when this warp finishes the tile.
+template <int BN>
+__device__ __forceinline__ bool sk_arrive(const SkFix& f, const Unit& u, int quarter, int lane,
+                                          uint32_t lane_addr) {
+  const int nc = f.wl - f.wf + 1;
+  uint32_t* cnt = g_sk_cnt + ((size_t)u.sk * f.ranks + f.rank) * 4 + quarter;
+  uint32_t seen = 0;
+  if (lane == 0) seen = *reinterpret_cast<volatile uint32_t*>(cnt);
+  seen = __shfl_sync(0xffffffffu, seen, 0);
+  bool last = seen == (uint32_t)(nc - 1);
+  if (!last) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+      tmem_ld_wait();
+      sk_store_chunk(f, u.part, c, v);
+    }
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(cnt, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    last = old == (uint32_t)(nc - 1);
+  }
+  if (last) {
+    __threadfence();
+    if (lane == 0) *cnt = 0u;  // ready for the next launch
+    __syncwarp();
+  }
+  return last;
+}
+
+__device__ __forceinline__ SkFix make_fix(const TileArgs& a, const Unit& u, int w, int rank,
+                                          int ranks, int row_local) {
+  SkFix f;
+  f.a = &a;
+  f.tile_begin = (long long)u.sk * a.k_tiles;
+  f.wf = sk_worker_of(a, f.tile_begin);
+  f.wl = sk_worker_of(a, f.tile_begin + a.k_tiles - 1);
+  f.self = w;
+  f.rank = rank;
+  f.ranks = ranks;
+  f.row_local = row_local;
+  return f;
+}
+
+template <int BN, bool GROUPED>
+__device__ __forceinline__ Tile unit_tile(const TileArgs& a, const Unit& u) {
+  Tile tl = decode_tile<BN, GROUPED>(a, u.t);
+  if (u.kt0 >= 0) {
+    tl.kt0 = u.kt0;
+    tl.nk = u.nk;
+  }
+  return tl;
+}
+
 template <int BN, int STAGES, int EPI, bool GROUPED>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -169,6 +388,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x;
 
   if (threadIdx.x == 0) {
 #pragma unroll
@@ -200,8 +420,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < args.total && ok; t += gridDim.x) {
-        const Tile tl = decode_tile<BN, GROUPED>(args, t);
+      Unit u;
+      for (int idx = 0; ok && get_unit(args, w, idx, u); ++idx) {
+        const Tile tl = unit_tile<BN, GROUPED>(args, u);
         if (!tl.valid) continue;
         for (int i = 0; i < tl.nk; ++i, ++it) {
           const int s = it % STAGES;
@@ -224,8 +445,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc = umma_idesc_bf16(kBM, BN);
       uint32_t it = 0, use = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < args.total && ok; t += gridDim.x) {
-        const Tile tl = decode_tile<BN, GROUPED>(args, t);
+      Unit u;
+      for (int idx = 0; ok && get_unit(args, w, idx, u); ++idx) {
+        const Tile tl = unit_tile<BN, GROUPED>(args, u);
         if (!tl.valid) continue;
         const int a = use & 1;
         const uint32_t aph = (use >> 1) & 1u;
@@ -259,8 +481,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----
     const int quarter = warp & 3;
     uint32_t use = 0;
-    for (int t = blockIdx.x; t < args.total; t += gridDim.x) {
-      const Tile tl = decode_tile<BN, GROUPED>(args, t);
+    Unit u;
+    for (int idx = 0; get_unit(args, w, idx, u); ++idx) {
+      const Tile tl = unit_tile<BN, GROUPED>(args, u);
       if (!tl.valid) continue;
       const int a = use & 1;
       const uint32_t aph = (use >> 1) & 1u;
@@ -278,32 +501,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, tl.row_end, tl.n0 + c * 32,
                                      args.N, z, nullptr);
         }
-      } else if (EPI == MUK_EPI_SWIGLU) {
-        const int nout = args.N >> 1;
-#pragma unroll 1
-        for (int grp = 0; grp < BN / 128; ++grp) {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t gv[32], uv[32];
-            tmem_ld_32x32b_x32(lane_addr + grp * 128 + c * 32, gv);
-            tmem_ld_32x32b_x32(lane_addr + grp * 128 + 64 + c * 32, uv);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
-            store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, tl.row_end,
-                                      (tl.n0 >> 1) + grp * 64 + c * 32, nout, gv, nullptr);
-          }
-        }
+      } else if (u.part >= 0) {
+        const SkFix f = make_fix(args, u, w, 0, 1, quarter * 32 + lane);
+        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
+          epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, &f);
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_addr + c * 32, v);
-          tmem_ld_wait();
-          store_chunk<EPI>(C, args.ldc, split_off, row, tl.row_end, tl.n0 + c * 32, args.N, v,
-                           args.bias);
-        }
+        epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, nullptr);
       }
       tc_fence_before();
       __syncwarp();
@@ -342,6 +545,26 @@ struct PairLayout {
   static constexpr int kBytes = kBarOff + (2 * kPairStages + 4) * 8 + 16 + 1024;
 };
 
+struct PairTile {
+  int mt, nt, split, kt0, nk;
+};
+
+__device__ __forceinline__ PairTile pair_tile(const TileArgs& a, const Unit& u) {
+  PairTile p;
+  p.mt = u.t % a.m_tiles;
+  const int rest = u.t / a.m_tiles;
+  p.nt = rest % a.n_tiles;
+  p.split = rest / a.n_tiles;
+  if (u.kt0 >= 0) {
+    p.kt0 = u.kt0;
+    p.nk = u.nk;
+  } else {
+    p.kt0 = p.split * a.kt_per_split;
+    p.nk = max(0, min(a.k_tiles, p.kt0 + a.kt_per_split) - p.kt0);
+  }
+  return p;
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -363,7 +586,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int pair = blockIdx.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -393,15 +616,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = pair; t < args.total && ok; t += npairs) {
-        const int mt = t % args.m_tiles, rest = t / args.m_tiles;
-        const int nt = rest % args.n_tiles, split = rest / args.n_tiles;
-        const int k_tiles = (args.K + kBK - 1) / kBK;
-        const int kt0 = split * args.kt_per_split;
-        const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
-        const int arow = mt * 256 + (int)rank * kBM;
-        const int brow = nt * BN + (int)rank * (BN / 2);
-        for (int i = 0; i < nk; ++i, ++it) {
+      Unit u;
+      for (int idx = 0; ok && get_unit(args, pair, idx, u); ++idx) {
+        const PairTile pt = pair_tile(args, u);
+        const int arow = pt.mt * 256 + (int)rank * kBM;
+        const int brow = pt.nt * BN + (int)rank * (BN / 2);
+        for (int i = 0; i < pt.nk; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) {
@@ -410,8 +630,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           if (leader) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)L::kStage);
           const uint32_t sa = base + (uint32_t)(s * L::kStage);
-          tma_load_2d_pair(sa, &tmA, &full[s], (kt0 + i) * kBK, arow);
-          tma_load_2d_pair(sa + L::kA, &tmB, &full[s], (kt0 + i) * kBK, brow);
+          tma_load_2d_pair(sa, &tmA, &full[s], (pt.kt0 + i) * kBK, arow);
+          tma_load_2d_pair(sa + L::kA, &tmB, &full[s], (pt.kt0 + i) * kBK, brow);
         }
       }
     }
@@ -421,18 +641,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
       uint32_t it = 0, use = 0;
       bool ok = true;
-      for (int t = pair; t < args.total && ok; t += npairs) {
-        const int rest = t / args.m_tiles;
-        const int split = rest / args.n_tiles;
-        const int k_tiles = (args.K + kBK - 1) / kBK;
-        const int kt0 = split * args.kt_per_split;
-        const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
+      Unit u;
+      for (int idx = 0; ok && get_unit(args, pair, idx, u); ++idx) {
+        const PairTile pt = pair_tile(args, u);
         const int a = use & 1;
         const uint32_t aph = (use >> 1) & 1u;
         if (!mbar_wait(&acc_empty[a], aph ^ 1u, kDevTimeoutAccum)) break;
         tc_fence_after();
         const uint32_t dacc = tmem + (uint32_t)(a * BN);
-        for (int i = 0; i < nk; ++i, ++it) {
+        for (int i = 0; i < pt.nk; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(&full[s], ph, kDevTimeoutFull)) {
@@ -458,21 +675,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     const int quarter = warp & 3;
     uint32_t use = 0;
-    for (int t = pair; t < args.total; t += npairs) {
-      const int mt = t % args.m_tiles, rest = t / args.m_tiles;
-      const int nt = rest % args.n_tiles, split = rest / args.n_tiles;
-      const int k_tiles = (args.K + kBK - 1) / kBK;
-      const int kt0 = split * args.kt_per_split;
-      const int nk = max(0, min(k_tiles, kt0 + args.kt_per_split) - kt0);
+    Unit u;
+    for (int idx = 0; get_unit(args, pair, idx, u); ++idx) {
+      const PairTile pt = pair_tile(args, u);
       const int a = use & 1;
       const uint32_t aph = (use >> 1) & 1u;
       if (!mbar_wait(&acc_full[a], aph, kDevTimeoutAccum)) break;
       tc_fence_after();
-      const int row = mt * 256 + (int)rank * kBM + quarter * 32 + lane;
-      const int n0 = nt * BN;
-      const int64_t split_off = (int64_t)split * args.split_stride;
+      const int row = pt.mt * 256 + (int)rank * kBM + quarter * 32 + lane;
+      const int n0 = pt.nt * BN;
+      const int64_t split_off = (int64_t)pt.split * args.split_stride;
       const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * BN);
-      if (nk == 0) {
+      if (pt.nk == 0) {
         if (EPI == MUK_EPI_F32) {
           uint32_t z[32];
 #pragma unroll
@@ -481,31 +695,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, args.M, n0 + c * 32, args.N, z,
                                      nullptr);
         }
-      } else if (EPI == MUK_EPI_SWIGLU) {
-        const int nout = args.N >> 1;
-#pragma unroll 1
-        for (int grp = 0; grp < BN / 128; ++grp) {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t gv[32], uv[32];
-            tmem_ld_32x32b_x32(lane_addr + grp * 128 + c * 32, gv);
-            tmem_ld_32x32b_x32(lane_addr + grp * 128 + 64 + c * 32, uv);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
-            store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, args.M, (n0 >> 1) + grp * 64 + c * 32,
-                                      nout, gv, nullptr);
-          }
-        }
+      } else if (u.part >= 0) {
+        const SkFix f = make_fix(args, u, pair, (int)rank, 2, quarter * 32 + lane);
+        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
+          epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, &f);
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_addr + c * 32, v);
-          tmem_ld_wait();
-          store_chunk<EPI>(C, args.ldc, split_off, row, args.M, n0 + c * 32, args.N, v, args.bias);
-        }
+        epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, nullptr);
       }
       tc_fence_before();
       __syncwarp();
@@ -589,61 +784,148 @@ static double wave_eff(long tiles, int sms) {
 
 // ---------------------------------------------------------------------------
 // Shape planner: pick the kernel (single CTA with BN 128/256, or CTA pair with
-// 256 x 256 tiles) and the split-K factor with the shortest estimated
-// makespan: ceil(tiles / workers) x (k-tiles per tile + pipeline fill) x the
-// per-k-tile cost of that tile shape on one SM.  Each extra split pays for
-// writing and re-reading an M x N f32 partial, which relative to the GEMM's
-// tensor time is about 860 / K (HBM ~6.5 TB/s vs ~1.4 PFLOP/s).
+// 256 x 256 tiles), the split-K factor and whether the last waves run
+// stream-K, by the shortest estimated makespan in k-tile steps of one worker:
+//   data-parallel  ceil(tiles / workers) x (k-tiles per tile + pipeline fill)
+//   stream-K       (full waves - 1) x (k-tiles + fill) + the even share of the
+//                  remaining tiles' k-tiles + fill per unit + ~6 steps to
+//                  publish / sum a shared tile's f32 partial (through L2)
+// times the per-k-tile cost of the tile shape on one SM.  Each extra split-K
+// slice pays for writing and re-reading an M x N f32 partial, which relative
+// to the GEMM's tensor time is about 860 / K (HBM ~6.5 TB/s vs ~1.4 PFLOP/s).
 // ---------------------------------------------------------------------------
+// Stream-K is off by default: on this power-capped part the SMs of a
+// partial last wave run at higher clocks, so balancing the wave bought
+// nothing measurable while the shared tiles cost their partial round trips
+// (809 x 6144 x 4096: 64 us stream-K vs 60 us data-parallel).  It stays
+// available (muk_gemm_set_stream_k, or MUK_GEMM_STREAMK=1) for parts and
+// shapes where it does pay.
+static int g_streamk = -1;
+
+static bool streamk_enabled() {
+  if (g_streamk < 0) {
+    const char* e = getenv("MUK_GEMM_STREAMK");
+    g_streamk = (e && e[0] == '1') ? 1 : 0;
+  }
+  return g_streamk == 1;
+}
+
 struct GemmPlan {
   int kind;   // 0: single CTA, 1: CTA pair
   int bn;     // 128 or 256
   int split;
+  bool sk;    // stream-K tail (split == 1 only)
 };
 
-static double plan_cost(int kind, int bn, int split, int M, int N, int K, int sms) {
-  const int k_tiles = (K + kBK - 1) / kBK;
-  const int kps = (k_tiles + split - 1) / split;
+struct PlanShape {
   long tiles;
-  int workers;
+  int workers, k_tiles;
   double per_k;
+};
+
+static PlanShape plan_shape(int kind, int bn, int split, int M, int N, int K, int sms) {
+  PlanShape p;
+  p.k_tiles = (K + kBK - 1) / kBK;
   if (kind == 1) {
-    tiles = (long)((M + 255) / 256) * ((N + 255) / 256) * split;
-    workers = sms / 2;
-    per_k = 0.88;  // measured: pair tiles run ~1.13x faster per SM than 128 x 256
+    p.tiles = (long)((M + 255) / 256) * ((N + 255) / 256) * split;
+    p.workers = sms / 2;
+    p.per_k = 0.88;  // measured: pair tiles run ~1.13x faster per SM than 128 x 256
   } else {
-    tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn) * split;
-    workers = sms;
-    per_k = bn == 256 ? 1.0 : 0.70;  // measured: a 128 x 128 tile costs ~0.7 of 128 x 256
+    p.tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn) * split;
+    p.workers = sms;
+    p.per_k = bn == 256 ? 1.0 : 0.70;  // measured: a 128 x 128 tile costs ~0.7 of 128 x 256
   }
-  const long rounds = (tiles + workers - 1) / workers;
-  return (double)rounds * (kps + 3) * per_k * (1.0 + (0.03 + 860.0 / K) * (split - 1));
+  return p;
+}
+
+// At most this many workers share one stream-K tile: the worker that
+// finishes a tile reads every other share back (128 KB per CTA each).
+constexpr int kSkMaxShares = 4;
+
+// Data-parallel and stream-K tile counts for `tiles` tiles over `workers`.
+static void sk_split(long tiles, int workers, long* dp, long* sk) {
+  if (tiles % workers == 0) {
+    *dp = tiles;
+    *sk = 0;
+  } else if (tiles > 2L * workers) {
+    *dp = (tiles / workers - 1) * workers;
+    *sk = tiles - *dp;
+  } else {
+    *dp = 0;
+    *sk = tiles;
+  }
+}
+
+static double plan_cost(int kind, int bn, int split, bool sk, int M, int N, int K, int sms) {
+  const PlanShape p = plan_shape(kind, bn, split, M, N, K, sms);
+  const int kps = (p.k_tiles + split - 1) / split;
+  double steps;
+  if (!sk) {
+    const long rounds = (p.tiles + p.workers - 1) / p.workers;
+    steps = (double)rounds * (kps + 3);
+  } else {
+    long dp, skt;
+    sk_split(p.tiles, p.workers, &dp, &skt);
+    const long w = std::min<long>(std::min<long>(p.workers, skt * kSkMaxShares),
+                                  skt * p.k_tiles);
+    const double share = (double)skt * p.k_tiles / w;
+    const double shares = skt < w ? (double)w / skt + 1.0 : 2.0;  // workers per shared tile
+    steps = (double)(dp / p.workers) * (p.k_tiles + 3) + share + 3.0 * (share / p.k_tiles + 2) +
+            2.5 * shares;
+  }
+  return steps * p.per_k * (1.0 + (0.03 + 860.0 / K) * (split - 1));
 }
 
 static GemmPlan plan_gemm(int M, int N, int K, int epilogue, int max_split, int sms) {
-  GemmPlan best = {0, 256, 1};
+  GemmPlan best = {0, 256, 1, false};
   double best_cost = 1e300;
   const bool swiglu = epilogue == MUK_EPI_SWIGLU;
   const int smax = epilogue == MUK_EPI_F32 ? max_split : 1;
+  const bool skok = streamk_enabled();
   for (int split = 1; split <= smax; ++split) {
-    for (int bn : {256, 128}) {
-      if (bn == 256 && swiglu && N % 256 != 0) continue;
-      if (bn == 256 && N <= 128) continue;
-      const double c = plan_cost(0, bn, split, M, N, K, sms);
-      if (c < best_cost * 0.999) {
-        best_cost = c;
-        best = {0, bn, split};
+    for (int sk = 0; sk < (split == 1 && skok ? 2 : 1); ++sk) {
+      for (int bn : {256, 128}) {
+        if (bn == 256 && swiglu && N % 256 != 0) continue;
+        if (bn == 256 && N <= 128) continue;
+        const double c = plan_cost(0, bn, split, sk, M, N, K, sms);
+        if (c < best_cost * 0.999) {
+          best_cost = c;
+          best = {0, bn, split, sk != 0};
+        }
       }
-    }
-    if (g_pair_enabled && M > 128 && N >= 256 && !(swiglu && N % 256 != 0)) {
-      const double c = plan_cost(1, 256, split, M, N, K, sms);
-      if (c < best_cost * 0.999) {
-        best_cost = c;
-        best = {1, 256, split};
+      if (g_pair_enabled && M > 128 && N >= 256 && !(swiglu && N % 256 != 0)) {
+        const double c = plan_cost(1, 256, split, sk, M, N, K, sms);
+        if (c < best_cost * 0.999) {
+          best_cost = c;
+          best = {1, 256, split, sk != 0};
+        }
       }
     }
   }
   return best;
+}
+
+// Fill the schedule fields of `a` (tiles = a.m_tiles * a.n_tiles * a.splits).
+// Returns the number of workers to launch.
+static int set_schedule(TileArgs& a, int max_workers, int ranks, bool sk) {
+  const long tiles = (long)a.total;
+  a.k_tiles = (a.K + kBK - 1) / kBK;
+  long dp = tiles, skt = 0;
+  // the in-library slots and counters hold kSkMaxWorkers CTAs' shares
+  if (sk && a.splits == 1 && max_workers * ranks <= kSkMaxWorkers)
+    sk_split(tiles, max_workers, &dp, &skt);
+  a.dp_tiles = (int)dp;
+  a.sk_tiles = (int)skt;
+  int workers = max_workers;
+  if (skt == 0) {
+    if (tiles < workers) workers = (int)tiles;
+  } else {
+    if ((long)skt * kSkMaxShares < workers) workers = (int)(skt * kSkMaxShares);
+    if ((long)skt * a.k_tiles < workers) workers = (int)((long)skt * a.k_tiles);  // >= 1 k-tile each
+  }
+  if (workers < 1) workers = 1;
+  a.workers = workers;
+  return workers;
 }
 
 template <int BN, int STAGES, int EPI, bool GROUPED>
@@ -661,8 +943,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const T
     }
     attr = true;
   }
-  const int grid = a.total < sms ? a.total : sms;
-  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, a);
+  kern<<<a.workers, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, a);
   return check_launch(GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16");
 }
 
@@ -707,8 +988,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
     }
     attr = true;
   }
-  int pairs = sms / 2;
-  if (a.total < pairs) pairs = a.total;
+  const int pairs = a.workers;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
@@ -730,7 +1010,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
 }
 
 static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
-                         int64_t ldc, int M, int N, int K, int epilogue, int split_k,
+                         int64_t ldc, int M, int N, int K, int epilogue, int split_k, bool sk,
                          const float* bias, int sms, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
@@ -751,6 +1031,7 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
   a.bias = bias;
   a.offsets = nullptr;
   a.num_experts = 0;
+  set_schedule(a, sms / 2, 2, sk);
   switch (epilogue) {
     case MUK_EPI_BF16:
       return launch_pair<MUK_EPI_BF16>(ma, mb, C, a, sms, stream);
@@ -773,6 +1054,26 @@ static bool use_pair(int M, int N, int epilogue) {
   return true;
 }
 
+// Kernel, tile width and schedule for a dense GEMM whose split_k is fixed.
+static GemmPlan plan_for_split(int M, int N, int K, int epilogue, int split_k, int sms) {
+  GemmPlan best = {0, 256, split_k, false};
+  double best_cost = 1e300;
+  const bool skok = split_k == 1 && streamk_enabled();
+  for (int kind = 0; kind < 2; ++kind)
+    for (int b : {256, 128})
+      for (int s = 0; s < (skok ? 2 : 1); ++s) {
+        if (kind == 1 && (b != 256 || !g_pair_enabled || !use_pair(M, N, epilogue))) continue;
+        if (kind == 0 && b == 256 && ((epilogue == MUK_EPI_SWIGLU && N % 256) || N <= 128))
+          continue;
+        const double c = plan_cost(kind, b, split_k, s != 0, M, N, K, sms);
+        if (c < best_cost * 0.999) {
+          best_cost = c;
+          best = {kind, b, split_k, s != 0};
+        }
+      }
+  return best;
+}
+
 static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
                     const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream) {
@@ -780,24 +1081,14 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   if (rc) return rc;
   const int sms = sm_count();
   int bn;
+  bool sk = false;
   if (!grouped) {
-    // the caller fixed split_k; choose the kernel and tile width for it
-    GemmPlan best = {0, 256, split_k};
-    double best_cost = 1e300;
-    for (int kind = 0; kind < 2; ++kind)
-      for (int b : {256, 128}) {
-        if (kind == 1 && (b != 256 || !g_pair_enabled || !use_pair(M, N, epilogue))) continue;
-        if (kind == 0 && b == 256 && ((epilogue == MUK_EPI_SWIGLU && N % 256) || N <= 128))
-          continue;
-        const double c = plan_cost(kind, b, split_k, M, N, K, sms);
-        if (c < best_cost * 0.999) {
-          best_cost = c;
-          best = {kind, b, split_k};
-        }
-      }
+    const GemmPlan best = plan_for_split(M, N, K, epilogue, split_k, sms);
     if (best.kind == 1)
-      return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, bias, sms, stream);
+      return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, sms,
+                           stream);
     bn = best.bn;
+    sk = best.sk;
   } else {
     bn = epilogue == MUK_EPI_SWIGLU ? (N % 256 == 0 ? 256 : 128)
                                     : pick_bn(m_tiles, N, split_k, sms);
@@ -820,6 +1111,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   a.bias = bias;
   a.offsets = offsets;
   a.num_experts = num_experts;
+  set_schedule(a, sms, 1, sk);
   if (bn == 256)
     return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
                    : dispatch<256, false>(epilogue, ma, mb, C, a, sms, stream);
@@ -875,4 +1167,38 @@ extern "C" int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, 
 extern "C" int muk_gemm_plan_split(int M, int N, int K, int epilogue, int max_split) {
   if (M <= 0 || N <= 0 || K <= 0 || max_split < 1) return 1;
   return plan_gemm(M, N, K, epilogue, max_split, sm_count()).split;
+}
+
+extern "C" int muk_gemm_plan_info(int M, int N, int K, int epilogue, int split_k, int32_t* out) {
+  MUK_REQUIRE(out && M > 0 && N > 0 && K > 0 && split_k >= 1, "muk_gemm_plan_info: bad arguments");
+  const int sms = sm_count();
+  const GemmPlan p = plan_for_split(M, N, K, epilogue, split_k, sms);
+  TileArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.splits = split_k;
+  if (p.kind == 1) {
+    a.m_tiles = (M + 255) / 256;
+    a.n_tiles = (N + kPairBN - 1) / kPairBN;
+  } else {
+    a.m_tiles = (M + kBM - 1) / kBM;
+    a.n_tiles = (N + p.bn - 1) / p.bn;
+  }
+  a.total = a.m_tiles * a.n_tiles * split_k;
+  const int workers = set_schedule(a, p.kind == 1 ? sms / 2 : sms, p.kind == 1 ? 2 : 1, p.sk);
+  out[0] = p.kind;
+  out[1] = p.bn;
+  out[2] = p.split;
+  out[3] = a.sk_tiles > 0 ? 1 : 0;
+  out[4] = a.dp_tiles;
+  out[5] = a.sk_tiles;
+  out[6] = workers;
+  return MUK_OK;
+}
+
+extern "C" int muk_gemm_set_stream_k(int enable) {
+  const int prev = streamk_enabled() ? 1 : 0;
+  g_streamk = enable ? 1 : 0;
+  return prev;
 }

@@ -55,6 +55,8 @@ SIGNATURES = {
     "muk_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, c_int, c_int,
                               c_int, _P, _P]),
     "muk_gemm_plan_split": (c_int, [c_int, c_int, c_int, c_int, c_int]),
+    "muk_gemm_plan_info": (c_int, [c_int, c_int, c_int, c_int, c_int, _P]),
+    "muk_gemm_set_stream_k": (c_int, [c_int]),
     "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,

@@ -20,7 +20,8 @@ __all__ = [
     "Clamp", "MUK_EPI_BF16", "MUK_EPI_F32", "MUK_EPI_SWIGLU", "MUK_EPI_BIAS_SILU",
     "embed", "residual_rmsnorm", "rmsnorm_rows", "rope_kv_append", "decode_attn_workspace_size",
     "decode_attn", "prefill_attn", "gemm", "grouped_gemm", "route_permute", "gather_rows",
-    "inl_dynamics", "reduce_clamp", "sample", "mark_seen", "fill_decode_inputs",
+    "inl_dynamics", "reduce_clamp", "sample", "mark_seen", "fill_decode_inputs", "gemm_plan_info",
+    "gemm_set_stream_k",
 ]
 
 
@@ -253,3 +254,21 @@ def fill_decode_inputs(input_ids: torch.Tensor, src: torch.Tensor, sampled: torc
     for t, name in ((input_ids, "input_ids"), (src, "src"), (sampled, "sampled")):
         _check(t, torch.int32, name)
     call("muk_fill_decode_inputs", _p(input_ids), _p(src), _p(sampled), n, _stream())
+
+
+def gemm_plan_info(M: int, N: int, K: int, epilogue: int, split_k: int = 1) -> dict:
+    """The launch muk_gemm_bf16 makes for a shape (kernel, tile width, schedule)."""
+    import ctypes
+
+    out = (ctypes.c_int32 * 7)()
+    lib = _lib.load()
+    rc = lib.muk_gemm_plan_info(M, N, K, epilogue, split_k, ctypes.addressof(out))
+    if rc != 0:
+        raise _lib.MukError("muk_gemm_plan_info", rc, _lib.last_error())
+    keys = ("kernel", "bn", "split", "stream_k", "dp_tiles", "sk_tiles", "workers")
+    return dict(zip(keys, list(out)))
+
+
+def gemm_set_stream_k(enable: bool) -> bool:
+    """Let the GEMM planner use stream-K schedules; returns the previous setting."""
+    return bool(_lib.load().muk_gemm_set_stream_k(int(bool(enable))))

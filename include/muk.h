@@ -180,6 +180,22 @@ int muk_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
  * 256 x 256 tiles.  Callers size their partial buffers from it. */
 int muk_gemm_plan_split(int M, int N, int K, int epilogue, int max_split);
 
+/* The launch muk_gemm_bf16 makes for this shape and split_k, written to
+ * out[7] = {kernel (0 single CTA, 1 CTA pair), tile width, split_k, stream-K
+ * (0/1), data-parallel tiles, stream-K tiles, workers}.  With split_k == 1,
+ * shapes whose tile count is not a multiple of the workers run their last
+ * waves stream-K (k-iterations shared evenly; the last CTA to finish a shared
+ * tile sums the f32 shares from in-library slots and applies the epilogue).
+ * Those slots are per device: stream-K GEMMs of one device must not run
+ * concurrently on different streams (MUK_GEMM_STREAMK=0 turns it off).
+ * No counterpart in the reference (introspection for tests and tuning). */
+int muk_gemm_plan_info(int M, int N, int K, int epilogue, int split_k, int32_t* out);
+
+/* Lets the planner consider stream-K schedules (enable != 0) or not (the
+ * default, also set by MUK_GEMM_STREAMK=1 in the environment); returns the
+ * previous setting.  Process-wide.  No counterpart in the reference. */
+int muk_gemm_set_stream_k(int enable);
+
 /* ---- K4: token-routed experts -------------------------------------------- */
 
 /* Stable counting sort of tokens by expert id.  expert_offsets[E+1] (prefix

@@ -201,3 +201,23 @@ def test_weight_layout_helpers():
     assert pad_to(688, 64) == 704
     assert choose_split(256, 4096, 4096, 8192) > 1
     assert choose_split(4096, 4096, 4096, 8192) == 1
+
+
+def test_gemm_planner_schedules():
+    """Host-side planner (no GPU needed; 148 SMs assumed without a device)."""
+    from mu_b200 import kernels as K
+
+    p = K.gemm_plan_info(809, 6144, 4096, K.MUK_EPI_BF16)  # default: data-parallel
+    assert p["stream_k"] == 0 and p["dp_tiles"] == 96 and p["workers"] == 74
+    prev = K.gemm_set_stream_k(True)
+    try:
+        p = K.gemm_plan_info(809, 6144, 4096, K.MUK_EPI_BF16)  # 96 pair tiles on 74 pairs
+        assert p["kernel"] == 1 and p["stream_k"] == 1 and p["sk_tiles"] == 96
+        p = K.gemm_plan_info(4096, 4096, 4096, K.MUK_EPI_BF16)  # 256 tiles: 2 DP waves + stream-K
+        assert p["dp_tiles"] == 148 and p["sk_tiles"] == 108
+        p = K.gemm_plan_info(1024, 8192, 4096, K.MUK_EPI_BF16, split_k=2)  # split-K: data-parallel
+        assert p["stream_k"] == 0 and p["split"] == 2
+        p = K.gemm_plan_info(1, 128, 64, K.MUK_EPI_F32)  # one tile, one k-tile
+        assert p["workers"] == 1
+    finally:
+        K.gemm_set_stream_k(prev)

@@ -434,3 +434,53 @@ def test_no_device_error_left(cuda):
     from mu_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+# Stream-K schedules: shapes whose tile count is not a multiple of the
+# workers; the plan is checked so the test cannot pass on a data-parallel
+# launch.  (M, N, K, epilogue): tiles < workers with many shares per tile,
+# one to two waves, more than two waves (SwiGLU), single-CTA kernel (M <= 128),
+# ragged K, bias + SiLU.
+SK_CASES = [(256, 4096, 4096, "f32"), (809, 6144, 4096, "bf16"), (809, 28672, 4096, "swiglu"),
+            (128, 4096, 4096, "bf16"), (640, 1536, 4000, "f32"), (300, 2816, 2048, "bias_silu")]
+
+
+@pytest.mark.parametrize("M,N,K,epi", SK_CASES)
+def test_gemm_stream_k(cuda, M, N, K, epi):
+    k = _kern()
+    code = {"f32": k.MUK_EPI_F32, "bf16": k.MUK_EPI_BF16, "swiglu": k.MUK_EPI_SWIGLU,
+            "bias_silu": k.MUK_EPI_BIAS_SILU}[epi]
+    prev = k.gemm_set_stream_k(True)
+    try:
+        _check_stream_k(k, cuda, M, N, K, epi, code)
+    finally:
+        k.gemm_set_stream_k(prev)
+
+
+def _check_stream_k(k, cuda, M, N, K, epi, code):
+    plan = k.gemm_plan_info(M, N, K, code)
+    assert plan["stream_k"] == 1 and plan["sk_tiles"] > 0, plan
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(N, device=cuda, generator=g) if epi == "bias_silu" else None
+    ref = A.float() @ B.float().t()
+    if epi == "swiglu":
+        I = N // 2
+        gate = ref.view(M, I // 64, 2, 64)[:, :, 0].reshape(M, I)
+        up = ref.view(M, I // 64, 2, 64)[:, :, 1].reshape(M, I)
+        ref = torch.nn.functional.silu(gate) * up
+    elif epi == "bias_silu":
+        ref = torch.nn.functional.silu(ref + bias)
+    out_dtype = torch.float32 if epi == "f32" else torch.bfloat16
+    C = torch.full((M, ref.shape[1]), float("nan"), device=cuda, dtype=out_dtype)
+    k.gemm(A, B, C, code, bias=bias)
+    tol = 1e-4 if epi == "f32" else 2e-2
+    torch.testing.assert_close(C.float(), ref, rtol=tol, atol=tol * ref.abs().max().item())
+    # shares are summed in a fixed order: bit-identical on a second launch
+    C2 = torch.full_like(C, float("nan"))
+    k.gemm(A, B, C2, code, bias=bias)
+    assert torch.equal(C, C2)
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
