@@ -19,12 +19,19 @@ The metric counts generated tokens (one per scheduled sequence per step).
   e2e       the same steps through the public StepEngine.step() API: host
             scheduling, packing, host->device copy of each step's arrays and
             device->host read of the sampled ids inside the timed region
-  roofline  paged decode attention of the running batch (HBM-bound) and the
-            decode GEMMs (tensor-bound), timed in isolation with CUDA events
+  roofline  the dominant kernel, muk_gemm_bf16 (tensor-bound): every GEMM
+            launch of the recorded eager steps timed with CUDA events;
+            beside it paged decode attention of the running batch and of
+            the isolated 128-sequence case (HBM-bound)
 
 Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-Under torchrun every rank serves its own 256 requests (replicas; no
-collective on the data path); value is the sum over ranks / max time.
+                        [--workload c3|c2|c5] [--parallel replicas|tp|ep]
+Under torchrun every rank serves its own requests by default (replicas; no
+collective on the data path; value is the sum over ranks / max time);
+--parallel tp runs one engine tensor-parallel over the ranks, --parallel ep
+also distributes the DeepForCausalLM experts whole (expert e on GPU e // (E/P)).
+The c2 / c5 workloads are the DeepForCausalLM configurations (token-routed
+MLP, INL dynamics, mu-guided attention, mu_clamp); c3 is the headline.
 """
 
 from __future__ import annotations
@@ -48,21 +55,42 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "complexity-inference_b200"))
 
 METRIC = "decode tokens/s @256 ragged reqs; paged-attn HBM GB/s vs 8 TB/s roofline"
-WORKLOAD = ("Llama-3-8B-shape (H4096 L32 32/8 heads D128 I14336 V128256 theta5e5), "
-            "256 concurrent ragged requests, steady-state continuous batching, greedy")
-C3 = dict(hidden=4096, layers=32, heads=32, kv=8, head_dim=128, inter=14336, vocab=128256,
-          theta=500000.0, seed=2)
-CONCURRENCY = 256
-OUT_TOKENS = 256
-PROMPT_MEDIAN, PROMPT_SIGMA, PROMPT_MIN, PROMPT_MAX = 512, 0.8, 32, 4096
+# The default workload is "c3"; "c2" and "c5" are the two DeepForCausalLM
+# (token-routed MLP, INL dynamics, mu-guided attention, mu_clamp) workloads.
+WORKLOADS = {
+    "c3": dict(desc="Llama-3-8B-shape (H4096 L32 32/8 heads D128 I14336 V128256 theta5e5), "
+                    "256 concurrent ragged requests, steady-state continuous batching, greedy",
+               arch="llama", hidden=4096, layers=32, heads=32, kv=8, head_dim=128, inter=14336,
+               experts=0, vocab=128256, theta=500000.0, eps=1e-5, seed=2, mu=False,
+               concurrency=256, prompt=("lognormal", 512, 0.8, 32, 4096), out=256,
+               sampling=(0.0, 0, 1.0), blocks=45000),
+    "c2": dict(desc="DeepForCausalLM (H2048 L24 16/8 heads D128, 4 experts x 2816, V32000, "
+                    "mu_clamp on), 64 concurrent requests, prompts U[64,512], 128 tokens at "
+                    "T0.7 / top-k 50 / top-p 0.9",
+               arch="deep", hidden=2048, layers=24, heads=16, kv=8, head_dim=128, inter=11264,
+               experts=4, vocab=32000, theta=10000.0, eps=1e-6, seed=1, mu=True,
+               concurrency=64, prompt=("uniform", 64, 512), out=128, sampling=(0.7, 50, 0.9),
+               blocks=4000),
+    "c5": dict(desc="scaled DeepForCausalLM (H4096 L32 32/8 heads D128, 8 experts x 3584, "
+                    "V32000, mu_clamp on), 512 concurrent requests, prompts U[128,2048], "
+                    "128 greedy tokens",
+               arch="deep", hidden=4096, layers=32, heads=32, kv=8, head_dim=128, inter=28672,
+               experts=8, vocab=32000, theta=10000.0, eps=1e-6, seed=4, mu=True,
+               concurrency=512, prompt=("uniform", 128, 2048), out=128, sampling=(0.0, 0, 1.0),
+               blocks=48000),
+}
+C3 = WORKLOADS["c3"]
+WORKLOAD = C3["desc"]
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        burst = float(d["bf16_tflops"])
+        return float(d["hbm_gbs"]), burst, float(d.get("bf16_tflops_sustained", burst)), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 # ---------------------------------------------------------------------------
@@ -124,57 +152,64 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------
-def model_config():
+def model_config(wl=C3):
     from mu_b200.core.config import ModelConfig
 
-    return ModelConfig(vocab_size=C3["vocab"], hidden_size=C3["hidden"],
-                       intermediate_size=C3["inter"], num_hidden_layers=C3["layers"],
-                       num_attention_heads=C3["heads"], num_key_value_heads=C3["kv"],
-                       head_dim=C3["head_dim"], max_position_embeddings=8192,
-                       rope_theta=C3["theta"], rms_norm_eps=1e-5, tie_word_embeddings=False)
+    return ModelConfig(vocab_size=wl["vocab"], hidden_size=wl["hidden"],
+                       intermediate_size=wl["inter"], num_hidden_layers=wl["layers"],
+                       num_attention_heads=wl["heads"], num_key_value_heads=wl["kv"],
+                       head_dim=wl["head_dim"], max_position_embeddings=8192,
+                       rope_theta=wl["theta"], rms_norm_eps=wl["eps"],
+                       num_experts=max(wl["experts"], 1), tie_word_embeddings=False)
 
 
 class Arrivals:
-    def __init__(self, seed: int, vocab: int):
+    def __init__(self, seed: int, wl=C3):
         self.rng = np.random.default_rng(seed)
-        self.vocab = vocab
+        self.wl = wl
         self.n = 0
 
     def prompt(self):
-        L = int(np.clip(np.round(self.rng.lognormal(math.log(PROMPT_MEDIAN), PROMPT_SIGMA)),
-                        PROMPT_MIN, PROMPT_MAX))
-        return self.rng.integers(0, self.vocab, L).tolist()
+        kind, *a = self.wl["prompt"]
+        if kind == "lognormal":
+            med, sig, lo, hi = a
+            L = int(np.clip(np.round(self.rng.lognormal(math.log(med), sig)), lo, hi))
+        else:
+            L = int(self.rng.integers(a[0], a[1] + 1))
+        return self.rng.integers(0, self.wl["vocab"], L).tolist()
 
     def new_request(self, engine, params_cls, already=0):
         prompt = self.prompt()
         if already:
-            prompt = prompt + self.rng.integers(0, self.vocab, already).tolist()
+            prompt = prompt + self.rng.integers(0, self.wl["vocab"], already).tolist()
         self.n += 1
-        sp = params_cls(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0,
-                        max_tokens=OUT_TOKENS - already)
+        t, k, p = self.wl["sampling"]
+        sp = params_cls(temperature=t, top_k=k, top_p=p, repetition_penalty=1.0,
+                        max_tokens=self.wl["out"] - already)
         return engine.add_request(prompt, sp, f"q{self.n}")
 
 
-def build(rank: int, tp: int = 1):
-    from mu_b200.core.config import CacheConfig, EngineConfig, SchedulerConfig
+def build(rank: int, tp: int = 1, wl=C3, ep: bool = False):
+    from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
     from mu_b200.models.weights import random_state_dict
     from mu_b200.serving.engine import StepEngine
     from mu_b200.serving.worker import MuWorker
 
-    cfg = model_config()
-    max_len = PROMPT_MAX + OUT_TOKENS + 16
-    # expected KV ~ 256 x ~830 tokens; keep 3x headroom for bursts of long prompts
-    blocks = 45000
-    ec = EngineConfig(model=cfg, dtype="bfloat16", tensor_parallel_size=tp,
-                      cache=CacheConfig(max_seq_len=max_len, block_size=16, max_num_blocks=blocks,
-                                        max_num_seqs=CONCURRENCY),
-                      scheduler=SchedulerConfig(max_batch_size=CONCURRENCY,
+    cfg = model_config(wl)
+    max_len = wl["prompt"][-1] + wl["out"] + 16
+    # headroom over the expected KV (C3: 256 x ~830 tokens, 3x) for bursts of long prompts
+    ec = EngineConfig(model=cfg, dtype="bfloat16", tensor_parallel_size=tp, expert_parallel=ep,
+                      mu=MuConfig(enabled=wl["mu"]),
+                      cache=CacheConfig(max_seq_len=max_len, block_size=16,
+                                        max_num_blocks=wl["blocks"],
+                                        max_num_seqs=wl["concurrency"]),
+                      scheduler=SchedulerConfig(max_batch_size=wl["concurrency"],
                                                 max_num_batched_tokens=8192,
                                                 max_prefill_tokens=8192))
-    sd = random_state_dict(cfg, "llama", C3["seed"], device="cuda", dtype=torch.bfloat16,
+    sd = random_state_dict(cfg, wl["arch"], wl["seed"], device="cuda", dtype=torch.bfloat16,
                            include_unused=False)
     worker = MuWorker(ec, "cuda")
-    worker.load_state_dict("llama", cfg, sd)
+    worker.load_state_dict(wl["arch"], cfg, sd)
     del sd
     torch.cuda.empty_cache()
     engine = StepEngine(worker, ec)
@@ -245,6 +280,81 @@ def time_attention(worker, reps=10):
     t = s.elapsed_time(e) / reps * 1e-3
     byts = float(lens.sum()) * Hkv * D * 2 * 2
     return byts, t, B, int(lens.sum())
+
+
+def time_attention_c4(reps=10, seed=3):
+    """The isolated paged-attention decode case: 128 sequences, context
+    U[1024, 32768], 32/8 heads, D 128, bf16 Q/K/V ~ N(0, 1), block size 16,
+    every block table a slice of a random permutation of a pool of
+    1.2 x the total tokens.  Returns (algorithmic bytes, seconds per launch,
+    sequences, total context)."""
+    from mu_b200 import kernels as K
+
+    Hq, Hkv, D, bs, B = 32, 8, 128, 16, 128
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(1024, 32768 + 1, B)
+    nblk = (ctx + bs - 1) // bs
+    pool = int(math.ceil(1.2 * ctx.sum() / bs))
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kc = torch.randn(pool, Hkv, bs, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(pool, Hkv, bs, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    perm = rng.permutation(pool)
+    bt = np.zeros((B, int(nblk.max())), np.int32)
+    i = 0
+    for b, n in enumerate(nblk):
+        bt[b, :n] = perm[i:i + n]
+        i += n
+    btd = torch.from_numpy(bt).cuda()
+    sl = torch.from_numpy(ctx.astype(np.int32)).cuda()
+    q = torch.randn(B, Hq * D, device="cuda", generator=g, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    mx = int(ctx.max())
+    ws = torch.empty(K.decode_attn_workspace_size(B, Hq, D, mx) // 4 + 4, device="cuda")
+
+    def fn():
+        K.decode_attn(q, out, kc, vc, btd, sl, Hq, Hkv, D, mx, workspace=ws)
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):  # the 10.5 GB pool is far larger than L2
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    t = s.elapsed_time(e) / reps * 1e-3
+    byts = float(ctx.sum()) * Hkv * D * 2 * 2
+    del kc, vc
+    torch.cuda.empty_cache()
+    return byts, t, B, int(ctx.sum())
+
+
+class GemmProbe:
+    """Times every muk_gemm_bf16 launch with CUDA events on the launching stream."""
+
+    def __init__(self):
+        self.recs = []
+
+    def __call__(self, flops):
+        import contextlib
+
+        @contextlib.contextmanager
+        def cm():
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            yield
+            e.record()
+            self.recs.append((flops, s, e))
+
+        return cm()
+
+    def result(self):
+        torch.cuda.synchronize()
+        flops = sum(f for f, _, _ in self.recs)
+        t = sum(s.elapsed_time(e) for _, s, e in self.recs) * 1e-3
+        return flops, t, len(self.recs)
 
 
 def time_gemms(worker, M=256, reps=10):
@@ -386,14 +496,16 @@ def run_ours(args, rank, world, local_rank):
     from mu_b200.core.config import SamplingParams
 
     torch.cuda.set_device(local_rank)
-    tp = world if args.parallel == "tp" else 1
-    engine, worker, ec = build(rank, tp)
+    wl = WORKLOADS[args.workload]
+    tp = world if args.parallel in ("tp", "ep") else 1
+    engine, worker, ec = build(rank, tp, wl, ep=args.parallel == "ep")
+    conc, out_tokens = wl["concurrency"], wl["out"]
     # tensor-parallel ranks serve the same requests; replicas serve their own
     seed_rank = 0 if tp > 1 else rank
-    arrivals = Arrivals(1000 + seed_rank, C3["vocab"])
+    arrivals = Arrivals(1000 + seed_rank, wl)
     rng = np.random.default_rng(7 + seed_rank)
-    for _ in range(CONCURRENCY):
-        arrivals.new_request(engine, SamplingParams, already=int(rng.integers(0, OUT_TOKENS)))
+    for _ in range(conc):
+        arrivals.new_request(engine, SamplingParams, already=int(rng.integers(0, out_tokens)))
     # initial fill: prefill every starting request (untimed)
     fill_steps = 0
     while engine.scheduler.waiting:
@@ -435,18 +547,19 @@ def run_ours(args, rank, world, local_rank):
     steps_meta = [(st.B, st.T, st.num_decode) for st, _ in rec.steps]
 
     # ---- value: same steps, arrays resident in HBM, no host work in between ----
-    sampler = engine.sampler
-    greedy_t = torch.zeros(CONCURRENCY * 2, device="cuda")
-    zeros_i = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int32)
-    ones_f = torch.ones(CONCURRENCY * 2, device="cuda")
-    seeds = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int64)
-    toks = torch.zeros(CONCURRENCY * 2, device="cuda", dtype=torch.int32)
+    temp, top_k, top_p = wl["sampling"]
+    temps = torch.full((conc * 2,), temp, device="cuda")
+    topks = torch.full((conc * 2,), top_k, device="cuda", dtype=torch.int32)
+    topps = torch.full((conc * 2,), top_p, device="cuda")
+    ones_f = torch.ones(conc * 2, device="cuda")
+    seeds = torch.zeros(conc * 2, device="cuda", dtype=torch.int64)
+    toks = torch.zeros(conc * 2, device="cuda", dtype=torch.int32)
 
     def replay():
         for st, buf in rec.steps:
             worker.packer.dev[:st.end].copy_(buf, non_blocking=True)
             logits, _ = worker.run_staged(st)
-            K.sample(logits, greedy_t, zeros_i, ones_f, ones_f, None, seeds, seeds, toks,
+            K.sample(logits, temps, topks, topps, ones_f, None, seeds, seeds, toks,
                      num_rows=st.B)
 
     replay()  # graphs for every bucket exist already; this warms the replay path
@@ -461,9 +574,17 @@ def run_ours(args, rank, world, local_rank):
     dev_t = s2.elapsed_time(e2) * 1e-3
 
     # ---- roofline pieces ------------------------------------------------------
-    hbm, tflops, peak_kind = peaks()
+    hbm, tflops, tflops_sus, peak_kind = peaks()
+    # the dominant kernel (GEMM, ~60 % of the step): every launch of the same
+    # steps timed with CUDA events (steps replayed from graphs are not seen)
+    probe = GemmProbe()
+    K.gemm_probe = probe
+    replay()
+    K.gemm_probe = None
+    gp_flops, gp_t, gp_n = probe.result()
     att_bytes, att_t, att_b, att_tok = time_attention(worker)
-    g_flops, g_t, g_wbytes = time_gemms(worker)
+    g_flops, g_t, g_wbytes = time_gemms(worker) if wl["arch"] == "llama" else (0.0, 0.0, 0.0)
+    c4 = time_attention_c4() if args.workload == "c3" and (rank == 0 or tp == 1) else None
 
     # ---- reduce over ranks ------------------------------------------------------
     vals = torch.tensor([n_tok, dev_t, e2e_t, wall], device="cuda", dtype=torch.float64)
@@ -480,15 +601,17 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return 0
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.workload == "c3":
         cb = CpuBaseline()
         per_tok = float(np.mean([cb.step() for _ in range(5)]))
         sample = cb.sample + ", mean of 5 steps"
         cpu = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
                "sample": sample}
     clk = clocks.summary()
+    c3 = args.workload == "c3"
+    par = {"tp": f"tp{tp}", "ep": f"tp{tp}+ep{tp}", "replicas": f"replicas{world}"}[args.parallel]
     line = {
-        "metric": METRIC,
+        "metric": METRIC if c3 else f"decode tokens/s ({args.workload})",
         "value": n_all / dev_max,
         "unit": "tokens/s",
         "n_gpus": world,
@@ -499,32 +622,55 @@ def run_ours(args, rank, world, local_rank):
         "scaling": "strong" if tp > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: random-init bf16 weights (seed 2), lognormal prompts, uniform ids",
+        "data": f"synthetic: random-init bf16 weights (seed {wl['seed']}), {wl['prompt'][0]} "
+                "prompt lengths, uniform ids",
         "config": {
-            "workload": WORKLOAD,
-            "model": "llama-3-8b-shape",
-            "global_batch": CONCURRENCY * (world // tp),
-            "seq_len": f"prompt lognormal(512, 0.8) in [32, 4096] + {OUT_TOKENS} generated",
-            "parallelism": (f"tp{tp}" if tp > 1 else f"replicas{world}") if world > 1 else "single",
-            "l2": "no flush needed: each step streams ~15 GB of weights and ~28 GB of KV (L2 126 MB)",
+            "workload": wl["desc"],
+            "model": {"c3": "llama-3-8b-shape", "c2": "deep-c2", "c5": "deep-c5"}[args.workload],
+            "global_batch": conc * (world // tp),
+            "seq_len": f"prompt {wl['prompt']} + {out_tokens} generated",
+            "parallelism": par if world > 1 else "single",
+            "l2": "no flush needed: each step streams the weights (GBs) and the KV of every "
+                  "running request (GBs) through HBM (L2 126 MB)",
             "tokens_timed": int(n_all),
             "steps_pure_decode": sum(1 for b, t, d in steps_meta if d == b),
             "mean_tokens_per_step": float(np.mean([t for _, t, _ in steps_meta])),
             "initial_fill_steps": fill_steps,
         },
         "e2e": {"value": n_all / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(4 * CONCURRENCY), "wall_s": wall_max,
+                "d2h_bytes_per_step": int(4 * conc), "wall_s": wall_max,
                 "api": "mu_b200.serving.engine.StepEngine.step"},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "muk_paged_decode_attn (layer, running batch)", "bound": "hbm",
-                     "achieved": att_bytes / att_t / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": att_bytes / att_t / 1e9 / hbm, "traffic": None,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "algorithmic_bytes": att_bytes, "seqs": att_b, "context_tokens": att_tok},
-        "roofline_gemm": {"kernel": "muk_gemm_bf16 decode layer (QKV+O+gate|up+down, M=256)",
-                          "bound": "tensor", "achieved": g_flops / g_t / 1e12, "peak": tflops,
-                          "unit": "TFLOP/s", "frac": g_flops / g_t / 1e12 / tflops,
-                          "weight_GBps": g_wbytes / g_t / 1e9, "peak_source": peak_kind},
+        "roofline": {"kernel": "muk_gemm_bf16 (every launch of the eager steps of the timed "
+                               "workload, CUDA events per launch)",
+                     "bound": "tensor", "achieved": gp_flops / gp_t / 1e12, "peak": tflops_sus,
+                     "unit": "TFLOP/s", "frac": gp_flops / gp_t / 1e12 / tflops_sus,
+                     "traffic": None,
+                     "traffic_note": "dram bytes per launch: profiles/gemm_step_shapes_llama3-8b.md",
+                     "peak_source": f"{peak_kind} sustained bf16 (MEASURED_PEAKS.json "
+                                    "bf16_tflops_sustained; kernel runs inside a long step)",
+                     "launches": gp_n, "flops_per_launch": gp_flops / max(gp_n, 1),
+                     "us_per_launch": gp_t / max(gp_n, 1) * 1e6},
+        "roofline_attention": {"kernel": "muk_paged_decode_attn (layer, running batch)",
+                               "bound": "hbm", "achieved": att_bytes / att_t / 1e9, "peak": hbm,
+                               "unit": "GB/s", "frac": att_bytes / att_t / 1e9 / hbm,
+                               "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                               "algorithmic_bytes": att_bytes, "seqs": att_b,
+                               "context_tokens": att_tok},
+        "roofline_attention_c4": None if c4 is None else {
+            "kernel": "muk_paged_decode_attn, 128 seqs ctx U[1024,32768], 32/8 heads D128, "
+                      "random-permutation block tables, pool 1.2x tokens",
+            "bound": "hbm", "achieved": c4[0] / c4[1] / 1e9, "peak": hbm, "unit": "GB/s",
+            "frac": c4[0] / c4[1] / 1e9 / hbm, "vs_8TBps": c4[0] / c4[1] / 8e12,
+            "algorithmic_bytes": c4[0], "us_per_launch": c4[1] * 1e6, "context_tokens": c4[3]},
+        "roofline_gemm_decode": None if not g_t else {
+                                 "kernel": "muk_gemm_bf16 decode layer (QKV+O+gate|up+down, "
+                                           "M=256)",
+                                 "bound": "tensor", "achieved": g_flops / g_t / 1e12,
+                                 "peak": tflops, "unit": "TFLOP/s",
+                                 "frac": g_flops / g_t / 1e12 / tflops,
+                                 "weight_GBps": g_wbytes / g_t / 1e9,
+                                 "peak_source": f"{peak_kind} burst bf16"},
         "cpu_baseline": cpu,
         "clocks": clk,
     }
@@ -600,8 +746,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--parallel", choices=["replicas", "tp"], default="replicas",
-                    help="N>1: independent replicas (default) or one tensor-parallel engine")
+    ap.add_argument("--parallel", choices=["replicas", "tp", "ep"], default="replicas",
+                    help="N>1: independent replicas (default), one tensor-parallel engine, or "
+                         "tensor-parallel attention with expert-parallel experts (Deep)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3",
+                    help="c3 (default, the headline), c2 / c5 (DeepForCausalLM)")
     ap.add_argument("--micro", choices=["decode_attn", "gemm"], default=None,
                     help="time one kernel on a small case (for ncu captures)")
     ap.add_argument("--seqs", type=int, default=64)

@@ -539,9 +539,17 @@ using namespace muk;
 extern "C" size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, int head_dim,
                                                  int max_seq_len, int block_size) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || block_size != kBlockSize) return 0;
-  DecodeSplit p = decode_split_policy(max_seq_len, num_seqs);
-  if (p.max_splits <= 1) return 0;
-  const size_t rows = (size_t)num_seqs * num_q_heads * p.max_splits;
+  // Smaller batches take shorter (so more) splits: size for the largest
+  // partial count of any batch of up to num_seqs sequences, so one buffer
+  // sized for the largest batch serves every smaller one.
+  size_t rows = 0;
+  for (int n = 1; n <= num_seqs; ++n) {
+    const DecodeSplit p = decode_split_policy(max_seq_len, n);
+    if (p.max_splits > 1) {
+      const size_t r = (size_t)n * num_q_heads * p.max_splits;
+      if (r > rows) rows = r;
+    }
+  }
   return rows * ((size_t)head_dim + 2) * sizeof(float);
 }
 

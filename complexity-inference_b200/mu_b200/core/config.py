@@ -198,6 +198,9 @@ class EngineConfig:
     device: str = "cuda"
     dtype: Literal["float16", "bfloat16", "float32"] = "float16"
     tensor_parallel_size: int = 1
+    # token-routed experts distributed whole over the tensor-parallel ranks
+    # (expert e on rank e // (E / P)) instead of split column-wise
+    expert_parallel: bool = False
     host: str = "0.0.0.0"
     port: int = 8080
     log_level: Literal["DEBUG", "INFO", "WARNING", "ERROR"] = "INFO"

@@ -177,8 +177,19 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epilogue: int = MUK_
     if B.shape[1] != K:
         raise ValueError(f"gemm: K mismatch A{tuple(A.shape)} B{tuple(B.shape)}")
     ldc = C.stride(-2)
-    call("muk_gemm_bf16", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"), _p(C), ldc, M, N,
-         K, epilogue, split_k, _p(bias), _stream())
+    args = ("muk_gemm_bf16", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"), _p(C), ldc, M,
+            N, K, epilogue, split_k, _p(bias), _stream())
+    if gemm_probe is None:
+        call(*args)
+    else:
+        with gemm_probe(2.0 * M * N * K):
+            call(*args)
+
+
+# Optional timing hook: a callable(flops) -> context manager wrapped around
+# every muk_gemm_bf16 launch (the benchmark uses it to time each launch with
+# CUDA events on the launching stream).
+gemm_probe = None
 
 
 def grouped_gemm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, expert_offsets: torch.Tensor,

@@ -43,6 +43,9 @@ class DeepForCausalLM(MuModelBase):
         self.i_pad = pad_to(inner, PAD_MULT)
         self.layers: List[Dict[str, torch.Tensor]] = []
         self.embed = self.norm_w = self.lm_w = None
+        # expert parallelism: this GPU holds experts [expert_lo, expert_lo + local_experts)
+        self.local_experts = config.num_experts if self.routed else 0
+        self.expert_lo = 0
 
     def act_width(self) -> int:
         return self.i_pad
@@ -101,9 +104,9 @@ class DeepForCausalLM(MuModelBase):
                 L["qn"] = f(a + "q_norm.weight")
                 L["kn"] = f(a + "k_norm.weight")
             if m.routed:
-                E = config.num_experts
-                gu = sd[p + "mlp.gate_up_proj"].to(dev, bf)   # [E, H, 2I]
+                gu = sd[p + "mlp.gate_up_proj"].to(dev, bf)   # [E, H, 2I] (local experts)
                 dn = sd[p + "mlp.down_proj"].to(dev, bf)      # [E, I, H]
+                E = m.local_experts = gu.shape[0]
                 Ie = gu.shape[2] // 2
                 L["wgu"] = torch.cat([interleave_gate_up(gu[e, :, :Ie].t(), gu[e, :, Ie:].t(), m.i_pad)
                                       for e in range(E)], 0).contiguous()
@@ -160,9 +163,13 @@ class DeepForCausalLM(MuModelBase):
             if self.routed:
                 K.route_permute(ws.eids, E, ws.offs, ws.perm, ws.inv, num_tokens=T)
                 K.gather_rows(ws.x2, ws.perm, ws.xs, num_rows=T)
-                K.grouped_gemm(ws.xs, L["wgu"], ws.act, ws.offs, E, 2 * self.i_pad,
+                El, e0 = self.local_experts, self.expert_lo
+                offs = ws.offs[e0:e0 + El + 1]   # rows of this GPU's experts (sorted order)
+                if El < E:  # other experts' rows arrive through the all-reduce
+                    ws.dpart[:T].zero_()
+                K.grouped_gemm(ws.xs, L["wgu"], ws.act, offs, El, 2 * self.i_pad,
                                K.MUK_EPI_SWIGLU, max_rows=T)
-                K.grouped_gemm(ws.act, L["wd"], ws.dpart, ws.offs, E, H, K.MUK_EPI_F32, max_rows=T)
+                K.grouped_gemm(ws.act, L["wd"], ws.dpart, offs, El, H, K.MUK_EPI_F32, max_rows=T)
                 self.reduce_partials(ws.dpart[:T])  # same expert order on every rank
                 K.residual_rmsnorm(resid, ws.dpart[:T], nxt_w, eps, nxt_out, clamp=cl,
                                    clamp_delta=True, clamp_sum=True, clamp_norm=True,

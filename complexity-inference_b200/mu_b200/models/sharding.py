@@ -8,11 +8,20 @@ Rank r of P keeps:
 * MLP: rows [r·I/P, (r+1)·I/P) of gate/up (column-parallel) and those
   columns of down (row-parallel); for token-routed experts the same split is
   applied inside every expert ([E, H, 2I] / [E, I, H] keep E whole);
+* with ``expert_parallel``, token-routed experts are instead kept whole and
+  distributed: rank r holds experts [r·E/P, (r+1)·E/P) (one per GPU when
+  P = E), so expert e lives on GPU e // (E/P).  Every rank routes every token
+  (the routing inputs are replicated), runs its own experts' tokens through
+  the grouped GEMMs and leaves the other rows zero;
 * everything else (embeddings, norms, LM head, INL dynamics, router) whole.
 
-After a row-parallel projection each rank holds a partial sum of the full
-[T, H] output; one all-reduce per projection (two per layer) restores it, so
-all ranks carry identical residual streams and sample identical tokens.
+After a row-parallel projection (or the expert MLP) each rank holds a
+partial sum of the full [T, H] output; one all-reduce per projection (two
+per layer) restores it, so all ranks carry identical residual streams and
+sample identical tokens.  Expert parallelism therefore needs no all-to-all:
+the tokens are already on every GPU (attention is head-parallel), and the
+all-reduce that follows the MLP carries each token's expert output from the
+GPU that owns the expert.
 The shard has the same names as the full dict and a ModelConfig whose head
 and intermediate counts are the local ones.
 """
@@ -28,11 +37,16 @@ from ..core.config import ModelConfig
 from .weights import expert_intermediate, is_routed
 
 
-def local_config(cfg: ModelConfig, arch: str, tp: int) -> ModelConfig:
+def local_config(cfg: ModelConfig, arch: str, tp: int, expert_parallel: bool = False
+                 ) -> ModelConfig:
     Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
     if Hq % tp or Hkv % tp:
         raise ValueError(f"tensor_parallel_size {tp} must divide heads {Hq}/{Hkv}")
-    if is_routed(arch, cfg):
+    if expert_parallel and is_routed(arch, cfg):
+        if cfg.num_experts % tp:
+            raise ValueError(f"tensor_parallel_size {tp} must divide num_experts {cfg.num_experts}")
+        inter = cfg.intermediate_size  # experts stay whole
+    elif is_routed(arch, cfg):
         ie = expert_intermediate(cfg)
         if ie % tp:
             raise ValueError(f"tensor_parallel_size {tp} must divide the expert width {ie}")
@@ -45,11 +59,21 @@ def local_config(cfg: ModelConfig, arch: str, tp: int) -> ModelConfig:
                                intermediate_size=inter, head_dim=cfg.head_dim)
 
 
+def expert_range(cfg: ModelConfig, rank: int, tp: int) -> Tuple[int, int]:
+    """Experts [lo, hi) held by ``rank`` under expert parallelism."""
+    n = cfg.num_experts // tp
+    return rank * n, (rank + 1) * n
+
+
 def shard_state_dict(sd: Dict[str, torch.Tensor], cfg: ModelConfig, arch: str, rank: int,
-                     tp: int) -> Tuple[Dict[str, torch.Tensor], ModelConfig]:
+                     tp: int, expert_parallel: bool = False
+                     ) -> Tuple[Dict[str, torch.Tensor], ModelConfig]:
     """The rank's shard of a full state dict plus its local ModelConfig."""
     if tp == 1:
         return dict(sd), cfg
+    ep = expert_parallel and is_routed(arch, cfg)
+    lcfg = local_config(cfg, arch, tp, ep)
+    e0, e1 = expert_range(cfg, rank, tp) if ep else (0, 0)
     D = cfg.head_dim
     hq = cfg.num_attention_heads // tp
     hkv = cfg.num_key_value_heads // tp
@@ -75,10 +99,12 @@ def shard_state_dict(sd: Dict[str, torch.Tensor], cfg: ModelConfig, arch: str, r
             out[name] = t[i0:i0 + il]
         elif leaf == "mlp.down_proj.weight" and not routed:
             out[name] = t[:, i0:i0 + il]
+        elif leaf in ("mlp.gate_up_proj", "mlp.down_proj") and ep:   # whole experts [e0, e1)
+            out[name] = t[e0:e1]
         elif leaf == "mlp.gate_up_proj":   # [E, H, 2I]: gate cols [0, I), up cols [I, 2I)
             out[name] = torch.cat([t[:, :, i0:i0 + il], t[:, :, ie + i0:ie + i0 + il]], 2)
         elif leaf == "mlp.down_proj" and routed:   # [E, I, H]
             out[name] = t[:, i0:i0 + il, :]
         else:
             out[name] = t
-    return {k: v.contiguous() for k, v in out.items()}, local_config(cfg, arch, tp)
+    return {k: v.contiguous() for k, v in out.items()}, lcfg

@@ -122,12 +122,18 @@ class MuWorker:
             if dist.get_world_size(group) != tp:
                 raise RuntimeError(f"tensor_parallel_size {tp} != group size "
                                    f"{dist.get_world_size(group)}")
-            sd, local = shard_state_dict(sd, model_config, arch, dist.get_rank(group), tp)
+            rank = dist.get_rank(group)
+            ep = bool(getattr(self.config, "expert_parallel", False))
+            sd, local = shard_state_dict(sd, model_config, arch, rank, tp, ep)
         self.model = build_model(arch, local, sd, self.config.mu, str(self.device))
         if tp > 1:
             import torch.distributed as dist
 
+            from ..models.sharding import expert_range
+
             self.model.tp_group = self.tp_group or dist.group.WORLD
+            if getattr(self.model, "local_experts", 0) and ep:
+                self.model.expert_lo = expert_range(model_config, rank, tp)[0]
         self._init_cache()
 
     def _init_cache(self) -> None:

@@ -108,7 +108,9 @@ int muk_rope_kv_append(void* qkv, int64_t qkv_stride, const int32_t* positions,
 
 /* ---- K2a: paged-attention decode (one query token per sequence) ---------- */
 
-/* Scratch bytes muk_paged_decode_attn needs for this shape (0 if none). */
+/* Scratch bytes muk_paged_decode_attn needs for any batch of up to num_seqs
+ * sequences whose contexts are at most max_seq_len (0 if none): one buffer of
+ * this size serves every smaller batch. */
 size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, int head_dim,
                                       int max_seq_len, int block_size);
 

@@ -484,3 +484,31 @@ def _check_stream_k(k, cuda, M, N, K, epi, code):
     from mu_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+def test_decode_workspace_covers_smaller_batches(cuda):
+    """A workspace sized for the largest batch must serve every smaller one
+    (smaller batches split their contexts more finely)."""
+    k = _kern()
+    Hq, Hkv, D, bs = 16, 8, 128, 16
+    max_len, max_seqs = 672, 64
+    ws_bytes = k.decode_attn_workspace_size(max_seqs, Hq, D, max_len)
+    ws = torch.empty(max(ws_bytes // 4, 4), device=cuda)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for B in (1, 5, 10, 40, 64):
+        nb = (max_len + bs - 1) // bs
+        kc = torch.randn(B * nb, Hkv, bs, D, device=cuda, generator=g).bfloat16()
+        vc = torch.randn(B * nb, Hkv, bs, D, device=cuda, generator=g).bfloat16()
+        bt = torch.arange(B * nb, device=cuda, dtype=torch.int32).view(B, nb)
+        sl = torch.full((B,), max_len, device=cuda, dtype=torch.int32)
+        q = torch.randn(B, Hq * D, device=cuda, generator=g).bfloat16()
+        out = torch.empty_like(q)
+        k.decode_attn(q, out, kc, vc, bt, sl, Hq, Hkv, D, max_len, workspace=ws)
+        Kf = kc.float().permute(0, 2, 1, 3).reshape(B, nb * bs, Hkv, D)[:, :max_len]
+        Vf = vc.float().permute(0, 2, 1, 3).reshape(B, nb * bs, Hkv, D)[:, :max_len]
+        Kf = Kf.repeat_interleave(Hq // Hkv, 2)
+        Vf = Vf.repeat_interleave(Hq // Hkv, 2)
+        qf = q.float().view(B, Hq, D)
+        att = torch.einsum("bhd,bthd->bht", qf, Kf) / math.sqrt(D)
+        ref = torch.einsum("bht,bthd->bhd", att.softmax(-1), Vf).reshape(B, Hq * D)
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)

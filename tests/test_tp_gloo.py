@@ -18,7 +18,7 @@ import torch.multiprocessing as mp
 
 from oracle import mu_oracle as O
 from golden_models import load_tiny
-from mu_b200.models.sharding import shard_state_dict
+from mu_b200.models.sharding import expert_range, shard_state_dict
 
 
 def _free_port():
@@ -35,8 +35,11 @@ def _allreduce(x):
     return t.numpy()
 
 
-def _tp_forward(model: O.OracleModel, ids):
-    """Prefill-only forward of a sharded OracleModel with all-reduces."""
+def _tp_forward(model: O.OracleModel, ids, experts=None):
+    """Prefill-only forward of a sharded OracleModel with all-reduces.
+
+    ``experts``: (lo, hi) when the shard holds whole experts [lo, hi)
+    (expert parallelism); tokens routed elsewhere contribute zero here."""
     s, p, mu = model.s, model.p, model.mu
     ids = np.asarray(ids)
     h = O._clamp(p["embed_tokens.weight"][ids].astype(np.float32), mu)
@@ -75,8 +78,15 @@ def _tp_forward(model: O.OracleModel, ids):
             e = O.route_experts(ids, mu_cur, p[pre + "mlp.mu_router.weight"], s.experts, s.vocab)
             gu, dn = p[pre + "mlp.gate_up_proj"], p[pre + "mlp.down_proj"]
             I = dn.shape[1]
-            part = np.stack([(O._silu(x2[t] @ gu[e[t]][:, :I]) * (x2[t] @ gu[e[t]][:, I:])) @ dn[e[t]]
-                             for t in range(S)])
+            lo, hi = experts if experts else (0, gu.shape[0])
+
+            def mlp(t):
+                if not lo <= e[t] < hi:
+                    return np.zeros(dn.shape[2], np.float32)
+                j = e[t] - lo
+                return (O._silu(x2[t] @ gu[j][:, :I]) * (x2[t] @ gu[j][:, I:])) @ dn[j]
+
+            part = np.stack([mlp(t) for t in range(S)])
             h = O._clamp(res + O._clamp(_allreduce(part), mu), mu)
             mu_prev = mu_cur
         else:
@@ -91,7 +101,7 @@ def _tp_forward(model: O.OracleModel, ids):
     return (hn[-1] @ p["lm_head.weight"].T).astype(np.float32)
 
 
-def _worker(rank, world, port, name, q):
+def _worker(rank, world, port, name, q, ep=False):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world,
@@ -101,12 +111,12 @@ def _worker(rank, world, port, name, q):
         return
     try:
         shape, cfg, sd, d, prompts = load_tiny(name)
-        shard, local = shard_state_dict(sd, cfg, shape.arch, rank, world)
+        shard, local = shard_state_dict(sd, cfg, shape.arch, rank, world, expert_parallel=ep)
         lshape = O.ModelShape(shape.arch, shape.hidden, shape.layers, local.num_attention_heads,
                               local.num_key_value_heads, shape.head_dim, shape.vocab,
                               experts=shape.experts, qk_norm=shape.qk_norm)
         model = O.OracleModel(lshape, {k: v.numpy() for k, v in shard.items()}, O.MuCfg(True))
-        logits = _tp_forward(model, prompts[0])
+        logits = _tp_forward(model, prompts[0], expert_range(cfg, rank, world) if ep else None)
         q.put((rank, logits))
     except Exception as e:
         import traceback
@@ -116,13 +126,15 @@ def _worker(rank, world, port, name, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
-def test_tp2_matches_unsharded(name):
+@pytest.mark.parametrize("name,ep", [("llama_tiny", False), ("deep_tiny", False),
+                                     ("deep_tiny", True)])
+def test_tp2_matches_unsharded(name, ep):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q, ep))
+             for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in range(world))
@@ -158,3 +170,10 @@ def test_shards_recombine(name):
         dn = torch.cat([s["layers.0.mlp.down_proj.weight"] for s in shards], 1)
         assert torch.equal(dn, sd["layers.0.mlp.down_proj.weight"])
     assert torch.equal(shards[1]["embed_tokens.weight"], sd["embed_tokens.weight"])
+    if shape.arch == "deep":  # expert parallelism: whole experts, split over the ranks
+        ep = [shard_state_dict(sd, cfg, shape.arch, r, tp, expert_parallel=True)[0]
+              for r in range(tp)]
+        for k in ("layers.0.mlp.gate_up_proj", "layers.0.mlp.down_proj"):
+            assert torch.equal(torch.cat([s[k] for s in ep]), sd[k])
+        assert ep[0]["layers.0.self_attn.q_proj.weight"].shape[0] == \
+            sd["layers.0.self_attn.q_proj.weight"].shape[0] // tp

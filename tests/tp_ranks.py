@@ -38,10 +38,12 @@ def main():
 
     worst = {}
     failures = []
-    for name, graphs in (("llama_tiny", False), ("llama_tiny", True), ("deep_tiny", False),
-                         ("deep_tiny", True)):
+    for name, graphs, ep in (("llama_tiny", False, False), ("llama_tiny", True, False),
+                             ("deep_tiny", False, False), ("deep_tiny", True, False),
+                             ("deep_tiny", False, True)):
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
+                          expert_parallel=ep,
                           cache=CacheConfig(max_seq_len=256, max_num_blocks=512, max_num_seqs=16),
                           scheduler=SchedulerConfig(max_batch_size=8, max_num_batched_tokens=2048))
         w = MuWorker(ec, f"cuda:{torch.cuda.current_device()}")
@@ -71,7 +73,7 @@ def main():
                     step_err.append((i, r, round(e, 5)))
         for r in range(R):
             w.free_request(f"r{r}")
-        worst[f"{name}/graphs={graphs}"] = err
+        worst[f"{name}/graphs={graphs}/ep={ep}"] = err
         if err > 2e-2:
             failures.append((name, graphs, rank, err, [x for x in step_err if x[2] > 2e-2][:6]))
         eng = StepEngine(w, ec)
