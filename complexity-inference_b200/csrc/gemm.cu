@@ -20,8 +20,9 @@
 // Tiles are ordered M-fastest so that the CTAs working on the row tiles of
 // one weight tile run at the same time and the weights stream from HBM once.
 //
-// Optional stream-K schedule (dense, split_k = 1; off unless enabled, see
-// streamk_enabled): when the tile count is not a multiple of the workers
+// Stream-K schedule (dense, split_k = 1; by default only for launches that
+// would leave most SMs idle, see streamk_mode): when the tile count is not a
+// multiple of the workers
 // (SMs, or SM pairs), whole waves of tiles run
 // data-parallel and the last one or two waves' k-iterations are divided
 // evenly over all workers, so no worker idles through a partial wave.  A tile
@@ -794,20 +795,31 @@ static double wave_eff(long tiles, int sms) {
 // slice pays for writing and re-reading an M x N f32 partial, which relative
 // to the GEMM's tensor time is about 860 / K (HBM ~6.5 TB/s vs ~1.4 PFLOP/s).
 // ---------------------------------------------------------------------------
-// Stream-K is off by default: on this power-capped part the SMs of a
-// partial last wave run at higher clocks, so balancing the wave bought
-// nothing measurable while the shared tiles cost their partial round trips
-// (809 x 6144 x 4096: 64 us stream-K vs 60 us data-parallel).  It stays
-// available (muk_gemm_set_stream_k, or MUK_GEMM_STREAMK=1) for parts and
-// shapes where it does pay.
+// Stream-K modes: 0 off, 1 on (the planner always weighs it), 2 auto (the
+// default): weighed only when a data-parallel launch would occupy at most a
+// quarter of the workers.  Measured on this power-capped part, stream-K lost
+// to data-parallel on well-filled shapes (809 x 6144 x 4096: 64 us vs 60 us;
+// SMs of a half-empty last wave run at higher clocks, so balancing the wave
+// bought little while the shared tiles cost their partial round trips), but
+// a launch of a few tiles (a 64-wide controller projection: 3 tiles on 148
+// SMs) leaves the GPU idle, which stream-K fixes.  muk_gemm_set_stream_k or
+// MUK_GEMM_STREAMK=0/1/2 selects the mode.
 static int g_streamk = -1;
 
-static bool streamk_enabled() {
+static int streamk_mode() {
   if (g_streamk < 0) {
     const char* e = getenv("MUK_GEMM_STREAMK");
-    g_streamk = (e && e[0] == '1') ? 1 : 0;
+    g_streamk = (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : 2;
   }
-  return g_streamk == 1;
+  return g_streamk;
+}
+
+static bool streamk_enabled() { return streamk_mode() != 0; }
+
+// Whether the planner may weigh stream-K for `tiles` tiles over `workers`.
+static bool streamk_allowed(long tiles, int workers) {
+  const int m = streamk_mode();
+  return m == 1 || (m == 2 && tiles * 4 <= workers);
 }
 
 struct GemmPlan {
@@ -858,6 +870,7 @@ static void sk_split(long tiles, int workers, long* dp, long* sk) {
 
 static double plan_cost(int kind, int bn, int split, bool sk, int M, int N, int K, int sms) {
   const PlanShape p = plan_shape(kind, bn, split, M, N, K, sms);
+  if (sk && !streamk_allowed(p.tiles, p.workers)) return 1e300;
   const int kps = (p.k_tiles + split - 1) / split;
   double steps;
   if (!sk) {
@@ -1197,8 +1210,8 @@ extern "C" int muk_gemm_plan_info(int M, int N, int K, int epilogue, int split_k
   return MUK_OK;
 }
 
-extern "C" int muk_gemm_set_stream_k(int enable) {
-  const int prev = streamk_enabled() ? 1 : 0;
-  g_streamk = enable ? 1 : 0;
+extern "C" int muk_gemm_set_stream_k(int mode) {
+  const int prev = streamk_mode();
+  g_streamk = (mode >= 0 && mode <= 2) ? mode : 2;
   return prev;
 }

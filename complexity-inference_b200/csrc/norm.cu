@@ -125,6 +125,89 @@ __global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const float* 
 }
 
 // ---------------------------------------------------------------------------
+// Same computation with the row held in registers: blockDim.x * VPT float4
+// = hidden, every load of a row issued before the first use (the generic
+// kernel above serialises them on its strided loop).
+template <int VPT>
+__global__ void __launch_bounds__(256, VPT <= 4 ? 4 : (VPT <= 8 ? 2 : 1))
+    residual_rmsnorm_vec_kernel(float* __restrict__ resid, const float* __restrict__ partials,
+                                int64_t partial_stride, int64_t partial_row_stride,
+                                int num_partials, const int32_t* __restrict__ delta_rows,
+                                const float* __restrict__ norm_w, float eps,
+                                __nv_bfloat16* __restrict__ out, int64_t out_stride, int hidden,
+                                int clamp_delta, int clamp_sum, ClampParams cp_norm,
+                                ClampParams cp) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int src = delta_rows ? delta_rows[t] : t;
+  float4* rrow = reinterpret_cast<float4*>(resid + (int64_t)t * hidden);
+  const int n = blockDim.x;
+  float4 r[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) r[i] = rrow[threadIdx.x + i * n];
+  if (num_partials > 0) {
+    float4 d[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) d[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < num_partials; ++p) {
+      const float4* prow = reinterpret_cast<const float4*>(partials + p * partial_stride +
+                                                           (int64_t)src * partial_row_stride);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const float4 x = prow[threadIdx.x + i * n];
+        d[i].x += x.x;
+        d[i].y += x.y;
+        d[i].z += x.z;
+        d[i].w += x.w;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      if (clamp_delta) {
+        d[i].x = mu_clamp(d[i].x, cp);
+        d[i].y = mu_clamp(d[i].y, cp);
+        d[i].z = mu_clamp(d[i].z, cp);
+        d[i].w = mu_clamp(d[i].w, cp);
+      }
+      r[i].x += d[i].x;
+      r[i].y += d[i].y;
+      r[i].z += d[i].z;
+      r[i].w += d[i].w;
+      if (clamp_sum) {
+        r[i].x = mu_clamp(r[i].x, cp);
+        r[i].y = mu_clamp(r[i].y, cp);
+        r[i].z = mu_clamp(r[i].z, cp);
+        r[i].w = mu_clamp(r[i].w, cp);
+      }
+      rrow[threadIdx.x + i * n] = r[i];
+    }
+  }
+  if (out == nullptr) return;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) ss += r[i].x * r[i].x + r[i].y * r[i].y + r[i].z * r[i].z + r[i].w * r[i].w;
+  const float inv = rsqrtf(block_sum(ss, red) / (float)hidden + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(norm_w);
+  uint2* orow = reinterpret_cast<uint2*>(out + (int64_t)t * out_stride);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const float4 w = w4[threadIdx.x + i * n];
+    uint2 o;
+    o.x = pack_bf16x2(mu_clamp(w.x * (r[i].x * inv), cp_norm), mu_clamp(w.y * (r[i].y * inv), cp_norm));
+    o.y = pack_bf16x2(mu_clamp(w.z * (r[i].z * inv), cp_norm), mu_clamp(w.w * (r[i].w * inv), cp_norm));
+    orow[threadIdx.x + i * n] = o;
+  }
+}
+
+// float4s per thread for the register-resident row kernels (0: use the
+// generic kernel): 256 threads when hidden is a multiple of 1024, else one
+// float4 per thread for hidden <= 4096 in whole warps.
+static int row_vpt(int hidden) {
+  if (hidden % 1024 == 0 && hidden / 1024 <= 16) return hidden / 1024;
+  if (hidden % 128 == 0 && hidden <= 4096) return -1;  // VPT 1, hidden / 4 threads
+  return 0;
+}
+
 __global__ void rmsnorm_rows_kernel(const float* __restrict__ resid, const int32_t* __restrict__ rows,
                                     const float* __restrict__ norm_w, float eps,
                                     __nv_bfloat16* __restrict__ out, int64_t out_stride, int hidden,
@@ -240,6 +323,128 @@ __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __
   }
 }
 
+// Register-resident INL step (same arithmetic as inl_dynamics_kernel):
+// blockDim.x * VPT float4 = hidden; all loads of a chunk issued together.
+template <int VPT>
+__global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
+    inl_dynamics_vec_kernel(const float* __restrict__ h, const float* __restrict__ ctrl_raw,
+                            const float* __restrict__ ctrl_bias, const float* __restrict__ muproj,
+                            const float* __restrict__ mu_param, float dt, float* __restrict__ v,
+                            __nv_bfloat16* __restrict__ v_bf16, int64_t v_bf16_stride,
+                            float* __restrict__ resid, __nv_bfloat16* __restrict__ mu_out,
+                            int64_t mu_out_stride, const float* __restrict__ norm_w, float eps,
+                            __nv_bfloat16* __restrict__ norm_out, int64_t norm_out_stride,
+                            const int32_t* __restrict__ token_ids,
+                            const __nv_bfloat16* __restrict__ router_w, int num_experts, int vocab,
+                            int32_t* __restrict__ expert_ids, int hidden, ClampParams cp_norm) {
+  __shared__ float red[32];
+  __shared__ float dots[kMaxExperts];
+  const int t = blockIdx.x;
+  const int n = blockDim.x;
+  const int64_t base4 = (int64_t)t * (hidden / 4);
+  const int H4 = hidden / 4;
+  const float4* h4 = reinterpret_cast<const float4*>(h) + base4;
+  const float4* c4 = reinterpret_cast<const float4*>(ctrl_raw) + (int64_t)t * 3 * H4;
+  const float4* b4 = reinterpret_cast<const float4*>(ctrl_bias);
+  const float4* mp4 = reinterpret_cast<const float4*>(muproj) + base4;
+  const float4* mu4 = reinterpret_cast<const float4*>(mu_param);
+  float4* v4 = reinterpret_cast<float4*>(v) + base4;
+  float4* r4 = reinterpret_cast<float4*>(resid) + base4;
+  float4 r[VPT];
+  float edot[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) edot[e] = 0.f;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int q = threadIdx.x + i * n;  // float4 index within the row
+    const float4 ca = c4[q], cb = c4[H4 + q], cg = c4[2 * H4 + q];
+    const float4 ba = b4[q], bb = b4[H4 + q], bg = b4[2 * H4 + q];
+    const float4 mpv = mp4[q], muv = mu4[q], hv = h4[q], vv = v4[q], rv = r4[q];
+    const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
+    const float cgv[4] = {cg.x, cg.y, cg.z, cg.w}, bav[4] = {ba.x, ba.y, ba.z, ba.w};
+    const float bbv[4] = {bb.x, bb.y, bb.z, bb.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
+    const float mpa[4] = {mpv.x, mpv.y, mpv.z, mpv.w}, mua[4] = {muv.x, muv.y, muv.z, muv.w};
+    const float ha[4] = {hv.x, hv.y, hv.z, hv.w}, va[4] = {vv.x, vv.y, vv.z, vv.w};
+    const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
+    float vn[4], rn[4], muc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a = sigmoidf_(cav[u] + bav[u]);
+      const float bta = fminf(softplusf_(cbv[u] + bbv[u]), 2.f);
+      const float g = sigmoidf_(cgv[u] + bgv[u]);
+      muc[u] = mua[u] + mpa[u];
+      float x = a * va[u] - bta * (ha[u] - muc[u]);
+      x = fminf(fmaxf(x, -10.f), 10.f);
+      vn[u] = x;
+      rn[u] = ra[u] + (ha[u] + dt * g * x);
+      ss += rn[u] * rn[u];
+    }
+    r[i] = make_float4(rn[0], rn[1], rn[2], rn[3]);
+    r4[q] = r[i];
+    v4[q] = make_float4(vn[0], vn[1], vn[2], vn[3]);
+    if (v_bf16) {
+      uint2 o;
+      o.x = pack_bf16x2(vn[0], vn[1]);
+      o.y = pack_bf16x2(vn[2], vn[3]);
+      *reinterpret_cast<uint2*>(v_bf16 + (int64_t)t * v_bf16_stride + 4 * q) = o;
+    }
+    if (mu_out) {
+      uint2 o;
+      o.x = pack_bf16x2(muc[0], muc[1]);
+      o.y = pack_bf16x2(muc[2], muc[3]);
+      *reinterpret_cast<uint2*>(mu_out + (int64_t)t * mu_out_stride + 4 * q) = o;
+    }
+    if (router_w) {
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e) {
+        if (e < num_experts) {
+          const uint2 w = *reinterpret_cast<const uint2*>(router_w + (int64_t)e * hidden + 4 * q);
+          const float2 w01 = unpack_bf16x2(w.x), w23 = unpack_bf16x2(w.y);
+          edot[e] += muc[0] * w01.x + muc[1] * w01.y + muc[2] * w23.x + muc[3] * w23.y;
+        }
+      }
+    }
+  }
+  const float total = block_sum(ss, red);
+  if (router_w) {
+    for (int e = 0; e < num_experts; ++e) {
+      const float d = block_sum(edot[e], red);
+      if (threadIdx.x == 0) dots[e] = d;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int id = token_ids[t];
+      id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+      const int base_e = id % num_experts;
+      int best = 0;
+      float bestv = -INFINITY;
+      for (int e = 0; e < num_experts; ++e) {
+        const float sc = (e == base_e ? 10.f : 0.f) + dots[e];
+        if (sc > bestv) {
+          bestv = sc;
+          best = e;
+        }
+      }
+      expert_ids[t] = best;
+    }
+  }
+  if (norm_out) {
+    const float inv = rsqrtf(total / (float)hidden + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(norm_w);
+    uint2* orow = reinterpret_cast<uint2*>(norm_out + (int64_t)t * norm_out_stride);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int q = threadIdx.x + i * n;
+      const float4 w = w4[q];
+      uint2 o;
+      o.x = pack_bf16x2(mu_clamp(w.x * (r[i].x * inv), cp_norm), mu_clamp(w.y * (r[i].y * inv), cp_norm));
+      o.y = pack_bf16x2(mu_clamp(w.z * (r[i].z * inv), cp_norm), mu_clamp(w.w * (r[i].w * inv), cp_norm));
+      orow[q] = o;
+    }
+  }
+}
+
 }  // namespace muk
 
 using namespace muk;
@@ -276,10 +481,35 @@ extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t
               "muk_residual_rmsnorm: out needs norm_w and an even stride >= hidden");
   if (num_tokens == 0) return MUK_OK;
   ClampParams cp = make_clamp(1, mu, clamp_min, clamp_max);
-  residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), as_stream(stream)>>>(
-      resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps,
-      reinterpret_cast<__nv_bfloat16*>(out), out_stride, hidden, clamp_delta, clamp_sum,
-      make_clamp(clamp_norm, mu, clamp_min, clamp_max), cp);
+  const ClampParams cpn = make_clamp(clamp_norm, mu, clamp_min, clamp_max);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+  const int vpt = row_vpt(hidden);
+  const bool vec_ok = vpt != 0 && MUK_ALIGNED16(norm_w) && out_stride % 4 == 0 &&
+                      (partial_row_stride % 4 == 0) && (out == nullptr || ((uintptr_t)out & 7) == 0);
+  cudaStream_t st = as_stream(stream);
+#define MUK_RRN(V, THREADS)                                                                     \
+  residual_rmsnorm_vec_kernel<V><<<num_tokens, THREADS, 0, st>>>(                              \
+      resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps, \
+      o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp)
+  if (vec_ok) {
+    switch (vpt) {
+      case -1: MUK_RRN(1, hidden / 4); break;
+      case 1: MUK_RRN(1, 256); break;
+      case 2: MUK_RRN(2, 256); break;
+      case 4: MUK_RRN(4, 256); break;
+      case 8: MUK_RRN(8, 256); break;
+      case 16: MUK_RRN(16, 256); break;
+      default:
+        residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+            resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w,
+            eps, o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp);
+    }
+  } else {
+    residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+        resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps,
+        o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp);
+  }
+#undef MUK_RRN
   return check_launch("muk_residual_rmsnorm");
 }
 
@@ -331,11 +561,40 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
               "muk_inl_dynamics: routing needs token_ids, expert_ids and 1..%d experts",
               kMaxExperts);
   if (num_tokens == 0) return MUK_OK;
-  inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), as_stream(stream)>>>(
-      h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, reinterpret_cast<__nv_bfloat16*>(v_bf16),
-      v_bf16_stride, resid, reinterpret_cast<__nv_bfloat16*>(mu_out), mu_out_stride, norm_w, eps,
-      reinterpret_cast<__nv_bfloat16*>(norm_out), norm_out_stride, token_ids,
-      reinterpret_cast<const __nv_bfloat16*>(router_w), num_experts, vocab, expert_ids, hidden,
-      make_clamp(clamp_norm, mu, clamp_min, clamp_max));
+  cudaStream_t st = as_stream(stream);
+  const ClampParams cpn = make_clamp(clamp_norm, mu, clamp_min, clamp_max);
+  __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(v_bf16);
+  __nv_bfloat16* mo = reinterpret_cast<__nv_bfloat16*>(mu_out);
+  __nv_bfloat16* no = reinterpret_cast<__nv_bfloat16*>(norm_out);
+  const __nv_bfloat16* rw = reinterpret_cast<const __nv_bfloat16*>(router_w);
+  const int vpt = row_vpt(hidden);
+  const bool vec_ok = vpt != 0 && MUK_ALIGNED16(h) && MUK_ALIGNED16(ctrl_raw) &&
+                      MUK_ALIGNED16(ctrl_bias) && MUK_ALIGNED16(muproj) &&
+                      MUK_ALIGNED16(mu_param) && MUK_ALIGNED16(v) && MUK_ALIGNED16(resid) &&
+                      (norm_out == nullptr || (MUK_ALIGNED16(norm_w) && norm_out_stride % 4 == 0 &&
+                                               ((uintptr_t)norm_out & 7) == 0)) &&
+                      (v_bf16 == nullptr || (v_bf16_stride % 4 == 0 && ((uintptr_t)v_bf16 & 7) == 0)) &&
+                      (mu_out == nullptr || (mu_out_stride % 4 == 0 && ((uintptr_t)mu_out & 7) == 0)) &&
+                      (router_w == nullptr || ((uintptr_t)router_w & 7) == 0);
+#define MUK_INL(V, THREADS)                                                                      \
+  inl_dynamics_vec_kernel<V><<<num_tokens, THREADS, 0, st>>>(                                   \
+      h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,            \
+      mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,        \
+      expert_ids, hidden, cpn)
+  if (vec_ok && vpt == -1) {
+    MUK_INL(1, hidden / 4);
+  } else if (vec_ok && vpt == 1) {
+    MUK_INL(1, 256);
+  } else if (vec_ok && vpt == 2) {
+    MUK_INL(2, 256);
+  } else if (vec_ok && vpt == 4) {
+    MUK_INL(4, 256);
+  } else {
+    inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,
+        mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
+        expert_ids, hidden, cpn);
+  }
+#undef MUK_INL
   return check_launch("muk_inl_dynamics");
 }

@@ -111,6 +111,113 @@ __global__ void rope_kv_append_kernel(__nv_bfloat16* __restrict__ qkv, int64_t q
   }
 }
 
+// Token-per-CTA variant: thread = (head, unit) where a unit is 8 elements
+// of the first half of the head and their 8 rotate-half partners (two 16-byte
+// loads and stores).  The D/16 units of a head are consecutive lanes, so the
+// QK-norm reduction is a shuffle over D/16 lanes; cos/sin of the token's
+// position are read once per unit and shared by all heads through L1.
+__global__ void rope_kv_append_vec_kernel(__nv_bfloat16* __restrict__ qkv, int64_t qkv_stride,
+                                          const int32_t* __restrict__ positions,
+                                          const int32_t* __restrict__ slot_mapping,
+                                          const float* __restrict__ rope_cos,
+                                          const float* __restrict__ rope_sin, int max_pos,
+                                          int num_q_heads, int num_kv_heads, int head_dim,
+                                          const float* __restrict__ q_norm_w,
+                                          const float* __restrict__ k_norm_w, float qk_eps,
+                                          __nv_bfloat16* __restrict__ k_cache,
+                                          __nv_bfloat16* __restrict__ v_cache, int num_blocks,
+                                          int block_size) {
+  const int t = blockIdx.x;
+  const int upd = head_dim >> 4;  // units per head (power of two, <= 32)
+  const int h = threadIdx.x / upd;
+  const int c = threadIdx.x - h * upd;
+  const int half = head_dim >> 1;
+  const bool is_q = h < num_q_heads;
+  const bool is_k = !is_q && h < num_q_heads + num_kv_heads;
+  __nv_bfloat16* row = qkv + (int64_t)t * qkv_stride + (int64_t)h * head_dim;
+  const int i0 = c * 8;
+  uint4 lo = *reinterpret_cast<const uint4*>(row + i0);
+  uint4 hi = *reinterpret_cast<const uint4*>(row + half + i0);
+
+  // No early returns: every lane takes part in the QK-norm shuffle below.
+  __nv_bfloat16* dst = row;
+  bool store = true;
+  if (!is_q) {
+    const int slot = slot_mapping[t];
+    const int blk = slot < 0 ? 0 : slot / block_size;
+    const int off = slot < 0 ? 0 : slot - blk * block_size;
+    if (slot < 0) store = false;  // padding token: nothing to append
+    if (blk >= num_blocks) {
+      if (c == 0) set_device_error(kDevBadIndex);
+      store = false;
+    }
+    const int kvh = is_k ? h - num_q_heads : h - num_q_heads - num_kv_heads;
+    dst = (is_k ? k_cache : v_cache) + (((int64_t)(store ? blk : 0) * num_kv_heads + kvh) *
+                                            block_size + off) * head_dim;
+  }
+  const bool rot = is_q || is_k;
+  int pos = positions[t];
+  if (pos < 0 || pos >= max_pos) {
+    if (rot && c == 0) set_device_error(kDevBadIndex);
+    if (rot) store = false;
+    pos = 0;
+  }
+  float a[8], b[8];
+  {
+    const uint32_t* lw = reinterpret_cast<const uint32_t*>(&lo);
+    const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hi);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 x = unpack_bf16x2(lw[u]), y = unpack_bf16x2(hw[u]);
+      a[2 * u] = x.x;
+      a[2 * u + 1] = x.y;
+      b[2 * u] = y.x;
+      b[2 * u + 1] = y.y;
+    }
+  }
+  if (q_norm_w != nullptr || k_norm_w != nullptr) {  // uniform over the CTA
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ss += a[u] * a[u] + b[u] * b[u];
+    // heads never straddle a warp: upd divides 32 and the block is whole heads
+    for (int m = upd >> 1; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    const float* nw = is_q ? q_norm_w : (is_k ? k_norm_w : nullptr);
+    if (nw != nullptr) {
+      const float inv = rsqrtf(ss / (float)head_dim + qk_eps);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        a[u] = nw[i0 + u] * (a[u] * inv);
+        b[u] = nw[half + i0 + u] * (b[u] * inv);
+      }
+    }
+  }
+  if (!rot) {  // v: copy
+    if (store) {
+      *reinterpret_cast<uint4*>(dst + i0) = lo;
+      *reinterpret_cast<uint4*>(dst + half + i0) = hi;
+    }
+    return;
+  }
+  const float4* cs = reinterpret_cast<const float4*>(rope_cos + (int64_t)pos * half + i0);
+  const float4* sn = reinterpret_cast<const float4*>(rope_sin + (int64_t)pos * half + i0);
+  const float4 c0 = cs[0], c1 = cs[1], s0 = sn[0], s1 = sn[1];
+  const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  uint4 olo, ohi;
+  uint32_t* ol = reinterpret_cast<uint32_t*>(&olo);
+  uint32_t* oh = reinterpret_cast<uint32_t*>(&ohi);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int e = 2 * u;
+    ol[u] = pack_bf16x2(a[e] * cv[e] - b[e] * sv[e], a[e + 1] * cv[e + 1] - b[e + 1] * sv[e + 1]);
+    oh[u] = pack_bf16x2(b[e] * cv[e] + a[e] * sv[e], b[e + 1] * cv[e + 1] + a[e + 1] * sv[e + 1]);
+  }
+  if (store) {
+    *reinterpret_cast<uint4*>(dst + i0) = olo;
+    *reinterpret_cast<uint4*>(dst + half + i0) = ohi;
+  }
+}
+
 }  // namespace muk
 
 using namespace muk;
@@ -134,6 +241,19 @@ extern "C" int muk_rope_kv_append(void* qkv, int64_t qkv_stride, const int32_t* 
   MUK_REQUIRE(block_size > 0 && num_blocks > 0 && max_pos > 0, "muk_rope_kv_append: bad cache");
   if (num_tokens <= 0) return MUK_OK;
   const int heads = num_q_heads + 2 * num_kv_heads;
+  const int upd = head_dim / 16;
+  const int vec_threads = heads * upd;
+  if (head_dim % 16 == 0 && (upd & (upd - 1)) == 0 && upd <= 32 && vec_threads <= 1024 &&
+      vec_threads % 32 == 0 && qkv_stride % 8 == 0 && MUK_ALIGNED16(qkv) &&
+      MUK_ALIGNED16(k_cache) && MUK_ALIGNED16(v_cache) && MUK_ALIGNED16(rope_cos) &&
+      MUK_ALIGNED16(rope_sin)) {
+    rope_kv_append_vec_kernel<<<num_tokens, vec_threads, 0, as_stream(stream)>>>(
+        reinterpret_cast<__nv_bfloat16*>(qkv), qkv_stride, positions, slot_mapping, rope_cos,
+        rope_sin, max_pos, num_q_heads, num_kv_heads, head_dim, q_norm_w, k_norm_w, qk_eps,
+        reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache),
+        num_blocks, block_size);
+    return check_launch("muk_rope_kv_append");
+  }
   const int64_t items = (int64_t)num_tokens * heads;
   const int warps = 8;
   const int64_t grid = (items + warps - 1) / warps;

@@ -280,6 +280,7 @@ def gemm_plan_info(M: int, N: int, K: int, epilogue: int, split_k: int = 1) -> d
     return dict(zip(keys, list(out)))
 
 
-def gemm_set_stream_k(enable: bool) -> bool:
-    """Let the GEMM planner use stream-K schedules; returns the previous setting."""
-    return bool(_lib.load().muk_gemm_set_stream_k(int(bool(enable))))
+def gemm_set_stream_k(mode: int) -> int:
+    """GEMM stream-K planning mode (0 off, 1 on, 2 auto = only for launches
+    that would leave most SMs idle); returns the previous mode."""
+    return int(_lib.load().muk_gemm_set_stream_k(int(mode)))

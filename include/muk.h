@@ -193,10 +193,12 @@ int muk_gemm_plan_split(int M, int N, int K, int epilogue, int max_split);
  * No counterpart in the reference (introspection for tests and tuning). */
 int muk_gemm_plan_info(int M, int N, int K, int epilogue, int split_k, int32_t* out);
 
-/* Lets the planner consider stream-K schedules (enable != 0) or not (the
- * default, also set by MUK_GEMM_STREAMK=1 in the environment); returns the
- * previous setting.  Process-wide.  No counterpart in the reference. */
-int muk_gemm_set_stream_k(int enable);
+/* Stream-K planning mode: 0 never, 1 whenever the planner's cost model
+ * prefers it, 2 (default) only for launches whose data-parallel schedule
+ * would occupy at most a quarter of the SMs.  Also set by MUK_GEMM_STREAMK
+ * in the environment.  Returns the previous mode.  Process-wide.  No
+ * counterpart in the reference. */
+int muk_gemm_set_stream_k(int mode);
 
 /* ---- K4: token-routed experts -------------------------------------------- */
 

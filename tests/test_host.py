@@ -209,7 +209,15 @@ def test_gemm_planner_schedules():
 
     p = K.gemm_plan_info(809, 6144, 4096, K.MUK_EPI_BF16)  # default: data-parallel
     assert p["stream_k"] == 0 and p["dp_tiles"] == 96 and p["workers"] == 74
-    prev = K.gemm_set_stream_k(True)
+    # default (auto): a 64-wide projection of 300 rows is 3 tiles -> stream-K
+    p = K.gemm_plan_info(300, 64, 4096, K.MUK_EPI_BIAS_SILU)
+    assert p["stream_k"] == 1 and p["sk_tiles"] == 3 and 3 < p["workers"] <= 12
+    prev = K.gemm_set_stream_k(0)
+    try:
+        assert K.gemm_plan_info(300, 64, 4096, K.MUK_EPI_BIAS_SILU)["stream_k"] == 0
+    finally:
+        K.gemm_set_stream_k(prev)
+    prev = K.gemm_set_stream_k(1)
     try:
         p = K.gemm_plan_info(809, 6144, 4096, K.MUK_EPI_BF16)  # 96 pair tiles on 74 pairs
         assert p["kernel"] == 1 and p["stream_k"] == 1 and p["sk_tiles"] == 96

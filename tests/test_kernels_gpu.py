@@ -103,7 +103,11 @@ def _rope_tables(max_pos, D, theta, device):
     return f.cos().to(device), f.sin().to(device)
 
 
-@pytest.mark.parametrize("D,Hq,Hkv,qk_norm", [(128, 32, 8, False), (64, 4, 2, True)])
+# token-per-CTA layout (D/16 lanes per head, heads of several kinds sharing a
+# warp in the small cases) and the warp-per-head fallback (D = 96)
+@pytest.mark.parametrize("D,Hq,Hkv,qk_norm", [(128, 32, 8, False), (64, 4, 2, True),
+                                              (128, 32, 8, True), (256, 8, 2, True),
+                                              (96, 4, 2, True)])
 def test_rope_kv_append(cuda, D, Hq, Hkv, qk_norm):
     k = _kern()
     T, NB, bs = 37, 20, 16
@@ -234,11 +238,14 @@ def _mu_clamp(x, mu=0.0, lo=-10.0, hi=10.0):
     return mu + torch.tanh((x - mu - c) / r) * r + c
 
 
-def test_residual_rmsnorm_and_embed(cuda):
+# hidden sizes reach every row-kernel layout: one float4 per thread (512),
+# 2 and 4 float4 per thread over 256 threads (2048, 4096), generic loop (320)
+@pytest.mark.parametrize("H", [512, 2048, 4096, 320])
+def test_residual_rmsnorm_and_embed(cuda, H):
     k = _kern()
     from mu_b200.kernels import Clamp
 
-    T, H, V, P = 19, 512, 300, 3
+    T, V, P = 19, 300, 3
     g = torch.Generator(device="cuda").manual_seed(9)
     table = torch.randn(V, H, device=cuda, generator=g).mul(5).bfloat16()
     ids = torch.randint(0, V, (T,), device=cuda, generator=g, dtype=torch.int32)
@@ -265,11 +272,12 @@ def test_residual_rmsnorm_and_embed(cuda):
     torch.testing.assert_close(out2.float(), n_ref[rows.long()], rtol=1e-2, atol=1e-2)
 
 
-def test_inl_dynamics_and_routing(cuda):
+@pytest.mark.parametrize("H", [256, 2048, 4096, 320])
+def test_inl_dynamics_and_routing(cuda, H):
     k = _kern()
     from mu_b200.kernels import Clamp
 
-    T, H, E, V = 23, 256, 4, 1000
+    T, E, V = 23, 4, 1000
     g = torch.Generator(device="cuda").manual_seed(4)
     h = torch.randn(T, H, device=cuda, generator=g)
     ctrl = torch.randn(T, 3 * H, device=cuda, generator=g)
@@ -450,7 +458,7 @@ def test_gemm_stream_k(cuda, M, N, K, epi):
     k = _kern()
     code = {"f32": k.MUK_EPI_F32, "bf16": k.MUK_EPI_BF16, "swiglu": k.MUK_EPI_SWIGLU,
             "bias_silu": k.MUK_EPI_BIAS_SILU}[epi]
-    prev = k.gemm_set_stream_k(True)
+    prev = k.gemm_set_stream_k(1)
     try:
         _check_stream_k(k, cuda, M, N, K, epi, code)
     finally:
