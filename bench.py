@@ -114,6 +114,11 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            # nvidia-smi's start-up (NVML init on every GPU) must not fall in
+            # the timed region: wait for its first sample
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 10.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -481,10 +486,11 @@ def run_reference_arm(args, rank, world):
 
 
 def release(worker):
-    """Drop captured CUDA graphs (they may hold NCCL calls) before the process group goes."""
+    """Drop captured CUDA graphs (they may hold NCCL calls) and peer mappings
+    before the process group goes."""
     import gc
 
-    worker._graphs.clear()
+    worker.close()
     gc.collect()
     torch.cuda.synchronize()
 
@@ -528,6 +534,8 @@ def run_ours(args, rank, world, local_rank):
     launches0 = _lib.launch_count
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
         start.record()

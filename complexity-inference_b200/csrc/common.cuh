@@ -30,6 +30,7 @@ enum DeviceError : int {
   kDevTimeoutAccum = 3,   // epilogue waited too long for the accumulator
   kDevBadShape = 4,       // a kernel saw an argument outside its contract
   kDevBadIndex = 5,       // an index (slot, block id, token id) out of range
+  kDevTimeoutPeer = 6,    // a peer GPU did not reach a cross-GPU barrier in time
 };
 
 extern __device__ int g_device_error;

@@ -57,6 +57,11 @@ SIGNATURES = {
     "muk_gemm_plan_split": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "muk_gemm_plan_info": (c_int, [c_int, c_int, c_int, c_int, c_int, _P]),
     "muk_gemm_set_stream_k": (c_int, [c_int]),
+    "muk_ipc_get_handle": (c_int, [_P, _P, POINTER(c_uint64)]),
+    "muk_ipc_open_handle": (c_int, [_P, c_uint64, POINTER(c_void_p), POINTER(c_void_p)]),
+    "muk_ipc_close_handle": (c_int, [_P]),
+    "muk_allreduce_flag_bytes": (c_size_t, []),
+    "muk_allreduce_f32": (c_int, [_P, _P, c_int, c_int, c_int64, _P]),
     "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
@@ -119,6 +124,14 @@ def call(name: str, *args) -> None:
         raise MukError(name, rc, last_error())
     if name != "muk_device_error":
         launch_count += 2 if name in _TWO_KERNELS else 1
+
+
+def call_status(name: str, *args) -> None:
+    """Call a status-returning entry point that launches no kernel."""
+    fn = getattr(load(), name)
+    rc = fn(*args)
+    if rc != MUK_OK:
+        raise MukError(name, rc, last_error())
 
 
 def device_error() -> int:

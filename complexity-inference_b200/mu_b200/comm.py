@@ -1,0 +1,89 @@
+"""Tensor-parallel all-reduce over NVLink peer memory (libmuk's
+``muk_allreduce_f32``), the replacement for the NCCL all-reduce after the
+row-parallel projections.
+
+Each rank allocates one symmetric buffer (PyTorch memory; the same size and
+layout on every rank), exports it through CUDA IPC and maps every peer's
+buffer.  The model writes its partial projection outputs into the buffer;
+``all_reduce_(t)`` then sums ``t`` (a view of the buffer) across the ranks in
+place, with both cross-GPU barriers inside the kernel, so the call is
+stream-ordered like any other kernel and can be captured in a CUDA graph.
+The handle exchange uses the torch.distributed process group once, at
+construction.  There is no counterpart in the reference, which has no
+multi-GPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+class PeerAllReduce:
+    def __init__(self, group, max_elems: int, device):
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("PeerAllReduce supports at most 8 ranks")
+        lib = _lib.load()
+        flag_words = int(lib.muk_allreduce_flag_bytes()) // 4
+        self.max_elems = (int(max_elems) + 63) // 64 * 64
+        # [data f32 | flags]; the flag area must start zeroed on every rank
+        self.buf = torch.zeros(self.max_elems + flag_words, dtype=torch.float32, device=device)
+        torch.cuda.synchronize(device)
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_uint64()
+        _lib.call_status("muk_ipc_get_handle", self.buf.data_ptr(), ctypes.addressof(handle),
+                         ctypes.byref(off))
+        mine = (bytes(handle), int(off.value))
+        objs = [None] * self.world
+        dist.all_gather_object(objs, mine, group=group)
+        self._bases = []
+        ptrs = []
+        for r, (h, o) in enumerate(objs):
+            if r == self.rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            p, base = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.call_status("muk_ipc_open_handle", ctypes.addressof(hb), o, ctypes.byref(p),
+                             ctypes.byref(base))
+            ptrs.append(p.value)
+            self._bases.append(base.value)
+        self.ptrs = ptrs
+        self.flag_ptrs = [p + self.max_elems * 4 for p in ptrs]
+        self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self._flags = (ctypes.c_void_p * self.world)(*self.flag_ptrs)
+        dist.barrier(group=group)
+
+    def view(self, n: int) -> torch.Tensor:
+        """The first n elements of this rank's buffer (the model writes partials here)."""
+        if n > self.max_elems:
+            raise ValueError(f"PeerAllReduce: {n} elements > capacity {self.max_elems}")
+        return self.buf[:n]
+
+    def owns(self, t: torch.Tensor) -> bool:
+        p = t.data_ptr()
+        return (self.buf.data_ptr() <= p and p + t.numel() * 4 <= self.buf.data_ptr()
+                + self.max_elems * 4 and t.is_contiguous())
+
+    def all_reduce_(self, t: torch.Tensor) -> None:
+        """Sum ``t`` (a contiguous f32 view of the buffer) over the ranks, in place."""
+        if not self.owns(t):
+            raise ValueError("PeerAllReduce.all_reduce_: tensor is not a view of the buffer")
+        off = t.data_ptr() - self.buf.data_ptr()
+        bufs = (ctypes.c_void_p * self.world)(*[p + off for p in self.ptrs])
+        _lib.call("muk_allreduce_f32", ctypes.addressof(bufs), ctypes.addressof(self._flags),
+                  self.rank, self.world, t.numel(), torch.cuda.current_stream().cuda_stream)
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        for b in self._bases:
+            _lib.call_status("muk_ipc_close_handle", b)
+        self._bases = []

@@ -89,7 +89,12 @@ class Workspace:
         self.qkv = torch.empty(T, (Hq + 2 * Hkv) * D, device=dev, dtype=bf)
         self.attn = torch.empty(T, Hq * D, device=dev, dtype=bf)
         self.part_rows = max(T, 2048)
-        self.part = torch.empty(self.part_rows * model.max_part_width(), device=dev, dtype=f32)
+        n = self.part_rows * model.max_part_width()
+        # under tensor parallelism the partials live in the peer-mapped buffer
+        # that the all-reduce kernel sums in place
+        comm = getattr(model, "comm", None)
+        self.shared_part = comm is not None and n <= comm.max_elems
+        self.part = comm.view(n) if self.shared_part else torch.empty(n, device=dev, dtype=f32)
         self.act = torch.empty(T, model.act_width(), device=dev, dtype=bf)
         self.xl = torch.empty(max_seqs, H, device=dev, dtype=bf)
         self.logits = torch.empty(max_seqs, cfg.vocab_size, device=dev, dtype=f32)
@@ -118,6 +123,7 @@ class MuModelBase:
         self.rope_sin: Optional[torch.Tensor] = None
         self._rope_len = 0
         self.tp_group = None   # torch.distributed group when tensor-parallel
+        self.comm = None       # mu_b200.comm.PeerAllReduce when tensor-parallel over NVLink
         self.ensure_rope(max(config.max_position_embeddings, 16))
 
     # ---- overridable sizes ---------------------------------------------------
@@ -126,6 +132,10 @@ class MuModelBase:
 
     def max_part_width(self) -> int:
         return self.config.hidden_size
+
+    def part_elems(self, max_tokens: int) -> int:
+        """f32 elements of the partial buffer for a workspace of max_tokens rows."""
+        return max(max_tokens, 2048) * self.max_part_width()
 
     def extra_workspace(self, ws: Workspace, T: int) -> None:
         pass
@@ -160,8 +170,14 @@ class MuModelBase:
 
     # ---- shared pieces of the step ---------------------------------------------
     def reduce_partials(self, part: torch.Tensor) -> None:
-        """Sum a row-parallel projection's partial output over the TP ranks (NCCL)."""
-        if self.tp_group is not None:
+        """Sum a row-parallel projection's partial output over the TP ranks:
+        in place through peer memory when the partials sit in the shared
+        buffer (``muk_allreduce_f32``), else with an NCCL all-reduce."""
+        if self.tp_group is None:
+            return
+        if self.comm is not None and self.comm.owns(part):
+            self.comm.all_reduce_(part)
+        else:
             import torch.distributed as dist
 
             dist.all_reduce(part, group=self.tp_group)

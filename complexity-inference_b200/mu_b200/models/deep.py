@@ -61,7 +61,11 @@ class DeepForCausalLM(MuModelBase):
         ws.mp = torch.empty(T, H, device=dev, dtype=torch.float32)
         ws.x2 = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
         ws.xs = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        ws.dpart = torch.empty(T, H, device=dev, dtype=torch.float32)
+        # the expert MLP's output is reduced over TP ranks like the partials:
+        # under peer-memory TP it shares their buffer (the O partials are
+        # consumed before the down GEMM writes it)
+        ws.dpart = (ws.part[:T * H].view(T, H) if ws.shared_part
+                    else torch.empty(T, H, device=dev, dtype=torch.float32))
         ws.eids = torch.zeros(T, device=dev, dtype=torch.int32)
         ws.offs = torch.zeros(max(cfg.num_experts, 1) + 1, device=dev, dtype=torch.int32)
         ws.perm = torch.arange(T, device=dev, dtype=torch.int32)

@@ -19,6 +19,7 @@ cost of the Python layer loop.
 from __future__ import annotations
 
 import logging
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -146,6 +147,13 @@ class MuWorker:
         max_blocks = (max_len + cc.block_size - 1) // cc.block_size + 1
         max_seqs = max(cc.max_num_seqs, sc.max_batch_size)
         max_tokens = max(sc.max_num_batched_tokens, max_seqs)
+        if self.model.tp_group is not None and os.environ.get("MU_TP_COMM", "peer") == "peer":
+            from ..comm import PeerAllReduce
+
+            # partials of every step size this worker will run (the workspace
+            # may round T up to a CUDA-graph bucket)
+            cap = self.model.part_elems(max(max_tokens, _bucket(max_seqs)))
+            self.model.comm = PeerAllReduce(self.model.tp_group, cap, self.device)
         self.packer = StepPacker(self.device, max_tokens, max_seqs, max_blocks)
         self.model.ensure_workspace(max_tokens, max_seqs, max_blocks * cc.block_size)
         self._graphs.clear()
@@ -214,9 +222,11 @@ class MuWorker:
                                             self._decode_bound())
         if grew:
             self._graphs.clear()
-        # Tensor-parallel steps run eagerly: replaying graphs that captured the
-        # torch NCCL all-reduce gave wrong results after the first replays.
-        graph = self.use_graphs and self.model.tp_group is None and num_decode == B and B > 0
+        # Tensor-parallel steps with the NCCL all-reduce run eagerly: replaying
+        # graphs that captured the torch NCCL all-reduce gave wrong results
+        # after the first replays.  The peer-memory all-reduce is graph-safe.
+        tp_ok = self.model.tp_group is None or self.model.comm is not None
+        graph = self.use_graphs and tp_ok and num_decode == B and B > 0
         allseq = seqs
         if graph:
             bucket = _bucket(B)
@@ -296,6 +306,14 @@ class MuWorker:
                 if r.request_id not in out or out[r.request_id].error is None:
                     out[r.request_id] = WorkerOutput(r.request_id, torch.zeros(1, V), True, str(e))
         return [out[r.request_id] for r in requests]
+
+    def close(self) -> None:
+        """Release CUDA graphs and peer mappings (before the process group goes)."""
+        self._graphs.clear()
+        comm = getattr(self.model, "comm", None) if self.model is not None else None
+        if comm is not None:
+            comm.close()
+            self.model.comm = None
 
     def get_stats(self) -> Dict:
         return {

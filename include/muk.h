@@ -283,6 +283,38 @@ int muk_mark_seen(uint32_t* seen_bits, int64_t seen_stride, const int32_t* rows,
 int muk_fill_decode_inputs(int32_t* input_ids, const int32_t* src, const int32_t* sampled, int n,
                            void* stream);
 
+/* ---- Tensor-parallel collectives over NVLink peer memory ------------------ */
+
+/* CUDA IPC export of the allocation holding dev_ptr: a 64-byte handle for
+ * the allocation and dev_ptr's byte offset inside it.  The reference has no
+ * multi-GPU path (mu_inference/core/config.py:304 declares
+ * tensor_parallel_size; nothing reads it). */
+int muk_ipc_get_handle(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+
+/* Maps a peer's allocation (handle from muk_ipc_get_handle on another
+ * process) into this process: *dev_ptr_out = mapped base + offset;
+ * *base_out is what muk_ipc_close_handle takes. */
+int muk_ipc_open_handle(const void* handle, uint64_t offset, void** dev_ptr_out,
+                        void** base_out);
+int muk_ipc_close_handle(void* base);
+
+/* Bytes of the flag area each rank keeps (zeroed before first use) for
+ * muk_allreduce_f32. */
+size_t muk_allreduce_flag_bytes(void);
+
+/* In-place sum of n f32 elements (n % 4 == 0) across `world` ranks (<= 8):
+ * bufs[s] / flags[s] are rank s's buffer range and flag area as mapped in
+ * this process (bufs[rank] / flags[rank] are this rank's own).  Rank r
+ * reduces its 1/world of the range in rank order 0..world-1 and writes the
+ * sum into every rank's buffer, between two cross-GPU barriers on the flags,
+ * so every rank ends with bit-identical sums.  All ranks must make the same
+ * sequence of calls (same n, same order).  Waits are bounded (5 s; then the
+ * device error word reads 6 and the result is undefined).  Replaces the NCCL
+ * all-reduce after the row-parallel projections; graph-capturable (the
+ * barrier epoch lives in the flag area). */
+int muk_allreduce_f32(float* const* bufs, uint32_t* const* flags, int rank, int world, int64_t n,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,53 @@ import torch.distributed as dist  # noqa: E402
 from golden_models import load_tiny  # noqa: E402
 
 
+def check_peer_allreduce(rank, world, failures):
+    """muk_allreduce_f32 alone: sums equal the NCCL reference on every rank,
+    bit-identical across ranks, also when replayed from a CUDA graph."""
+    from mu_b200.comm import PeerAllReduce
+
+    comm = PeerAllReduce(dist.group.WORLD, 1 << 20, torch.device("cuda"))
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    for n in (4, 1000, 1 << 20):
+        x = comm.view(n)
+        x.copy_(torch.randn(n, device="cuda", generator=g))
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.clone())
+        ref = torch.stack(parts).sum(0)   # rank order, like the kernel
+        comm.all_reduce_(x)
+        torch.cuda.synchronize()
+        if not torch.allclose(x, ref, rtol=1e-6, atol=1e-6):
+            failures.append(("peer allreduce", n, float((x - ref).abs().max())))
+        allx = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(allx, x)
+        if not all(torch.equal(a, allx[0]) for a in allx):
+            failures.append(("peer allreduce not identical across ranks", n))
+    # graph capture and replay
+    n = 4096
+    x = comm.view(n)
+    src = torch.empty(n, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        x.copy_(src)
+        comm.all_reduce_(x)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        x.copy_(src)
+        comm.all_reduce_(x)
+    for it in range(3):
+        src.copy_(torch.full((n,), float(rank + 1 + it), device="cuda"))
+        graph.replay()
+        torch.cuda.synchronize()
+        want = float(sum(r + 1 + it for r in range(world)))
+        if not torch.all(x == want):
+            failures.append(("peer allreduce graph replay", it, float(x[0])))
+    del graph
+    comm.close()
+    dist.barrier()
+
+
 def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -38,9 +85,15 @@ def main():
 
     worst = {}
     failures = []
-    for name, graphs, ep in (("llama_tiny", False, False), ("llama_tiny", True, False),
-                             ("deep_tiny", False, False), ("deep_tiny", True, False),
-                             ("deep_tiny", False, True)):
+    check_peer_allreduce(rank, world, failures)
+    # (model, CUDA graphs, expert parallel, all-reduce: peer memory or NCCL)
+    for name, graphs, ep, comm in (("llama_tiny", False, False, "nccl"),
+                                   ("llama_tiny", True, False, "peer"),
+                                   ("llama_tiny", False, False, "peer"),
+                                   ("deep_tiny", False, False, "nccl"),
+                                   ("deep_tiny", True, False, "peer"),
+                                   ("deep_tiny", True, True, "peer")):
+        os.environ["MU_TP_COMM"] = comm
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
                           expert_parallel=ep,
@@ -73,7 +126,7 @@ def main():
                     step_err.append((i, r, round(e, 5)))
         for r in range(R):
             w.free_request(f"r{r}")
-        worst[f"{name}/graphs={graphs}/ep={ep}"] = err
+        worst[f"{name}/graphs={graphs}/ep={ep}/{comm}"] = err
         if err > 2e-2:
             failures.append((name, graphs, rank, err, [x for x in step_err if x[2] > 2e-2][:6]))
         eng = StepEngine(w, ec)
@@ -89,7 +142,7 @@ def main():
         for g in allg:
             if not torch.equal(g, allg[0]):
                 failures.append((name, graphs, rank, "ranks generated different tokens"))
-        w._graphs.clear()  # graphs holding NCCL calls must go before the process group
+        w.close()  # graphs (which may hold NCCL calls) and peer mappings go before the group
         del eng, w
     from mu_b200 import _lib
 
