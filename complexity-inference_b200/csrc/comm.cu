@@ -4,24 +4,27 @@
 // tensor_parallel_size but nothing reads it).
 //
 // Every rank owns one symmetric buffer (same layout on all ranks) that the
-// others map through CUDA IPC.  The kernel sums a range of f32 elements
-// across the ranks in place:
-//   1. barrier A: each rank tells every peer "my data is ready" (a release
-//      store of the step's epoch into the peer's flag slot) and waits until
-//      all peers have said so;
-//   2. reduce-scatter + push: rank r sums its 1/P of the range over all P
-//      buffers in rank order 0..P-1 (so every rank ends with bit-identical
-//      values) and stores the sum into every rank's buffer;
-//   3. barrier B: the last CTA of each rank signals the peers and waits for
-//      them, so when the kernel ends every rank's buffer holds the full sum
-//      and no peer still reads or writes it.
-// Traffic per rank: (P-1)/P of the range read and written over NVLink, the
-// same as a ring all-reduce.  The epoch lives in device memory and is bumped
-// by the kernel itself, so the launch can sit inside a CUDA graph.  Every
-// wait is bounded by %globaltimer; on time-out the kernel records
-// kDevTimeoutPeer and returns (the result is then undefined, the device error
-// word says so).  Loads and stores are plain P2P accesses, no TMA and no
-// multicast.
+// others map through CUDA IPC: a data range (the partials, overwritten with
+// the sum), a scratch area of world x share floats and a flag area.  Two
+// kernels, in which every NVLink access is a store (stores are posted, loads
+// over NVLink would stall on the round trip):
+//   push    rank r stores share s of its data into rank s's scratch slot r,
+//           for every peer s; its last CTA then signals "pushed" (a release
+//           store of the call's epoch into every peer's flag slot r);
+//   finish  waits for every peer's "pushed", sums share r over the ranks in
+//           rank order 0..P-1 (own data + the P-1 scratch slots, all local
+//           reads), stores the sum into share r of every rank's data, and its
+//           last CTA signals "done" and waits for every peer's "done".
+// When finish ends, every rank's data range holds the full, bit-identical
+// sum and no peer still touches this rank's buffer.  NVLink bytes per rank:
+// 2 (P-1)/P of the range out, like a ring all-reduce.  The kernel boundary
+// between push and finish is the grid-wide barrier inside each rank, so no
+// CTA ever waits on another CTA of its own grid.  The epoch lives in the
+// flag area and is bumped by finish, so both launches can sit inside a CUDA
+// graph.  Every wait is bounded by %globaltimer; on time-out the kernel
+// records kDevTimeoutPeer and returns (the result is then undefined, the
+// device error word says so).  Plain P2P stores and local loads; no TMA and
+// no multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -36,19 +39,37 @@ namespace muk {
 
 constexpr int kMaxRanks = 8;
 constexpr int kArThreads = 512;
-// flag area (uint32 words) at the caller-given offset of every rank's buffer
-constexpr int kFlagA = 0;          // [kMaxRanks] "data ready" epochs, by source rank
+// flag area (uint32 words) of every rank
+constexpr int kFlagA = 0;          // [kMaxRanks] "pushed" epochs, by source rank
 constexpr int kFlagB = kMaxRanks;  // [kMaxRanks] "done" epochs, by source rank
 constexpr int kFlagEpoch = 2 * kMaxRanks;
-constexpr int kFlagArrive = 2 * kMaxRanks + 1;
+constexpr int kFlagArrive1 = 2 * kMaxRanks + 1;
+constexpr int kFlagArrive2 = 2 * kMaxRanks + 2;
 constexpr uint64_t kPeerTimeoutNs = 5ull * 1000 * 1000 * 1000;  // 5 s
 
 struct ArArgs {
-  float* buf[kMaxRanks];
+  float4* data[kMaxRanks];     // each rank's data range (as mapped here)
+  float4* scratch[kMaxRanks];  // each rank's scratch area: [world][share] float4
   uint32_t* flags[kMaxRanks];
   int rank, world;
-  int64_t n4;  // float4 elements in the range
+  int64_t n4;     // float4 elements in the range (one slice)
+  int64_t share;  // float4 elements per rank share = ceil(n4 / world)
+  int slices;     // the data holds `slices` partial slices summed first (split-K)
+  int64_t slice_stride4;
 };
+
+// Sum of the slices of this rank's data at float4 index i (slice 0 first).
+__device__ __forceinline__ float4 folded(const ArArgs& a, const float4* src, int64_t i) {
+  float4 v = src[i];
+  for (int q = 1; q < a.slices; ++q) {
+    const float4 x = src[(int64_t)q * a.slice_stride4 + i];
+    v.x += x.x;
+    v.y += x.y;
+    v.z += x.z;
+    v.w += x.w;
+  }
+  return v;
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -81,28 +102,55 @@ __device__ bool wait_all(const uint32_t* flags, int base, int world, uint32_t ep
   return true;
 }
 
-__global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const ArArgs a) {
+// True in exactly one thread of the grid: the last CTA to arrive (its thread
+// 0), after every thread's earlier stores were fenced system-wide.
+__device__ __forceinline__ bool last_cta(uint32_t* counter) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return false;
+  const uint32_t prev = atomicAdd(counter, 1u);
+  if (prev != gridDim.x - 1) return false;
+  *counter = 0u;  // ready for the next call
+  __threadfence_system();
+  return true;
+}
+
+__global__ void __launch_bounds__(kArThreads) allreduce_push_kernel(const ArArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) + 1u;
+  const float4* src = a.data[a.rank];
+  // share s of my data -> rank s's scratch slot [rank], for every peer s
+  const int64_t total = a.share * a.world;
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(j / a.share);
+    const int64_t k = j - (int64_t)s * a.share;
+    const int64_t i = (int64_t)s * a.share + k;
+    if (s == a.rank || i >= a.n4) continue;
+    a.scratch[s][(int64_t)a.rank * a.share + k] = folded(a, src, i);
+  }
+  if (last_cta(my + kFlagArrive1))
+    for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagA + a.rank, epoch);
+}
+
+__global__ void __launch_bounds__(kArThreads) allreduce_finish_kernel(const ArArgs a) {
   uint32_t* my = a.flags[a.rank];
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) + 1u;
   __shared__ int ok;
-  // ---- barrier A ----
-  if (blockIdx.x == 0 && threadIdx.x < a.world) {
-    __threadfence_system();
-    st_release_sys(a.flags[threadIdx.x] + kFlagA + a.rank, epoch);
-  }
   if (threadIdx.x == 0) ok = wait_all(my, kFlagA, a.world, epoch);
   __syncthreads();
   if (ok) {
-    // ---- reduce my share, push to every rank ----
-    const int64_t share = (a.n4 + a.world - 1) / a.world;
-    const int64_t lo = share * a.rank;
-    const int64_t hi = lo + share < a.n4 ? lo + share : a.n4;
+    const int64_t lo = (int64_t)a.rank * a.share;
+    const int64_t hi = lo + a.share < a.n4 ? lo + a.share : a.n4;
+    const float4* own = a.data[a.rank];
+    const float4* scr = a.scratch[a.rank];
     for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi;
          i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t k = i - lo;
       float4 v[kMaxRanks];
 #pragma unroll
       for (int s = 0; s < kMaxRanks; ++s)
-        if (s < a.world) v[s] = reinterpret_cast<const float4*>(a.buf[s])[i];
+        if (s < a.world) v[s] = s == a.rank ? folded(a, own, i) : scr[(int64_t)s * a.share + k];
       float4 sum = v[0];
 #pragma unroll
       for (int s = 1; s < kMaxRanks; ++s)
@@ -114,21 +162,13 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const ArArgs 
         }
 #pragma unroll
       for (int s = 0; s < kMaxRanks; ++s)
-        if (s < a.world) reinterpret_cast<float4*>(a.buf[s])[i] = sum;
+        if (s < a.world) a.data[s][i] = sum;
     }
   }
-  __threadfence_system();  // this thread's pushes reach the peers before the signal
-  __syncthreads();
-  // ---- barrier B (the last CTA of this rank) ----
-  if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(my + kFlagArrive, 1u);
-    if (prev == gridDim.x - 1) {
-      my[kFlagArrive] = 0u;
-      __threadfence_system();
-      for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagB + a.rank, epoch);
-      wait_all(my, kFlagB, a.world, epoch);
-      *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) = epoch;
-    }
+  if (last_cta(my + kFlagArrive2)) {
+    for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagB + a.rank, epoch);
+    wait_all(my, kFlagB, a.world, epoch);
+    *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) = epoch;
   }
 }
 
@@ -209,29 +249,49 @@ extern "C" int muk_ipc_close_handle(void* base) {
 
 extern "C" size_t muk_allreduce_flag_bytes(void) { return 64 * sizeof(uint32_t); }
 
-extern "C" int muk_allreduce_f32(float* const* bufs, uint32_t* const* flags, int rank, int world,
-                                 int64_t n, void* stream) {
-  MUK_REQUIRE(bufs && flags && world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world,
+extern "C" int64_t muk_allreduce_scratch_elems(int64_t n, int world) {
+  if (n < 0 || world < 1) return 0;
+  const int64_t n4 = (n + 3) / 4;
+  return ((n4 + world - 1) / world) * world * 4;
+}
+
+extern "C" int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags,
+                                 int rank, int world, int64_t n, int slices, int64_t slice_stride,
+                                 void* stream) {
+  MUK_REQUIRE(bufs && scratch && flags && world >= 1 && world <= kMaxRanks && rank >= 0 &&
+                  rank < world,
               "muk_allreduce_f32: rank %d of %d (at most %d ranks)", rank, world, kMaxRanks);
   MUK_REQUIRE(n >= 0 && n % 4 == 0, "muk_allreduce_f32: n=%lld must be a multiple of 4",
               (long long)n);
+  MUK_REQUIRE(slices >= 1 && (slices == 1 || (slice_stride >= n && slice_stride % 4 == 0)),
+              "muk_allreduce_f32: %d slices need a slice stride >= n, multiple of 4", slices);
   ArArgs a;
   for (int s = 0; s < kMaxRanks; ++s) {
-    a.buf[s] = s < world ? bufs[s] : nullptr;
+    a.data[s] = s < world ? reinterpret_cast<float4*>(bufs[s]) : nullptr;
+    a.scratch[s] = s < world ? reinterpret_cast<float4*>(scratch[s]) : nullptr;
     a.flags[s] = s < world ? flags[s] : nullptr;
   }
   for (int s = 0; s < world; ++s)
-    MUK_REQUIRE(a.buf[s] && a.flags[s] && MUK_ALIGNED16(a.buf[s]) && MUK_ALIGNED16(a.flags[s]),
-                "muk_allreduce_f32: rank %d buffer or flags null / not 16-byte aligned", s);
+    MUK_REQUIRE(a.data[s] && a.scratch[s] && a.flags[s] && MUK_ALIGNED16(a.data[s]) &&
+                    MUK_ALIGNED16(a.scratch[s]) && MUK_ALIGNED16(a.flags[s]),
+                "muk_allreduce_f32: rank %d buffer, scratch or flags null / not 16-byte aligned",
+                s);
   a.rank = rank;
   a.world = world;
   a.n4 = n / 4;
-  if (world == 1) return MUK_OK;
-  // enough CTAs to cover this rank's share once, at most two per SM
-  const int64_t share = (a.n4 + world - 1) / world;
-  int grid = (int)((share + kArThreads - 1) / kArThreads);
-  if (grid > 296) grid = 296;
-  if (grid < 1) grid = 1;
-  allreduce_f32_kernel<<<grid, kArThreads, 0, as_stream(stream)>>>(a);
-  return check_launch("muk_allreduce_f32");
+  a.share = (a.n4 + world - 1) / world;
+  a.slices = slices;
+  a.slice_stride4 = slice_stride / 4;
+  if (n == 0) return MUK_OK;
+  if (world == 1 && slices == 1) return MUK_OK;
+  cudaStream_t st = as_stream(stream);
+  int grid = (int)((a.share * (world - 1) + kArThreads - 1) / kArThreads);
+  grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
+  allreduce_push_kernel<<<grid, kArThreads, 0, st>>>(a);
+  int rc = check_launch("muk_allreduce_f32(push)");
+  if (rc) return rc;
+  grid = (int)((a.share + kArThreads - 1) / kArThreads);
+  grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
+  allreduce_finish_kernel<<<grid, kArThreads, 0, st>>>(a);
+  return check_launch("muk_allreduce_f32(finish)");
 }

@@ -61,7 +61,8 @@ SIGNATURES = {
     "muk_ipc_open_handle": (c_int, [_P, c_uint64, POINTER(c_void_p), POINTER(c_void_p)]),
     "muk_ipc_close_handle": (c_int, [_P]),
     "muk_allreduce_flag_bytes": (c_size_t, []),
-    "muk_allreduce_f32": (c_int, [_P, _P, c_int, c_int, c_int64, _P]),
+    "muk_allreduce_scratch_elems": (c_int64, [c_int64, c_int]),
+    "muk_allreduce_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int64, c_int, c_int64, _P]),
     "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
@@ -82,7 +83,7 @@ _lib: ctypes.CDLL | None = None
 # Kernel launches issued through call() (entry points that launch two kernels
 # count both); the benchmark reports it as its launch count.
 launch_count = 0
-_TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static"}
+_TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32"}
 
 
 class MukError(RuntimeError):

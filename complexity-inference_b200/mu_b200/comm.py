@@ -6,8 +6,10 @@ Each rank allocates one symmetric buffer (PyTorch memory; the same size and
 layout on every rank), exports it through CUDA IPC and maps every peer's
 buffer.  The model writes its partial projection outputs into the buffer;
 ``all_reduce_(t)`` then sums ``t`` (a view of the buffer) across the ranks in
-place, with both cross-GPU barriers inside the kernel, so the call is
-stream-ordered like any other kernel and can be captured in a CUDA graph.
+place (two kernels: NVLink stores of each share to its owner, then the
+owner's rank-ordered sum stored to every rank, with the cross-GPU barriers
+inside the kernels), so the call is stream-ordered like any other kernel and
+can be captured in a CUDA graph.
 The handle exchange uses the torch.distributed process group once, at
 construction.  There is no counterpart in the reference, which has no
 multi-GPU path.
@@ -34,8 +36,11 @@ class PeerAllReduce:
         lib = _lib.load()
         flag_words = int(lib.muk_allreduce_flag_bytes()) // 4
         self.max_elems = (int(max_elems) + 63) // 64 * 64
-        # [data f32 | flags]; the flag area must start zeroed on every rank
-        self.buf = torch.zeros(self.max_elems + flag_words, dtype=torch.float32, device=device)
+        self.scratch_elems = (int(lib.muk_allreduce_scratch_elems(self.max_elems, self.world))
+                              + 63) // 64 * 64
+        # [data | scratch (world shares) | flags], f32; the flag area starts zeroed
+        self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words,
+                               dtype=torch.float32, device=device)
         torch.cuda.synchronize(device)
         handle = (ctypes.c_uint8 * 64)()
         off = ctypes.c_uint64()
@@ -45,6 +50,7 @@ class PeerAllReduce:
         objs = [None] * self.world
         dist.all_gather_object(objs, mine, group=group)
         self._bases = []
+        self._data_arrays = {}
         ptrs = []
         for r, (h, o) in enumerate(objs):
             if r == self.rank:
@@ -57,8 +63,9 @@ class PeerAllReduce:
             ptrs.append(p.value)
             self._bases.append(base.value)
         self.ptrs = ptrs
-        self.flag_ptrs = [p + self.max_elems * 4 for p in ptrs]
-        self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.scratch_ptrs = [p + self.max_elems * 4 for p in ptrs]
+        self.flag_ptrs = [p + (self.max_elems + self.scratch_elems) * 4 for p in ptrs]
+        self._scratch = (ctypes.c_void_p * self.world)(*self.scratch_ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*self.flag_ptrs)
         dist.barrier(group=group)
 
@@ -73,14 +80,23 @@ class PeerAllReduce:
         return (self.buf.data_ptr() <= p and p + t.numel() * 4 <= self.buf.data_ptr()
                 + self.max_elems * 4 and t.is_contiguous())
 
-    def all_reduce_(self, t: torch.Tensor) -> None:
-        """Sum ``t`` (a contiguous f32 view of the buffer) over the ranks, in place."""
+    def all_reduce_(self, t: torch.Tensor, slices: int = 1) -> torch.Tensor:
+        """Sum ``t`` (a contiguous f32 view of the buffer) over the ranks, in
+        place.  With ``slices`` > 1, ``t`` is [slices, ...] split-K partials:
+        they are folded first and the sum lands in ``t[0]``, which is returned
+        (else ``t``)."""
         if not self.owns(t):
             raise ValueError("PeerAllReduce.all_reduce_: tensor is not a view of the buffer")
+        n = t.numel() // slices
         off = t.data_ptr() - self.buf.data_ptr()
-        bufs = (ctypes.c_void_p * self.world)(*[p + off for p in self.ptrs])
-        _lib.call("muk_allreduce_f32", ctypes.addressof(bufs), ctypes.addressof(self._flags),
-                  self.rank, self.world, t.numel(), torch.cuda.current_stream().cuda_stream)
+        bufs = self._data_arrays.get(off)
+        if bufs is None:
+            bufs = self._data_arrays[off] = (ctypes.c_void_p * self.world)(
+                *[p + off for p in self.ptrs])
+        _lib.call("muk_allreduce_f32", ctypes.addressof(bufs), ctypes.addressof(self._scratch),
+                  ctypes.addressof(self._flags), self.rank, self.world, n, slices, n,
+                  torch.cuda.current_stream().cuda_stream)
+        return t[0] if slices > 1 else t
 
     def close(self) -> None:
         torch.cuda.synchronize()

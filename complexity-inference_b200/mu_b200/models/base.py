@@ -169,18 +169,23 @@ class MuModelBase:
         return True
 
     # ---- shared pieces of the step ---------------------------------------------
-    def reduce_partials(self, part: torch.Tensor) -> None:
-        """Sum a row-parallel projection's partial output over the TP ranks:
-        in place through peer memory when the partials sit in the shared
-        buffer (``muk_allreduce_f32``), else with an NCCL all-reduce."""
+    def reduce_partials(self, part: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel projection's output over the TP ranks and return
+        what the consumer reads: in place through peer memory when the
+        partials sit in the shared buffer (``muk_allreduce_f32``; split-K
+        slices [S, T, N] are folded first and the sum returned as [1, T, N]),
+        else with an NCCL all-reduce of every slice."""
         if self.tp_group is None:
-            return
+            return part
         if self.comm is not None and self.comm.owns(part):
-            self.comm.all_reduce_(part)
-        else:
-            import torch.distributed as dist
+            if part.dim() == 3:
+                return self.comm.all_reduce_(part, slices=part.shape[0]).unsqueeze(0) \
+                    if part.shape[0] > 1 else self.comm.all_reduce_(part)
+            return self.comm.all_reduce_(part)
+        import torch.distributed as dist
 
-            dist.all_reduce(part, group=self.tp_group)
+        dist.all_reduce(part, group=self.tp_group)
+        return part
 
     def attention(self, layer: int, batch, cache, q_norm_w=None, k_norm_w=None) -> torch.Tensor:
         """RoPE + KV append, then paged decode / varlen prefill attention -> ws.attn."""

@@ -152,7 +152,7 @@ class DeepForCausalLM(MuModelBase):
             s = choose_split(T, H, attn.shape[1], ws.part_rows)
             part = ws.part_view(s, T, H)
             K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            self.reduce_partials(part)
+            part = self.reduce_partials(part)
             K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)   # h = clamp(o_proj)
             K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
             K.gemm(ws.ch, L["wco"], ws.ctrl, K.MUK_EPI_F32, M=T)
@@ -183,7 +183,7 @@ class DeepForCausalLM(MuModelBase):
                 s = choose_split(T, H, self.i_pad, ws.part_rows)
                 part = ws.part_view(s, T, H)
                 K.gemm(ws.act, L["wd"], part, K.MUK_EPI_F32, split_k=s, M=T)
-                self.reduce_partials(part)
+                part = self.reduce_partials(part)
                 K.residual_rmsnorm(resid, part, nxt_w, eps, nxt_out, clamp=cl, clamp_delta=True,
                                    clamp_sum=True, clamp_norm=True)
         return self.lm_head(batch, self.norm_w, self.lm_w)

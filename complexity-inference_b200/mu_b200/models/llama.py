@@ -97,7 +97,7 @@ class LlamaForCausalLM(MuModelBase):
             s = choose_split(T, H, attn.shape[1], ws.part_rows)
             part = ws.part_view(s, T, H)
             K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            self.reduce_partials(part)
+            part = self.reduce_partials(part)
             # h += clamp(attn_out); x = clamp(norm_post(h))    (llama.py:111-115)
             K.residual_rmsnorm(resid, part, L["w_post"], eps, x, clamp=cl, clamp_delta=True,
                                clamp_norm=True)
@@ -105,7 +105,7 @@ class LlamaForCausalLM(MuModelBase):
             s = choose_split(T, H, self.i_pad, ws.part_rows)
             part = ws.part_view(s, T, H)
             K.gemm(ws.act, L["wd"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            self.reduce_partials(part)
+            part = self.reduce_partials(part)
             # h = clamp(h + clamp(mlp_out)); x = clamp(norm_in_next(h))   (llama.py:116-126)
             last = l + 1 == nl
             K.residual_rmsnorm(resid, part, None if last else self.layers[l + 1]["w_in"], eps,

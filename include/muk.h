@@ -302,18 +302,27 @@ int muk_ipc_close_handle(void* base);
  * muk_allreduce_f32. */
 size_t muk_allreduce_flag_bytes(void);
 
-/* In-place sum of n f32 elements (n % 4 == 0) across `world` ranks (<= 8):
- * bufs[s] / flags[s] are rank s's buffer range and flag area as mapped in
- * this process (bufs[rank] / flags[rank] are this rank's own).  Rank r
- * reduces its 1/world of the range in rank order 0..world-1 and writes the
- * sum into every rank's buffer, between two cross-GPU barriers on the flags,
- * so every rank ends with bit-identical sums.  All ranks must make the same
- * sequence of calls (same n, same order).  Waits are bounded (5 s; then the
- * device error word reads 6 and the result is undefined).  Replaces the NCCL
- * all-reduce after the row-parallel projections; graph-capturable (the
- * barrier epoch lives in the flag area). */
-int muk_allreduce_f32(float* const* bufs, uint32_t* const* flags, int rank, int world, int64_t n,
-                      void* stream);
+/* f32 elements of the scratch area each rank needs for an all-reduce of n
+ * elements over `world` ranks (world equal shares, rounded up to float4s). */
+int64_t muk_allreduce_scratch_elems(int64_t n, int world);
+
+/* In-place sum of n f32 elements (n % 4 == 0) across `world` ranks (<= 8).
+ * bufs[s], scratch[s] and flags[s] are rank s's data range, scratch area and
+ * flag area as mapped in this process (index `rank` = this rank's own).
+ * With slices > 1 each rank's data holds that many split-K partial slices
+ * (slice_stride elements apart); they are summed locally first, and the
+ * result lands in slice 0 only (NVLink carries one slice).
+ * Two kernels: every rank stores share s of its data into rank s's scratch
+ * (NVLink stores only); after a cross-GPU barrier, rank r sums share r in
+ * rank order 0..world-1 from local memory and stores the sum into every
+ * rank's data; a second barrier ends the call.  Every rank ends with
+ * bit-identical sums.  All ranks must make the same sequence of calls (same
+ * n, same order).  Waits are bounded (5 s; then the device error word reads
+ * 6 and the result is undefined).  Replaces the NCCL all-reduce after the
+ * row-parallel projections; graph-capturable (the barrier epoch lives in the
+ * flag area).  Launches two kernels. */
+int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags, int rank,
+                      int world, int64_t n, int slices, int64_t slice_stride, void* stream);
 
 #ifdef __cplusplus
 }

@@ -15,7 +15,7 @@ HEADER = ROOT / "include" / "muk.h"
 
 def _declared():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(muk_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t|const char\*)\s+(muk_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_entry_points():

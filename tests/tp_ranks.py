@@ -46,6 +46,17 @@ def check_peer_allreduce(rank, world, failures):
         dist.all_gather(allx, x)
         if not all(torch.equal(a, allx[0]) for a in allx):
             failures.append(("peer allreduce not identical across ranks", n))
+    # split-K slices are folded before the exchange; the sum lands in slice 0
+    n, S = 1000, 3
+    x = comm.view(S * n).view(S, n)
+    x.copy_(torch.randn(S, n, device="cuda", generator=g))
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x.clone())
+    ref = torch.stack([p.sum(0) for p in parts]).sum(0)
+    out = comm.all_reduce_(x, slices=S)
+    torch.cuda.synchronize()
+    if out.data_ptr() != x.data_ptr() or not torch.allclose(out, ref, rtol=1e-5, atol=1e-5):
+        failures.append(("peer allreduce slices", float((out - ref).abs().max())))
     # graph capture and replay
     n = 4096
     x = comm.view(n)
