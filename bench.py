@@ -507,7 +507,11 @@ def run_ours(args, rank, world, local_rank):
     engine, worker, ec = build(rank, tp, wl, ep=args.parallel == "ep")
     conc, out_tokens = wl["concurrency"], wl["out"]
     # tensor-parallel ranks serve the same requests; replicas serve their own
-    seed_rank = 0 if tp > 1 else rank
+    # Every engine serves the same seeded request stream (replicas each serve
+    # their own copy of it): the step-to-step mix of prompt lengths is then
+    # the same on every GPU, so the max-over-ranks time measures the scaling
+    # of the hardware, not the spread of eight independent random draws.
+    seed_rank = 0
     arrivals = Arrivals(1000 + seed_rank, wl)
     rng = np.random.default_rng(7 + seed_rank)
     for _ in range(conc):
@@ -638,6 +642,8 @@ def run_ours(args, rank, world, local_rank):
             "global_batch": conc * (world // tp),
             "seq_len": f"prompt {wl['prompt']} + {out_tokens} generated",
             "parallelism": par if world > 1 else "single",
+            "request_stream": ("one seeded stream; every replica serves its own copy"
+                               if world > 1 and tp == 1 else "one seeded stream"),
             "l2": "no flush needed: each step streams the weights (GBs) and the KV of every "
                   "running request (GBs) through HBM (L2 126 MB)",
             "tokens_timed": int(n_all),
