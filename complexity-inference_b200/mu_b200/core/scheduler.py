@@ -17,7 +17,7 @@ import uuid
 from collections import deque
 from dataclasses import dataclass, field
 from enum import Enum
-from typing import Callable, Deque, Dict, List, Optional, Set
+from typing import Callable, Deque, Dict, List, Optional, Set, Tuple
 
 from .config import SamplingParams, SchedulerConfig
 from .mu import MuDynamics, soft_clamp
@@ -49,6 +49,9 @@ class Request:
     num_generated_tokens: int = 0
     max_tokens: int = 512
     num_preemptions: int = 0
+    # chunked prefill: tokens of (prompt + generated) already in the KV cache
+    # while the request's prefill is split over several steps
+    num_prefilled: int = 0
     on_token: Optional[Callable[[int, str], None]] = None
     on_finish: Optional[Callable[["Request"], None]] = None
 
@@ -82,6 +85,8 @@ class SchedulerOutput:
     preempted_requests: List[Request] = field(default_factory=list)
     num_prefill_tokens: int = 0
     num_decode_tokens: int = 0
+    # (start, length) of the tokens each prefill request runs this step
+    prefill_chunks: List[Tuple[int, int]] = field(default_factory=list)
 
     @property
     def total_tokens(self) -> int:
@@ -126,27 +131,54 @@ class MuScheduler:
                 out.decode_requests.append(req)
                 out.num_decode_tokens += 1
                 decode_budget -= 1
-        slots = self.config.max_batch_size - len(out.decode_requests)
         prefill_budget = min(self.config.max_prefill_tokens, decode_budget)
+        chunked = self.config.enable_chunked_prefill
+        # Chunked prefill, for real: the reference records min(prompt, budget)
+        # as the tokens needed but then runs every prompt whole.  Here a prompt
+        # longer than the remaining budget runs its first `budget` tokens now
+        # and the rest in the following steps (KV appended chunk by chunk;
+        # only the last chunk's logits are sampled).  Requests part-way
+        # through their prefill continue first, in admission order.
+        continuing = [r for r in self.running.values()
+                      if r.status == RequestStatus.PREFILL and r.num_prefilled > 0
+                      and not (hold and r.request_id in hold)]
+        for req in continuing:
+            need = req.num_prompt_tokens + req.num_generated_tokens - req.num_prefilled
+            take = min(need, prefill_budget)
+            if take <= 0:
+                continue
+            out.prefill_requests.append(req)
+            out.prefill_chunks.append((req.num_prefilled, take))
+            out.num_prefill_tokens += take
+            prefill_budget -= take
+        slots = self.config.max_batch_size - len(out.decode_requests) - len(continuing)
         # Admission differs from the reference on purpose: there a popped request
-        # that misses the budget is neither scheduled nor re-queued (it is lost),
-        # and with chunked prefill every waiting request is admitted at once
-        # although prompts are always run whole.  Here a request is admitted when
-        # its whole prompt (plus tokens generated before a preemption) fits the
-        # remaining budget — the first prefill of a step always does — and the
-        # rest go back to the front of the queue in their original order.
+        # that misses the budget is neither scheduled nor re-queued (it is lost).
+        # Here a request is admitted when its prompt (plus tokens generated
+        # before a preemption) fits the remaining budget, or, with chunked
+        # prefill, when any budget is left (it starts with a partial chunk);
+        # without chunking the first prefill of a step is always admitted
+        # whole.  The rest go back to the front of the queue in their order.
         deferred: List[Request] = []
         for req in self._get_next_requests(slots):
             need = req.num_prompt_tokens + req.num_generated_tokens
-            if deferred or (out.prefill_requests and need > prefill_budget):
+            if chunked:
+                take = min(need, prefill_budget)
+                admit = not deferred and take > 0
+            else:
+                take = need
+                admit = not deferred and not (out.prefill_requests and need > prefill_budget)
+            if not admit:
                 deferred.append(req)
                 continue
             req.status = RequestStatus.PREFILL
             req.start_time = req.start_time or time.time()
+            req.num_prefilled = 0
             self.running[req.request_id] = req
             out.prefill_requests.append(req)
-            out.num_prefill_tokens += need
-            prefill_budget -= need
+            out.prefill_chunks.append((0, take))
+            out.num_prefill_tokens += take
+            prefill_budget -= take
         self._requeue_front(deferred)
         if self._should_preempt(out):
             out.preempted_requests = self._preempt_requests(out)

@@ -166,15 +166,18 @@ class StepEngine:
         for req in out.preempted_requests:  # recompute preemption: drop KV, re-prefill later
             self._release(req.request_id)
         prefills: List[Request] = []
-        for req in out.prefill_requests:
+        chunks: List[tuple] = []
+        for req, chunk in zip(out.prefill_requests, out.prefill_chunks):
             if req.request_id not in self.worker.active_requests:
                 if not self.worker.allocate_request(req.request_id):
                     req.status = RequestStatus.PENDING
+                    req.num_prefilled = 0
                     self.scheduler.running.pop(req.request_id, None)
                     self.scheduler.waiting.appendleft(req)
                     continue
             self.sampler.add(req.request_id)
             prefills.append(req)
+            chunks.append(chunk)
         decodes = out.decode_requests
         if not decodes and not prefills:
             return None
@@ -187,8 +190,12 @@ class StepEngine:
             src = prev_rows.get(rid, -1)
             toks = _ZERO if src >= 0 else np.asarray(r.output_token_ids[-1:], dtype=np.int32)
             work.append((rid, toks, src, row_of[rid]))
-        work += [(r.request_id, np.asarray(r.prompt_token_ids + r.output_token_ids, dtype=np.int32),
-                  -1, row_of[r.request_id]) for r in prefills]
+        final = {}
+        for r, (start, length) in zip(prefills, chunks):
+            toks = r.prompt_token_ids + r.output_token_ids
+            final[r.request_id] = start + length >= len(toks)
+            work.append((r.request_id, np.asarray(toks[start:start + length], dtype=np.int32), -1,
+                         row_of[r.request_id]))
         seqs, errors = self.worker.prepare(work, len(decodes))
         for rid, err in errors:
             req = self.requests[rid]
@@ -208,20 +215,31 @@ class StepEngine:
                                      batch.token_rows, batch.input_ids, T)
         self.num_steps += 1
         idx = []
-        for req in reqs:  # the pending token takes its place now; its value comes later
+        for s, req in zip(seqs, reqs):
+            if not final.get(req.request_id, True):
+                # a prefill chunk that is not the prompt's last: no token (its
+                # sample is dropped), the next chunk follows in a later step
+                req.num_prefilled += len(s.token_ids)
+                idx.append(-1)
+                continue
+            # the pending token takes its place now; its value comes later
+            req.num_prefilled = 0
             idx.append(len(req.output_token_ids))
             req.output_token_ids.append(-1)
             req.num_generated_tokens += 1
             req.status = RequestStatus.DECODE
             if req.num_generated_tokens >= req.sampling_params.max_tokens:
                 self._closing.add(req.request_id)
-        return _Launched(reqs, idx, {rid: i for i, rid in enumerate(ids)}, handle)
+        rows = {rid: i for i, (rid, j) in enumerate(zip(ids, idx)) if j >= 0}
+        return _Launched(reqs, idx, rows, handle)
 
     def _complete(self, launched: _Launched) -> List[StepOutput]:
         toks = launched.handle.wait()
         results: List[StepOutput] = []
         eos = self.eos_token_id
         for req, i, tok in zip(launched.reqs, launched.idx, toks):
+            if i < 0:
+                continue  # a prefill chunk before the prompt's last
             if req.is_finished or self.requests.get(req.request_id) is not req:
                 continue  # stopped on the step before, or aborted
             req.output_token_ids[i] = tok

@@ -70,6 +70,7 @@ class FakeWorker:
         self.cache = PagedKVCache(1, 1, 2, 4, blocks, torch.float32, "cpu")
         self.active_requests = {}
         self.steps = []
+        self.tokens = []
 
     def run_step(self, seqs, nd, sampled=None):
         out = []
@@ -81,6 +82,7 @@ class FakeWorker:
                 last = int(s.token_ids[-1])
             out.append(next_token(last, s.start_pos + len(s.token_ids) - 1))
         self.steps.append((len(seqs), nd))
+        self.tokens.append(sum(len(s.token_ids) for s in seqs))
         return out, type("B", (), {"token_rows": None, "input_ids": None})()
 
 
@@ -95,11 +97,13 @@ def expected(prompt, max_tokens, stop):
     return gen
 
 
-def run(overlap, prompts, limits, stop, max_batch, abort=None, monkeypatch=None):
+def run(overlap, prompts, limits, stop, max_batch, abort=None, monkeypatch=None, budget=64,
+        chunked=True):
     monkeypatch.setattr(E, "BatchSampler", FakeSampler)
     ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=max_batch),
                       scheduler=SchedulerConfig(max_batch_size=max_batch, max_num_batched_tokens=64,
-                                                max_prefill_tokens=64))
+                                                max_prefill_tokens=budget,
+                                                enable_chunked_prefill=chunked))
     w = FakeWorker()
     eng = E.StepEngine(w, ec, overlap=overlap)
     for i, (p, m) in enumerate(zip(prompts, limits)):
@@ -153,4 +157,26 @@ def test_abort_while_in_flight(monkeypatch):
                            monkeypatch=monkeypatch)
     assert "r0" not in eng.requests
     assert eng.requests["r1"].output_token_ids == expected(prompts[1], 6, [])
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_chunked_prefill(overlap, monkeypatch):
+    """Prompts longer than the prefill budget run in chunks over several steps
+    (KV appended chunk by chunk, no token until the last chunk) and generate
+    exactly what a whole-prompt prefill generates; no step exceeds the budget
+    plus its decodes."""
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in (23, 5, 17, 9, 30)]
+    limits = [6, 4, 7, 3, 5]
+    budget = 6
+    eng, w, reported = run(overlap, prompts, limits, [], max_batch=3, monkeypatch=monkeypatch,
+                           budget=budget)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        want = expected(p, m, [])
+        assert eng.requests[f"r{i}"].output_token_ids == want
+        assert reported[f"r{i}"] == want
+    for (b, nd), t in zip(w.steps, w.tokens):
+        assert t - nd <= budget
+    assert max(w.tokens) <= budget + 3
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks

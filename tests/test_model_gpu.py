@@ -170,3 +170,32 @@ def test_engine_stops_on_eos_with_overlap(cuda, overlap):
             assert got.index(eos) == len(got) - 1 and eng.requests[f"r{r}"].finish_reason == "stop"
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
     assert not eng.sampler.row_of
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+def test_engine_chunked_prefill(cuda, name):
+    """Prompts run in chunks of at most 24 tokens (KV of earlier chunks read
+    back from the paged cache by the prefill kernel): greedy tokens must match
+    the reference's as in the whole-prompt test."""
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    toks = np.load(__import__("golden_models").G / f"{name}.npz")["tokens"]
+    R, n = toks.shape
+    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=R)
+    ec.scheduler.max_prefill_tokens = 24
+    ec.scheduler.enable_chunked_prefill = True
+    assert max(len(p) for p in prompts) > 24
+    eng = StepEngine(w, ec)
+    for r in range(R):
+        eng.add_request(prompts[r], SamplingParams(temperature=0.0, top_k=0, top_p=1.0,
+                                                   repetition_penalty=1.0, max_tokens=n), f"r{r}")
+    eng.run_to_completion()
+    for r in range(R):
+        got = eng.requests[f"r{r}"].output_token_ids
+        assert len(got) == n
+        for i, t in enumerate(got):
+            if t != int(toks[r, i]):
+                assert d["top2_gap"][r, i] <= GAP_TOL, (name, r, i, t, int(toks[r, i]))
+                break
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
