@@ -29,7 +29,7 @@ and intermediate counts are the local ones.
 from __future__ import annotations
 
 import dataclasses
-from typing import Dict, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -65,6 +65,57 @@ def expert_range(cfg: ModelConfig, rank: int, tp: int) -> Tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+def shard_index(name: str, cfg: ModelConfig, arch: str, rank: int, tp: int,
+                expert_parallel: bool = False) -> Optional[Tuple[int, List[tuple]]]:
+    """How rank ``rank`` of ``tp`` slices parameter ``name``: None for the
+    whole tensor, else (concat dim, [index tuples]) — the rank's shard is the
+    concatenation of ``t[idx]`` over the tuples.  One rule set serves both a
+    tensor in memory and a lazy safetensors slice read from disk."""
+    if tp == 1:
+        return None
+    D = cfg.head_dim
+    hq = cfg.num_attention_heads // tp
+    hkv = cfg.num_key_value_heads // tp
+    q0, k0 = rank * hq * D, rank * hkv * D
+    routed = is_routed(arch, cfg)
+    ep = expert_parallel and routed
+    if routed:
+        ie = expert_intermediate(cfg)
+        il = ie // tp
+    else:
+        il = cfg.intermediate_size // tp
+    i0 = rank * il
+    leaf = name.split(".", 2)[-1] if name.startswith("layers.") else name
+    all_ = slice(None)
+    if leaf in ("self_attn.q_proj.weight", "self_attn.mu_to_q.weight"):
+        return 0, [(slice(q0, q0 + hq * D),)]
+    if leaf in ("self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                "self_attn.mu_to_k.weight", "self_attn.mu_to_v.weight"):
+        return 0, [(slice(k0, k0 + hkv * D),)]
+    if leaf == "self_attn.o_proj.weight":
+        return 1, [(all_, slice(q0, q0 + hq * D))]
+    if leaf in ("mlp.gate_proj.weight", "mlp.up_proj.weight"):
+        return 0, [(slice(i0, i0 + il),)]
+    if leaf == "mlp.down_proj.weight" and not routed:
+        return 1, [(all_, slice(i0, i0 + il))]
+    if leaf in ("mlp.gate_up_proj", "mlp.down_proj") and ep:   # whole experts [e0, e1)
+        e0, e1 = expert_range(cfg, rank, tp)
+        return 0, [(slice(e0, e1),)]
+    if leaf == "mlp.gate_up_proj":   # [E, H, 2I]: gate cols [0, I), up cols [I, 2I)
+        return 2, [(all_, all_, slice(i0, i0 + il)), (all_, all_, slice(ie + i0, ie + i0 + il))]
+    if leaf == "mlp.down_proj" and routed:   # [E, I, H]
+        return 1, [(all_, slice(i0, i0 + il), all_)]
+    return None
+
+
+def _take(t, spec) -> torch.Tensor:
+    if spec is None:
+        return t[:] if not isinstance(t, torch.Tensor) else t
+    dim, idxs = spec
+    parts = [t[idx] for idx in idxs]
+    return parts[0] if len(parts) == 1 else torch.cat(parts, dim)
+
+
 def shard_state_dict(sd: Dict[str, torch.Tensor], cfg: ModelConfig, arch: str, rank: int,
                      tp: int, expert_parallel: bool = False
                      ) -> Tuple[Dict[str, torch.Tensor], ModelConfig]:
@@ -73,38 +124,35 @@ def shard_state_dict(sd: Dict[str, torch.Tensor], cfg: ModelConfig, arch: str, r
         return dict(sd), cfg
     ep = expert_parallel and is_routed(arch, cfg)
     lcfg = local_config(cfg, arch, tp, ep)
-    e0, e1 = expert_range(cfg, rank, tp) if ep else (0, 0)
-    D = cfg.head_dim
-    hq = cfg.num_attention_heads // tp
-    hkv = cfg.num_key_value_heads // tp
-    q0, k0 = rank * hq * D, rank * hkv * D
-    out: Dict[str, torch.Tensor] = {}
-    routed = is_routed(arch, cfg)
-    if routed:
-        ie = expert_intermediate(cfg)
-        il = ie // tp
-    else:
-        il = cfg.intermediate_size // tp
-    i0 = rank * il
-    for name, t in sd.items():
-        leaf = name.split(".", 2)[-1] if name.startswith("layers.") else name
-        if leaf in ("self_attn.q_proj.weight", "self_attn.mu_to_q.weight"):
-            out[name] = t[q0:q0 + hq * D]
-        elif leaf in ("self_attn.k_proj.weight", "self_attn.v_proj.weight",
-                      "self_attn.mu_to_k.weight", "self_attn.mu_to_v.weight"):
-            out[name] = t[k0:k0 + hkv * D]
-        elif leaf == "self_attn.o_proj.weight":
-            out[name] = t[:, q0:q0 + hq * D]
-        elif leaf in ("mlp.gate_proj.weight", "mlp.up_proj.weight"):
-            out[name] = t[i0:i0 + il]
-        elif leaf == "mlp.down_proj.weight" and not routed:
-            out[name] = t[:, i0:i0 + il]
-        elif leaf in ("mlp.gate_up_proj", "mlp.down_proj") and ep:   # whole experts [e0, e1)
-            out[name] = t[e0:e1]
-        elif leaf == "mlp.gate_up_proj":   # [E, H, 2I]: gate cols [0, I), up cols [I, 2I)
-            out[name] = torch.cat([t[:, :, i0:i0 + il], t[:, :, ie + i0:ie + i0 + il]], 2)
-        elif leaf == "mlp.down_proj" and routed:   # [E, I, H]
-            out[name] = t[:, i0:i0 + il, :]
-        else:
-            out[name] = t
+    out = {name: _take(t, shard_index(name, cfg, arch, rank, tp, ep)) for name, t in sd.items()}
     return {k: v.contiguous() for k, v in out.items()}, lcfg
+
+
+def load_sharded_state_dict(path, cfg: ModelConfig, arch: str, rank: int, tp: int,
+                            expert_parallel: bool = False
+                            ) -> Tuple[Dict[str, torch.Tensor], ModelConfig]:
+    """Read only this rank's shard of every parameter from a model dir's
+    safetensors files (lazy slices; the full tensors are never materialised),
+    with the reference's prefix stripping (mu_inference/models/loader.py:188-227).
+    Directories without safetensors fall back to loading and slicing in memory."""
+    from pathlib import Path
+
+    from .weights import load_state_dict, strip_prefix
+
+    files = sorted(Path(path).glob("*.safetensors"))
+    if not files:
+        return shard_state_dict(load_state_dict(path), cfg, arch, rank, tp, expert_parallel)
+    from safetensors import safe_open
+
+    ep = expert_parallel and is_routed(arch, cfg)
+    out: Dict[str, torch.Tensor] = {}
+    for f in files:
+        with safe_open(str(f), framework="pt", device="cpu") as h:
+            for key in h.keys():
+                name = strip_prefix(key)
+                spec = shard_index(name, cfg, arch, rank, tp, ep)
+                out[name] = (h.get_tensor(key) if spec is None
+                             else _take(h.get_slice(key), spec)).contiguous()
+    if not out:
+        raise FileNotFoundError(f"no weight files in {path}")
+    return out, (local_config(cfg, arch, tp, ep) if tp > 1 else cfg)

@@ -154,14 +154,16 @@ def load_state_dict(path) -> Dict[str, torch.Tensor]:
             sd.update(torch.load(str(f), map_location="cpu", weights_only=True))
     if not sd:
         raise FileNotFoundError(f"no weight files in {path}")
-    out = {}
-    for k, v in sd.items():
-        for pre in ("model.", "transformer.", "decoder."):
-            if k.startswith(pre):
-                k = k[len(pre):]
-                break
-        out[k] = v
-    return out
+    return {strip_prefix(k): v for k, v in sd.items()}
+
+
+def strip_prefix(name: str) -> str:
+    """Parameter name without the "model." / "transformer." / "decoder."
+    prefix (mu_inference/models/loader.py:188-227)."""
+    for pre in ("model.", "transformer.", "decoder."):
+        if name.startswith(pre):
+            return name[len(pre):]
+    return name
 
 
 def state_dict_digest(sd: Dict[str, torch.Tensor]) -> float:

@@ -105,27 +105,44 @@ class MuWorker:
         if mcfg is None or mcfg.hidden_size != cfg_dict.get("hidden_size", mcfg.hidden_size):
             mcfg = config_from_dict(cfg_dict)
             self.config.model = mcfg
-        self.load_state_dict(arch, mcfg, load_state_dict(model_path))
+        if int(self.config.tensor_parallel_size or 1) > 1:
+            # read only this rank's slices of every tensor from disk
+            from ..models.sharding import load_sharded_state_dict
 
-    def load_state_dict(self, arch: str, model_config: ModelConfig, sd) -> None:
-        """Build the model from a full state dict (sharded here when tensor-parallel)."""
+            rank, tp, ep = self._tp_coords()
+            sd, _ = load_sharded_state_dict(model_path, mcfg, arch, rank, tp, ep)
+            self.load_state_dict(arch, mcfg, sd, sharded=True)
+        else:
+            self.load_state_dict(arch, mcfg, load_state_dict(model_path))
+
+    def _tp_coords(self):
+        import torch.distributed as dist
+
+        tp = int(self.config.tensor_parallel_size or 1)
+        if not dist.is_initialized():
+            raise RuntimeError("tensor_parallel_size > 1 needs torch.distributed initialised")
+        if dist.get_world_size(self.tp_group) != tp:
+            raise RuntimeError(f"tensor_parallel_size {tp} != group size "
+                               f"{dist.get_world_size(self.tp_group)}")
+        return (dist.get_rank(self.tp_group), tp,
+                bool(getattr(self.config, "expert_parallel", False)))
+
+    def load_state_dict(self, arch: str, model_config: ModelConfig, sd, sharded: bool = False
+                        ) -> None:
+        """Build the model from a full state dict (sharded here when
+        tensor-parallel) or, with ``sharded``, from this rank's shard."""
         self.config.model = model_config
         tp = int(self.config.tensor_parallel_size or 1)
         local = model_config
         if tp > 1:
-            import torch.distributed as dist
+            from ..models.sharding import local_config, shard_state_dict
+            from ..models.weights import is_routed
 
-            from ..models.sharding import shard_state_dict
-
-            if not dist.is_initialized():
-                raise RuntimeError("tensor_parallel_size > 1 needs torch.distributed initialised")
-            group = self.tp_group
-            if dist.get_world_size(group) != tp:
-                raise RuntimeError(f"tensor_parallel_size {tp} != group size "
-                                   f"{dist.get_world_size(group)}")
-            rank = dist.get_rank(group)
-            ep = bool(getattr(self.config, "expert_parallel", False))
-            sd, local = shard_state_dict(sd, model_config, arch, rank, tp, ep)
+            rank, tp, ep = self._tp_coords()
+            if sharded:
+                local = local_config(model_config, arch, tp, ep and is_routed(arch, model_config))
+            else:
+                sd, local = shard_state_dict(sd, model_config, arch, rank, tp, ep)
         self.model = build_model(arch, local, sd, self.config.mu, str(self.device))
         if tp > 1:
             import torch.distributed as dist

@@ -177,3 +177,21 @@ def test_shards_recombine(name):
             assert torch.equal(torch.cat([s[k] for s in ep]), sd[k])
         assert ep[0]["layers.0.self_attn.q_proj.weight"].shape[0] == \
             sd["layers.0.self_attn.q_proj.weight"].shape[0] // tp
+
+
+@pytest.mark.parametrize("name,ep", [("llama_tiny", False), ("deep_tiny", False), ("deep_tiny", True)])
+def test_sharded_safetensors_load(tmp_path, name, ep):
+    """Reading a rank's slices straight from a model dir's safetensors (with
+    the reference's "model." prefix) gives exactly the in-memory shard."""
+    from mu_b200.models.sharding import load_sharded_state_dict
+    from safetensors.torch import save_file
+
+    shape, cfg, sd, d, prompts = load_tiny(name)
+    save_file({"model." + k: v.contiguous() for k, v in sd.items()},
+              str(tmp_path / "model.safetensors"))
+    for rank in range(2):
+        want, wcfg = shard_state_dict(sd, cfg, shape.arch, rank, 2, expert_parallel=ep)
+        got, gcfg = load_sharded_state_dict(tmp_path, cfg, shape.arch, rank, 2, expert_parallel=ep)
+        assert gcfg == wcfg and sorted(got) == sorted(want)
+        for k in want:
+            assert torch.equal(got[k], want[k]), k
