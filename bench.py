@@ -80,6 +80,10 @@ WORKLOADS = {
                blocks=48000),
 }
 C3 = WORKLOADS["c3"]
+# ncu capture summarised in profiles/gemm_step_shapes_llama3-8b.md
+GEMM_NCU_TRAFFIC = {"shape": "M857 N28672 K4096 (gate|up at the C3 mean step)",
+                    "dram_bytes": 245.386e6 + 35.695e6, "algorithmic_bytes": 290.9e6,
+                    "source": "profiles/gemm_step_shapes_llama3-8b.md"}
 WORKLOAD = C3["desc"]
 
 
@@ -591,7 +595,12 @@ def run_ours(args, rank, world, local_rank):
     # steps timed with CUDA events (steps replayed from graphs are not seen)
     probe = GemmProbe()
     K.gemm_probe = probe
+    # the per-kernel Python step issues the same GEMM launches as the native
+    # executor, one at a time, so each can be bracketed by events
+    native = getattr(worker.model, "native", False)
+    worker.model.native = False
     replay()
+    worker.model.native = native
     K.gemm_probe = None
     gp_flops, gp_t, gp_n = probe.result()
     att_bytes, att_t, att_b, att_tok = time_attention(worker)
@@ -659,8 +668,11 @@ def run_ours(args, rank, world, local_rank):
                                "workload, CUDA events per launch)",
                      "bound": "tensor", "achieved": gp_flops / gp_t / 1e12, "peak": tflops_sus,
                      "unit": "TFLOP/s", "frac": gp_flops / gp_t / 1e12 / tflops_sus,
-                     "traffic": None,
-                     "traffic_note": "dram bytes per launch: profiles/gemm_step_shapes_llama3-8b.md",
+                     # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum)
+                     # of the step's gate|up launch at the mean step size, beside
+                     # that launch's algorithmic bytes (A + B + C)
+                     "traffic": GEMM_NCU_TRAFFIC["dram_bytes"],
+                     "traffic_launch": GEMM_NCU_TRAFFIC,
                      "peak_source": f"{peak_kind} sustained bf16 (MEASURED_PEAKS.json "
                                     "bf16_tflops_sustained; kernel runs inside a long step)",
                      "launches": gp_n, "flops_per_launch": gp_flops / max(gp_n, 1),

@@ -1,0 +1,128 @@
+// Native step executor for the dense Llama-family model: the whole forward
+// step (embedding, every layer, final norm, LM head) issued from C++ in one
+// call, so a step costs one host call instead of ~10 per layer through the
+// Python wrappers.  It launches exactly the kernels, with exactly the
+// arguments, of the Python step in mu_b200/models/llama.py (the parity tests
+// compare the two bit for bit); the launches are stream-ordered and can be
+// captured in a CUDA graph.
+//
+// Restates the layer loop of mu_inference/models/llama.py:91-128 and
+// :184-245 (pre-norm, GQA attention with RoPE, SwiGLU MLP, mu_clamp at the
+// embedding, every norm output, the attention and MLP outputs and the layer
+// output) over the flat step batch.
+#include <math.h>
+#include <stdint.h>
+
+#include "abi_util.h"
+
+using namespace muk;
+
+namespace {
+
+constexpr int kEpiBf16 = MUK_EPI_BF16;
+constexpr int kEpiF32 = MUK_EPI_F32;
+constexpr int kEpiSwiglu = MUK_EPI_SWIGLU;
+
+// Split-K factor for an f32-output projection, bounded by the rows of the
+// partial buffer (same rule as mu_b200.models.base.choose_split).
+int choose_split(int M, int N, int K, int64_t max_rows) {
+  int64_t s = max_rows / (M > 0 ? M : 1);
+  if (s > 16) s = 16;
+  if (s < 1) s = 1;
+  return muk_gemm_plan_split(M, N, K, kEpiF32, (int)s);
+}
+
+#define MUK_TRY(expr)         \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != MUK_OK) return rc_; \
+  } while (0)
+
+}  // namespace
+
+extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, void* stream) {
+  MUK_REQUIRE(m && b && m->layers && m->num_layers > 0, "muk_llama_forward: null model or batch");
+  MUK_REQUIRE(b->num_tokens > 0 && b->num_seqs > 0 && b->num_decode >= 0 &&
+                  b->num_decode <= b->num_seqs,
+              "muk_llama_forward: bad batch (T=%d B=%d decode=%d)", b->num_tokens, b->num_seqs,
+              b->num_decode);
+  MUK_REQUIRE(m->tp_world >= 1 && m->tp_world <= 8, "muk_llama_forward: tp_world %d", m->tp_world);
+  const int T = b->num_tokens, B = b->num_seqs, nd = b->num_decode;
+  const int H = m->hidden, Hq = m->num_q_heads, Hkv = m->num_kv_heads, D = m->head_dim;
+  const int qkv_n = (Hq + 2 * Hkv) * D, attn_n = Hq * D;
+  const int cl = m->clamp;
+  const float mu = m->mu, cmin = m->clamp_min, cmax = m->clamp_max;
+  const float scale = 1.0f / sqrtf((float)D);
+  // bf16 buffers, addressed in 2-byte elements
+  auto* qkv = static_cast<uint16_t*>(m->qkv);
+  auto* attn = static_cast<uint16_t*>(m->attn);
+  auto* x = static_cast<uint16_t*>(m->x);
+  const int64_t layer_elems = (int64_t)m->num_blocks * Hkv * m->block_size * D;
+  auto* pool = static_cast<uint16_t*>(m->kv_pool);
+
+  MUK_TRY(muk_embed(b->input_ids, m->embed, H, m->resid, T, H, m->vocab, cl, mu, cmin, cmax,
+                    stream));
+  MUK_TRY(muk_residual_rmsnorm(m->resid, nullptr, 0, 0, 0, nullptr, m->layers[0].in_norm, m->eps,
+                               x, m->x_stride, T, H, 0, 0, cl, mu, cmin, cmax, stream));
+
+  // Sum a row-parallel projection over the tensor-parallel ranks; returns the
+  // number of slices the consumer reads.
+  auto reduce = [&](int slices) -> int {
+    if (m->tp_world == 1) return slices;
+    int rc = muk_allreduce_f32(m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world,
+                               (int64_t)T * H, slices, (int64_t)T * H, stream);
+    return rc == MUK_OK ? 1 : rc;
+  };
+
+  for (int l = 0; l < m->num_layers; ++l) {
+    const MukLlamaLayer& L = m->layers[l];
+    void* kc = pool + (int64_t)(2 * l) * layer_elems;
+    void* vc = pool + (int64_t)(2 * l + 1) * layer_elems;
+    MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, qkv_n, H, kEpiBf16, 1,
+                          nullptr, stream));
+    MUK_TRY(muk_rope_kv_append(qkv, qkv_n, b->positions, b->slot_mapping, m->rope_cos,
+                               m->rope_sin, m->rope_len, T, Hq, Hkv, D, nullptr, nullptr, 1e-6f,
+                               kc, vc, m->num_blocks, m->block_size, stream));
+    if (nd > 0) {
+      int bound = b->decode_len_bound;
+      const int bt_cap = b->block_table_stride * m->block_size;
+      if (bound > bt_cap) bound = bt_cap;
+      MUK_TRY(muk_paged_decode_attn(qkv, qkv_n, attn, attn_n, kc, vc, b->block_tables,
+                                    b->block_table_stride, b->seq_lens, nd, Hq, Hkv, D,
+                                    m->block_size, m->num_blocks, scale, bound, m->attn_ws,
+                                    m->attn_ws_bytes, stream));
+    }
+    if (B > nd) {
+      MUK_TRY(muk_paged_prefill_attn(qkv + (int64_t)nd * qkv_n, qkv_n, attn + (int64_t)nd * attn_n,
+                                     attn_n, kc, vc, b->block_tables + (int64_t)nd * b->block_table_stride,
+                                     b->block_table_stride, b->seq_lens + nd, b->prefill_cu,
+                                     B - nd, b->max_q_len, Hq, Hkv, D, m->block_size,
+                                     m->num_blocks, scale, stream));
+    }
+    // O projection (split-K f32 partials) -> reduce -> h += clamp(o); x = clamp(norm(h))
+    int s = choose_split(T, H, attn_n, m->part_rows);
+    MUK_TRY(muk_gemm_bf16(attn, attn_n, L.wo, attn_n, m->part, H, T, H, attn_n, kEpiF32, s,
+                          nullptr, stream));
+    int np = reduce(s);
+    if (np < 0) return np;
+    MUK_TRY(muk_residual_rmsnorm(m->resid, m->part, (int64_t)T * H, H, np, nullptr, L.post_norm,
+                                 m->eps, x, m->x_stride, T, H, cl, 0, cl, mu, cmin, cmax, stream));
+    // SwiGLU MLP -> reduce -> h = clamp(h + clamp(mlp)); x = clamp(next_norm(h))
+    MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wgu, H, m->act, m->inter_pad, T, 2 * m->inter_pad, H,
+                          kEpiSwiglu, 1, nullptr, stream));
+    s = choose_split(T, H, m->inter_pad, m->part_rows);
+    MUK_TRY(muk_gemm_bf16(m->act, m->inter_pad, L.wd, m->inter_pad, m->part, H, T, H,
+                          m->inter_pad, kEpiF32, s, nullptr, stream));
+    np = reduce(s);
+    if (np < 0) return np;
+    const bool last = l + 1 == m->num_layers;
+    MUK_TRY(muk_residual_rmsnorm(m->resid, m->part, (int64_t)T * H, H, np, nullptr,
+                                 last ? nullptr : m->layers[l + 1].in_norm, m->eps,
+                                 last ? nullptr : x, m->x_stride, T, H, cl, cl, cl, mu, cmin, cmax,
+                                 stream));
+  }
+  MUK_TRY(muk_rmsnorm_rows(m->resid, b->last_token_idx, B, m->final_norm, m->eps, m->xl, H, H, cl,
+                           mu, cmin, cmax, stream));
+  return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32, 1,
+                       nullptr, stream);
+}

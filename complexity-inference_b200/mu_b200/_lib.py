@@ -63,6 +63,7 @@ SIGNATURES = {
     "muk_allreduce_flag_bytes": (c_size_t, []),
     "muk_allreduce_scratch_elems": (c_int64, [c_int64, c_int]),
     "muk_allreduce_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int64, c_int, c_int64, _P]),
+    "muk_llama_forward": (c_int, [_P, _P, _P]),
     "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
@@ -77,6 +78,35 @@ SIGNATURES = {
     "muk_mark_seen": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P]),
     "muk_fill_decode_inputs": (c_int, [_P, _P, _P, c_int, _P]),
 }
+
+class MukLlamaLayer(ctypes.Structure):
+    _fields_ = [("in_norm", c_void_p), ("wqkv", c_void_p), ("wo", c_void_p),
+                ("post_norm", c_void_p), ("wgu", c_void_p), ("wd", c_void_p)]
+
+
+class MukLlamaModel(ctypes.Structure):
+    _fields_ = [("num_layers", c_int), ("hidden", c_int), ("num_q_heads", c_int),
+                ("num_kv_heads", c_int), ("head_dim", c_int), ("inter_pad", c_int),
+                ("vocab", c_int), ("eps", c_float), ("clamp", c_int), ("mu", c_float),
+                ("clamp_min", c_float), ("clamp_max", c_float),
+                ("layers", ctypes.POINTER(MukLlamaLayer)), ("embed", c_void_p),
+                ("final_norm", c_void_p), ("lm_head", c_void_p), ("rope_cos", c_void_p),
+                ("rope_sin", c_void_p), ("rope_len", c_int), ("kv_pool", c_void_p),
+                ("num_blocks", c_int), ("block_size", c_int), ("resid", c_void_p),
+                ("x", c_void_p), ("x_stride", c_int64), ("qkv", c_void_p), ("attn", c_void_p),
+                ("act", c_void_p), ("part", c_void_p), ("part_rows", c_int64), ("xl", c_void_p),
+                ("logits", c_void_p), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
+                ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
+                ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8)]
+
+
+class MukStepBatch(ctypes.Structure):
+    _fields_ = [("num_tokens", c_int), ("num_seqs", c_int), ("num_decode", c_int),
+                ("max_q_len", c_int), ("decode_len_bound", c_int), ("input_ids", c_void_p),
+                ("positions", c_void_p), ("slot_mapping", c_void_p), ("seq_lens", c_void_p),
+                ("prefill_cu", c_void_p), ("last_token_idx", c_void_p),
+                ("block_tables", c_void_p), ("block_table_stride", c_int)]
+
 
 _lib: ctypes.CDLL | None = None
 
@@ -125,6 +155,16 @@ def call(name: str, *args) -> None:
         raise MukError(name, rc, last_error())
     if name != "muk_device_error":
         launch_count += 2 if name in _TWO_KERNELS else 1
+
+
+def call_counted(name: str, launches: int, *args) -> None:
+    """Call an entry point that launches ``launches`` kernels (native executors)."""
+    global launch_count
+    fn = getattr(load(), name)
+    rc = fn(*args)
+    if rc != MUK_OK:
+        raise MukError(name, rc, last_error())
+    launch_count += launches
 
 
 def call_status(name: str, *args) -> None:

@@ -17,10 +17,13 @@ intermediate padded with zero rows/columns to a multiple of 64 (exact).
 
 from __future__ import annotations
 
+import ctypes
+import os
 from typing import Dict, List, Optional
 
 import torch
 
+from .. import _lib
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
 from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
@@ -39,6 +42,11 @@ class LlamaForCausalLM(MuModelBase):
         self.embed = None
         self.norm_w = None
         self.lm_w = None
+        # whole step issued by libmuk's native executor (muk_llama_forward);
+        # MU_NATIVE_STEP=0 keeps the per-kernel Python path
+        self.native = os.environ.get("MU_NATIVE_STEP", "1") != "0"
+        self._native_key = None
+        self._native_model = None
 
     def act_width(self) -> int:
         return self.i_pad
@@ -84,7 +92,71 @@ class LlamaForCausalLM(MuModelBase):
         return ts
 
     # ---- step ------------------------------------------------------------------
+    def _native_ok(self) -> bool:
+        if not self.native:
+            return False
+        if self.tp_group is None:
+            return True
+        return self.comm is not None and self.ws.shared_part  # peer all-reduce only
+
+    def _native(self, cache) -> "_lib.MukLlamaModel":
+        """The executor's model struct (rebuilt when a buffer moves)."""
+        ws, cfg = self.ws, self.config
+        key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm))
+        if key == self._native_key:
+            return self._native_model
+        layers = (_lib.MukLlamaLayer * len(self.layers))()
+        for i, L in enumerate(self.layers):
+            layers[i] = _lib.MukLlamaLayer(L["w_in"].data_ptr(), L["wqkv"].data_ptr(),
+                                           L["wo"].data_ptr(), L["w_post"].data_ptr(),
+                                           L["wgu"].data_ptr(), L["wd"].data_ptr())
+        cl = self.clamp
+        m = _lib.MukLlamaModel()
+        m.num_layers, m.hidden = len(self.layers), cfg.hidden_size
+        m.num_q_heads, m.num_kv_heads = cfg.num_attention_heads, cfg.num_key_value_heads
+        m.head_dim, m.inter_pad, m.vocab = cfg.head_dim, self.i_pad, cfg.vocab_size
+        m.eps = cfg.rms_norm_eps
+        m.clamp, m.mu, m.clamp_min, m.clamp_max = int(cl.enabled), cl.mu, cl.clamp_min, cl.clamp_max
+        m.layers = layers
+        m.embed, m.final_norm, m.lm_head = (self.embed.data_ptr(), self.norm_w.data_ptr(),
+                                            self.lm_w.data_ptr())
+        m.rope_cos, m.rope_sin, m.rope_len = (self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+                                              self.rope_cos.shape[0])
+        m.kv_pool, m.num_blocks, m.block_size = (cache.block_pool.data_ptr(), cache.max_num_blocks,
+                                                 cache.block_size)
+        m.resid, m.x, m.x_stride = ws.resid.data_ptr(), ws.x.data_ptr(), ws.x.stride(0)
+        m.qkv, m.attn, m.act = ws.qkv.data_ptr(), ws.attn.data_ptr(), ws.act.data_ptr()
+        m.part, m.part_rows = ws.part.data_ptr(), ws.part_rows
+        m.xl, m.logits = ws.xl.data_ptr(), ws.logits.data_ptr()
+        m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
+        m.tp_world, m.tp_rank = 1, 0
+        if self.comm is not None:
+            c = self.comm
+            m.tp_world, m.tp_rank = c.world, c.rank
+            for r in range(c.world):
+                m.ar_data[r], m.ar_scratch[r], m.ar_flags[r] = (c.ptrs[r], c.scratch_ptrs[r],
+                                                                 c.flag_ptrs[r])
+        m._keep = layers  # the layer array must outlive the struct
+        self._native_key, self._native_model = key, m
+        return m
+
+    def _forward_native(self, batch, cache) -> torch.Tensor:
+        m = self._native(cache)
+        T, B, nd = batch.num_tokens, batch.num_seqs, batch.num_decode
+        b = _lib.MukStepBatch(T, B, nd, batch.max_q_len, batch.decode_len_bound,
+                              batch.input_ids.data_ptr(), batch.positions.data_ptr(),
+                              batch.slot_mapping.data_ptr(), batch.seq_lens.data_ptr(),
+                              batch.prefill_cu.data_ptr(), batch.last_token_idx.data_ptr(),
+                              batch.block_tables.data_ptr(), batch.block_tables.stride(0))
+        tp = 4 if m.tp_world > 1 else 0  # two all-reduces of two kernels each
+        per_layer = 7 + (2 if nd > 0 else 0) + (1 if B > nd else 0) + tp
+        _lib.call_counted("muk_llama_forward", 4 + per_layer * m.num_layers, ctypes.byref(m),
+                          ctypes.byref(b), torch.cuda.current_stream().cuda_stream)
+        return self.ws.logits[:B]
+
     def forward_step(self, batch, cache) -> torch.Tensor:
+        if self._native_ok():
+            return self._forward_native(batch, cache)
         cfg, ws, cl = self.config, self.ws, self.clamp
         T, H, eps = batch.num_tokens, cfg.hidden_size, cfg.rms_norm_eps
         resid, x = ws.resid[:T], ws.x[:T, :H]

@@ -324,6 +324,78 @@ int64_t muk_allreduce_scratch_elems(int64_t n, int world);
 int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags, int rank,
                       int world, int64_t n, int slices, int64_t slice_stride, void* stream);
 
+/* ---- Native step executor (dense Llama family) ----------------------------- */
+
+/* One decoder layer's weights: f32 norm weights, bf16 K-major matrices
+ * ([Wq;Wk;Wv] fused, gate/up interleaved in 64-row groups and zero-padded to
+ * inter_pad, down with inter_pad columns). */
+typedef struct {
+  const float* in_norm;
+  const void* wqkv;
+  const void* wo;
+  const float* post_norm;
+  const void* wgu;
+  const void* wd;
+} MukLlamaLayer;
+
+/* Model, workspace and (optional) tensor-parallel peer buffers.  All device
+ * pointers; x is [rows][x_stride] bf16, qkv / attn / act are row-contiguous,
+ * part holds part_rows x hidden f32 partials (the peer-mapped data range of
+ * this rank under tensor parallelism), kv_pool is [layers][2][num_blocks]
+ * [num_kv_heads][block_size][head_dim] bf16. */
+typedef struct {
+  int num_layers, hidden, num_q_heads, num_kv_heads, head_dim, inter_pad, vocab;
+  float eps;
+  int clamp;
+  float mu, clamp_min, clamp_max;
+  const MukLlamaLayer* layers;
+  const void* embed;
+  const float* final_norm;
+  const void* lm_head;
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_len;
+  void* kv_pool;
+  int num_blocks, block_size;
+  float* resid;
+  void* x;
+  int64_t x_stride;
+  void* qkv;
+  void* attn;
+  void* act;
+  float* part;
+  int64_t part_rows;
+  void* xl;
+  float* logits;
+  void* attn_ws;
+  size_t attn_ws_bytes;
+  int tp_world, tp_rank;
+  float* ar_data[8];
+  float* ar_scratch[8];
+  uint32_t* ar_flags[8];
+} MukLlamaModel;
+
+/* The packed step (StepPacker layout; device pointers). */
+typedef struct {
+  int num_tokens, num_seqs, num_decode, max_q_len, decode_len_bound;
+  const int32_t* input_ids;
+  const int32_t* positions;
+  const int32_t* slot_mapping;
+  const int32_t* seq_lens;
+  const int32_t* prefill_cu;
+  const int32_t* last_token_idx;
+  const int32_t* block_tables;
+  int block_table_stride;
+} MukStepBatch;
+
+/* The whole forward step of a Llama-family model (embedding, all layers, the
+ * tensor-parallel all-reduces when tp_world > 1, final norm of each
+ * sequence's last token, LM head -> logits [num_seqs][vocab] f32) issued in
+ * one call: the same kernels with the same arguments as the Python step,
+ * without a host round trip per kernel.  Replaces LlamaForCausalLM.forward
+ * (mu_inference/models/llama.py:184-245) for a flat step. */
+int muk_llama_forward(const MukLlamaModel* model, const MukStepBatch* batch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -199,3 +199,31 @@ def test_engine_chunked_prefill(cuda, name):
                 assert d["top2_gap"][r, i] <= GAP_TOL, (name, r, i, t, int(toks[r, i]))
                 break
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_native_executor_matches_python_step(cuda, graphs):
+    """muk_llama_forward launches the same kernels with the same arguments as
+    the per-kernel Python step: logits must be bit-identical."""
+    from mu_b200.serving.worker import WorkerRequest
+
+    outs = []
+    for native in (False, True):
+        w, shape, d, prompts, _ = _worker("llama_tiny", cuda, graphs)
+        w.model.native = native
+        toks = d["tokens"]
+        R = toks.shape[0]
+        for r in range(R):
+            assert w.allocate_request(f"r{r}")
+        got = []
+        for i in range(4):
+            if i == 0:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([prompts[r]]), is_prefill=True)
+                        for r in range(R)]
+            else:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([[int(toks[r, i - 1])]]),
+                                      is_prefill=False) for r in range(R)]
+            got.append(torch.cat([o.logits for o in w.execute(reqs)]).float().cpu())
+        outs.append(got)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
