@@ -78,11 +78,18 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
     const MukLlamaLayer& L = m->layers[l];
     void* kc = pool + (int64_t)(2 * l) * layer_elems;
     void* vc = pool + (int64_t)(2 * l + 1) * layer_elems;
-    MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, qkv_n, H, kEpiBf16, 1,
-                          nullptr, stream));
-    MUK_TRY(muk_rope_kv_append(qkv, qkv_n, b->positions, b->slot_mapping, m->rope_cos,
-                               m->rope_sin, m->rope_len, T, Hq, Hkv, D, nullptr, nullptr, 1e-6f,
-                               kc, vc, m->num_blocks, m->block_size, stream));
+    if (m->fused_rope) {
+      MUK_TRY(muk_gemm_qkv_rope(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, H, b->positions,
+                                b->slot_mapping, m->rope_cos, m->rope_sin, m->rope_len, Hq, Hkv,
+                                D, nullptr, nullptr, 1e-6f, kc, vc, m->num_blocks, m->block_size,
+                                stream));
+    } else {
+      MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, qkv_n, H, kEpiBf16, 1,
+                            nullptr, stream));
+      MUK_TRY(muk_rope_kv_append(qkv, qkv_n, b->positions, b->slot_mapping, m->rope_cos,
+                                 m->rope_sin, m->rope_len, T, Hq, Hkv, D, nullptr, nullptr, 1e-6f,
+                                 kc, vc, m->num_blocks, m->block_size, stream));
+    }
     if (nd > 0) {
       int bound = b->decode_len_bound;
       const int bt_cap = b->block_table_stride * m->block_size;

@@ -72,6 +72,20 @@ struct GemmLayout {
   static constexpr int kBytes = kBarOff + (2 * STAGES + 4) * 8 + 16 + 1024;
 };
 
+// RoPE + paged-KV epilogue (MUK_EPI_ROPE_KV) of the fused q|k|v projection.
+struct RopeArgs {
+  const int32_t* positions;
+  const int32_t* slots;
+  const float* cos;
+  const float* sin;
+  const float* q_norm;
+  const float* k_norm;
+  void* k_cache;
+  void* v_cache;
+  float eps;
+  int max_pos, hq, hkv, head_dim, num_blocks, block_size;
+};
+
 struct TileArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kt_per_split, total;
@@ -82,6 +96,7 @@ struct TileArgs {
   // schedule: units [0, dp_tiles) data-parallel (tile x split order), then
   // tiles [dp_tiles, dp_tiles + sk_tiles) stream-K over `workers` workers
   int dp_tiles, sk_tiles, k_tiles, workers;
+  RopeArgs rope;
 };
 
 // Stream-K partial slots: (worker, which of its two split units, CTA rank)
@@ -274,6 +289,128 @@ __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_
   }
 }
 
+// One 32-column chunk of this lane's accumulator row (+ the other stream-K
+// shares when `fix`).  Warp-collective: every lane must call it.
+__device__ __forceinline__ void acc_chunk(uint32_t lane_addr, int c, uint32_t (&v)[32],
+                                          const SkFix* fix) {
+  tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+  tmem_ld_wait();
+  if (fix) sk_sum_chunk(*fix, c, v);
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&f)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    uint4 pk;
+    pk.x = pack_bf16x2(f[j], f[j + 1]);
+    pk.y = pack_bf16x2(f[j + 2], f[j + 3]);
+    pk.z = pack_bf16x2(f[j + 4], f[j + 5]);
+    pk.w = pack_bf16x2(f[j + 6], f[j + 7]);
+    *reinterpret_cast<uint4*>(dst + j) = pk;
+  }
+}
+
+// MUK_EPI_ROPE_KV: the tile's columns are whole heads of the q|k|v
+// projection.  Per row (token): q heads get the optional QK-norm and
+// rotate-half RoPE at the token's position and go to C (row stride ldc);
+// k heads the same and go to the paged K cache at slot_mapping[row]; v heads
+// go to the V cache unchanged.  The rotation runs on the f32 accumulator and
+// rounds once (mu_inference/models/layers.py:671-702 rounds q/k to the model
+// dtype first; the difference is within one bf16 rounding).  All branches
+// depend only on the tile, so the warp-collective TMEM loads stay uniform;
+// stores are per lane.
+template <int BN>
+__device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int row, int row_end,
+                                              int n0, uint32_t lane_addr, const SkFix* fix) {
+  const RopeArgs& r = a.rope;
+  const int D = r.head_dim, half = D >> 1, cph = D >> 5;
+  const bool valid = row < row_end;
+  int pos = valid ? r.positions[row] : 0;
+  const int slot = valid ? r.slots[row] : -1;
+  if (valid && (pos < 0 || pos >= r.max_pos)) {
+    set_device_error(kDevBadIndex);
+    pos = -1;
+  }
+  const int heads_total = r.hq + 2 * r.hkv;
+  for (int hh = 0; hh < BN / D; ++hh) {
+    const int head = n0 / D + hh;
+    if (head >= heads_total) break;
+    const int c0 = hh * cph;
+    const bool is_q = head < r.hq, is_k = !is_q && head < r.hq + r.hkv;
+    bool store = valid;
+    __nv_bfloat16* dst = nullptr;
+    if (is_q) {
+      dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)row * a.ldc + (int64_t)head * D;
+      store = store && pos >= 0;
+    } else {
+      const int blk = slot < 0 ? 0 : slot / r.block_size;
+      const int off = slot < 0 ? 0 : slot - blk * r.block_size;
+      if (slot < 0) store = false;
+      if (valid && blk >= r.num_blocks) {
+        set_device_error(kDevBadIndex);
+        store = false;
+      }
+      if (is_k && pos < 0) store = false;
+      const int kvh = is_k ? head - r.hq : head - r.hq - r.hkv;
+      dst = reinterpret_cast<__nv_bfloat16*>(is_k ? r.k_cache : r.v_cache) +
+            (((int64_t)(store ? blk : 0) * r.hkv + kvh) * r.block_size + off) * D;
+    }
+    if (!is_q && !is_k) {  // v: straight to the cache
+      for (int c = 0; c < cph; ++c) {
+        uint32_t v[32];
+        acc_chunk(lane_addr, c0 + c, v, fix);
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+        if (store) store_bf16x32(dst + c * 32, f);
+      }
+      continue;
+    }
+    const float* nw = is_q ? r.q_norm : r.k_norm;
+    float inv = 1.f;
+    if (nw != nullptr) {  // QK-norm over the head (nn.RMSNorm over head_dim)
+      float ss = 0.f;
+      for (int c = 0; c < cph; ++c) {
+        uint32_t v[32];
+        acc_chunk(lane_addr, c0 + c, v, fix);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ss += __uint_as_float(v[j]) * __uint_as_float(v[j]);
+      }
+      inv = rsqrtf(ss / (float)D + r.eps);
+    }
+    const int p = pos < 0 ? 0 : pos;
+    for (int c = 0; c < cph / 2; ++c) {  // chunk c of the first half with its partner
+      uint32_t lo[32], hi[32];
+      acc_chunk(lane_addr, c0 + c, lo, fix);
+      acc_chunk(lane_addr, c0 + c + cph / 2, hi, fix);
+      const int i0 = c * 32;
+      const float4* cs = reinterpret_cast<const float4*>(r.cos + (int64_t)p * half + i0);
+      const float4* sn = reinterpret_cast<const float4*>(r.sin + (int64_t)p * half + i0);
+      float olo[32], ohi[32];
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 c4 = cs[j4], s4 = sn[j4];
+        const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * j4 + u;
+          float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
+          if (nw != nullptr) {
+            x = nw[i0 + j] * (x * inv);
+            y = nw[half + i0 + j] * (y * inv);
+          }
+          olo[j] = x * cv[u] - y * sv[u];
+          ohi[j] = y * cv[u] + x * sv[u];
+        }
+      }
+      if (store) {
+        store_bf16x32(dst + i0, olo);
+        store_bf16x32(dst + half + i0, ohi);
+      }
+    }
+  }
+}
+
 // Epilogue of one accumulator (this warp's 32 rows): TMEM -> registers ->
 // fused epilogue -> global.  With `fix`, each chunk is first replaced by the
 // sum of all stream-K shares of the tile.
@@ -281,7 +418,9 @@ template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int row, int row_end,
                                               int n0, int64_t split_off, uint32_t lane_addr,
                                               const SkFix* fix) {
-  if (EPI == MUK_EPI_SWIGLU) {
+  if (EPI == MUK_EPI_ROPE_KV) {
+    epilogue_rope<BN>(C, args, row, row_end, n0, lane_addr, fix);
+  } else if (EPI == MUK_EPI_SWIGLU) {
     const int nout = args.N >> 1;
 #pragma unroll 1
     for (int grp = 0; grp < BN / 128; ++grp) {
@@ -973,6 +1112,9 @@ static int dispatch(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, 
       return launch<BN, S, MUK_EPI_SWIGLU, GROUPED>(ma, mb, C, a, sms, s);
     case MUK_EPI_BIAS_SILU:
       return launch<BN, S, MUK_EPI_BIAS_SILU, GROUPED>(ma, mb, C, a, sms, s);
+    case MUK_EPI_ROPE_KV:
+      if (!GROUPED) return launch<BN, S, MUK_EPI_ROPE_KV, false>(ma, mb, C, a, sms, s);
+      break;
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1024,7 +1166,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
 
 static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                          int64_t ldc, int M, int N, int K, int epilogue, int split_k, bool sk,
-                         const float* bias, int sms, cudaStream_t stream) {
+                         const float* bias, const RopeArgs* rope, int sms, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
@@ -1044,6 +1186,7 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
   a.bias = bias;
   a.offsets = nullptr;
   a.num_experts = 0;
+  a.rope = rope ? *rope : RopeArgs{};
   set_schedule(a, sms / 2, 2, sk);
   switch (epilogue) {
     case MUK_EPI_BF16:
@@ -1054,6 +1197,8 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
       return launch_pair<MUK_EPI_SWIGLU>(ma, mb, C, a, sms, stream);
     case MUK_EPI_BIAS_SILU:
       return launch_pair<MUK_EPI_BIAS_SILU>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_ROPE_KV:
+      return launch_pair<MUK_EPI_ROPE_KV>(ma, mb, C, a, sms, stream);
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1089,7 +1234,8 @@ static GemmPlan plan_for_split(int M, int N, int K, int epilogue, int split_k, i
 
 static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
-                    const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream) {
+                    const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream,
+                    const RopeArgs* rope = nullptr) {
   int rc = get_encode();
   if (rc) return rc;
   const int sms = sm_count();
@@ -1098,8 +1244,8 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   if (!grouped) {
     const GemmPlan best = plan_for_split(M, N, K, epilogue, split_k, sms);
     if (best.kind == 1)
-      return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, sms,
-                           stream);
+      return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, rope,
+                           sms, stream);
     bn = best.bn;
     sk = best.sk;
   } else {
@@ -1124,6 +1270,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   a.bias = bias;
   a.offsets = offsets;
   a.num_experts = num_experts;
+  a.rope = rope ? *rope : RopeArgs{};
   set_schedule(a, sms, 1, sk);
   if (bn == 256)
     return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
@@ -1214,4 +1361,48 @@ extern "C" int muk_gemm_set_stream_k(int mode) {
   const int prev = streamk_mode();
   g_streamk = (mode >= 0 && mode <= 2) ? mode : 2;
   return prev;
+}
+
+extern "C" int muk_gemm_qkv_rope(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                 void* q_out, int64_t ldq, int M, int K, const int32_t* positions,
+                                 const int32_t* slot_mapping, const float* rope_cos,
+                                 const float* rope_sin, int max_pos, int num_q_heads,
+                                 int num_kv_heads, int head_dim, const float* q_norm_w,
+                                 const float* k_norm_w, float qk_eps, void* k_cache, void* v_cache,
+                                 int num_blocks, int block_size, void* stream) {
+  MUK_REQUIRE(A && B && q_out && positions && slot_mapping && rope_cos && rope_sin && k_cache &&
+                  v_cache,
+              "muk_gemm_qkv_rope: null pointer");
+  MUK_REQUIRE(head_dim == 64 || head_dim == 128, "muk_gemm_qkv_rope: head_dim %d (64 or 128)",
+              head_dim);
+  MUK_REQUIRE(num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "muk_gemm_qkv_rope: heads %d/%d", num_q_heads, num_kv_heads);
+  MUK_REQUIRE(M >= 0 && K > 0 && lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 &&
+                  MUK_ALIGNED16(A) && MUK_ALIGNED16(B),
+              "muk_gemm_qkv_rope: A/B shape or alignment");
+  MUK_REQUIRE(ldq >= (int64_t)num_q_heads * head_dim && ldq % 8 == 0 && MUK_ALIGNED16(q_out) &&
+                  MUK_ALIGNED16(k_cache) && MUK_ALIGNED16(v_cache) && MUK_ALIGNED16(rope_cos) &&
+                  MUK_ALIGNED16(rope_sin),
+              "muk_gemm_qkv_rope: q_out / cache / table alignment");
+  MUK_REQUIRE(max_pos > 0 && num_blocks > 0 && block_size > 0, "muk_gemm_qkv_rope: bad cache");
+  if (M == 0) return MUK_OK;
+  RopeArgs r;
+  r.positions = positions;
+  r.slots = slot_mapping;
+  r.cos = rope_cos;
+  r.sin = rope_sin;
+  r.q_norm = q_norm_w;
+  r.k_norm = k_norm_w;
+  r.k_cache = k_cache;
+  r.v_cache = v_cache;
+  r.eps = qk_eps;
+  r.max_pos = max_pos;
+  r.hq = num_q_heads;
+  r.hkv = num_kv_heads;
+  r.head_dim = head_dim;
+  r.num_blocks = num_blocks;
+  r.block_size = block_size;
+  const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  return run_gemm(false, A, lda, B, ldb, q_out, ldq, M, N, K, MUK_EPI_ROPE_KV, 1, nullptr,
+                  nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), &r);
 }

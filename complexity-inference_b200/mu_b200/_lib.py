@@ -24,6 +24,7 @@ MUK_EPI_BF16 = 0
 MUK_EPI_F32 = 1
 MUK_EPI_SWIGLU = 2
 MUK_EPI_BIAS_SILU = 3
+MUK_EPI_ROPE_KV = 4
 
 _P = c_void_p
 _I32P = c_void_p  # device pointers are passed as integers
@@ -55,6 +56,9 @@ SIGNATURES = {
     "muk_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, c_int, c_int,
                               c_int, _P, _P]),
     "muk_gemm_plan_split": (c_int, [c_int, c_int, c_int, c_int, c_int]),
+    "muk_gemm_qkv_rope": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, _P, _P, _P,
+                                  _P, c_int, c_int, c_int, c_int, _P, _P, c_float, _P, _P, c_int,
+                                  c_int, _P]),
     "muk_gemm_plan_info": (c_int, [c_int, c_int, c_int, c_int, c_int, _P]),
     "muk_gemm_set_stream_k": (c_int, [c_int]),
     "muk_ipc_get_handle": (c_int, [_P, _P, POINTER(c_uint64)]),
@@ -97,7 +101,7 @@ class MukLlamaModel(ctypes.Structure):
                 ("act", c_void_p), ("part", c_void_p), ("part_rows", c_int64), ("xl", c_void_p),
                 ("logits", c_void_p), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
                 ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
-                ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8)]
+                ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int)]
 
 
 class MukStepBatch(ctypes.Structure):

@@ -14,14 +14,14 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import MUK_EPI_BF16, MUK_EPI_BIAS_SILU, MUK_EPI_F32, MUK_EPI_SWIGLU, call
+from ._lib import MUK_EPI_BF16, MUK_EPI_BIAS_SILU, MUK_EPI_F32, MUK_EPI_ROPE_KV, MUK_EPI_SWIGLU, call
 
 __all__ = [
     "Clamp", "MUK_EPI_BF16", "MUK_EPI_F32", "MUK_EPI_SWIGLU", "MUK_EPI_BIAS_SILU",
     "embed", "residual_rmsnorm", "rmsnorm_rows", "rope_kv_append", "decode_attn_workspace_size",
     "decode_attn", "prefill_attn", "gemm", "grouped_gemm", "route_permute", "gather_rows",
     "inl_dynamics", "reduce_clamp", "sample", "mark_seen", "fill_decode_inputs", "gemm_plan_info",
-    "gemm_set_stream_k",
+    "gemm_set_stream_k", "gemm_qkv_rope",
 ]
 
 
@@ -284,3 +284,29 @@ def gemm_set_stream_k(mode: int) -> int:
     """GEMM stream-K planning mode (0 off, 1 on, 2 auto = only for launches
     that would leave most SMs idle); returns the previous mode."""
     return int(_lib.load().muk_gemm_set_stream_k(int(mode)))
+
+
+def gemm_qkv_rope(A: torch.Tensor, B: torch.Tensor, q_out: torch.Tensor, positions: torch.Tensor,
+                  slot_mapping: torch.Tensor, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+                  num_q_heads: int, num_kv_heads: int, head_dim: int, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, q_norm_w: torch.Tensor | None = None,
+                  k_norm_w: torch.Tensor | None = None, qk_eps: float = 1e-6,
+                  M: int | None = None):
+    """q|k|v projection with RoPE (+QK-norm) and the paged-KV append fused in
+    the GEMM epilogue: q heads -> q_out, k/v heads -> the caches."""
+    _check(A, torch.bfloat16, "A")
+    _check(B, torch.bfloat16, "B")
+    _check(k_cache, torch.bfloat16, "k_cache")
+    M = A.shape[0] if M is None else M
+    K = A.shape[1]
+    num_blocks, _, block_size, _ = k_cache.shape
+    args = ("muk_gemm_qkv_rope", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"),
+            _p(q_out), _row_stride(q_out, "q_out"), M, K, _p(positions), _p(slot_mapping),
+            _p(rope_cos), _p(rope_sin), rope_cos.shape[0], num_q_heads, num_kv_heads, head_dim,
+            _p(q_norm_w), _p(k_norm_w), qk_eps, _p(k_cache), _p(v_cache), num_blocks, block_size,
+            _stream())
+    if gemm_probe is None:
+        call(*args)
+    else:
+        with gemm_probe(2.0 * M * (num_q_heads + 2 * num_kv_heads) * head_dim * K):
+            call(*args)

@@ -14,6 +14,7 @@ table built exactly as RotaryEmbeddingCompat builds it (layers.py:286-299).
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
@@ -122,6 +123,7 @@ class MuModelBase:
         self.rope_cos: Optional[torch.Tensor] = None
         self.rope_sin: Optional[torch.Tensor] = None
         self._rope_len = 0
+        self._fused_rope = os.environ.get("MU_FUSED_ROPE", "1") != "0"
         self.tp_group = None   # torch.distributed group when tensor-parallel
         self.comm = None       # mu_b200.comm.PeerAllReduce when tensor-parallel over NVLink
         self.ensure_rope(max(config.max_position_embeddings, 16))
@@ -187,13 +189,31 @@ class MuModelBase:
         dist.all_reduce(part, group=self.tp_group)
         return part
 
-    def attention(self, layer: int, batch, cache, q_norm_w=None, k_norm_w=None) -> torch.Tensor:
-        """RoPE + KV append, then paged decode / varlen prefill attention -> ws.attn."""
+    def fused_rope(self) -> bool:
+        """RoPE + KV append in the q|k|v GEMM's epilogue (MU_FUSED_ROPE=0: separate kernel)."""
+        return self._fused_rope and self.config.head_dim in (64, 128)
+
+    def qkv_proj(self, layer: int, x: torch.Tensor, w: torch.Tensor, batch, cache,
+                 q_norm_w=None, k_norm_w=None) -> None:
+        """q|k|v projection of the step's tokens, RoPE'd, with k/v appended to
+        the paged cache and q left in ws.qkv for the attention kernels."""
         cfg, ws = self.config, self.ws
         T, Hq, Hkv, D = batch.num_tokens, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         kc, vc = cache.k_cache(layer), cache.v_cache(layer)
+        if self.fused_rope():
+            K.gemm_qkv_rope(x, w, ws.qkv, batch.positions, batch.slot_mapping, self.rope_cos,
+                            self.rope_sin, Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, M=T)
+            return
+        K.gemm(x, w, ws.qkv, K.MUK_EPI_BF16, M=T)
         K.rope_kv_append(ws.qkv, batch.positions, batch.slot_mapping, self.rope_cos, self.rope_sin,
                          Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, num_tokens=T)
+
+    def attention(self, layer: int, batch, cache) -> torch.Tensor:
+        """Paged decode / varlen prefill attention over the cache -> ws.attn
+        (q in ws.qkv, k/v already appended by qkv_proj)."""
+        cfg, ws = self.config, self.ws
+        Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        kc, vc = cache.k_cache(layer), cache.v_cache(layer)
         nd, B = batch.num_decode, batch.num_seqs
         bt = batch.block_tables
         if nd > 0:

@@ -147,8 +147,9 @@ class DeepForCausalLM(MuModelBase):
         nl = len(self.layers)
         for l, L in enumerate(self.layers):
             kdim = H if l == 0 else 2 * H  # layer 0 has no mu_prev (deep.py:296)
-            K.gemm(xcat[:, :kdim], L["wcat"][:, :kdim], ws.qkv, K.MUK_EPI_BF16, M=T)
-            attn = self.attention(l, batch, cache, L.get("qn"), L.get("kn"))
+            self.qkv_proj(l, xcat[:, :kdim], L["wcat"][:, :kdim], batch, cache, L.get("qn"),
+                          L.get("kn"))
+            attn = self.attention(l, batch, cache)
             s = choose_split(T, H, attn.shape[1], ws.part_rows)
             part = ws.part_view(s, T, H)
             K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)

@@ -102,7 +102,8 @@ class LlamaForCausalLM(MuModelBase):
     def _native(self, cache) -> "_lib.MukLlamaModel":
         """The executor's model struct (rebuilt when a buffer moves)."""
         ws, cfg = self.ws, self.config
-        key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm))
+        key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
+               self.fused_rope())
         if key == self._native_key:
             return self._native_model
         layers = (_lib.MukLlamaLayer * len(self.layers))()
@@ -129,6 +130,7 @@ class LlamaForCausalLM(MuModelBase):
         m.part, m.part_rows = ws.part.data_ptr(), ws.part_rows
         m.xl, m.logits = ws.xl.data_ptr(), ws.logits.data_ptr()
         m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
+        m.fused_rope = int(self.fused_rope())
         m.tp_world, m.tp_rank = 1, 0
         if self.comm is not None:
             c = self.comm
@@ -149,7 +151,7 @@ class LlamaForCausalLM(MuModelBase):
                               batch.prefill_cu.data_ptr(), batch.last_token_idx.data_ptr(),
                               batch.block_tables.data_ptr(), batch.block_tables.stride(0))
         tp = 4 if m.tp_world > 1 else 0  # two all-reduces of two kernels each
-        per_layer = 7 + (2 if nd > 0 else 0) + (1 if B > nd else 0) + tp
+        per_layer = (6 if m.fused_rope else 7) + (2 if nd > 0 else 0) + (1 if B > nd else 0) + tp
         _lib.call_counted("muk_llama_forward", 4 + per_layer * m.num_layers, ctypes.byref(m),
                           ctypes.byref(b), torch.cuda.current_stream().cuda_stream)
         return self.ws.logits[:B]
@@ -164,7 +166,7 @@ class LlamaForCausalLM(MuModelBase):
         K.residual_rmsnorm(resid, None, self.layers[0]["w_in"], eps, x, clamp=cl, clamp_norm=True)
         nl = len(self.layers)
         for l, L in enumerate(self.layers):
-            K.gemm(x, L["wqkv"], ws.qkv, K.MUK_EPI_BF16, M=T)
+            self.qkv_proj(l, x, L["wqkv"], batch, cache)
             attn = self.attention(l, batch, cache)
             s = choose_split(T, H, attn.shape[1], ws.part_rows)
             part = ws.part_view(s, T, H)

@@ -46,6 +46,8 @@ extern "C" {
 #define MUK_EPI_SWIGLU 2      /* B rows interleaved in 64-row gate/up groups; C[:, j] =
                                  bf16(silu(g_j)·u_j), N/2 output columns                   */
 #define MUK_EPI_BIAS_SILU 3   /* C = bf16(silu(A·Bᵀ + bias))                               */
+#define MUK_EPI_ROPE_KV 4     /* q|k|v projection: RoPE (+QK-norm) and paged-KV append,
+                                 see muk_gemm_qkv_rope                                     */
 
 /* ---- housekeeping -------------------------------------------------------- */
 int muk_version(void);
@@ -175,6 +177,24 @@ int muk_paged_prefill_attn(const void* q, int64_t q_stride, void* out, int64_t o
 int muk_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                   int M, int N, int K, int epilogue, int split_k, const float* bias,
                   void* stream);
+
+/* The q|k|v projection with RoPE, optional QK-norm and the paged-KV append
+ * in its epilogue: A [M, K] bf16 (the normed activations), B the fused
+ * [(Hq + 2Hkv)·D, K] weight.  Per token t: q heads get QK-norm (q_norm_w,
+ * nn.RMSNorm over head_dim with qk_eps, when non-NULL) and rotate-half RoPE
+ * at positions[t] (f32 tables [max_pos][D/2]) and are stored to q_out[t]
+ * (row stride ldq); k heads the same, stored to k_cache at slot_mapping[t];
+ * v heads are stored to v_cache unchanged (slot -1: nothing appended).  The
+ * rotation runs on the f32 accumulator before the single bf16 rounding.
+ * head_dim 64 or 128.  Replaces the q/k/v projections plus the RoPE and KV
+ * concatenation of mu_inference/models/layers.py:661-702 (one kernel instead
+ * of a GEMM and muk_rope_kv_append). */
+int muk_gemm_qkv_rope(const void* A, int64_t lda, const void* B, int64_t ldb, void* q_out,
+                      int64_t ldq, int M, int K, const int32_t* positions,
+                      const int32_t* slot_mapping, const float* rope_cos, const float* rope_sin,
+                      int max_pos, int num_q_heads, int num_kv_heads, int head_dim,
+                      const float* q_norm_w, const float* k_norm_w, float qk_eps, void* k_cache,
+                      void* v_cache, int num_blocks, int block_size, void* stream);
 
 /* Split-K factor (1..max_split) that muk_gemm_bf16 runs fastest for this
  * shape with MUK_EPI_F32 (1 for other epilogues): the same makespan model the
@@ -373,6 +393,7 @@ typedef struct {
   float* ar_data[8];
   float* ar_scratch[8];
   uint32_t* ar_flags[8];
+  int fused_rope; /* 1: RoPE + KV append in the q|k|v GEMM epilogue (muk_gemm_qkv_rope) */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */

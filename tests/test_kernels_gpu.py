@@ -520,3 +520,54 @@ def test_decode_workspace_covers_smaller_batches(cuda):
         att = torch.einsum("bhd,bthd->bht", qf, Kf) / math.sqrt(D)
         ref = torch.einsum("bht,bthd->bhd", att.softmax(-1), Vf).reshape(B, Hq * D)
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+# q|k|v projection with RoPE (+QK-norm) and the KV append in the GEMM epilogue:
+# 1-SM and CTA-pair kernels, head_dim 64 and 128, padding slots (-1)
+@pytest.mark.parametrize("M,Hq,Hkv,D,qk_norm", [(37, 4, 2, 64, True), (300, 32, 8, 128, False),
+                                                (600, 32, 8, 128, True), (130, 16, 8, 128, False)])
+def test_gemm_qkv_rope(cuda, M, Hq, Hkv, D, qk_norm):
+    k = _kern()
+    K_, NB, bs = 512, 64, 16
+    N = (Hq + 2 * Hkv) * D
+    g = torch.Generator(device="cuda").manual_seed(M + D)
+    A = torch.randn(M, K_, device=cuda, generator=g).bfloat16()
+    W = (torch.randn(N, K_, device=cuda, generator=g) * 0.05).bfloat16()
+    pos = torch.randint(0, 500, (M,), device=cuda, generator=g, dtype=torch.int32)
+    slots = torch.randperm(NB * bs, device=cuda, generator=g)[:M].to(torch.int32)
+    slots[M // 3] = -1
+    cos, sin = _rope_tables(512, D, 10000.0, cuda)
+    kc = torch.zeros(NB, Hkv, bs, D, device=cuda, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    qn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)) if qk_norm else None
+    kn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)) if qk_norm else None
+    q_out = torch.zeros(M, N, device=cuda, dtype=torch.bfloat16)
+    k.gemm_qkv_rope(A, W, q_out, pos, slots, cos, sin, Hq, Hkv, D, kc, vc, qn, kn, 1e-6)
+    x = A.float() @ W.float().t()
+    q = x[:, : Hq * D].view(M, Hq, D)
+    kk = x[:, Hq * D:(Hq + Hkv) * D].view(M, Hkv, D)
+    v = x[:, (Hq + Hkv) * D:].view(M, Hkv, D)
+    if qk_norm:
+        q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + 1e-6) * qn
+        kk = kk * torch.rsqrt(kk.pow(2).mean(-1, keepdim=True) + 1e-6) * kn
+    c = torch.cat([cos, cos], -1)[pos.long()].unsqueeze(1)
+    s = torch.cat([sin, sin], -1)[pos.long()].unsqueeze(1)
+
+    def rot(t):
+        return torch.cat([-t[..., D // 2:], t[..., : D // 2]], -1)
+
+    q_ref = q * c + rot(q) * s
+    k_ref = kk * c + rot(kk) * s
+    tol = dict(rtol=2e-2, atol=2e-2 * max(1.0, float(q_ref.abs().max())))
+    torch.testing.assert_close(q_out[:, : Hq * D].float().view(M, Hq, D), q_ref, **tol)
+    for t in range(M):
+        sl = int(slots[t])
+        if sl < 0:
+            continue
+        blk, off = sl // bs, sl % bs
+        torch.testing.assert_close(kc[blk, :, off].float(), k_ref[t], **tol)
+        torch.testing.assert_close(vc[blk, :, off].float(), v[t], **tol)
+    # the padding token appended nothing
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
