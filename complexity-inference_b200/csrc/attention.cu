@@ -301,14 +301,15 @@ __global__ void decode_merge_kernel(__nv_bfloat16* __restrict__ out, int64_t out
 }
 
 // ---------------------------------------------------------------------------
-// K2b: varlen causal prefill
+// K2b: varlen causal prefill.  A CTA serves G query heads that share one KV
+// head (GQA) over 16·WR query rows each: warp w handles head w / WR, rows
+// 16·(w % WR) .. +16.  Every 64-key K/V tile is staged once per CTA and read
+// by all G·WR warps, so a KV byte leaves L2 once per G heads.
 // ---------------------------------------------------------------------------
-constexpr int kPfWarps = 4;
-constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
 constexpr int kPfKeys = 64;             // keys per tile (4 paged blocks)
 
-template <int D>
-__global__ void __launch_bounds__(kPfWarps * 32)
+template <int D, int G, int WR>
+__global__ void __launch_bounds__(G * WR * 32)
     paged_prefill_kernel(const __nv_bfloat16* __restrict__ q, int64_t q_stride,
                          __nv_bfloat16* __restrict__ out, int64_t out_stride,
                          const __nv_bfloat16* __restrict__ k_cache,
@@ -319,35 +320,39 @@ __global__ void __launch_bounds__(kPfWarps * 32)
   constexpr int kChunks = D / 8;
   constexpr int kKS = D / 16;
   constexpr int kDT = D / 8;
-  constexpr int kQTile = kPfRows * D * 2;
+  constexpr int kRows = 16 * WR;           // query rows per head
+  constexpr int kQTile = G * kRows * D * 2;
   constexpr int kKVTile = kPfKeys * D * 2;
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const int b = blockIdx.z, h = blockIdx.y, qt = blockIdx.x;
+  const int b = blockIdx.z, qt = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
+  const int hq = warp / WR, wr = warp % WR;  // this warp's head (within the CTA) and row block
+  const int h = blockIdx.y * G + hq;
   const int q_begin = cu_q[b];
   const int q_len = cu_q[b + 1] - q_begin;
-  const int row0 = qt * kPfRows;
+  const int row0 = qt * kRows;
   if (row0 >= q_len) return;
   const int ctx = seq_lens[b];
   const int past = ctx - q_len;
-  const int kvh = h / (num_q_heads / num_kv_heads);
+  const int kvh = (blockIdx.y * G) / (num_q_heads / num_kv_heads);
   const int32_t* bt = block_tables + (int64_t)b * bt_stride;
 
   const uint32_t sq = smem_u32(smem);
   const uint32_t skv = sq + kQTile;  // two stages of (K tile, V tile)
 
-  // Load the Q tile (rows beyond q_len zero-filled).
-  for (int idx = threadIdx.x; idx < kPfRows * kChunks; idx += blockDim.x) {
-    const int r = idx / kChunks, ch = idx % kChunks;
+  // Load the Q tiles of the G heads (rows beyond q_len zero-filled).
+  for (int idx = threadIdx.x; idx < G * kRows * kChunks; idx += blockDim.x) {
+    const int rr = idx / kChunks, ch = idx % kChunks;
+    const int hh = rr / kRows, r = rr % kRows;
     const int qi = row0 + r;
     const bool valid = qi < q_len;
-    const __nv_bfloat16* src =
-        q + (int64_t)(q_begin + (valid ? qi : 0)) * q_stride + (int64_t)h * D + ch * 8;
-    cp_async_16_zfill(sq + swz<D>(r, ch), src, valid);
+    const __nv_bfloat16* src = q + (int64_t)(q_begin + (valid ? qi : 0)) * q_stride +
+                               (int64_t)(blockIdx.y * G + hh) * D + ch * 8;
+    cp_async_16_zfill(sq + swz<D>(rr, ch), src, valid);
   }
-  const int last_q = min(row0 + kPfRows, q_len) - 1;
+  const int last_q = min(row0 + kRows, q_len) - 1;
   const int kmax = past + last_q;  // inclusive
   const int ntiles = kmax / kPfKeys + 1;
 
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 #pragma unroll
   for (int i = 0; i < kDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   uint32_t qa[kKS][4];
-  const int qrow_lo = row0 + warp * 16 + g;  // query index of rows g / g+8
+  const int qrow_lo = row0 + wr * 16 + g;  // query index of rows g / g+8
   const int qpos_lo = past + qrow_lo, qpos_hi = qpos_lo + 8;
 
   for (int t = 0; t < ntiles; ++t) {
@@ -388,7 +393,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
     __syncthreads();
     if (t == 0) {
       const int mi = lane >> 3, r = lane & 7;
-      const int row = warp * 16 + ((mi & 1) ? 8 : 0) + r;
+      const int row = hq * kRows + wr * 16 + ((mi & 1) ? 8 : 0) + r;
 #pragma unroll
       for (int ks = 0; ks < kKS; ++ks)
         ldmatrix_x4(sq + swz<D>(row, 2 * ks + (mi >> 1)), qa[ks][0], qa[ks][1], qa[ks][2],
@@ -527,9 +532,9 @@ static size_t decode_smem_bytes() {
   return ring > merge ? ring : merge;
 }
 
-template <int D>
+template <int D, int G, int WR>
 static size_t prefill_smem_bytes() {
-  return (size_t)kPfRows * D * 2 + 2 * 2 * (size_t)kPfKeys * D * 2;
+  return (size_t)G * 16 * WR * D * 2 + 2 * 2 * (size_t)kPfKeys * D * 2;
 }
 
 }  // namespace muk
@@ -630,26 +635,54 @@ extern "C" int muk_paged_decode_attn(const void* q, int64_t q_stride, void* out,
   return MUK_ERR_UNSUPPORTED;
 }
 
+template <int D, int G, int WR>
+static int launch_prefill_g(const void* q, int64_t q_stride, void* out, int64_t out_stride,
+                            const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                            int bt_stride, const int32_t* seq_lens, const int32_t* cu_q,
+                            int num_seqs, int max_q_len, int num_q_heads, int num_kv_heads,
+                            int num_blocks, float scale, cudaStream_t stream) {
+  const size_t smem = prefill_smem_bytes<D, G, WR>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(paged_prefill_kernel<D, G, WR>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  dim3 grid((max_q_len + 16 * WR - 1) / (16 * WR), num_q_heads / G, num_seqs);
+  paged_prefill_kernel<D, G, WR><<<grid, G * WR * 32, smem, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<__nv_bfloat16*>(out),
+      out_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
+      reinterpret_cast<const __nv_bfloat16*>(v_cache), block_tables, bt_stride, seq_lens, cu_q,
+      num_q_heads, num_kv_heads, num_blocks, scale * 1.4426950408889634f);
+  return check_launch("muk_paged_prefill_attn");
+}
+
+// Heads per CTA: the whole GQA group up to 4 (fewer when the group size is
+// not a multiple), at most 8 warps per CTA (more would cap the registers
+// below what the tile needs); with 2 heads, 2 warps (32 rows) per head when
+// 4-warp tiles would leave SMs idle.
 template <int D>
 static int launch_prefill(const void* q, int64_t q_stride, void* out, int64_t out_stride,
                           const void* k_cache, const void* v_cache, const int32_t* block_tables,
                           int bt_stride, const int32_t* seq_lens, const int32_t* cu_q,
                           int num_seqs, int max_q_len, int num_q_heads, int num_kv_heads,
                           int num_blocks, float scale, cudaStream_t stream) {
-  const size_t smem = prefill_smem_bytes<D>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(paged_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr_set = true;
+  const int gs = num_q_heads / num_kv_heads;
+  const int G = gs % 4 == 0 ? 4 : (gs % 2 == 0 ? 2 : 1);
+  const long ctas64 = (long)((max_q_len + 63) / 64) * (num_q_heads / G) * num_seqs;
+  const bool wide = ctas64 >= 2L * 148;
+#define MUK_PF(GG, WW)                                                                          \
+  return launch_prefill_g<D, GG, WW>(q, q_stride, out, out_stride, k_cache, v_cache,            \
+                                     block_tables, bt_stride, seq_lens, cu_q, num_seqs,         \
+                                     max_q_len, num_q_heads, num_kv_heads, num_blocks, scale,   \
+                                     stream)
+  if (G == 4) MUK_PF(4, 2);
+  if (G == 2) {
+    if (wide) MUK_PF(2, 4);
+    MUK_PF(2, 2);
   }
-  dim3 grid((max_q_len + kPfRows - 1) / kPfRows, num_q_heads, num_seqs);
-  paged_prefill_kernel<D><<<grid, kPfWarps * 32, smem, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<__nv_bfloat16*>(out),
-      out_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
-      reinterpret_cast<const __nv_bfloat16*>(v_cache), block_tables, bt_stride, seq_lens, cu_q,
-      num_q_heads, num_kv_heads, num_blocks, scale * 1.4426950408889634f);
-  return check_launch("muk_paged_prefill_attn");
+  MUK_PF(1, 4);
+#undef MUK_PF
 }
 
 extern "C" int muk_paged_prefill_attn(const void* q, int64_t q_stride, void* out,

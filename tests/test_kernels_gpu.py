@@ -200,7 +200,10 @@ def test_paged_decode_attention(cuda, Hq, Hkv, D):
         torch.testing.assert_close(out[b].float().view(Hq, D), ref, rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (4, 2, 64)])
+# one CTA per (query tile, group of G query heads sharing a KV head): G = 4
+# (32/8, and 32/4 where two CTAs share a KV head), G = 2 (4/2, 16/8), G = 1
+@pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (4, 2, 64), (32, 4, 128), (16, 8, 128),
+                                      (8, 8, 64)])
 def test_paged_prefill_attention(cuda, Hq, Hkv, D):
     k = _kern()
     # (past, q_len): fresh prompts and continuations with a cached prefix
