@@ -17,6 +17,15 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // Returns MUK_ERR_CUDA (with the message) if the last launch failed.
 int check_launch(const char* what);
 
+// The "finish" half of the peer all-reduce (comm.cu): waits for every rank's
+// "pushed" signal, sums share `rank` (share_elems f32 per rank, a multiple
+// of 4) over the ranks in rank order from the scratch slots (and this rank's
+// data unless own_in_scratch), stores the sum into every rank's data and
+// ends with the cross-GPU "done" barrier.
+int launch_allreduce_finish(float* const* bufs, float* const* scratch, uint32_t* const* flags,
+                            int rank, int world, int64_t n, int64_t share_elems,
+                            bool own_in_scratch, cudaStream_t stream);
+
 }  // namespace muk
 
 #define MUK_REQUIRE(cond, ...)            \

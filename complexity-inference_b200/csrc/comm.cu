@@ -37,14 +37,14 @@
 
 namespace muk {
 
-constexpr int kMaxRanks = 8;
+constexpr int kMaxRanks = kArMaxRanks;
 constexpr int kArThreads = 512;
-// flag area (uint32 words) of every rank
-constexpr int kFlagA = 0;          // [kMaxRanks] "pushed" epochs, by source rank
-constexpr int kFlagB = kMaxRanks;  // [kMaxRanks] "done" epochs, by source rank
-constexpr int kFlagEpoch = 2 * kMaxRanks;
-constexpr int kFlagArrive1 = 2 * kMaxRanks + 1;
-constexpr int kFlagArrive2 = 2 * kMaxRanks + 2;
+// flag area (uint32 words) of every rank, shared with the GEMM's push epilogue
+constexpr int kFlagA = kArFlagA;          // [kMaxRanks] "pushed" epochs, by source rank
+constexpr int kFlagB = kArFlagB;          // [kMaxRanks] "done" epochs, by source rank
+constexpr int kFlagEpoch = kArFlagEpoch;
+constexpr int kFlagArrive1 = kArFlagArrive1;
+constexpr int kFlagArrive2 = kArFlagArrive2;
 constexpr uint64_t kPeerTimeoutNs = 5ull * 1000 * 1000 * 1000;  // 5 s
 
 struct ArArgs {
@@ -56,6 +56,7 @@ struct ArArgs {
   int64_t share;  // float4 elements per rank share = ceil(n4 / world)
   int slices;     // the data holds `slices` partial slices summed first (split-K)
   int64_t slice_stride4;
+  int own_in_scratch;  // this rank's share was pushed into its own scratch slot too
 };
 
 // Sum of the slices of this rank's data at float4 index i (slice 0 first).
@@ -150,7 +151,9 @@ __global__ void __launch_bounds__(kArThreads) allreduce_finish_kernel(const ArAr
       float4 v[kMaxRanks];
 #pragma unroll
       for (int s = 0; s < kMaxRanks; ++s)
-        if (s < a.world) v[s] = s == a.rank ? folded(a, own, i) : scr[(int64_t)s * a.share + k];
+        if (s < a.world)
+          v[s] = (s == a.rank && !a.own_in_scratch) ? folded(a, own, i)
+                                                     : scr[(int64_t)s * a.share + k];
       float4 sum = v[0];
 #pragma unroll
       for (int s = 1; s < kMaxRanks; ++s)
@@ -199,6 +202,28 @@ static int base_of(const void* p, void** base) {
   }
   *base = reinterpret_cast<void*>(start);
   return MUK_OK;
+}
+
+int launch_allreduce_finish(float* const* bufs, float* const* scratch, uint32_t* const* flags,
+                            int rank, int world, int64_t n, int64_t share_elems,
+                            bool own_in_scratch, cudaStream_t stream) {
+  ArArgs a;
+  for (int s = 0; s < kMaxRanks; ++s) {
+    a.data[s] = s < world ? reinterpret_cast<float4*>(bufs[s]) : nullptr;
+    a.scratch[s] = s < world ? reinterpret_cast<float4*>(scratch[s]) : nullptr;
+    a.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  a.rank = rank;
+  a.world = world;
+  a.n4 = n / 4;
+  a.share = share_elems / 4;
+  a.slices = 1;
+  a.slice_stride4 = 0;
+  a.own_in_scratch = own_in_scratch ? 1 : 0;
+  int grid = (int)((a.share + kArThreads - 1) / kArThreads);
+  grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
+  allreduce_finish_kernel<<<grid, kArThreads, 0, stream>>>(a);
+  return check_launch("allreduce finish");
 }
 
 }  // namespace muk
@@ -282,6 +307,7 @@ extern "C" int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint
   a.share = (a.n4 + world - 1) / world;
   a.slices = slices;
   a.slice_stride4 = slice_stride / 4;
+  a.own_in_scratch = 0;
   if (n == 0) return MUK_OK;
   if (world == 1 && slices == 1) return MUK_OK;
   cudaStream_t st = as_stream(stream);

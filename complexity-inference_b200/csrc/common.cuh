@@ -39,6 +39,16 @@ __device__ __forceinline__ void set_device_error(int code) {
   atomicCAS(&g_device_error, 0, code);
 }
 
+// Flag area of the tensor-parallel peer buffers (uint32 words, one area per
+// rank; see comm.cu): "pushed" / "done" epochs by source rank, the call
+// epoch, and two CTA-arrival counters.
+constexpr int kArMaxRanks = 8;
+constexpr int kArFlagA = 0;
+constexpr int kArFlagB = kArMaxRanks;
+constexpr int kArFlagEpoch = 2 * kArMaxRanks;
+constexpr int kArFlagArrive1 = 2 * kArMaxRanks + 1;
+constexpr int kArFlagArrive2 = 2 * kArMaxRanks + 2;
+
 // Poll budget for every mbarrier wait: ~2^26 polls is about a second on a
 // B200, far beyond any legitimate stage latency.  Waiters also give up early
 // once any CTA has recorded an error, so a fault costs one time-out, not one

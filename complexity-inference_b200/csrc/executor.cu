@@ -67,6 +67,9 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
 
   // Sum a row-parallel projection over the tensor-parallel ranks; returns the
   // number of slices the consumer reads.
+  // GEMM + reduce-scatter in one kernel while the step has few rows (see
+  // FUSED_TP_MAX_ROWS in mu_b200/models/base.py: 512)
+  const bool fused_tp = m->tp_world > 1 && m->tp_fused && T <= 512;
   auto reduce = [&](int slices) -> int {
     if (m->tp_world == 1) return slices;
     int rc = muk_allreduce_f32(m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world,
@@ -107,21 +110,35 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
                                      m->num_blocks, scale, stream));
     }
     // O projection (split-K f32 partials) -> reduce -> h += clamp(o); x = clamp(norm(h))
-    int s = choose_split(T, H, attn_n, m->part_rows);
-    MUK_TRY(muk_gemm_bf16(attn, attn_n, L.wo, attn_n, m->part, H, T, H, attn_n, kEpiF32, s,
-                          nullptr, stream));
-    int np = reduce(s);
-    if (np < 0) return np;
+    int np;
+    if (fused_tp) {
+      MUK_TRY(muk_gemm_allreduce_f32(attn, attn_n, L.wo, attn_n, T, H, attn_n, m->ar_data,
+                                     m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world, stream));
+      np = 1;
+    } else {
+      const int s = choose_split(T, H, attn_n, m->part_rows);
+      MUK_TRY(muk_gemm_bf16(attn, attn_n, L.wo, attn_n, m->part, H, T, H, attn_n, kEpiF32, s,
+                            nullptr, stream));
+      np = reduce(s);
+      if (np < 0) return np;
+    }
     MUK_TRY(muk_residual_rmsnorm(m->resid, m->part, (int64_t)T * H, H, np, nullptr, L.post_norm,
                                  m->eps, x, m->x_stride, T, H, cl, 0, cl, mu, cmin, cmax, stream));
     // SwiGLU MLP -> reduce -> h = clamp(h + clamp(mlp)); x = clamp(next_norm(h))
     MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wgu, H, m->act, m->inter_pad, T, 2 * m->inter_pad, H,
                           kEpiSwiglu, 1, nullptr, stream));
-    s = choose_split(T, H, m->inter_pad, m->part_rows);
-    MUK_TRY(muk_gemm_bf16(m->act, m->inter_pad, L.wd, m->inter_pad, m->part, H, T, H,
-                          m->inter_pad, kEpiF32, s, nullptr, stream));
-    np = reduce(s);
-    if (np < 0) return np;
+    if (fused_tp) {
+      MUK_TRY(muk_gemm_allreduce_f32(m->act, m->inter_pad, L.wd, m->inter_pad, T, H, m->inter_pad,
+                                     m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank,
+                                     m->tp_world, stream));
+      np = 1;
+    } else {
+      const int s = choose_split(T, H, m->inter_pad, m->part_rows);
+      MUK_TRY(muk_gemm_bf16(m->act, m->inter_pad, L.wd, m->inter_pad, m->part, H, T, H,
+                            m->inter_pad, kEpiF32, s, nullptr, stream));
+      np = reduce(s);
+      if (np < 0) return np;
+    }
     const bool last = l + 1 == m->num_layers;
     MUK_TRY(muk_residual_rmsnorm(m->resid, m->part, (int64_t)T * H, H, np, nullptr,
                                  last ? nullptr : m->layers[l + 1].in_norm, m->eps,

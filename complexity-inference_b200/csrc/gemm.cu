@@ -86,6 +86,20 @@ struct RopeArgs {
   int max_pos, hq, hkv, head_dim, num_blocks, block_size;
 };
 
+// Epilogue of the row-parallel projections under tensor parallelism
+// (muk_gemm_allreduce_f32): f32 rows pushed to the rank that owns them.
+constexpr int kEpiF32Push = 5;
+
+// Rows [r * share_rows, (r + 1) * share_rows) of the output belong to rank r;
+// this rank's f32 tile rows go to scratch[owner][rank][row - owner's first]
+// (NVLink stores for peers), and when the whole grid is done its last CTA
+// signals "pushed" to every rank.
+struct PushArgs {
+  float* scratch[kArMaxRanks];
+  uint32_t* flags[kArMaxRanks];
+  int rank, world, share_rows;
+};
+
 struct TileArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kt_per_split, total;
@@ -97,7 +111,46 @@ struct TileArgs {
   // tiles [dp_tiles, dp_tiles + sk_tiles) stream-K over `workers` workers
   int dp_tiles, sk_tiles, k_tiles, workers;
   RopeArgs rope;
+  PushArgs push;
 };
+
+__device__ __forceinline__ void store_push(const TileArgs& a, int row, int row_end, int col,
+                                           const uint32_t (&v)[32]) {
+  if (row >= row_end) return;
+  const PushArgs& p = a.push;
+  const int owner = row / p.share_rows;
+  const int r = row - owner * p.share_rows;
+  float* dst = p.scratch[owner] + ((int64_t)p.rank * p.share_rows + r) * a.ldc + col;
+  if (col + 32 <= a.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(dst + j) =
+          make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                      __uint_as_float(v[j + 3]));
+  } else {
+    for (int j = 0; j < 32 && col + j < a.N; ++j) dst[j] = __uint_as_float(v[j]);
+  }
+}
+
+// End of a push GEMM, every thread: its pushes fenced system-wide; the last
+// CTA of the grid then tells every rank "pushed" (the epoch of the call that
+// the finish kernel closes).
+__device__ __forceinline__ void push_done(const TileArgs& a) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const PushArgs& p = a.push;
+  uint32_t* my = p.flags[p.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kArFlagEpoch) + 1u;
+  const uint32_t prev = atomicAdd(my + kArFlagArrive1, 1u);
+  if (prev != gridDim.x - 1) return;
+  my[kArFlagArrive1] = 0u;
+  __threadfence_system();
+  for (int s = 0; s < p.world; ++s)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[s] + kArFlagA + p.rank),
+                 "r"(epoch)
+                 : "memory");
+}
 
 // Stream-K partial slots: (worker, which of its two split units, CTA rank)
 // -> 128 rows x 256 columns f32, stored [column chunk][float4 j][row] so a
@@ -448,7 +501,10 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
       tmem_ld_32x32b_x32(lane_addr + c * 32, v);
       tmem_ld_wait();
       if (fix) sk_sum_chunk(*fix, c, v);
-      store_chunk<EPI>(C, args.ldc, split_off, row, row_end, n0 + c * 32, args.N, v, args.bias);
+      if (EPI == kEpiF32Push)
+        store_push(args, row, row_end, n0 + c * 32, v);
+      else
+        store_chunk<EPI>(C, args.ldc, split_off, row, row_end, n0 + c * 32, args.N, v, args.bias);
     }
   }
 }
@@ -661,6 +717,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
   }
+  if (EPI == kEpiF32Push) push_done(args);
 }
 
 
@@ -858,6 +915,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem, 2 * BN);
   }
+  if (EPI == kEpiF32Push) push_done(args);
 }
 
 // ---------------------------------------------------------------------------
@@ -1115,6 +1173,9 @@ static int dispatch(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, 
     case MUK_EPI_ROPE_KV:
       if (!GROUPED) return launch<BN, S, MUK_EPI_ROPE_KV, false>(ma, mb, C, a, sms, s);
       break;
+    case kEpiF32Push:
+      if (!GROUPED) return launch<BN, S, kEpiF32Push, false>(ma, mb, C, a, sms, s);
+      break;
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1166,7 +1227,8 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
 
 static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                          int64_t ldc, int M, int N, int K, int epilogue, int split_k, bool sk,
-                         const float* bias, const RopeArgs* rope, int sms, cudaStream_t stream) {
+                         const float* bias, const RopeArgs* rope, const PushArgs* push, int sms,
+                         cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
@@ -1187,6 +1249,7 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
   a.offsets = nullptr;
   a.num_experts = 0;
   a.rope = rope ? *rope : RopeArgs{};
+  a.push = push ? *push : PushArgs{};
   set_schedule(a, sms / 2, 2, sk);
   switch (epilogue) {
     case MUK_EPI_BF16:
@@ -1199,6 +1262,8 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
       return launch_pair<MUK_EPI_BIAS_SILU>(ma, mb, C, a, sms, stream);
     case MUK_EPI_ROPE_KV:
       return launch_pair<MUK_EPI_ROPE_KV>(ma, mb, C, a, sms, stream);
+    case kEpiF32Push:
+      return launch_pair<kEpiF32Push>(ma, mb, C, a, sms, stream);
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1235,7 +1300,7 @@ static GemmPlan plan_for_split(int M, int N, int K, int epilogue, int split_k, i
 static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
                     const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream,
-                    const RopeArgs* rope = nullptr) {
+                    const RopeArgs* rope = nullptr, const PushArgs* push = nullptr) {
   int rc = get_encode();
   if (rc) return rc;
   const int sms = sm_count();
@@ -1245,7 +1310,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
     const GemmPlan best = plan_for_split(M, N, K, epilogue, split_k, sms);
     if (best.kind == 1)
       return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, rope,
-                           sms, stream);
+                           push, sms, stream);
     bn = best.bn;
     sk = best.sk;
   } else {
@@ -1271,6 +1336,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   a.offsets = offsets;
   a.num_experts = num_experts;
   a.rope = rope ? *rope : RopeArgs{};
+  a.push = push ? *push : PushArgs{};
   set_schedule(a, sms, 1, sk);
   if (bn == 256)
     return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
@@ -1405,4 +1471,40 @@ extern "C" int muk_gemm_qkv_rope(const void* A, int64_t lda, const void* B, int6
   const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
   return run_gemm(false, A, lda, B, ldb, q_out, ldq, M, N, K, MUK_EPI_ROPE_KV, 1, nullptr,
                   nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), &r);
+}
+
+extern "C" int64_t muk_gemm_allreduce_scratch_elems(int M, int N, int world) {
+  if (M < 0 || N <= 0 || world < 1) return 0;
+  return (int64_t)world * ((M + world - 1) / world) * N;
+}
+
+extern "C" int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                      int M, int N, int K, float* const* bufs,
+                                      float* const* scratch, uint32_t* const* flags, int rank,
+                                      int world, void* stream) {
+  MUK_REQUIRE(A && B && bufs && scratch && flags && world >= 1 && world <= kArMaxRanks &&
+                  rank >= 0 && rank < world,
+              "muk_gemm_allreduce_f32: rank %d of %d", rank, world);
+  MUK_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 4 == 0 && lda >= K && ldb >= K && lda % 8 == 0 &&
+                  ldb % 8 == 0 && MUK_ALIGNED16(A) && MUK_ALIGNED16(B),
+              "muk_gemm_allreduce_f32: shape M=%d N=%d K=%d or A/B alignment", M, N, K);
+  for (int s = 0; s < world; ++s)
+    MUK_REQUIRE(bufs[s] && scratch[s] && flags[s] && MUK_ALIGNED16(bufs[s]) &&
+                    MUK_ALIGNED16(scratch[s]) && MUK_ALIGNED16(flags[s]),
+                "muk_gemm_allreduce_f32: rank %d buffer, scratch or flags", s);
+  if (M == 0) return MUK_OK;
+  PushArgs p;
+  for (int s = 0; s < kArMaxRanks; ++s) {
+    p.scratch[s] = s < world ? scratch[s] : nullptr;
+    p.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  p.rank = rank;
+  p.world = world;
+  p.share_rows = (M + world - 1) / world;
+  cudaStream_t st = as_stream(stream);
+  int rc = run_gemm(false, A, lda, B, ldb, bufs[rank], N, M, N, K, kEpiF32Push, 1, nullptr,
+                    nullptr, 0, (M + kBM - 1) / kBM, st, nullptr, &p);
+  if (rc) return rc;
+  return launch_allreduce_finish(bufs, scratch, flags, rank, world, (int64_t)M * N,
+                                 (int64_t)p.share_rows * N, true, st);
 }

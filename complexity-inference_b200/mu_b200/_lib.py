@@ -68,6 +68,9 @@ SIGNATURES = {
     "muk_allreduce_scratch_elems": (c_int64, [c_int64, c_int]),
     "muk_allreduce_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int64, c_int, c_int64, _P]),
     "muk_llama_forward": (c_int, [_P, _P, _P]),
+    "muk_gemm_allreduce_scratch_elems": (c_int64, [c_int, c_int, c_int]),
+    "muk_gemm_allreduce_f32": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P, _P,
+                                       c_int, c_int, _P]),
     "muk_route_permute": (c_int, [_P, c_int, c_int, _P, _P, _P, _P]),
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
@@ -101,7 +104,8 @@ class MukLlamaModel(ctypes.Structure):
                 ("act", c_void_p), ("part", c_void_p), ("part_rows", c_int64), ("xl", c_void_p),
                 ("logits", c_void_p), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
                 ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
-                ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int)]
+                ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int),
+                ("tp_fused", c_int)]
 
 
 class MukStepBatch(ctypes.Structure):
@@ -117,7 +121,8 @@ _lib: ctypes.CDLL | None = None
 # Kernel launches issued through call() (entry points that launch two kernels
 # count both); the benchmark reports it as its launch count.
 launch_count = 0
-_TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32"}
+_TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32",
+                "muk_gemm_allreduce_f32"}
 
 
 class MukError(RuntimeError):

@@ -36,8 +36,10 @@ class PeerAllReduce:
         lib = _lib.load()
         flag_words = int(lib.muk_allreduce_flag_bytes()) // 4
         self.max_elems = (int(max_elems) + 63) // 64 * 64
+        # row-owned shares of the fused GEMM + all-reduce round rows up per
+        # rank: room for one extra row per rank at the widest hidden size
         self.scratch_elems = (int(lib.muk_allreduce_scratch_elems(self.max_elems, self.world))
-                              + 63) // 64 * 64
+                              + self.world * 16384 + 63) // 64 * 64
         # [data | scratch (world shares) | flags], f32; the flag area starts zeroed
         self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words,
                                dtype=torch.float32, device=device)
@@ -97,6 +99,25 @@ class PeerAllReduce:
                   ctypes.addressof(self._flags), self.rank, self.world, n, slices, n,
                   torch.cuda.current_stream().cuda_stream)
         return t[0] if slices > 1 else t
+
+    def gemm_all_reduce(self, A: torch.Tensor, W: torch.Tensor, M: int) -> torch.Tensor:
+        """out = Σ_ranks A_r · W_rᵀ as f32 [M, N] in every rank's buffer (start
+        of the data range, returned as [1, M, N]): the row-parallel GEMM whose
+        epilogue pushes each row to its owner rank, then the owners' sums
+        stored to every rank (``muk_gemm_allreduce_f32``)."""
+        N, K = W.shape[0], A.shape[1]
+        lib = _lib.load()
+        need = int(lib.muk_gemm_allreduce_scratch_elems(M, N, self.world))
+        if M * N > self.max_elems or need > self.scratch_elems:
+            raise ValueError(f"PeerAllReduce: {M}x{N} does not fit the peer buffers")
+        bufs = self._data_arrays.get(0)
+        if bufs is None:
+            bufs = self._data_arrays[0] = (ctypes.c_void_p * self.world)(*self.ptrs)
+        _lib.call("muk_gemm_allreduce_f32", A.data_ptr(), A.stride(0), W.data_ptr(), W.stride(0),
+                  M, N, K, ctypes.addressof(bufs), ctypes.addressof(self._scratch),
+                  ctypes.addressof(self._flags), self.rank, self.world,
+                  torch.cuda.current_stream().cuda_stream)
+        return self.buf[:M * N].view(1, M, N)
 
     def close(self) -> None:
         torch.cuda.synchronize()

@@ -25,6 +25,11 @@ from ..core.config import ModelConfig, MuConfig
 from ..kernels import Clamp
 
 PAD_MULT = 64  # SwiGLU weights are interleaved in 64-row gate/up groups
+# Row-parallel GEMM with the reduce-scatter in its epilogue pays while the
+# GEMM has few rows (decode steps: 68 vs 79 us at 256 x 4096 x 2048 on 2
+# GPUs); with more rows the epilogue's row-per-lane NVLink stores lose to a
+# local GEMM plus the coalesced push kernel (117 vs 91 us at 1000 rows).
+FUSED_TP_MAX_ROWS = 512
 
 
 @dataclass
@@ -124,6 +129,7 @@ class MuModelBase:
         self.rope_sin: Optional[torch.Tensor] = None
         self._rope_len = 0
         self._fused_rope = os.environ.get("MU_FUSED_ROPE", "1") != "0"
+        self._tp_fused = os.environ.get("MU_TP_FUSED", "1") != "0"
         self.tp_group = None   # torch.distributed group when tensor-parallel
         self.comm = None       # mu_b200.comm.PeerAllReduce when tensor-parallel over NVLink
         self.ensure_rope(max(config.max_position_embeddings, 16))
@@ -171,6 +177,20 @@ class MuModelBase:
         return True
 
     # ---- shared pieces of the step ---------------------------------------------
+    def row_parallel(self, A: torch.Tensor, W: torch.Tensor, T: int, N: int) -> torch.Tensor:
+        """A row-parallel projection (O, down) summed over the TP ranks; returns
+        the [S, T, N] f32 slices the consumer reads.  Under peer-memory TP the
+        GEMM and the reduce-scatter are one kernel (``muk_gemm_allreduce_f32``;
+        MU_TP_FUSED=0: GEMM, then ``muk_allreduce_f32``); otherwise split-K
+        partials, all-reduced by NCCL under TP."""
+        ws = self.ws
+        if self.comm is not None and ws.shared_part and self._tp_fused and T <= FUSED_TP_MAX_ROWS:
+            return self.comm.gemm_all_reduce(A, W, T)
+        s = choose_split(T, N, A.shape[1], ws.part_rows)
+        part = ws.part_view(s, T, N)
+        K.gemm(A, W, part, K.MUK_EPI_F32, split_k=s, M=T)
+        return self.reduce_partials(part)
+
     def reduce_partials(self, part: torch.Tensor) -> torch.Tensor:
         """Sum a row-parallel projection's output over the TP ranks and return
         what the consumer reads: in place through peer memory when the

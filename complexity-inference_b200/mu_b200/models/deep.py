@@ -26,7 +26,7 @@ import torch
 
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
-from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
+from .base import PAD_MULT, MuModelBase, interleave_gate_up, pad_cols, pad_to
 from .registry import register_model
 from .weights import expert_intermediate, is_routed
 
@@ -150,10 +150,7 @@ class DeepForCausalLM(MuModelBase):
             self.qkv_proj(l, xcat[:, :kdim], L["wcat"][:, :kdim], batch, cache, L.get("qn"),
                           L.get("kn"))
             attn = self.attention(l, batch, cache)
-            s = choose_split(T, H, attn.shape[1], ws.part_rows)
-            part = ws.part_view(s, T, H)
-            K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            part = self.reduce_partials(part)
+            part = self.row_parallel(attn[:T], L["wo"], T, H)
             K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)   # h = clamp(o_proj)
             K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
             K.gemm(ws.ch, L["wco"], ws.ctrl, K.MUK_EPI_F32, M=T)
@@ -181,10 +178,7 @@ class DeepForCausalLM(MuModelBase):
                                    delta_rows=ws.inv)
             else:
                 K.gemm(ws.x2, L["wgu"], ws.act, K.MUK_EPI_SWIGLU, M=T)
-                s = choose_split(T, H, self.i_pad, ws.part_rows)
-                part = ws.part_view(s, T, H)
-                K.gemm(ws.act, L["wd"], part, K.MUK_EPI_F32, split_k=s, M=T)
-                part = self.reduce_partials(part)
+                part = self.row_parallel(ws.act[:T], L["wd"], T, H)
                 K.residual_rmsnorm(resid, part, nxt_w, eps, nxt_out, clamp=cl, clamp_delta=True,
                                    clamp_sum=True, clamp_norm=True)
         return self.lm_head(batch, self.norm_w, self.lm_w)

@@ -26,7 +26,7 @@ import torch
 from .. import _lib
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
-from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
+from .base import PAD_MULT, MuModelBase, interleave_gate_up, pad_cols, pad_to
 from .registry import register_model
 
 
@@ -103,7 +103,7 @@ class LlamaForCausalLM(MuModelBase):
         """The executor's model struct (rebuilt when a buffer moves)."""
         ws, cfg = self.ws, self.config
         key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
-               self.fused_rope())
+               self.fused_rope(), self._tp_fused)
         if key == self._native_key:
             return self._native_model
         layers = (_lib.MukLlamaLayer * len(self.layers))()
@@ -131,6 +131,7 @@ class LlamaForCausalLM(MuModelBase):
         m.xl, m.logits = ws.xl.data_ptr(), ws.logits.data_ptr()
         m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
         m.fused_rope = int(self.fused_rope())
+        m.tp_fused = int(self._tp_fused)
         m.tp_world, m.tp_rank = 1, 0
         if self.comm is not None:
             c = self.comm
@@ -150,7 +151,9 @@ class LlamaForCausalLM(MuModelBase):
                               batch.slot_mapping.data_ptr(), batch.seq_lens.data_ptr(),
                               batch.prefill_cu.data_ptr(), batch.last_token_idx.data_ptr(),
                               batch.block_tables.data_ptr(), batch.block_tables.stride(0))
-        tp = 4 if m.tp_world > 1 else 0  # two all-reduces of two kernels each
+        # two all-reduces per layer: fused (GEMM + finish: one extra kernel each)
+        # or separate (push + finish: two each)
+        tp = (2 if (m.tp_fused and T <= 512) else 4) if m.tp_world > 1 else 0
         per_layer = (6 if m.fused_rope else 7) + (2 if nd > 0 else 0) + (1 if B > nd else 0) + tp
         _lib.call_counted("muk_llama_forward", 4 + per_layer * m.num_layers, ctypes.byref(m),
                           ctypes.byref(b), torch.cuda.current_stream().cuda_stream)
@@ -168,18 +171,12 @@ class LlamaForCausalLM(MuModelBase):
         for l, L in enumerate(self.layers):
             self.qkv_proj(l, x, L["wqkv"], batch, cache)
             attn = self.attention(l, batch, cache)
-            s = choose_split(T, H, attn.shape[1], ws.part_rows)
-            part = ws.part_view(s, T, H)
-            K.gemm(attn, L["wo"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            part = self.reduce_partials(part)
+            part = self.row_parallel(attn[:T], L["wo"], T, H)
             # h += clamp(attn_out); x = clamp(norm_post(h))    (llama.py:111-115)
             K.residual_rmsnorm(resid, part, L["w_post"], eps, x, clamp=cl, clamp_delta=True,
                                clamp_norm=True)
             K.gemm(x, L["wgu"], ws.act, K.MUK_EPI_SWIGLU, M=T)
-            s = choose_split(T, H, self.i_pad, ws.part_rows)
-            part = ws.part_view(s, T, H)
-            K.gemm(ws.act, L["wd"], part, K.MUK_EPI_F32, split_k=s, M=T)
-            part = self.reduce_partials(part)
+            part = self.row_parallel(ws.act[:T], L["wd"], T, H)
             # h = clamp(h + clamp(mlp_out)); x = clamp(norm_in_next(h))   (llama.py:116-126)
             last = l + 1 == nl
             K.residual_rmsnorm(resid, part, None if last else self.layers[l + 1]["w_in"], eps,

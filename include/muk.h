@@ -344,6 +344,25 @@ int64_t muk_allreduce_scratch_elems(int64_t n, int world);
 int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags, int rank,
                       int world, int64_t n, int slices, int64_t slice_stride, void* stream);
 
+/* f32 scratch elements per rank that muk_gemm_allreduce_f32 needs. */
+int64_t muk_gemm_allreduce_scratch_elems(int M, int N, int world);
+
+/* Row-parallel projection and its all-reduce fused over NVLink: out =
+ * Σ_ranks A_r · B_rᵀ (f32 [M, N]) in every rank's bufs[rank].  The GEMM's
+ * epilogue stores each f32 output row straight into the scratch slot of the
+ * rank that owns the row (rows split evenly over the ranks; NVLink stores
+ * for peers) and the GEMM's last CTA signals the peers, so the tile math and
+ * the exchange overlap in one kernel (GEMM -> reduce-scatter); a second
+ * kernel sums the owned rows in rank order and stores them to every rank
+ * (all-gather), ending with a cross-GPU barrier.  Same buffers, flags and
+ * call-order rules as muk_allreduce_f32; the scratch must hold
+ * muk_gemm_allreduce_scratch_elems(M, N, world) floats.  Replaces the O and
+ * down projections (nn.Linear, mu_inference/models/layers.py:421, 730) plus
+ * the all-reduce tensor parallelism needs. */
+int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
+                           int K, float* const* bufs, float* const* scratch,
+                           uint32_t* const* flags, int rank, int world, void* stream);
+
 /* ---- Native step executor (dense Llama family) ----------------------------- */
 
 /* One decoder layer's weights: f32 norm weights, bf16 K-major matrices
@@ -394,6 +413,7 @@ typedef struct {
   float* ar_scratch[8];
   uint32_t* ar_flags[8];
   int fused_rope; /* 1: RoPE + KV append in the q|k|v GEMM epilogue (muk_gemm_qkv_rope) */
+  int tp_fused;   /* 1: O / down projections as muk_gemm_allreduce_f32 under TP */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */

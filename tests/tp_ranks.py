@@ -57,6 +57,20 @@ def check_peer_allreduce(rank, world, failures):
     torch.cuda.synchronize()
     if out.data_ptr() != x.data_ptr() or not torch.allclose(out, ref, rtol=1e-5, atol=1e-5):
         failures.append(("peer allreduce slices", float((out - ref).abs().max())))
+    # GEMM and reduce-scatter fused (muk_gemm_allreduce_f32): out = sum_r A_r W_r^T
+    M, N, Kd = 37, 256, 320
+    A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).bfloat16()
+    ref = A.float() @ W.float().t()
+    dist.all_reduce(ref)
+    out = comm.gemm_all_reduce(A, W, M)[0]
+    torch.cuda.synchronize()
+    if not torch.allclose(out, ref, rtol=1e-4, atol=1e-4 * float(ref.abs().max())):
+        failures.append(("fused gemm allreduce", float((out - ref).abs().max())))
+    allx = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(allx, out.contiguous())
+    if not all(torch.equal(a, allx[0]) for a in allx):
+        failures.append(("fused gemm allreduce not identical across ranks",))
     # graph capture and replay
     n = 4096
     x = comm.view(n)
@@ -98,13 +112,15 @@ def main():
     failures = []
     check_peer_allreduce(rank, world, failures)
     # (model, CUDA graphs, expert parallel, all-reduce: peer memory or NCCL)
+    # "peer": GEMM + reduce-scatter fused; "peer-split": GEMM, then muk_allreduce_f32
     for name, graphs, ep, comm in (("llama_tiny", False, False, "nccl"),
                                    ("llama_tiny", True, False, "peer"),
-                                   ("llama_tiny", False, False, "peer"),
+                                   ("llama_tiny", False, False, "peer-split"),
                                    ("deep_tiny", False, False, "nccl"),
                                    ("deep_tiny", True, False, "peer"),
-                                   ("deep_tiny", True, True, "peer")):
-        os.environ["MU_TP_COMM"] = comm
+                                   ("deep_tiny", True, True, "peer-split")):
+        os.environ["MU_TP_COMM"] = "nccl" if comm == "nccl" else "peer"
+        os.environ["MU_TP_FUSED"] = "0" if comm == "peer-split" else "1"
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
                           expert_parallel=ep,
