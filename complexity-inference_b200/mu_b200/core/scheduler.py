@@ -224,6 +224,81 @@ class MuScheduler:
             to_free -= 1
         return preempted
 
+    def fit_blocks(self, out: SchedulerOutput, free: int, need_of: Callable[[Request, int], int],
+                   held_of: Callable[[Request], int]) -> List[Request]:
+        """Shrink a scheduled step until its new KV blocks fit the ``free`` ones.
+
+        ``need_of(req, n)``: blocks that appending ``n`` tokens to ``req``
+        takes (a request not yet in the cache counts its first block);
+        ``held_of(req)``: blocks ``req`` holds now.  The reference never runs
+        out of KV memory (its cache grows by ``torch.cat``), so this is an
+        addition, in the reference's own terms.  In order:
+
+        1. requests admitted by this ``schedule`` go back to the front of the
+           queue (newest first), while a running request holds blocks that
+           will come free;
+        2. prefills already under way are preempted (newest first);
+        3. decodes are preempted as ``_preempt_requests`` does it (most
+           generated tokens first).
+
+        Preemption is by recompute: the engine frees the request's blocks and
+        it re-prefills prompt + generated tokens when readmitted.  Every
+        preemption frees blocks, so the loop cannot cycle; a request that
+        does not fit an otherwise empty pool is left for the cache's
+        all-or-nothing reserve to reject.  Returns the requests preempted
+        here (also appended to ``out.preempted_requests``)."""
+        need = {id(r): need_of(r, 1) for r in out.decode_requests}
+        for r, (_, n) in zip(out.prefill_requests, out.prefill_chunks):
+            need[id(r)] = need_of(r, n)
+        total = sum(need.values())
+        if total <= free:
+            return []
+
+        def drop_prefill(req: Request) -> None:
+            nonlocal total
+            i = out.prefill_requests.index(req)
+            out.prefill_requests.pop(i)
+            _, n = out.prefill_chunks.pop(i)
+            out.num_prefill_tokens -= n
+            total -= need.pop(id(req))
+
+        fresh = [r for r in out.prefill_requests if r.num_prefilled == 0 and held_of(r) == 0]
+        others_hold = any(held_of(r) > 0 for r in self.running.values())
+        deferred: List[Request] = []
+        for req in reversed(fresh):
+            if total <= free or not others_hold:
+                break
+            drop_prefill(req)
+            self.running.pop(req.request_id, None)
+            req.status = RequestStatus.PREEMPTED if req.num_generated_tokens else RequestStatus.PENDING
+            deferred.insert(0, req)
+        self._requeue_front(deferred)
+
+        victims = [r for r in reversed(out.prefill_requests) if held_of(r) > 0]
+        victims += sorted(out.decode_requests, key=lambda r: r.num_generated_tokens, reverse=True)
+        preempted: List[Request] = []
+        for req in victims:
+            if total <= free:
+                break
+            free += held_of(req)
+            if req in out.prefill_requests:
+                drop_prefill(req)
+            else:
+                out.decode_requests.remove(req)
+                out.num_decode_tokens -= 1
+                total -= need.pop(id(req))
+            req.status = RequestStatus.PREEMPTED
+            req.num_preemptions += 1
+            req.num_prefilled = 0
+            if self.config.policy == "priority":
+                req.priority = soft_clamp(req.priority - 1.0, -10.0, 10.0)
+                heapq.heappush(self.priority_queue, req)
+            else:
+                self.waiting.appendleft(req)
+            preempted.append(req)
+        out.preempted_requests.extend(preempted)
+        return preempted
+
     def finish_request(self, request_id: str, success: bool = True) -> None:
         req = self.running.pop(request_id, None)
         if req is None:  # finished while re-queued after a preemption

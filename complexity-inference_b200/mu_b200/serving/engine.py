@@ -165,6 +165,19 @@ class StepEngine:
         out = self.scheduler.schedule(self._closing)
         for req in out.preempted_requests:  # recompute preemption: drop KV, re-prefill later
             self._release(req.request_id)
+        # the step's new KV blocks must fit the pool: defer admissions, then
+        # preempt (recompute) until they do
+        cache, active = self.worker.cache, self.worker.active_requests
+        bs = cache.block_size
+
+        def need_of(r: Request, n: int) -> int:
+            if r.request_id in active:
+                return cache.blocks_needed(r.request_id, n)
+            return max(1, -(-n // bs))
+
+        for req in self.scheduler.fit_blocks(out, len(cache.free_blocks), need_of,
+                                             lambda r: len(cache.block_table(r.request_id))):
+            self._release(req.request_id)
         prefills: List[Request] = []
         chunks: List[tuple] = []
         for req, chunk in zip(out.prefill_requests, out.prefill_chunks):

@@ -98,13 +98,14 @@ def expected(prompt, max_tokens, stop):
 
 
 def run(overlap, prompts, limits, stop, max_batch, abort=None, monkeypatch=None, budget=64,
-        chunked=True):
+        chunked=True, blocks=64, batched_tokens=64):
     monkeypatch.setattr(E, "BatchSampler", FakeSampler)
-    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=max_batch),
-                      scheduler=SchedulerConfig(max_batch_size=max_batch, max_num_batched_tokens=64,
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=blocks, max_num_seqs=max_batch),
+                      scheduler=SchedulerConfig(max_batch_size=max_batch,
+                                                max_num_batched_tokens=batched_tokens,
                                                 max_prefill_tokens=budget,
                                                 enable_chunked_prefill=chunked))
-    w = FakeWorker()
+    w = FakeWorker(blocks)
     eng = E.StepEngine(w, ec, overlap=overlap)
     for i, (p, m) in enumerate(zip(prompts, limits)):
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=m, stop_token_ids=stop),
@@ -179,4 +180,45 @@ def test_chunked_prefill(overlap, monkeypatch):
     for (b, nd), t in zip(w.steps, w.tokens):
         assert t - nd <= budget
     assert max(w.tokens) <= budget + 3
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+@pytest.mark.parametrize("chunked", [False, True])
+def test_kv_pool_exhaustion_preempts_and_recomputes(overlap, chunked, monkeypatch):
+    """A pool far smaller than the requests' final lengths: admissions wait and
+    running requests are preempted (KV freed, prompt + generated tokens
+    re-prefilled on readmission) instead of failing; every request still
+    generates exactly its sequential tokens and every block comes back."""
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in (7, 10, 4, 9, 6, 8)]
+    limits = [14, 9, 16, 12, 11, 15]
+    blocks = 12  # 48 token slots; the requests end at 18-26 tokens each
+    eng, w, reported = run(overlap, prompts, limits, [], max_batch=4, monkeypatch=monkeypatch,
+                           budget=8, chunked=chunked, blocks=blocks)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        req = eng.requests[f"r{i}"]
+        want = expected(p, m, [])
+        assert req.output_token_ids == want, (i, overlap, chunked)
+        assert reported[f"r{i}"] == want
+        assert req.finish_reason == "length"
+    assert sum(eng.requests[f"r{i}"].num_preemptions for i in range(len(prompts))) > 0
+    assert not w.active_requests and len(w.cache.free_blocks) == blocks
+    assert not eng.sampler.row_of and not eng._closing
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_token_budget_preemption_recomputes(overlap, monkeypatch):
+    """The reference's own preemption (more decodes than max_num_batched_tokens:
+    the most advanced go back to the queue) under the engine: preempted
+    requests re-prefill and finish with their sequential tokens."""
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in (3, 5, 4, 6, 2, 5)]
+    limits = [8, 6, 9, 5, 7, 6]
+    eng, w, reported = run(overlap, prompts, limits, [], max_batch=6, monkeypatch=monkeypatch,
+                           chunked=False, batched_tokens=4)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        assert eng.requests[f"r{i}"].output_token_ids == expected(p, m, []), (i, overlap)
+        assert reported[f"r{i}"] == expected(p, m, [])
+    assert sum(eng.requests[f"r{i}"].num_preemptions for i in range(len(prompts))) > 0
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks

@@ -161,6 +161,52 @@ def test_scheduler_order_budget_and_preemption():
     assert st["finished"] == 1 and st["policy"] == "fcfs"
 
 
+def test_scheduler_fit_blocks_order():
+    """KV-pool fit: fresh admissions wait first, then prefills under way and
+    the most advanced decodes are preempted, until the step's new blocks fit."""
+    sc = MuScheduler(SchedulerConfig(max_batch_size=8, max_num_batched_tokens=64,
+                                     max_prefill_tokens=64))
+    held = {"d0": 3, "d1": 2, "p": 1}
+    for rid, gen in (("d0", 5), ("d1", 2)):
+        q = Request(request_id=rid, num_prompt_tokens=4, num_generated_tokens=gen)
+        q.status = RequestStatus.DECODE
+        sc.running[rid] = q
+    cont = Request(request_id="p", num_prompt_tokens=20, num_prefilled=8)
+    cont.status = RequestStatus.PREFILL
+    sc.running["p"] = cont
+    sc.add_request(Request(request_id="n", num_prompt_tokens=12))
+    out = sc.schedule()
+    assert [r.request_id for r in out.prefill_requests] == ["p", "n"]
+    need_of = lambda r, n: 1 if r.status == RequestStatus.DECODE else -(-n // 4)
+    held_of = lambda r: held.get(r.request_id, 0)
+    # 2 decode blocks + 3 for p's 12 tokens + 3 for n: 8 > 6 free -> n waits
+    pre = sc.fit_blocks(out, 6, need_of, held_of)
+    assert pre == [] and [r.request_id for r in out.prefill_requests] == ["p"]
+    assert sc.waiting[0].request_id == "n" and "n" not in sc.running
+    # everything fits: nothing changes
+    out = sc.schedule()
+    n_out = [r.request_id for r in out.prefill_requests]
+    assert sc.fit_blocks(out, 100, need_of, held_of) == [] and n_out == ["p", "n"]
+    # no free block: p (under way) is preempted, then d0 (most generated)
+    sc.waiting.clear()
+    sc.running.pop("n", None)
+    out = sc.schedule()
+    pre = sc.fit_blocks(out, 0, need_of, held_of)
+    assert [r.request_id for r in pre] == ["p", "d0"]
+    assert [r.request_id for r in out.decode_requests] == ["d1"] and not out.prefill_requests
+    assert out.num_prefill_tokens == 0 and out.num_decode_tokens == 1
+    assert all(r.status == RequestStatus.PREEMPTED and r.num_preemptions == 1 for r in pre)
+    assert sc.running["p"].num_prefilled == 0
+    assert [r.request_id for r in sc.waiting][:2] == ["d0", "p"]
+    # alone in the pool a request is never deferred: the cache's reserve rejects it
+    sc3 = MuScheduler(SchedulerConfig(max_batch_size=2, max_num_batched_tokens=64,
+                                      max_prefill_tokens=64))
+    sc3.add_request(Request(request_id="huge", num_prompt_tokens=40))
+    out = sc3.schedule()
+    assert sc3.fit_blocks(out, 4, need_of, lambda r: 0) == []
+    assert [r.request_id for r in out.prefill_requests] == ["huge"]
+
+
 def test_sampling_params_validation():
     SamplingParams(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0)
     for kw in ({"temperature": -1}, {"top_k": -1}, {"top_p": 0.0}, {"top_p": 1.5},

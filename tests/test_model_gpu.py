@@ -25,13 +25,13 @@ LOGIT_TOL = 2e-2      # max-abs, bf16 path vs fp32 reference
 GAP_TOL = 0.05        # reference top-2 gap below which argmax may flip
 
 
-def _worker(name, cuda, graphs=True, max_batch=8):
+def _worker(name, cuda, graphs=True, max_batch=8, blocks=512):
     from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
     from mu_b200.serving.worker import MuWorker
 
     shape, cfg, sd, d, prompts = load_tiny(name)
     ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True),
-                      cache=CacheConfig(max_seq_len=256, max_num_blocks=512, max_num_seqs=16),
+                      cache=CacheConfig(max_seq_len=256, max_num_blocks=blocks, max_num_seqs=16),
                       scheduler=SchedulerConfig(max_batch_size=max_batch,
                                                 max_num_batched_tokens=2048))
     w = MuWorker(ec, str(cuda))
@@ -193,6 +193,40 @@ def test_engine_chunked_prefill(cuda, name):
     eng.run_to_completion()
     for r in range(R):
         got = eng.requests[f"r{r}"].output_token_ids
+        assert len(got) == n
+        for i, t in enumerate(got):
+            if t != int(toks[r, i]):
+                assert d["top2_gap"][r, i] <= GAP_TOL, (name, r, i, t, int(toks[r, i]))
+                break
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
+def test_engine_kv_pool_exhaustion(cuda, name):
+    """A KV pool too small for all requests at once: admissions wait and
+    running requests are preempted and recomputed (prompt + generated tokens
+    re-prefilled through the paged prefill kernel); greedy tokens must still
+    match the reference's, and every block must come back."""
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    toks = np.load(__import__("golden_models").G / f"{name}.npz")["tokens"]
+    R, n = toks.shape
+    shape, cfg, sd, d, prompts = load_tiny(name)
+    per = [-(-(len(p) + n) // 16) for p in prompts]
+    blocks = max(per) + 1
+    assert sum(per) > blocks
+    w, shape, d, prompts, ec = _worker(name, cuda, graphs=True, max_batch=R, blocks=blocks)
+    eng = StepEngine(w, ec)
+    for r in range(R):
+        eng.add_request(prompts[r], SamplingParams(temperature=0.0, top_k=0, top_p=1.0,
+                                                   repetition_penalty=1.0, max_tokens=n), f"r{r}")
+    eng.run_to_completion()
+    assert sum(eng.requests[f"r{r}"].num_preemptions for r in range(R)) > 0
+    for r in range(R):
+        req = eng.requests[f"r{r}"]
+        assert req.finish_reason == "length", (r, req.finish_reason)
+        got = req.output_token_ids
         assert len(got) == n
         for i, t in enumerate(got):
             if t != int(toks[r, i]):
