@@ -198,7 +198,7 @@ class Arrivals:
         return engine.add_request(prompt, sp, f"q{self.n}")
 
 
-def build(rank: int, tp: int = 1, wl=C3, ep: bool = False):
+def build(rank: int, tp: int = 1, wl=C3, ep: bool = False, align: int = 0):
     from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
     from mu_b200.models.weights import random_state_dict
     from mu_b200.serving.engine import StepEngine
@@ -214,7 +214,8 @@ def build(rank: int, tp: int = 1, wl=C3, ep: bool = False):
                                         max_num_seqs=wl["concurrency"]),
                       scheduler=SchedulerConfig(max_batch_size=wl["concurrency"],
                                                 max_num_batched_tokens=8192,
-                                                max_prefill_tokens=8192))
+                                                max_prefill_tokens=8192,
+                                                step_token_alignment=align))
     sd = random_state_dict(cfg, wl["arch"], wl["seed"], device="cuda", dtype=torch.bfloat16,
                            include_unused=False)
     worker = MuWorker(ec, "cuda")
@@ -508,7 +509,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     wl = WORKLOADS[args.workload]
     tp = world if args.parallel in ("tp", "ep") else 1
-    engine, worker, ec = build(rank, tp, wl, ep=args.parallel == "ep")
+    engine, worker, ec = build(rank, tp, wl, ep=args.parallel == "ep", align=args.step_align)
     conc, out_tokens = wl["concurrency"], wl["out"]
     # tensor-parallel ranks serve the same requests; replicas serve their own
     # Every engine serves the same seeded request stream (replicas each serve
@@ -659,6 +660,7 @@ def run_ours(args, rank, world, local_rank):
             "steps_pure_decode": sum(1 for b, t, d in steps_meta if d == b),
             "mean_tokens_per_step": float(np.mean([t for _, t, _ in steps_meta])),
             "initial_fill_steps": fill_steps,
+            "step_token_alignment": args.step_align,
         },
         "e2e": {"value": n_all / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(4 * conc), "wall_s": wall_max,
@@ -772,6 +774,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--step-align", type=int, default=0,
+                    help="trim each step's last prefill chunk to a multiple of this many tokens")
     ap.add_argument("--parallel", choices=["replicas", "tp", "ep"], default="replicas",
                     help="N>1: independent replicas (default), one tensor-parallel engine, or "
                          "tensor-parallel attention with expert-parallel experts (Deep)")

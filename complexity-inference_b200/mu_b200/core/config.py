@@ -2,9 +2,11 @@
 
 The dataclasses keep the reference's names, defaults and validation
 (mu_inference/core/config.py:25-345) so existing callers construct them
-unchanged.  Two additions, both optional: ``CacheConfig.num_gpu_blocks``
-(pool size override used by the paged cache) and
-``EngineConfig.max_seq_len_hint`` (sizes decode scratch for graph capture).
+unchanged.  Additions, all optional: ``CacheConfig.num_gpu_blocks``
+(pool size override used by the paged cache),
+``EngineConfig.max_seq_len_hint`` (sizes decode scratch for graph capture),
+``EngineConfig.expert_parallel`` and ``SchedulerConfig.step_token_alignment``
+(tile-aligned step sizes under chunked prefill).
 """
 
 from __future__ import annotations
@@ -180,6 +182,11 @@ class SchedulerConfig:
     preemption_mode: Literal["recompute", "swap"] = "recompute"
     enable_chunked_prefill: bool = True
     max_prefill_tokens: int = 4096
+    # With chunked prefill: trim the step's last prefill chunk so that the
+    # step's token count is a multiple of this (0 = off).  GEMM tiles cover
+    # 128 or 256 rows, so rows past the last full tile cost a whole tile; the
+    # trimmed tokens run first in the next step.  Not in the reference.
+    step_token_alignment: int = 0
     enable_continuous_batching: bool = True
     batch_wait_time_ms: float = 5.0
     min_batch_size: int = 1

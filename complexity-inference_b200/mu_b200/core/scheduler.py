@@ -180,6 +180,15 @@ class MuScheduler:
             out.num_prefill_tokens += take
             prefill_budget -= take
         self._requeue_front(deferred)
+        align = self.config.step_token_alignment
+        if chunked and align > 0 and out.prefill_requests and out.total_tokens > align:
+            # tile-aligned step: the last chunk gives up the rows past the
+            # last full multiple of `align` (it continues next step)
+            extra = out.total_tokens % align
+            start, n = out.prefill_chunks[-1]
+            if 0 < extra < n:
+                out.prefill_chunks[-1] = (start, n - extra)
+                out.num_prefill_tokens -= extra
         if self._should_preempt(out):
             out.preempted_requests = self._preempt_requests(out)
         return out
@@ -235,8 +244,8 @@ class MuScheduler:
         addition, in the reference's own terms.  In order:
 
         1. requests admitted by this ``schedule`` go back to the front of the
-           queue (newest first), while a running request holds blocks that
-           will come free;
+           queue (newest first); the first of them stays when no other
+           request holds blocks;
         2. prefills already under way are preempted (newest first);
         3. decodes are preempted as ``_preempt_requests`` does it (most
            generated tokens first).
@@ -266,7 +275,9 @@ class MuScheduler:
         others_hold = any(held_of(r) > 0 for r in self.running.values())
         deferred: List[Request] = []
         for req in reversed(fresh):
-            if total <= free or not others_hold:
+            # with nothing else in the pool the first admission stays (alone,
+            # it either fits or is rejected by reserve)
+            if total <= free or (not others_hold and req is fresh[0]):
                 break
             drop_prefill(req)
             self.running.pop(req.request_id, None)

@@ -98,13 +98,14 @@ def expected(prompt, max_tokens, stop):
 
 
 def run(overlap, prompts, limits, stop, max_batch, abort=None, monkeypatch=None, budget=64,
-        chunked=True, blocks=64, batched_tokens=64):
+        chunked=True, blocks=64, batched_tokens=64, align=0):
     monkeypatch.setattr(E, "BatchSampler", FakeSampler)
     ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=blocks, max_num_seqs=max_batch),
                       scheduler=SchedulerConfig(max_batch_size=max_batch,
                                                 max_num_batched_tokens=batched_tokens,
                                                 max_prefill_tokens=budget,
-                                                enable_chunked_prefill=chunked))
+                                                enable_chunked_prefill=chunked,
+                                                step_token_alignment=align))
     w = FakeWorker(blocks)
     eng = E.StepEngine(w, ec, overlap=overlap)
     for i, (p, m) in enumerate(zip(prompts, limits)):
@@ -184,8 +185,9 @@ def test_chunked_prefill(overlap, monkeypatch):
 
 
 @pytest.mark.parametrize("overlap", [False, True])
-@pytest.mark.parametrize("chunked", [False, True])
-def test_kv_pool_exhaustion_preempts_and_recomputes(overlap, chunked, monkeypatch):
+@pytest.mark.parametrize("chunked,budget,blocks", [(False, 8, 12), (True, 8, 12), (True, 64, 8),
+                                                   (False, 64, 8)])
+def test_kv_pool_exhaustion_preempts_and_recomputes(overlap, chunked, budget, blocks, monkeypatch):
     """A pool far smaller than the requests' final lengths: admissions wait and
     running requests are preempted (KV freed, prompt + generated tokens
     re-prefilled on readmission) instead of failing; every request still
@@ -193,9 +195,10 @@ def test_kv_pool_exhaustion_preempts_and_recomputes(overlap, chunked, monkeypatc
     rng = np.random.default_rng(5)
     prompts = [rng.integers(0, V, int(L)).tolist() for L in (7, 10, 4, 9, 6, 8)]
     limits = [14, 9, 16, 12, 11, 15]
-    blocks = 12  # 48 token slots; the requests end at 18-26 tokens each
+    # 32-48 token slots; the requests end at 17-23 tokens each; with the
+    # large budget the first step's admissions alone overflow the pool
     eng, w, reported = run(overlap, prompts, limits, [], max_batch=4, monkeypatch=monkeypatch,
-                           budget=8, chunked=chunked, blocks=blocks)
+                           budget=budget, chunked=chunked, blocks=blocks)
     for i, (p, m) in enumerate(zip(prompts, limits)):
         req = eng.requests[f"r{i}"]
         want = expected(p, m, [])
@@ -222,3 +225,24 @@ def test_token_budget_preemption_recomputes(overlap, monkeypatch):
         assert reported[f"r{i}"] == expected(p, m, [])
     assert sum(eng.requests[f"r{i}"].num_preemptions for i in range(len(prompts))) > 0
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_step_token_alignment(overlap, monkeypatch):
+    """Tile-aligned steps: the last prefill chunk is trimmed so that a step
+    with prefill tokens has a multiple of `align` tokens; generation is
+    unchanged."""
+    rng = np.random.default_rng(7)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in (13, 7, 22, 5, 17, 11, 9)]
+    limits = [9, 12, 6, 10, 8, 7, 11]
+    align = 8
+    eng, w, reported = run(overlap, prompts, limits, [], max_batch=4, monkeypatch=monkeypatch,
+                           budget=64, align=align)
+    for i, (p, m) in enumerate(zip(prompts, limits)):
+        assert eng.requests[f"r{i}"].output_token_ids == expected(p, m, [])
+        assert reported[f"r{i}"] == expected(p, m, [])
+    trimmed = [(b, nd, t) for (b, nd), t in zip(w.steps, w.tokens) if b > nd and t > align]
+    assert trimmed and sum(t % align == 0 for _, _, t in trimmed) >= len(trimmed) // 2
+    _, w0, _ = run(overlap, prompts, limits, [], max_batch=4, monkeypatch=monkeypatch, budget=64)
+    assert sum(t % align == 0 for (b, nd), t in zip(w0.steps, w0.tokens) if b > nd and t > align) \
+        < sum(t % align == 0 for _, _, t in trimmed)
