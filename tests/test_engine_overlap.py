@@ -85,6 +85,9 @@ class FakeWorker:
         self.tokens.append(sum(len(s.token_ids) for s in seqs))
         return out, type("B", (), {"token_rows": None, "input_ids": None})()
 
+    def get_stats(self):
+        return {"steps": len(self.steps)}
+
 
 def expected(prompt, max_tokens, stop):
     toks, gen = list(prompt), []
@@ -246,3 +249,52 @@ def test_step_token_alignment(overlap, monkeypatch):
     _, w0, _ = run(overlap, prompts, limits, [], max_batch=4, monkeypatch=monkeypatch, budget=64)
     assert sum(t % align == 0 for (b, nd), t in zip(w0.steps, w0.tokens) if b > nd and t > align) \
         < sum(t % align == 0 for _, _, t in trimmed)
+
+
+def test_public_engines_over_stand_in(monkeypatch):
+    """MuEngine / MuBatchEngine async plumbing (generate, generate_stream,
+    concurrent requests, stats, shutdown) over the stand-in worker."""
+    import asyncio
+
+    from mu_b200 import MuBatchEngine, MuEngine
+
+    monkeypatch.setattr(E, "BatchSampler", FakeSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=4),
+                      scheduler=SchedulerConfig(max_batch_size=3, max_num_batched_tokens=64))
+    prompts = [[1, 2, 3], [4, 5], [6, 7, 8, 9], [10]]
+    sp = lambda m: SamplingParams(temperature=0.0, max_tokens=m)
+
+    async def seq():
+        eng = MuEngine(ec)
+        eng.initialize_from_worker(FakeWorker())
+        a = await eng.generate(prompts[0], sp(5), "a")
+        s = [o async for o in eng.generate_stream(prompts[1], sp(4), "s")]
+        st = eng.get_stats()
+        await eng.shutdown()
+        return a, s, st
+
+    a, s, st = asyncio.run(seq())
+    assert a.token_ids == expected(prompts[0], 5, []) and a.finish_reason == "length"
+    assert a.usage == {"prompt_tokens": 3, "completion_tokens": 5, "total_tokens": 8}
+    assert [o.token_id for o in s] == expected(prompts[1], 4, []) and s[-1].finished
+    assert st["total_requests"] == 2 and st["total_tokens_generated"] == 9
+
+    async def batch():
+        eng = MuBatchEngine(ec)
+        eng.initialize_from_worker(FakeWorker())
+
+        async def stream(i):
+            return [o async for o in eng.generate_stream(prompts[i], sp(6), f"s{i}")]
+
+        outs = await asyncio.gather(*[eng.generate(prompts[i], sp(3 + i), f"b{i}")
+                                      for i in range(3)], stream(3))
+        st = eng.get_stats()
+        await eng.shutdown()
+        return outs, st
+
+    outs, st = asyncio.run(batch())
+    for i in range(3):
+        assert outs[i].token_ids == expected(prompts[i], 3 + i, []), i
+    assert [o.token_id for o in outs[3][:-1]] == expected(prompts[3], 6, [])
+    assert outs[3][-1].finished and outs[3][-1].token_id == -1
+    assert st["total_requests"] == 4 and st["engine_type"] == "continuous_batching"

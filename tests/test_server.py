@@ -83,3 +83,28 @@ def test_chat_template_and_response():
     out = asyncio.run(srv.chat_completion(ChatCompletionRequest(model="tiny", messages=msgs)))
     assert out.object == "chat.completion" and out.choices[0].message.role == "assistant"
     assert out.choices[0].message.content == "abc"
+
+
+def test_http_round_trip():
+    """The same routes over HTTP (FastAPI's test client): JSON bodies in and
+    out, validation errors, 404 for an unknown model, an SSE stream."""
+    pytest.importorskip("httpx")
+    from fastapi.testclient import TestClient
+
+    srv = MuServer(FakeEngine(), "tiny")
+    with TestClient(srv.app) as client:
+        assert client.get("/health").json() == {"status": "healthy", "model": "tiny"}
+        assert client.get("/v1/models/tiny").json()["id"] == "tiny"
+        assert client.get("/v1/models/other").status_code == 404
+        r = client.post("/v1/completions", json={"model": "tiny", "prompt": [1, 2], "max_tokens": 3})
+        assert r.status_code == 200 and r.json()["choices"][0]["token_ids"] == [7, 8, 9]
+        assert client.post("/v1/completions",
+                           json={"model": "tiny", "prompt": "x", "max_tokens": 0}).status_code == 422
+        r = client.post("/v1/chat/completions",
+                        json={"model": "tiny", "messages": [{"role": "user", "content": "hi"}]})
+        assert r.json()["choices"][0]["message"] == {"role": "assistant", "content": "abc"}
+        with client.stream("POST", "/v1/completions",
+                           json={"model": "tiny", "prompt": [1], "stream": True}) as s:
+            lines = [ln for ln in s.iter_lines() if ln]
+        assert lines[-1] == "data: [DONE]" and len(lines) == 4
+        assert client.get("/stats").json()["total_requests"] == 2
