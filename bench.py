@@ -739,6 +739,50 @@ def run_micro(args):
             K.decode_attn(q, out, kc, vc, btd, sl, Hq, Hkv, D, mx, workspace=ws)
         byts = float(ctx.sum()) * Hkv * D * 4
         res.update(seqs=args.seqs, ctx_sum=int(ctx.sum()), algorithmic_bytes=byts)
+    elif args.micro == "prefill_attn":
+        # causal prefill of fresh prompts (no cached prefix), Llama-3-8B heads
+        Hq, Hkv, D = 32, 8, 128
+        lens = [int(x) for x in args.prompts.split(",")]
+        nblk = [(n + 15) // 16 for n in lens]
+        NB = sum(nblk) + 8
+        kc = torch.randn(NB, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+        vc = torch.randn(NB, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+        bt = np.zeros((len(lens), max(nblk)), np.int32)
+        i = 0
+        for b, n in enumerate(nblk):
+            bt[b, :n] = np.arange(i, i + n)
+            i += n
+        btd = torch.from_numpy(bt).cuda()
+        sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device="cuda")
+        q = torch.randn(sum(lens), Hq * D, device="cuda", generator=g).bfloat16()
+        out = torch.empty_like(q)
+
+        def fn():
+            K.prefill_attn(q, out, kc, vc, btd, sl, cu, max(lens), Hq, Hkv, D)
+        byts = float(sum(4.0 * n * (n + 1) / 2 * Hq * D for n in lens))
+        res.update(prompts=lens, flops=byts)
+    elif args.micro == "qkv_rope":
+        # q|k|v projection with RoPE and the paged-KV append in its epilogue,
+        # Llama-3-8B shape (H 4096, 32/8 heads, D 128), M tokens
+        M, Kd, Hq, Hkv, D = args.m, 4096, 32, 8, 128
+        N = (Hq + 2 * Hkv) * D
+        A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
+        B = (torch.randn(N, Kd, device="cuda", generator=g) * 0.02).bfloat16()
+        qo = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        NB = (M + 15) // 16 + 8
+        kc = torch.zeros(NB, Hkv, 16, D, device="cuda", dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        pos = torch.arange(M, device="cuda", dtype=torch.int32)
+        slots = torch.randperm(NB * 16, device="cuda", generator=g)[:M].to(torch.int32)
+        inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+        ang = torch.arange(M + 1, device="cuda").float()[:, None] * inv[None]
+        cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+
+        def fn():
+            K.gemm_qkv_rope(A, B, qo, pos, slots, cos, sin, Hq, Hkv, D, kc, vc)
+        byts = 2.0 * M * N * Kd
+        res.update(M=M, N=N, K=Kd, flops=byts)
     else:
         M, N, Kd = args.m, args.n, args.k
         A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
@@ -752,6 +796,9 @@ def run_micro(args):
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    # a device-side wait keeps the GPU busy while the timed launches queue up,
+    # so the events see kernel time, not the host's launch rate
+    torch.cuda._sleep(20_000_000)
     s.record()
     for _ in range(args.reps):
         fn()
@@ -781,7 +828,8 @@ def main():
                          "tensor-parallel attention with expert-parallel experts (Deep)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3",
                     help="c3 (default, the headline), c2 / c5 (DeepForCausalLM)")
-    ap.add_argument("--micro", choices=["decode_attn", "gemm"], default=None,
+    ap.add_argument("--micro", choices=["decode_attn", "gemm", "prefill_attn", "qkv_rope"],
+                    default=None,
                     help="time one kernel on a small case (for ncu captures)")
     ap.add_argument("--seqs", type=int, default=64)
     ap.add_argument("--ctx-min", type=int, default=256)
@@ -790,6 +838,7 @@ def main():
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--prompts", default="600", help="prefill_attn micro: comma-separated prompt lengths")
     args = ap.parse_args()
     if args.micro:
         return run_micro(args)
