@@ -713,6 +713,9 @@ def run_micro(args):
     torch.cuda.set_device(0)
     g = torch.Generator(device="cuda").manual_seed(3)
     res = {"micro": args.micro}
+    if args.streamk is not None:
+        K.gemm_set_stream_k(args.streamk)
+        res["stream_k_mode"] = args.streamk
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if args.micro == "decode_attn":
         Hq, Hkv, D = 32, 8, 128
@@ -782,7 +785,7 @@ def run_micro(args):
         def fn():
             K.gemm_qkv_rope(A, B, qo, pos, slots, cos, sin, Hq, Hkv, D, kc, vc)
         byts = 2.0 * M * N * Kd
-        res.update(M=M, N=N, K=Kd, flops=byts)
+        res.update(M=M, N=N, K=Kd, flops=byts, plan=K.gemm_plan_info(M, N, Kd, K.MUK_EPI_ROPE_KV))
     else:
         M, N, Kd = args.m, args.n, args.k
         A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
@@ -792,7 +795,7 @@ def run_micro(args):
         def fn():
             K.gemm(A, B, C, K.MUK_EPI_BF16)
         byts = 2.0 * M * N * Kd
-        res.update(M=M, N=N, K=Kd, flops=byts)
+        res.update(M=M, N=N, K=Kd, flops=byts, plan=K.gemm_plan_info(M, N, Kd, K.MUK_EPI_BF16))
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
@@ -839,6 +842,8 @@ def main():
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--prompts", default="600", help="prefill_attn micro: comma-separated prompt lengths")
+    ap.add_argument("--streamk", type=int, choices=[0, 1, 2], default=None,
+                    help="GEMM micro cases: stream-K planning mode (0 off, 1 on, 2 auto)")
     args = ap.parse_args()
     if args.micro:
         return run_micro(args)
