@@ -310,15 +310,23 @@ class MuScheduler:
         out.preempted_requests.extend(preempted)
         return preempted
 
+    def _unqueue(self, request_id: str) -> Optional[Request]:
+        """Take a request out of the waiting queue / priority heap, if there."""
+        req = next((r for r in list(self.waiting) + self.priority_queue
+                    if r.request_id == request_id), None)
+        if req is not None:
+            self.waiting = deque(r for r in self.waiting if r is not req)
+            self.priority_queue = [r for r in self.priority_queue if r is not req]
+            heapq.heapify(self.priority_queue)
+        return req
+
     def finish_request(self, request_id: str, success: bool = True) -> None:
+        # A preempted request is both in `running` (status PREEMPTED, as in the
+        # reference) and back in the queue: take it out of both, or it would
+        # be readmitted after finishing.
         req = self.running.pop(request_id, None)
-        if req is None:  # finished while re-queued after a preemption
-            req = next((r for r in list(self.waiting) + self.priority_queue
-                        if r.request_id == request_id), None)
-            if req is not None:
-                self.waiting = deque(r for r in self.waiting if r is not req)
-                self.priority_queue = [r for r in self.priority_queue if r is not req]
-                heapq.heapify(self.priority_queue)
+        queued = self._unqueue(request_id)
+        req = req or queued
         if req:
             req.status = RequestStatus.FINISHED if success else RequestStatus.FAILED
             req.finish_time = time.time()
@@ -342,14 +350,14 @@ class MuScheduler:
         return self.running.get(request_id) or self.finished.get(request_id)
 
     def abort_request(self, request_id: str) -> None:
-        if request_id in self.running:
-            req = self.running.pop(request_id)
+        # Unlike the reference (scheduler.py:345-359), which returns after
+        # popping a running request, also drop it from the queue: a preempted
+        # request is in both.
+        req = self.running.pop(request_id, None)
+        self._unqueue(request_id)
+        if req is not None:
             req.status = RequestStatus.FAILED
             self.finished[request_id] = req
-            return
-        self.waiting = deque(r for r in self.waiting if r.request_id != request_id)
-        self.priority_queue = [r for r in self.priority_queue if r.request_id != request_id]
-        heapq.heapify(self.priority_queue)
 
     def has_unfinished(self) -> bool:
         return bool(self.waiting or self.priority_queue or self.running)

@@ -298,3 +298,63 @@ def test_public_engines_over_stand_in(monkeypatch):
     assert [o.token_id for o in outs[3][:-1]] == expected(prompts[3], 6, [])
     assert outs[3][-1].finished and outs[3][-1].token_id == -1
     assert st["total_requests"] == 4 and st["engine_type"] == "continuous_batching"
+
+
+@pytest.mark.parametrize("seed", list(range(12)) + [75])
+def test_engine_fuzz(seed, monkeypatch):
+    """Random workloads through the whole host path: arrivals mid-run, aborts,
+    stop tokens, chunked or whole prefills, small KV pools (preemption),
+    tile-aligned steps, overlap on or off.  Every request that is not aborted
+    must generate exactly its sequential tokens, and every block and bitmap
+    row must come back."""
+    rng = np.random.default_rng(100 + seed)
+    overlap = bool(seed % 2)
+    chunked = seed % 3 != 0
+    n = int(rng.integers(4, 14))
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in rng.integers(1, 30, n)]
+    limits = [int(m) for m in rng.integers(1, 20, n)]
+    stop = [int(s) for s in rng.integers(0, V, int(rng.integers(0, 3)))]
+    max_batch = int(rng.integers(2, 7))
+    budget = int(rng.integers(4, 40))
+    longest = max(len(p) + m for p, m in zip(prompts, limits))
+    blocks = max(-(-longest // 4) + 1, int(rng.integers(6, 40)))
+    align = int(rng.choice([0, 0, 4, 8]))
+    policy = "priority" if seed % 5 == 4 else "fcfs"
+    # a token budget below the batch size makes the reference's own
+    # preemption (most advanced decodes back to the queue) fire too
+    batched = int(rng.choice([64, 64, max(1, max_batch - 1)]))
+    monkeypatch.setattr(E, "BatchSampler", FakeSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=blocks, max_num_seqs=max_batch),
+                      scheduler=SchedulerConfig(max_batch_size=max_batch,
+                                                max_num_batched_tokens=batched,
+                                                max_prefill_tokens=budget, policy=policy,
+                                                enable_chunked_prefill=chunked,
+                                                step_token_alignment=align))
+    w = FakeWorker(blocks)
+    eng = E.StepEngine(w, ec, overlap=overlap)
+    arrive = sorted(int(x) for x in rng.integers(0, 15, n))
+    aborts = {int(rng.integers(0, n)): int(rng.integers(1, 25)) for _ in range(int(rng.integers(0, 3)))}
+    reported = {f"r{i}": [] for i in range(n)}
+    added, step, aborted = 0, 0, set()
+    while added < n or eng.has_unfinished():
+        while added < n and arrive[added] <= step:
+            eng.add_request(prompts[added], SamplingParams(temperature=0.0, max_tokens=limits[added],
+                                                           stop_token_ids=stop), f"r{added}")
+            added += 1
+        for o in eng.step():
+            reported[o.request_id].append(o.token_id)
+        step += 1
+        for i, at in aborts.items():
+            if at == step and i < added and f"r{i}" in eng.requests:
+                eng.abort_request(f"r{i}")
+                aborted.add(i)
+        assert step < 2000
+    for i in range(n):
+        if i in aborted:
+            continue
+        want = expected(prompts[i], limits[i], stop)
+        req = eng.requests[f"r{i}"]
+        assert req.output_token_ids == want, (seed, i)
+        assert reported[f"r{i}"] == want, (seed, i)
+    assert not w.active_requests and len(w.cache.free_blocks) == blocks
+    assert not eng.sampler.row_of and not eng._closing and eng._inflight is None

@@ -207,6 +207,30 @@ def test_scheduler_fit_blocks_order():
     assert [r.request_id for r in out.prefill_requests] == ["huge"]
 
 
+def test_scheduler_finish_and_abort_of_preempted_requests():
+    """A preempted request sits in `running` (status PREEMPTED, as in the
+    reference) and back in the queue; finishing or aborting it must take it
+    out of both, or it is readmitted later."""
+    for how in ("finish", "abort"):
+        sc = MuScheduler(SchedulerConfig(max_batch_size=8, max_num_batched_tokens=2,
+                                         max_prefill_tokens=8))
+        for i in range(3):
+            q = Request(request_id=f"d{i}", num_prompt_tokens=1, num_generated_tokens=i)
+            q.status = RequestStatus.DECODE
+            sc.running[q.request_id] = q
+        o = sc.schedule()
+        assert [r.request_id for r in o.preempted_requests] == ["d2"]
+        assert "d2" in sc.running and sc.waiting[0].request_id == "d2"
+        if how == "finish":
+            sc.finish_request("d2")
+        else:
+            sc.abort_request("d2")
+        assert "d2" not in sc.running and all(r.request_id != "d2" for r in sc.waiting)
+        assert sc.finished["d2"].is_finished
+        o = sc.schedule()
+        assert "d2" not in {r.request_id for r in o.prefill_requests + o.decode_requests}
+
+
 def test_sampling_params_validation():
     SamplingParams(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0)
     for kw in ({"temperature": -1}, {"top_k": -1}, {"top_p": 0.0}, {"top_p": 1.5},
