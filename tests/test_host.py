@@ -118,6 +118,51 @@ def test_step_packer_layout():
     assert p.generation > g and b2.num_tokens == 100 and b2.block_tables.shape[1] >= 7
 
 
+def test_step_packer_randomised():
+    """Packed arrays against a per-sequence loop over random steps (decodes
+    first, ragged prefills, buffer growth, both staging buffers)."""
+    rng = np.random.default_rng(11)
+    p = StepPacker("cpu", 16, 2, 2)
+    for trial in range(60):
+        B = int(rng.integers(1, 12))
+        nd = int(rng.integers(0, B + 1))
+        seqs = []
+        for i in range(B):
+            q = 1 if i < nd else int(rng.integers(1, 40))
+            start = int(rng.integers(0, 200))
+            nb = (start + q + 15) // 16
+            seqs.append(SeqWork(f"s{i}", rng.integers(0, 1000, q).astype(np.int32), start,
+                                rng.integers(0, 5000, q).astype(np.int32),
+                                rng.integers(0, 9000, nb).tolist(),
+                                int(rng.integers(-1, 50)) if i < nd else -1, int(rng.integers(0, 64))))
+        b = p.pack(seqs, nd)
+        ids, pos, slots, rows, cu, last = [], [], [], [], [0], []
+        for s_ in seqs:
+            n = len(s_.token_ids)
+            ids += s_.token_ids.tolist()
+            pos += list(range(s_.start_pos, s_.start_pos + n))
+            slots += s_.slots.tolist()
+            rows += [s_.row] * n
+            cu.append(cu[-1] + n)
+            last.append(cu[-1] - 1)
+        assert b.num_tokens == cu[-1] and b.num_seqs == B and b.num_decode == nd
+        assert b.input_ids.tolist() == ids and b.positions.tolist() == pos
+        assert b.slot_mapping.tolist() == slots and b.token_rows.tolist() == rows
+        assert b.cu_seqlens_q.tolist() == cu and b.last_token_idx.tolist() == last
+        assert b.seq_lens.tolist() == [s_.start_pos + len(s_.token_ids) for s_ in seqs]
+        assert b.prefill_cu.tolist() == [c - cu[nd] for c in cu[nd:]]
+        assert b.decode_src.tolist() == [s_.src for s_ in seqs]
+        assert b.max_q_len == (max(len(s_.token_ids) for s_ in seqs[nd:]) if B > nd else 0)
+        maxb = max(len(s_.block_table) for s_ in seqs)
+        for i, s_ in enumerate(seqs):
+            n = len(s_.block_table)
+            assert b.block_tables[i, :n].tolist() == s_.block_table
+            # padded to the step's widest table with block 0 (kernels read
+            # only a sequence's own blocks; columns past the step's width
+            # are never read)
+            assert int(b.block_tables[i, n:maxb].abs().sum()) == 0
+
+
 def test_scheduler_order_budget_and_preemption():
     sc = MuScheduler(SchedulerConfig(max_batch_size=3, max_num_batched_tokens=10,
                                      max_prefill_tokens=8, enable_chunked_prefill=False))
