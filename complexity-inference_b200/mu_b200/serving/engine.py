@@ -325,6 +325,7 @@ class MuEngine:
         self.scheduler = None
         self._initialized = False
         self._lock = asyncio.Lock()
+        self._sync_loop: Optional[asyncio.AbstractEventLoop] = None
         self.stats = {"total_requests": 0, "total_tokens_generated": 0, "start_time": None}
 
     async def initialize(self, model_path: Optional[str] = None) -> None:
@@ -357,8 +358,18 @@ class MuEngine:
 
     def generate_sync(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
                       request_id: Optional[str] = None) -> GenerationOutput:
-        return asyncio.get_event_loop().run_until_complete(
-            self.generate(prompt, sampling_params, request_id))
+        """Blocking generate (engine.py:131-150).  Runs on an event loop the
+        engine keeps for its synchronous calls (the reference takes the
+        thread's default loop, which newer Pythons no longer create)."""
+        try:
+            asyncio.get_running_loop()
+        except RuntimeError:
+            pass
+        else:
+            raise RuntimeError("generate_sync called inside a running event loop; await generate()")
+        if self._sync_loop is None or self._sync_loop.is_closed():
+            self._sync_loop = asyncio.new_event_loop()
+        return self._sync_loop.run_until_complete(self.generate(prompt, sampling_params, request_id))
 
     async def generate(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
                        request_id: Optional[str] = None) -> GenerationOutput:
@@ -437,9 +448,17 @@ class MuBatchEngine(MuEngine):
         super()._make_core()
         self._running = True
         try:
-            self._task = asyncio.get_event_loop().create_task(self._loop())
-        except RuntimeError:
+            self._task = asyncio.get_running_loop().create_task(self._loop())
+        except RuntimeError:  # no loop running: started by the first request
             self._task = None
+
+    def _ensure_task(self) -> None:
+        """Run the batching loop on the caller's event loop (a task left on
+        a loop that has since closed is replaced)."""
+        loop = asyncio.get_running_loop()
+        if self._task is None or self._task.done() or self._task.get_loop() is not loop:
+            self._running = True
+            self._task = loop.create_task(self._loop())
 
     async def _loop(self) -> None:
         while self._running:
@@ -481,11 +500,10 @@ class MuBatchEngine(MuEngine):
     async def generate(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
                        request_id: Optional[str] = None) -> GenerationOutput:
         self._check()
-        if self._task is None:
-            self._task = asyncio.get_event_loop().create_task(self._loop())
+        self._ensure_task()
         ids = _encode(self.tokenizer, prompt)
         rid = self.core.add_request(ids, sampling_params or SamplingParams(), request_id)
-        fut = asyncio.get_event_loop().create_future()
+        fut = asyncio.get_running_loop().create_future()
         self._futures[rid] = fut
         self._prompt_len[rid] = len(ids)
         return await fut
@@ -493,8 +511,7 @@ class MuBatchEngine(MuEngine):
     async def generate_stream(self, prompt: Prompt, sampling_params: Optional[SamplingParams] = None,
                               request_id: Optional[str] = None) -> AsyncIterator[StreamOutput]:
         self._check()
-        if self._task is None:
-            self._task = asyncio.get_event_loop().create_task(self._loop())
+        self._ensure_task()
         ids = _encode(self.tokenizer, prompt)
         q: asyncio.Queue = asyncio.Queue()
         rid = self.core.add_request(ids, sampling_params or SamplingParams(), request_id)

@@ -358,3 +358,32 @@ def test_engine_fuzz(seed, monkeypatch):
         assert reported[f"r{i}"] == want, (seed, i)
     assert not w.active_requests and len(w.cache.free_blocks) == blocks
     assert not eng.sampler.row_of and not eng._closing and eng._inflight is None
+
+
+def test_engines_across_event_loops(monkeypatch):
+    """generate_sync from plain code (twice), and MuBatchEngine requests from
+    two successive asyncio.run loops: the batching task follows the loop."""
+    import asyncio
+
+    from mu_b200 import MuBatchEngine, MuEngine
+
+    monkeypatch.setattr(E, "BatchSampler", FakeSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=4),
+                      scheduler=SchedulerConfig(max_batch_size=3, max_num_batched_tokens=64))
+    sp = SamplingParams(temperature=0.0, max_tokens=4)
+    eng = MuEngine(ec)
+    eng.initialize_from_worker(FakeWorker())
+    assert eng.generate_sync([1, 2, 3], sp).token_ids == expected([1, 2, 3], 4, [])
+    assert eng.generate_sync([4, 5], sp).token_ids == expected([4, 5], 4, [])
+
+    async def inside():
+        with pytest.raises(RuntimeError):
+            eng.generate_sync([1], sp)
+    asyncio.run(inside())
+
+    beng = MuBatchEngine(ec)
+    beng.initialize_from_worker(FakeWorker())   # no loop running yet
+    for prompt in ([7, 8], [9, 10, 11]):
+        out = asyncio.run(beng.generate(prompt, sp))
+        assert out.token_ids == expected(prompt, 4, [])
+    asyncio.run(beng.shutdown())
