@@ -125,6 +125,9 @@ class StepEngine:
         self.overlap = overlap
         self.requests: Dict[str, Request] = {}
         self.num_steps = 0
+        self.num_step_tokens = 0     # tokens run (prefill + decode) over all steps
+        self.num_decode_tokens = 0
+        self._t0 = time.time()
         self._inflight: Optional[_Launched] = None
         self._closing: set = set()   # last token in flight and length limit reached
 
@@ -146,6 +149,16 @@ class StepEngine:
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_unfinished() or self._inflight is not None
+
+    def get_stats(self) -> Dict:
+        """Step counters: steps launched, tokens per step, and rates over the
+        engine's lifetime (host wall clock)."""
+        up = max(time.time() - self._t0, 1e-9)
+        n = max(self.num_steps, 1)
+        return {"steps": self.num_steps, "tokens_per_step": self.num_step_tokens / n,
+                "decode_tokens_per_step": self.num_decode_tokens / n,
+                "step_tokens_per_second": self.num_step_tokens / up,
+                "steps_per_second": self.num_steps / up}
 
     def _release(self, rid: str) -> None:
         if rid in self.worker.active_requests:
@@ -243,6 +256,8 @@ class StepEngine:
                                      [r.num_generated_tokens for r in reqs],
                                      batch.token_rows, batch.input_ids, T)
         self.num_steps += 1
+        self.num_step_tokens += T
+        self.num_decode_tokens += nd
         idx = []
         for s, req in zip(seqs, reqs):
             if not final.get(req.request_id, True):
@@ -525,10 +540,18 @@ class MuBatchEngine(MuEngine):
 
     def get_stats(self) -> Dict:
         s = super().get_stats()
+        sched = self.core.scheduler if self.core else None
         s.update({"engine_type": "continuous_batching",
                   "batches_processed": self.stats["batches_processed"],
                   "avg_batch_size": round(self.stats["avg_batch_size"], 2),
-                  "scheduler": self.core.scheduler.get_stats() if self.core else {}})
+                  "pending_requests": (len(sched.waiting) + len(sched.priority_queue)) if sched else 0,
+                  "active_requests": len(sched.running) if sched else 0,
+                  "continuous_batching": {
+                      "enabled": self.config.scheduler.enable_continuous_batching,
+                      "batch_wait_time_ms": self.config.scheduler.batch_wait_time_ms,
+                      "max_batch_size": self.config.scheduler.max_batch_size},
+                  "scheduler": sched.get_stats() if sched else {},
+                  "steps": self.core.get_stats() if self.core else {}})
         return s
 
     async def shutdown(self) -> None:

@@ -298,6 +298,11 @@ def test_public_engines_over_stand_in(monkeypatch):
     assert [o.token_id for o in outs[3][:-1]] == expected(prompts[3], 6, [])
     assert outs[3][-1].finished and outs[3][-1].token_id == -1
     assert st["total_requests"] == 4 and st["engine_type"] == "continuous_batching"
+    # the reference's keys (engine.py:802-823) plus step counters
+    for key in ("batches_processed", "avg_batch_size", "uptime_seconds", "tokens_per_second",
+                "pending_requests", "active_requests", "worker", "continuous_batching"):
+        assert key in st, key
+    assert st["steps"]["steps"] > 0 and st["steps"]["tokens_per_step"] > 0
 
 
 @pytest.mark.parametrize("seed", list(range(12)) + [75])
