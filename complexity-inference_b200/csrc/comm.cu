@@ -45,7 +45,8 @@ constexpr int kFlagB = kArFlagB;          // [kMaxRanks] "done" epochs, by sourc
 constexpr int kFlagEpoch = kArFlagEpoch;
 constexpr int kFlagArrive1 = kArFlagArrive1;
 constexpr int kFlagArrive2 = kArFlagArrive2;
-constexpr uint64_t kPeerTimeoutNs = 5ull * 1000 * 1000 * 1000;  // 5 s
+// Bound of every cross-GPU wait, per device (muk_set_peer_timeout_ms).
+__device__ uint64_t g_peer_timeout_ns = 5ull * 1000 * 1000 * 1000;  // 5 s
 
 struct ArArgs {
   float4* data[kMaxRanks];     // each rank's data range (as mapped here)
@@ -91,9 +92,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // Wait until flags[base + s] >= epoch for every rank s (bounded).
 __device__ bool wait_all(const uint32_t* flags, int base, int world, uint32_t epoch) {
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = g_peer_timeout_ns;
   for (int s = 0; s < world; ++s) {
     while ((int32_t)(ld_acquire_sys(flags + base + s) - epoch) < 0) {
-      if (globaltimer() - t0 > kPeerTimeoutNs) {
+      if (globaltimer() - t0 > limit) {
         set_device_error(kDevTimeoutPeer);
         return false;
       }
@@ -278,6 +280,14 @@ extern "C" int64_t muk_allreduce_scratch_elems(int64_t n, int world) {
   if (n < 0 || world < 1) return 0;
   const int64_t n4 = (n + 3) / 4;
   return ((n4 + world - 1) / world) * world * 4;
+}
+
+extern "C" int muk_set_peer_timeout_ms(int ms) {
+  MUK_REQUIRE(ms >= 1 && ms <= 600000, "muk_set_peer_timeout_ms: %d ms (1 .. 600000)", ms);
+  const uint64_t ns = (uint64_t)ms * 1000000ull;
+  if (cudaMemcpyToSymbol(g_peer_timeout_ns, &ns, sizeof(ns)) != cudaSuccess)
+    return check_launch("muk_set_peer_timeout_ms");
+  return MUK_OK;
 }
 
 extern "C" int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags,

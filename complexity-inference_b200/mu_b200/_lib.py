@@ -61,6 +61,7 @@ SIGNATURES = {
                                   c_int, _P]),
     "muk_gemm_plan_info": (c_int, [c_int, c_int, c_int, c_int, c_int, _P]),
     "muk_gemm_set_stream_k": (c_int, [c_int]),
+    "muk_set_peer_timeout_ms": (c_int, [c_int]),
     "muk_ipc_get_handle": (c_int, [_P, _P, POINTER(c_uint64)]),
     "muk_ipc_open_handle": (c_int, [_P, c_uint64, POINTER(c_void_p), POINTER(c_void_p)]),
     "muk_ipc_close_handle": (c_int, [_P]),

@@ -280,6 +280,11 @@ def gemm_plan_info(M: int, N: int, K: int, epilogue: int, split_k: int = 1) -> d
     return dict(zip(keys, list(out)))
 
 
+def set_peer_timeout_ms(ms: int) -> None:
+    """Bound of the collectives' cross-GPU waits on the current device."""
+    call("muk_set_peer_timeout_ms", int(ms))
+
+
 def gemm_set_stream_k(mode: int) -> int:
     """GEMM stream-K planning mode (0 off, 1 on, 2 auto = only for launches
     that would leave most SMs idle); returns the previous mode."""

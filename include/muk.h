@@ -337,12 +337,19 @@ int64_t muk_allreduce_scratch_elems(int64_t n, int world);
  * rank order 0..world-1 from local memory and stores the sum into every
  * rank's data; a second barrier ends the call.  Every rank ends with
  * bit-identical sums.  All ranks must make the same sequence of calls (same
- * n, same order).  Waits are bounded (5 s; then the device error word reads
- * 6 and the result is undefined).  Replaces the NCCL all-reduce after the
+ * n, same order).  Waits are bounded (5 s by default, see
+ * muk_set_peer_timeout_ms; then the device error word reads 6 and the result
+ * is undefined).  Replaces the NCCL all-reduce after the
  * row-parallel projections; graph-capturable (the barrier epoch lives in the
  * flag area).  Launches two kernels. */
 int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags, int rank,
                       int world, int64_t n, int slices, int64_t slice_stride, void* stream);
+
+/* Bound of every cross-GPU wait of the collectives on the current device, in
+ * ms (1 .. 600000; default 5000).  A wait that runs out records device error
+ * 6 (muk_device_error) and its kernel returns, leaving the context usable.
+ * No counterpart in the reference (it has no collectives). */
+int muk_set_peer_timeout_ms(int ms);
 
 /* f32 scratch elements per rank that muk_gemm_allreduce_f32 needs. */
 int64_t muk_gemm_allreduce_scratch_elems(int M, int N, int world);
