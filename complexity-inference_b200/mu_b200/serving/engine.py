@@ -185,6 +185,27 @@ class StepEngine:
             results += self._complete(prev)
         return results
 
+    def _fail_step(self, launched: _Launched, err: Exception) -> List[StepOutput]:
+        """A step whose results cannot be read: every request in it finishes
+        with "error" (blocks and bitmap rows freed), as the reference maps a
+        failed forward to WorkerOutput.error -> finish_reason "error"
+        (worker.py:179-206, engine.py:210-212).  Requests not in the step go
+        on."""
+        logger.error("step failed: %s", err)
+        results: List[StepOutput] = []
+        seen = set()
+        for req in launched.reqs:
+            rid = req.request_id
+            if rid in seen or req.is_finished or self.requests.get(rid) is not req:
+                continue
+            seen.add(rid)
+            while req.output_token_ids and req.output_token_ids[-1] == -1:  # pending tokens
+                req.output_token_ids.pop()
+                req.num_generated_tokens -= 1
+            self._finish(req, "error", success=False)
+            results.append(StepOutput(rid, -1, True, "error"))
+        return results
+
     def flush(self) -> List[StepOutput]:
         """Wait for the step in flight, if any, and return its outputs."""
         prev, self._inflight = self._inflight, None
@@ -278,7 +299,10 @@ class StepEngine:
         return _Launched(reqs, idx, rows, handle)
 
     def _complete(self, launched: _Launched) -> List[StepOutput]:
-        toks = launched.handle.wait()
+        try:
+            toks = launched.handle.wait()
+        except Exception as e:  # noqa: BLE001 - a failed step fails its requests, not the engine
+            return self._fail_step(launched, e)
         results: List[StepOutput] = []
         eos = self.eos_token_id
         for req, i, tok in zip(launched.reqs, launched.idx, toks):

@@ -392,3 +392,44 @@ def test_engines_across_event_loops(monkeypatch):
         out = asyncio.run(beng.generate(prompt, sp))
         assert out.token_ids == expected(prompt, 4, [])
     asyncio.run(beng.shutdown())
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_failed_step_fails_its_requests(overlap, monkeypatch):
+    """A step whose sampled tokens cannot be read (a device error surfacing
+    at the read) finishes the requests in it with "error" and frees their
+    blocks; requests admitted later still generate their tokens."""
+    state = {"launch": 0}
+
+    class FailingSampler(FakeSampler):
+        def launch(self, logits, ids, params, steps, token_rows=None, input_ids=None,
+                   num_tokens=0):
+            state["launch"] += 1
+            h = _Handle(logits)
+            if state["launch"] == 3:
+                def boom():
+                    raise RuntimeError("device error 6")
+                h.wait = boom
+            return h
+
+    monkeypatch.setattr(E, "BatchSampler", FailingSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=2),
+                      scheduler=SchedulerConfig(max_batch_size=2, max_num_batched_tokens=64))
+    w = FakeWorker()
+    eng = E.StepEngine(w, ec, overlap=overlap)
+    prompts = [[1, 2, 3], [4, 5], [6, 7, 8, 9]]
+    for i, p in enumerate(prompts):
+        eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=6), f"r{i}")
+    reasons = {}
+    while eng.has_unfinished():
+        for o in eng.step():
+            if o.finished:
+                reasons[o.request_id] = o.finish_reason
+    assert reasons["r0"] == "error" and reasons["r1"] == "error"
+    assert reasons["r2"] == "length"
+    assert eng.requests["r2"].output_token_ids == expected(prompts[2], 6, [])
+    for rid in ("r0", "r1"):
+        toks = eng.requests[rid].output_token_ids
+        assert -1 not in toks and toks == expected(prompts[int(rid[1])], 6, [])[:len(toks)]
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+    assert not eng.sampler.row_of and not eng._closing
