@@ -151,6 +151,54 @@ def test_tp2_matches_unsharded(name, ep):
     assert np.array_equal(got[0], got[1])  # every rank holds the same logits
 
 
+def _dying_worker(rank, world, port, q):
+    """Rank 1 fails (an exception, then the process exits) before its first
+    all-reduce; rank 0 runs the sharded forward and must see its next
+    collective end with an error, not wait forever."""
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "injected failure"))
+        q.close()
+        q.join_thread()  # flush the message before the abrupt exit
+        os._exit(3)  # dies without leaving the group
+    shape, cfg, sd, d, prompts = load_tiny("llama_tiny")
+    shard, local = shard_state_dict(sd, cfg, shape.arch, rank, world)
+    lshape = O.ModelShape(shape.arch, shape.hidden, shape.layers, local.num_attention_heads,
+                          local.num_key_value_heads, shape.head_dim, shape.vocab)
+    model = O.OracleModel(lshape, {k: v.numpy() for k, v in shard.items()}, O.MuCfg(True))
+    t0 = time.time()
+    try:
+        _tp_forward(model, prompts[0])
+        q.put((rank, ("no error", time.time() - t0)))
+    except Exception as e:  # noqa: BLE001 - the collective's failure is the result
+        q.put((rank, ("error", time.time() - t0, type(e).__name__)))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_death_ends_the_peers_collective():
+    """Failure detection on the host: a rank that dies between steps makes
+    the survivor's next all-reduce fail within the process-group timeout."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1] == "injected failure" and procs[1].exitcode == 3
+    assert got[0][0] == "error", got[0]
+    assert got[0][1] < 60.0, got[0]
+
+
 @pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
 def test_shards_recombine(name):
     shape, cfg, sd, d, prompts = load_tiny(name)
