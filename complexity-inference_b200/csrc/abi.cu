@@ -32,6 +32,21 @@ extern "C" int muk_version(void) { return 1; }
 
 extern "C" const char* muk_last_error(void) { return muk::t_last_error; }
 
+extern "C" int muk_device_error_async(int* dst, void* stream) {
+  if (dst == nullptr) {
+    muk::set_last_error("muk_device_error_async: dst is NULL");
+    return MUK_ERR_INVALID_ARG;
+  }
+  cudaError_t e = cudaMemcpyFromSymbolAsync(dst, muk::g_device_error, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost,
+                                            reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    muk::set_last_error("muk_device_error_async: %s", cudaGetErrorString(e));
+    return MUK_ERR_CUDA;
+  }
+  return MUK_OK;
+}
+
 extern "C" int muk_device_error(int* code) {
   if (code == nullptr) {
     muk::set_last_error("muk_device_error: code is NULL");

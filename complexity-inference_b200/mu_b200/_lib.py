@@ -34,6 +34,7 @@ SIGNATURES = {
     "muk_version": (c_int, []),
     "muk_last_error": (c_char_p, []),
     "muk_device_error": (c_int, [POINTER(c_int)]),
+    "muk_device_error_async": (c_int, [_P, _P]),
     "muk_embed": (c_int, [_P, _P, c_int64, _P, c_int, c_int, c_int, c_int, c_float, c_float,
                           c_float, _P]),
     "muk_residual_rmsnorm": (c_int, [_P, _P, c_int64, c_int64, c_int, _P, _P, c_float, _P,
@@ -132,6 +133,15 @@ class MukError(RuntimeError):
     def __init__(self, name: str, code: int, message: str):
         super().__init__(f"{name} failed ({code}): {message}")
         self.code = code
+
+
+class DeviceError(MukError):
+    """A kernel recorded a device-side error (time-out, bad index, shape);
+    ``device_code`` is the error word (see common.cuh)."""
+
+    def __init__(self, device_code: int, where: str = "step"):
+        super().__init__(where, MUK_ERR_DEVICE, f"device error word {device_code}")
+        self.device_code = device_code
 
 
 def load() -> ctypes.CDLL:

@@ -282,7 +282,7 @@ def gemm_plan_info(M: int, N: int, K: int, epilogue: int, split_k: int = 1) -> d
 
 def set_peer_timeout_ms(ms: int) -> None:
     """Bound of the collectives' cross-GPU waits on the current device."""
-    call("muk_set_peer_timeout_ms", int(ms))
+    _lib.call_status("muk_set_peer_timeout_ms", int(ms))
 
 
 def gemm_set_stream_k(mode: int) -> int:

@@ -29,6 +29,7 @@ from typing import AsyncIterator, Dict, List, Optional, Sequence, Union
 import numpy as np
 import torch
 
+from .. import _lib
 from ..core.config import EngineConfig, SamplingParams
 from ..core.scheduler import MuScheduler, Request, RequestStatus
 from ..utils.sampling import BatchSampler, SampleHandle
@@ -192,6 +193,9 @@ class StepEngine:
         (worker.py:179-206, engine.py:210-212).  Requests not in the step go
         on."""
         logger.error("step failed: %s", err)
+        if isinstance(err, _lib.DeviceError):
+            # read and clear the word (synchronises) so later steps start clean
+            _lib.device_error()
         results: List[StepOutput] = []
         seen = set()
         for req in launched.reqs:

@@ -20,6 +20,7 @@ import zlib
 import numpy as np
 import torch
 
+from .. import _lib
 from .. import kernels as K
 from ..core.config import SamplingParams
 
@@ -27,16 +28,24 @@ from ..core.config import SamplingParams
 class SampleHandle:
     """Tokens of one launched sampling step: ``dev`` (int32 on the device,
     valid for the next step's inputs) and a pinned host copy that is ready
-    once ``event`` has completed."""
+    once ``event`` has completed.  ``err`` (pinned, optional) receives the
+    device error word as of the end of the step; ``wait`` raises
+    :class:`~mu_b200._lib.DeviceError` when it is set, so a device-side
+    time-out or bad index fails the step instead of returning its tokens."""
 
-    __slots__ = ("dev", "host", "event")
+    __slots__ = ("dev", "host", "event", "err")
 
-    def __init__(self, dev: torch.Tensor, host: torch.Tensor, event):
-        self.dev, self.host, self.event = dev, host, event
+    def __init__(self, dev: torch.Tensor, host: torch.Tensor, event,
+                 err: Optional[torch.Tensor] = None):
+        self.dev, self.host, self.event, self.err = dev, host, event, err
 
     def wait(self) -> List[int]:
         if self.event is not None:
             self.event.synchronize()
+        if self.err is not None:
+            code = int(self.err[0])
+            if code:
+                raise _lib.DeviceError(code, "sampled step")
         return self.host.tolist()
 
 
@@ -68,6 +77,7 @@ class BatchSampler:
                         for _ in range(2)]
         self._blob_ev: List[Optional[torch.cuda.Event]] = [None, None]
         self._out_h = [torch.zeros(n, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._err_h = [torch.zeros(4, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self._cur = 0
         self._blob_d = torch.zeros(self._WORDS * n, dtype=torch.int32, device=self.device)
         d = self._blob_d
@@ -146,10 +156,12 @@ class BatchSampler:
                  self.d_seed, self.d_off, self.d_out, num_rows=B, seen_rows=self.d_rows)
         host = self._out_h[k][:B]
         host.copy_(self.d_out[:B], non_blocking=True)
+        err = self._err_h[k]
+        _lib.call_status("muk_device_error_async", err.data_ptr(), stream.cuda_stream)
         done = torch.cuda.Event()
         done.record(stream)
         self._cur ^= 1
-        return SampleHandle(self.d_out[:B], host, done)
+        return SampleHandle(self.d_out[:B], host, done, err)
 
     def sample(self, logits: torch.Tensor, request_ids: Sequence[str],
                params: Sequence[SamplingParams], steps: Sequence[int],

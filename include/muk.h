@@ -54,8 +54,14 @@ int muk_version(void);
 const char* muk_last_error(void);
 /* Reads and clears the device-side error word of the current device.
  * *code receives 0 (none) or a kernel error code (1-3 time-out, 4 shape,
- * 5 index).  Synchronises the device. */
+ * 5 index, 6 cross-GPU time-out).  Synchronises the device. */
 int muk_device_error(int* code);
+/* Enqueues on `stream` a copy of the current device's error word (not
+ * cleared) into *dst, pinned host memory: once the stream has passed this
+ * point, *dst holds 0 or the code of a device-side error recorded by any
+ * kernel before it.  No synchronisation; the serving loop reads it with each
+ * step's sampled tokens. */
+int muk_device_error_async(int* dst, void* stream);
 
 /* ---- K6: embedding, RMSNorm, residual reduction -------------------------- */
 

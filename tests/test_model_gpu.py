@@ -235,6 +235,54 @@ def test_engine_kv_pool_exhaustion(cuda, name):
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
 
 
+def test_device_error_fails_the_step_not_the_engine(cuda):
+    """A device-side error recorded during a step (here: an out-of-range token
+    id given to the embedding kernel, which records it and writes zeros)
+    reaches the host with that step's sampled tokens: the requests in the
+    step finish with "error", the word is cleared, and a request submitted
+    afterwards generates the reference's greedy tokens."""
+    import ctypes
+
+    from mu_b200 import _lib
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    toks = np.load(__import__("golden_models").G / "llama_tiny.npz")["tokens"]
+    n = toks.shape[1]
+    w, shape, d, prompts, ec = _worker("llama_tiny", cuda, graphs=True, max_batch=4)
+    eng = StepEngine(w, ec, overlap=True)
+    sp = SamplingParams(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0, max_tokens=n)
+    for r in range(2):
+        eng.add_request(prompts[r], sp, f"r{r}")
+    reasons = {}
+
+    def run(k):
+        for _ in range(k):
+            for o in eng.step():
+                if o.finished:
+                    reasons[o.request_id] = o.finish_reason
+
+    run(2)
+    bad = torch.tensor([1 << 20], dtype=torch.int32, device=cuda)
+    table = torch.zeros(8, 64, dtype=torch.bfloat16, device=cuda)
+    resid = torch.zeros(1, 64, dtype=torch.float32, device=cuda)
+    _lib.call("muk_embed", bad.data_ptr(), table.data_ptr(), 64, resid.data_ptr(), 1, 64, 8, 0,
+              0.0, -10.0, 10.0, torch.cuda.current_stream().cuda_stream)
+    run(3)
+    assert reasons.get("r0") == "error" and reasons.get("r1") == "error", reasons
+    eng.add_request(prompts[2], sp, "r2")
+    while eng.has_unfinished():
+        run(1)
+    assert reasons["r2"] == "length"
+    got = eng.requests["r2"].output_token_ids
+    for i, t in enumerate(got):
+        if t != int(toks[2, i]):
+            assert d["top2_gap"][2, i] <= GAP_TOL, (i, t, int(toks[2, i]))
+            break
+    assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("graphs", [False, True])
 def test_native_executor_matches_python_step(cuda, graphs):
     """muk_llama_forward launches the same kernels with the same arguments as
