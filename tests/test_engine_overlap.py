@@ -433,3 +433,34 @@ def test_failed_step_fails_its_requests(overlap, monkeypatch):
         assert -1 not in toks and toks == expected(prompts[int(rid[1])], 6, [])[:len(toks)]
     assert not w.active_requests and len(w.cache.free_blocks) == w.cache.max_num_blocks
     assert not eng.sampler.row_of and not eng._closing
+
+
+def test_text_prompts_through_an_offline_tokenizer(tmp_path, monkeypatch):
+    """String prompts: a tokenizer shipped in the model directory is loaded
+    offline (load_tokenizer), prompts are encoded, generated ids decoded."""
+    import asyncio
+
+    tokenizers = pytest.importorskip("tokenizers")
+    from transformers import PreTrainedTokenizerFast
+
+    from mu_b200 import MuEngine
+    from mu_b200.utils.tokenizer import load_tokenizer
+
+    vocab = {f"w{i}": i for i in range(V)}
+    tok = tokenizers.Tokenizer(tokenizers.models.WordLevel(vocab, unk_token="w0"))
+    tok.pre_tokenizer = tokenizers.pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="w0").save_pretrained(str(tmp_path))
+    tk = load_tokenizer(str(tmp_path))
+    assert tk is not None and tk.encode("w1 w2 w3") == [1, 2, 3]
+    assert load_tokenizer(str(tmp_path / "missing")) is None
+
+    monkeypatch.setattr(E, "BatchSampler", FakeSampler)
+    ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=2),
+                      scheduler=SchedulerConfig(max_batch_size=2, max_num_batched_tokens=64))
+    eng = MuEngine(ec)
+    eng.initialize_from_worker(FakeWorker(), tk)
+    out = asyncio.run(eng.generate("w1 w2 w3", SamplingParams(temperature=0.0, max_tokens=5)))
+    want = expected([1, 2, 3], 5, [])
+    assert out.token_ids == want
+    assert out.text == tk.decode(want, skip_special_tokens=True)
+    assert out.usage["prompt_tokens"] == 3
