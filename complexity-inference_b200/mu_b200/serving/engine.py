@@ -78,17 +78,26 @@ class _Launched:
     handle: SampleHandle
 
 
+_heap_frozen = False
+
+
 def freeze_startup_heap() -> None:
-    """Move every object alive now (imported modules, the loaded model's
-    bookkeeping: typically hundreds of thousands of objects) out of the
-    cyclic collector's generations.  A full collection during serving then
-    walks only objects made since, instead of pausing the step loop for
-    tens of milliseconds; nothing frozen is ever freed by the collector,
-    which for a server's start-up state is no loss."""
+    """Once per process: move every object alive now (imported modules, the
+    loaded model's bookkeeping: typically hundreds of thousands of objects)
+    out of the cyclic collector's generations.  A full collection during
+    serving then walks only objects made since, instead of pausing the step
+    loop for tens of milliseconds.  Frozen objects are still freed by
+    reference counting; only cycles among them are never collected, which
+    for a server's start-up state is no loss.  Later engines in the same
+    process do not freeze again."""
+    global _heap_frozen
+    if _heap_frozen:
+        return
     import gc
 
     gc.collect()
     gc.freeze()
+    _heap_frozen = True
 
 
 class StepEngine:
@@ -106,7 +115,8 @@ class StepEngine:
     with the request), so the generated tokens are exactly those of the
     non-overlapped engine.  ``overlap=False`` runs each step to completion
     (the reference's order, engine.py:560-680).  ``freeze_gc`` (default)
-    calls :func:`freeze_startup_heap` once at construction.
+    calls :func:`freeze_startup_heap` (a no-op after the process's first
+    engine).
     """
 
     def __init__(self, worker: MuWorker, config: EngineConfig, eos_token_id: Optional[int] = None,
