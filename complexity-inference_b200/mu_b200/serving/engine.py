@@ -239,9 +239,13 @@ class StepEngine:
                 return cache.blocks_needed(r.request_id, n)
             return max(1, -(-n // bs))
 
-        for req in self.scheduler.fit_blocks(out, len(cache.free_blocks), need_of,
-                                             lambda r: len(cache.block_table(r.request_id))):
-            self._release(req.request_id)
+        free = len(cache.free_blocks)
+        # a decode takes at most one new block, a chunk of n tokens at most n // bs + 2
+        worst = len(out.decode_requests) + sum(n // bs + 2 for _, n in out.prefill_chunks)
+        if worst > free:
+            for req in self.scheduler.fit_blocks(out, free, need_of,
+                                                 lambda r: len(cache.block_table(r.request_id))):
+                self._release(req.request_id)
         prefills: List[Request] = []
         chunks: List[tuple] = []
         for req, chunk in zip(out.prefill_requests, out.prefill_chunks):
