@@ -4,6 +4,9 @@
 
 #include <cuda_runtime.h>
 #include <stdarg.h>
+#include <stdint.h>
+
+#include <atomic>
 #include <stdio.h>
 
 #include "../../include/muk.h"
@@ -13,6 +16,22 @@ namespace muk {
 void set_last_error(const char* fmt, ...);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Sets a kernel's dynamic shared-memory limit on the current device.  The
+// attribute is per device, so `done` (one per kernel) records the devices
+// (ids below 64) it has been set on; callers on several threads may race,
+// which only repeats the idempotent call.
+template <typename Kernel>
+inline cudaError_t smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 // Returns MUK_ERR_CUDA (with the message) if the last launch failed.
 int check_launch(const char* what);

@@ -89,6 +89,13 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   if (blk_begin >= nblk || ctx <= 0) return;
   const int blk_end = min(nblk, blk_begin + blocks_per_split);
   const int nsplit_b = (nblk + blocks_per_split - 1) / blocks_per_split;
+  // A context longer than the launch was sized for would read past its
+  // block-table row or write past its split slots (or through the null
+  // partials of a single-split launch): latch the error and skip it.
+  if (nblk > bt_stride || nsplit_b > max_splits) {
+    if (threadIdx.x == 0) set_device_error(kDevBadIndex);
+    return;
+  }
 
   // Query fragments (A operand, rows = heads of the group; rows >= G are 0).
   uint32_t qa[kKS][4];
@@ -285,7 +292,7 @@ __global__ void decode_merge_kernel(__nv_bfloat16* __restrict__ out, int64_t out
   const int ctx = seq_lens[b];
   const int nblk = (ctx + kBlockSize - 1) / kBlockSize;
   const int ns = (nblk + blocks_per_split - 1) / blocks_per_split;
-  if (ns <= 1) return;
+  if (ns <= 1 || ns > max_splits) return;  // ns > max_splits: latched by the decode kernel
   const int64_t base = ((int64_t)b * num_q_heads + h) * max_splits;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
@@ -558,6 +565,11 @@ extern "C" size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, 
   return rows * ((size_t)head_dim + 2) * sizeof(float);
 }
 
+extern "C" int muk_decode_attn_splits(int num_seqs, int max_seq_len, int block_size) {
+  if (num_seqs <= 0 || max_seq_len <= 0 || block_size != kBlockSize) return 0;
+  return decode_split_policy(max_seq_len, num_seqs).max_splits;
+}
+
 template <int D>
 static int launch_decode(const void* q, int64_t q_stride, void* out, int64_t out_stride,
                          const void* k_cache, const void* v_cache, const int32_t* block_tables,
@@ -579,11 +591,11 @@ static int launch_decode(const void* q, int64_t q_stride, void* out, int64_t out
     part_ml = part_o + (size_t)num_seqs * num_q_heads * p.max_splits * D;
   }
   const size_t smem = decode_smem_bytes<D>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr_set = true;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t ae = smem_attr_once(paged_decode_kernel<D>, (int)smem, attr_done);
+  if (ae != cudaSuccess) {
+    set_last_error("muk_paged_decode_attn: cudaFuncSetAttribute: %s", cudaGetErrorString(ae));
+    return MUK_ERR_CUDA;
   }
   dim3 grid(p.max_splits, num_kv_heads, num_seqs);
   paged_decode_kernel<D><<<grid, kDecWarps * 32, smem, stream>>>(
@@ -642,11 +654,11 @@ static int launch_prefill_g(const void* q, int64_t q_stride, void* out, int64_t 
                             int num_seqs, int max_q_len, int num_q_heads, int num_kv_heads,
                             int num_blocks, float scale, cudaStream_t stream) {
   const size_t smem = prefill_smem_bytes<D, G, WR>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(paged_prefill_kernel<D, G, WR>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t ae = smem_attr_once(paged_prefill_kernel<D, G, WR>, (int)smem, attr_done);
+  if (ae != cudaSuccess) {
+    set_last_error("muk_paged_prefill_attn: cudaFuncSetAttribute: %s", cudaGetErrorString(ae));
+    return MUK_ERR_CUDA;
   }
   dim3 grid((max_q_len + 16 * WR - 1) / (16 * WR), num_q_heads / G, num_seqs);
   paged_prefill_kernel<D, G, WR><<<grid, G * WR * 32, smem, stream>>>(

@@ -1143,15 +1143,11 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const T
                   int sms, cudaStream_t stream) {
   using L = GemmLayout<BN, STAGES>;
   auto kern = gemm_persistent_kernel<BN, STAGES, EPI, GROUPED>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) {
-      set_last_error("gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      return MUK_ERR_CUDA;
-    }
-    attr = true;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t e = smem_attr_once(kern, L::kBytes, attr_done);
+  if (e != cudaSuccess) {
+    set_last_error("gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return MUK_ERR_CUDA;
   }
   kern<<<a.workers, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, a);
   return check_launch(GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16");
@@ -1194,15 +1190,11 @@ template <int EPI>
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
                        int sms, cudaStream_t stream) {
   auto kern = gemm_pair_kernel<EPI>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairLayout::kBytes);
-    if (e != cudaSuccess) {
-      set_last_error("gemm(pair): cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      return MUK_ERR_CUDA;
-    }
-    attr = true;
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t ae = smem_attr_once(kern, PairLayout::kBytes, attr_done);
+  if (ae != cudaSuccess) {
+    set_last_error("gemm(pair): cudaFuncSetAttribute: %s", cudaGetErrorString(ae));
+    return MUK_ERR_CUDA;
   }
   const int pairs = a.workers;
   cudaLaunchConfig_t cfg = {};

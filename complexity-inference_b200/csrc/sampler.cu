@@ -13,7 +13,8 @@
 //      top_p.  With at most 1024 survivors they are sorted in shared memory
 //      and the prefix is walked exactly as the reference does (cumsum, drop
 //      where the previous cumsum > p); otherwise the cut value is found by a
-//      radix search over the softmax mass;
+//      radix search over the softmax mass, summed in fixed point so the cut
+//      does not depend on the order of the additions;
 //   5. draw: Gumbel-max over the survivors with Philox4x32-10 noise keyed by
 //      (seed, offset, token) — an exact categorical draw from the filtered
 //      softmax, reproducible for a given seed and step offset.
@@ -129,19 +130,52 @@ __device__ int blk_argmax(float v, int idx, float* redv, int* redi) {
   return redi[0];
 }
 
+// Mass of a survivor in the radix top-p search: exp(v - max) in (0, 1] as an
+// unsigned fixed-point number with 40 fraction bits.  Integer sums are exact
+// and do not depend on the order in which threads add them, so the cut (and
+// with it the sampled token) is the same on every run.
+constexpr float kMassScale = 1099511627776.0f;  // 2^40
+__device__ __forceinline__ unsigned long long mass_q(float v, float mx) {
+  return __float2ull_rz(expf(v - mx) * kMassScale);
+}
+
+__device__ unsigned long long blk_sum_u64(unsigned long long v, unsigned long long* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long t = red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// kFilter = false: one sampled token per row (tokens_out).
+// kFilter = true:  the processed logits of prepare_logits per row (filt):
+//                  penalised and temperature-scaled values where kept, -inf
+//                  where top-k / top-p removed the token; nothing is drawn.
+template <bool kFilter>
 __global__ void __launch_bounds__(kSampThreads)
     sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
                   const float* __restrict__ temperature, const int32_t* __restrict__ top_k,
                   const float* __restrict__ top_p, const float* __restrict__ rep_penalty,
                   const uint32_t* __restrict__ seen_bits, int64_t seen_stride,
-                  const int32_t* __restrict__ seen_rows, const uint64_t* __restrict__ seeds, const uint64_t* __restrict__ offsets,
-                  int32_t* __restrict__ out) {
+                  const int32_t* __restrict__ seen_rows, const uint64_t* __restrict__ seeds,
+                  const uint64_t* __restrict__ offsets, int32_t* __restrict__ out,
+                  float* __restrict__ filt, int64_t ld_filt) {
   __shared__ float redv[32];
   __shared__ int redi[32];
+  __shared__ unsigned long long redq[32];
   __shared__ uint32_t hist[256];
-  __shared__ float mhist[256];
+  __shared__ unsigned long long mhist[256];
   __shared__ uint32_t s_prefix;
   __shared__ int s_cnt;
+  __shared__ unsigned long long s_above;
   __shared__ float cand_v[kCandMax];
   __shared__ int cand_i[kCandMax];
   __shared__ int s_keep;
@@ -154,8 +188,9 @@ __global__ void __launch_bounds__(kSampThreads)
   p.seen = (seen_bits != nullptr && p.rp != 1.f) ? seen_bits + (int64_t)srow * seen_stride : nullptr;
   p.temp = temperature ? temperature[row] : 1.f;
   const int tid = threadIdx.x;
+  float* frow = kFilter ? filt + (int64_t)row * ld_filt : nullptr;
 
-  if (p.temp <= 0.f) {
+  if (!kFilter && p.temp <= 0.f) {
     // Greedy: argmax of the penalised logits (scaling by 1/1e-8 keeps the order).
     RowParams q = p;
     q.temp = 1.f;
@@ -207,7 +242,7 @@ __global__ void __launch_bounds__(kSampThreads)
     thr_key = prefix;
   }
 
-  // ---- max and mass over the top-k survivors ----
+  // ---- max and count over the top-k survivors ----
   float mx = -INFINITY;
   int nkeep = 0;
   for (int i = tid; i < V; i += blockDim.x) {
@@ -263,23 +298,33 @@ __global__ void __launch_bounds__(kSampThreads)
           __syncthreads();
         }
       }
-      // Probabilities, inclusive cumsum, reference keep rule.
+      // Reference keep rule over the sorted survivors: f32 probabilities,
+      // a running sum held in double and read back as f32 (torch's CPU
+      // cumsum accumulates float in double), token i kept while the sum of
+      // the tokens before it is <= top_p; the first token always stays.
       if (tid == 0) {
-        float z = 0.f;
-        for (int i = 0; i < n; ++i) z += expf(cand_v[i] - mx);
-        float cum = 0.f;
+        double z = 0.0;
+        for (int i = 0; i < n; ++i) z += (double)expf(cand_v[i] - mx);
+        const float zf = (float)z;
+        double cum = 0.0;
         int keep = n;
         for (int i = 0; i < n; ++i) {
-          if (i > 0 && cum > pp) {
+          if (i > 0 && (float)cum > pp) {
             keep = i;
             break;
           }
-          cum += expf(cand_v[i] - mx) / z;
+          cum += (double)(expf(cand_v[i] - mx) / zf);
         }
         s_keep = keep;
       }
       __syncthreads();
       const int keep = s_keep;
+      if (kFilter) {
+        for (int i = tid; i < V; i += blockDim.x) frow[i] = -INFINITY;
+        __syncthreads();
+        for (int i = tid; i < keep; i += blockDim.x) frow[cand_i[i]] = cand_v[i];
+        return;
+      }
       // Gumbel-max over the kept prefix.
       const uint64_t seed = seeds ? seeds[row] : 0ull, off = offsets ? offsets[row] : 0ull;
       float best = -INFINITY;
@@ -298,43 +343,55 @@ __global__ void __launch_bounds__(kSampThreads)
       if (tid == 0) out[row] = r < V ? r : 0;
       return;
     }
-    // Radix search for the cut: largest key with mass(key' >= key) > pp.
-    float z = 0.f;
+    // Radix search for the cut: the largest key K whose mass(key >= K)
+    // exceeds top_p of the total, i.e. the sorted prefix up to and including
+    // the first token at which the running mass passes top_p.  Masses are
+    // fixed-point integers (mass_q), so the sums are exact and the cut does
+    // not depend on the order of the additions.
+    unsigned long long zq = 0ull;
     for (int i = tid; i < V; i += blockDim.x) {
       const float v = row_val(p, i);
-      if (f2key(v) >= thr_key) z += expf(v - mx);
+      if (f2key(v) >= thr_key) zq += mass_q(v, mx);
     }
-    z = blk_sum(z, redv);
-    const float target = pp * z;
+    zq = blk_sum_u64(zq, redq);
+    const unsigned long long target = (unsigned long long)((double)pp * (double)zq);
     uint32_t prefix = 0u;
-    float above = 0.f;  // mass strictly above the current prefix range
+    unsigned long long above = 0ull;  // mass strictly above the current prefix range
     for (int shift = 24; shift >= 0; shift -= 8) {
-      if (tid < 256) mhist[tid] = 0.f;
+      if (tid < 256) mhist[tid] = 0ull;
       __syncthreads();
       const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
       for (int i = tid; i < V; i += blockDim.x) {
         const float v = row_val(p, i);
         const uint32_t key = f2key(v);
         if (key >= thr_key && (key & hi_mask) == (prefix & hi_mask))
-          atomicAdd(&mhist[(key >> shift) & 255u], expf(v - mx));
+          atomicAdd(&mhist[(key >> shift) & 255u], mass_q(v, mx));
       }
       __syncthreads();
       if (tid == 0) {
-        float acc = above;
+        unsigned long long acc = above;
         int d = 255;
         for (; d > 0; --d) {
           if (acc + mhist[d] > target) break;
           acc += mhist[d];
         }
-        redv[0] = acc;
+        s_above = acc;
         s_prefix = prefix | ((uint32_t)d << shift);
       }
       __syncthreads();
-      above = redv[0];
+      above = s_above;
       prefix = s_prefix;
       __syncthreads();
     }
     cut_key = prefix > thr_key ? prefix : thr_key;
+  }
+
+  if (kFilter) {
+    for (int i = tid; i < V; i += blockDim.x) {
+      const float v = row_val(p, i);
+      frow[i] = f2key(v) >= cut_key ? v : -INFINITY;
+    }
+    return;
   }
 
   // ---- Gumbel-max draw over key >= cut_key ----
@@ -369,8 +426,24 @@ extern "C" int muk_sample(const float* logits, int64_t ld, int num_rows, int voc
   MUK_REQUIRE(logits && tokens_out && vocab > 0 && ld >= vocab, "muk_sample: bad arguments");
   MUK_REQUIRE(seen_bits == nullptr || seen_stride * 32 >= vocab, "muk_sample: seen_stride");
   if (num_rows <= 0) return MUK_OK;
-  sample_kernel<<<num_rows, kSampThreads, 0, as_stream(stream)>>>(
+  sample_kernel<false><<<num_rows, kSampThreads, 0, as_stream(stream)>>>(
       logits, ld, vocab, temperature, top_k, top_p, rep_penalty, seen_bits, seen_stride, seen_rows,
-      seeds, offsets, tokens_out);
+      seeds, offsets, tokens_out, nullptr, 0);
   return check_launch("muk_sample");
+}
+
+extern "C" int muk_prepare_logits(const float* logits, int64_t ld, int num_rows, int vocab,
+                                  const float* temperature, const int32_t* top_k,
+                                  const float* top_p, const float* rep_penalty,
+                                  const uint32_t* seen_bits, int64_t seen_stride,
+                                  const int32_t* seen_rows, float* out, int64_t ld_out,
+                                  void* stream) {
+  MUK_REQUIRE(logits && out && vocab > 0 && ld >= vocab && ld_out >= vocab,
+              "muk_prepare_logits: bad arguments");
+  MUK_REQUIRE(seen_bits == nullptr || seen_stride * 32 >= vocab, "muk_prepare_logits: seen_stride");
+  if (num_rows <= 0) return MUK_OK;
+  sample_kernel<true><<<num_rows, kSampThreads, 0, as_stream(stream)>>>(
+      logits, ld, vocab, temperature, top_k, top_p, rep_penalty, seen_bits, seen_stride, seen_rows,
+      nullptr, nullptr, nullptr, out, ld_out);
+  return check_launch("muk_prepare_logits");
 }

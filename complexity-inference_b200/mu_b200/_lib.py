@@ -45,6 +45,7 @@ SIGNATURES = {
     "muk_rope_kv_append": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
                                    _P, _P, c_float, _P, _P, c_int, c_int, _P]),
     "muk_decode_attn_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "muk_decode_attn_splits": (c_int, [c_int, c_int, c_int]),
     "muk_paged_decode_attn": (c_int, [_P, c_int64, _P, c_int64, _P, _P, _P, c_int, _P, c_int,
                                       c_int, c_int, c_int, c_int, c_int, c_float, c_int, _P,
                                       c_size_t, _P]),
@@ -84,6 +85,8 @@ SIGNATURES = {
                                  c_float, c_float, c_float, _P]),
     "muk_sample": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P, _P, _P,
                            _P, _P]),
+    "muk_prepare_logits": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P,
+                                   _P, c_int64, _P]),
     "muk_mark_seen": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P]),
     "muk_fill_decode_inputs": (c_int, [_P, _P, _P, c_int, _P]),
 }

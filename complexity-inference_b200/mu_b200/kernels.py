@@ -253,6 +253,20 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
          _p(seen_rows), _p(seeds), _p(offsets), _p(out), _stream())
 
 
+def prepare_logits(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+                   top_p: torch.Tensor, rep_penalty: torch.Tensor, seen_bits: torch.Tensor | None,
+                   out: torch.Tensor, seen_rows: torch.Tensor | None = None):
+    """prepare_logits per row (mu_inference/utils/sampling.py:20-87): out gets the
+    penalised, temperature-scaled logits where kept and -inf where removed."""
+    _check(logits, torch.float32, "logits")
+    _check(out, torch.float32, "out")
+    B, V = logits.shape
+    call("muk_prepare_logits", _p(logits), _row_stride(logits, "logits"), B, V, _p(temperature),
+         _p(top_k), _p(top_p), _p(rep_penalty), _p(seen_bits),
+         0 if seen_bits is None else seen_bits.stride(0), _p(seen_rows), _p(out),
+         _row_stride(out, "out"), _stream())
+
+
 def mark_seen(seen_bits: torch.Tensor, rows: torch.Tensor, tokens: torch.Tensor, vocab: int,
               n: int | None = None):
     n = tokens.numel() if n is None else n

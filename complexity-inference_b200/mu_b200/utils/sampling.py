@@ -178,34 +178,46 @@ class BatchSampler:
 def prepare_logits(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,
                    top_p: float = 1.0, repetition_penalty: float = 1.0,
                    past_tokens: Optional[List[int]] = None) -> torch.Tensor:
-    """Reference-compatible filtered logits [1, V] (sampling.py:20-87).
-
-    Returned as a lazy record: the filtering itself happens inside the GPU
-    sampler when ``sample_token`` consumes it."""
-    out = logits.detach().float().reshape(1, -1)
-    out._mu_params = (temperature, top_k, top_p, repetition_penalty, list(past_tokens or []))
-    return out
+    """Processed logits [B, V] as the reference returns them (sampling.py:20-87):
+    repetition penalty on row 0's past tokens (the reference indexes
+    ``logits[0, id]``), temperature, top-k and top-p with removed entries at
+    -inf.  Computed by the GPU sampler's filter (muk_prepare_logits); the
+    result is returned on the input's device."""
+    src = logits.detach()
+    x = src.reshape(-1, src.shape[-1]).float()
+    dev = x.device if x.is_cuda else torch.device("cuda")
+    x = x.to(dev).contiguous()
+    B, V = x.shape
+    words = (V + 31) // 32
+    seen = torch.zeros(2, words, dtype=torch.int32, device=dev)
+    rows = torch.ones(B, dtype=torch.int32, device=dev)
+    rows[0] = 0
+    if past_tokens and repetition_penalty != 1.0:
+        ids = sorted(set(int(i) for i in past_tokens if 0 <= int(i) < V))
+        if ids:
+            ids_t = torch.as_tensor(ids, dtype=torch.int32, device=dev)
+            K.mark_seen(seen, torch.zeros_like(ids_t), ids_t, V)
+    out = torch.empty_like(x)
+    K.prepare_logits(x, torch.full((B,), float(temperature), device=dev),
+                     torch.full((B,), int(top_k), device=dev, dtype=torch.int32),
+                     torch.full((B,), float(top_p), device=dev),
+                     torch.full((B,), float(repetition_penalty), device=dev), seen, out,
+                     seen_rows=rows)
+    return out.reshape(src.shape).to(src.device)
 
 
 def sample_token(logits: torch.Tensor, do_sample: bool = True, seed: int = 0, step: int = 0) -> int:
-    """One token from [1, V] logits (sampling.py:90-120) via the GPU sampler."""
-    t, k, p, rp, past = getattr(logits, "_mu_params", (1.0, 0, 1.0, 1.0, []))
-    if not do_sample:
-        t = 0.0
-    dev = logits.device
+    """One token from processed logits [1, V] (sampling.py:90-120): a draw from
+    softmax(logits) (Gumbel-max with Philox noise keyed by ``seed`` and
+    ``step``; -inf entries are never drawn, and a row that is all -inf gives
+    token 0), or the argmax when ``do_sample`` is False."""
+    dev = logits.device if logits.is_cuda else torch.device("cuda")
     V = logits.shape[-1]
-    x = logits.reshape(1, V).float().contiguous().to(dev)
-    words = (V + 31) // 32
-    seen = torch.zeros(1, words, dtype=torch.int32, device=dev)
-    if past and rp != 1.0:
-        ids = torch.as_tensor(sorted(set(i for i in past if 0 <= i < V)), dtype=torch.int32, device=dev)
-        if ids.numel():
-            K.mark_seen(seen, torch.zeros_like(ids), ids, V)
+    x = logits.reshape(-1, V)[:1].float().contiguous().to(dev)
     out = torch.zeros(1, dtype=torch.int32, device=dev)
-    K.sample(x, torch.tensor([t], device=dev, dtype=torch.float32),
-             torch.tensor([k], device=dev, dtype=torch.int32),
-             torch.tensor([p], device=dev, dtype=torch.float32),
-             torch.tensor([rp], device=dev, dtype=torch.float32), seen,
+    one = torch.ones(1, device=dev, dtype=torch.float32)
+    K.sample(x, torch.tensor([1.0 if do_sample else 0.0], device=dev), torch.zeros(1, device=dev,
+             dtype=torch.int32), one, one, None,
              torch.tensor([seed], device=dev, dtype=torch.int64),
              torch.tensor([step], device=dev, dtype=torch.int64), out)
     return int(out.item())

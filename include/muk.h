@@ -122,11 +122,20 @@ int muk_rope_kv_append(void* qkv, int64_t qkv_stride, const int32_t* positions,
 size_t muk_decode_attn_workspace_size(int num_seqs, int num_q_heads, int head_dim,
                                       int max_seq_len, int block_size);
 
+/* Splits per sequence (grid x of the decode kernel) that muk_paged_decode_attn
+ * uses for a batch of num_seqs sequences sized for max_seq_len; 1 means no
+ * split-K scratch is touched.  0 for invalid arguments.  A launch-plan query
+ * with no counterpart in the reference. */
+int muk_decode_attn_splits(int num_seqs, int max_seq_len, int block_size);
+
 /* out[b, h, :] = softmax(q·Kᵀ·scale)·V over the sequence's first seq_lens[b]
  * cached tokens (GQA: q head h reads kv head h / (Hq/Hkv)).  Split-K over
  * blocks with a merge pass.  Replaces the decode branch of MuAttention
  * (torch.cat + repeat_interleave + SDPA, is_causal=False),
- * mu_inference/models/layers.py:700-723. */
+ * mu_inference/models/layers.py:700-723.  A sequence whose seq_lens[b]
+ * exceeds what the launch was sized for (more blocks than its block-table
+ * row, or more splits than max_seq_len gives) is skipped and latches device
+ * error 5 (bad index); block ids outside [0, num_blocks) latch the same. */
 int muk_paged_decode_attn(const void* q, int64_t q_stride, void* out, int64_t out_stride,
                           const void* k_cache, const void* v_cache, const int32_t* block_tables,
                           int block_table_stride, const int32_t* seq_lens, int num_seqs,
@@ -295,6 +304,17 @@ int muk_sample(const float* logits, int64_t ld, int num_rows, int vocab,
                const float* rep_penalty, const uint32_t* seen_bits, int64_t seen_stride,
                const int32_t* seen_rows, const uint64_t* seeds, const uint64_t* offsets,
                int32_t* tokens_out, void* stream);
+
+/* The processed logits of prepare_logits, mu_inference/utils/sampling.py:20-87,
+ * one row per row of logits: out[b][i] = the penalised, temperature-scaled
+ * logit where top-k / top-p keep token i, -inf where they remove it.  Same
+ * arguments and the same filter code as muk_sample (so the kept set is the
+ * one muk_sample draws from), no draw.  Temperature 0 divides by 1e-8 as the
+ * reference does.  out has row stride ld_out >= vocab. */
+int muk_prepare_logits(const float* logits, int64_t ld, int num_rows, int vocab,
+                       const float* temperature, const int32_t* top_k, const float* top_p,
+                       const float* rep_penalty, const uint32_t* seen_bits, int64_t seen_stride,
+                       const int32_t* seen_rows, float* out, int64_t ld_out, void* stream);
 
 /* Sets bit tokens[b] in seen_bits[rows[b]] for b < n (keeps the repetition
  * bitmaps current after each step without a host round trip). */

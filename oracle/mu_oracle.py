@@ -92,15 +92,20 @@ def sdpa(q, k, v, causal: bool):
     G = Hq // k.shape[0]
     k = np.repeat(k, G, axis=0)
     v = np.repeat(v, G, axis=0)
-    s = np.einsum("hqd,hkd->hqk", q, k).astype(F32) / F32(np.sqrt(D))
-    if causal:
-        Sk = k.shape[1]
-        mask = np.tril(np.ones((Sq, Sk), dtype=bool))
-        s = np.where(mask[None], s, -np.inf)
-    s = s - s.max(-1, keepdims=True)
-    p = np.exp(s)
-    p = p / p.sum(-1, keepdims=True)
-    return np.einsum("hqk,hkd->hqd", p.astype(F32), v).astype(F32)
+    Sk = k.shape[1]
+    mask = np.tril(np.ones((Sq, Sk), dtype=bool)) if causal else None
+    out = np.empty((Hq, Sq, v.shape[2]), dtype=F32)
+    step = max(1, (1 << 26) // max(1, Sq * Sk))  # heads per chunk: ~256 MB of scores
+    for h0 in range(0, Hq, step):  # per-head math; chunks only bound host memory
+        hs = slice(h0, min(Hq, h0 + step))
+        s = np.matmul(q[hs], k[hs].transpose(0, 2, 1)).astype(F32) / F32(np.sqrt(D))
+        if causal:
+            s = np.where(mask[None], s, -np.inf)
+        s = s - s.max(-1, keepdims=True)
+        p = np.exp(s)
+        p = p / p.sum(-1, keepdims=True)
+        out[hs] = np.matmul(p.astype(F32), v[hs])
+    return out
 
 
 def _silu(x):
@@ -174,16 +179,22 @@ class OracleModel:
 
     def __init__(self, shape: ModelShape, params: Dict[str, np.ndarray], mu: MuCfg):
         self.s = shape
+        # set to a list to record each routed layer's expert ids per forward
+        self.expert_trace: Optional[List[np.ndarray]] = None
         self.p = {k: np.asarray(v, dtype=F32) for k, v in params.items()}
         self.mu = mu
         self.cos, self.sin = rope_tables(shape.head_dim, shape.theta, max(shape.max_pos, 8192))
         if shape.tie or "lm_head.weight" not in self.p:
             self.p["lm_head.weight"] = self.p["embed_tokens.weight"]
 
-    def _attention(self, l, x, past, mu_prev):
+    def _attention(self, l, x, segs, pasts, mu_prev):
+        """Attention of every request's rows: x [T, H] holds the requests'
+        new tokens back to back (segs = (start, length) per request), pasts
+        their caches.  Projections are row-wise, so they run on all rows at
+        once; RoPE positions and SDPA are per request (layers.py:626-741)."""
         s, p = self.s, self.p
         pre = f"layers.{l}.self_attn."
-        S = x.shape[0]
+        T = x.shape[0]
         k = x @ p[pre + "k_proj.weight"].T
         q = x @ p[pre + "q_proj.weight"].T
         v = x @ p[pre + "v_proj.weight"].T
@@ -191,57 +202,89 @@ class OracleModel:
             k = k + mu_prev @ p[pre + "mu_to_k.weight"].T
             q = q + mu_prev @ p[pre + "mu_to_q.weight"].T
             v = v + mu_prev @ p[pre + "mu_to_v.weight"].T
-        q = q.reshape(S, s.heads, s.head_dim).astype(F32)
-        k = k.reshape(S, s.kv_heads, s.head_dim).astype(F32)
-        v = v.reshape(S, s.kv_heads, s.head_dim).astype(F32)
+        q = q.reshape(T, s.heads, s.head_dim).astype(F32)
+        k = k.reshape(T, s.kv_heads, s.head_dim).astype(F32)
+        v = v.reshape(T, s.kv_heads, s.head_dim).astype(F32)
         if s.qk_norm:  # layers.py:677-679
             q = rmsnorm(q, p[pre + "q_norm.weight"], 1e-6)
             k = rmsnorm(k, p[pre + "k_norm.weight"], 1e-6)
-        past_len = 0 if past is None else past[0].shape[1]
-        pos = np.arange(past_len, past_len + S)
-        q = apply_rope(q, self.cos, self.sin, pos)
-        k = apply_rope(k, self.cos, self.sin, pos)
-        K = k.transpose(1, 0, 2)
-        V = v.transpose(1, 0, 2)
-        if past is not None:
-            K = np.concatenate([past[0], K], 1)
-            V = np.concatenate([past[1], V], 1)
-        o = sdpa(q.transpose(1, 0, 2), K, V, causal=(S == K.shape[1]))
-        o = o.transpose(1, 0, 2).reshape(S, -1)
+        o = np.empty((T, s.heads * s.head_dim), dtype=F32)
+        kvs = []
+        for (a, S), past in zip(segs, pasts):
+            past_len = 0 if past is None else past[0].shape[1]
+            pos = np.arange(past_len, past_len + S)
+            qr = apply_rope(q[a:a + S], self.cos, self.sin, pos)
+            kr = apply_rope(k[a:a + S], self.cos, self.sin, pos)
+            K = kr.transpose(1, 0, 2)
+            V = v[a:a + S].transpose(1, 0, 2)
+            if past is not None:
+                K = np.concatenate([past[0], K], 1)
+                V = np.concatenate([past[1], V], 1)
+            orow = sdpa(qr.transpose(1, 0, 2), K, V, causal=(S == K.shape[1]))
+            o[a:a + S] = orow.transpose(1, 0, 2).reshape(S, -1)
+            kvs.append((K, V))
         out = _clamp((o @ p[pre + "o_proj.weight"].T).astype(F32), self.mu)
-        return out, (K, V)
+        return out, kvs
 
     def _mlp(self, l, x, token_ids, mu_cur):
         s, p = self.s, self.p
         pre = f"layers.{l}.mlp."
         if s.arch == "deep" and s.experts and s.experts > 1:
             e = route_experts(token_ids, mu_cur, p[pre + "mu_router.weight"], s.experts, s.vocab)
+            if self.expert_trace is not None:
+                self.expert_trace.append(e.copy())
             gu_w = p[pre + "gate_up_proj"]
             d_w = p[pre + "down_proj"]
             I = d_w.shape[1]
             out = np.empty_like(x)
-            for t in range(x.shape[0]):  # layers.py:534-547 per-token expert weights
-                gu = x[t] @ gu_w[e[t]]
-                inter = _silu(gu[:I]) * gu[I:]
-                out[t] = inter @ d_w[e[t]]
+            # layers.py:534-547 gathers each token's expert weights and runs a
+            # per-token bmm; tokens are independent, so the rows of one
+            # expert are computed together here (same products, one matmul)
+            for ex in np.unique(e):
+                rows = np.nonzero(e == ex)[0]
+                gu = x[rows] @ gu_w[ex]
+                inter = _silu(gu[:, :I]) * gu[:, I:]
+                out[rows] = inter @ d_w[ex]
             return _clamp(out.astype(F32), self.mu)
         gate = _silu(x @ p[pre + "gate_proj.weight"].T)
         up = x @ p[pre + "up_proj.weight"].T
         return _clamp(((gate * up) @ p[pre + "down_proj.weight"].T).astype(F32), self.mu)
 
     def forward(self, ids: Sequence[int], past=None, return_hidden: bool = False):
+        """One request: last-token logits [V] and its grown cache."""
+        logits, pasts, hn = self.forward_batch([ids], [past])
+        if return_hidden:
+            return logits[0], pasts[0], hn
+        return logits[0], pasts[0]
+
+    def forward_batch(self, ids_list: Sequence[Sequence[int]], past_list=None):
+        """Several requests at once, each with its own new tokens and cache.
+
+        Every request's rows get exactly the per-request math of the
+        reference's batch-1 forward (all matmuls, norms, INL, routing and the
+        MLP act row by row; attention and RoPE positions per request).
+        Returns (last-token logits [R, V], new caches, final-norm rows)."""
         s, p, mu = self.s, self.p, self.mu
-        ids = np.asarray(ids, dtype=np.int64)
+        if past_list is None:
+            past_list = [None] * len(ids_list)
+        seqs = [np.asarray(i, dtype=np.int64).reshape(-1) for i in ids_list]
+        segs, a = [], 0
+        for q in seqs:
+            segs.append((a, len(q)))
+            a += len(q)
+        ids = np.concatenate(seqs)
         h = _clamp(p["embed_tokens.weight"][ids].astype(F32), mu)
-        new_past = []
+        new_past = [[] for _ in seqs]
         v_state, mu_prev = None, None
         for l in range(s.layers):
             pre = f"layers.{l}."
             res = h
             x = rmsnorm(h, p[pre + "input_layernorm.weight"], s.eps, mu)
-            attn, kv = self._attention(l, x, None if past is None else past[l],
-                                       mu_prev if s.arch == "deep" else None)
-            new_past.append(kv)
+            attn, kvs = self._attention(l, x, segs,
+                                        [None if pp is None else pp[l] for pp in past_list],
+                                        mu_prev if s.arch == "deep" else None)
+            for r, kv in enumerate(kvs):
+                new_past[r].append(kv)
             if s.arch == "deep":  # deep.py:151-176
                 h_next, v_state, mu_cur = inl_dynamics(attn, v_state, p, pre + "dynamics.", s.dt)
                 h = res + h_next
@@ -256,10 +299,9 @@ class OracleModel:
                 x2 = rmsnorm(h, p[pre + "post_attention_layernorm.weight"], s.eps, mu)
                 h = _clamp(res + self._mlp(l, x2, ids, None), mu)
         hn = rmsnorm(h, p["norm.weight"], s.eps, mu)
-        logits = (hn[-1] @ p["lm_head.weight"].T).astype(F32)
-        if return_hidden:
-            return logits, new_past, hn
-        return logits, new_past
+        last = np.array([a + n - 1 for a, n in segs])
+        logits = (hn[last] @ p["lm_head.weight"].T).astype(F32)
+        return logits, new_past, hn
 
 
 def greedy_generate(model: OracleModel, prompt: Sequence[int], n: int):
@@ -358,7 +400,9 @@ def prepare_logits(logits, temperature=1.0, top_k=0, top_p=1.0, repetition_penal
         order = np.argsort(-x, kind="stable")
         sx = x[order]
         e = np.exp(sx - sx.max())
-        cum = np.cumsum(e / e.sum())
+        # torch.cumsum on a CPU float tensor accumulates in double and stores
+        # float; a float32 running sum drifts by ~1e-5 over 1e5 tokens
+        cum = np.cumsum((e / e.sum()).astype(F32), dtype=np.float64).astype(F32)
         remove = cum > top_p
         remove[1:] = remove[:-1].copy()
         remove[0] = False

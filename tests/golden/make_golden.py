@@ -7,8 +7,6 @@ path (``tests/test_model_gpu.py``).  /root/reference does not exist on the
 GPU box, so only the .npz files travel; this script is committed so the
 fixtures can be regenerated:
 
-    python tests/golden/make_golden.py
-
 Contents
   mu_clamp.npz        mu_clamp / soft_clamp on fixed inputs (core/mu.py)
   paged_cache.npz     MuPagedCache block tables and lengths along an
@@ -21,13 +19,26 @@ Contents
   llama_tiny.npz      served path (MuWorker.execute, fp32, greedy argmax) of a
   deep_tiny.npz       tiny LlamaForCausalLM / DeepForCausalLM: prompts, tokens,
                       logits at selected steps, top-2 gaps at every step
+  sampling_large.npz  prepare_logits kept-token masks at V = 32000 and 128256
+                      (the radix top-p path of the GPU sampler); the logits
+                      are regenerated from a seed (golden_models.large_logits)
+  llama_decisive.npz  served path of a C1-shaped Llama whose logits have a wide
+                      top-2 gap at every step (golden_models.decisive_state_dict),
+                      so greedy tokens can be compared without exceptions
 Weights come from mu_b200.models.weights.random_state_dict (seeded, CPU);
 each model fixture stores the weights' digest.
+
+Usage (the reference checkout is given by argument or environment):
+
+    python tests/golden/make_golden.py --reference <complexity-inference checkout>
+    MU_REFERENCE=<checkout> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
 
+import argparse
 import math
+import os
 import sys
 import tempfile
 from pathlib import Path
@@ -37,8 +48,28 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
+
+
+def _args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--reference", default=os.environ.get("MU_REFERENCE"),
+                    help="checkout of Complexity-ML/complexity-inference (or MU_REFERENCE)")
+    ap.add_argument("--only", default="",
+                    help="comma-separated fixture names (without .npz) to regenerate")
+    args = ap.parse_args()
+    if not args.reference or not (Path(args.reference) / "mu_inference").is_dir():
+        ap.error("--reference (or MU_REFERENCE) must name a checkout containing mu_inference/")
+    args.reference = str(Path(args.reference).resolve())
+    return args
+
+
+ARGS = _args() if __name__ == "__main__" else None
+REFERENCE = ARGS.reference if ARGS else None
 sys.path.insert(0, str(ROOT / "complexity-inference_b200"))
-sys.path.insert(0, "/root/reference")
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+if REFERENCE:
+    sys.path.insert(0, REFERENCE)
 
 from mu_b200.core.config import ModelConfig as MyModelConfig  # noqa: E402
 from mu_b200.models.weights import random_state_dict, state_dict_digest, write_model_dir  # noqa: E402
@@ -52,7 +83,10 @@ from mu_inference.models.loader import config_from_dict  # noqa: E402
 from mu_inference.serving.worker import MuWorker, WorkerRequest  # noqa: E402
 from mu_inference.utils.sampling import prepare_logits  # noqa: E402
 
-assert "reference" in str(Path(mu_inference.__file__).resolve()), mu_inference.__file__
+from golden_models import (DECISIVE, LARGE_SAMPLING_CASES, LARGE_SAMPLING_VOCABS,  # noqa: E402
+                           decisive_state_dict, large_logits, large_past)
+
+assert str(Path(mu_inference.__file__).resolve()).startswith(REFERENCE), mu_inference.__file__
 
 LLAMA_TINY = dict(arch="llama", hidden=256, layers=4, heads=4, kv=2, head_dim=64, inter=688,
                   vocab=1024, seed=0, reqs=8, plen=(16, 128), ntok=32, qk_norm=False)
@@ -66,7 +100,7 @@ def model_config(spec) -> MyModelConfig:
         num_hidden_layers=spec["layers"], num_attention_heads=spec["heads"],
         num_key_value_heads=spec["kv"], head_dim=spec["head_dim"], max_position_embeddings=2048,
         rope_theta=10000.0, rms_norm_eps=1e-6, num_experts=spec.get("experts", 4),
-        use_qk_norm=spec["qk_norm"], tie_word_embeddings=True)
+        use_qk_norm=spec["qk_norm"], tie_word_embeddings=spec.get("tie", True))
 
 
 def prompts_for(spec):
@@ -76,9 +110,9 @@ def prompts_for(spec):
             for _ in range(spec["reqs"])]
 
 
-def run_model(spec, out_name):
+def run_model(spec, out_name, make_sd=None):
     cfg = model_config(spec)
-    sd = random_state_dict(cfg, spec["arch"], spec["seed"])
+    sd = (make_sd or (lambda c, s: random_state_dict(c, spec["arch"], s)))(cfg, spec["seed"])
     with tempfile.TemporaryDirectory() as td:
         path = write_model_dir(td, cfg, spec["arch"], sd)
         import json
@@ -178,6 +212,25 @@ def make_sampling():
                         cases=np.array(cases), out=outs)
 
 
+def make_sampling_large():
+    """Kept-token masks of the reference's prepare_logits at vocabulary sizes
+    where the GPU sampler runs its radix top-p search; packed bits per case."""
+    out = {}
+    for V in LARGE_SAMPLING_VOCABS:
+        x = large_logits(V)
+        past = large_past(V)
+        logits = torch.from_numpy(x)[None]
+        masks = []
+        for t, k, p, rp in LARGE_SAMPLING_CASES:
+            got = prepare_logits(logits, t, k, p, rp, past).numpy()[0]
+            masks.append(np.packbits(~np.isinf(got)))
+        out[f"masks_{V}"] = np.stack(masks)
+        out[f"checksum_{V}"] = np.array([float(x.astype(np.float64).sum()),
+                                         float((x.astype(np.float64) ** 2).sum())])
+    np.savez_compressed(HERE / "sampling_large.npz", cases=np.array(LARGE_SAMPLING_CASES),
+                        vocabs=np.array(LARGE_SAMPLING_VOCABS), **out)
+
+
 def make_routing():
     torch.manual_seed(0)
     H, E, V, T = 32, 4, 1000, 96
@@ -224,13 +277,21 @@ def make_inl():
 
 def main():
     torch.set_num_threads(8)
-    make_mu_clamp()
-    make_paged_cache()
-    make_sampling()
-    make_routing()
-    make_inl()
-    run_model(LLAMA_TINY, "llama_tiny.npz")
-    run_model(DEEP_TINY, "deep_tiny.npz")
+    makers = {
+        "mu_clamp": make_mu_clamp,
+        "paged_cache": make_paged_cache,
+        "sampling": make_sampling,
+        "sampling_large": make_sampling_large,
+        "routing": make_routing,
+        "inl": make_inl,
+        "llama_tiny": lambda: run_model(LLAMA_TINY, "llama_tiny.npz"),
+        "deep_tiny": lambda: run_model(DEEP_TINY, "deep_tiny.npz"),
+        "llama_decisive": lambda: run_model(DECISIVE, "llama_decisive.npz", decisive_state_dict),
+    }
+    only = [n for n in ARGS.only.split(",") if n]
+    for name, make in makers.items():
+        if not only or name in only:
+            make()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -200,6 +200,39 @@ def test_paged_decode_attention(cuda, Hq, Hkv, D):
         torch.testing.assert_close(out[b].float().view(Hq, D), ref, rtol=2e-2, atol=2e-2)
 
 
+def test_decode_latches_over_long_context(cuda):
+    """A context longer than the launch was sized for is skipped with device
+    error 5 (bad index) instead of writing past its split slots; the other
+    sequences of the batch are unaffected.  Sequence 0 is the long one
+    (600 tokens = 38 blocks, 3 splits of 16 against the 2 that max_seq_len 512
+    gives), so even its unguarded writes would stay inside this workspace."""
+    from mu_b200 import _lib
+
+    k = _kern()
+    Hq, Hkv, D = 32, 8, 128
+    ctx = [600, 100, 300]
+    max_len = 512
+    assert _lib.load().muk_decode_attn_splits(len(ctx), max_len, 16) == 2
+    kc, vc, bt = _build_cache(ctx, Hkv, D, cuda, seed=17)
+    assert bt.shape[1] == 38  # the long row is inside its block-table row
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(len(ctx), Hq * D, device=cuda, generator=g).bfloat16()
+    out = torch.zeros_like(q)
+    sl = torch.tensor(ctx, dtype=torch.int32, device=cuda)
+    ws = torch.empty(k.decode_attn_workspace_size(len(ctx), Hq, D, max_len) // 4 + 4, device=cuda)
+    k.decode_attn(q, out, kc, vc, bt, sl, Hq, Hkv, D, max_len, workspace=ws)
+    assert _lib.device_error() == 5
+    assert bool((out[0] == 0).all())
+    G = Hq // Hkv
+    for b in (1, 2):
+        K, V = _gather_kv(kc, vc, bt, b, ctx[b])
+        qb = q[b].float().view(Hq, D)
+        att = torch.softmax((qb.unsqueeze(1) @ K.repeat_interleave(G, 0).transpose(1, 2))
+                            .squeeze(1) / math.sqrt(D), -1)
+        ref = (att.unsqueeze(1) @ V.repeat_interleave(G, 0)).squeeze(1)
+        torch.testing.assert_close(out[b].float().view(Hq, D), ref, rtol=2e-2, atol=2e-2)
+
+
 # one CTA per (query tile, group of G query heads sharing a KV head): G = 4
 # (32/8, and 32/4 where two CTAs share a KV head), G = 2 (4/2, 16/8), G = 1
 @pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (4, 2, 64), (32, 4, 128), (16, 8, 128),
@@ -424,7 +457,8 @@ def test_sampler_topk_topp_support_and_distribution(cuda):
     freq = torch.bincount(out.long(), minlength=V).float() / draws
     # total-variation distance of 4000 draws from the filtered softmax
     assert 0.5 * (freq - probs).abs().sum().item() < 0.08
-    # top_k disabled: radix top-p path over the full vocabulary
+    # top_k disabled: 1000 survivors, still at most 1024, so this is the exact
+    # sorted path again; the radix path runs in test_prepare_logits_large_vocab
     k.sample(logits, torch.full((draws,), temp, device=cuda),
              torch.zeros(draws, device=cuda, dtype=torch.int32),
              torch.full((draws,), P, device=cuda), torch.ones(draws, device=cuda), None,
@@ -439,6 +473,120 @@ def test_sampler_topk_topp_support_and_distribution(cuda):
     allowed2 = torch.zeros(V, dtype=torch.bool, device=cuda)
     allowed2[si[~rm]] = True
     assert bool(allowed2[out.long()].all())
+
+
+def _prepare_rows(k, cuda, x, cases, past, V):
+    """muk_prepare_logits of one logits row under each (T, top_k, top_p, rp) case."""
+    n = len(cases)
+    logits = torch.from_numpy(x).to(cuda).expand(n, V).contiguous()
+    seen = torch.zeros(n, (V + 31) // 32, device=cuda, dtype=torch.int32)
+    if past:
+        toks = torch.tensor(past, device=cuda, dtype=torch.int32)
+        for r in range(n):
+            k.mark_seen(seen, torch.full_like(toks, r), toks, V)
+    col = lambda i, dt: torch.tensor([c[i] for c in cases], device=cuda, dtype=dt)  # noqa: E731
+    out = torch.empty(n, V, device=cuda)
+    k.prepare_logits(logits, col(0, torch.float32), col(1, torch.int32), col(2, torch.float32),
+                     col(3, torch.float32), seen, out)
+    return out.cpu().numpy(), (logits, seen, col)
+
+
+def test_prepare_logits_reference_cases(cuda):
+    """GPU prepare_logits on the reference-made fixture (V = 1000, exact path):
+    same removed set, same kept values."""
+    import numpy as np
+
+    import oracle as O  # noqa: F401
+    from golden_models import G, top_p_band
+
+    k = _kern()
+    d = np.load(G / "sampling.npz")
+    cases = [tuple(c) for c in d["cases"]]
+    past = d["past"].tolist()
+    got, _ = _prepare_rows(k, cuda, d["logits"], cases, past, d["logits"].shape[0])
+    for c, (t, kk, p, rp) in enumerate(cases):
+        ref = d["out"][c]
+        band = top_p_band(d["logits"], t, int(kk), rp, past, p)
+        assert np.array_equal(np.isinf(got[c])[~band], np.isinf(ref)[~band]), c
+        fin = ~np.isinf(ref) & ~np.isinf(got[c])
+        np.testing.assert_allclose(got[c][fin], ref[fin], rtol=1e-6, atol=1e-6)
+
+
+def test_reference_api_prepare_logits_and_sample_token(cuda):
+    """mu_b200.utils.sampling.prepare_logits / sample_token, the reference's
+    single-row API (utils/sampling.py:20-120), on a CPU [1, V] tensor: the
+    processed logits equal the reference's for every fixture case, and the
+    draws of sample_token land in the kept set."""
+    import numpy as np
+
+    from golden_models import G, top_p_band
+    from mu_b200.utils.sampling import prepare_logits, sample_token
+
+    d = np.load(G / "sampling.npz")
+    past = d["past"].tolist()
+    x = torch.from_numpy(d["logits"])[None]
+    for c, (t, kk, p, rp) in enumerate(d["cases"]):
+        got = prepare_logits(x, float(t), int(kk), float(p), float(rp), past)
+        assert got.device.type == "cpu" and got.shape == x.shape
+        got = got.numpy()[0]
+        ref = d["out"][c]
+        band = top_p_band(d["logits"], t, int(kk), rp, past, p)
+        assert np.array_equal(np.isinf(got)[~band], np.isinf(ref)[~band]), c
+        fin = ~np.isinf(ref) & ~np.isinf(got)
+        np.testing.assert_allclose(got[fin], ref[fin], rtol=1e-6, atol=1e-6)
+        proc = torch.from_numpy(got)[None]
+        for s in range(8):
+            tok = sample_token(proc, True, seed=s, step=c)
+            assert np.isfinite(got[tok]), (c, s, tok)
+        assert sample_token(proc, False) == int(np.argmax(got))
+
+
+def test_prepare_logits_large_vocab(cuda):
+    """Radix top-p path (more than 1024 survivors) at V = 32000 and 128256,
+    top_k 0 or 2000, top_p 0.5 / 0.9 / 0.99, T 0.7, with and without a
+    repetition penalty.  The kept set must equal the reference's outside the
+    top-p boundary band (its float32 softmax sum moves the cut; see
+    golden_models.TOP_P_BAND) and the oracle's outside a 1e-6 band; kept
+    values are bit-identical to the penalised, temperature-scaled logits.
+    The draws of muk_sample land in the kept set and repeat exactly."""
+    import numpy as np
+
+    import oracle as O
+    from golden_models import (G, LARGE_SAMPLING_CASES, LARGE_SAMPLING_VOCABS, large_logits,
+                               large_past, top_p_band)
+
+    k = _kern()
+    d = np.load(G / "sampling_large.npz")
+    cases = list(LARGE_SAMPLING_CASES)
+    for V in LARGE_SAMPLING_VOCABS:
+        x = large_logits(V)
+        past = large_past(V)
+        got, (logits, seen, col) = _prepare_rows(k, cuda, x, cases, past, V)
+        for c, (t, kk, p, rp) in enumerate(cases):
+            ref = np.unpackbits(d[f"masks_{V}"][c])[:V].astype(bool)
+            ora = O.prepare_logits(x, t, kk, p, rp, past)
+            kept = ~np.isinf(got[c])
+            band = top_p_band(x, t, kk, rp, past, p)
+            tight = top_p_band(x, t, kk, rp, past, p, 1e-6)
+            assert np.array_equal(kept[~band], ref[~band]), (V, c)
+            assert np.array_equal(kept[~tight], ~np.isinf(ora)[~tight]), (V, c)
+            both = kept & ~np.isinf(ora)
+            assert np.array_equal(got[c][both], ora[both]), (V, c)
+            # draws: 64 seeds per case, inside the kept set, identical on repeat
+            n = 64
+            lg = logits[c:c + 1].expand(n, V).contiguous()
+            sr = torch.full((n,), c, device=cuda, dtype=torch.int32)
+            args = (lg, torch.full((n,), t, device=cuda), torch.full((n,), kk, device=cuda,
+                                                                   dtype=torch.int32),
+                    torch.full((n,), p, device=cuda), torch.full((n,), rp, device=cuda), seen,
+                    torch.arange(n, device=cuda, dtype=torch.int64),
+                    torch.full((n,), 5, device=cuda, dtype=torch.int64))
+            o1 = torch.empty(n, device=cuda, dtype=torch.int32)
+            o2 = torch.empty_like(o1)
+            k.sample(*args, o1, seen_rows=sr)
+            k.sample(*args, o2, seen_rows=sr)
+            assert torch.equal(o1, o2)
+            assert kept[o1.cpu().numpy()].all(), (V, c)
 
 
 def test_no_device_error_left(cuda):

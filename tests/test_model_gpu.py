@@ -120,6 +120,32 @@ def test_engine_greedy_continuous_batching(cuda, name):
     assert w.get_stats()["cuda_graphs"], "pure-decode steps should replay a CUDA graph"
 
 
+def test_decisive_fixture_all_greedy_tokens(cuda):
+    """llama_decisive (the reference's top-2 logit gap is above 3 at every
+    step): greedy generation through StepEngine, with continuous batching
+    (one batch slot short, so the last request joins mid-run) and CUDA-graph
+    replay of pure decode steps, reproduces all 32 reference tokens of all 8
+    requests; no near-tie exception applies."""
+    from mu_b200.core.config import SamplingParams
+    from mu_b200.serving.engine import StepEngine
+
+    w, shape, d, prompts, ec = _worker("llama_decisive", cuda, graphs=True, max_batch=7)
+    toks = d["tokens"]
+    R, n = toks.shape
+    assert float(d["top2_gap"].min()) > 1.0
+    eng = StepEngine(w, ec)
+    for r in range(R):
+        eng.add_request(prompts[r], SamplingParams(temperature=0.0, top_k=0, top_p=1.0,
+                                                   repetition_penalty=1.0, max_tokens=n), f"r{r}")
+    eng.run_to_completion()
+    for r in range(R):
+        assert eng.requests[f"r{r}"].output_token_ids == [int(t) for t in toks[r]], r
+    assert w.get_stats()["cuda_graphs"], "pure-decode steps should replay a CUDA graph"
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
+
+
 def test_sampled_generation_is_seeded(cuda):
     from mu_b200.core.config import SamplingParams
     from mu_b200.serving.engine import StepEngine

@@ -1,0 +1,151 @@
+"""Model-level parity at the benchmark configurations' real widths.
+
+Two-layer slices of the three serving workloads, with every other dimension
+of the benchmark: the Llama-3-8B shape (H 4096, 32/8 heads, head_dim 128,
+SwiGLU 14336, vocabulary 128256, RoPE theta 5e5, eps 1e-5, untied LM head)
+and the two DeepForCausalLM shapes (H 2048, 16/8 heads, 4 experts x 2816,
+vocabulary 32000; H 4096, 32/8 heads, 8 experts x 3584, vocabulary 32000;
+mu_clamp, INL dynamics and mu-guided attention on).  Weights are the
+benchmark's seeded bf16 draw; the oracle computes in fp32 from the same bf16
+values (the reference's fp32 path on a bf16 checkpoint).
+
+Six ragged requests (one of them at least 2048 tokens long, 4000 for the
+Llama shape so that theta = 5e5 RoPE runs far out) are prefilled in one flat
+step through MuWorker.execute and then decoded for 32 steps with the
+oracle's greedy tokens forced as inputs.  At every step of every request:
+  * bf16 logits within 2e-2 max-abs of the oracle's fp32 logits;
+  * block tables and sequence lengths equal to the reference allocator's;
+  * (Deep) each layer's expert ids equal to the oracle's, bit for bit;
+  * the GPU argmax equals the oracle's token wherever the oracle's top-2
+    gap exceeds 0.05 (random weights give near ties; the decisive fixture
+    in test_model_gpu.py enforces all 32 tokens without exception).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+GAP_TOL = 0.05
+N_DECODE = 32
+PROMPT_LENS = {
+    "c3": [4000, 700, 129, 33, 300, 17],
+    "c2": [512, 300, 129, 64, 33, 17],
+    "c5": [2048, 600, 129, 128, 300, 17],
+}
+
+
+def _build(name):
+    import bench
+    from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
+    from mu_b200.models.weights import random_state_dict
+    from mu_b200.serving.worker import MuWorker
+
+    wl = dict(bench.WORKLOADS[name], layers=2)
+    cfg = bench.model_config(wl)
+    sd = random_state_dict(cfg, wl["arch"], wl["seed"], device="cuda", dtype=torch.bfloat16,
+                           include_unused=False)
+    lens = PROMPT_LENS[name]
+    blocks = sum((n + N_DECODE + 15) // 16 + 1 for n in lens) + 64
+    ec = EngineConfig(model=cfg, dtype="bfloat16", mu=MuConfig(enabled=wl["mu"]),
+                      cache=CacheConfig(max_seq_len=max(lens) + N_DECODE + 16, block_size=16,
+                                        max_num_blocks=blocks, max_num_seqs=8),
+                      scheduler=SchedulerConfig(max_batch_size=8, max_num_batched_tokens=8192,
+                                                max_prefill_tokens=8192))
+    w = MuWorker(ec, "cuda")
+    w.load_state_dict(wl["arch"], cfg, sd)
+    w.use_graphs = False  # expert ids are read from eager launches
+    shape = O.ModelShape(arch=wl["arch"], hidden=wl["hidden"], layers=2, heads=wl["heads"],
+                         kv_heads=wl["kv"], head_dim=wl["head_dim"], vocab=wl["vocab"],
+                         eps=wl["eps"], theta=wl["theta"],
+                         experts=wl["experts"] if wl["arch"] == "deep" else 0,
+                         qk_norm=cfg.use_qk_norm, tie=cfg.tie_word_embeddings,
+                         max_pos=max(lens) + N_DECODE + 16)
+    params = {k: v.float().cpu().numpy() for k, v in sd.items()}
+    del sd
+    oracle = O.OracleModel(shape, params, O.MuCfg(wl["mu"]))
+    rng = np.random.default_rng(100 + wl["seed"])
+    prompts = [rng.integers(0, wl["vocab"], n).tolist() for n in lens]
+    return wl, w, oracle, prompts
+
+
+def _oracle_run(oracle, prompts, routed):
+    """Greedy decode of all requests with the batched oracle: per step the
+    logits [R, V] and (routed) the per-layer expert ids in flat order."""
+    oracle.expert_trace = [] if routed else None
+    logits, pasts, _ = oracle.forward_batch(prompts)
+    steps, experts = [logits], [oracle.expert_trace]
+    toks = [np.argmax(logits, -1)]
+    for _ in range(N_DECODE - 1):
+        oracle.expert_trace = [] if routed else None
+        logits, pasts, _ = oracle.forward_batch([[int(t)] for t in toks[-1]], pasts)
+        steps.append(logits)
+        experts.append(oracle.expert_trace)
+        toks.append(np.argmax(logits, -1))
+    return np.stack(steps, 1), np.stack(toks, 1), experts
+
+
+@pytest.mark.parametrize("name", ["c3", "c2", "c5"])
+def test_wide_model_teacher_forced(cuda, name, monkeypatch):
+    from mu_b200 import _lib
+    from mu_b200 import kernels as K
+    from mu_b200.serving.worker import WorkerRequest
+
+    wl, w, oracle, prompts = _build(name)
+    routed = wl["arch"] == "deep" and wl["experts"] > 1
+    ref_logits, ref_toks, ref_experts = _oracle_run(oracle, prompts, routed)
+    s = np.sort(ref_logits, -1)
+    gaps = s[..., -1] - s[..., -2]
+
+    seen = []
+    if routed:
+        orig = K.inl_dynamics
+
+        def traced(*a, **kw):
+            orig(*a, **kw)
+            seen.append(a[17][:kw["num_tokens"]].cpu().numpy().astype(np.int64))
+
+        monkeypatch.setattr(K, "inl_dynamics", traced)
+
+    R = len(prompts)
+    alloc = O.PagedAllocatorOracle(w.cache.max_num_blocks, 16)
+    for r in range(R):
+        assert w.allocate_request(f"r{r}") and alloc.allocate(f"r{r}")
+    worst, flips = 0.0, 0
+    for i in range(N_DECODE):
+        seen.clear()
+        if i == 0:
+            reqs = [WorkerRequest(f"r{r}", torch.tensor([prompts[r]]), is_prefill=True)
+                    for r in range(R)]
+            for r in range(R):
+                alloc.append(f"r{r}", len(prompts[r]))
+        else:
+            reqs = [WorkerRequest(f"r{r}", torch.tensor([[int(ref_toks[r, i - 1])]]),
+                                  is_prefill=False) for r in range(R)]
+            for r in range(R):
+                alloc.append(f"r{r}", 1)
+        outs = w.execute(reqs)
+        for r, o in enumerate(outs):
+            assert o.error is None, o.error
+            lg = o.logits.float().cpu().numpy().reshape(-1)
+            err = float(np.abs(lg - ref_logits[r, i]).max())
+            worst = max(worst, err)
+            assert err <= LOGIT_TOL, (name, r, i, err)
+            if gaps[r, i] > GAP_TOL:
+                assert int(np.argmax(lg)) == int(ref_toks[r, i]), (name, r, i)
+            else:
+                flips += int(np.argmax(lg)) != int(ref_toks[r, i])
+        for r in range(R):
+            assert w.cache.block_table(f"r{r}") == alloc.blocks[f"r{r}"]
+            assert w.cache.get_seq_len(f"r{r}") == alloc.seq_len(f"r{r}")
+        if routed:
+            assert len(seen) == 2 and len(ref_experts[i]) == 2
+            for l in range(2):
+                assert np.array_equal(seen[l], ref_experts[i][l]), (name, i, l)
+    assert _lib.device_error() == 0
+    print(f"{name}: worst logit max-abs {worst:.4g} over {R} requests x {N_DECODE} steps; "
+          f"{int((gaps <= GAP_TOL).sum())} near ties, {flips} flipped")

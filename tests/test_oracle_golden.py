@@ -58,6 +58,29 @@ def test_prepare_logits_cases():
         np.testing.assert_allclose(got[fin], ref[fin], rtol=1e-6, atol=1e-6)
 
 
+def test_prepare_logits_large_vocab():
+    """The oracle's kept sets at V = 32000 / 128256 equal the reference's
+    outside the top-p boundary band, and the masks are pinned to the seeded
+    logits by their checksum."""
+    from golden_models import (LARGE_SAMPLING_CASES, LARGE_SAMPLING_VOCABS, large_logits,
+                               large_past, top_p_band)
+
+    d = _load("sampling_large.npz")
+    assert tuple(d["vocabs"]) == LARGE_SAMPLING_VOCABS
+    for V in LARGE_SAMPLING_VOCABS:
+        x = large_logits(V)
+        np.testing.assert_allclose(d[f"checksum_{V}"], [x.astype(np.float64).sum(),
+                                                        (x.astype(np.float64) ** 2).sum()],
+                                   rtol=1e-12)
+        past = large_past(V)
+        for c, (t, k, p, rp) in enumerate(LARGE_SAMPLING_CASES):
+            ref = np.unpackbits(d[f"masks_{V}"][c])[:V].astype(bool)
+            got = ~np.isinf(O.prepare_logits(x, t, int(k), p, rp, past))
+            band = top_p_band(x, t, int(k), rp, past, p)
+            assert np.array_equal(ref[~band], got[~band]), (V, c)
+            assert ref.sum() > 1 and band.sum() < 0.02 * ref.sum() + 2, (V, c, band.sum())
+
+
 def test_routing():
     d = _load("routing.npz")
     E, V = int(d["num_experts"]), int(d["vocab"])
@@ -98,3 +121,31 @@ def test_oracle_model_matches_reference(name):
         for j, s in enumerate(steps):
             np.testing.assert_allclose(lg[s], d["logits"][r, j], rtol=1e-4, atol=2e-4)
         assert list(np.argmax(lg, -1)) == list(toks)
+
+
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny", "llama_decisive"])
+def test_oracle_batch_forward_equals_per_request(name):
+    """forward_batch (ragged requests, each with its own cache) gives every
+    request the logits and cache of its own batch-1 forward; the decisive
+    fixture is pinned to the reference's tokens for two requests."""
+    spec, cfg, sd, d, prompts = _tiny(name)
+    model = O.OracleModel(spec, {k: v.numpy() for k, v in sd.items()}, O.MuCfg(True))
+    singles = [model.forward(p) for p in prompts[:3]]
+    lg, pasts, _ = model.forward_batch(prompts[:3])
+    for r, (l1, p1) in enumerate(singles):
+        np.testing.assert_allclose(lg[r], l1, rtol=1e-5, atol=1e-5)
+        for (k1, v1), (k2, v2) in zip(p1, pasts[r]):
+            np.testing.assert_allclose(k2, k1, rtol=1e-5, atol=1e-5)
+            np.testing.assert_allclose(v2, v1, rtol=1e-5, atol=1e-5)
+    toks = [int(np.argmax(x)) for x in lg]
+    lg2, _, _ = model.forward_batch([[t] for t in toks], pasts)
+    for r in range(3):
+        l2, _ = model.forward([toks[r]], singles[r][1])
+        np.testing.assert_allclose(lg2[r], l2, rtol=1e-5, atol=1e-5)
+    if name == "llama_decisive":
+        for r in range(2):
+            got = O.teacher_forced_logits(model, prompts[r], d["tokens"][r])
+            assert list(np.argmax(got, -1)) == list(d["tokens"][r])
+            np.testing.assert_allclose(got[d["logit_steps"]], d["logits"][r], rtol=1e-4,
+                                       atol=2e-4)
+        assert float(d["top2_gap"].min()) > 1.0

@@ -9,8 +9,11 @@ and after the other tests.
 
 Checks, through the C ABI: two calls in a row (different contexts, so the
 second reuses scratch the first left behind) match the workspace-taking
-muk_paged_decode_attn within the attention tests' tolerance, and a shape
-needing more scratch than the array holds is rejected with a clear error.
+muk_paged_decode_attn within the attention tests' tolerance; both batches
+really split (so the static array is written and read); the first call,
+which resolves the array's device address, changes neither the caching
+allocator's count nor the device's free memory; and a shape needing more
+scratch than the array holds is rejected with a clear error.
 """
 
 import ctypes
@@ -56,14 +59,22 @@ def test_static_scratch_matches_workspace_entry_point(cuda, Hq, Hkv, D):
         mx = max(ctx)
         need = _lib.load().muk_decode_attn_workspace_size(len(ctx), Hq, D, mx, 16)
         assert 0 < need <= _lib.load().muk_decode_attn_static_scratch_bytes()
+        # the launched batch itself splits, so the static array carries partials
+        assert _lib.load().muk_decode_attn_splits(len(ctx), mx, 16) > 1
         ws = torch.empty(need // 4 + 4, device="cuda")
         ref = torch.empty_like(q)
         got = torch.full_like(q, float("nan"))
         _lib.call("muk_paged_decode_attn", *_args(q, ref, kc, vc, bt, sl, Hq, Hkv, D, mx),
                   ws.data_ptr(), ws.numel() * 4, stream)
+        torch.cuda.synchronize()
+        # The workspace call above loaded the library's device code (and with
+        # it the static array), so nothing may be allocated from here on.
+        alloc0, free0 = torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0]
         _lib.call("muk_paged_decode_attn_static", *_args(q, got, kc, vc, bt, sl, Hq, Hkv, D, mx),
                   stream)
         torch.cuda.synchronize()
+        assert torch.cuda.memory_allocated() == alloc0
+        assert torch.cuda.mem_get_info()[0] == free0
         torch.testing.assert_close(got.float(), ref.float(), rtol=2e-2, atol=2e-2)
     assert _lib.device_error() == 0
 
