@@ -143,10 +143,14 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
+    def mark(self) -> int:
+        """Index of the next sample (bracket a timed region with two marks)."""
+        return len(self.lines)
+
+    def summary(self, lo: int = 0, hi: int | None = None):
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[lo:hi]:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -544,6 +548,10 @@ def run_ours(args, rank, world, local_rank):
     while engine.scheduler.waiting:
         steady_state_step(engine, arrivals, SamplingParams)
         fill_steps += 1
+    # The clock sampler starts before the warm-up steps (its start-up would
+    # otherwise leave the GPU idle, and cooler, right before the timed
+    # region); only the samples taken inside the timed region are reported.
+    clocks = ClockSampler(local_rank).__enter__()
     for _ in range(args.warmup):
         steady_state_step(engine, arrivals, SamplingParams)
     # the engine overlaps host work with the step before: start the timed
@@ -556,14 +564,14 @@ def run_ours(args, rank, world, local_rank):
     # ---- e2e: the public step API, host work and copies included ----------
     rec = Recorder(engine, worker)
     rec.on = True
-    h2d0 = 0
     n_tok = 0
     launches0 = _lib.launch_count
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
+    try:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        clk0 = clocks.mark()
         torch.cuda.nvtx.range_push("timed")
         start.record()
         t0 = time.perf_counter()
@@ -574,6 +582,9 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+        clk1 = clocks.mark()
+    finally:
+        clocks.__exit__(None, None, None)
     launches = _lib.launch_count - launches0
     rec.on = False
     e2e_t = start.elapsed_time(end) * 1e-3
@@ -659,7 +670,7 @@ def run_ours(args, rank, world, local_rank):
         sample = cb.sample + ", mean of 5 steps"
         cpu = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
                "sample": sample}
-    clk = clocks.summary()
+    clk = clocks.summary(clk0, clk1)
     c3 = args.workload == "c3"
     par = {"tp": f"tp{tp}", "ep": f"tp{tp}+ep{tp}", "replicas": f"replicas{world}"}[args.parallel]
     line = {

@@ -41,6 +41,7 @@ class PeerAllReduce:
         self.scratch_elems = (int(lib.muk_allreduce_scratch_elems(self.max_elems, self.world))
                               + self.world * 16384 + 63) // 64 * 64
         # [data | scratch (world shares) | flags], f32; the flag area starts zeroed
+        self.flag_words = flag_words
         self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words,
                                dtype=torch.float32, device=device)
         torch.cuda.synchronize(device)
@@ -118,6 +119,13 @@ class PeerAllReduce:
                   ctypes.addressof(self._flags), self.rank, self.world,
                   torch.cuda.current_stream().cuda_stream)
         return self.buf[:M * N].view(1, M, N)
+
+    def reset_flags(self) -> None:
+        """Zero this rank's flag words (pushed / done epochs and its own
+        epoch).  Only safe while no all-reduce kernel runs on any rank: the
+        caller synchronises every rank and puts host barriers on both sides
+        (MuWorker.tp_reset)."""
+        self.buf[self.max_elems + self.scratch_elems:].zero_()
 
     def close(self) -> None:
         torch.cuda.synchronize()

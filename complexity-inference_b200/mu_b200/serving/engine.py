@@ -203,7 +203,8 @@ class StepEngine:
         (worker.py:179-206, engine.py:210-212).  Requests not in the step go
         on."""
         logger.error("step failed: %s", err)
-        if isinstance(err, _lib.DeviceError):
+        dev = getattr(self.worker, "device", None)
+        if isinstance(err, _lib.DeviceError) and getattr(dev, "type", "cuda") == "cuda":
             # read and clear the word (synchronises) so later steps start clean
             _lib.device_error()
         results: List[StepOutput] = []
@@ -317,10 +318,28 @@ class StepEngine:
         return _Launched(reqs, idx, rows, handle)
 
     def _complete(self, launched: _Launched) -> List[StepOutput]:
+        err: Optional[Exception] = None
         try:
             toks = launched.handle.wait()
         except Exception as e:  # noqa: BLE001 - a failed step fails its requests, not the engine
-            return self._fail_step(launched, e)
+            err = e
+        agree = getattr(self.worker, "tp_agree", None)
+        if agree is not None and not agree(err is None):
+            # tensor parallel: some rank could not read this step, so every
+            # rank fails it (the same requests: the schedulers are identical)
+            # and the cross-GPU flags restart together
+            res = self._fail_step(launched, err or RuntimeError(
+                "step failed on another tensor-parallel rank"))
+            # the step launched after it ran its collectives against the
+            # failed step's flags: fail it too (same decision on every rank)
+            nxt, self._inflight = self._inflight, None
+            if nxt is not None and nxt is not launched:
+                res += self._fail_step(nxt, RuntimeError(
+                    "step launched before a failed tensor-parallel step was reset"))
+            self.worker.tp_reset()
+            return res
+        if err is not None:
+            return self._fail_step(launched, err)
         results: List[StepOutput] = []
         eos = self.eos_token_id
         for req, i, tok in zip(launched.reqs, launched.idx, toks):

@@ -95,6 +95,9 @@ class MuWorker:
         self.use_graphs = True
         self._graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, int]] = {}
         self._graph_key = None
+        # host-side (gloo) group of the tensor-parallel ranks, used to agree on
+        # every step's success so that all ranks fail the same steps
+        self._agree_group = None
 
     # ---- loading ---------------------------------------------------------------
     def load_model(self, model_path: str) -> None:
@@ -152,7 +155,46 @@ class MuWorker:
             self.model.tp_group = self.tp_group or dist.group.WORLD
             if getattr(self.model, "local_experts", 0) and ep:
                 self.model.expert_lo = expert_range(model_config, rank, tp)[0]
+            if os.environ.get("MU_TP_STEP_AGREE", "1") != "0" and self._agree_group is None:
+                ranks = dist.get_process_group_ranks(self.model.tp_group)
+                self._agree_group = dist.new_group(ranks, backend="gloo")
         self._init_cache()
+
+    # ---- tensor-parallel step agreement ----------------------------------------
+    def tp_agree(self, ok: bool) -> bool:
+        """True when every tensor-parallel rank read its copy of the step's
+        results (one host-side all-reduce over gloo, no GPU work); always
+        ``ok`` on a single GPU.  A device error or peer time-out on any rank
+        thereby fails the same step, and the same requests, on all ranks, so
+        their schedulers stay identical."""
+        if self._agree_group is None:
+            return ok
+        import torch.distributed as dist
+
+        t = torch.tensor([0 if ok else 1], dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self._agree_group)
+        return int(t[0]) == 0
+
+    def tp_reset(self) -> None:
+        """After an agreed step failure: let every rank's kernels end (their
+        cross-GPU waits are bounded), clear this GPU's error word, then zero
+        the peer all-reduce flags and epoch on every rank between two host
+        barriers, so no late store from the failed step meets a later call
+        and all ranks restart their epochs together."""
+        if self._agree_group is None:
+            return
+        import torch.distributed as dist
+
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            _lib.device_error()
+        dist.barrier(group=self._agree_group)
+        comm = getattr(self.model, "comm", None)
+        if comm is not None:
+            comm.reset_flags()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self._agree_group)
 
     def _init_cache(self) -> None:
         mc, cc, sc = self.model.config, self.config.cache, self.config.scheduler

@@ -16,10 +16,21 @@ import numpy as np
 
 F32 = np.float32
 
+
+def round_bf16(x):
+    """Round float32 values to the nearest bfloat16 (ties to even), kept as float32."""
+    u = np.ascontiguousarray(x, dtype=F32).view(np.uint32)
+    r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return r.astype(np.uint32).view(F32)
+
+
+def _ident(x):
+    return x
+
 __all__ = [
     "MuCfg", "ModelShape", "mu_clamp", "soft_clamp", "rmsnorm", "rope_tables", "apply_rope",
     "sdpa", "OracleModel", "PagedAllocatorOracle", "prepare_logits", "route_experts",
-    "inl_dynamics", "greedy_generate", "teacher_forced_logits",
+    "inl_dynamics", "greedy_generate", "teacher_forced_logits", "round_bf16",
 ]
 
 
@@ -83,11 +94,13 @@ def apply_rope(x, cos, sin, pos):
     return (x * c + rot * s).astype(F32)
 
 
-def sdpa(q, k, v, causal: bool):
+def sdpa(q, k, v, causal: bool, round_p=_ident):
     """GQA via repeat_interleave + scaled dot-product attention (layers.py:706-723).
 
     q [Hq, Sq, D], k/v [Hkv, Sk, D].  ``causal`` is the reference rule
-    is_causal = (q_len == k_len); with q_len < k_len nothing is masked."""
+    is_causal = (q_len == k_len); with q_len < k_len nothing is masked.
+    ``round_p`` (bf16 emulation only) rounds the unnormalised probabilities
+    before P·V while their sum stays float32."""
     Hq, Sq, D = q.shape
     G = Hq // k.shape[0]
     k = np.repeat(k, G, axis=0)
@@ -103,8 +116,11 @@ def sdpa(q, k, v, causal: bool):
             s = np.where(mask[None], s, -np.inf)
         s = s - s.max(-1, keepdims=True)
         p = np.exp(s)
-        p = p / p.sum(-1, keepdims=True)
-        out[hs] = np.matmul(p.astype(F32), v[hs])
+        if round_p is _ident:
+            p = p / p.sum(-1, keepdims=True)
+            out[hs] = np.matmul(p.astype(F32), v[hs])
+        else:
+            out[hs] = np.matmul(round_p(p), v[hs]) / p.sum(-1, keepdims=True)
     return out
 
 
@@ -121,18 +137,21 @@ def _softplus(x):
     return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))).astype(F32)
 
 
-def inl_dynamics(h, v, p: Dict[str, np.ndarray], prefix: str, dt: float):
-    """INLDynamics.forward (layers.py:81-127).  Returns h_next, v_next, mu_contextual."""
+def inl_dynamics(h, v, p: Dict[str, np.ndarray], prefix: str, dt: float, R=_ident):
+    """INLDynamics.forward (layers.py:81-127).  Returns h_next, v_next, mu_contextual.
+
+    ``R`` (bf16 emulation only) rounds the matmul inputs: [h, v] and the
+    controller's hidden layer, and h before mu_proj."""
     H = h.shape[-1]
     if v is None:
         v = np.zeros_like(h)
-    hv = np.concatenate([h, v], -1)
-    ch = _silu(hv @ p[prefix + "controller_in.weight"].T + p[prefix + "controller_in.bias"])
+    hv = np.concatenate([R(h), R(v)], -1)
+    ch = R(_silu(hv @ p[prefix + "controller_in.weight"].T + p[prefix + "controller_in.bias"]))
     co = (ch @ p[prefix + "controller_out.weight"].T + p[prefix + "controller_out.bias"]).astype(F32)
     alpha = _sigmoid(co[:, :H])
     beta = np.minimum(_softplus(co[:, H:2 * H]), F32(2.0))
     gate = _sigmoid(co[:, 2 * H:])
-    mu_c = (p[prefix + "mu"] + h @ p[prefix + "mu_proj.weight"].T).astype(F32)
+    mu_c = (p[prefix + "mu"] + R(h) @ p[prefix + "mu_proj.weight"].T).astype(F32)
     v_next = np.clip(alpha * v - beta * (h - mu_c), -10.0, 10.0).astype(F32)
     h_next = (h + F32(dt) * gate * v_next).astype(F32)
     return h_next, v_next, mu_c
@@ -177,7 +196,16 @@ class OracleModel:
     logits and the grown cache.  past is a list of (K, V) [Hkv, P, D] or None.
     """
 
-    def __init__(self, shape: ModelShape, params: Dict[str, np.ndarray], mu: MuCfg):
+    def __init__(self, shape: ModelShape, params: Dict[str, np.ndarray], mu: MuCfg,
+                 bf16_activations: bool = False):
+        """``bf16_activations``: emulate a bf16 engine (not the reference):
+        round to bfloat16 every value such an engine stores as bf16 between
+        its f32-accumulating matmuls (matmul inputs, q/k after RoPE and v as
+        cached, attention probabilities before P·V, the attention output,
+        the final norm).  The residual stream and all accumulations stay
+        float32.  Used by tests to measure the rounding floor of bf16
+        activations at a given width."""
+        self.R = round_bf16 if bf16_activations else _ident
         self.s = shape
         # set to a list to record each routed layer's expert ids per forward
         self.expert_trace: Optional[List[np.ndarray]] = None
@@ -192,9 +220,12 @@ class OracleModel:
         new tokens back to back (segs = (start, length) per request), pasts
         their caches.  Projections are row-wise, so they run on all rows at
         once; RoPE positions and SDPA are per request (layers.py:626-741)."""
-        s, p = self.s, self.p
+        s, p, R = self.s, self.p, self.R
         pre = f"layers.{l}.self_attn."
         T = x.shape[0]
+        x = R(x)
+        if mu_prev is not None:
+            mu_prev = R(mu_prev)
         k = x @ p[pre + "k_proj.weight"].T
         q = x @ p[pre + "q_proj.weight"].T
         v = x @ p[pre + "v_proj.weight"].T
@@ -213,15 +244,15 @@ class OracleModel:
         for (a, S), past in zip(segs, pasts):
             past_len = 0 if past is None else past[0].shape[1]
             pos = np.arange(past_len, past_len + S)
-            qr = apply_rope(q[a:a + S], self.cos, self.sin, pos)
-            kr = apply_rope(k[a:a + S], self.cos, self.sin, pos)
+            qr = R(apply_rope(q[a:a + S], self.cos, self.sin, pos))
+            kr = R(apply_rope(k[a:a + S], self.cos, self.sin, pos))
             K = kr.transpose(1, 0, 2)
-            V = v[a:a + S].transpose(1, 0, 2)
+            V = R(v[a:a + S]).transpose(1, 0, 2)
             if past is not None:
                 K = np.concatenate([past[0], K], 1)
                 V = np.concatenate([past[1], V], 1)
-            orow = sdpa(qr.transpose(1, 0, 2), K, V, causal=(S == K.shape[1]))
-            o[a:a + S] = orow.transpose(1, 0, 2).reshape(S, -1)
+            orow = sdpa(qr.transpose(1, 0, 2), K, V, causal=(S == K.shape[1]), round_p=R)
+            o[a:a + S] = R(orow.transpose(1, 0, 2).reshape(S, -1))
             kvs.append((K, V))
         out = _clamp((o @ p[pre + "o_proj.weight"].T).astype(F32), self.mu)
         return out, kvs
@@ -240,15 +271,18 @@ class OracleModel:
             # layers.py:534-547 gathers each token's expert weights and runs a
             # per-token bmm; tokens are independent, so the rows of one
             # expert are computed together here (same products, one matmul)
+            xr = self.R(x)
             for ex in np.unique(e):
                 rows = np.nonzero(e == ex)[0]
-                gu = x[rows] @ gu_w[ex]
-                inter = _silu(gu[:, :I]) * gu[:, I:]
+                gu = xr[rows] @ gu_w[ex]
+                inter = self.R(_silu(gu[:, :I]) * gu[:, I:])
                 out[rows] = inter @ d_w[ex]
             return _clamp(out.astype(F32), self.mu)
-        gate = _silu(x @ p[pre + "gate_proj.weight"].T)
-        up = x @ p[pre + "up_proj.weight"].T
-        return _clamp(((gate * up) @ p[pre + "down_proj.weight"].T).astype(F32), self.mu)
+        xr = self.R(x)
+        gate = _silu(xr @ p[pre + "gate_proj.weight"].T)
+        up = xr @ p[pre + "up_proj.weight"].T
+        act = self.R(gate * up)
+        return _clamp((act @ p[pre + "down_proj.weight"].T).astype(F32), self.mu)
 
     def forward(self, ids: Sequence[int], past=None, return_hidden: bool = False):
         """One request: last-token logits [V] and its grown cache."""
@@ -286,7 +320,8 @@ class OracleModel:
             for r, kv in enumerate(kvs):
                 new_past[r].append(kv)
             if s.arch == "deep":  # deep.py:151-176
-                h_next, v_state, mu_cur = inl_dynamics(attn, v_state, p, pre + "dynamics.", s.dt)
+                h_next, v_state, mu_cur = inl_dynamics(attn, v_state, p, pre + "dynamics.", s.dt,
+                                                       self.R)
                 h = res + h_next
                 res = h
                 x2 = rmsnorm(h, p[pre + "post_attention_layernorm.weight"], s.eps, mu)
@@ -300,7 +335,7 @@ class OracleModel:
                 h = _clamp(res + self._mlp(l, x2, ids, None), mu)
         hn = rmsnorm(h, p["norm.weight"], s.eps, mu)
         last = np.array([a + n - 1 for a, n in segs])
-        logits = (hn[last] @ p["lm_head.weight"].T).astype(F32)
+        logits = (self.R(hn[last]) @ p["lm_head.weight"].T).astype(F32)
         return logits, new_past, hn
 
 

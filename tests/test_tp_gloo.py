@@ -243,3 +243,94 @@ def test_sharded_safetensors_load(tmp_path, name, ep):
         assert gcfg == wcfg and sorted(got) == sorted(want)
         for k in want:
             assert torch.equal(got[k], want[k]), k
+
+
+def _agree_worker(rank, world, port, q, fail_rank, fail_at):
+    """One tensor-parallel rank of the CPU stand-in engine (test_engine_overlap's
+    fake worker and sampler) with MuWorker's step agreement over gloo; the
+    sampler of ``fail_rank`` raises a device error when the ``fail_at``-th
+    step is read back."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, f"init failed: {e!r}"))
+        return
+    try:
+        import test_engine_overlap as T
+        from mu_b200 import _lib
+        from mu_b200.core.config import CacheConfig, EngineConfig, SamplingParams, SchedulerConfig
+        from mu_b200.serving import engine as E
+        from mu_b200.serving.worker import MuWorker
+
+        class _Bad:
+            def __init__(self, toks):
+                self.dev = torch.tensor(toks, dtype=torch.int32)
+
+            def wait(self):
+                raise _lib.DeviceError(5, "sampled step")
+
+        class Sampler(T.FakeSampler):
+            n = 0
+
+            def launch(self, logits, ids, params, steps, token_rows=None, input_ids=None,
+                       num_tokens=0):
+                Sampler.n += 1
+                if rank == fail_rank and Sampler.n == fail_at:
+                    return _Bad(logits)
+                return T._Handle(logits)
+
+        E.BatchSampler = Sampler
+        resets = []
+        w = T.FakeWorker(64)
+        w._agree_group = dist.group.WORLD
+        w.tp_agree = MuWorker.tp_agree.__get__(w)
+        w.tp_reset = lambda: (resets.append(1), MuWorker.tp_reset(w))
+        ec = EngineConfig(cache=CacheConfig(block_size=4, max_num_blocks=64, max_num_seqs=4),
+                          scheduler=SchedulerConfig(max_batch_size=4, max_num_batched_tokens=64,
+                                                    max_prefill_tokens=64))
+        eng = E.StepEngine(w, ec, overlap=True)
+        rng = np.random.default_rng(5)
+        for i in range(6):
+            eng.add_request(rng.integers(0, T.V, int(rng.integers(3, 9))).tolist(),
+                            SamplingParams(temperature=0.0, max_tokens=8), f"r{i}")
+        reasons = {}
+        while eng.has_unfinished():
+            for o in eng.step():
+                if o.finished:
+                    reasons[o.request_id] = o.finish_reason
+        out = {rid: (reasons.get(rid), list(r.output_token_ids)) for rid, r in eng.requests.items()}
+        q.put((rank, (out, len(resets))))
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_step_failure_is_agreed_across_ranks():
+    """A device error read back on one tensor-parallel rank fails the same
+    step (and the one launched after it) on every rank: both ranks finish
+    the same requests with "error", reset their cross-GPU flags once, and
+    generate identical tokens for every other request."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, world, port, q, 1, 4))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert not isinstance(got[r], str), got[r]
+    (out0, resets0), (out1, resets1) = got[0], got[1]
+    assert out0 == out1
+    assert resets0 == resets1 == 1
+    errs = [rid for rid, (reason, _) in out0.items() if reason == "error"]
+    assert errs and len(errs) < len(out0)
+    assert all(reason in ("length", "stop") for rid, (reason, _) in out0.items() if rid not in errs)
