@@ -825,6 +825,90 @@ def run_micro(args):
             K.gemm_qkv_rope(A, B, qo, pos, slots, cos, sin, Hq, Hkv, D, kc, vc)
         byts = 2.0 * M * N * Kd
         res.update(M=M, N=N, K=Kd, flops=byts, plan=K.gemm_plan_info(M, N, Kd, K.MUK_EPI_ROPE_KV))
+    elif args.micro == "norm":
+        # residual + RMSNorm (+ bf16 out) over a step's rows, H = args.k
+        T, H = args.m, args.k
+        resid = torch.randn(T, H, device="cuda", generator=g)
+        part = torch.randn(1, T, H, device="cuda", generator=g)
+        w = torch.ones(H, device="cuda")
+        out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+
+        def fn():
+            K.residual_rmsnorm(resid, part, w, 1e-5, out)
+        byts = float(T * H * (4 + 4 + 4 + 2))  # partial + resid read, resid + out written
+        res.update(T=T, H=H, algorithmic_bytes=byts)
+    elif args.micro == "inl":
+        # INL dynamics row kernel of a Deep step (post-norm and routing fused), H = args.k
+        T, H, E, V = args.m, args.k, 8, 32000
+        h = torch.randn(T, H, device="cuda", generator=g)
+        ctrl = torch.randn(T, 3 * H, device="cuda", generator=g)
+        cb = torch.randn(3 * H, device="cuda", generator=g)
+        mp = torch.randn(T, H, device="cuda", generator=g) * 0.1
+        mu_param = torch.zeros(H, device="cuda")
+        v = torch.randn(T, H, device="cuda", generator=g)
+        resid = torch.randn(T, H, device="cuda", generator=g)
+        router = (torch.randn(E, H, device="cuda", generator=g) * 0.02).bfloat16()
+        ids = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
+        w = torch.ones(H, device="cuda")
+        v_bf = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+        mu_out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+        nout = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+        eids = torch.empty(T, device="cuda", dtype=torch.int32)
+        cl = K.Clamp(True)
+
+        def fn():
+            K.inl_dynamics(h, ctrl, cb, mp, mu_param, 0.1, v, v_bf, resid, mu_out, w, 1e-6, nout,
+                           ids, router, E, V, eids, cl)
+        # f32 in: h, ctrl (3H), muproj, v, resid; out: v, resid f32 + v, mu, norm bf16
+        byts = float(T * H * (4 * 7 + 4 * 2 + 2 * 3))
+        res.update(T=T, H=H, algorithmic_bytes=byts)
+    elif args.micro == "route":
+        # stable expert sort of a step's tokens, then the row gather (H = args.k)
+        T, H, E = args.m, args.k, 8
+        eids = torch.randint(0, E, (T,), device="cuda", generator=g, dtype=torch.int32)
+        offs = torch.zeros(E + 1, device="cuda", dtype=torch.int32)
+        perm = torch.empty(T, device="cuda", dtype=torch.int32)
+        inv = torch.empty(T, device="cuda", dtype=torch.int32)
+        x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+        xs = torch.empty_like(x)
+
+        def fn():
+            K.route_permute(eids, E, offs, perm, inv)
+            K.gather_rows(x, perm, xs)
+        byts = float(T * H * 2 * 2)
+        res.update(T=T, H=H, algorithmic_bytes=byts)
+    elif args.micro == "grouped_gemm":
+        # a Deep step's expert gate|up GEMM (SwiGLU epilogue): T rows spread evenly over
+        # E experts, per-expert width args.n (gate + up), K = args.k
+        T, E, N2, Kd = args.m, 8, args.n, args.k
+        counts = [T // E + (1 if e < T % E else 0) for e in range(E)]
+        offs = torch.tensor(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32),
+                            device="cuda")
+        A = torch.randn(T, Kd, device="cuda", generator=g).bfloat16()
+        W = (torch.randn(E * N2, Kd, device="cuda", generator=g) * 0.02).bfloat16()
+        C = torch.empty(T, N2 // 2, device="cuda", dtype=torch.bfloat16)
+
+        def fn():
+            K.grouped_gemm(A, W, C, offs, E, N2, K.MUK_EPI_SWIGLU)
+        byts = 2.0 * T * N2 * Kd
+        res.update(T=T, E=E, N=N2, K=Kd, flops=byts)
+    elif args.micro == "sampler":
+        # one sampling launch over [B, V] f32 logits: greedy (--k 0) or top-p 0.9 at T 0.7
+        B, V = args.m, args.n
+        logits = torch.randn(B, V, device="cuda", generator=g) * 2.5
+        greedy = args.k == 0
+        temp = torch.full((B,), 0.0 if greedy else 0.7, device="cuda")
+        tk = torch.zeros(B, device="cuda", dtype=torch.int32)
+        tp = torch.full((B,), 1.0 if greedy else 0.9, device="cuda")
+        rp = torch.ones(B, device="cuda")
+        seeds = torch.arange(B, device="cuda", dtype=torch.int64)
+        out = torch.empty(B, device="cuda", dtype=torch.int32)
+
+        def fn():
+            K.sample(logits, temp, tk, tp, rp, None, seeds, seeds, out)
+        byts = float(B * V * 4)
+        res.update(B=B, V=V, mode="greedy" if greedy else "top_p 0.9, T 0.7",
+                   algorithmic_bytes=byts)
     else:
         M, N, Kd = args.m, args.n, args.k
         A = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
@@ -848,7 +932,7 @@ def run_micro(args):
     torch.cuda.synchronize()
     t = s.elapsed_time(e) / args.reps * 1e-3
     res["us_per_launch"] = t * 1e6
-    if args.micro == "decode_attn":
+    if "algorithmic_bytes" in res:
         res["GBps"] = byts / t / 1e9
     else:
         res["TFLOPs"] = byts / t / 1e12
@@ -871,7 +955,8 @@ def main():
                          "workloads c2/c5), or independent replicas")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3",
                     help="c3 (default, the headline), c2 / c5 (DeepForCausalLM)")
-    ap.add_argument("--micro", choices=["decode_attn", "gemm", "prefill_attn", "qkv_rope"],
+    ap.add_argument("--micro", choices=["decode_attn", "gemm", "prefill_attn", "qkv_rope", "norm",
+                                        "inl", "route", "grouped_gemm", "sampler"],
                     default=None,
                     help="time one kernel on a small case (for ncu captures)")
     ap.add_argument("--seqs", type=int, default=64)

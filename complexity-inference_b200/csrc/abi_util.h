@@ -2,6 +2,7 @@
 // thread-local last-error message and argument checks.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
@@ -32,6 +33,12 @@ inline cudaError_t smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>&
   if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_release);
   return e;
 }
+
+// 2-D bf16 TMA map over a row-major [rows][inner] array with row stride `ld`
+// elements: box {box_inner, box_rows}, 128-byte swizzle (box_inner * 2 must
+// be 128), no out-of-bounds fill.  Returns MUK_OK or MUK_ERR_CUDA (message set).
+int tma_map_bf16_2d(CUtensorMap* map, const void* ptr, int64_t ld, int64_t inner, int64_t rows,
+                    int box_inner, int box_rows);
 
 // Returns MUK_ERR_CUDA (with the message) if the last launch failed.
 int check_launch(const char* what);

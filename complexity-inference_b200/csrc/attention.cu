@@ -676,12 +676,28 @@ static int launch_prefill_g(const void* q, int64_t q_stride, void* out, int64_t 
 // prompts, with identical outputs (more, smaller CTAs on the causal
 // triangle).  With 2 heads, 2 warps (32 rows) per head when 4-warp tiles
 // would leave SMs idle.
+namespace muk {
+// tcgen05 kernel for head_dim 128 (prefill_tc.cu)
+bool prefill_tc_supported(int head_dim, int num_q_heads, int num_kv_heads);
+int launch_prefill_tc(const void* q, int64_t q_stride, void* out, int64_t out_stride,
+                      const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                      int bt_stride, const int32_t* seq_lens, const int32_t* cu_q, int num_seqs,
+                      int max_q_len, int num_q_heads, int num_kv_heads, int num_blocks,
+                      float scale, cudaStream_t stream);
+}  // namespace muk
+
 template <int D>
 static int launch_prefill(const void* q, int64_t q_stride, void* out, int64_t out_stride,
                           const void* k_cache, const void* v_cache, const int32_t* block_tables,
                           int bt_stride, const int32_t* seq_lens, const int32_t* cu_q,
                           int num_seqs, int max_q_len, int num_q_heads, int num_kv_heads,
                           int num_blocks, float scale, cudaStream_t stream) {
+  // head_dim 128 runs on the tensor cores (tcgen05 + TMEM, 16-byte row stores)
+  if (D == 128 && prefill_tc_supported(D, num_q_heads, num_kv_heads) && out_stride % 8 == 0 &&
+      MUK_ALIGNED16(out))
+    return launch_prefill_tc(q, q_stride, out, out_stride, k_cache, v_cache, block_tables,
+                             bt_stride, seq_lens, cu_q, num_seqs, max_q_len, num_q_heads,
+                             num_kv_heads, num_blocks, scale, stream);
   const int gs = num_q_heads / num_kv_heads;
   const int G = gs % 4 == 0 ? 4 : (gs % 2 == 0 ? 2 : 1);
   const long ctas64 = (long)((max_q_len + 63) / 64) * (num_q_heads / G) * num_seqs;

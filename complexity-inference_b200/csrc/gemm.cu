@@ -959,6 +959,29 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t ld, int K, int ro
   return MUK_OK;
 }
 
+}  // namespace muk
+
+int muk::tma_map_bf16_2d(CUtensorMap* map, const void* ptr, int64_t ld, int64_t inner,
+                         int64_t rows, int box_inner, int box_rows) {
+  if (get_encode() != MUK_OK) return MUK_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed (%d): ld=%lld inner=%lld rows=%lld", (int)r,
+                   (long long)ld, (long long)inner, (long long)rows);
+    return MUK_ERR_CUDA;
+  }
+  return MUK_OK;
+}
+
+namespace muk {
+
 // SM count of the current device (cached per device).
 static int sm_count() {
   static int cache[64] = {0};
