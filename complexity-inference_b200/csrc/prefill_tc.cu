@@ -81,6 +81,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int co
   return __all_sync(0xffffffffu, ok);
 }
 
+// 2^x with one MUFU op (PTX ex2.approx, ~2 ulp); the probabilities are rounded
+// to bf16 right after, so the approximation is far below what they keep.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const TcArgs a) {
@@ -146,37 +154,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------
-    if (lane == 0) {
-      const int64_t head_rows = (int64_t)a.num_kv_heads * kTcBlk;
-      int pad = __ldg(bt);
-      if (pad < 0 || pad >= a.num_blocks) {
-        set_device_error(kDevBadIndex);
-        pad = 0;
+    // Lanes 0-7 read the tile's eight block ids together (before the wait for
+    // a free stage, so their latency hides behind it); lane 0 issues the TMAs.
+    constexpr int kBpt = kTcKeys / kTcBlk;  // blocks per tile
+    const int64_t head_rows = (int64_t)a.num_kv_heads * kTcBlk;
+    int pad = __ldg(bt);
+    if (pad < 0 || pad >= a.num_blocks) {
+      if (lane == 0) set_device_error(kDevBadIndex);
+      pad = 0;
+    }
+    for (int t = 0; t < nt; ++t) {
+      int my = pad;
+      if (lane < kBpt) {
+        const int blk = t * kBpt + lane;
+        // blocks past the last key load a real block (finite data, masked)
+        my = blk < nblk ? __ldg(bt + blk) : pad;
+        if (my < 0 || my >= a.num_blocks) {
+          set_device_error(kDevBadIndex);
+          my = pad;
+        }
       }
-      for (int t = 0; t < nt; ++t) {
-        const int s = t % kTcStages;
-        if (!mbar_wait(&kv_empty[s], ((t / kTcStages) & 1u) ^ 1u, kDevTimeoutEmpty)) break;
+      const int s = t % kTcStages;
+      if (!warp_wait(&kv_empty[s], ((t / kTcStages) & 1u) ^ 1u, kDevTimeoutEmpty)) break;
+      int ys[kBpt];
+#pragma unroll
+      for (int i = 0; i < kBpt; ++i)
+        ys[i] = (int)((int64_t)__shfl_sync(0xffffffffu, my, i) * head_rows + (int64_t)kvh * kTcBlk);
+      if (lane == 0) {
         mbar_arrive_expect_tx(&kv_full[s], (uint32_t)TcLayout::kStage);
         const uint32_t st = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kStage);
-        for (int i = 0; i < kTcKeys / kTcBlk; ++i) {
-          const int blk = t * (kTcKeys / kTcBlk) + i;
-          // blocks past the last key load a real block (finite data, masked)
-          int phys = blk < nblk ? __ldg(bt + blk) : pad;
-          if (phys < 0 || phys >= a.num_blocks) {
-            set_device_error(kDevBadIndex);
-            phys = pad;
-          }
-          const int y = (int)((int64_t)phys * head_rows + (int64_t)kvh * kTcBlk);
+#pragma unroll
+        for (int i = 0; i < kBpt; ++i) {
 #pragma unroll
           for (int pn = 0; pn < 2; ++pn) {
             const uint32_t off = (uint32_t)(pn * kTcPanel + i * kTcBlk * 128);
-            tma_load_2d(st + off, &tmK, &kv_full[s], pn * 64, y);
-            tma_load_2d(st + 2 * kTcPanel + off, &tmV, &kv_full[s], pn * 64, y);
+            tma_load_2d(st + off, &tmK, &kv_full[s], pn * 64, ys[i]);
+            tma_load_2d(st + 2 * kTcPanel + off, &tmV, &kv_full[s], pn * 64, ys[i]);
           }
         }
       }
+      __syncwarp();
     }
-    __syncwarp();
   } else if (warp == 1) {
     // ---- MMA issuer ---------------------------------------------------------
     if (lane == 0) {
@@ -258,16 +276,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
+      // raw scores of this row: four 32-column loads, one wait
       float sv[kTcKeys];
       {
-        uint32_t rr[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld_32x32b_x32(lane_base + (uint32_t)((t & 1) * kTcKeys + c * 32), rr);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]) * a.scale_log2;
-        }
+        uint32_t (&r4)[4][32] = *reinterpret_cast<uint32_t(*)[4][32]>(sv);
+        const uint32_t ta = lane_base + (uint32_t)((t & 1) * kTcKeys);
+        tmem_ld_32x32b_x32(ta, r4[0]);
+        tmem_ld_32x32b_x32(ta + 32, r4[1]);
+        tmem_ld_32x32b_x32(ta + 64, r4[2]);
+        tmem_ld_32x32b_x32(ta + 96, r4[3]);
+        tmem_ld_wait();
       }
       const int k0 = t * kTcKeys;
       if (k0 + kTcKeys - 1 > row_min_limit) {     // the tile reaches past some row's limit
@@ -275,19 +293,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < kTcKeys; ++i)
           if (k0 + i > limit) sv[i] = -INFINITY;
       }
-      float mt = -INFINITY;
+      float mraw = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kTcKeys; ++i) mt = fmaxf(mt, sv[i]);
+      for (int i = 0; i < kTcKeys; ++i) mraw = fmaxf(mraw, sv[i]);
+      const float mt = mraw * a.scale_log2;       // scale > 0: max commutes with it
       float corr = 1.f;
       if (mt > m_used + 8.f) {                    // also true on the first unmasked tile
-        corr = m_used == -INFINITY ? 0.f : exp2f(m_used - mt);
+        corr = m_used == -INFINITY ? 0.f : fast_exp2(m_used - mt);
         m_used = mt;
       }
       const float mu = m_used == -INFINITY ? 0.f : m_used;
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < kTcKeys; ++i) {
-        sv[i] = exp2f(sv[i] - mu);
+        sv[i] = fast_exp2(fmaf(sv[i], a.scale_log2, -mu));
         sum += sv[i];
       }
       l = l * corr + sum;
