@@ -13,9 +13,11 @@
 // walked in tiles of 128 (eight 16-token paged blocks).
 //
 // Warp roles (6 warps):
-//   warp 0    TMA producer: per key tile, 32 two-kilobyte boxes (8 blocks x
-//             2 column panels x K and V) from the layer's pool into a 2-deep
-//             ring, 128-byte swizzled, completion on the stage's mbarrier.
+//   warp 0    TMA producer: K_0, V_0, K_1, V_1, ... each 16 two-kilobyte
+//             boxes (8 blocks x 2 column panels) from the layer's pool into a
+//             5-slot ring, 128-byte swizzled, completion on the slot's
+//             mbarrier.  K_t's slot frees as soon as S_t is computed, so the
+//             loads run one and a half key tiles ahead of the MMAs.
 //   warp 1    TMEM owner and MMA issuer (one thread):
 //               S_j  = Q · K_jᵀ    (tcgen05.mma M128 N128 K128, both K-major)
 //               O   += P_j · V_j   (A = P from shared memory, B = V MN-major)
@@ -47,18 +49,19 @@ constexpr int kTcD = 128;           // head_dim
 constexpr int kTcRows = 128;        // query rows per CTA
 constexpr int kTcKeys = 128;        // keys per tile
 constexpr int kTcBlk = 16;          // tokens per paged block
-constexpr int kTcStages = 2;        // K/V ring depth
+constexpr int kTcSlots = 5;         // ring of K / V tiles (K_0 V_0 K_1 V_1 ...)
 constexpr int kTcThreads = 192;
 constexpr int kTcPanel = 128 * 128;  // [128 rows][64 bf16] = 16 KB, one swizzled column panel
 
 struct TcLayout {
   static constexpr int kQ = 0;                          // 2 panels
-  static constexpr int kKV = kQ + 2 * kTcPanel;         // stage s: K (2 panels), V (2 panels)
-  static constexpr int kStage = 4 * kTcPanel;
-  static constexpr int kP = kKV + kTcStages * kStage;   // 2 panels
-  static constexpr int kBar = kP + 2 * kTcPanel;
-  static constexpr int kBytes = kBar + 128 + 1024;      // barriers + slot, 1024-B alignment slack
+  static constexpr int kP = kQ + 2 * kTcPanel;          // 2 panels
+  static constexpr int kKV = kP + 2 * kTcPanel;         // slot s: one K or V tile (2 panels)
+  static constexpr int kSlot = 2 * kTcPanel;
+  static constexpr int kBar = kKV + kTcSlots * kSlot;
+  static constexpr int kBytes = kBar + 192 + 1024;      // barriers + slot, 1024-B alignment slack
 };
+static_assert(TcLayout::kBytes <= 232448, "prefill tile exceeds 227 KB of shared memory");
 
 struct TcArgs {
   const __nv_bfloat16* q;
@@ -97,8 +100,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* basep = smem_raw + (base - raw);
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(basep + TcLayout::kBar);
-  uint64_t* kv_empty = kv_full + kTcStages;
-  uint64_t* s_full = kv_empty + kTcStages;   // [2]
+  uint64_t* kv_empty = kv_full + kTcSlots;
+  uint64_t* s_full = kv_empty + kTcSlots;    // [2]
   uint64_t* q_full = s_full + 2;
   uint64_t* p_full = q_full + 1;
   uint64_t* o_done = p_full + 1;
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int32_t* bt = a.block_tables + (int64_t)b * a.bt_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < kTcSlots; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
@@ -163,7 +166,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) set_device_error(kDevBadIndex);
       pad = 0;
     }
-    for (int t = 0; t < nt; ++t) {
+    bool ok = true;
+    for (int t = 0; ok && t < nt; ++t) {
       int my = pad;
       if (lane < kBpt) {
         const int blk = t * kBpt + lane;
@@ -174,26 +178,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           my = pad;
         }
       }
-      const int s = t % kTcStages;
-      if (!warp_wait(&kv_empty[s], ((t / kTcStages) & 1u) ^ 1u, kDevTimeoutEmpty)) break;
       int ys[kBpt];
 #pragma unroll
       for (int i = 0; i < kBpt; ++i)
         ys[i] = (int)((int64_t)__shfl_sync(0xffffffffu, my, i) * head_rows + (int64_t)kvh * kTcBlk);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&kv_full[s], (uint32_t)TcLayout::kStage);
-        const uint32_t st = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kStage);
 #pragma unroll
-        for (int i = 0; i < kBpt; ++i) {
+      for (int kv = 0; kv < 2; ++kv) {            // item 2t (K_t), then 2t + 1 (V_t)
+        const int it = 2 * t + kv;
+        const int s = it % kTcSlots;
+        if (!warp_wait(&kv_empty[s], ((it / kTcSlots) & 1u) ^ 1u, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const CUtensorMap* map = kv == 0 ? &tmK : &tmV;
+          mbar_arrive_expect_tx(&kv_full[s], (uint32_t)TcLayout::kSlot);
+          const uint32_t st = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kSlot);
 #pragma unroll
-          for (int pn = 0; pn < 2; ++pn) {
-            const uint32_t off = (uint32_t)(pn * kTcPanel + i * kTcBlk * 128);
-            tma_load_2d(st + off, &tmK, &kv_full[s], pn * 64, ys[i]);
-            tma_load_2d(st + 2 * kTcPanel + off, &tmV, &kv_full[s], pn * 64, ys[i]);
+          for (int i = 0; i < kBpt; ++i) {
+#pragma unroll
+            for (int pn = 0; pn < 2; ++pn)
+              tma_load_2d(st + (uint32_t)(pn * kTcPanel + i * kTcBlk * 128), map, &kv_full[s],
+                          pn * 64, ys[i]);
           }
         }
+        __syncwarp();
       }
-      __syncwarp();
     }
   } else if (warp == 1) {
     // ---- MMA issuer ---------------------------------------------------------
@@ -204,10 +214,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t sp = base + TcLayout::kP;
       bool ok = mbar_wait(q_full, 0, kDevTimeoutFull);
       auto mma_s = [&](int t) -> bool {  // S_t = Q · K_tᵀ
-        const int s = t % kTcStages;
-        if (!mbar_wait(&kv_full[s], (t / kTcStages) & 1u, kDevTimeoutFull)) return false;
+        const int it = 2 * t, s = it % kTcSlots;
+        if (!mbar_wait(&kv_full[s], (it / kTcSlots) & 1u, kDevTimeoutFull)) return false;
         tc_fence_after();
-        const uint32_t sk = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kStage);
+        const uint32_t sk = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kSlot);
         const uint32_t d = tmem + (uint32_t)((t & 1) * kTcKeys);
 #pragma unroll
         for (int k = 0; k < kTcD / 16; ++k) {
@@ -216,16 +226,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      k > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[t & 1]);
+        tc_commit(&kv_empty[s]);         // K_t is no longer needed
         return true;
       };
       if (ok) ok = mma_s(0);
       for (int t = 0; ok && t < nt; ++t) {
         if (t + 1 < nt && !mma_s(t + 1)) break;
+        const int itv = 2 * t + 1, s = itv % kTcSlots;
+        if (!mbar_wait(&kv_full[s], (itv / kTcSlots) & 1u, kDevTimeoutFull)) break;
         if (!mbar_wait(p_full, t & 1u, kDevTimeoutFull)) break;
         tc_fence_after();
         // O += P_t · V_t: K = keys; V is [key][d] (MN-major B, 2 column panels)
-        const int s = t % kTcStages;
-        const uint32_t sv = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kStage + 2 * kTcPanel);
+        const uint32_t sv = base + (uint32_t)(TcLayout::kKV + s * TcLayout::kSlot);
         const uint32_t d = tmem + 2u * kTcKeys;
 #pragma unroll
         for (int k = 0; k < kTcKeys / 16; ++k) {
