@@ -177,6 +177,71 @@ __global__ void __launch_bounds__(kArThreads) allreduce_finish_kernel(const ArAr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Expert-parallel combine: every rank holds every token (head-parallel
+// attention), routes them identically and computes only its own experts'
+// rows, which sit at the same expert-sorted row indices on every rank.  The
+// combine copies each rank's rows [offs[e_lo], offs[e_hi]) (bf16) into the
+// same rows of every peer's buffer, so afterwards every rank holds all T
+// expert outputs.  NVLink carries stores only: (P-1) x the rank's rows out.
+//   push    (a) announce "arrived" for this call to every peer and wait until
+//           every peer has arrived too: each rank launches the push after the
+//           kernels that consumed the previous call's rows, so no store below
+//           can overwrite rows a peer still reads; (b) store the rows; (c) the
+//           last CTA signals "pushed".
+//   finish  one CTA waits for every peer's "pushed" and bumps the epoch.
+// The epoch lives in the flag area (its own words, apart from the all-reduce
+// ones), so the pair is graph-capturable.  Every wait is bounded.
+constexpr int kFlagGPushed = 24;   // [kMaxRanks] "pushed" epochs by source rank
+constexpr int kFlagGArrived = 32;  // [kMaxRanks] "arrived" epochs by source rank
+constexpr int kFlagGEpoch = 40;
+constexpr int kFlagArrive3 = 41;
+constexpr int kGatherThreads = 512;
+
+struct GatherArgs {
+  uint4* data[kMaxRanks];     // each rank's row buffer (as mapped here), [rows][row_u4]
+  uint32_t* flags[kMaxRanks];
+  const int32_t* offs;        // expert offsets in the sorted order, [E + 1]
+  int e_lo, e_hi;             // this rank's experts
+  int rank, world;
+  int row_u4;                 // 16-byte units per row
+};
+
+__global__ void __launch_bounds__(kGatherThreads) ep_gather_push_kernel(const GatherArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagGEpoch) + 1u;
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0)
+      for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagGArrived + a.rank, epoch);
+    ok = wait_all(my, kFlagGArrived, a.world, epoch);
+  }
+  __syncthreads();
+  if (ok) {
+    const int64_t lo = (int64_t)a.offs[a.e_lo] * a.row_u4;
+    const int64_t hi = (int64_t)a.offs[a.e_hi] * a.row_u4;
+    const uint4* src = a.data[a.rank];
+    for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 v = src[i];
+#pragma unroll
+      for (int s = 0; s < kMaxRanks; ++s)
+        if (s < a.world && s != a.rank) a.data[s][i] = v;
+    }
+  }
+  if (last_cta(my + kFlagArrive3))
+    for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagGPushed + a.rank, epoch);
+}
+
+__global__ void ep_gather_finish_kernel(const GatherArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagGEpoch) + 1u;
+  if (threadIdx.x == 0) {
+    wait_all(my, kFlagGPushed, a.world, epoch);
+    *reinterpret_cast<volatile uint32_t*>(my + kFlagGEpoch) = epoch;
+  }
+}
+
 // ---- IPC plumbing: the allocation base of a pointer (cudaIpc works on whole
 // allocations) through the driver entry point, like the tensor-map encoder.
 static PFN_cuPointerGetAttribute_v4000 g_ptr_attr = nullptr;
@@ -330,4 +395,38 @@ extern "C" int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint
   grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
   allreduce_finish_kernel<<<grid, kArThreads, 0, st>>>(a);
   return check_launch("muk_allreduce_f32(finish)");
+}
+
+extern "C" int muk_ep_gather_bf16(void* const* bufs, uint32_t* const* flags, int rank, int world,
+                                  const int32_t* expert_offsets, int e_lo, int e_hi, int hidden,
+                                  void* stream) {
+  MUK_REQUIRE(bufs && flags && expert_offsets && world >= 1 && world <= kMaxRanks && rank >= 0 &&
+                  rank < world,
+              "muk_ep_gather_bf16: rank %d of %d (at most %d ranks)", rank, world, kMaxRanks);
+  MUK_REQUIRE(e_lo >= 0 && e_hi >= e_lo && hidden > 0 && hidden % 8 == 0,
+              "muk_ep_gather_bf16: experts [%d, %d), hidden %d (a multiple of 8)", e_lo, e_hi,
+              hidden);
+  GatherArgs a;
+  for (int s = 0; s < kMaxRanks; ++s) {
+    a.data[s] = s < world ? reinterpret_cast<uint4*>(bufs[s]) : nullptr;
+    a.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  for (int s = 0; s < world; ++s)
+    MUK_REQUIRE(a.data[s] && a.flags[s] && MUK_ALIGNED16(a.data[s]) && MUK_ALIGNED16(a.flags[s]),
+                "muk_ep_gather_bf16: rank %d buffer or flags null / not 16-byte aligned", s);
+  a.offs = expert_offsets;
+  a.e_lo = e_lo;
+  a.e_hi = e_hi;
+  a.rank = rank;
+  a.world = world;
+  a.row_u4 = hidden / 8;
+  if (world == 1) return MUK_OK;
+  cudaStream_t st = as_stream(stream);
+  // one CTA per SM at most: every CTA waits on the peers' arrival, so all of
+  // them must be resident together
+  ep_gather_push_kernel<<<148, kGatherThreads, 0, st>>>(a);
+  int rc = check_launch("muk_ep_gather_bf16(push)");
+  if (rc) return rc;
+  ep_gather_finish_kernel<<<1, 32, 0, st>>>(a);
+  return check_launch("muk_ep_gather_bf16(finish)");
 }

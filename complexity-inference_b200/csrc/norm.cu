@@ -66,8 +66,20 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat1
   }
 }
 
+// Four consecutive delta values as a float4, from f32 or bf16 rows (index in
+// units of 4 elements).
+__device__ __forceinline__ float4 load4(const float* p, int64_t i4) {
+  return reinterpret_cast<const float4*>(p)[i4];
+}
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t i4) {
+  const uint2 u = reinterpret_cast<const uint2*>(p)[i4];
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // ---------------------------------------------------------------------------
-__global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const float* __restrict__ partials,
+template <typename DT>
+__global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const DT* __restrict__ partials,
                                         int64_t partial_stride, int64_t partial_row_stride,
                                         int num_partials, const int32_t* __restrict__ delta_rows,
                                         const float* __restrict__ norm_w, float eps,
@@ -85,8 +97,7 @@ __global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const float* 
     if (num_partials > 0) {
       float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int p = 0; p < num_partials; ++p) {
-        float4 x = *reinterpret_cast<const float4*>(partials + p * partial_stride +
-                                                    (int64_t)src * partial_row_stride + j);
+        float4 x = load4(partials + p * partial_stride + (int64_t)src * partial_row_stride, j / 4);
         d.x += x.x;
         d.y += x.y;
         d.z += x.z;
@@ -128,9 +139,9 @@ __global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const float* 
 // Same computation with the row held in registers: blockDim.x * VPT float4
 // = hidden, every load of a row issued before the first use (the generic
 // kernel above serialises them on its strided loop).
-template <int VPT>
+template <int VPT, typename DT>
 __global__ void __launch_bounds__(256, VPT <= 4 ? 4 : (VPT <= 8 ? 2 : 1))
-    residual_rmsnorm_vec_kernel(float* __restrict__ resid, const float* __restrict__ partials,
+    residual_rmsnorm_vec_kernel(float* __restrict__ resid, const DT* __restrict__ partials,
                                 int64_t partial_stride, int64_t partial_row_stride,
                                 int num_partials, const int32_t* __restrict__ delta_rows,
                                 const float* __restrict__ norm_w, float eps,
@@ -150,11 +161,10 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 4 : (VPT <= 8 ? 2 : 1))
 #pragma unroll
     for (int i = 0; i < VPT; ++i) d[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int p = 0; p < num_partials; ++p) {
-      const float4* prow = reinterpret_cast<const float4*>(partials + p * partial_stride +
-                                                           (int64_t)src * partial_row_stride);
+      const DT* prow = partials + p * partial_stride + (int64_t)src * partial_row_stride;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const float4 x = prow[threadIdx.x + i * n];
+        const float4 x = load4(prow, threadIdx.x + i * n);
         d[i].x += x.x;
         d[i].y += x.y;
         d[i].z += x.z;
@@ -463,22 +473,23 @@ extern "C" int muk_embed(const int32_t* ids, const void* table, int64_t table_st
   return check_launch("muk_embed");
 }
 
-extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t partial_stride,
-                                    int64_t partial_row_stride, int num_partials,
-                                    const int32_t* delta_rows, const float* norm_w, float eps,
-                                    void* out, int64_t out_stride, int num_tokens, int hidden,
-                                    int clamp_delta, int clamp_sum, int clamp_norm, float mu,
-                                    float clamp_min, float clamp_max, void* stream) {
+template <typename DT>
+static int launch_residual_rmsnorm(float* resid, const DT* partials, int64_t partial_stride,
+                                   int64_t partial_row_stride, int num_partials,
+                                   const int32_t* delta_rows, const float* norm_w, float eps,
+                                   void* out, int64_t out_stride, int num_tokens, int hidden,
+                                   int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                                   float clamp_min, float clamp_max, void* stream,
+                                   const char* name) {
   MUK_REQUIRE(num_tokens >= 0 && hidden > 0 && hidden % 4 == 0 && hidden <= kMaxHidden,
-              "muk_residual_rmsnorm: hidden=%d must be a multiple of 4 and <= %d", hidden,
-              kMaxHidden);
-  MUK_REQUIRE(resid != nullptr && MUK_ALIGNED16(resid), "muk_residual_rmsnorm: resid");
+              "%s: hidden=%d must be a multiple of 4 and <= %d", name, hidden, kMaxHidden);
+  MUK_REQUIRE(resid != nullptr && MUK_ALIGNED16(resid), "%s: resid", name);
   MUK_REQUIRE(num_partials >= 0 && (num_partials == 0 || (partials && MUK_ALIGNED16(partials) &&
                                                           partial_row_stride % 4 == 0 &&
                                                           partial_stride % 4 == 0)),
-              "muk_residual_rmsnorm: partials must be 16-byte aligned rows");
+              "%s: partials must be 16-byte aligned rows", name);
   MUK_REQUIRE(out == nullptr || (norm_w && out_stride >= hidden && out_stride % 2 == 0),
-              "muk_residual_rmsnorm: out needs norm_w and an even stride >= hidden");
+              "%s: out needs norm_w and an even stride >= hidden", name);
   if (num_tokens == 0) return MUK_OK;
   ClampParams cp = make_clamp(1, mu, clamp_min, clamp_max);
   const ClampParams cpn = make_clamp(clamp_norm, mu, clamp_min, clamp_max);
@@ -488,10 +499,12 @@ extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t
                       (partial_row_stride % 4 == 0) && (out == nullptr || ((uintptr_t)out & 7) == 0);
   cudaStream_t st = as_stream(stream);
 #define MUK_RRN(V, THREADS)                                                                     \
-  residual_rmsnorm_vec_kernel<V><<<num_tokens, THREADS, 0, st>>>(                              \
+  residual_rmsnorm_vec_kernel<V, DT><<<num_tokens, THREADS, 0, st>>>(                          \
       resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps, \
       o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp)
+  bool done = false;
   if (vec_ok) {
+    done = true;
     switch (vpt) {
       case -1: MUK_RRN(1, hidden / 4); break;
       case 1: MUK_RRN(1, 256); break;
@@ -499,18 +512,39 @@ extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t
       case 4: MUK_RRN(4, 256); break;
       case 8: MUK_RRN(8, 256); break;
       case 16: MUK_RRN(16, 256); break;
-      default:
-        residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
-            resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w,
-            eps, o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp);
+      default: done = false;
     }
-  } else {
-    residual_rmsnorm_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+  }
+  if (!done)
+    residual_rmsnorm_kernel<DT><<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
         resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps,
         o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp);
-  }
 #undef MUK_RRN
-  return check_launch("muk_residual_rmsnorm");
+  return check_launch(name);
+}
+
+extern "C" int muk_residual_rmsnorm(float* resid, const float* partials, int64_t partial_stride,
+                                    int64_t partial_row_stride, int num_partials,
+                                    const int32_t* delta_rows, const float* norm_w, float eps,
+                                    void* out, int64_t out_stride, int num_tokens, int hidden,
+                                    int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                                    float clamp_min, float clamp_max, void* stream) {
+  return launch_residual_rmsnorm<float>(resid, partials, partial_stride, partial_row_stride,
+                                        num_partials, delta_rows, norm_w, eps, out, out_stride,
+                                        num_tokens, hidden, clamp_delta, clamp_sum, clamp_norm, mu,
+                                        clamp_min, clamp_max, stream, "muk_residual_rmsnorm");
+}
+
+extern "C" int muk_residual_rmsnorm_bf16(float* resid, const void* delta, int64_t delta_row_stride,
+                                         const int32_t* delta_rows, const float* norm_w, float eps,
+                                         void* out, int64_t out_stride, int num_tokens, int hidden,
+                                         int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                                         float clamp_min, float clamp_max, void* stream) {
+  MUK_REQUIRE(delta != nullptr, "muk_residual_rmsnorm_bf16: delta is null");
+  return launch_residual_rmsnorm<__nv_bfloat16>(
+      resid, reinterpret_cast<const __nv_bfloat16*>(delta), 0, delta_row_stride, 1, delta_rows,
+      norm_w, eps, out, out_stride, num_tokens, hidden, clamp_delta, clamp_sum, clamp_norm, mu,
+      clamp_min, clamp_max, stream, "muk_residual_rmsnorm_bf16");
 }
 
 extern "C" int muk_rmsnorm_rows(const float* resid, const int32_t* rows, int num_rows,

@@ -40,6 +40,9 @@ SIGNATURES = {
     "muk_residual_rmsnorm": (c_int, [_P, _P, c_int64, c_int64, c_int, _P, _P, c_float, _P,
                                      c_int64, c_int, c_int, c_int, c_int, c_int, c_float,
                                      c_float, c_float, _P]),
+    "muk_residual_rmsnorm_bf16": (c_int, [_P, _P, c_int64, _P, _P, c_float, _P, c_int64, c_int,
+                                          c_int, c_int, c_int, c_int, c_float, c_float, c_float,
+                                          _P]),
     "muk_rmsnorm_rows": (c_int, [_P, _P, c_int, _P, c_float, _P, c_int64, c_int, c_int, c_float,
                                  c_float, c_float, _P]),
     "muk_rope_kv_append": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
@@ -70,6 +73,7 @@ SIGNATURES = {
     "muk_allreduce_flag_bytes": (c_size_t, []),
     "muk_allreduce_scratch_elems": (c_int64, [c_int64, c_int]),
     "muk_allreduce_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int64, c_int, c_int64, _P]),
+    "muk_ep_gather_bf16": (c_int, [_P, _P, c_int, c_int, _P, c_int, c_int, c_int, _P]),
     "muk_llama_forward": (c_int, [_P, _P, _P]),
     "muk_gemm_allreduce_scratch_elems": (c_int64, [c_int, c_int, c_int]),
     "muk_gemm_allreduce_f32": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P, _P,
@@ -127,7 +131,7 @@ _lib: ctypes.CDLL | None = None
 # count both); the benchmark reports it as its launch count.
 launch_count = 0
 _TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32",
-                "muk_gemm_allreduce_f32"}
+                "muk_gemm_allreduce_f32", "muk_ep_gather_bf16"}
 
 
 class MukError(RuntimeError):

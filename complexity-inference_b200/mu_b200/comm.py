@@ -120,6 +120,29 @@ class PeerAllReduce:
                   torch.cuda.current_stream().cuda_stream)
         return self.buf[:M * N].view(1, M, N)
 
+    def rows_view(self, T: int, H: int) -> torch.Tensor:
+        """[T, H] bf16 rows at the start of this rank's data range: where the
+        expert-parallel combine expects each rank's expert rows."""
+        n = T * H
+        if (n + 1) // 2 > self.max_elems:
+            raise ValueError(f"PeerAllReduce: {T}x{H} bf16 rows do not fit the peer buffer")
+        return self.buf[:(n + 1) // 2].view(torch.bfloat16)[:n].view(T, H)
+
+    def ep_gather_(self, rows: torch.Tensor, expert_offsets: torch.Tensor, e_lo: int,
+                   e_hi: int) -> torch.Tensor:
+        """Expert-parallel combine: this rank's rows [offs[e_lo], offs[e_hi]) of
+        ``rows`` (a rows_view) copied into the same rows of every rank, so that
+        every rank ends with every expert's rows (``muk_ep_gather_bf16``)."""
+        if rows.data_ptr() != self.buf.data_ptr() or rows.dtype != torch.bfloat16:
+            raise ValueError("PeerAllReduce.ep_gather_: rows must be a rows_view")
+        bufs = self._data_arrays.get(0)
+        if bufs is None:
+            bufs = self._data_arrays[0] = (ctypes.c_void_p * self.world)(*self.ptrs)
+        _lib.call("muk_ep_gather_bf16", ctypes.addressof(bufs), ctypes.addressof(self._flags),
+                  self.rank, self.world, expert_offsets.data_ptr(), e_lo, e_hi, rows.shape[1],
+                  torch.cuda.current_stream().cuda_stream)
+        return rows
+
     def reset_flags(self) -> None:
         """Zero this rank's flag words (pushed / done epochs and its own
         epoch).  Only safe while no all-reduce kernel runs on any rank: the

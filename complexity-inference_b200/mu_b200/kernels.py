@@ -81,10 +81,18 @@ def residual_rmsnorm(resid: torch.Tensor, partials: torch.Tensor | None, norm_w:
                      delta_rows: torch.Tensor | None = None):
     """resid += mu_clamp?(Σ partials); out = mu_clamp?(RMSNorm(resid)).
 
-    ``partials`` is [P, rows, H] (or [rows, H]) f32; ``delta_rows`` optionally
-    gathers partial rows per token."""
+    ``partials`` is [P, rows, H] (or [rows, H]) f32, or one [rows, H] bf16
+    slice; ``delta_rows`` optionally gathers partial rows per token."""
     _check(resid, torch.float32, "resid")
     T, H = resid.shape
+    en = clamp.enabled
+    if partials is not None and partials.dtype == torch.bfloat16:
+        ostride = 0 if out is None else _row_stride(out, "out")
+        call("muk_residual_rmsnorm_bf16", _p(resid), _p(partials), _row_stride(partials, "partials"),
+             _p(delta_rows), _p(norm_w), eps, _p(out), ostride, T, H, int(en and clamp_delta),
+             int(en and clamp_sum), int(en and clamp_norm), clamp.mu, clamp.clamp_min,
+             clamp.clamp_max, _stream())
+        return
     np_, pstride, prow = 0, 0, 0
     if partials is not None:
         _check(partials, torch.float32, "partials")
@@ -97,7 +105,6 @@ def residual_rmsnorm(resid: torch.Tensor, partials: torch.Tensor | None, norm_w:
     if out is not None:
         _check(out, torch.bfloat16, "out")
         ostride = _row_stride(out, "out")
-    en = clamp.enabled
     call("muk_residual_rmsnorm", _p(resid), _p(partials), pstride, prow, np_, _p(delta_rows),
          _p(norm_w), eps, _p(out), ostride, T, H, int(en and clamp_delta), int(en and clamp_sum),
          int(en and clamp_norm), clamp.mu, clamp.clamp_min, clamp.clamp_max, _stream())

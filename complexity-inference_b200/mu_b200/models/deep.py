@@ -20,6 +20,7 @@ K-major ([E·2I, H] interleaved gate/up, [E·H, I]).
 
 from __future__ import annotations
 
+import os
 from typing import Dict, List, Optional
 
 import torch
@@ -46,6 +47,10 @@ class DeepForCausalLM(MuModelBase):
         # expert parallelism: this GPU holds experts [expert_lo, expert_lo + local_experts)
         self.local_experts = config.num_experts if self.routed else 0
         self.expert_lo = 0
+        # how expert outputs reach every GPU under expert parallelism with the
+        # peer-memory collectives: "gather" (each GPU's expert rows in bf16,
+        # muk_ep_gather_bf16) or "allreduce" (full-width f32 all-reduce)
+        self.ep_combine = os.environ.get("MU_EP_COMBINE", "gather")
 
     def act_width(self) -> int:
         return self.i_pad
@@ -167,13 +172,24 @@ class DeepForCausalLM(MuModelBase):
                 K.gather_rows(ws.x2, ws.perm, ws.xs, num_rows=T)
                 El, e0 = self.local_experts, self.expert_lo
                 offs = ws.offs[e0:e0 + El + 1]   # rows of this GPU's experts (sorted order)
-                if El < E:  # other experts' rows arrive through the all-reduce
-                    ws.dpart[:T].zero_()
                 K.grouped_gemm(ws.xs, L["wgu"], ws.act, offs, El, 2 * self.i_pad,
                                K.MUK_EPI_SWIGLU, max_rows=T)
-                K.grouped_gemm(ws.act, L["wd"], ws.dpart, offs, El, H, K.MUK_EPI_F32, max_rows=T)
-                self.reduce_partials(ws.dpart[:T])  # same expert order on every rank
-                K.residual_rmsnorm(resid, ws.dpart[:T], nxt_w, eps, nxt_out, clamp=cl,
+                if El < E and self.comm is not None and self.ep_combine == "gather":
+                    # expert parallel: every rank holds every token, so dispatch
+                    # is local; the combine copies each rank's expert rows (bf16)
+                    # into every rank's buffer over NVLink
+                    rows = self.comm.rows_view(T, H)
+                    K.grouped_gemm(ws.act, L["wd"], rows, offs, El, H, K.MUK_EPI_BF16, max_rows=T)
+                    self.comm.ep_gather_(rows, ws.offs, e0, e0 + El)
+                    delta = rows
+                else:
+                    if El < E:  # other experts' rows arrive through the all-reduce
+                        ws.dpart[:T].zero_()
+                    K.grouped_gemm(ws.act, L["wd"], ws.dpart, offs, El, H, K.MUK_EPI_F32,
+                                   max_rows=T)
+                    self.reduce_partials(ws.dpart[:T])  # same expert order on every rank
+                    delta = ws.dpart[:T]
+                K.residual_rmsnorm(resid, delta, nxt_w, eps, nxt_out, clamp=cl,
                                    clamp_delta=True, clamp_sum=True, clamp_norm=True,
                                    delta_rows=ws.inv)
             else:

@@ -90,6 +90,16 @@ int muk_residual_rmsnorm(float* resid, const float* partials, int64_t partial_st
                          int clamp_norm, float mu, float clamp_min, float clamp_max,
                          void* stream);
 
+/* muk_residual_rmsnorm with one bf16 delta slice: d = delta[delta_rows ? delta_rows[t] : t]
+ * (rows of delta_row_stride elements).  Used for the expert outputs that the
+ * expert-parallel combine (muk_ep_gather_bf16) leaves in bf16; same
+ * reference sites as muk_residual_rmsnorm. */
+int muk_residual_rmsnorm_bf16(float* resid, const void* delta, int64_t delta_row_stride,
+                              const int32_t* delta_rows, const float* norm_w, float eps, void* out,
+                              int64_t out_stride, int num_tokens, int hidden, int clamp_delta,
+                              int clamp_sum, int clamp_norm, float mu, float clamp_min,
+                              float clamp_max, void* stream);
+
 /* out[i,:] = bf16(mu_clamp?(RMSNorm(resid[rows[i],:]))) — the final norm on the
  * last token of each sequence before the LM head
  * (mu_inference/models/llama.py:233-237, mu_inference/models/deep.py:318-322). */
@@ -370,6 +380,24 @@ int64_t muk_allreduce_scratch_elems(int64_t n, int world);
  * flag area).  Launches two kernels. */
 int muk_allreduce_f32(float* const* bufs, float* const* scratch, uint32_t* const* flags, int rank,
                       int world, int64_t n, int slices, int64_t slice_stride, void* stream);
+
+/* Expert-parallel combine over NVLink peer memory.  Every rank holds every
+ * token and the same expert-sorted row order (expert_offsets [E + 1], on the
+ * device); rank `rank` computed the rows of experts [e_lo, e_hi) into its own
+ * buffer bufs[rank] ([rows][hidden] bf16, rows at their sorted index).  On
+ * return (stream order) every rank's buffer holds every expert's rows.  Two
+ * kernels: push (an arrival barrier, so no peer still reads the previous
+ * call's rows, then NVLink stores of this rank's rows into every peer's
+ * buffer, then a "pushed" signal) and finish (waits for every peer's
+ * signal).  flags as for muk_allreduce_f32 (the same flag area; separate
+ * words).  Every rank must make the same sequence of calls.  Waits are
+ * bounded (muk_set_peer_timeout_ms); on time-out the device error word reads
+ * 6.  Replaces the per-token expert gather and bmm of MuTokenRoutedMLP
+ * (mu_inference/models/layers.py:530-547) when the experts are spread over
+ * GPUs; the reference has no multi-GPU path. */
+int muk_ep_gather_bf16(void* const* bufs, uint32_t* const* flags, int rank, int world,
+                       const int32_t* expert_offsets, int e_lo, int e_hi, int hidden,
+                       void* stream);
 
 /* Bound of every cross-GPU wait of the collectives on the current device, in
  * ms (1 .. 600000; default 5000).  A wait that runs out records device error

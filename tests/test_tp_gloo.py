@@ -334,3 +334,102 @@ def test_tp_step_failure_is_agreed_across_ranks():
     errs = [rid for rid, (reason, _) in out0.items() if reason == "error"]
     assert errs and len(errs) < len(out0)
     assert all(reason in ("length", "stop") for rid, (reason, _) in out0.items() if rid not in errs)
+
+
+def _ep_combine_worker(rank, world, port, q):
+    """One rank of the expert-parallel combine on CPU: every rank routes all
+    tokens identically, sorts them stably by expert (as muk_route_permute
+    does), computes only its own experts' rows in that sorted order, and the
+    ranks exchange those rows (gloo all-gather of each rank's contiguous
+    range, as muk_ep_gather_bf16 does over NVLink); un-permuting gives every
+    token's expert output."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, f"init failed: {e!r}"))
+        return
+    try:
+        shape, cfg, sd, d, prompts = load_tiny("deep_tiny")
+        p = {k: v.numpy() for k, v in sd.items()}
+        E, V, H = shape.experts, shape.vocab, shape.hidden
+        rng = np.random.default_rng(3)
+        T = 97
+        ids = rng.integers(0, V, T)
+        x = rng.standard_normal((T, H)).astype(np.float32)
+        mu = (rng.standard_normal((T, H)) * 0.3).astype(np.float32)
+        pre = "layers.0.mlp."
+        e = O.route_experts(ids, mu, p[pre + "mu_router.weight"], E, V)
+        perm = np.argsort(e, kind="stable")          # sorted row i holds token perm[i]
+        inv = np.empty(T, dtype=np.int64)
+        inv[perm] = np.arange(T)                      # token t sits at sorted row inv[t]
+        offs = np.concatenate([[0], np.cumsum(np.bincount(e, minlength=E))])
+        lo, hi = expert_range(cfg, rank, world)
+        gu, dn = p[pre + "gate_up_proj"], p[pre + "down_proj"]
+        I = dn.shape[1]
+        rows = np.zeros((T, H), dtype=np.float32)
+        xs = x[perm]
+        for ex in range(lo, hi):
+            a, b = offs[ex], offs[ex + 1]
+            g = xs[a:b] @ gu[ex]
+            rows[a:b] = (O._silu(g[:, :I]) * g[:, I:]) @ dn[ex]
+        # exchange: every rank contributes its range [offs[lo], offs[hi])
+        mine = torch.from_numpy(np.ascontiguousarray(rows[offs[lo]:offs[hi]]))
+        sizes = [None] * world
+        dist.all_gather_object(sizes, (int(offs[lo]), int(offs[hi])))
+        parts = [torch.zeros(b - a, H) for a, b in sizes]
+        counts = torch.tensor([b - a for a, b in sizes])
+        mx = int(counts.max())
+        pad = torch.zeros(mx, H)
+        pad[:mine.shape[0]] = mine
+        gathered = [torch.zeros(mx, H) for _ in range(world)]
+        dist.all_gather(gathered, pad)
+        full = np.zeros((T, H), dtype=np.float32)
+        for (a, b), gpart in zip(sizes, gathered):
+            full[a:b] = gpart[:b - a].numpy()
+        out = full[inv]                               # back to token order
+        q.put((rank, (out, e, (lo, hi))))
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_combine_bookkeeping_matches_unsharded():
+    """Expert-parallel routing, stable expert sort, per-rank expert rows, the
+    row exchange and the un-permute reproduce the unsharded token-routed MLP
+    (layers.py:485-559, via the oracle) on both ranks, and the two ranks' expert
+    ranges cover every expert exactly once."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_combine_worker, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert not isinstance(got[r], str), got[r]
+    shape, cfg, sd, d, prompts = load_tiny("deep_tiny")
+    p = {k: v.numpy() for k, v in sd.items()}
+    E, V, H = shape.experts, shape.vocab, shape.hidden
+    rng = np.random.default_rng(3)
+    T = 97
+    ids = rng.integers(0, V, T)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    mu = (rng.standard_normal((T, H)) * 0.3).astype(np.float32)
+    model = O.OracleModel(shape, p, O.MuCfg(False))
+    ref = model._mlp(0, x, ids, mu)
+    ranges = sorted(got[r][2] for r in range(world))
+    assert ranges[0][0] == 0 and ranges[-1][1] == E and ranges[0][1] == ranges[1][0]
+    for r in range(world):
+        out, e, _ = got[r]
+        np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-5)
+        assert np.array_equal(e, O.route_experts(ids, mu, p["layers.0.mlp.mu_router.weight"], E, V))
+    assert len(np.unique(got[0][1])) > 1   # tokens really spread over both ranks' experts

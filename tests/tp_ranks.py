@@ -93,6 +93,42 @@ def check_peer_allreduce(rank, world, failures):
         if not torch.all(x == want):
             failures.append(("peer allreduce graph replay", it, float(x[0])))
     del graph
+    # expert-parallel combine (muk_ep_gather_bf16): rank r owns the sorted rows of
+    # experts [2r, 2r + 2); afterwards every rank holds every owner's rows, also
+    # when the call is replayed from a CUDA graph
+    T, H, E = 37, 256, 2 * world
+    offs = torch.tensor([0, 5, 5, 20, 33, 37, 37, 37, 37][:E + 1] + [37] * max(0, E + 1 - 9),
+                        device="cuda", dtype=torch.int32)[:E + 1]
+    offs[-1] = T
+    rows = comm.rows_view(T, H)
+    lo, hi = int(offs[2 * rank]), int(offs[2 * rank + 2])
+    val = torch.arange(T, device="cuda", dtype=torch.float32)[:, None] + 1000.0 * torch.arange(
+        H, device="cuda", dtype=torch.float32)[None, :] / H
+    want = val.bfloat16()
+    rows.fill_(float("nan"))
+    rows[lo:hi] = want[lo:hi]
+    comm.ep_gather_(rows, offs, 2 * rank, 2 * rank + 2)
+    torch.cuda.synchronize()
+    if not torch.equal(rows, want):
+        failures.append(("ep gather", int((rows != want).sum())))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    src = torch.zeros(T, H, device="cuda", dtype=torch.bfloat16)
+    with torch.cuda.stream(side):
+        rows[lo:hi] = src[lo:hi]
+        comm.ep_gather_(rows, offs, 2 * rank, 2 * rank + 2)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        rows[lo:hi] = src[lo:hi]
+        comm.ep_gather_(rows, offs, 2 * rank, 2 * rank + 2)
+    for it in range(3):
+        src.copy_((val + it).bfloat16())
+        graph.replay()
+        torch.cuda.synchronize()
+        if not torch.equal(rows, (val + it).bfloat16()):
+            failures.append(("ep gather graph replay", it))
+    del graph
     comm.close()
     dist.barrier()
 
@@ -113,14 +149,18 @@ def main():
     check_peer_allreduce(rank, world, failures)
     # (model, CUDA graphs, expert parallel, all-reduce: peer memory or NCCL)
     # "peer": GEMM + reduce-scatter fused; "peer-split": GEMM, then muk_allreduce_f32
-    for name, graphs, ep, comm in (("llama_tiny", False, False, "nccl"),
-                                   ("llama_tiny", True, False, "peer"),
-                                   ("llama_tiny", False, False, "peer-split"),
-                                   ("deep_tiny", False, False, "nccl"),
-                                   ("deep_tiny", True, False, "peer"),
-                                   ("deep_tiny", True, True, "peer-split")):
+    # expert-parallel cases combine expert outputs by the bf16 row exchange
+    # ("gather", the default) or the f32 all-reduce ("allreduce")
+    for name, graphs, ep, comm, combine in (("llama_tiny", False, False, "nccl", "-"),
+                                            ("llama_tiny", True, False, "peer", "-"),
+                                            ("llama_tiny", False, False, "peer-split", "-"),
+                                            ("deep_tiny", False, False, "nccl", "-"),
+                                            ("deep_tiny", True, False, "peer", "-"),
+                                            ("deep_tiny", True, True, "peer-split", "gather"),
+                                            ("deep_tiny", False, True, "peer", "allreduce")):
         os.environ["MU_TP_COMM"] = "nccl" if comm == "nccl" else "peer"
         os.environ["MU_TP_FUSED"] = "0" if comm == "peer-split" else "1"
+        os.environ["MU_EP_COMBINE"] = "allreduce" if combine == "allreduce" else "gather"
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
                           expert_parallel=ep,
@@ -153,7 +193,7 @@ def main():
                     step_err.append((i, r, round(e, 5)))
         for r in range(R):
             w.free_request(f"r{r}")
-        worst[f"{name}/graphs={graphs}/ep={ep}/{comm}"] = err
+        worst[f"{name}/graphs={graphs}/ep={ep}/{comm}/{combine}"] = err
         if err > 2e-2:
             failures.append((name, graphs, rank, err, [x for x in step_err if x[2] > 2e-2][:6]))
         eng = StepEngine(w, ec)
