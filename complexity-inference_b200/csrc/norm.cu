@@ -257,6 +257,7 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 
 constexpr int kMaxExperts = 16;
+constexpr int kInlMaxVecExperts = 8;  // the register-resident INL kernel routes over up to 8
 
 __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __restrict__ ctrl_raw,
                                     const float* __restrict__ ctrl_bias,
@@ -335,8 +336,29 @@ __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __
 
 // Register-resident INL step (same arithmetic as inl_dynamics_kernel):
 // blockDim.x * VPT float4 = hidden; all loads of a chunk issued together.
+// Per-row sums of the INL kernel: the squared residual and one router dot
+// product per expert, reduced over the CTA together (one shared-memory pass
+// for all of them instead of one per value).
+template <int NV>
+__device__ __forceinline__ void block_sums(float (&x)[NV], float* red /* [32][NV] */) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) x[k] = warp_sum(x[k]);
+  if (lane == 0)
+#pragma unroll
+    for (int k = 0; k < NV; ++k) red[warp * NV + k] = x[k];
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += red[w * NV + k];  // same order in every thread
+    x[k] = t;
+  }
+}
+
 template <int VPT>
-__global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
+__global__ void __launch_bounds__(256, VPT <= 4 ? 3 : 1)
     inl_dynamics_vec_kernel(const float* __restrict__ h, const float* __restrict__ ctrl_raw,
                             const float* __restrict__ ctrl_bias, const float* __restrict__ muproj,
                             const float* __restrict__ mu_param, float dt, float* __restrict__ v,
@@ -347,8 +369,8 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
                             const int32_t* __restrict__ token_ids,
                             const __nv_bfloat16* __restrict__ router_w, int num_experts, int vocab,
                             int32_t* __restrict__ expert_ids, int hidden, ClampParams cp_norm) {
-  __shared__ float red[32];
-  __shared__ float dots[kMaxExperts];
+  constexpr int NV = 1 + kInlMaxVecExperts;      // squared sum + router dots
+  __shared__ float red[32 * NV];
   const int t = blockIdx.x;
   const int n = blockDim.x;
   const int64_t base4 = (int64_t)t * (hidden / 4);
@@ -360,17 +382,15 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
   const float4* mu4 = reinterpret_cast<const float4*>(mu_param);
   float4* v4 = reinterpret_cast<float4*>(v) + base4;
   float4* r4 = reinterpret_cast<float4*>(resid) + base4;
-  float4 r[VPT];
-  float edot[kMaxExperts];
+  float acc[NV];
 #pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) edot[e] = 0.f;
-  float ss = 0.f;
+  for (int e = 0; e < NV; ++e) acc[e] = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int q = threadIdx.x + i * n;  // float4 index within the row
     const float4 ca = c4[q], cb = c4[H4 + q], cg = c4[2 * H4 + q];
-    const float4 ba = b4[q], bb = b4[H4 + q], bg = b4[2 * H4 + q];
-    const float4 mpv = mp4[q], muv = mu4[q], hv = h4[q], vv = v4[q], rv = r4[q];
+    const float4 mpv = mp4[q], hv = h4[q], vv = v4[q], rv = r4[q];
+    const float4 ba = b4[q], bb = b4[H4 + q], bg = b4[2 * H4 + q], muv = mu4[q];
     const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
     const float cgv[4] = {cg.x, cg.y, cg.z, cg.w}, bav[4] = {ba.x, ba.y, ba.z, ba.w};
     const float bbv[4] = {bb.x, bb.y, bb.z, bb.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
@@ -388,10 +408,9 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
       x = fminf(fmaxf(x, -10.f), 10.f);
       vn[u] = x;
       rn[u] = ra[u] + (ha[u] + dt * g * x);
-      ss += rn[u] * rn[u];
+      acc[0] += rn[u] * rn[u];
     }
-    r[i] = make_float4(rn[0], rn[1], rn[2], rn[3]);
-    r4[q] = r[i];
+    r4[q] = make_float4(rn[0], rn[1], rn[2], rn[3]);
     v4[q] = make_float4(vn[0], vn[1], vn[2], vn[3]);
     if (v_bf16) {
       uint2 o;
@@ -407,49 +426,46 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 2 : 1)
     }
     if (router_w) {
 #pragma unroll
-      for (int e = 0; e < kMaxExperts; ++e) {
+      for (int e = 0; e < kInlMaxVecExperts; ++e) {
         if (e < num_experts) {
           const uint2 w = *reinterpret_cast<const uint2*>(router_w + (int64_t)e * hidden + 4 * q);
           const float2 w01 = unpack_bf16x2(w.x), w23 = unpack_bf16x2(w.y);
-          edot[e] += muc[0] * w01.x + muc[1] * w01.y + muc[2] * w23.x + muc[3] * w23.y;
+          acc[1 + e] += muc[0] * w01.x + muc[1] * w01.y + muc[2] * w23.x + muc[3] * w23.y;
         }
       }
     }
   }
-  const float total = block_sum(ss, red);
-  if (router_w) {
-    for (int e = 0; e < num_experts; ++e) {
-      const float d = block_sum(edot[e], red);
-      if (threadIdx.x == 0) dots[e] = d;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int id = token_ids[t];
-      id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
-      const int base_e = id % num_experts;
-      int best = 0;
-      float bestv = -INFINITY;
-      for (int e = 0; e < num_experts; ++e) {
-        const float sc = (e == base_e ? 10.f : 0.f) + dots[e];
+  block_sums<NV>(acc, red);
+  if (router_w && threadIdx.x == 0) {
+    int id = token_ids[t];
+    id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+    const int base_e = id % num_experts;
+    int best = 0;
+    float bestv = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < kInlMaxVecExperts; ++e) {
+      if (e < num_experts) {
+        const float sc = (e == base_e ? 10.f : 0.f) + acc[1 + e];
         if (sc > bestv) {
           bestv = sc;
           best = e;
         }
       }
-      expert_ids[t] = best;
     }
+    expert_ids[t] = best;
   }
   if (norm_out) {
-    const float inv = rsqrtf(total / (float)hidden + eps);
+    // the row just written by this same thread comes back from L1
+    const float inv = rsqrtf(acc[0] / (float)hidden + eps);
     const float4* w4 = reinterpret_cast<const float4*>(norm_w);
     uint2* orow = reinterpret_cast<uint2*>(norm_out + (int64_t)t * norm_out_stride);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int q = threadIdx.x + i * n;
-      const float4 w = w4[q];
+      const float4 w = w4[q], r = r4[q];
       uint2 o;
-      o.x = pack_bf16x2(mu_clamp(w.x * (r[i].x * inv), cp_norm), mu_clamp(w.y * (r[i].y * inv), cp_norm));
-      o.y = pack_bf16x2(mu_clamp(w.z * (r[i].z * inv), cp_norm), mu_clamp(w.w * (r[i].w * inv), cp_norm));
+      o.x = pack_bf16x2(mu_clamp(w.x * (r.x * inv), cp_norm), mu_clamp(w.y * (r.y * inv), cp_norm));
+      o.y = pack_bf16x2(mu_clamp(w.z * (r.z * inv), cp_norm), mu_clamp(w.w * (r.w * inv), cp_norm));
       orow[q] = o;
     }
   }
@@ -615,7 +631,12 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
       h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,            \
       mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,        \
       expert_ids, hidden, cpn)
-  if (vec_ok && vpt == -1) {
+  if (router_w != nullptr && num_experts > kInlMaxVecExperts) {
+    inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,
+        mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
+        expert_ids, hidden, cpn);
+  } else if (vec_ok && vpt == -1) {
     MUK_INL(1, hidden / 4);
   } else if (vec_ok && vpt == 1) {
     MUK_INL(1, 256);
