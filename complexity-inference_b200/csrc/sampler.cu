@@ -155,6 +155,36 @@ __device__ unsigned long long blk_sum_u64(unsigned long long v, unsigned long lo
   return red[0];
 }
 
+// Histogram adds aggregated per warp: lanes with the same bin (bins >= 256
+// add nothing) are grouped with __match_any_sync, each lane sums its group's
+// values by a fixed 32-step shuffle walk (exact, order-independent), and one
+// lane per group issues the shared-memory atomic.  The float keys' top digits
+// fall in a handful of bins, so unaggregated atomics serialise on them.  All
+// 32 lanes of the warp must call these.
+__device__ __forceinline__ void warp_hist_add(uint32_t* hist, uint32_t bin, uint32_t c) {
+  if (__ballot_sync(0xffffffffu, bin < 256u) == 0u) return;  // nothing to add in this warp
+  const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+  uint32_t sum = 0u;
+#pragma unroll
+  for (int src = 0; src < 32; ++src) {
+    const uint32_t x = __shfl_sync(0xffffffffu, c, src);
+    if ((peers >> src) & 1u) sum += x;
+  }
+  if (bin < 256u && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], sum);
+}
+__device__ __forceinline__ void warp_hist_add(unsigned long long* hist, uint32_t bin,
+                                              unsigned long long q) {
+  if (__ballot_sync(0xffffffffu, bin < 256u) == 0u) return;  // nothing to add in this warp
+  const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+  unsigned long long sum = 0ull;
+#pragma unroll
+  for (int src = 0; src < 32; ++src) {
+    const unsigned long long x = __shfl_sync(0xffffffffu, q, src);
+    if ((peers >> src) & 1u) sum += x;
+  }
+  if (bin < 256u && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], sum);
+}
+
 // kFilter = false: one sampled token per row (tokens_out).
 // kFilter = true:  the processed logits of prepare_logits per row (filt):
 //                  penalised and temperature-scaled values where kept, -inf
@@ -220,9 +250,14 @@ __global__ void __launch_bounds__(kSampThreads)
       if (tid < 256) hist[tid] = 0u;
       __syncthreads();
       const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      for (int i = tid; i < V; i += blockDim.x) {
-        const uint32_t key = f2key(row_val(p, i));
-        if ((key & hi_mask) == (prefix & hi_mask)) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      for (int b0 = tid - (tid & 31); b0 < V; b0 += blockDim.x) {  // whole warps
+        const int i = b0 + (tid & 31);
+        uint32_t bin = 256u;
+        if (i < V) {
+          const uint32_t key = f2key(row_val(p, i));
+          if ((key & hi_mask) == (prefix & hi_mask)) bin = (key >> shift) & 255u;
+        }
+        warp_hist_add(hist, bin, 1u);
       }
       __syncthreads();
       if (tid == 0) {
@@ -361,11 +396,19 @@ __global__ void __launch_bounds__(kSampThreads)
       if (tid < 256) mhist[tid] = 0ull;
       __syncthreads();
       const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      for (int i = tid; i < V; i += blockDim.x) {
-        const float v = row_val(p, i);
-        const uint32_t key = f2key(v);
-        if (key >= thr_key && (key & hi_mask) == (prefix & hi_mask))
-          atomicAdd(&mhist[(key >> shift) & 255u], mass_q(v, mx));
+      for (int b0 = tid - (tid & 31); b0 < V; b0 += blockDim.x) {  // whole warps
+        const int i = b0 + (tid & 31);
+        uint32_t bin = 256u;
+        unsigned long long q = 0ull;
+        if (i < V) {
+          const float v = row_val(p, i);
+          const uint32_t key = f2key(v);
+          if (key >= thr_key && (key & hi_mask) == (prefix & hi_mask)) {
+            bin = (key >> shift) & 255u;
+            q = mass_q(v, mx);
+          }
+        }
+        warp_hist_add(mhist, bin, q);
       }
       __syncthreads();
       if (tid == 0) {
