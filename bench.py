@@ -603,6 +603,7 @@ def run_ours(args, rank, world, local_rank):
     assert len(rec.blobs) == len(rec.steps)
     assert all(b.numel() == smp._blob_d.numel() for _, _, b in rec.blobs)
 
+    @torch.inference_mode()  # the engine's buffers are inference tensors
     def replay():
         for (st, buf), (B, T, blob) in zip(rec.steps, rec.blobs):
             worker.packer.dev[:st.end].copy_(buf, non_blocking=True)
