@@ -65,6 +65,29 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
   MUK_TRY(muk_residual_rmsnorm(m->resid, nullptr, 0, 0, 0, nullptr, m->layers[0].in_norm, m->eps,
                                x, m->x_stride, T, H, 0, 0, cl, mu, cmin, cmax, stream));
 
+  // Paged decode attention over the decode rows, varlen prefill attention
+  // over the rest (decode sequences own one row each, so prefill starts at nd).
+  auto attention = [&](int l, void* kc, void* vc) -> int {
+    (void)l;
+    if (nd > 0) {
+      int bound = b->decode_len_bound;
+      const int bt_cap = b->block_table_stride * m->block_size;
+      if (bound > bt_cap) bound = bt_cap;
+      MUK_TRY(muk_paged_decode_attn(qkv, qkv_n, attn, attn_n, kc, vc, b->block_tables,
+                                    b->block_table_stride, b->seq_lens, nd, Hq, Hkv, D,
+                                    m->block_size, m->num_blocks, scale, bound, m->attn_ws,
+                                    m->attn_ws_bytes, stream));
+    }
+    if (B > nd) {
+      MUK_TRY(muk_paged_prefill_attn(qkv + (int64_t)nd * qkv_n, qkv_n, attn + (int64_t)nd * attn_n,
+                                     attn_n, kc, vc, b->block_tables + (int64_t)nd * b->block_table_stride,
+                                     b->block_table_stride, b->seq_lens + nd, b->prefill_cu,
+                                     B - nd, b->max_q_len, Hq, Hkv, D, m->block_size,
+                                     m->num_blocks, scale, stream));
+    }
+    return MUK_OK;
+  };
+
   // Sum a row-parallel projection over the tensor-parallel ranks; returns the
   // number of slices the consumer reads.
   // GEMM + reduce-scatter in one kernel while the step has few rows (see
@@ -76,6 +99,40 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
                                (int64_t)T * H, slices, (int64_t)T * H, stream);
     return rc == MUK_OK ? 1 : rc;
   };
+
+  if (m->fused_norm > 0 && T >= m->fused_norm) {
+    MUK_REQUIRE(m->tp_world == 1 && !cl && H % 128 == 0 && m->fused_rope && m->sumsq,
+                "muk_llama_forward: fused_norm needs one rank, no clamp, hidden %% 128 == 0, "
+                "fused_rope and a sumsq buffer");
+    // x holds bf16(w * h); the GEMM reading it scales each row by
+    // rsqrt(mean(h^2) + eps) from the partial sums the producer left in sumsq
+    const MukRowNorm rn = {m->sumsq, (int64_t)T, H / 128, H, m->eps};
+    for (int l = 0; l < m->num_layers; ++l) {
+      const MukLlamaLayer& L = m->layers[l];
+      void* kc = pool + (int64_t)(2 * l) * layer_elems;
+      void* vc = pool + (int64_t)(2 * l + 1) * layer_elems;
+      MUK_TRY(muk_gemm_qkv_rope_rownorm(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, H, b->positions,
+                                        b->slot_mapping, m->rope_cos, m->rope_sin, m->rope_len,
+                                        Hq, Hkv, D, nullptr, nullptr, 1e-6f, kc, vc,
+                                        m->num_blocks, m->block_size, l > 0 ? &rn : nullptr,
+                                        stream));
+      MUK_TRY(attention(l, kc, vc));
+      MUK_TRY(muk_gemm_residual_norm(attn, attn_n, L.wo, attn_n, T, H, attn_n, m->resid, H,
+                                     L.post_norm, x, m->x_stride, m->sumsq, T, stream));
+      MUK_TRY(muk_gemm_swiglu_rownorm(x, m->x_stride, L.wgu, H, m->act, m->inter_pad, T,
+                                      2 * m->inter_pad, H, &rn, stream));
+      const bool last = l + 1 == m->num_layers;
+      MUK_TRY(muk_gemm_residual_norm(m->act, m->inter_pad, L.wd, m->inter_pad, T, H,
+                                     m->inter_pad, m->resid, H,
+                                     last ? nullptr : m->layers[l + 1].in_norm,
+                                     last ? nullptr : x, m->x_stride,
+                                     last ? nullptr : m->sumsq, T, stream));
+    }
+    MUK_TRY(muk_rmsnorm_rows(m->resid, b->last_token_idx, B, m->final_norm, m->eps, m->xl, H, H,
+                             cl, mu, cmin, cmax, stream));
+    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32,
+                         1, nullptr, stream);
+  }
 
   for (int l = 0; l < m->num_layers; ++l) {
     const MukLlamaLayer& L = m->layers[l];
@@ -93,22 +150,7 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
                                  m->rope_sin, m->rope_len, T, Hq, Hkv, D, nullptr, nullptr, 1e-6f,
                                  kc, vc, m->num_blocks, m->block_size, stream));
     }
-    if (nd > 0) {
-      int bound = b->decode_len_bound;
-      const int bt_cap = b->block_table_stride * m->block_size;
-      if (bound > bt_cap) bound = bt_cap;
-      MUK_TRY(muk_paged_decode_attn(qkv, qkv_n, attn, attn_n, kc, vc, b->block_tables,
-                                    b->block_table_stride, b->seq_lens, nd, Hq, Hkv, D,
-                                    m->block_size, m->num_blocks, scale, bound, m->attn_ws,
-                                    m->attn_ws_bytes, stream));
-    }
-    if (B > nd) {
-      MUK_TRY(muk_paged_prefill_attn(qkv + (int64_t)nd * qkv_n, qkv_n, attn + (int64_t)nd * attn_n,
-                                     attn_n, kc, vc, b->block_tables + (int64_t)nd * b->block_table_stride,
-                                     b->block_table_stride, b->seq_lens + nd, b->prefill_cu,
-                                     B - nd, b->max_q_len, Hq, Hkv, D, m->block_size,
-                                     m->num_blocks, scale, stream));
-    }
+    MUK_TRY(attention(l, kc, vc));
     // O projection (split-K f32 partials) -> reduce -> h += clamp(o); x = clamp(norm(h))
     int np;
     if (fused_tp) {

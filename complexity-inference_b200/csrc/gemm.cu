@@ -62,6 +62,17 @@ static bool g_pair_enabled = false;
 #else
 static bool g_pair_enabled = true;
 #endif
+// Planner cost of one k-tile of a 256 x 128 pair tile, in units of a 128 x 256
+// single-CTA tile's k-tile: measured 0.67, not the 0.44 of its share of the
+// flops.  Per CTA and k-tile the 256 x 128 MMAs need 256 SM clocks, while the
+// shared memory moves 24 KB of TMA writes plus 4 x 6 KB of operand reads
+// (~384 clocks at 128 B/clock), so these tiles are shared-memory-bound; they
+// win only where tile count dominates (M 256, N 4096: 32 tiles on 74 pairs,
+// 31 us vs 38 us with 256-wide tiles).  MUK_GEMM_PAIR128_COST overrides.
+static double g_pair128_cost = [] {
+  const char* e = getenv("MUK_GEMM_PAIR128_COST");
+  return e ? atof(e) : 0.67;
+}();
 
 template <int BN, int STAGES>
 struct GemmLayout {
@@ -100,6 +111,29 @@ struct PushArgs {
   int rank, world, share_rows;
 };
 
+// RMSNorm split across two GEMMs (dense, one GPU, no mu_clamp on the norm):
+// the producer (O or down projection, kEpiResidNorm) adds its output to the
+// f32 residual, stores x~ = bf16(w * r) and, per 128 output columns, the
+// row's partial sum of r^2; the consumer (the next q|k|v or gate|up GEMM)
+// multiplies each accumulator row by rsqrt(sum of the partials / H + eps)
+// before its own epilogue.  RMSNorm's per-row scale commutes with the matmul,
+// so this is the norm, with bf16(w * r) rounded in place of bf16(w * r * s).
+struct NormArgs {
+  float* resid;              // producer: [M][ld_resid] f32, updated in place
+  int64_t ld_resid;
+  const float* w;            // producer: norm weight [N]; nullptr = residual add only
+  __nv_bfloat16* xout;       // producer: x~ rows, [M][ldx]
+  int64_t ldx;
+  float* sumsq_out;          // producer: [N / 128][sumsq_stride] partial sums of r^2
+  const float* sumsq_in;     // consumer: the producer's partials; nullptr = no scaling
+  int64_t sumsq_stride;
+  int parts;                 // consumer: number of 128-column partials per row
+  float inv_h, eps;          // consumer: 1 / H and the norm's eps
+};
+
+// Epilogue of the producer (see NormArgs).
+constexpr int kEpiResidNorm = 6;
+
 struct TileArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kt_per_split, total;
@@ -112,7 +146,18 @@ struct TileArgs {
   int dp_tiles, sk_tiles, k_tiles, workers;
   RopeArgs rope;
   PushArgs push;
+  NormArgs norm;
 };
+
+// Consumer row scale rsqrt(mean(r^2) + eps) from the producer's partials
+// (1 when the launch has none, or for rows past the end).
+__device__ __forceinline__ float row_norm_scale(const TileArgs& a, int row, int row_end) {
+  const NormArgs& n = a.norm;
+  if (n.sumsq_in == nullptr || row >= row_end) return 1.f;
+  float ss = 0.f;
+  for (int p = 0; p < n.parts; ++p) ss += n.sumsq_in[(int64_t)p * n.sumsq_stride + row];
+  return rsqrtf(ss * n.inv_h + n.eps);
+}
 
 __device__ __forceinline__ void store_push(const TileArgs& a, int row, int row_end, int col,
                                            const uint32_t (&v)[32]) {
@@ -378,6 +423,7 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
   const RopeArgs& r = a.rope;
   const int D = r.head_dim, half = D >> 1, cph = D >> 5;
   const bool valid = row < row_end;
+  const float rs = row_norm_scale(a, row, row_end);  // the input row's RMSNorm scale
   int pos = valid ? r.positions[row] : 0;
   const int slot = valid ? r.slots[row] : -1;
   if (valid && (pos < 0 || pos >= r.max_pos)) {
@@ -414,7 +460,7 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
         acc_chunk(lane_addr, c0 + c, v, fix);
         float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
         if (store) store_bf16x32(dst + c * 32, f);
       }
       continue;
@@ -427,7 +473,10 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
         uint32_t v[32];
         acc_chunk(lane_addr, c0 + c, v, fix);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ss += __uint_as_float(v[j]) * __uint_as_float(v[j]);
+        for (int j = 0; j < 32; ++j) {
+          const float x = __uint_as_float(v[j]) * rs;
+          ss += x * x;
+        }
       }
       inv = rsqrtf(ss / (float)D + r.eps);
     }
@@ -447,7 +496,7 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = 4 * j4 + u;
-          float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
+          float x = __uint_as_float(lo[j]) * rs, y = __uint_as_float(hi[j]) * rs;
           if (nw != nullptr) {
             x = nw[i0 + j] * (x * inv);
             y = nw[half + i0 + j] * (y * inv);
@@ -473,8 +522,50 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
                                               const SkFix* fix) {
   if (EPI == MUK_EPI_ROPE_KV) {
     epilogue_rope<BN>(C, args, row, row_end, n0, lane_addr, fix);
+  } else if (EPI == kEpiResidNorm) {
+    // resid += acc; x~ = bf16(w * resid); one partial sum of resid^2 per 128 columns
+    const NormArgs& nm = args.norm;
+    const bool valid = row < row_end;
+    float* rrow = nm.resid + (int64_t)row * nm.ld_resid;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+      tmem_ld_wait();
+      if (fix) sk_sum_chunk(*fix, c, v);
+      const int col = n0 + c * 32;
+      if (valid && col < args.N) {  // N % 128 == 0: a chunk is wholly inside or outside
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 r4 = *reinterpret_cast<const float4*>(rrow + col + j);
+          r4.x += __uint_as_float(v[j]);
+          r4.y += __uint_as_float(v[j + 1]);
+          r4.z += __uint_as_float(v[j + 2]);
+          r4.w += __uint_as_float(v[j + 3]);
+          *reinterpret_cast<float4*>(rrow + col + j) = r4;
+          ss += r4.x * r4.x + r4.y * r4.y + r4.z * r4.z + r4.w * r4.w;
+          if (nm.w != nullptr) {
+            const float4 w4 = *reinterpret_cast<const float4*>(nm.w + col + j);
+            f[j] = w4.x * r4.x;
+            f[j + 1] = w4.y * r4.y;
+            f[j + 2] = w4.z * r4.z;
+            f[j + 3] = w4.w * r4.w;
+          }
+        }
+        if (nm.w != nullptr) {
+          store_bf16x32(nm.xout + (int64_t)row * nm.ldx + col, f);
+          if ((c & 3) == 3) {
+            nm.sumsq_out[(int64_t)(col >> 7) * nm.sumsq_stride + row] = ss;
+            ss = 0.f;
+          }
+        }
+      }
+    }
   } else if (EPI == MUK_EPI_SWIGLU) {
     const int nout = args.N >> 1;
+    const float rs = row_norm_scale(args, row, row_end);  // the input row's RMSNorm scale
 #pragma unroll 1
     for (int grp = 0; grp < BN / 128; ++grp) {
 #pragma unroll 1
@@ -489,7 +580,7 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          gv[j] = __float_as_uint(silu(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
+          gv[j] = __float_as_uint(silu(__uint_as_float(gv[j]) * rs) * (__uint_as_float(uv[j]) * rs));
         store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, row_end, (n0 >> 1) + grp * 64 + c * 32,
                                   nout, gv, nullptr);
       }
@@ -731,15 +822,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // on the `empty` / `acc_full` barriers of both CTAs; both epilogues release the
 // accumulator on its `acc_empty`.  Each CTA's TMEM holds its 128 rows.
 // ---------------------------------------------------------------------------
-constexpr int kPairBN = 256;
-constexpr int kPairStages = 6;
-
+// PBN = 128 (256 x 128 tiles, 8 KB of B per CTA and k-tile) doubles the tile
+// count of a launch, for shapes whose 256-wide tiles fill the pairs badly
+// (q|k|v at M ~ 900: 96 tiles on 74 pairs vs 192).
+template <int PBN>
 struct PairLayout {
-  static constexpr int kA = kBM * kBK * 2;             // 16 KB: this CTA's 128 rows of A
-  static constexpr int kB = (kPairBN / 2) * kBK * 2;   // 16 KB: this CTA's half of B
+  static constexpr int kStages = PBN == 256 ? 6 : 8;
+  static constexpr int kA = kBM * kBK * 2;         // 16 KB: this CTA's 128 rows of A
+  static constexpr int kB = (PBN / 2) * kBK * 2;   // this CTA's half of B
   static constexpr int kStage = kA + kB;
-  static constexpr int kBarOff = kPairStages * kStage;
-  static constexpr int kBytes = kBarOff + (2 * kPairStages + 4) * 8 + 16 + 1024;
+  static constexpr int kBarOff = kStages * kStage;
+  static constexpr int kBytes = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
 };
 
 struct PairTile {
@@ -762,14 +855,14 @@ __device__ __forceinline__ PairTile pair_tile(const TileArgs& a, const Unit& u) 
   return p;
 }
 
-template <int EPI>
+template <int EPI, int PBN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
                      const TileArgs args) {
-  using L = PairLayout;
-  constexpr int BN = kPairBN;
-  constexpr int S = kPairStages;
+  using L = PairLayout<PBN>;
+  constexpr int BN = PBN;
+  constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1042,6 +1135,14 @@ static bool streamk_allowed(long tiles, int workers) {
   return m == 1 || (m == 2 && tiles * 4 <= workers);
 }
 
+// Pairs pay off once both CTAs of a pair have rows to work on and N fills
+// the tile width (SwiGLU needs N % bn for its 128-column gate/up groups).
+static bool use_pair(int M, int N, int epilogue, int bn) {
+  if (M <= 128 || N < bn) return false;
+  if (epilogue == MUK_EPI_SWIGLU && N % bn != 0) return false;
+  return true;
+}
+
 struct GemmPlan {
   int kind;   // 0: single CTA, 1: CTA pair
   int bn;     // 128 or 256
@@ -1059,9 +1160,10 @@ static PlanShape plan_shape(int kind, int bn, int split, int M, int N, int K, in
   PlanShape p;
   p.k_tiles = (K + kBK - 1) / kBK;
   if (kind == 1) {
-    p.tiles = (long)((M + 255) / 256) * ((N + 255) / 256) * split;
+    p.tiles = (long)((M + 255) / 256) * ((N + bn - 1) / bn) * split;
     p.workers = sms / 2;
-    p.per_k = 0.88;  // measured: pair tiles run ~1.13x faster per SM than 128 x 256
+    // measured: 256 x 256 pair tiles run ~1.13x faster per SM than 128 x 256
+    p.per_k = bn == 256 ? 0.88 : g_pair128_cost;
   } else {
     p.tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn) * split;
     p.workers = sms;
@@ -1126,11 +1228,12 @@ static GemmPlan plan_gemm(int M, int N, int K, int epilogue, int max_split, int 
           best = {0, bn, split, sk != 0};
         }
       }
-      if (g_pair_enabled && M > 128 && N >= 256 && !(swiglu && N % 256 != 0)) {
-        const double c = plan_cost(1, 256, split, sk, M, N, K, sms);
+      for (int bn : {256, 128}) {
+        if (!g_pair_enabled || !use_pair(M, N, epilogue, bn)) continue;
+        const double c = plan_cost(1, bn, split, sk, M, N, K, sms);
         if (c < best_cost * 0.999) {
           best_cost = c;
-          best = {1, 256, split, sk != 0};
+          best = {1, bn, split, sk != 0};
         }
       }
     }
@@ -1195,6 +1298,9 @@ static int dispatch(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, 
     case kEpiF32Push:
       if (!GROUPED) return launch<BN, S, kEpiF32Push, false>(ma, mb, C, a, sms, s);
       break;
+    case kEpiResidNorm:
+      if (!GROUPED) return launch<BN, S, kEpiResidNorm, false>(ma, mb, C, a, sms, s);
+      break;
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1209,12 +1315,13 @@ static int pick_bn(long m_tiles, int N, int splits, int sms) {
   return wave_eff(t128, sms) > wave_eff(t256, sms) + 0.15 ? 128 : 256;
 }
 
-template <int EPI>
+template <int EPI, int PBN>
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
                        int sms, cudaStream_t stream) {
-  auto kern = gemm_pair_kernel<EPI>;
+  using L = PairLayout<PBN>;
+  auto kern = gemm_pair_kernel<EPI, PBN>;
   static std::atomic<uint64_t> attr_done{0};
-  const cudaError_t ae = smem_attr_once(kern, PairLayout::kBytes, attr_done);
+  const cudaError_t ae = smem_attr_once(kern, L::kBytes, attr_done);
   if (ae != cudaSuccess) {
     set_last_error("gemm(pair): cudaFuncSetAttribute: %s", cudaGetErrorString(ae));
     return MUK_ERR_CUDA;
@@ -1223,7 +1330,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = PairLayout::kBytes;
+  cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[1];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -1240,20 +1347,43 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
   return check_launch("muk_gemm_bf16(pair)");
 }
 
+template <int PBN>
+static int launch_pair_epi(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, void* C,
+                           const TileArgs& a, int sms, cudaStream_t stream) {
+  switch (epilogue) {
+    case MUK_EPI_BF16:
+      return launch_pair<MUK_EPI_BF16, PBN>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_F32:
+      return launch_pair<MUK_EPI_F32, PBN>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_SWIGLU:
+      return launch_pair<MUK_EPI_SWIGLU, PBN>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_BIAS_SILU:
+      return launch_pair<MUK_EPI_BIAS_SILU, PBN>(ma, mb, C, a, sms, stream);
+    case MUK_EPI_ROPE_KV:
+      return launch_pair<MUK_EPI_ROPE_KV, PBN>(ma, mb, C, a, sms, stream);
+    case kEpiF32Push:
+      return launch_pair<kEpiF32Push, PBN>(ma, mb, C, a, sms, stream);
+    case kEpiResidNorm:
+      return launch_pair<kEpiResidNorm, PBN>(ma, mb, C, a, sms, stream);
+  }
+  set_last_error("gemm: unknown epilogue %d", epilogue);
+  return MUK_ERR_INVALID_ARG;
+}
+
 static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                          int64_t ldc, int M, int N, int K, int epilogue, int split_k, bool sk,
                          const float* bias, const RopeArgs* rope, const PushArgs* push, int sms,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const NormArgs* norm = nullptr, int pbn = 256) {
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
-  if ((rc = make_map(&mb, B, ldb, K, N, kPairBN / 2))) return rc;
+  if ((rc = make_map(&mb, B, ldb, K, N, pbn / 2))) return rc;
   TileArgs a;
   a.M = M;
   a.N = N;
   a.K = K;
   a.m_tiles = (M + 255) / 256;
-  a.n_tiles = (N + kPairBN - 1) / kPairBN;
+  a.n_tiles = (N + pbn - 1) / pbn;
   a.splits = split_k;
   const int k_tiles = (K + kBK - 1) / kBK;
   a.kt_per_split = (k_tiles + split_k - 1) / split_k;
@@ -1265,31 +1395,10 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
   a.num_experts = 0;
   a.rope = rope ? *rope : RopeArgs{};
   a.push = push ? *push : PushArgs{};
+  a.norm = norm ? *norm : NormArgs{};
   set_schedule(a, sms / 2, 2, sk);
-  switch (epilogue) {
-    case MUK_EPI_BF16:
-      return launch_pair<MUK_EPI_BF16>(ma, mb, C, a, sms, stream);
-    case MUK_EPI_F32:
-      return launch_pair<MUK_EPI_F32>(ma, mb, C, a, sms, stream);
-    case MUK_EPI_SWIGLU:
-      return launch_pair<MUK_EPI_SWIGLU>(ma, mb, C, a, sms, stream);
-    case MUK_EPI_BIAS_SILU:
-      return launch_pair<MUK_EPI_BIAS_SILU>(ma, mb, C, a, sms, stream);
-    case MUK_EPI_ROPE_KV:
-      return launch_pair<MUK_EPI_ROPE_KV>(ma, mb, C, a, sms, stream);
-    case kEpiF32Push:
-      return launch_pair<kEpiF32Push>(ma, mb, C, a, sms, stream);
-  }
-  set_last_error("gemm: unknown epilogue %d", epilogue);
-  return MUK_ERR_INVALID_ARG;
-}
-
-// Pairs pay off once both CTAs of a pair have rows to work on and N fills
-// 256-wide tiles (SwiGLU needs N % 256 for its 128-row gate/up groups).
-static bool use_pair(int M, int N, int epilogue) {
-  if (M <= 128 || N < 256) return false;
-  if (epilogue == MUK_EPI_SWIGLU && N % 256 != 0) return false;
-  return true;
+  return pbn == 256 ? launch_pair_epi<256>(epilogue, ma, mb, C, a, sms, stream)
+                    : launch_pair_epi<128>(epilogue, ma, mb, C, a, sms, stream);
 }
 
 // Kernel, tile width and schedule for a dense GEMM whose split_k is fixed.
@@ -1300,7 +1409,7 @@ static GemmPlan plan_for_split(int M, int N, int K, int epilogue, int split_k, i
   for (int kind = 0; kind < 2; ++kind)
     for (int b : {256, 128})
       for (int s = 0; s < (skok ? 2 : 1); ++s) {
-        if (kind == 1 && (b != 256 || !g_pair_enabled || !use_pair(M, N, epilogue))) continue;
+        if (kind == 1 && (!g_pair_enabled || !use_pair(M, N, epilogue, b))) continue;
         if (kind == 0 && b == 256 && ((epilogue == MUK_EPI_SWIGLU && N % 256) || N <= 128))
           continue;
         const double c = plan_cost(kind, b, split_k, s != 0, M, N, K, sms);
@@ -1315,7 +1424,8 @@ static GemmPlan plan_for_split(int M, int N, int K, int epilogue, int split_k, i
 static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
                     const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream,
-                    const RopeArgs* rope = nullptr, const PushArgs* push = nullptr) {
+                    const RopeArgs* rope = nullptr, const PushArgs* push = nullptr,
+                    const NormArgs* norm = nullptr) {
   int rc = get_encode();
   if (rc) return rc;
   const int sms = sm_count();
@@ -1325,7 +1435,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
     const GemmPlan best = plan_for_split(M, N, K, epilogue, split_k, sms);
     if (best.kind == 1)
       return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, rope,
-                           push, sms, stream);
+                           push, sms, stream, norm, best.bn);
     bn = best.bn;
     sk = best.sk;
   } else {
@@ -1352,6 +1462,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   a.num_experts = num_experts;
   a.rope = rope ? *rope : RopeArgs{};
   a.push = push ? *push : PushArgs{};
+  a.norm = norm ? *norm : NormArgs{};
   set_schedule(a, sms, 1, sk);
   if (bn == 256)
     return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
@@ -1421,7 +1532,7 @@ extern "C" int muk_gemm_plan_info(int M, int N, int K, int epilogue, int split_k
   a.splits = split_k;
   if (p.kind == 1) {
     a.m_tiles = (M + 255) / 256;
-    a.n_tiles = (N + kPairBN - 1) / kPairBN;
+    a.n_tiles = (N + p.bn - 1) / p.bn;
   } else {
     a.m_tiles = (M + kBM - 1) / kBM;
     a.n_tiles = (N + p.bn - 1) / p.bn;
@@ -1486,6 +1597,115 @@ extern "C" int muk_gemm_qkv_rope(const void* A, int64_t lda, const void* B, int6
   const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
   return run_gemm(false, A, lda, B, ldb, q_out, ldq, M, N, K, MUK_EPI_ROPE_KV, 1, nullptr,
                   nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), &r);
+}
+
+static bool rownorm_ok(const MukRowNorm* rn, int M) {
+  return rn == nullptr ||
+         (rn->sumsq && rn->parts >= 1 && rn->hidden > 0 && rn->stride >= M && rn->eps >= 0.f);
+}
+
+static NormArgs consumer_norm(const MukRowNorm* rn) {
+  NormArgs n{};
+  if (rn != nullptr) {
+    n.sumsq_in = rn->sumsq;
+    n.sumsq_stride = rn->stride;
+    n.parts = rn->parts;
+    n.inv_h = 1.f / (float)rn->hidden;
+    n.eps = rn->eps;
+  }
+  return n;
+}
+
+extern "C" int muk_gemm_residual_norm(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                      int M, int N, int K, float* resid, int64_t ld_resid,
+                                      const float* norm_w, void* x_out, int64_t ldx, float* sumsq,
+                                      int64_t sumsq_stride, void* stream) {
+  MUK_REQUIRE(A && B && resid, "muk_gemm_residual_norm: null pointer");
+  MUK_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 128 == 0,
+              "muk_gemm_residual_norm: bad shape M=%d N=%d K=%d (N a multiple of 128)", M, N, K);
+  MUK_REQUIRE(lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 && MUK_ALIGNED16(A) &&
+                  MUK_ALIGNED16(B),
+              "muk_gemm_residual_norm: A/B shape or alignment");
+  MUK_REQUIRE(ld_resid >= N && ld_resid % 4 == 0 && MUK_ALIGNED16(resid),
+              "muk_gemm_residual_norm: resid must be 16-byte aligned rows of >= N floats");
+  MUK_REQUIRE(norm_w == nullptr || (x_out && sumsq && ldx >= N && ldx % 8 == 0 &&
+                                    MUK_ALIGNED16(x_out) && MUK_ALIGNED16(norm_w) &&
+                                    sumsq_stride >= M),
+              "muk_gemm_residual_norm: norm output needs x_out (16-byte rows), norm_w and sumsq");
+  if (M == 0) return MUK_OK;
+  NormArgs n{};
+  n.resid = resid;
+  n.ld_resid = ld_resid;
+  n.w = norm_w;
+  n.xout = reinterpret_cast<__nv_bfloat16*>(x_out);
+  n.ldx = ldx;
+  n.sumsq_out = sumsq;
+  n.sumsq_stride = sumsq_stride;
+  return run_gemm(false, A, lda, B, ldb, resid, ld_resid, M, N, K, kEpiResidNorm, 1, nullptr,
+                  nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), nullptr, nullptr, &n);
+}
+
+extern "C" int muk_gemm_swiglu_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                       void* C, int64_t ldc, int M, int N, int K,
+                                       const MukRowNorm* rownorm, void* stream) {
+  MUK_REQUIRE(A && B && C, "muk_gemm_swiglu_rownorm: null pointer");
+  MUK_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 128 == 0 && ldc >= N / 2,
+              "muk_gemm_swiglu_rownorm: bad shape M=%d N=%d K=%d", M, N, K);
+  MUK_REQUIRE(lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 && MUK_ALIGNED16(A) &&
+                  MUK_ALIGNED16(B),
+              "muk_gemm_swiglu_rownorm: A/B shape or alignment");
+  MUK_REQUIRE(rownorm_ok(rownorm, M), "muk_gemm_swiglu_rownorm: bad row-norm source");
+  if (M == 0) return MUK_OK;
+  const NormArgs n = consumer_norm(rownorm);
+  return run_gemm(false, A, lda, B, ldb, C, ldc, M, N, K, MUK_EPI_SWIGLU, 1, nullptr, nullptr, 0,
+                  (M + kBM - 1) / kBM, as_stream(stream), nullptr, nullptr, &n);
+}
+
+extern "C" int muk_gemm_qkv_rope_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                 void* q_out, int64_t ldq, int M, int K, const int32_t* positions,
+                                 const int32_t* slot_mapping, const float* rope_cos,
+                                 const float* rope_sin, int max_pos, int num_q_heads,
+                                 int num_kv_heads, int head_dim, const float* q_norm_w,
+                                 const float* k_norm_w, float qk_eps, void* k_cache, void* v_cache,
+                                 int num_blocks, int block_size,
+                                 const MukRowNorm* rownorm, void* stream) {
+  MUK_REQUIRE(A && B && q_out && positions && slot_mapping && rope_cos && rope_sin && k_cache &&
+                  v_cache,
+              "muk_gemm_qkv_rope_rownorm: null pointer");
+  MUK_REQUIRE(head_dim == 64 || head_dim == 128, "muk_gemm_qkv_rope_rownorm: head_dim %d (64 or 128)",
+              head_dim);
+  MUK_REQUIRE(num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "muk_gemm_qkv_rope_rownorm: heads %d/%d", num_q_heads, num_kv_heads);
+  MUK_REQUIRE(M >= 0 && K > 0 && lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 &&
+                  MUK_ALIGNED16(A) && MUK_ALIGNED16(B),
+              "muk_gemm_qkv_rope_rownorm: A/B shape or alignment");
+  MUK_REQUIRE(ldq >= (int64_t)num_q_heads * head_dim && ldq % 8 == 0 && MUK_ALIGNED16(q_out) &&
+                  MUK_ALIGNED16(k_cache) && MUK_ALIGNED16(v_cache) && MUK_ALIGNED16(rope_cos) &&
+                  MUK_ALIGNED16(rope_sin),
+              "muk_gemm_qkv_rope_rownorm: q_out / cache / table alignment");
+  MUK_REQUIRE(max_pos > 0 && num_blocks > 0 && block_size > 0, "muk_gemm_qkv_rope_rownorm: bad cache");
+  MUK_REQUIRE(rownorm_ok(rownorm, M), "muk_gemm_qkv_rope_rownorm: bad row-norm source");
+  if (M == 0) return MUK_OK;
+  const NormArgs n = consumer_norm(rownorm);
+  RopeArgs r;
+  r.positions = positions;
+  r.slots = slot_mapping;
+  r.cos = rope_cos;
+  r.sin = rope_sin;
+  r.q_norm = q_norm_w;
+  r.k_norm = k_norm_w;
+  r.k_cache = k_cache;
+  r.v_cache = v_cache;
+  r.eps = qk_eps;
+  r.max_pos = max_pos;
+  r.hq = num_q_heads;
+  r.hkv = num_kv_heads;
+  r.head_dim = head_dim;
+  r.num_blocks = num_blocks;
+  r.block_size = block_size;
+  const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  return run_gemm(false, A, lda, B, ldb, q_out, ldq, M, N, K, MUK_EPI_ROPE_KV, 1, nullptr,
+                  nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), &r, nullptr, &n);
 }
 
 extern "C" int64_t muk_gemm_allreduce_scratch_elems(int M, int N, int world) {

@@ -64,6 +64,13 @@ SIGNATURES = {
     "muk_gemm_qkv_rope": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, _P, _P, _P,
                                   _P, c_int, c_int, c_int, c_int, _P, _P, c_float, _P, _P, c_int,
                                   c_int, _P]),
+    "muk_gemm_residual_norm": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P,
+                                       c_int64, _P, _P, c_int64, _P, c_int64, _P]),
+    "muk_gemm_swiglu_rownorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int,
+                                        c_int, _P, _P]),
+    "muk_gemm_qkv_rope_rownorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, _P,
+                                          _P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, c_float,
+                                          _P, _P, c_int, c_int, _P, _P]),
     "muk_gemm_plan_info": (c_int, [c_int, c_int, c_int, c_int, c_int, _P]),
     "muk_gemm_set_stream_k": (c_int, [c_int]),
     "muk_set_peer_timeout_ms": (c_int, [c_int]),
@@ -95,6 +102,11 @@ SIGNATURES = {
     "muk_fill_decode_inputs": (c_int, [_P, _P, _P, c_int, _P]),
 }
 
+class MukRowNorm(ctypes.Structure):
+    _fields_ = [("sumsq", c_void_p), ("stride", c_int64), ("parts", c_int), ("hidden", c_int),
+                ("eps", c_float)]
+
+
 class MukLlamaLayer(ctypes.Structure):
     _fields_ = [("in_norm", c_void_p), ("wqkv", c_void_p), ("wo", c_void_p),
                 ("post_norm", c_void_p), ("wgu", c_void_p), ("wd", c_void_p)]
@@ -114,7 +126,7 @@ class MukLlamaModel(ctypes.Structure):
                 ("logits", c_void_p), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
                 ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
                 ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int),
-                ("tp_fused", c_int)]
+                ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p)]
 
 
 class MukStepBatch(ctypes.Structure):

@@ -8,6 +8,7 @@ sm_100a kernels.  Errors surface as :class:`mu_b200._lib.MukError`.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -317,22 +318,82 @@ def gemm_qkv_rope(A: torch.Tensor, B: torch.Tensor, q_out: torch.Tensor, positio
                   num_q_heads: int, num_kv_heads: int, head_dim: int, k_cache: torch.Tensor,
                   v_cache: torch.Tensor, q_norm_w: torch.Tensor | None = None,
                   k_norm_w: torch.Tensor | None = None, qk_eps: float = 1e-6,
-                  M: int | None = None):
+                  M: int | None = None, rownorm: "_lib.MukRowNorm | None" = None):
     """q|k|v projection with RoPE (+QK-norm) and the paged-KV append fused in
-    the GEMM epilogue: q heads -> q_out, k/v heads -> the caches."""
+    the GEMM epilogue: q heads -> q_out, k/v heads -> the caches.  With
+    ``rownorm`` (see :func:`row_norm`) each input row is first scaled by its
+    RMSNorm factor from a producer's partial sums."""
     _check(A, torch.bfloat16, "A")
     _check(B, torch.bfloat16, "B")
     _check(k_cache, torch.bfloat16, "k_cache")
     M = A.shape[0] if M is None else M
     K = A.shape[1]
     num_blocks, _, block_size, _ = k_cache.shape
-    args = ("muk_gemm_qkv_rope", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"),
+    name = "muk_gemm_qkv_rope" if rownorm is None else "muk_gemm_qkv_rope_rownorm"
+    args = (name, _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"),
             _p(q_out), _row_stride(q_out, "q_out"), M, K, _p(positions), _p(slot_mapping),
             _p(rope_cos), _p(rope_sin), rope_cos.shape[0], num_q_heads, num_kv_heads, head_dim,
-            _p(q_norm_w), _p(k_norm_w), qk_eps, _p(k_cache), _p(v_cache), num_blocks, block_size,
-            _stream())
+            _p(q_norm_w), _p(k_norm_w), qk_eps, _p(k_cache), _p(v_cache), num_blocks, block_size) + \
+        ((_stream(),) if rownorm is None else (ctypes.byref(rownorm), _stream()))
     if gemm_probe is None:
         call(*args)
     else:
         with gemm_probe(2.0 * M * (num_q_heads + 2 * num_kv_heads) * head_dim * K):
+            call(*args)
+
+
+def row_norm(sumsq: torch.Tensor, hidden: int, eps: float) -> "_lib.MukRowNorm":
+    """The consumer side of an RMSNorm split across two GEMMs: ``sumsq``
+    [hidden / 128, stride] f32 holds the producer's (:func:`gemm_residual_norm`)
+    per-128-column partial sums of r^2 for each row."""
+    _check(sumsq, torch.float32, "sumsq")
+    if sumsq.dim() != 2 or sumsq.stride(1) != 1 or sumsq.shape[0] != hidden // 128:
+        raise ValueError(f"row_norm: sumsq must be [{hidden // 128}, rows], got {tuple(sumsq.shape)}")
+    return _lib.MukRowNorm(sumsq.data_ptr(), sumsq.stride(0), sumsq.shape[0], hidden, eps)
+
+
+def gemm_residual_norm(A: torch.Tensor, B: torch.Tensor, resid: torch.Tensor,
+                       norm_w: torch.Tensor | None, x_out: torch.Tensor | None,
+                       sumsq: torch.Tensor | None, M: int | None = None):
+    """resid[:M] += A · Bᵀ (f32, in place); with ``norm_w``, also
+    x_out = bf16(norm_w * resid) and the per-128-column partial sums of
+    resid^2 into ``sumsq`` [N / 128, stride] — the first half of the next
+    RMSNorm, finished by a consumer GEMM given :func:`row_norm`."""
+    _check(A, torch.bfloat16, "A")
+    _check(B, torch.bfloat16, "B")
+    _check(resid, torch.float32, "resid")
+    M = A.shape[0] if M is None else M
+    N, K = B.shape[0], A.shape[1]
+    if norm_w is not None:
+        _check(norm_w, torch.float32, "norm_w")
+        _check(x_out, torch.bfloat16, "x_out")
+        _check(sumsq, torch.float32, "sumsq")
+        if sumsq.dim() != 2 or sumsq.shape[0] != N // 128 or sumsq.shape[1] < M:
+            raise ValueError(f"gemm_residual_norm: sumsq must be [{N // 128}, >= {M}]")
+    args = ("muk_gemm_residual_norm", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"), M,
+            N, K, _p(resid), _row_stride(resid, "resid"), _p(norm_w), _p(x_out),
+            _row_stride(x_out, "x_out") if x_out is not None else 0, _p(sumsq),
+            sumsq.stride(0) if sumsq is not None else 0, _stream())
+    if gemm_probe is None:
+        call(*args)
+    else:
+        with gemm_probe(2.0 * M * N * K):
+            call(*args)
+
+
+def gemm_swiglu_rownorm(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                        rownorm: "_lib.MukRowNorm | None", M: int | None = None):
+    """:func:`gemm` with MUK_EPI_SWIGLU, each input row first scaled by its
+    RMSNorm factor (``rownorm`` from :func:`row_norm`; None: unscaled)."""
+    _check(A, torch.bfloat16, "A")
+    _check(B, torch.bfloat16, "B")
+    M = A.shape[0] if M is None else M
+    N, K = B.shape[0], A.shape[1]
+    args = ("muk_gemm_swiglu_rownorm", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"),
+            _p(C), C.stride(-2), M, N, K, None if rownorm is None else ctypes.byref(rownorm),
+            _stream())
+    if gemm_probe is None:
+        call(*args)
+    else:
+        with gemm_probe(2.0 * M * N * K):
             call(*args)

@@ -214,16 +214,19 @@ class MuModelBase:
         return self._fused_rope and self.config.head_dim in (64, 128)
 
     def qkv_proj(self, layer: int, x: torch.Tensor, w: torch.Tensor, batch, cache,
-                 q_norm_w=None, k_norm_w=None) -> None:
+                 q_norm_w=None, k_norm_w=None, rownorm=None) -> None:
         """q|k|v projection of the step's tokens, RoPE'd, with k/v appended to
-        the paged cache and q left in ws.qkv for the attention kernels."""
+        the paged cache and q left in ws.qkv for the attention kernels
+        (``rownorm``: finish the input's RMSNorm in the GEMM, fused path only)."""
         cfg, ws = self.config, self.ws
         T, Hq, Hkv, D = batch.num_tokens, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         kc, vc = cache.k_cache(layer), cache.v_cache(layer)
         if self.fused_rope():
             K.gemm_qkv_rope(x, w, ws.qkv, batch.positions, batch.slot_mapping, self.rope_cos,
-                            self.rope_sin, Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, M=T)
+                            self.rope_sin, Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, M=T,
+                            rownorm=rownorm)
             return
+        assert rownorm is None, "row-norm scaling needs the fused q|k|v epilogue"
         K.gemm(x, w, ws.qkv, K.MUK_EPI_BF16, M=T)
         K.rope_kv_append(ws.qkv, batch.positions, batch.slot_mapping, self.rope_cos, self.rope_sin,
                          Hq, Hkv, D, kc, vc, q_norm_w, k_norm_w, 1e-6, num_tokens=T)

@@ -47,9 +47,28 @@ class LlamaForCausalLM(MuModelBase):
         self.native = os.environ.get("MU_NATIVE_STEP", "1") != "0"
         self._native_key = None
         self._native_model = None
+        # RMSNorm split across the projection before it and the GEMM after it,
+        # in steps of at least MU_FUSED_NORM_MIN_ROWS tokens (MU_FUSED_NORM=0:
+        # separate residual + norm kernels always).  Below that the O / down
+        # projections keep split-K, which the fused epilogue cannot use
+        # (B200, M 256: 48 us fused vs 36 us split-K + norm; M 857: 44 vs 47).
+        self._fused_norm = os.environ.get("MU_FUSED_NORM", "1") != "0"
+        self.fused_norm_min_rows = int(os.environ.get("MU_FUSED_NORM_MIN_ROWS", "512"))
 
     def act_width(self) -> int:
         return self.i_pad
+
+    def extra_workspace(self, ws, T: int) -> None:
+        H = self.config.hidden_size
+        ws.sumsq = torch.empty(max(H // 128, 1), T, device=self.device, dtype=torch.float32)
+
+    def fused_norm(self) -> bool:
+        """Residual add + RMSNorm in the O / down projection's epilogue and the
+        row scale in the next GEMM: one GPU, no mu_clamp (its clamp of the norm
+        output does not commute with the matmul), hidden a multiple of 128,
+        RoPE in the q|k|v epilogue."""
+        return (self._fused_norm and self.tp_group is None and not self.clamp.enabled
+                and self.config.hidden_size % 128 == 0 and self.fused_rope())
 
     # ---- weights -------------------------------------------------------------
     @classmethod
@@ -103,7 +122,7 @@ class LlamaForCausalLM(MuModelBase):
         """The executor's model struct (rebuilt when a buffer moves)."""
         ws, cfg = self.ws, self.config
         key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
-               self.fused_rope(), self._tp_fused)
+               self.fused_rope(), self._tp_fused, self.fused_norm(), self.fused_norm_min_rows)
         if key == self._native_key:
             return self._native_model
         layers = (_lib.MukLlamaLayer * len(self.layers))()
@@ -132,6 +151,8 @@ class LlamaForCausalLM(MuModelBase):
         m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
         m.fused_rope = int(self.fused_rope())
         m.tp_fused = int(self._tp_fused)
+        m.fused_norm = max(1, self.fused_norm_min_rows) if self.fused_norm() else 0
+        m.sumsq = ws.sumsq.data_ptr()
         m.tp_world, m.tp_rank = 1, 0
         if self.comm is not None:
             c = self.comm
@@ -154,7 +175,9 @@ class LlamaForCausalLM(MuModelBase):
         # two all-reduces per layer: fused (GEMM + finish: one extra kernel each)
         # or separate (push + finish: two each)
         tp = (2 if (m.tp_fused and T <= 512) else 4) if m.tp_world > 1 else 0
-        per_layer = (6 if m.fused_rope else 7) + (2 if nd > 0 else 0) + (1 if B > nd else 0) + tp
+        fused = m.fused_norm > 0 and T >= m.fused_norm
+        per_layer = ((4 if fused else 6 if m.fused_rope else 7) + (2 if nd > 0 else 0)
+                     + (1 if B > nd else 0) + tp)
         _lib.call_counted("muk_llama_forward", 4 + per_layer * m.num_layers, ctypes.byref(m),
                           ctypes.byref(b), torch.cuda.current_stream().cuda_stream)
         return self.ws.logits[:B]
@@ -168,6 +191,20 @@ class LlamaForCausalLM(MuModelBase):
         K.embed(batch.input_ids, self.embed, resid, cl)
         K.residual_rmsnorm(resid, None, self.layers[0]["w_in"], eps, x, clamp=cl, clamp_norm=True)
         nl = len(self.layers)
+        if self.fused_norm() and T >= max(1, self.fused_norm_min_rows):
+            # x holds bf16(w * h); the GEMM that reads it scales each row by
+            # rsqrt(mean(h^2) + eps) from the producer's partial sums
+            rn = K.row_norm(ws.sumsq, H, eps)
+            for l, L in enumerate(self.layers):
+                self.qkv_proj(l, x, L["wqkv"], batch, cache, rownorm=rn if l > 0 else None)
+                attn = self.attention(l, batch, cache)
+                K.gemm_residual_norm(attn[:T], L["wo"], resid, L["w_post"], x, ws.sumsq, M=T)
+                K.gemm_swiglu_rownorm(x, L["wgu"], ws.act, rn, M=T)
+                last = l + 1 == nl
+                K.gemm_residual_norm(ws.act[:T], L["wd"], resid,
+                                     None if last else self.layers[l + 1]["w_in"],
+                                     None if last else x, None if last else ws.sumsq, M=T)
+            return self.lm_head(batch, self.norm_w, self.lm_w)
         for l, L in enumerate(self.layers):
             self.qkv_proj(l, x, L["wqkv"], batch, cache)
             attn = self.attention(l, batch, cache)

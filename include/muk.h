@@ -221,6 +221,52 @@ int muk_gemm_qkv_rope(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       const float* q_norm_w, const float* k_norm_w, float qk_eps, void* k_cache,
                       void* v_cache, int num_blocks, int block_size, void* stream);
 
+/* ---- RMSNorm split across a projection and the next GEMM ----------------- */
+
+/* Where a consumer GEMM finds the per-row RMSNorm of its input rows: the
+ * producer's partial sums of squares sumsq[p * stride + row] for p < parts
+ * (one per 128 columns of the hidden size); the row scale is
+ * rsqrt(sum / hidden + eps). */
+typedef struct MukRowNorm {
+  const float* sumsq;
+  int64_t stride;
+  int parts;
+  int hidden;
+  float eps;
+} MukRowNorm;
+
+/* Row-parallel projection (O or down, one GPU, split-K 1) with the residual
+ * update and half of the next RMSNorm in its epilogue:
+ *   resid[m, :] += A[m, :] · Bᵀ                       (f32, in place)
+ *   if norm_w:  x_out[m, :] = bf16(norm_w ⊙ resid[m, :]) and
+ *               sumsq[p * sumsq_stride + m] = Σ_{128 p <= n < 128 (p+1)} resid[m, n]²
+ * N must be a multiple of 128.  The consumer (muk_gemm_swiglu_rownorm,
+ * muk_gemm_qkv_rope_rownorm) applies rsqrt(Σ_p sumsq / N + eps) to its
+ * accumulator rows, which makes it the RMSNorm of
+ * mu_inference/models/layers.py:149-164 (without mu_clamp on the norm, whose
+ * nonlinearity does not commute) fused into the two GEMMs around it; the
+ * residual add is llama.py:111-126. */
+int muk_gemm_residual_norm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
+                           int K, float* resid, int64_t ld_resid, const float* norm_w, void* x_out,
+                           int64_t ldx, float* sumsq, int64_t sumsq_stride, void* stream);
+
+/* muk_gemm_bf16 with MUK_EPI_SWIGLU whose accumulator rows are scaled by the
+ * row norm of `rownorm` (NULL: unscaled) before the SwiGLU. */
+int muk_gemm_swiglu_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
+                            int64_t ldc, int M, int N, int K, const MukRowNorm* rownorm,
+                            void* stream);
+
+/* muk_gemm_qkv_rope whose accumulator rows are scaled by the row norm of
+ * `rownorm` (NULL: unscaled) before QK-norm / RoPE / the KV append. */
+int muk_gemm_qkv_rope_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb,
+                              void* q_out, int64_t ldq, int M, int K, const int32_t* positions,
+                              const int32_t* slot_mapping, const float* rope_cos,
+                              const float* rope_sin, int max_pos, int num_q_heads,
+                              int num_kv_heads, int head_dim, const float* q_norm_w,
+                              const float* k_norm_w, float qk_eps, void* k_cache, void* v_cache,
+                              int num_blocks, int block_size, const MukRowNorm* rownorm,
+                              void* stream);
+
 /* Split-K factor (1..max_split) that muk_gemm_bf16 runs fastest for this
  * shape with MUK_EPI_F32 (1 for other epilogues): the same makespan model the
  * launcher uses to choose between 128/256-wide single-CTA tiles and CTA-pair
@@ -475,6 +521,11 @@ typedef struct {
   uint32_t* ar_flags[8];
   int fused_rope; /* 1: RoPE + KV append in the q|k|v GEMM epilogue (muk_gemm_qkv_rope) */
   int tp_fused;   /* 1: O / down projections as muk_gemm_allreduce_f32 under TP */
+  int fused_norm; /* > 0: steps of at least this many tokens split residual + RMSNorm across
+                     the GEMMs (muk_gemm_residual_norm and the _rownorm consumers; needs
+                     tp_world 1, clamp 0, hidden % 128 == 0, fused_rope); smaller steps keep
+                     split-K projections and the separate norm kernel.  0: never */
+  float* sumsq;   /* [hidden / 128][max tokens] f32 partial sums when fused_norm */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */

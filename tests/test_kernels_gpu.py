@@ -722,3 +722,105 @@ def test_gemm_qkv_rope(cuda, M, Hq, Hkv, D, qk_norm):
     from mu_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+# RMSNorm split across two GEMMs: the producer (O / down projection) adds its
+# output to the f32 residual and leaves bf16(w * r) plus per-128-column
+# partial sums of r^2; the consumer (gate|up or q|k|v) scales each row by
+# rsqrt(mean(r^2) + eps).  (M, N, K, stream-K mode): one row, a CTA-pair
+# shape, the Llama-3-8B O projection at a mean step, one 128-column part.
+@pytest.mark.parametrize("M,N,K,sk", [(1, 512, 384, 0), (130, 1024, 640, 0),
+                                      (857, 4096, 4096, 1), (600, 4096, 4096, 0),
+                                      (300, 128, 256, 2)])
+def test_gemm_residual_norm(cuda, M, N, K, sk):
+    k = _kern()
+    prev = k.gemm_set_stream_k(sk)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(M + N)
+        A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+        W = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+        r0 = torch.randn(M + 3, N, device=cuda, generator=g) * 2
+        w = 1 + 0.1 * torch.randn(N, device=cuda, generator=g)
+        resid = r0.clone()
+        xbuf = torch.full((M + 3, 2 * N), float("nan"), device=cuda, dtype=torch.bfloat16)
+        x = xbuf[:, :N]                                   # row stride 2N, like [x | mu_prev]
+        sumsq = torch.full((N // 128, M + 5), float("nan"), device=cuda)
+        k.gemm_residual_norm(A, W, resid, w, x, sumsq, M=M)
+        ref = r0[:M] + A.float() @ W.float().t()
+        torch.testing.assert_close(resid[:M], ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
+        assert torch.equal(resid[M:], r0[M:])            # rows past M untouched
+        assert torch.equal(x[:M], (w * resid[:M]).bfloat16())
+        assert torch.isnan(xbuf[M:].float()).all() and torch.isnan(xbuf[:, N:].float()).all()
+        ss = resid[:M].pow(2).view(M, N // 128, 128).sum(-1).t()
+        torch.testing.assert_close(sumsq[:, :M], ss, rtol=1e-5, atol=1e-5 * ss.max().item())
+        assert torch.isnan(sumsq[:, M:]).all()
+        # without a norm weight: the residual add alone
+        resid2 = r0.clone()
+        k.gemm_residual_norm(A, W, resid2, None, None, None, M=M)
+        assert torch.equal(resid2, resid)
+    finally:
+        k.gemm_set_stream_k(prev)
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,sk", [(1, 0), (300, 0), (809, 1)])
+def test_gemm_rownorm_consumers(cuda, M, sk):
+    k = _kern()
+    H, I, eps = 1024, 1536, 1e-5
+    Hq, Hkv, D, NB, bs = 8, 2, 128, 64, 16
+    g = torch.Generator(device="cuda").manual_seed(M + 11)
+    h = torch.randn(M, H, device=cuda, generator=g) * 3
+    w = 1 + 0.1 * torch.randn(H, device=cuda, generator=g)
+    xt = (w * h).bfloat16()
+    sumsq = torch.zeros(H // 128, M + 7, device=cuda)
+    sumsq[:, :M] = h.pow(2).view(M, H // 128, 128).sum(-1).t()
+    s = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    a = xt.float() * s                                  # the normed input the consumers see
+    rn = k.row_norm(sumsq, H, eps)
+    prev = k.gemm_set_stream_k(sk)
+    try:
+        Wg = (torch.randn(I, H, device=cuda, generator=g) * 0.05).bfloat16()
+        Wu = (torch.randn(I, H, device=cuda, generator=g) * 0.05).bfloat16()
+        W = torch.stack([Wg.view(I // 64, 64, H), Wu.view(I // 64, 64, H)], 1).reshape(2 * I, H)
+        C = torch.empty(M, I, device=cuda, dtype=torch.bfloat16)
+        k.gemm_swiglu_rownorm(xt, W, C, rn)
+        ref = torch.nn.functional.silu(a @ Wg.float().t()) * (a @ Wu.float().t())
+        torch.testing.assert_close(C.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+        # no row norm: the plain SwiGLU GEMM
+        C0 = torch.empty_like(C)
+        k.gemm_swiglu_rownorm(xt, W, C0, None)
+        C1 = torch.empty_like(C)
+        k.gemm(xt, W, C1, k.MUK_EPI_SWIGLU)
+        assert torch.equal(C0, C1)
+
+        N = (Hq + 2 * Hkv) * D
+        Wq = (torch.randn(N, H, device=cuda, generator=g) * 0.05).bfloat16()
+        pos = torch.randint(0, 500, (M,), device=cuda, generator=g, dtype=torch.int32)
+        slots = torch.randperm(NB * bs, device=cuda, generator=g)[:M].to(torch.int32)
+        cos, sin = _rope_tables(512, D, 10000.0, cuda)
+        kc = torch.zeros(NB, Hkv, bs, D, device=cuda, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        q_out = torch.zeros(M, N, device=cuda, dtype=torch.bfloat16)
+        k.gemm_qkv_rope(xt, Wq, q_out, pos, slots, cos, sin, Hq, Hkv, D, kc, vc, rownorm=rn)
+    finally:
+        k.gemm_set_stream_k(prev)
+    x = a @ Wq.float().t()
+    c = torch.cat([cos, cos], -1)[pos.long()].unsqueeze(1)
+    sn = torch.cat([sin, sin], -1)[pos.long()].unsqueeze(1)
+
+    def rope(t):
+        return t * c + torch.cat([-t[..., D // 2:], t[..., : D // 2]], -1) * sn
+
+    q_ref = rope(x[:, : Hq * D].view(M, Hq, D))
+    k_ref = rope(x[:, Hq * D:(Hq + Hkv) * D].view(M, Hkv, D))
+    v_ref = x[:, (Hq + Hkv) * D:].view(M, Hkv, D)
+    tol = dict(rtol=2e-2, atol=2e-2 * max(1.0, float(q_ref.abs().max())))
+    torch.testing.assert_close(q_out[:, : Hq * D].float().view(M, Hq, D), q_ref, **tol)
+    blk, off = (slots // bs).long(), (slots % bs).long()
+    torch.testing.assert_close(kc[blk, :, off].float(), k_ref, **tol)
+    torch.testing.assert_close(vc[blk, :, off].float(), v_ref, **tol)
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0

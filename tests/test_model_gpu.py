@@ -25,12 +25,12 @@ LOGIT_TOL = 2e-2      # max-abs, bf16 path vs fp32 reference
 GAP_TOL = 0.05        # reference top-2 gap below which argmax may flip
 
 
-def _worker(name, cuda, graphs=True, max_batch=8, blocks=512):
+def _worker(name, cuda, graphs=True, max_batch=8, blocks=512, mu=True):
     from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
     from mu_b200.serving.worker import MuWorker
 
     shape, cfg, sd, d, prompts = load_tiny(name)
-    ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True),
+    ec = EngineConfig(model=cfg, mu=MuConfig(enabled=mu),
                       cache=CacheConfig(max_seq_len=256, max_num_blocks=blocks, max_num_seqs=16),
                       scheduler=SchedulerConfig(max_batch_size=max_batch,
                                                 max_num_batched_tokens=2048))
@@ -335,3 +335,51 @@ def test_native_executor_matches_python_step(cuda, graphs):
         outs.append(got)
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_fused_norm_step_without_mu_clamp(cuda):
+    """With mu_clamp off (the Llama-3-8B serving configuration) the residual
+    add + RMSNorm run inside the O / down projections' epilogues and the next
+    GEMM's row scale.  Against the live fp32 oracle (no clamp) over a prefill
+    step and five teacher-forced decode steps: the fused step (Python and
+    native executor, bit-identical to each other) and the unfused step stay
+    within 2e-2 max-abs of the oracle's logits."""
+    from mu_b200.serving.worker import WorkerRequest
+
+    w, shape, d, prompts, _ = _worker("llama_tiny", cuda, graphs=False, mu=False)
+    params = {k: v.float().cpu().numpy() for k, v in load_tiny("llama_tiny")[2].items()}
+    oracle = O.OracleModel(shape, params, O.MuCfg(False))
+    R, n = len(prompts), 6
+    logits, pasts, _ = oracle.forward_batch(prompts)
+    ref, toks = [logits], [np.argmax(logits, -1)]
+    for i in range(n - 1):
+        logits, pasts, _ = oracle.forward_batch([[int(t)] for t in toks[-1]], pasts)
+        ref.append(logits)
+        toks.append(np.argmax(logits, -1))
+    runs = {}
+    for fused, native in ((True, False), (True, True), (False, True)):
+        w, *_ = _worker("llama_tiny", cuda, graphs=False, mu=False)
+        w.model.native = native
+        w.model._fused_norm = fused
+        w.model.fused_norm_min_rows = 1   # decode steps too
+        assert w.model.fused_norm() == fused
+        for r in range(R):
+            assert w.allocate_request(f"r{r}")
+        got = []
+        for i in range(n):
+            if i == 0:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([prompts[r]]), is_prefill=True)
+                        for r in range(R)]
+            else:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([[int(toks[i - 1][r])]]),
+                                      is_prefill=False) for r in range(R)]
+            lg = torch.cat([o.logits for o in w.execute(reqs)]).float().cpu()
+            err = float(np.abs(lg.numpy() - ref[i]).max())
+            assert err <= LOGIT_TOL, (fused, native, i, err)
+            got.append(lg)
+        runs[(fused, native)] = got
+    for a, b in zip(runs[(True, False)], runs[(True, True)]):
+        assert torch.equal(a, b)
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
