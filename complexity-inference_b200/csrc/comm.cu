@@ -178,6 +178,117 @@ __global__ void __launch_bounds__(kArThreads) allreduce_finish_kernel(const ArAr
 }
 
 // ---------------------------------------------------------------------------
+// Reduce-scatter + residual + RMSNorm + all-gather (muk_tp_residual_norm):
+// the tensor-parallel form of "all-reduce the row-parallel projection, then
+// h += delta; x = norm(h)".  Rows are owned in contiguous shares of
+// share_rows rows; the pushes (the push kernel above, or the GEMM's push
+// epilogue) leave every rank's partial of rank r's rows in r's scratch.
+// Finish, one CTA per owned row: wait for every rank's "pushed", sum the
+// row over the ranks in rank order (bit-identical to the all-reduce's sum),
+// add it to this rank's f32 residual row (only owned rows of the residual
+// are kept current), normalise, and store the bf16 row into every rank's x
+// buffer (NVLink stores), then the "done" barrier.  Per rank and projection
+// NVLink carries (P-1)/P of the f32 partials plus (P-1)/P of the bf16 rows,
+// against 2 (P-1)/P of the f32 partials for the all-reduce, and the
+// residual/norm pass covers T/P rows instead of T.
+struct TpNormArgs {
+  ArArgs ar;
+  int T, H, share_rows;
+  float* resid;
+  int64_t ld_resid;
+  const float* w;
+  float eps;
+  uint4* x[kMaxRanks];
+  int64_t ldx8;  // row stride of x in 16-byte units
+  int clamp_delta, clamp_sum;
+  ClampParams cp, cp_norm;
+};
+
+constexpr int kTpNormThreads = 256;
+
+__global__ void __launch_bounds__(kTpNormThreads) tp_norm_finish_kernel(const TpNormArgs a) {
+  const ArArgs& ar = a.ar;
+  uint32_t* my = ar.flags[ar.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) + 1u;
+  __shared__ int ok;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) ok = wait_all(my, kFlagA, ar.world, epoch);
+  __syncthreads();
+  if (ok) {
+    const int row0 = ar.rank * a.share_rows;
+    const int rows = min(a.T, row0 + a.share_rows) - row0;
+    const int h4 = a.H >> 2;
+    const float4* own = ar.data[ar.rank];
+    const float4* scr = ar.scratch[ar.rank];
+    for (int rl = blockIdx.x; rl < rows; rl += gridDim.x) {
+      const int row = row0 + rl;
+      float4* rrow = reinterpret_cast<float4*>(a.resid + (int64_t)row * a.ld_resid);
+      float ss = 0.f;
+      for (int j = threadIdx.x; j < h4; j += blockDim.x) {
+        const int64_t i = (int64_t)row * h4 + j;
+        const int64_t k = (int64_t)rl * h4 + j;
+        float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+          if (s < ar.world) {
+            const float4 v = (s == ar.rank && !ar.own_in_scratch) ? folded(ar, own, i)
+                                                                   : scr[(int64_t)s * ar.share + k];
+            d.x += v.x;
+            d.y += v.y;
+            d.z += v.z;
+            d.w += v.w;
+          }
+        if (a.clamp_delta) {
+          d.x = mu_clamp(d.x, a.cp);
+          d.y = mu_clamp(d.y, a.cp);
+          d.z = mu_clamp(d.z, a.cp);
+          d.w = mu_clamp(d.w, a.cp);
+        }
+        float4 r = rrow[j];
+        r.x += d.x;
+        r.y += d.y;
+        r.z += d.z;
+        r.w += d.w;
+        if (a.clamp_sum) {
+          r.x = mu_clamp(r.x, a.cp);
+          r.y = mu_clamp(r.y, a.cp);
+          r.z = mu_clamp(r.z, a.cp);
+          r.w = mu_clamp(r.w, a.cp);
+        }
+        rrow[j] = r;
+        ss += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
+      }
+      if (a.w == nullptr) continue;
+      // block_sum's barriers also make this CTA's residual stores visible to
+      // the second pass
+      const float inv = rsqrtf(block_sum(ss, red) / (float)a.H + a.eps);
+      const float4* w4 = reinterpret_cast<const float4*>(a.w);
+      for (int j = threadIdx.x; j < (a.H >> 3); j += blockDim.x) {
+        const float4 r0 = rrow[2 * j], r1 = rrow[2 * j + 1];
+        const float4 w0 = w4[2 * j], w1 = w4[2 * j + 1];
+        uint4 pk;
+        pk.x = pack_bf16x2(mu_clamp(w0.x * (r0.x * inv), a.cp_norm),
+                           mu_clamp(w0.y * (r0.y * inv), a.cp_norm));
+        pk.y = pack_bf16x2(mu_clamp(w0.z * (r0.z * inv), a.cp_norm),
+                           mu_clamp(w0.w * (r0.w * inv), a.cp_norm));
+        pk.z = pack_bf16x2(mu_clamp(w1.x * (r1.x * inv), a.cp_norm),
+                           mu_clamp(w1.y * (r1.y * inv), a.cp_norm));
+        pk.w = pack_bf16x2(mu_clamp(w1.z * (r1.z * inv), a.cp_norm),
+                           mu_clamp(w1.w * (r1.w * inv), a.cp_norm));
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+          if (s < ar.world) a.x[s][(int64_t)row * a.ldx8 + j] = pk;
+      }
+    }
+  }
+  if (last_cta(my + kFlagArrive2)) {
+    for (int s = 0; s < ar.world; ++s) st_release_sys(ar.flags[s] + kFlagB + ar.rank, epoch);
+    wait_all(my, kFlagB, ar.world, epoch);
+    *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) = epoch;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Expert-parallel combine: every rank holds every token (head-parallel
 // attention), routes them identically and computes only its own experts'
 // rows, which sit at the same expert-sorted row indices on every rank.  The
@@ -291,6 +402,43 @@ int launch_allreduce_finish(float* const* bufs, float* const* scratch, uint32_t*
   grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
   allreduce_finish_kernel<<<grid, kArThreads, 0, stream>>>(a);
   return check_launch("allreduce finish");
+}
+
+int launch_tp_norm_finish(float* const* bufs, float* const* scratch, uint32_t* const* flags,
+                          int rank, int world, int T, int H, int share_rows, int slices,
+                          int64_t slice_stride, bool own_in_scratch, float* resid,
+                          int64_t ld_resid, const float* norm_w, float eps, void* const* x_bufs,
+                          int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                          float cmin, float cmax, cudaStream_t stream) {
+  TpNormArgs a;
+  for (int s = 0; s < kMaxRanks; ++s) {
+    a.ar.data[s] = s < world ? reinterpret_cast<float4*>(bufs[s]) : nullptr;
+    a.ar.scratch[s] = s < world ? reinterpret_cast<float4*>(scratch[s]) : nullptr;
+    a.ar.flags[s] = s < world ? flags[s] : nullptr;
+    a.x[s] = s < world ? reinterpret_cast<uint4*>(x_bufs[s]) : nullptr;
+  }
+  a.ar.rank = rank;
+  a.ar.world = world;
+  a.ar.n4 = (int64_t)T * H / 4;
+  a.ar.share = (int64_t)share_rows * H / 4;
+  a.ar.slices = slices;
+  a.ar.slice_stride4 = slice_stride / 4;
+  a.ar.own_in_scratch = own_in_scratch ? 1 : 0;
+  a.T = T;
+  a.H = H;
+  a.share_rows = share_rows;
+  a.resid = resid;
+  a.ld_resid = ld_resid;
+  a.w = norm_w;
+  a.eps = eps;
+  a.ldx8 = ldx / 8;
+  a.clamp_delta = clamp_delta;
+  a.clamp_sum = clamp_sum;
+  a.cp = make_clamp(clamp_delta || clamp_sum, mu, cmin, cmax);
+  a.cp_norm = make_clamp(clamp_norm, mu, cmin, cmax);
+  int grid = share_rows < 1 ? 1 : (share_rows > 1184 ? 1184 : share_rows);
+  tp_norm_finish_kernel<<<grid, kTpNormThreads, 0, stream>>>(a);
+  return check_launch("tp residual norm (finish)");
 }
 
 }  // namespace muk
@@ -429,4 +577,57 @@ extern "C" int muk_ep_gather_bf16(void* const* bufs, uint32_t* const* flags, int
   if (rc) return rc;
   ep_gather_finish_kernel<<<1, 32, 0, st>>>(a);
   return check_launch("muk_ep_gather_bf16(finish)");
+}
+
+extern "C" int muk_tp_residual_norm(float* const* bufs, float* const* scratch,
+                                    uint32_t* const* flags, int rank, int world, int T, int H,
+                                    int slices, int64_t slice_stride, float* resid,
+                                    const float* norm_w, float eps, void* const* x_bufs,
+                                    int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm,
+                                    float mu, float cmin, float cmax, void* stream) {
+  MUK_REQUIRE(bufs && scratch && flags && world >= 1 && world <= kMaxRanks && rank >= 0 &&
+                  rank < world,
+              "muk_tp_residual_norm: rank %d of %d (at most %d ranks)", rank, world, kMaxRanks);
+  MUK_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "muk_tp_residual_norm: T=%d H=%d (H %% 8 == 0)", T,
+              H);
+  MUK_REQUIRE(slices >= 1 && (slices == 1 || (slice_stride >= (int64_t)T * H &&
+                                              slice_stride % 4 == 0)),
+              "muk_tp_residual_norm: %d slices need a slice stride >= T*H, multiple of 4", slices);
+  MUK_REQUIRE(resid && MUK_ALIGNED16(resid), "muk_tp_residual_norm: resid null / unaligned");
+  MUK_REQUIRE(norm_w == nullptr || (x_bufs && ldx >= H && ldx % 8 == 0 && MUK_ALIGNED16(norm_w)),
+              "muk_tp_residual_norm: a norm needs x buffers (row stride a multiple of 8) and an "
+              "aligned weight");
+  for (int s = 0; s < world; ++s) {
+    MUK_REQUIRE(bufs[s] && scratch[s] && flags[s] && MUK_ALIGNED16(bufs[s]) &&
+                    MUK_ALIGNED16(scratch[s]) && MUK_ALIGNED16(flags[s]),
+                "muk_tp_residual_norm: rank %d buffer, scratch or flags null / not aligned", s);
+    MUK_REQUIRE(norm_w == nullptr || (x_bufs[s] && MUK_ALIGNED16(x_bufs[s])),
+                "muk_tp_residual_norm: rank %d x buffer null / not 16-byte aligned", s);
+  }
+  if (T == 0) return MUK_OK;
+  const int share_rows = (T + world - 1) / world;
+  cudaStream_t st = as_stream(stream);
+  {  // with one rank the push only signals "pushed"
+    ArArgs a;
+    for (int s = 0; s < kMaxRanks; ++s) {
+      a.data[s] = s < world ? reinterpret_cast<float4*>(bufs[s]) : nullptr;
+      a.scratch[s] = s < world ? reinterpret_cast<float4*>(scratch[s]) : nullptr;
+      a.flags[s] = s < world ? flags[s] : nullptr;
+    }
+    a.rank = rank;
+    a.world = world;
+    a.n4 = (int64_t)T * H / 4;
+    a.share = (int64_t)share_rows * H / 4;
+    a.slices = slices;
+    a.slice_stride4 = slice_stride / 4;
+    a.own_in_scratch = 0;
+    int grid = (int)((a.share * (world - 1) + kArThreads - 1) / kArThreads);
+    grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
+    allreduce_push_kernel<<<grid, kArThreads, 0, st>>>(a);
+    const int rc = check_launch("muk_tp_residual_norm(push)");
+    if (rc) return rc;
+  }
+  return launch_tp_norm_finish(bufs, scratch, flags, rank, world, T, H, share_rows, slices,
+                               slice_stride, false, resid, H, norm_w, eps, x_bufs, ldx,
+                               clamp_delta, clamp_sum, clamp_norm, mu, cmin, cmax, st);
 }

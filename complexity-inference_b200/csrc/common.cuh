@@ -94,6 +94,32 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+__host__ __device__ inline ClampParams make_clamp(int enabled, float mu, float cmin, float cmax) {
+  ClampParams p;
+  p.enabled = enabled;
+  p.mu = mu;
+  p.center = (cmax + cmin) * 0.5f;
+  p.range = (cmax - cmin) * 0.5f;
+  p.inv_range = p.range > 0.f ? 1.f / p.range : 0.f;
+  return p;
+}
+
+// Sum of `v` over the CTA; `red` is >= 32 floats of shared scratch.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (warp == 0) {
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -197,6 +223,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "%4}], [%2];\n" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start before the previous kernel on
+// its stream has finished; griddepcontrol.wait blocks until that kernel has
+// completed and its memory operations are visible (it returns at once when
+// the launch has no such dependency).  launch_dependents lets the next
+// kernel start launching before this one ends.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -134,6 +134,57 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
                          1, nullptr, stream);
   }
 
+  // q|k|v projection with RoPE and the KV append (fused or as two kernels)
+  auto qkv_proj = [&](const MukLlamaLayer& L, void* kc, void* vc) -> int {
+    if (m->fused_rope)
+      return muk_gemm_qkv_rope(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, H, b->positions,
+                               b->slot_mapping, m->rope_cos, m->rope_sin, m->rope_len, Hq, Hkv, D,
+                               nullptr, nullptr, 1e-6f, kc, vc, m->num_blocks, m->block_size,
+                               stream);
+    MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wqkv, H, qkv, qkv_n, T, qkv_n, H, kEpiBf16, 1, nullptr,
+                          stream));
+    return muk_rope_kv_append(qkv, qkv_n, b->positions, b->slot_mapping, m->rope_cos, m->rope_sin,
+                              m->rope_len, T, Hq, Hkv, D, nullptr, nullptr, 1e-6f, kc, vc,
+                              m->num_blocks, m->block_size, stream);
+  };
+
+  if (m->tp_world > 1 && m->tp_norm) {
+    MUK_REQUIRE(m->x == m->x_peer[m->tp_rank], "muk_llama_forward: tp_norm needs x = x_peer[rank]");
+    // Row-parallel projection -> reduce-scatter -> h += clamp(delta) on the
+    // owned rows -> x = clamp(norm(h)) all-gathered to every rank.  The
+    // residual stays row-sharded; the last layer applies the final norm, and
+    // the LM head reads each sequence's last row of x.
+    auto project_norm = [&](const void* A, int lda, const void* W, int K, const float* norm_w,
+                            int clamp_sum) -> int {
+      if (fused_tp)
+        return muk_gemm_tp_residual_norm(A, lda, W, K, T, H, K, m->ar_data, m->ar_scratch,
+                                         m->ar_flags, m->tp_rank, m->tp_world, m->resid, norm_w,
+                                         m->eps, m->x_peer, m->x_stride, cl, clamp_sum, cl, mu,
+                                         cmin, cmax, stream);
+      const int s = choose_split(T, H, K, m->part_rows);
+      MUK_TRY(muk_gemm_bf16(A, lda, W, K, m->part, H, T, H, K, kEpiF32, s, nullptr, stream));
+      return muk_tp_residual_norm(m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world,
+                                  T, H, s, (int64_t)T * H, m->resid, norm_w, m->eps, m->x_peer,
+                                  m->x_stride, cl, clamp_sum, cl, mu, cmin, cmax, stream);
+    };
+    for (int l = 0; l < m->num_layers; ++l) {
+      const MukLlamaLayer& L = m->layers[l];
+      void* kc = pool + (int64_t)(2 * l) * layer_elems;
+      void* vc = pool + (int64_t)(2 * l + 1) * layer_elems;
+      MUK_TRY(qkv_proj(L, kc, vc));
+      MUK_TRY(attention(l, kc, vc));
+      MUK_TRY(project_norm(attn, attn_n, L.wo, attn_n, L.post_norm, 0));
+      MUK_TRY(muk_gemm_bf16(x, m->x_stride, L.wgu, H, m->act, m->inter_pad, T, 2 * m->inter_pad,
+                            H, kEpiSwiglu, 1, nullptr, stream));
+      const bool last = l + 1 == m->num_layers;
+      MUK_TRY(project_norm(m->act, m->inter_pad, L.wd, m->inter_pad,
+                           last ? m->final_norm : m->layers[l + 1].in_norm, cl));
+    }
+    MUK_TRY(muk_gather_rows_bf16(x, m->x_stride, b->last_token_idx, B, m->xl, H, H, stream));
+    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32,
+                         1, nullptr, stream);
+  }
+
   for (int l = 0; l < m->num_layers; ++l) {
     const MukLlamaLayer& L = m->layers[l];
     void* kc = pool + (int64_t)(2 * l) * layer_elems;

@@ -69,6 +69,17 @@ static bool g_pair_enabled = true;
 // (~384 clocks at 128 B/clock), so these tiles are shared-memory-bound; they
 // win only where tile count dominates (M 256, N 4096: 32 tiles on 74 pairs,
 // 31 us vs 38 us with 256-wide tiles).  MUK_GEMM_PAIR128_COST overrides.
+// GEMMs launch as programmatic dependents of the previous kernel on the
+// stream (prologue and the first weight tiles overlap its tail); MUK_PDL=0
+// launches them fully serialised.
+static int g_pdl = -1;
+static bool pdl_enabled() {
+  if (g_pdl < 0) {
+    const char* e = getenv("MUK_PDL");
+    g_pdl = (e && e[0] == '0') ? 0 : 1;
+  }
+  return g_pdl != 0;
+}
 static double g_pair128_cost = [] {
   const char* e = getenv("MUK_GEMM_PAIR128_COST");
   return e ? atof(e) : 0.67;
@@ -701,10 +712,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // every CTA of this persistent grid is resident: the next kernel on the
+  // stream may start launching (its CTAs take SMs as ours leave)
+  grid_dep_launch();
 
   if (warp == 0) {
     // ---- TMA producer ----
     if (lane == 0) {
+      // Weights do not depend on the previous kernel: with a dense schedule
+      // the first tile's B k-tiles are requested before waiting for it.
+      int pre = 0;
+      if (!GROUPED) {
+        Unit u0;
+        for (int idx = 0; get_unit(args, w, idx, u0); ++idx) {
+          const Tile t0 = unit_tile<BN, GROUPED>(args, u0);
+          if (!t0.valid) continue;
+          pre = t0.nk < STAGES ? t0.nk : STAGES;
+          for (int i = 0; i < pre; ++i) {  // fresh ring: stage i, no empty wait
+            mbar_arrive_expect_tx(&full[i], (uint32_t)L::kStage);
+            tma_load_2d(base + (uint32_t)(i * L::kStage) + L::kA, &tmB, &full[i],
+                        (t0.kt0 + i) * kBK, t0.brow0);
+          }
+          break;
+        }
+      }
+      grid_dep_wait();
       uint32_t it = 0;
       bool ok = true;
       Unit u;
@@ -714,19 +746,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < tl.nk; ++i, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
+          if ((int)it < pre) {  // B already requested, the barrier armed
+            tma_load_2d(sa, &tmA, &full[s], (tl.kt0 + i) * kBK, tl.row0);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[s], (uint32_t)L::kStage);
-          const uint32_t sa = base + (uint32_t)(s * L::kStage);
           tma_load_2d(sa, &tmA, &full[s], (tl.kt0 + i) * kBK, tl.row0);
           tma_load_2d(sa + L::kA, &tmB, &full[s], (tl.kt0 + i) * kBK, tl.brow0);
         }
       }
+    } else {
+      grid_dep_wait();
     }
     __syncwarp();
   } else if (warp == 1) {
+    grid_dep_wait();
     // ---- MMA issuer ----
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kBM, BN);
@@ -765,6 +804,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else {
+    grid_dep_wait();
     // ---- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----
     const int quarter = warp & 3;
     uint32_t use = 0;
@@ -901,9 +941,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_launch();  // all pairs are resident (see the dense kernel)
 
   if (warp == 0) {
     if (lane == 0) {
+      // the first tile's B halves (weights) before waiting for the previous kernel
+      int pre = 0;
+      {
+        Unit u0;
+        if (get_unit(args, pair, 0, u0)) {
+          const PairTile p0 = pair_tile(args, u0);
+          pre = p0.nk < S ? p0.nk : S;
+          const int brow0 = p0.nt * BN + (int)rank * (BN / 2);
+          for (int i = 0; i < pre; ++i) {  // fresh ring: stage i, no empty wait
+            if (leader) mbar_arrive_expect_tx(&full[i], 2u * (uint32_t)L::kStage);
+            tma_load_2d_pair(base + (uint32_t)(i * L::kStage) + L::kA, &tmB, &full[i],
+                             (p0.kt0 + i) * kBK, brow0);
+          }
+        }
+      }
+      grid_dep_wait();
       uint32_t it = 0;
       bool ok = true;
       Unit u;
@@ -914,19 +971,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < pt.nk; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
+          const uint32_t sa = base + (uint32_t)(s * L::kStage);
+          if ((int)it < pre) {  // B already requested, the barrier armed
+            tma_load_2d_pair(sa, &tmA, &full[s], (pt.kt0 + i) * kBK, arow);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
           if (leader) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)L::kStage);
-          const uint32_t sa = base + (uint32_t)(s * L::kStage);
           tma_load_2d_pair(sa, &tmA, &full[s], (pt.kt0 + i) * kBK, arow);
           tma_load_2d_pair(sa + L::kA, &tmB, &full[s], (pt.kt0 + i) * kBK, brow);
         }
       }
+    } else {
+      grid_dep_wait();
     }
     __syncwarp();
   } else if (warp == 1) {
+    grid_dep_wait();
     if (leader && lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
       uint32_t it = 0, use = 0;
@@ -963,6 +1027,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else {
+    grid_dep_wait();
     const int quarter = warp & 3;
     uint32_t use = 0;
     Unit u;
@@ -1275,7 +1340,22 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const T
     set_last_error("gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     return MUK_ERR_CUDA;
   }
-  kern<<<a.workers, kGemmThreads, L::kBytes, stream>>>(ma, mb, C, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.workers, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, C, a);
+  if (e != cudaSuccess) {
+    set_last_error("%s: launch failed: %s", GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16",
+                   cudaGetErrorString(e));
+    return MUK_ERR_CUDA;
+  }
   return check_launch(GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16");
 }
 
@@ -1332,13 +1412,15 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = 2;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, C, a);
   if (e != cudaSuccess) {
     set_last_error("muk_gemm_bf16(pair): launch failed: %s", cudaGetErrorString(e));
@@ -1742,4 +1824,45 @@ extern "C" int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B,
   if (rc) return rc;
   return launch_allreduce_finish(bufs, scratch, flags, rank, world, (int64_t)M * N,
                                  (int64_t)p.share_rows * N, true, st);
+}
+
+extern "C" int muk_gemm_tp_residual_norm(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                         int M, int N, int K, float* const* bufs,
+                                         float* const* scratch, uint32_t* const* flags, int rank,
+                                         int world, float* resid, const float* norm_w, float eps,
+                                         void* const* x_bufs, int64_t ldx, int clamp_delta,
+                                         int clamp_sum, int clamp_norm, float mu, float cmin,
+                                         float cmax, void* stream) {
+  MUK_REQUIRE(A && B && bufs && scratch && flags && world >= 1 && world <= kArMaxRanks &&
+                  rank >= 0 && rank < world,
+              "muk_gemm_tp_residual_norm: rank %d of %d", rank, world);
+  MUK_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 8 == 0 && lda >= K && ldb >= K && lda % 8 == 0 &&
+                  ldb % 8 == 0 && MUK_ALIGNED16(A) && MUK_ALIGNED16(B),
+              "muk_gemm_tp_residual_norm: shape M=%d N=%d K=%d or A/B alignment", M, N, K);
+  MUK_REQUIRE(resid && MUK_ALIGNED16(resid), "muk_gemm_tp_residual_norm: resid null / unaligned");
+  MUK_REQUIRE(norm_w == nullptr || (x_bufs && ldx >= N && ldx % 8 == 0 && MUK_ALIGNED16(norm_w)),
+              "muk_gemm_tp_residual_norm: a norm needs x buffers and an aligned weight");
+  for (int s = 0; s < world; ++s) {
+    MUK_REQUIRE(bufs[s] && scratch[s] && flags[s] && MUK_ALIGNED16(bufs[s]) &&
+                    MUK_ALIGNED16(scratch[s]) && MUK_ALIGNED16(flags[s]),
+                "muk_gemm_tp_residual_norm: rank %d buffer, scratch or flags", s);
+    MUK_REQUIRE(norm_w == nullptr || (x_bufs[s] && MUK_ALIGNED16(x_bufs[s])),
+                "muk_gemm_tp_residual_norm: rank %d x buffer null / not 16-byte aligned", s);
+  }
+  if (M == 0) return MUK_OK;
+  PushArgs p;
+  for (int s = 0; s < kArMaxRanks; ++s) {
+    p.scratch[s] = s < world ? scratch[s] : nullptr;
+    p.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  p.rank = rank;
+  p.world = world;
+  p.share_rows = (M + world - 1) / world;
+  cudaStream_t st = as_stream(stream);
+  int rc = run_gemm(false, A, lda, B, ldb, bufs[rank], N, M, N, K, kEpiF32Push, 1, nullptr,
+                    nullptr, 0, (M + kBM - 1) / kBM, st, nullptr, &p);
+  if (rc) return rc;
+  return launch_tp_norm_finish(bufs, scratch, flags, rank, world, M, N, p.share_rows, 1, 0, true,
+                               resid, N, norm_w, eps, x_bufs, ldx, clamp_delta, clamp_sum,
+                               clamp_norm, mu, cmin, cmax, st);
 }

@@ -20,32 +20,6 @@ struct ClampArgs {
   float mu, cmin, cmax;
 };
 
-__host__ __device__ inline ClampParams make_clamp(int enabled, float mu, float cmin, float cmax) {
-  ClampParams p;
-  p.enabled = enabled;
-  p.mu = mu;
-  p.center = (cmax + cmin) * 0.5f;
-  p.range = (cmax - cmin) * 0.5f;
-  p.inv_range = p.range > 0.f ? 1.f / p.range : 0.f;
-  return p;
-}
-
-// Sum of `v` over the CTA; `red` is >= 32 floats of shared scratch.
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
-  if (warp == 0) {
-    t = warp_sum(t);
-    if (lane == 0) red[0] = t;
-  }
-  __syncthreads();
-  return red[0];
-}
-
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              int64_t table_stride, float* __restrict__ resid, int hidden, int vocab,
@@ -263,7 +237,8 @@ __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __
                                     const float* __restrict__ ctrl_bias,
                                     const float* __restrict__ muproj,
                                     const float* __restrict__ mu_param, float dt, float* __restrict__ v,
-                                    __nv_bfloat16* __restrict__ v_bf16, int64_t v_bf16_stride,
+                                    int v_zero, __nv_bfloat16* __restrict__ v_bf16,
+                                    int64_t v_bf16_stride,
                                     float* __restrict__ resid, __nv_bfloat16* __restrict__ mu_out,
                                     int64_t mu_out_stride, const float* __restrict__ norm_w, float eps,
                                     __nv_bfloat16* __restrict__ norm_out, int64_t norm_out_stride,
@@ -287,7 +262,7 @@ __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __
     const float g = sigmoidf_(crow[2 * hidden + j] + ctrl_bias[2 * hidden + j]);
     const float mu_c = mu_param[j] + muproj[base + j];
     const float hj = h[base + j];
-    float vn = a * v[base + j] - b * (hj - mu_c);
+    float vn = a * (v_zero ? 0.f : v[base + j]) - b * (hj - mu_c);
     vn = fminf(fmaxf(vn, -10.f), 10.f);
     const float hn = hj + dt * g * vn;
     const float r = resid[base + j] + hn;
@@ -362,7 +337,7 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 3 : 1)
     inl_dynamics_vec_kernel(const float* __restrict__ h, const float* __restrict__ ctrl_raw,
                             const float* __restrict__ ctrl_bias, const float* __restrict__ muproj,
                             const float* __restrict__ mu_param, float dt, float* __restrict__ v,
-                            __nv_bfloat16* __restrict__ v_bf16, int64_t v_bf16_stride,
+                            int v_zero, __nv_bfloat16* __restrict__ v_bf16, int64_t v_bf16_stride,
                             float* __restrict__ resid, __nv_bfloat16* __restrict__ mu_out,
                             int64_t mu_out_stride, const float* __restrict__ norm_w, float eps,
                             __nv_bfloat16* __restrict__ norm_out, int64_t norm_out_stride,
@@ -389,7 +364,8 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 3 : 1)
   for (int i = 0; i < VPT; ++i) {
     const int q = threadIdx.x + i * n;  // float4 index within the row
     const float4 ca = c4[q], cb = c4[H4 + q], cg = c4[2 * H4 + q];
-    const float4 mpv = mp4[q], hv = h4[q], vv = v4[q], rv = r4[q];
+    const float4 mpv = mp4[q], hv = h4[q], rv = r4[q];
+    const float4 vv = v_zero ? make_float4(0.f, 0.f, 0.f, 0.f) : v4[q];
     const float4 ba = b4[q], bb = b4[H4 + q], bg = b4[2 * H4 + q], muv = mu4[q];
     const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
     const float cgv[4] = {cg.x, cg.y, cg.z, cg.w}, bav[4] = {ba.x, ba.y, ba.z, ba.w};
@@ -595,7 +571,8 @@ extern "C" int muk_reduce_clamp(const float* partials, int64_t partial_stride, i
 
 extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bias,
                                 const float* muproj, const float* mu_param, float dt, float* v,
-                                void* v_bf16, int64_t v_bf16_stride, float* resid, void* mu_out,
+                                int v_zero, void* v_bf16, int64_t v_bf16_stride, float* resid,
+                                void* mu_out,
                                 int64_t mu_out_stride, const float* norm_w, float eps,
                                 void* norm_out, int64_t norm_out_stride, const int32_t* token_ids,
                                 const void* router_w, int num_experts, int vocab,
@@ -628,12 +605,12 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
                       (router_w == nullptr || ((uintptr_t)router_w & 7) == 0);
 #define MUK_INL(V, THREADS)                                                                      \
   inl_dynamics_vec_kernel<V><<<num_tokens, THREADS, 0, st>>>(                                   \
-      h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,            \
+      h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,            \
       mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,        \
       expert_ids, hidden, cpn)
   if (router_w != nullptr && num_experts > kInlMaxVecExperts) {
     inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
-        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,
+        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,
         mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
         expert_ids, hidden, cpn);
   } else if (vec_ok && vpt == -1) {
@@ -646,7 +623,7 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
     MUK_INL(4, 256);
   } else {
     inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
-        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, vb, v_bf16_stride, resid, mo,
+        h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,
         mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
         expert_ids, hidden, cpn);
   }

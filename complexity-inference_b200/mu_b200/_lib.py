@@ -80,6 +80,12 @@ SIGNATURES = {
     "muk_allreduce_flag_bytes": (c_size_t, []),
     "muk_allreduce_scratch_elems": (c_int64, [c_int64, c_int]),
     "muk_allreduce_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int64, c_int, c_int64, _P]),
+    "muk_tp_residual_norm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int64, _P,
+                                     _P, c_float, _P, c_int64, c_int, c_int, c_int, c_float,
+                                     c_float, c_float, _P]),
+    "muk_gemm_tp_residual_norm": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P,
+                                          _P, c_int, c_int, _P, _P, c_float, _P, c_int64, c_int,
+                                          c_int, c_int, c_float, c_float, c_float, _P]),
     "muk_ep_gather_bf16": (c_int, [_P, _P, c_int, c_int, _P, c_int, c_int, c_int, _P]),
     "muk_llama_forward": (c_int, [_P, _P, _P]),
     "muk_gemm_allreduce_scratch_elems": (c_int64, [c_int, c_int, c_int]),
@@ -89,7 +95,8 @@ SIGNATURES = {
     "muk_gather_rows_bf16": (c_int, [_P, c_int64, _P, c_int, _P, c_int64, c_int, _P]),
     "muk_grouped_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, c_int,
                                       c_int, c_int, c_int, _P]),
-    "muk_inl_dynamics": (c_int, [_P, _P, _P, _P, _P, c_float, _P, _P, c_int64, _P, _P, c_int64,
+    "muk_inl_dynamics": (c_int, [_P, _P, _P, _P, _P, c_float, _P, c_int, _P, c_int64, _P, _P,
+                                 c_int64,
                                  _P, c_float, _P, c_int64, _P, _P, c_int, c_int, _P, c_int, c_int,
                                  c_int, c_float, c_float, c_float, _P]),
     "muk_reduce_clamp": (c_int, [_P, c_int64, c_int, _P, _P, c_int64, c_int, c_int, c_int,
@@ -126,7 +133,8 @@ class MukLlamaModel(ctypes.Structure):
                 ("logits", c_void_p), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
                 ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
                 ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int),
-                ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p)]
+                ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p),
+                ("tp_norm", c_int), ("x_peer", c_void_p * 8)]
 
 
 class MukStepBatch(ctypes.Structure):
@@ -143,7 +151,8 @@ _lib: ctypes.CDLL | None = None
 # count both); the benchmark reports it as its launch count.
 launch_count = 0
 _TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32",
-                "muk_gemm_allreduce_f32", "muk_ep_gather_bf16"}
+                "muk_gemm_allreduce_f32", "muk_ep_gather_bf16", "muk_tp_residual_norm",
+                "muk_gemm_tp_residual_norm"}
 
 
 class MukError(RuntimeError):

@@ -25,7 +25,7 @@ from . import _lib
 
 
 class PeerAllReduce:
-    def __init__(self, group, max_elems: int, device):
+    def __init__(self, group, max_elems: int, device, x_elems: int = 0):
         import torch.distributed as dist
 
         self.group = group
@@ -40,9 +40,12 @@ class PeerAllReduce:
         # rank: room for one extra row per rank at the widest hidden size
         self.scratch_elems = (int(lib.muk_allreduce_scratch_elems(self.max_elems, self.world))
                               + self.world * 16384 + 63) // 64 * 64
-        # [data | scratch (world shares) | flags], f32; the flag area starts zeroed
+        # [data | scratch (world shares) | flags | x rows], f32 words; the flag
+        # area starts zeroed.  The x area (bf16) receives every rank's
+        # normalised rows from muk_tp_residual_norm.
         self.flag_words = flag_words
-        self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words,
+        self.x_words = (int(x_elems) + 1) // 2 + 15 & ~15
+        self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words + self.x_words,
                                dtype=torch.float32, device=device)
         torch.cuda.synchronize(device)
         handle = (ctypes.c_uint8 * 64)()
@@ -68,6 +71,9 @@ class PeerAllReduce:
         self.ptrs = ptrs
         self.scratch_ptrs = [p + self.max_elems * 4 for p in ptrs]
         self.flag_ptrs = [p + (self.max_elems + self.scratch_elems) * 4 for p in ptrs]
+        self._x_off = self.max_elems + self.scratch_elems + flag_words
+        self.x_ptrs = [p + self._x_off * 4 for p in ptrs]
+        self._xs = (ctypes.c_void_p * self.world)(*self.x_ptrs)
         self._scratch = (ctypes.c_void_p * self.world)(*self.scratch_ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*self.flag_ptrs)
         dist.barrier(group=group)
@@ -77,6 +83,56 @@ class PeerAllReduce:
         if n > self.max_elems:
             raise ValueError(f"PeerAllReduce: {n} elements > capacity {self.max_elems}")
         return self.buf[:n]
+
+    def x_view(self, rows: int, cols: int) -> torch.Tensor | None:
+        """[rows, cols] bf16 in this rank's x area (None if it does not fit):
+        the activation buffer that muk_tp_residual_norm fills on every rank."""
+        if rows * cols > 2 * self.x_words:
+            return None
+        x = self.buf[self._x_off:self._x_off + self.x_words].view(torch.bfloat16)
+        return x[: rows * cols].view(rows, cols)
+
+    def residual_norm_(self, part: torch.Tensor, resid: torch.Tensor, norm_w, eps: float,
+                       x: torch.Tensor, clamp, clamp_delta: bool, clamp_sum: bool,
+                       clamp_norm: bool) -> None:
+        """Reduce-scatter the split-K partials ``part`` [S, T, H] (a view at the
+        start of the buffer), add the owned rows' sums to ``resid`` and
+        all-gather their norm into every rank's x (``muk_tp_residual_norm``)."""
+        S, T, H = part.shape
+        if part.data_ptr() != self.buf.data_ptr() or x.data_ptr() != self.x_ptrs[self.rank]:
+            raise ValueError("residual_norm_: partials / x must live in the peer buffer")
+        bufs = self._data_arrays.get(0)
+        if bufs is None:
+            bufs = self._data_arrays[0] = (ctypes.c_void_p * self.world)(*self.ptrs)
+        _lib.call("muk_tp_residual_norm", ctypes.addressof(bufs), ctypes.addressof(self._scratch),
+                  ctypes.addressof(self._flags), self.rank, self.world, T, H, S, T * H,
+                  resid.data_ptr(), None if norm_w is None else norm_w.data_ptr(), eps,
+                  ctypes.addressof(self._xs), x.stride(0), int(clamp_delta and clamp.enabled),
+                  int(clamp_sum and clamp.enabled), int(clamp_norm and clamp.enabled), clamp.mu,
+                  clamp.clamp_min, clamp.clamp_max, torch.cuda.current_stream().cuda_stream)
+
+    def gemm_residual_norm_(self, A: torch.Tensor, W: torch.Tensor, M: int, resid: torch.Tensor,
+                            norm_w, eps: float, x: torch.Tensor, clamp, clamp_delta: bool,
+                            clamp_sum: bool, clamp_norm: bool) -> None:
+        """:meth:`residual_norm_` with the projection GEMM in front, its
+        epilogue pushing rows to their owners (``muk_gemm_tp_residual_norm``)."""
+        N, K = W.shape[0], A.shape[1]
+        lib = _lib.load()
+        need = int(lib.muk_gemm_allreduce_scratch_elems(M, N, self.world))
+        if M * N > self.max_elems or need > self.scratch_elems:
+            raise ValueError(f"PeerAllReduce: {M}x{N} does not fit the peer buffers")
+        if x.data_ptr() != self.x_ptrs[self.rank]:
+            raise ValueError("gemm_residual_norm_: x must live in the peer buffer")
+        bufs = self._data_arrays.get(0)
+        if bufs is None:
+            bufs = self._data_arrays[0] = (ctypes.c_void_p * self.world)(*self.ptrs)
+        _lib.call("muk_gemm_tp_residual_norm", A.data_ptr(), A.stride(0), W.data_ptr(),
+                  W.stride(0), M, N, K, ctypes.addressof(bufs), ctypes.addressof(self._scratch),
+                  ctypes.addressof(self._flags), self.rank, self.world, resid.data_ptr(),
+                  None if norm_w is None else norm_w.data_ptr(), eps, ctypes.addressof(self._xs),
+                  x.stride(0), int(clamp_delta and clamp.enabled), int(clamp_sum and clamp.enabled),
+                  int(clamp_norm and clamp.enabled), clamp.mu, clamp.clamp_min, clamp.clamp_max,
+                  torch.cuda.current_stream().cuda_stream)
 
     def owns(self, t: torch.Tensor) -> bool:
         p = t.data_ptr()
@@ -148,7 +204,7 @@ class PeerAllReduce:
         epoch).  Only safe while no all-reduce kernel runs on any rank: the
         caller synchronises every rank and puts host barriers on both sides
         (MuWorker.tp_reset)."""
-        self.buf[self.max_elems + self.scratch_elems:].zero_()
+        self.buf[self.max_elems + self.scratch_elems:self._x_off].zero_()
 
     def close(self) -> None:
         torch.cuda.synchronize()

@@ -237,11 +237,13 @@ def reduce_clamp(partials: torch.Tensor, dst: torch.Tensor, dst_bf16: torch.Tens
 
 def inl_dynamics(h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_bf16, resid, mu_out, norm_w,
                  eps, norm_out, token_ids=None, router_w=None, num_experts=0, vocab=0,
-                 expert_ids=None, clamp: Clamp = NO_CLAMP, num_tokens: int | None = None):
+                 expert_ids=None, clamp: Clamp = NO_CLAMP, num_tokens: int | None = None,
+                 v_zero: bool = False):
+    """v_zero: read the incoming velocity as zero (the first layer) instead of v."""
     T = h.shape[0] if num_tokens is None else num_tokens
     H = h.shape[1]
     call("muk_inl_dynamics", _p(h), _p(ctrl_raw), _p(ctrl_bias), _p(muproj), _p(mu_param), dt,
-         _p(v), _p(v_bf16), 0 if v_bf16 is None else _row_stride(v_bf16, "v_bf16"), _p(resid),
+         _p(v), int(v_zero), _p(v_bf16), 0 if v_bf16 is None else _row_stride(v_bf16, "v_bf16"), _p(resid),
          _p(mu_out), 0 if mu_out is None else _row_stride(mu_out, "mu_out"), _p(norm_w), eps,
          _p(norm_out), 0 if norm_out is None else _row_stride(norm_out, "norm_out"), _p(token_ids),
          _p(router_w), num_experts, vocab, _p(expert_ids), T, H, int(clamp.enabled), clamp.mu,

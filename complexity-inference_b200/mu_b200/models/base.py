@@ -91,14 +91,18 @@ class Workspace:
         self.max_tokens, self.max_seqs, self.max_seq_len = T, max_seqs, max_seq_len
         bf, f32 = torch.bfloat16, torch.float32
         self.resid = torch.empty(T, H, device=dev, dtype=f32)
-        self.x = torch.zeros(T, 2 * H, device=dev, dtype=bf)  # [x | mu_prev] for Deep
+        # [x | mu_prev] for Deep; under peer-memory TP the model may keep x in
+        # the peer-mapped area, where every rank's normalised rows land
+        comm = getattr(model, "comm", None)
+        px = comm.x_view(T, 2 * H) if comm is not None and model.peer_x_elems(T) else None
+        self.shared_x = px is not None
+        self.x = px if px is not None else torch.zeros(T, 2 * H, device=dev, dtype=bf)
         self.qkv = torch.empty(T, (Hq + 2 * Hkv) * D, device=dev, dtype=bf)
         self.attn = torch.empty(T, Hq * D, device=dev, dtype=bf)
         self.part_rows = max(T, 2048)
         n = self.part_rows * model.max_part_width()
         # under tensor parallelism the partials live in the peer-mapped buffer
         # that the all-reduce kernel sums in place
-        comm = getattr(model, "comm", None)
         self.shared_part = comm is not None and n <= comm.max_elems
         self.part = comm.view(n) if self.shared_part else torch.empty(n, device=dev, dtype=f32)
         self.act = torch.empty(T, model.act_width(), device=dev, dtype=bf)
@@ -147,6 +151,11 @@ class MuModelBase:
 
     def extra_workspace(self, ws: Workspace, T: int) -> None:
         pass
+
+    def peer_x_elems(self, max_tokens: int) -> int:
+        """bf16 elements of the activation rows kept in peer memory under
+        tensor parallelism (0: x stays private)."""
+        return 0
 
     # ---- setup -----------------------------------------------------------------
     def ensure_rope(self, n: int) -> None:

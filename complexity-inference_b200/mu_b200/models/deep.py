@@ -145,8 +145,6 @@ class DeepForCausalLM(MuModelBase):
         resid = ws.resid[:T]
         xcat = ws.x[:T]             # [x | mu_prev]
         K.embed(batch.input_ids, self.embed, resid, cl)
-        ws.v[:T].zero_()            # velocity starts at zero (layers.py:99-100)
-        ws.hv[:T, H:].zero_()
         K.residual_rmsnorm(resid, None, self.layers[0]["w_in"], eps, xcat[:, :H], clamp=cl,
                            clamp_norm=True)
         nl = len(self.layers)
@@ -157,13 +155,19 @@ class DeepForCausalLM(MuModelBase):
             attn = self.attention(l, batch, cache)
             part = self.row_parallel(attn[:T], L["wo"], T, H)
             K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)   # h = clamp(o_proj)
-            K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
+            # controller input [h | v]: the velocity starts at zero
+            # (layers.py:99-100), so layer 0 multiplies the h half only
+            if l == 0:
+                K.gemm(ws.hv[:, :H], L["wci"][:, :H], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"],
+                       M=T)
+            else:
+                K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
             K.gemm(ws.ch, L["wco"], ws.ctrl, K.MUK_EPI_F32, M=T)
             K.gemm(ws.hv[:, :H], L["wmu"], ws.mp, K.MUK_EPI_F32, M=T)
             K.inl_dynamics(ws.h, ws.ctrl, L["bco"], ws.mp, L["mu"], cfg.dynamics_dt, ws.v,
                            ws.hv[:, H:], ws.resid, ws.x[:, H:], L["w_post"], eps, ws.x2,
                            batch.input_ids, L.get("router"), E if self.routed else 0, V,
-                           ws.eids, cl, num_tokens=T)
+                           ws.eids, cl, num_tokens=T, v_zero=l == 0)
             last = l + 1 == nl
             nxt_w = None if last else self.layers[l + 1]["w_in"]
             nxt_out = None if last else xcat[:, :H]

@@ -26,7 +26,8 @@ import torch
 from .. import _lib
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
-from .base import PAD_MULT, MuModelBase, interleave_gate_up, pad_cols, pad_to
+from .base import (FUSED_TP_MAX_ROWS, PAD_MULT, MuModelBase, choose_split, interleave_gate_up,
+                   pad_cols, pad_to)
 from .registry import register_model
 
 
@@ -61,6 +62,19 @@ class LlamaForCausalLM(MuModelBase):
     def extra_workspace(self, ws, T: int) -> None:
         H = self.config.hidden_size
         ws.sumsq = torch.empty(max(H // 128, 1), T, device=self.device, dtype=torch.float32)
+
+    def peer_x_elems(self, max_tokens: int) -> int:
+        if os.environ.get("MU_TP_NORM", "1") == "0" or self.config.hidden_size % 8:
+            return 0
+        return max_tokens * 2 * self.config.hidden_size
+
+    def tp_norm(self) -> bool:
+        """Under peer-memory TP: reduce-scatter + residual/RMSNorm on each
+        rank's rows + all-gather of x (muk_tp_residual_norm) in place of an
+        all-reduce followed by a replicated residual/norm."""
+        ws = self.ws
+        return (self.tp_group is not None and self.comm is not None and ws is not None
+                and ws.shared_part and ws.shared_x)
 
     def fused_norm(self) -> bool:
         """Residual add + RMSNorm in the O / down projection's epilogue and the
@@ -122,7 +136,8 @@ class LlamaForCausalLM(MuModelBase):
         """The executor's model struct (rebuilt when a buffer moves)."""
         ws, cfg = self.ws, self.config
         key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
-               self.fused_rope(), self._tp_fused, self.fused_norm(), self.fused_norm_min_rows)
+               self.fused_rope(), self._tp_fused, self.fused_norm(), self.fused_norm_min_rows,
+               self.tp_norm())
         if key == self._native_key:
             return self._native_model
         layers = (_lib.MukLlamaLayer * len(self.layers))()
@@ -153,6 +168,7 @@ class LlamaForCausalLM(MuModelBase):
         m.tp_fused = int(self._tp_fused)
         m.fused_norm = max(1, self.fused_norm_min_rows) if self.fused_norm() else 0
         m.sumsq = ws.sumsq.data_ptr()
+        m.tp_norm = int(self.tp_norm())
         m.tp_world, m.tp_rank = 1, 0
         if self.comm is not None:
             c = self.comm
@@ -160,6 +176,7 @@ class LlamaForCausalLM(MuModelBase):
             for r in range(c.world):
                 m.ar_data[r], m.ar_scratch[r], m.ar_flags[r] = (c.ptrs[r], c.scratch_ptrs[r],
                                                                  c.flag_ptrs[r])
+                m.x_peer[r] = c.x_ptrs[r]
         m._keep = layers  # the layer array must outlive the struct
         self._native_key, self._native_model = key, m
         return m
@@ -174,11 +191,18 @@ class LlamaForCausalLM(MuModelBase):
                               batch.block_tables.data_ptr(), batch.block_tables.stride(0))
         # two all-reduces per layer: fused (GEMM + finish: one extra kernel each)
         # or separate (push + finish: two each)
-        tp = (2 if (m.tp_fused and T <= 512) else 4) if m.tp_world > 1 else 0
-        fused = m.fused_norm > 0 and T >= m.fused_norm
-        per_layer = ((4 if fused else 6 if m.fused_rope else 7) + (2 if nd > 0 else 0)
-                     + (1 if B > nd else 0) + tp)
-        _lib.call_counted("muk_llama_forward", 4 + per_layer * m.num_layers, ctypes.byref(m),
+        attn = (2 if nd > 0 else 0) + (1 if B > nd else 0)
+        if m.tp_world > 1 and m.tp_norm:
+            # q|k|v (+RoPE), attention, 2 x (projection + finish [+ push]), SwiGLU
+            per_layer = (1 if m.fused_rope else 2) + attn + 1 + \
+                (4 if (m.tp_fused and T <= 512) else 6)
+            n = 2 + per_layer * m.num_layers + 2
+        else:
+            tp = (2 if (m.tp_fused and T <= 512) else 4) if m.tp_world > 1 else 0
+            fused = m.fused_norm > 0 and T >= m.fused_norm
+            per_layer = (4 if fused else 6 if m.fused_rope else 7) + attn + tp
+            n = 4 + per_layer * m.num_layers
+        _lib.call_counted("muk_llama_forward", n, ctypes.byref(m),
                           ctypes.byref(b), torch.cuda.current_stream().cuda_stream)
         return self.ws.logits[:B]
 
@@ -191,6 +215,35 @@ class LlamaForCausalLM(MuModelBase):
         K.embed(batch.input_ids, self.embed, resid, cl)
         K.residual_rmsnorm(resid, None, self.layers[0]["w_in"], eps, x, clamp=cl, clamp_norm=True)
         nl = len(self.layers)
+        if self.tp_norm():
+            # reduce-scatter + residual/norm on the owned rows + all-gather of x;
+            # the residual stays row-sharded and the last layer applies the
+            # final norm (the LM head reads each sequence's last row of x)
+            c = self.comm
+            fused_tp = self._tp_fused and T <= FUSED_TP_MAX_ROWS
+
+            def project_norm(A, W, norm_w, clamp_sum):
+                if fused_tp:
+                    c.gemm_residual_norm_(A, W, T, resid, norm_w, eps, x, cl, True, clamp_sum,
+                                          True)
+                    return
+                s = choose_split(T, H, A.shape[1], ws.part_rows)
+                part = ws.part_view(s, T, H)
+                K.gemm(A, W, part, K.MUK_EPI_F32, split_k=s, M=T)
+                c.residual_norm_(part, resid, norm_w, eps, x, cl, True, clamp_sum, True)
+
+            for l, L in enumerate(self.layers):
+                self.qkv_proj(l, x, L["wqkv"], batch, cache)
+                attn = self.attention(l, batch, cache)
+                project_norm(attn[:T], L["wo"], L["w_post"], False)
+                K.gemm(x, L["wgu"], ws.act, K.MUK_EPI_SWIGLU, M=T)
+                last = l + 1 == nl
+                project_norm(ws.act[:T], L["wd"],
+                             self.norm_w if last else self.layers[l + 1]["w_in"], True)
+            B = batch.num_seqs
+            K.gather_rows(x, batch.last_token_idx[:B], ws.xl, num_rows=B)
+            K.gemm(ws.xl, self.lm_w, ws.logits, K.MUK_EPI_F32, M=B)
+            return ws.logits[:B]
         if self.fused_norm() and T >= max(1, self.fused_norm_min_rows):
             # x holds bf16(w * h); the GEMM that reads it scales each row by
             # rsqrt(mean(h^2) + eps) from the producer's partial sums

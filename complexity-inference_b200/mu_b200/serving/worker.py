@@ -211,8 +211,10 @@ class MuWorker:
 
             # partials of every step size this worker will run (the workspace
             # may round T up to a CUDA-graph bucket)
-            cap = self.model.part_elems(max(max_tokens, _bucket(max_seqs)))
-            self.model.comm = PeerAllReduce(self.model.tp_group, cap, self.device)
+            rows = max(max_tokens, _bucket(max_seqs))
+            cap = self.model.part_elems(rows)
+            self.model.comm = PeerAllReduce(self.model.tp_group, cap, self.device,
+                                            x_elems=self.model.peer_x_elems(rows))
         self.packer = StepPacker(self.device, max_tokens, max_seqs, max_blocks)
         self.model.ensure_workspace(max_tokens, max_seqs, max_blocks * cc.block_size)
         self._graphs.clear()

@@ -319,6 +319,7 @@ int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb
  *   ctrl = ctrl_raw[t] + ctrl_bias                    (3H: alpha | beta | gate)
  *   mu_c = mu_param + muproj[t]
  *   v'   = clamp(sigmoid(a)·v[t] − min(softplus(b),2)·(h[t] − mu_c), −10, 10)
+ *          (v[t] read as 0 when v_zero: the first layer's initial velocity)
  *   h'   = h[t] + dt·sigmoid(g)·v'
  *   resid[t] += h' ;  v[t] = v'
  *   v_bf16[t] = bf16(v')            (A-operand copy for the next controller GEMM)
@@ -330,7 +331,7 @@ int muk_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb
  * post_attention_layernorm of DeepDecoderLayer (mu_inference/models/deep.py:152-158)
  * and the routing of MuTokenRoutedMLP (layers.py:510-528). */
 int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bias,
-                     const float* muproj, const float* mu_param, float dt, float* v,
+                     const float* muproj, const float* mu_param, float dt, float* v, int v_zero,
                      void* v_bf16, int64_t v_bf16_stride, float* resid, void* mu_out,
                      int64_t mu_out_stride, const float* norm_w, float eps, void* norm_out,
                      int64_t norm_out_stride, const int32_t* token_ids, const void* router_w,
@@ -470,6 +471,34 @@ int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B, int64_t ld
                            int K, float* const* bufs, float* const* scratch,
                            uint32_t* const* flags, int rank, int world, void* stream);
 
+/* Tensor-parallel "h += all-reduce(partials); x = norm(h)" as reduce-scatter
+ * + residual/RMSNorm on this rank's rows + all-gather of the bf16 rows, over
+ * NVLink peer memory (replaces muk_allreduce_f32 + muk_residual_rmsnorm
+ * after the row-parallel O / down projections of
+ * mu_inference/models/llama.py:111-126 under tensor parallelism).
+ * bufs/scratch/flags as for muk_allreduce_f32; this rank's data holds
+ * `slices` f32 partial slices [T][H] (stride slice_stride).  Rows are owned
+ * in shares of ceil(T / world); only the owned rows of `resid` ([T][H] f32,
+ * local) are updated, so a caller keeps the residual row-sharded.  With
+ * norm_w, every rank's x_bufs[s] ([T][ldx] bf16, peer-mapped) receives all
+ * T normalised rows; mu_clamp flags as in muk_residual_rmsnorm. */
+int muk_tp_residual_norm(float* const* bufs, float* const* scratch, uint32_t* const* flags,
+                         int rank, int world, int T, int H, int slices, int64_t slice_stride,
+                         float* resid, const float* norm_w, float eps, void* const* x_bufs,
+                         int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm, float mu,
+                         float cmin, float cmax, void* stream);
+
+/* The same with the projection GEMM (A [M][K] · B [N][K]ᵀ, this rank's
+ * K-slice) in front: its epilogue stores each f32 output row straight into
+ * the owner rank's scratch (muk_gemm_allreduce_f32's push), then the finish
+ * above. */
+int muk_gemm_tp_residual_norm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
+                              int K, float* const* bufs, float* const* scratch,
+                              uint32_t* const* flags, int rank, int world, float* resid,
+                              const float* norm_w, float eps, void* const* x_bufs, int64_t ldx,
+                              int clamp_delta, int clamp_sum, int clamp_norm, float mu, float cmin,
+                              float cmax, void* stream);
+
 /* ---- Native step executor (dense Llama family) ----------------------------- */
 
 /* One decoder layer's weights: f32 norm weights, bf16 K-major matrices
@@ -526,6 +555,9 @@ typedef struct {
                      tp_world 1, clamp 0, hidden % 128 == 0, fused_rope); smaller steps keep
                      split-K projections and the separate norm kernel.  0: never */
   float* sumsq;   /* [hidden / 128][max tokens] f32 partial sums when fused_norm */
+  int tp_norm;    /* 1 (tp_world > 1): reduce-scatter + residual/RMSNorm on owned rows +
+                     all-gather of x (muk_tp_residual_norm); x must be x_peer[tp_rank] */
+  void* x_peer[8]; /* every rank's x buffer as mapped here (tp_norm) */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */

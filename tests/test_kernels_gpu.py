@@ -352,6 +352,17 @@ def test_inl_dynamics_and_routing(cuda, H):
     top2 = logits.topk(2, -1).values
     clear = (top2[:, 0] - top2[:, 1]) > 1e-3
     assert torch.equal(eids[clear], ref_e[clear])
+    # the first layer: v_zero reads the incoming velocity as 0 (v's contents ignored)
+    vz, rz = torch.full_like(v0, float("nan")), r0.clone()
+    vz0, rz0 = torch.zeros_like(v0), r0.clone()
+    outs = []
+    for vv, rr, flag in ((vz, rz, True), (vz0, rz0, False)):
+        nb = torch.empty(T, H, device=cuda, dtype=torch.bfloat16)
+        k.inl_dynamics(h, ctrl, cb, mp, mu_param, 0.1, vv, v_bf, rr, mu_out, w, 1e-6, nb, ids,
+                       router, E, V, eids, cl, v_zero=flag)
+        outs.append((vv.clone(), rr.clone(), nb))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
 
 
 def test_grouped_gemm_swiglu(cuda):

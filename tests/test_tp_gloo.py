@@ -101,7 +101,66 @@ def _tp_forward(model: O.OracleModel, ids, experts=None):
     return (hn[-1] @ p["lm_head.weight"].T).astype(np.float32)
 
 
-def _worker(rank, world, port, name, q, ep=False):
+def _rows_of(rank, world, S):
+    """Rows [lo, hi) owned by ``rank``: contiguous shares of ceil(S / world)."""
+    sr = (S + world - 1) // world
+    lo = min(S, rank * sr)
+    return sr, lo, min(S, lo + sr)
+
+
+def _reduce_scatter_rows(part, sr, lo, hi):
+    """This rank's rows of the sum over the ranks (gloo has no
+    reduce-scatter: all-reduce, then keep the owned rows)."""
+    return _allreduce(part)[lo:hi]
+
+
+def _all_gather_rows(rows, sr, S, world):
+    pad = np.zeros((sr, rows.shape[1]), np.float32)
+    pad[:rows.shape[0]] = rows
+    out = [torch.empty(sr, rows.shape[1]) for _ in range(world)]
+    dist.all_gather(out, torch.from_numpy(pad))
+    return torch.cat(out).numpy()[:S]
+
+
+def _tp_forward_rs_norm(model: O.OracleModel, ids):
+    """Llama prefill under tensor parallelism in the reduce-scatter form of
+    muk_tp_residual_norm: after each row-parallel projection a rank keeps
+    only its own rows of the sum, adds them to its rows of the residual
+    (the other rows are never kept), normalises them and all-gathers the
+    normalised rows; the last layer normalises with the final norm and the
+    LM head reads the last row of x."""
+    s, p, mu = model.s, model.p, model.mu
+    ids = np.asarray(ids)
+    S = len(ids)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    sr, lo, hi = _rows_of(rank, world, S)
+    h = O._clamp(p["embed_tokens.weight"][ids].astype(np.float32), mu)
+    x = O.rmsnorm(h, p["layers.0.input_layernorm.weight"], s.eps, mu)
+    h = h[lo:hi].copy()                      # the residual is row-sharded from here on
+    for l in range(s.layers):
+        pre = f"layers.{l}."
+        a = pre + "self_attn."
+        q = (x @ p[a + "q_proj.weight"].T).reshape(S, s.heads, s.head_dim).astype(np.float32)
+        k = (x @ p[a + "k_proj.weight"].T).reshape(S, s.kv_heads, s.head_dim).astype(np.float32)
+        v = (x @ p[a + "v_proj.weight"].T).reshape(S, s.kv_heads, s.head_dim).astype(np.float32)
+        pos = np.arange(S)
+        q = O.apply_rope(q, model.cos, model.sin, pos)
+        k = O.apply_rope(k, model.cos, model.sin, pos)
+        o = O.sdpa(q.transpose(1, 0, 2), k.transpose(1, 0, 2), v.transpose(1, 0, 2), True)
+        o = o.transpose(1, 0, 2).reshape(S, -1)
+        h = h + O._clamp(_reduce_scatter_rows(o @ p[a + "o_proj.weight"].T, sr, lo, hi), mu)
+        x2 = _all_gather_rows(O.rmsnorm(h, p[pre + "post_attention_layernorm.weight"], s.eps, mu),
+                              sr, S, world)
+        m = pre + "mlp."
+        part = (O._silu(x2 @ p[m + "gate_proj.weight"].T) * (x2 @ p[m + "up_proj.weight"].T)
+                ) @ p[m + "down_proj.weight"].T
+        h = O._clamp(h + O._clamp(_reduce_scatter_rows(part, sr, lo, hi), mu), mu)
+        w = p["norm.weight"] if l + 1 == s.layers else p[f"layers.{l + 1}.input_layernorm.weight"]
+        x = _all_gather_rows(O.rmsnorm(h, w, s.eps, mu), sr, S, world)
+    return (x[-1] @ p["lm_head.weight"].T).astype(np.float32)
+
+
+def _worker(rank, world, port, name, q, ep=False, rs_norm=False, trim=0):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world,
@@ -116,7 +175,11 @@ def _worker(rank, world, port, name, q, ep=False):
                               local.num_key_value_heads, shape.head_dim, shape.vocab,
                               experts=shape.experts, qk_norm=shape.qk_norm)
         model = O.OracleModel(lshape, {k: v.numpy() for k, v in shard.items()}, O.MuCfg(True))
-        logits = _tp_forward(model, prompts[0], expert_range(cfg, rank, world) if ep else None)
+        ids = prompts[0][:len(prompts[0]) - trim]
+        if rs_norm:
+            logits = _tp_forward_rs_norm(model, ids)
+        else:
+            logits = _tp_forward(model, ids, expert_range(cfg, rank, world) if ep else None)
         q.put((rank, logits))
     except Exception as e:
         import traceback
@@ -126,14 +189,19 @@ def _worker(rank, world, port, name, q, ep=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,ep", [("llama_tiny", False), ("deep_tiny", False),
-                                     ("deep_tiny", True)])
-def test_tp2_matches_unsharded(name, ep):
+@pytest.mark.parametrize("name,ep,rs_norm,trim", [("llama_tiny", False, False, 0),
+                                                  ("deep_tiny", False, False, 0),
+                                                  ("deep_tiny", True, False, 0),
+                                                  ("llama_tiny", False, True, 0),
+                                                  ("llama_tiny", False, True, 1)])
+def test_tp2_matches_unsharded(name, ep, rs_norm, trim):
+    """rs_norm: the reduce-scatter + owned-row residual/norm + all-gather
+    form; trim drops prompt tokens so the two ranks own unequal shares."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q, ep))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q, ep, rs_norm, trim))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -145,7 +213,10 @@ def test_tp2_matches_unsharded(name, ep):
         assert p.exitcode == 0
     shape, cfg, sd, d, prompts = load_tiny(name)
     full = O.OracleModel(shape, {k: v.numpy() for k, v in sd.items()}, O.MuCfg(True))
-    ref, _ = full.forward(prompts[0])
+    ids = prompts[0][:len(prompts[0]) - trim]
+    if trim:
+        assert (len(ids) % world) != 0
+    ref, _ = full.forward(ids)
     for r in range(world):
         np.testing.assert_allclose(got[r], ref, rtol=1e-4, atol=1e-4)
     assert np.array_equal(got[0], got[1])  # every rank holds the same logits

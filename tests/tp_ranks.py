@@ -147,20 +147,30 @@ def main():
     worst = {}
     failures = []
     check_peer_allreduce(rank, world, failures)
-    # (model, CUDA graphs, expert parallel, all-reduce: peer memory or NCCL)
-    # "peer": GEMM + reduce-scatter fused; "peer-split": GEMM, then muk_allreduce_f32
+    # (model, CUDA graphs, expert parallel, all-reduce: peer memory or NCCL,
+    # expert combine, Llama step form)
+    # "peer": GEMM + reduce-scatter fused; "peer-split": GEMM, then the push kernel
     # expert-parallel cases combine expert outputs by the bf16 row exchange
-    # ("gather", the default) or the f32 all-reduce ("allreduce")
-    for name, graphs, ep, comm, combine in (("llama_tiny", False, False, "nccl", "-"),
-                                            ("llama_tiny", True, False, "peer", "-"),
-                                            ("llama_tiny", False, False, "peer-split", "-"),
-                                            ("deep_tiny", False, False, "nccl", "-"),
-                                            ("deep_tiny", True, False, "peer", "-"),
-                                            ("deep_tiny", True, True, "peer-split", "gather"),
-                                            ("deep_tiny", False, True, "peer", "allreduce")):
+    # ("gather", the default) or the f32 all-reduce ("allreduce").
+    # Llama steps under peer memory: "rs-norm" (default: reduce-scatter, residual
+    # + norm on the owned rows, all-gather of x) from the native executor or the
+    # Python step, or "allreduce" (all-reduce, then the replicated residual/norm)
+    for name, graphs, ep, comm, combine, form in (
+            ("llama_tiny", False, False, "nccl", "-", "-"),
+            ("llama_tiny", True, False, "peer", "-", "rs-norm"),
+            ("llama_tiny", False, False, "peer-split", "-", "rs-norm"),
+            ("llama_tiny", False, False, "peer", "-", "rs-norm-python"),
+            ("llama_tiny", False, False, "peer-split", "-", "rs-norm-python"),
+            ("llama_tiny", True, False, "peer", "-", "allreduce"),
+            ("deep_tiny", False, False, "nccl", "-", "-"),
+            ("deep_tiny", True, False, "peer", "-", "-"),
+            ("deep_tiny", True, True, "peer-split", "gather", "-"),
+            ("deep_tiny", False, True, "peer", "allreduce", "-")):
         os.environ["MU_TP_COMM"] = "nccl" if comm == "nccl" else "peer"
         os.environ["MU_TP_FUSED"] = "0" if comm == "peer-split" else "1"
         os.environ["MU_EP_COMBINE"] = "allreduce" if combine == "allreduce" else "gather"
+        os.environ["MU_TP_NORM"] = "0" if form == "allreduce" else "1"
+        os.environ["MU_NATIVE_STEP"] = "0" if form == "rs-norm-python" else "1"
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
                           expert_parallel=ep,
@@ -169,6 +179,8 @@ def main():
         w = MuWorker(ec, f"cuda:{torch.cuda.current_device()}")
         w.load_state_dict(shape.arch, cfg, sd)
         w.use_graphs = graphs
+        if form.startswith("rs-norm"):
+            assert w.model.tp_norm(), "peer-memory TP should take the reduce-scatter + norm path"
         toks = d["tokens"]
         R, n = toks.shape
         steps = list(d["logit_steps"])
@@ -193,7 +205,7 @@ def main():
                     step_err.append((i, r, round(e, 5)))
         for r in range(R):
             w.free_request(f"r{r}")
-        worst[f"{name}/graphs={graphs}/ep={ep}/{comm}/{combine}"] = err
+        worst[f"{name}/graphs={graphs}/ep={ep}/{comm}/{combine}/{form}"] = err
         if err > 2e-2:
             failures.append((name, graphs, rank, err, [x for x in step_err if x[2] > 2e-2][:6]))
         eng = StepEngine(w, ec)
