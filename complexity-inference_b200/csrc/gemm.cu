@@ -91,7 +91,9 @@ struct GemmLayout {
   static constexpr int kB = BN * kBK * 2;
   static constexpr int kStage = kA + kB;
   static constexpr int kBarOff = STAGES * kStage;
-  static constexpr int kBytes = kBarOff + (2 * STAGES + 4) * 8 + 16 + 1024;
+  // epilogue staging: 4 warps x 32 x 32 f32 (see stage_transpose)
+  static constexpr int kEpiOff = (kBarOff + (2 * STAGES + 4) * 8 + 16 + 127) / 128 * 128;
+  static constexpr int kBytes = kEpiOff + 4 * 4096 + 1024;
 };
 
 // RoPE + paged-KV epilogue (MUK_EPI_ROPE_KV) of the fused q|k|v projection.
@@ -145,6 +147,16 @@ struct NormArgs {
 // Epilogue of the producer (see NormArgs).
 constexpr int kEpiResidNorm = 6;
 
+// f32 output c = mu_clamp(acc) to C and its bf16 copy to out2
+// (muk_gemm_clamp_dual: the Deep O projection, whose clamped output feeds the
+// INL dynamics in f32 and the controller / mu GEMMs in bf16).
+constexpr int kEpiClampDual = 7;
+struct DualArgs {
+  __nv_bfloat16* out2;
+  int64_t ld2;
+  ClampParams cp;
+};
+
 struct TileArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kt_per_split, total;
@@ -158,6 +170,7 @@ struct TileArgs {
   RopeArgs rope;
   PushArgs push;
   NormArgs norm;
+  DualArgs dual;
 };
 
 // Consumer row scale rsqrt(mean(r^2) + eps) from the producer's partials
@@ -170,21 +183,90 @@ __device__ __forceinline__ float row_norm_scale(const TileArgs& a, int row, int 
   return rsqrtf(ss * n.inv_h + n.eps);
 }
 
-__device__ __forceinline__ void store_push(const TileArgs& a, int row, int row_end, int col,
-                                           const uint32_t (&v)[32]) {
-  if (row >= row_end) return;
-  const PushArgs& p = a.push;
-  const int owner = row / p.share_rows;
-  const int r = row - owner * p.share_rows;
-  float* dst = p.scratch[owner] + ((int64_t)p.rank * p.share_rows + r) * a.ldc + col;
-  if (col + 32 <= a.N) {
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&f)[32]) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      *reinterpret_cast<float4*>(dst + j) =
-          make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                      __uint_as_float(v[j + 3]));
+  for (int j = 0; j < 32; j += 8) {
+    uint4 pk;
+    pk.x = pack_bf16x2(f[j], f[j + 1]);
+    pk.y = pack_bf16x2(f[j + 2], f[j + 3]);
+    pk.z = pack_bf16x2(f[j + 4], f[j + 5]);
+    pk.w = pack_bf16x2(f[j + 6], f[j + 7]);
+    *reinterpret_cast<uint4*>(dst + j) = pk;
+  }
+}
+
+// Epilogue stores go through a per-warp 32 x 32 f32 staging tile in shared
+// memory.  In TMEM-lane order every lane holds one row's 32 consecutive
+// values, so a warp-wide store would touch 32 rows (32 cache lines per
+// instruction; measured ~30 GB/s of output per SM).  After the transpose,
+// lane l holds piece i (i = 0..7) = row 4i + l/8 of the chunk, columns
+// 4 (l % 8) .. +3, so 8 lanes write one row's 128 contiguous bytes.  The
+// float4 index is XOR-swizzled by row so that both the write and the read
+// phase take the minimum four shared-memory wavefronts.  Warp-collective.
+__device__ __forceinline__ void stage_transpose(float* stage, int lane, const float (&f)[32],
+                                                float4 (&pc)[8]) {
+  float4* s4 = reinterpret_cast<float4*>(stage);
+  __syncwarp();  // the previous chunk's reads are done
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    s4[lane * 8 + (c ^ (lane & 7))] = make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3), c = lane & 7;
+    pc[i] = s4[r * 8 + (c ^ (r & 7))];
+  }
+}
+
+// Four consecutive f32 / bf16 values of a row at column cx (cx % 4 == 0),
+// clipped at ncols; `vec` when the row stride keeps the vector aligned.
+__device__ __forceinline__ void put4_f32(float* dst, float4 v, int cx, int ncols, bool vec) {
+  if (vec && cx + 4 <= ncols) {
+    *reinterpret_cast<float4*>(dst) = v;
   } else {
-    for (int j = 0; j < 32 && col + j < a.N; ++j) dst[j] = __uint_as_float(v[j]);
+    if (cx < ncols) dst[0] = v.x;
+    if (cx + 1 < ncols) dst[1] = v.y;
+    if (cx + 2 < ncols) dst[2] = v.z;
+    if (cx + 3 < ncols) dst[3] = v.w;
+  }
+}
+__device__ __forceinline__ void put4_bf16(__nv_bfloat16* dst, float4 v, int cx, int ncols,
+                                          bool vec) {
+  if (vec && cx + 4 <= ncols) {
+    uint2 o;
+    o.x = pack_bf16x2(v.x, v.y);
+    o.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst) = o;
+  } else {
+    if (cx < ncols) dst[0] = f_to_bf16(v.x);
+    if (cx + 1 < ncols) dst[1] = f_to_bf16(v.y);
+    if (cx + 2 < ncols) dst[2] = f_to_bf16(v.z);
+    if (cx + 3 < ncols) dst[3] = f_to_bf16(v.w);
+  }
+}
+
+// kEpiF32Push: this warp's rows of a 32-column chunk, each row to the scratch
+// of the rank that owns it (NVLink stores for peers), staged so that 8 lanes
+// store a row's 128 contiguous bytes.  Warp-collective.
+__device__ __forceinline__ void store_push(const TileArgs& a, int row, int row_end, int col,
+                                           const uint32_t (&v)[32], float* stage) {
+  const int lane = threadIdx.x & 31;
+  const PushArgs& p = a.push;
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+  float4 pc[8];
+  stage_transpose(stage, lane, f, pc);
+  const int rb = row - lane + (lane >> 3);
+  const int cx = col + (lane & 7) * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = rb + 4 * i;
+    if (r >= row_end) break;
+    const int owner = r / p.share_rows;
+    const int rr = r - owner * p.share_rows;
+    float* dst = p.scratch[owner] + ((int64_t)p.rank * p.share_rows + rr) * a.ldc + cx;
+    put4_f32(dst, pc[i], cx, a.N, (a.ldc & 3) == 0);
   }
 }
 
@@ -355,46 +437,67 @@ __device__ __forceinline__ Tile decode_tile(const TileArgs& a, int t) {
   return r;
 }
 
+// One 32-column chunk of this warp's 32 rows (lane = row - row0_of_warp):
+// F32 to C (+ split_off), else bf16 (BIAS_SILU applies bias + SiLU first).
+// With a staging tile: warp-collective, every lane calls it, rows at or past
+// row_end are skipped.  stage == nullptr: each lane stores its own row (no
+// shared-memory traffic; for epilogues hidden behind the next tile's main
+// loop, whose shared-memory bandwidth staging would take).
 template <int EPI>
 __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_off, int row,
                                             int row_end, int col, int ncols,
-                                            const uint32_t (&v)[32], const float* bias) {
-  if (row >= row_end) return;
-  if (EPI == MUK_EPI_F32) {
-    float* dst = reinterpret_cast<float*>(C) + split_off + (int64_t)row * ldc + col;
-    if (col + 32 <= ncols && (ldc & 3) == 0) {
+                                            const uint32_t (&v)[32], const float* bias,
+                                            float* stage) {
+  const int lane = threadIdx.x & 31;
+  float f[32];
 #pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(dst + j) =
-            make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                        __uint_as_float(v[j + 3]));
-    } else {
-      for (int j = 0; j < 32 && col + j < ncols; ++j) dst[j] = __uint_as_float(v[j]);
+  for (int j = 0; j < 32; ++j) {
+    f[j] = __uint_as_float(v[j]);
+    if (EPI == MUK_EPI_BIAS_SILU) {
+      const float b = (col + j < ncols) ? bias[col + j] : 0.f;
+      f[j] = silu(f[j] + b);
     }
-  } else {
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)row * ldc + col;
-    float f[32];
+  }
+  if (stage == nullptr) {
+    if (row >= row_end) return;
+    if (EPI == MUK_EPI_F32) {
+      float* dst = reinterpret_cast<float*>(C) + split_off + (int64_t)row * ldc + col;
+      if (col + 32 <= ncols && (ldc & 3) == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      f[j] = __uint_as_float(v[j]);
-      if (EPI == MUK_EPI_BIAS_SILU) {
-        const float b = (col + j < ncols) ? bias[col + j] : 0.f;
-        f[j] = silu(f[j] + b);
-      }
-    }
-    if (col + 32 <= ncols && (ldc & 7) == 0) {
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 pk;
-        pk.x = pack_bf16x2(f[j], f[j + 1]);
-        pk.y = pack_bf16x2(f[j + 2], f[j + 3]);
-        pk.z = pack_bf16x2(f[j + 4], f[j + 5]);
-        pk.w = pack_bf16x2(f[j + 6], f[j + 7]);
-        *reinterpret_cast<uint4*>(dst + j) = pk;
+        for (int j = 0; j < 32; ++j)
+          if (col + j < ncols) dst[j] = f[j];
       }
     } else {
-      for (int j = 0; j < 32 && col + j < ncols; ++j) dst[j] = f_to_bf16(f[j]);
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)row * ldc + col;
+      if (col + 32 <= ncols && (ldc & 7) == 0) {
+        store_bf16x32(dst, f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col + j < ncols) dst[j] = f_to_bf16(f[j]);
+      }
     }
+    return;
+  }
+  float4 pc[8];
+  stage_transpose(stage, lane, f, pc);
+  const int rb = row - lane + (lane >> 3);
+  const int cx = col + (lane & 7) * 4;
+  const bool vec = (ldc & 3) == 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = rb + 4 * i;
+    if (r >= row_end) break;
+    if (EPI == MUK_EPI_F32)
+      put4_f32(reinterpret_cast<float*>(C) + split_off + (int64_t)r * ldc + cx, pc[i], cx, ncols,
+               vec);
+    else
+      put4_bf16(reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)r * ldc + cx, pc[i], cx, ncols,
+                vec);
   }
 }
 
@@ -405,18 +508,6 @@ __device__ __forceinline__ void acc_chunk(uint32_t lane_addr, int c, uint32_t (&
   tmem_ld_32x32b_x32(lane_addr + c * 32, v);
   tmem_ld_wait();
   if (fix) sk_sum_chunk(*fix, c, v);
-}
-
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&f)[32]) {
-#pragma unroll
-  for (int j = 0; j < 32; j += 8) {
-    uint4 pk;
-    pk.x = pack_bf16x2(f[j], f[j + 1]);
-    pk.y = pack_bf16x2(f[j + 2], f[j + 3]);
-    pk.z = pack_bf16x2(f[j + 4], f[j + 5]);
-    pk.w = pack_bf16x2(f[j + 6], f[j + 7]);
-    *reinterpret_cast<uint4*>(dst + j) = pk;
-  }
 }
 
 // MUK_EPI_ROPE_KV: the tile's columns are whole heads of the q|k|v
@@ -530,48 +621,101 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int row, int row_end,
                                               int n0, int64_t split_off, uint32_t lane_addr,
-                                              const SkFix* fix) {
+                                              const SkFix* fix, float* stage, bool last_unit) {
   if (EPI == MUK_EPI_ROPE_KV) {
     epilogue_rope<BN>(C, args, row, row_end, n0, lane_addr, fix);
   } else if (EPI == kEpiResidNorm) {
-    // resid += acc; x~ = bf16(w * resid); one partial sum of resid^2 per 128 columns
+    // resid += acc; x~ = bf16(w * resid); one partial sum of resid^2 per 128
+    // columns.  Staged: lane holds 4 columns of rows rb + 4i (i = 0..7).
     const NormArgs& nm = args.norm;
-    const bool valid = row < row_end;
-    float* rrow = nm.resid + (int64_t)row * nm.ld_resid;
-    float ss = 0.f;
+    const int lane = threadIdx.x & 31;
+    const int rb = row - lane + (lane >> 3);
+    float ssp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ssp[i] = 0.f;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t v[32];
       tmem_ld_32x32b_x32(lane_addr + c * 32, v);
       tmem_ld_wait();
       if (fix) sk_sum_chunk(*fix, c, v);
-      const int col = n0 + c * 32;
-      if (valid && col < args.N) {  // N % 128 == 0: a chunk is wholly inside or outside
-        float f[32];
+      float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 r4 = *reinterpret_cast<const float4*>(rrow + col + j);
-          r4.x += __uint_as_float(v[j]);
-          r4.y += __uint_as_float(v[j + 1]);
-          r4.z += __uint_as_float(v[j + 2]);
-          r4.w += __uint_as_float(v[j + 3]);
-          *reinterpret_cast<float4*>(rrow + col + j) = r4;
-          ss += r4.x * r4.x + r4.y * r4.y + r4.z * r4.z + r4.w * r4.w;
-          if (nm.w != nullptr) {
-            const float4 w4 = *reinterpret_cast<const float4*>(nm.w + col + j);
-            f[j] = w4.x * r4.x;
-            f[j + 1] = w4.y * r4.y;
-            f[j + 2] = w4.z * r4.z;
-            f[j + 3] = w4.w * r4.w;
-          }
-        }
+      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+      float4 pc[8];
+      stage_transpose(stage, lane, f, pc);
+      const int col = n0 + c * 32;
+      if (col >= args.N) continue;  // N % 128 == 0: warp-uniform
+      const int cx = col + (lane & 7) * 4;
+      const float4 w4 = nm.w != nullptr ? *reinterpret_cast<const float4*>(nm.w + cx)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      // all eight residual loads issued before the first use (predicated,
+      // no early exit), then the updates and stores
+      float4 r4[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        r4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rb + 4 * i < row_end)
+          r4[i] = *reinterpret_cast<const float4*>(nm.resid + (int64_t)(rb + 4 * i) * nm.ld_resid +
+                                                   cx);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = rb + 4 * i;
+        if (r >= row_end) continue;
+        float4 q = r4[i];
+        q.x += pc[i].x;
+        q.y += pc[i].y;
+        q.z += pc[i].z;
+        q.w += pc[i].w;
+        *reinterpret_cast<float4*>(nm.resid + (int64_t)r * nm.ld_resid + cx) = q;
+        ssp[i] += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
         if (nm.w != nullptr) {
-          store_bf16x32(nm.xout + (int64_t)row * nm.ldx + col, f);
-          if ((c & 3) == 3) {
-            nm.sumsq_out[(int64_t)(col >> 7) * nm.sumsq_stride + row] = ss;
-            ss = 0.f;
-          }
+          uint2 o;
+          o.x = pack_bf16x2(w4.x * q.x, w4.y * q.y);
+          o.y = pack_bf16x2(w4.z * q.z, w4.w * q.w);
+          *reinterpret_cast<uint2*>(nm.xout + (int64_t)r * nm.ldx + cx) = o;
         }
+      }
+      if (nm.w != nullptr && (c & 3) == 3) {  // a 128-column part is complete
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float t = ssp[i];
+          t += __shfl_xor_sync(0xffffffffu, t, 1);
+          t += __shfl_xor_sync(0xffffffffu, t, 2);
+          t += __shfl_xor_sync(0xffffffffu, t, 4);
+          const int r = rb + 4 * i;
+          if ((lane & 7) == 0 && r < row_end)
+            nm.sumsq_out[(int64_t)(col >> 7) * nm.sumsq_stride + r] = t;
+          ssp[i] = 0.f;
+        }
+      }
+    }
+  } else if (EPI == kEpiClampDual) {
+    const DualArgs& du = args.dual;
+    const int lane = threadIdx.x & 31;
+    const int rb = row - lane + (lane >> 3);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+      tmem_ld_wait();
+      if (fix) sk_sum_chunk(*fix, c, v);
+      float f[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = mu_clamp(__uint_as_float(v[j]), du.cp);
+      float4 pc[8];
+      stage_transpose(stage, lane, f, pc);
+      const int col = n0 + c * 32;
+      if (col >= args.N) continue;  // N % 32 == 0: warp-uniform
+      const int cx = col + (lane & 7) * 4;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = rb + 4 * i;
+        if (r >= row_end) break;
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(C) + (int64_t)r * args.ldc + cx) =
+            pc[i];
+        put4_bf16(du.out2 + (int64_t)r * du.ld2 + cx, pc[i], cx, args.N, true);
       }
     }
   } else if (EPI == MUK_EPI_SWIGLU) {
@@ -593,7 +737,7 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
         for (int j = 0; j < 32; ++j)
           gv[j] = __float_as_uint(silu(__uint_as_float(gv[j]) * rs) * (__uint_as_float(uv[j]) * rs));
         store_chunk<MUK_EPI_BF16>(C, args.ldc, 0, row, row_end, (n0 >> 1) + grp * 64 + c * 32,
-                                  nout, gv, nullptr);
+                                  nout, gv, nullptr, last_unit ? stage : nullptr);
       }
     }
   } else {
@@ -604,9 +748,10 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
       tmem_ld_wait();
       if (fix) sk_sum_chunk(*fix, c, v);
       if (EPI == kEpiF32Push)
-        store_push(args, row, row_end, n0 + c * 32, v);
+        store_push(args, row, row_end, n0 + c * 32, v, stage);
       else
-        store_chunk<EPI>(C, args.ldc, split_off, row, row_end, n0 + c * 32, args.N, v, args.bias);
+        store_chunk<EPI>(C, args.ldc, split_off, row, row_end, n0 + c * 32, args.N, v, args.bias,
+                         stage);
     }
   }
 }
@@ -807,11 +952,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     grid_dep_wait();
     // ---- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----
     const int quarter = warp & 3;
+    float* stage = reinterpret_cast<float*>(basep + L::kEpiOff) + quarter * 1024;
     uint32_t use = 0;
     Unit u;
     for (int idx = 0; get_unit(args, w, idx, u); ++idx) {
       const Tile tl = unit_tile<BN, GROUPED>(args, u);
       if (!tl.valid) continue;
+      Unit nx;
+      const bool last_unit = !get_unit(args, w, idx + 1, nx);  // nothing left to overlap with
       const int a = use & 1;
       const uint32_t aph = (use >> 1) & 1u;
       if (!mbar_wait(&acc_full[a], aph, kDevTimeoutAccum)) break;
@@ -826,14 +974,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < 32; ++j) z[j] = 0u;
           for (int c = 0; c < BN / 32; ++c)
             store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, tl.row_end, tl.n0 + c * 32,
-                                     args.N, z, nullptr);
+                                     args.N, z, nullptr, stage);
         }
       } else if (u.part >= 0) {
         const SkFix f = make_fix(args, u, w, 0, 1, quarter * 32 + lane);
         if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
-          epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, &f);
+          epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, &f, stage,
+                                 last_unit);
       } else {
-        epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, nullptr);
+        epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, nullptr,
+                               stage, last_unit);
       }
       tc_fence_before();
       __syncwarp();
@@ -872,7 +1022,8 @@ struct PairLayout {
   static constexpr int kB = (PBN / 2) * kBK * 2;   // this CTA's half of B
   static constexpr int kStage = kA + kB;
   static constexpr int kBarOff = kStages * kStage;
-  static constexpr int kBytes = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
+  static constexpr int kEpiOff = (kBarOff + (2 * kStages + 4) * 8 + 16 + 127) / 128 * 128;
+  static constexpr int kBytes = kEpiOff + 4 * 4096 + 1024;
 };
 
 struct PairTile {
@@ -1029,10 +1180,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     grid_dep_wait();
     const int quarter = warp & 3;
+    float* stage = reinterpret_cast<float*>(basep + L::kEpiOff) + quarter * 1024;
     uint32_t use = 0;
     Unit u;
     for (int idx = 0; get_unit(args, pair, idx, u); ++idx) {
       const PairTile pt = pair_tile(args, u);
+      Unit nx;
+      const bool last_unit = !get_unit(args, pair, idx + 1, nx);  // nothing left to overlap with
       const int a = use & 1;
       const uint32_t aph = (use >> 1) & 1u;
       if (!mbar_wait(&acc_full[a], aph, kDevTimeoutAccum)) break;
@@ -1048,14 +1202,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < 32; ++j) z[j] = 0u;
           for (int c = 0; c < BN / 32; ++c)
             store_chunk<MUK_EPI_F32>(C, args.ldc, split_off, row, args.M, n0 + c * 32, args.N, z,
-                                     nullptr);
+                                     nullptr, stage);
         }
       } else if (u.part >= 0) {
         const SkFix f = make_fix(args, u, pair, (int)rank, 2, quarter * 32 + lane);
         if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
-          epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, &f);
+          epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, &f, stage,
+                                 last_unit);
       } else {
-        epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, nullptr);
+        epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, nullptr, stage,
+                               last_unit);
       }
       tc_fence_before();
       __syncwarp();
@@ -1381,6 +1537,9 @@ static int dispatch(int epilogue, const CUtensorMap& ma, const CUtensorMap& mb, 
     case kEpiResidNorm:
       if (!GROUPED) return launch<BN, S, kEpiResidNorm, false>(ma, mb, C, a, sms, s);
       break;
+    case kEpiClampDual:
+      if (!GROUPED) return launch<BN, S, kEpiClampDual, false>(ma, mb, C, a, sms, s);
+      break;
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1447,6 +1606,8 @@ static int launch_pair_epi(int epilogue, const CUtensorMap& ma, const CUtensorMa
       return launch_pair<kEpiF32Push, PBN>(ma, mb, C, a, sms, stream);
     case kEpiResidNorm:
       return launch_pair<kEpiResidNorm, PBN>(ma, mb, C, a, sms, stream);
+    case kEpiClampDual:
+      return launch_pair<kEpiClampDual, PBN>(ma, mb, C, a, sms, stream);
   }
   set_last_error("gemm: unknown epilogue %d", epilogue);
   return MUK_ERR_INVALID_ARG;
@@ -1455,7 +1616,8 @@ static int launch_pair_epi(int epilogue, const CUtensorMap& ma, const CUtensorMa
 static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                          int64_t ldc, int M, int N, int K, int epilogue, int split_k, bool sk,
                          const float* bias, const RopeArgs* rope, const PushArgs* push, int sms,
-                         cudaStream_t stream, const NormArgs* norm = nullptr, int pbn = 256) {
+                         cudaStream_t stream, const NormArgs* norm = nullptr, int pbn = 256,
+                         const DualArgs* dual = nullptr) {
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_map(&ma, A, lda, K, M, kBM))) return rc;
@@ -1478,6 +1640,7 @@ static int run_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb,
   a.rope = rope ? *rope : RopeArgs{};
   a.push = push ? *push : PushArgs{};
   a.norm = norm ? *norm : NormArgs{};
+  a.dual = dual ? *dual : DualArgs{};
   set_schedule(a, sms / 2, 2, sk);
   return pbn == 256 ? launch_pair_epi<256>(epilogue, ma, mb, C, a, sms, stream)
                     : launch_pair_epi<128>(epilogue, ma, mb, C, a, sms, stream);
@@ -1507,7 +1670,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
                     int64_t ldc, int M, int N, int K, int epilogue, int split_k, const float* bias,
                     const int32_t* offsets, int num_experts, int m_tiles, cudaStream_t stream,
                     const RopeArgs* rope = nullptr, const PushArgs* push = nullptr,
-                    const NormArgs* norm = nullptr) {
+                    const NormArgs* norm = nullptr, const DualArgs* dual = nullptr) {
   int rc = get_encode();
   if (rc) return rc;
   const int sms = sm_count();
@@ -1517,7 +1680,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
     const GemmPlan best = plan_for_split(M, N, K, epilogue, split_k, sms);
     if (best.kind == 1)
       return run_gemm_pair(A, lda, B, ldb, C, ldc, M, N, K, epilogue, split_k, best.sk, bias, rope,
-                           push, sms, stream, norm, best.bn);
+                           push, sms, stream, norm, best.bn, dual);
     bn = best.bn;
     sk = best.sk;
   } else {
@@ -1545,6 +1708,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
   a.rope = rope ? *rope : RopeArgs{};
   a.push = push ? *push : PushArgs{};
   a.norm = norm ? *norm : NormArgs{};
+  a.dual = dual ? *dual : DualArgs{};
   set_schedule(a, sms, 1, sk);
   if (bn == 256)
     return grouped ? dispatch<256, true>(epilogue, ma, mb, C, a, sms, stream)
@@ -1725,6 +1889,28 @@ extern "C" int muk_gemm_residual_norm(const void* A, int64_t lda, const void* B,
   n.sumsq_stride = sumsq_stride;
   return run_gemm(false, A, lda, B, ldb, resid, ld_resid, M, N, K, kEpiResidNorm, 1, nullptr,
                   nullptr, 0, (M + kBM - 1) / kBM, as_stream(stream), nullptr, nullptr, &n);
+}
+
+extern "C" int muk_gemm_clamp_dual(const void* A, int64_t lda, const void* B, int64_t ldb,
+                                   float* C, int64_t ldc, void* C_bf16, int64_t ld_bf16, int M,
+                                   int N, int K, int clamp, float mu, float clamp_min,
+                                   float clamp_max, void* stream) {
+  MUK_REQUIRE(A && B && C && C_bf16, "muk_gemm_clamp_dual: null pointer");
+  MUK_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 32 == 0,
+              "muk_gemm_clamp_dual: bad shape M=%d N=%d K=%d (N a multiple of 32)", M, N, K);
+  MUK_REQUIRE(lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 && MUK_ALIGNED16(A) &&
+                  MUK_ALIGNED16(B),
+              "muk_gemm_clamp_dual: A/B shape or alignment");
+  MUK_REQUIRE(ldc >= N && ldc % 4 == 0 && MUK_ALIGNED16(C) && ld_bf16 >= N && ld_bf16 % 8 == 0 &&
+                  MUK_ALIGNED16(C_bf16),
+              "muk_gemm_clamp_dual: outputs must be 16-byte aligned rows of >= N elements");
+  if (M == 0) return MUK_OK;
+  DualArgs d;
+  d.out2 = reinterpret_cast<__nv_bfloat16*>(C_bf16);
+  d.ld2 = ld_bf16;
+  d.cp = make_clamp(clamp, mu, clamp_min, clamp_max);
+  return run_gemm(false, A, lda, B, ldb, C, ldc, M, N, K, kEpiClampDual, 1, nullptr, nullptr, 0,
+                  (M + kBM - 1) / kBM, as_stream(stream), nullptr, nullptr, nullptr, &d);
 }
 
 extern "C" int muk_gemm_swiglu_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb,

@@ -225,6 +225,22 @@ __global__ void reduce_clamp_kernel(const float* __restrict__ partials, int64_t 
   }
 }
 
+// out[t][c] = bf16(silu(sum_p partials[p][t][c] + bias[c])): the split-K
+// tail of a narrow bias + SiLU projection (the INL controller's input layer).
+__global__ void reduce_bias_silu_kernel(const float* __restrict__ partials, int64_t partial_stride,
+                                        int num_partials, const float* __restrict__ bias,
+                                        __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                                        int cols, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / cols;
+    const int c = (int)(i - t * cols);
+    float s = bias[c];
+    for (int p = 0; p < num_partials; ++p) s += partials[p * partial_stride + i];
+    out[t * out_stride + c] = f_to_bf16(silu(s));
+  }
+}
+
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 // torch.nn.functional.softplus with beta=1, threshold=20.
@@ -567,6 +583,23 @@ extern "C" int muk_reduce_clamp(const float* partials, int64_t partial_stride, i
       partials, partial_stride, num_partials, dst_f32, reinterpret_cast<__nv_bfloat16*>(dst_bf16),
       dst_bf16_stride, hidden, total, make_clamp(clamp, mu, clamp_min, clamp_max));
   return check_launch("muk_reduce_clamp");
+}
+
+extern "C" int muk_reduce_bias_silu(const float* partials, int64_t partial_stride,
+                                    int num_partials, const float* bias, void* out,
+                                    int64_t out_stride, int rows, int cols, void* stream) {
+  MUK_REQUIRE(partials && bias && out && num_partials >= 1 && rows >= 0 && cols > 0 &&
+                  out_stride >= cols && (num_partials == 1 || partial_stride >= (int64_t)rows * cols),
+              "muk_reduce_bias_silu: bad arguments (rows %d cols %d partials %d)", rows, cols,
+              num_partials);
+  if (rows == 0) return MUK_OK;
+  const int64_t total = (int64_t)rows * cols;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 4 * 148) blocks = 4 * 148;
+  reduce_bias_silu_kernel<<<blocks, 256, 0, as_stream(stream)>>>(
+      partials, partial_stride, num_partials, bias, reinterpret_cast<__nv_bfloat16*>(out),
+      out_stride, cols, total);
+  return check_launch("muk_reduce_bias_silu");
 }
 
 extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bias,

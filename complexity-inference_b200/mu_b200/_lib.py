@@ -66,6 +66,8 @@ SIGNATURES = {
                                   c_int, _P]),
     "muk_gemm_residual_norm": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P,
                                        c_int64, _P, _P, c_int64, _P, c_int64, _P]),
+    "muk_gemm_clamp_dual": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_int64, c_int,
+                                    c_int, c_int, c_int, c_float, c_float, c_float, _P]),
     "muk_gemm_swiglu_rownorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int,
                                         c_int, _P, _P]),
     "muk_gemm_qkv_rope_rownorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int, c_int, _P,
@@ -99,6 +101,7 @@ SIGNATURES = {
                                  c_int64,
                                  _P, c_float, _P, c_int64, _P, _P, c_int, c_int, _P, c_int, c_int,
                                  c_int, c_float, c_float, c_float, _P]),
+    "muk_reduce_bias_silu": (c_int, [_P, c_int64, c_int, _P, _P, c_int64, c_int, c_int, _P]),
     "muk_reduce_clamp": (c_int, [_P, c_int64, c_int, _P, _P, c_int64, c_int, c_int, c_int,
                                  c_float, c_float, c_float, _P]),
     "muk_sample": (c_int, [_P, c_int64, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P, _P, _P,

@@ -224,6 +224,17 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor, dst: torch.Tensor, num_ro
          _row_stride(dst, "dst"), src.shape[1], _stream())
 
 
+def reduce_bias_silu(partials: torch.Tensor, bias: torch.Tensor, out: torch.Tensor,
+                     num_rows: int | None = None):
+    """out = bf16(silu(sum of the [S, T, N] f32 partials + bias))."""
+    if partials.dim() == 2:
+        partials = partials.unsqueeze(0)
+    T = out.shape[0] if num_rows is None else num_rows
+    N = out.shape[1]
+    call("muk_reduce_bias_silu", _p(partials), partials.stride(0), partials.shape[0], _p(bias),
+         _p(out), _row_stride(out, "out"), T, N, _stream())
+
+
 def reduce_clamp(partials: torch.Tensor, dst: torch.Tensor, dst_bf16: torch.Tensor | None,
                  clamp: Clamp = NO_CLAMP, num_tokens: int | None = None):
     if partials.dim() == 2:
@@ -376,6 +387,26 @@ def gemm_residual_norm(A: torch.Tensor, B: torch.Tensor, resid: torch.Tensor,
             N, K, _p(resid), _row_stride(resid, "resid"), _p(norm_w), _p(x_out),
             _row_stride(x_out, "x_out") if x_out is not None else 0, _p(sumsq),
             sumsq.stride(0) if sumsq is not None else 0, _stream())
+    if gemm_probe is None:
+        call(*args)
+    else:
+        with gemm_probe(2.0 * M * N * K):
+            call(*args)
+
+
+def gemm_clamp_dual(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, C_bf16: torch.Tensor,
+                    clamp: Clamp = NO_CLAMP, M: int | None = None):
+    """C = mu_clamp?(A · Bᵀ) in f32 and its bf16 copy C_bf16, in one GEMM
+    (split-K 1)."""
+    _check(A, torch.bfloat16, "A")
+    _check(B, torch.bfloat16, "B")
+    _check(C, torch.float32, "C")
+    _check(C_bf16, torch.bfloat16, "C_bf16")
+    M = A.shape[0] if M is None else M
+    N, K = B.shape[0], A.shape[1]
+    args = ("muk_gemm_clamp_dual", _p(A), _row_stride(A, "A"), _p(B), _row_stride(B, "B"), _p(C),
+            _row_stride(C, "C"), _p(C_bf16), _row_stride(C_bf16, "C_bf16"), M, N, K,
+            int(clamp.enabled), clamp.mu, clamp.clamp_min, clamp.clamp_max, _stream())
     if gemm_probe is None:
         call(*args)
     else:

@@ -25,9 +25,10 @@ from typing import Dict, List, Optional
 
 import torch
 
+from .. import _lib
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
-from .base import PAD_MULT, MuModelBase, interleave_gate_up, pad_cols, pad_to
+from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
 from .registry import register_model
 from .weights import expert_intermediate, is_routed
 
@@ -138,6 +139,12 @@ class DeepForCausalLM(MuModelBase):
         return ts
 
     # ---- step ------------------------------------------------------------------
+    def _ctrl_split(self, T: int, N: int, K: int) -> int:
+        """Split-K factor of the controller's input layer (the partials live
+        in ws.ctrl, [T, 3H] f32)."""
+        cap = (3 * self.config.hidden_size) // max(N, 1)
+        return int(_lib.load().muk_gemm_plan_split(T, N, K, _lib.MUK_EPI_F32, max(1, min(16, cap))))
+
     def forward_step(self, batch, cache) -> torch.Tensor:
         cfg, ws, cl = self.config, self.ws, self.clamp
         T, H, eps = batch.num_tokens, cfg.hidden_size, cfg.rms_norm_eps
@@ -153,15 +160,28 @@ class DeepForCausalLM(MuModelBase):
             self.qkv_proj(l, xcat[:, :kdim], L["wcat"][:, :kdim], batch, cache, L.get("qn"),
                           L.get("kn"))
             attn = self.attention(l, batch, cache)
-            part = self.row_parallel(attn[:T], L["wo"], T, H)
-            K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)   # h = clamp(o_proj)
+            # h = clamp(o_proj(attn)) in f32 (INL input) and bf16 (controller / mu GEMMs)
+            if self.tp_group is None and H % 32 == 0 and \
+                    choose_split(T, H, attn.shape[1], ws.part_rows) == 1:
+                K.gemm_clamp_dual(attn[:T], L["wo"], ws.h, ws.hv[:, :H], cl, M=T)
+            else:
+                part = self.row_parallel(attn[:T], L["wo"], T, H)
+                K.reduce_clamp(part, ws.h, ws.hv[:, :H], cl, num_tokens=T)
             # controller input [h | v]: the velocity starts at zero
             # (layers.py:99-100), so layer 0 multiplies the h half only
-            if l == 0:
-                K.gemm(ws.hv[:, :H], L["wci"][:, :H], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"],
-                       M=T)
+            kc = H if l == 0 else 2 * H
+            a_ci, w_ci = ws.hv[:, :kc], L["wci"][:, :kc]
+            nc = w_ci.shape[0]
+            # the narrow (64-wide) layer is a few tiles over a long K: split-K
+            # partials (in ws.ctrl, written only later by controller_out) and a
+            # bias + SiLU pass keep every SM streaming
+            s = self._ctrl_split(T, nc, kc) if nc <= 128 else 1
+            if s > 1:
+                part = ws.ctrl.view(-1)[: s * T * nc].view(s, T, nc)
+                K.gemm(a_ci, w_ci, part, K.MUK_EPI_F32, split_k=s, M=T)
+                K.reduce_bias_silu(part, L["bci"], ws.ch, num_rows=T)
             else:
-                K.gemm(ws.hv, L["wci"], ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
+                K.gemm(a_ci, w_ci, ws.ch, K.MUK_EPI_BIAS_SILU, bias=L["bci"], M=T)
             K.gemm(ws.ch, L["wco"], ws.ctrl, K.MUK_EPI_F32, M=T)
             K.gemm(ws.hv[:, :H], L["wmu"], ws.mp, K.MUK_EPI_F32, M=T)
             K.inl_dynamics(ws.h, ws.ctrl, L["bco"], ws.mp, L["mu"], cfg.dynamics_dt, ws.v,

@@ -250,6 +250,17 @@ int muk_gemm_residual_norm(const void* A, int64_t lda, const void* B, int64_t ld
                            int K, float* resid, int64_t ld_resid, const float* norm_w, void* x_out,
                            int64_t ldx, float* sumsq, int64_t sumsq_stride, void* stream);
 
+/* One-GPU O projection of the Deep layer with the clamp and both output
+ * copies in the epilogue (split-K 1): C[m, :] = c and C_bf16[m, :] = bf16(c)
+ * with c = mu_clamp?(A[m, :] · Bᵀ) (f32 rows, row strides ldc / ld_bf16,
+ * N a multiple of 32).  Replaces muk_gemm_bf16 (MUK_EPI_F32) followed by
+ * muk_reduce_clamp for `h = mu_clamp(o_proj(attn))` (the end of
+ * MuAttention.forward, mu_inference/models/layers.py:730-739), the input of
+ * the INL dynamics (mu_inference/models/deep.py:151-152). */
+int muk_gemm_clamp_dual(const void* A, int64_t lda, const void* B, int64_t ldb, float* C,
+                        int64_t ldc, void* C_bf16, int64_t ld_bf16, int M, int N, int K, int clamp,
+                        float mu, float clamp_min, float clamp_max, void* stream);
+
 /* muk_gemm_bf16 with MUK_EPI_SWIGLU whose accumulator rows are scaled by the
  * row norm of `rownorm` (NULL: unscaled) before the SwiGLU. */
 int muk_gemm_swiglu_rownorm(const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
@@ -337,6 +348,16 @@ int muk_inl_dynamics(const float* h, const float* ctrl_raw, const float* ctrl_bi
                      int64_t norm_out_stride, const int32_t* token_ids, const void* router_w,
                      int num_experts, int vocab, int32_t* expert_ids, int num_tokens, int hidden,
                      int clamp_norm, float mu, float clamp_min, float clamp_max, void* stream);
+
+/* Split-K tail of the INL controller's input layer: out[t][c] =
+ * bf16(silu(Σ_p partials[p][t][c] + bias[c])) for rows x cols f32 partials
+ * (slice stride partial_stride).  With muk_gemm_bf16 (MUK_EPI_F32, split-K)
+ * it is silu(controller_in([h, v])) of INLDynamics,
+ * mu_inference/models/layers.py:103-104, for the narrow (64-wide) layer
+ * whose one-pass GEMM leaves most SMs idle. */
+int muk_reduce_bias_silu(const float* partials, int64_t partial_stride, int num_partials,
+                         const float* bias, void* out, int64_t out_stride, int rows, int cols,
+                         void* stream);
 
 /* f32 row pass used around the INL GEMMs: dst_f32[t] = mu_clamp?(Σ_p partials[p][t]),
  * dst_bf16[t] = bf16(dst_f32[t]). */

@@ -835,3 +835,47 @@ def test_gemm_rownorm_consumers(cuda, M, sk):
     from mu_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+# O projection of the Deep layer with the clamp and both output copies in
+# the epilogue: one row, a CTA-pair shape, the C5 step shape.
+@pytest.mark.parametrize("M,N,K", [(1, 256, 320), (300, 1024, 640), (2338, 4096, 4096)])
+def test_gemm_clamp_dual(cuda, M, N, K):
+    k = _kern()
+    from mu_b200.kernels import Clamp
+
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    W = (torch.randn(N, K, device=cuda, generator=g) * 0.3).bfloat16()
+    for cl in (Clamp(True), Clamp(False)):
+        C = torch.full((M + 2, N), float("nan"), device=cuda)
+        Cb = torch.full((M + 2, 2 * N), float("nan"), device=cuda, dtype=torch.bfloat16)
+        k.gemm_clamp_dual(A, W, C, Cb[:, :N], cl, M=M)
+        ref = A.float() @ W.float().t()
+        if cl.enabled:
+            ref = _mu_clamp(ref)
+        torch.testing.assert_close(C[:M], ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
+        assert torch.equal(Cb[:M, :N], C[:M].bfloat16())
+        assert torch.isnan(C[M:]).all() and torch.isnan(Cb[M:].float()).all()
+        assert torch.isnan(Cb[:, N:].float()).all()
+    from mu_b200 import _lib
+
+    assert _lib.device_error() == 0
+
+
+def test_reduce_bias_silu(cuda):
+    """Split-K tail of the INL controller's input layer: the f32 GEMM
+    partials summed, bias added, SiLU, bf16."""
+    k = _kern()
+    T, N, Kd, S = 300, 64, 2048, 6
+    g = torch.Generator(device="cuda").manual_seed(21)
+    A = torch.randn(T, Kd, device=cuda, generator=g).bfloat16()
+    W = (torch.randn(N, Kd, device=cuda, generator=g) * 0.05).bfloat16()
+    b = torch.randn(N, device=cuda, generator=g)
+    part = torch.empty(S, T, N, device=cuda)
+    k.gemm(A, W, part, k.MUK_EPI_F32, split_k=S)
+    out = torch.full((T + 1, 2 * N), float("nan"), device=cuda, dtype=torch.bfloat16)
+    k.reduce_bias_silu(part, b, out[:, :N], num_rows=T)
+    ref = torch.nn.functional.silu(A.float() @ W.float().t() + b)
+    torch.testing.assert_close(out[:T, :N].float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+    assert torch.isnan(out[T:].float()).all() and torch.isnan(out[:, N:].float()).all()
