@@ -263,7 +263,8 @@ class Recorder:
         h = self.orig_launch(logits, request_ids, params, steps, token_rows, input_ids,
                              num_tokens)
         if self.on:  # stream-ordered after the blob's host-to-device copy
-            self.blobs.append((len(request_ids), num_tokens, self.sampler._blob_d.clone()))
+            self.blobs.append((len(request_ids), num_tokens, self.sampler._blob_d.clone(),
+                               all(p.temperature <= 0 for p in params)))
         return h
 
 
@@ -601,18 +602,17 @@ def run_ours(args, rank, world, local_rank):
     # path are absent.
     smp = engine.sampler
     assert len(rec.blobs) == len(rec.steps)
-    assert all(b.numel() == smp._blob_d.numel() for _, _, b in rec.blobs)
+    assert all(b.numel() == smp._blob_d.numel() for _, _, b, _ in rec.blobs)
 
     @torch.inference_mode()  # the engine's buffers are inference tensors
     def replay():
-        for (st, buf), (B, T, blob) in zip(rec.steps, rec.blobs):
+        for (st, buf), (B, T, blob, greedy) in zip(rec.steps, rec.blobs):
             worker.packer.dev[:st.end].copy_(buf, non_blocking=True)
             logits, batch = worker.run_staged(st)
             smp._blob_d[:blob.numel()].copy_(blob, non_blocking=True)
             if T > 0:
                 smp.mark_inputs(batch.token_rows, batch.input_ids, T)
-            K.sample(logits, smp.d_temp, smp.d_topk, smp.d_topp, smp.d_rep, smp.seen,
-                     smp.d_seed, smp.d_off, smp.d_out, num_rows=B, seen_rows=smp.d_rows)
+            smp.device_sample(logits, B, greedy)
 
     replay()  # graphs for every bucket exist already; this warms the replay path
     torch.cuda.synchronize()

@@ -353,6 +353,185 @@ __global__ void ep_gather_finish_kernel(const GatherArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Vocabulary-parallel LM head under tensor parallelism: rank r computes the
+// logits of vocabulary columns [col0_r, col0_r + cols) into its [rows][ld]
+// logits buffer (peer-mapped, the same layout on every rank).
+//
+// Column all-gather (any sampling): every rank stores its column slice into
+// every peer's buffer, so each ends with the full [rows][V] logits; push and
+// finish as the expert combine above (arrival barrier, NVLink stores,
+// "pushed" barrier), with its own flag words.
+constexpr int kFlagCPushed = 42;   // [kMaxRanks]
+constexpr int kFlagCArrived = 50;  // [kMaxRanks]
+constexpr int kFlagCEpoch = 58;
+constexpr int kFlagArrive4 = 59;
+// Greedy (every row at temperature 0): each rank reduces its slice to one
+// (value, index) pair per row, stores the pair into every rank's pair
+// buffer, and every rank picks the largest value, lowest index on ties: the
+// argmax of the full row, as the sampler's greedy path computes it.  Pair
+// buffers alternate by the call's epoch parity, so a rank can store the
+// next call's pairs while a slower peer still reads this call's.
+constexpr int kFlagTPushed = 64;   // [kMaxRanks]
+constexpr int kFlagTEpoch = 72;
+constexpr int kFlagArrive5 = 73;
+constexpr int kFlagWords = 128;
+
+struct ColGatherArgs {
+  float4* data[kMaxRanks];  // each rank's logits buffer (as mapped here)
+  uint32_t* flags[kMaxRanks];
+  int rank, world, rows;
+  int64_t ld4;              // row stride in float4 units
+  int col0_4, cols4;        // this rank's slice, float4 units
+};
+
+__global__ void __launch_bounds__(kGatherThreads) col_gather_push_kernel(const ColGatherArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagCEpoch) + 1u;
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0)
+      for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagCArrived + a.rank, epoch);
+    ok = wait_all(my, kFlagCArrived, a.world, epoch);
+  }
+  __syncthreads();
+  if (ok) {
+    const float4* src = a.data[a.rank];
+    const int64_t total = (int64_t)a.rows * a.cols4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = i / a.cols4;
+      const int64_t off = r * a.ld4 + a.col0_4 + (i - r * a.cols4);
+      const float4 v = src[off];
+#pragma unroll
+      for (int s = 0; s < kMaxRanks; ++s)
+        if (s < a.world && s != a.rank) a.data[s][off] = v;
+    }
+  }
+  if (last_cta(my + kFlagArrive4))
+    for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagCPushed + a.rank, epoch);
+}
+
+__global__ void col_gather_finish_kernel(const ColGatherArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagCEpoch) + 1u;
+  if (threadIdx.x == 0) {
+    wait_all(my, kFlagCPushed, a.world, epoch);
+    *reinterpret_cast<volatile uint32_t*>(my + kFlagCEpoch) = epoch;
+  }
+}
+
+struct GreedyArgs {
+  const float* logits;      // this rank's buffer; its slice holds this rank's logits
+  int64_t ld;
+  int col0, cols;
+  const float* rep;         // [rows] repetition penalty, or null
+  const int32_t* seen;      // [*][seen_stride] bitmaps, or null
+  int64_t seen_stride;
+  const int32_t* seen_rows; // bitmap row of each row, or null (= row)
+  uint2* pairs[kMaxRanks];  // each rank's pair buffer: [2 parities][world][rows_cap]
+  uint32_t* flags[kMaxRanks];
+  int rank, world, rows, rows_cap;
+  int32_t* out;
+};
+
+constexpr int kGreedyThreads = 256;
+
+__global__ void __launch_bounds__(kGreedyThreads) tp_greedy_push_kernel(const GreedyArgs a) {
+  __shared__ float redv[32];
+  __shared__ int redi[32];
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagTEpoch) + 1u;
+  const int row = blockIdx.x;
+  const float* x = a.logits + (int64_t)row * a.ld;
+  const float rp = a.rep ? a.rep[row] : 1.f;
+  const int srow = a.seen_rows ? a.seen_rows[row] : row;
+  const int32_t* seen = (a.seen != nullptr && rp != 1.f) ? a.seen + (int64_t)srow * a.seen_stride
+                                                         : nullptr;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  // each thread keeps the first maximum of its indices, visited in
+  // increasing order; the sampler's penalty divides positive logits of seen
+  // tokens and multiplies the others
+  auto visit = [&](float v, int g) {
+    if (seen != nullptr && ((seen[g >> 5] >> (g & 31)) & 1)) v = v > 0.f ? v / rp : v * rp;
+    if (v > best) {
+      best = v;
+      bi = g;
+    }
+  };
+  int scalar_from = 0;
+  if (((a.col0 | a.cols) & 3) == 0 && (a.ld & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x + a.col0);
+    const int n4 = a.cols >> 2;
+    for (int i4 = threadIdx.x; i4 < n4; i4 += blockDim.x) {
+      const float4 q = x4[i4];
+      const int g = a.col0 + 4 * i4;
+      visit(q.x, g);
+      visit(q.y, g + 1);
+      visit(q.z, g + 2);
+      visit(q.w, g + 3);
+    }
+    scalar_from = a.cols;
+  }
+  for (int i = scalar_from + (int)threadIdx.x; i < a.cols; i += blockDim.x)
+    visit(x[a.col0 + i], a.col0 + i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    redv[threadIdx.x >> 5] = best;
+    redi[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (redv[w] > best || (redv[w] == best && redi[w] < bi)) {
+        best = redv[w];
+        bi = redi[w];
+      }
+    const uint2 pr = make_uint2(__float_as_uint(best), (uint32_t)bi);
+    const int64_t slot = ((int64_t)(epoch & 1u) * a.world + a.rank) * a.rows_cap + row;
+    for (int s = 0; s < a.world; ++s) a.pairs[s][slot] = pr;
+  }
+  if (last_cta(my + kFlagArrive5))
+    for (int s = 0; s < a.world; ++s) st_release_sys(a.flags[s] + kFlagTPushed + a.rank, epoch);
+}
+
+__global__ void __launch_bounds__(kGreedyThreads) tp_greedy_finish_kernel(const GreedyArgs a) {
+  uint32_t* my = a.flags[a.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagTEpoch) + 1u;
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = wait_all(my, kFlagTPushed, a.world, epoch);
+  __syncthreads();
+  if (ok) {
+    const uint2* pr = a.pairs[a.rank] + (int64_t)(epoch & 1u) * a.world * a.rows_cap;
+    for (int row = threadIdx.x; row < a.rows; row += blockDim.x) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int s = 0; s < a.world; ++s) {  // rank order = vocabulary order
+        const uint2 p = pr[(int64_t)s * a.rows_cap + row];
+        const float v = __uint_as_float(p.x);
+        const int i = (int)p.y;
+        if (v > best || (v == best && i < bi)) {
+          best = v;
+          bi = i;
+        }
+      }
+      a.out[row] = bi == 0x7fffffff ? 0 : bi;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(my + kFlagTEpoch) = epoch;
+}
+
 // ---- IPC plumbing: the allocation base of a pointer (cudaIpc works on whole
 // allocations) through the driver entry point, like the tensor-map encoder.
 static PFN_cuPointerGetAttribute_v4000 g_ptr_attr = nullptr;
@@ -487,7 +666,7 @@ extern "C" int muk_ipc_close_handle(void* base) {
   return MUK_OK;
 }
 
-extern "C" size_t muk_allreduce_flag_bytes(void) { return 64 * sizeof(uint32_t); }
+extern "C" size_t muk_allreduce_flag_bytes(void) { return kFlagWords * sizeof(uint32_t); }
 
 extern "C" int64_t muk_allreduce_scratch_elems(int64_t n, int world) {
   if (n < 0 || world < 1) return 0;
@@ -630,4 +809,78 @@ extern "C" int muk_tp_residual_norm(float* const* bufs, float* const* scratch,
   return launch_tp_norm_finish(bufs, scratch, flags, rank, world, T, H, share_rows, slices,
                                slice_stride, false, resid, H, norm_w, eps, x_bufs, ldx,
                                clamp_delta, clamp_sum, clamp_norm, mu, cmin, cmax, st);
+}
+
+extern "C" int muk_tp_allgather_cols(float* const* bufs, uint32_t* const* flags, int rank,
+                                     int world, int rows, int64_t ld, int col0, int cols,
+                                     void* stream) {
+  MUK_REQUIRE(bufs && flags && world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world,
+              "muk_tp_allgather_cols: rank %d of %d (at most %d ranks)", rank, world, kMaxRanks);
+  MUK_REQUIRE(rows >= 0 && cols > 0 && col0 >= 0 && ld >= (int64_t)col0 + cols && ld % 4 == 0 &&
+                  cols % 4 == 0 && col0 % 4 == 0,
+              "muk_tp_allgather_cols: rows %d, columns [%d, %d) of %lld (multiples of 4)", rows,
+              col0, col0 + cols, (long long)ld);
+  ColGatherArgs a;
+  for (int s = 0; s < kMaxRanks; ++s) {
+    a.data[s] = s < world ? reinterpret_cast<float4*>(bufs[s]) : nullptr;
+    a.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  for (int s = 0; s < world; ++s)
+    MUK_REQUIRE(a.data[s] && a.flags[s] && MUK_ALIGNED16(a.data[s]) && MUK_ALIGNED16(a.flags[s]),
+                "muk_tp_allgather_cols: rank %d buffer or flags null / not 16-byte aligned", s);
+  a.rank = rank;
+  a.world = world;
+  a.rows = rows;
+  a.ld4 = ld / 4;
+  a.col0_4 = col0 / 4;
+  a.cols4 = cols / 4;
+  if (world == 1 || rows == 0) return MUK_OK;
+  cudaStream_t st = as_stream(stream);
+  col_gather_push_kernel<<<148, kGatherThreads, 0, st>>>(a);
+  int rc = check_launch("muk_tp_allgather_cols(push)");
+  if (rc) return rc;
+  col_gather_finish_kernel<<<1, 32, 0, st>>>(a);
+  return check_launch("muk_tp_allgather_cols(finish)");
+}
+
+extern "C" int muk_tp_greedy(const float* logits, int64_t ld, int rows, int col0, int cols,
+                             const float* rep_penalty, const int32_t* seen_bits,
+                             int64_t seen_stride, const int32_t* seen_rows, void* const* pair_bufs,
+                             int rows_cap, uint32_t* const* flags, int rank, int world,
+                             int32_t* out, void* stream) {
+  MUK_REQUIRE(logits && pair_bufs && flags && out && world >= 1 && world <= kMaxRanks &&
+                  rank >= 0 && rank < world,
+              "muk_tp_greedy: rank %d of %d (at most %d ranks)", rank, world, kMaxRanks);
+  MUK_REQUIRE(rows >= 0 && rows <= rows_cap && cols > 0 && col0 >= 0 && ld >= (int64_t)col0 + cols,
+              "muk_tp_greedy: rows %d (capacity %d), columns [%d, %d) of %lld", rows, rows_cap,
+              col0, col0 + cols, (long long)ld);
+  GreedyArgs a;
+  for (int s = 0; s < kMaxRanks; ++s) {
+    a.pairs[s] = s < world ? reinterpret_cast<uint2*>(pair_bufs[s]) : nullptr;
+    a.flags[s] = s < world ? flags[s] : nullptr;
+  }
+  for (int s = 0; s < world; ++s)
+    MUK_REQUIRE(a.pairs[s] && a.flags[s] && ((uintptr_t)a.pairs[s] & 7) == 0 &&
+                    MUK_ALIGNED16(a.flags[s]),
+                "muk_tp_greedy: rank %d pair buffer or flags null / misaligned", s);
+  a.logits = logits;
+  a.ld = ld;
+  a.col0 = col0;
+  a.cols = cols;
+  a.rep = rep_penalty;
+  a.seen = seen_bits;
+  a.seen_stride = seen_stride;
+  a.seen_rows = seen_rows;
+  a.rank = rank;
+  a.world = world;
+  a.rows = rows;
+  a.rows_cap = rows_cap;
+  a.out = out;
+  if (rows == 0) return MUK_OK;
+  cudaStream_t st = as_stream(stream);
+  tp_greedy_push_kernel<<<rows, kGreedyThreads, 0, st>>>(a);
+  int rc = check_launch("muk_tp_greedy(push)");
+  if (rc) return rc;
+  tp_greedy_finish_kernel<<<1, kGreedyThreads, 0, st>>>(a);
+  return check_launch("muk_tp_greedy(finish)");
 }

@@ -47,6 +47,9 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
               "muk_llama_forward: bad batch (T=%d B=%d decode=%d)", b->num_tokens, b->num_seqs,
               b->num_decode);
   MUK_REQUIRE(m->tp_world >= 1 && m->tp_world <= 8, "muk_llama_forward: tp_world %d", m->tp_world);
+  MUK_REQUIRE(m->lm_rows > 0 && m->lm_rows <= m->vocab && m->logits_ld >= m->lm_rows,
+              "muk_llama_forward: LM head rows %d / logits stride %lld (vocab %d)", m->lm_rows,
+              (long long)m->logits_ld, m->vocab);
   const int T = b->num_tokens, B = b->num_seqs, nd = b->num_decode;
   const int H = m->hidden, Hq = m->num_q_heads, Hkv = m->num_kv_heads, D = m->head_dim;
   const int qkv_n = (Hq + 2 * Hkv) * D, attn_n = Hq * D;
@@ -130,8 +133,8 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
     }
     MUK_TRY(muk_rmsnorm_rows(m->resid, b->last_token_idx, B, m->final_norm, m->eps, m->xl, H, H,
                              cl, mu, cmin, cmax, stream));
-    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32,
-                         1, nullptr, stream);
+    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->logits_ld, B, m->lm_rows, H,
+                         kEpiF32, 1, nullptr, stream);
   }
 
   // q|k|v projection with RoPE and the KV append (fused or as two kernels)
@@ -181,8 +184,8 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
                            last ? m->final_norm : m->layers[l + 1].in_norm, cl));
     }
     MUK_TRY(muk_gather_rows_bf16(x, m->x_stride, b->last_token_idx, B, m->xl, H, H, stream));
-    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32,
-                         1, nullptr, stream);
+    return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->logits_ld, B, m->lm_rows, H,
+                         kEpiF32, 1, nullptr, stream);
   }
 
   for (int l = 0; l < m->num_layers; ++l) {
@@ -240,6 +243,6 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
   }
   MUK_TRY(muk_rmsnorm_rows(m->resid, b->last_token_idx, B, m->final_norm, m->eps, m->xl, H, H, cl,
                            mu, cmin, cmax, stream));
-  return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->vocab, B, m->vocab, H, kEpiF32, 1,
-                       nullptr, stream);
+  return muk_gemm_bf16(m->xl, H, m->lm_head, H, m->logits, m->logits_ld, B, m->lm_rows, H,
+                       kEpiF32, 1, nullptr, stream);
 }

@@ -226,7 +226,59 @@ __global__ void __launch_bounds__(kSampThreads)
     q.temp = 1.f;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = tid; i < V; i += blockDim.x) {
+    // each thread visits its indices in increasing order and keeps the first
+    // maximum; the block reduction then takes the lowest index among equals
+    int tail = 0;
+    if ((V & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(p.x);
+      const int v4 = V >> 2;
+      int i4 = tid;
+      for (; i4 + (int)blockDim.x < v4; i4 += 2 * blockDim.x) {  // two loads in flight
+        const float4 a = x4[i4], b = x4[i4 + blockDim.x];
+        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float v = av[k];
+          const int i = 4 * i4 + k;
+          if (q.seen != nullptr && ((q.seen[i >> 5] >> (i & 31)) & 1u))
+            v = v > 0.f ? v / q.rp : v * q.rp;
+          if (v > best) {
+            best = v;
+            bi = i;
+          }
+        }
+        // a thread's second float4 lies past its first, so order is kept
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float v = bv[k];
+          const int i = 4 * (i4 + blockDim.x) + k;
+          if (q.seen != nullptr && ((q.seen[i >> 5] >> (i & 31)) & 1u))
+            v = v > 0.f ? v / q.rp : v * q.rp;
+          if (v > best) {
+            best = v;
+            bi = i;
+          }
+        }
+      }
+      for (; i4 < v4; i4 += blockDim.x) {
+        const float4 a = x4[i4];
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float v = av[k];
+          const int i = 4 * i4 + k;
+          if (q.seen != nullptr && ((q.seen[i >> 5] >> (i & 31)) & 1u))
+            v = v > 0.f ? v / q.rp : v * q.rp;
+          if (v > best) {
+            best = v;
+            bi = i;
+          }
+        }
+      }
+    } else {
+      tail = V;
+    }
+    for (int i = tid; i < tail; i += blockDim.x) {
       const float v = row_val(q, i);
       if (v > best) {
         best = v;

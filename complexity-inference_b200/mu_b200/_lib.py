@@ -88,6 +88,9 @@ SIGNATURES = {
     "muk_gemm_tp_residual_norm": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P,
                                           _P, c_int, c_int, _P, _P, c_float, _P, c_int64, c_int,
                                           c_int, c_int, c_float, c_float, c_float, _P]),
+    "muk_tp_allgather_cols": (c_int, [_P, _P, c_int, c_int, c_int, c_int64, c_int, c_int, _P]),
+    "muk_tp_greedy": (c_int, [_P, c_int64, c_int, c_int, c_int, _P, _P, c_int64, _P, _P, c_int,
+                              _P, c_int, c_int, _P, _P]),
     "muk_ep_gather_bf16": (c_int, [_P, _P, c_int, c_int, _P, c_int, c_int, c_int, _P]),
     "muk_llama_forward": (c_int, [_P, _P, _P]),
     "muk_gemm_allreduce_scratch_elems": (c_int64, [c_int, c_int, c_int]),
@@ -137,7 +140,8 @@ class MukLlamaModel(ctypes.Structure):
                 ("tp_world", c_int), ("tp_rank", c_int), ("ar_data", c_void_p * 8),
                 ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int),
                 ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p),
-                ("tp_norm", c_int), ("x_peer", c_void_p * 8)]
+                ("tp_norm", c_int), ("x_peer", c_void_p * 8), ("lm_rows", c_int),
+                ("logits_ld", c_int64)]
 
 
 class MukStepBatch(ctypes.Structure):
@@ -155,7 +159,7 @@ _lib: ctypes.CDLL | None = None
 launch_count = 0
 _TWO_KERNELS = {"muk_paged_decode_attn", "muk_paged_decode_attn_static", "muk_allreduce_f32",
                 "muk_gemm_allreduce_f32", "muk_ep_gather_bf16", "muk_tp_residual_norm",
-                "muk_gemm_tp_residual_norm"}
+                "muk_gemm_tp_residual_norm", "muk_tp_allgather_cols", "muk_tp_greedy"}
 
 
 class MukError(RuntimeError):

@@ -25,7 +25,8 @@ from . import _lib
 
 
 class PeerAllReduce:
-    def __init__(self, group, max_elems: int, device, x_elems: int = 0):
+    def __init__(self, group, max_elems: int, device, x_elems: int = 0, logits_elems: int = 0,
+                 pair_rows: int = 0):
         import torch.distributed as dist
 
         self.group = group
@@ -45,7 +46,13 @@ class PeerAllReduce:
         # normalised rows from muk_tp_residual_norm.
         self.flag_words = flag_words
         self.x_words = (int(x_elems) + 1) // 2 + 15 & ~15
-        self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words + self.x_words,
+        # [... | logits (f32, the vocabulary-parallel LM head) | greedy pairs
+        # (2 parities x world x pair_rows x 8 bytes)]
+        self.logits_words = int(logits_elems) + 15 & ~15
+        self.pair_rows = int(pair_rows)
+        self.pair_words = 2 * self.world * self.pair_rows * 2 + 15 & ~15
+        self.buf = torch.zeros(self.max_elems + self.scratch_elems + flag_words + self.x_words
+                               + self.logits_words + self.pair_words,
                                dtype=torch.float32, device=device)
         torch.cuda.synchronize(device)
         handle = (ctypes.c_uint8 * 64)()
@@ -74,6 +81,10 @@ class PeerAllReduce:
         self._x_off = self.max_elems + self.scratch_elems + flag_words
         self.x_ptrs = [p + self._x_off * 4 for p in ptrs]
         self._xs = (ctypes.c_void_p * self.world)(*self.x_ptrs)
+        self._lg_off = self._x_off + self.x_words
+        self._lgs = (ctypes.c_void_p * self.world)(*[p + self._lg_off * 4 for p in ptrs])
+        self._pr_off = self._lg_off + self.logits_words
+        self._prs = (ctypes.c_void_p * self.world)(*[p + self._pr_off * 4 for p in ptrs])
         self._scratch = (ctypes.c_void_p * self.world)(*self.scratch_ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*self.flag_ptrs)
         dist.barrier(group=group)
@@ -91,6 +102,39 @@ class PeerAllReduce:
             return None
         x = self.buf[self._x_off:self._x_off + self.x_words].view(torch.bfloat16)
         return x[: rows * cols].view(rows, cols)
+
+    def logits_view(self, rows: int, cols: int) -> torch.Tensor | None:
+        """[rows, cols] f32 in this rank's logits area (None if it does not
+        fit): the buffer the vocabulary-parallel LM head writes its column
+        slice into and the column all-gather fills."""
+        if rows * cols > self.logits_words:
+            return None
+        return self.buf[self._lg_off:self._lg_off + rows * cols].view(rows, cols)
+
+    def allgather_cols_(self, logits: torch.Tensor, rows: int, col0: int, cols: int) -> None:
+        """Store this rank's columns [col0, col0 + cols) of rows [0, rows) of
+        ``logits`` (a logits_view) into every rank's buffer
+        (``muk_tp_allgather_cols``)."""
+        if logits.data_ptr() != self.buf.data_ptr() + self._lg_off * 4:
+            raise ValueError("allgather_cols_: logits must be the logits_view")
+        _lib.call("muk_tp_allgather_cols", ctypes.addressof(self._lgs),
+                  ctypes.addressof(self._flags), self.rank, self.world, rows, logits.stride(0),
+                  col0, cols, torch.cuda.current_stream().cuda_stream)
+
+    def greedy_(self, logits: torch.Tensor, rows: int, col0: int, cols: int, rep_penalty,
+                seen_bits, seen_rows, out: torch.Tensor) -> None:
+        """out[:rows] = the argmax of every full row (with the repetition
+        penalty) from this rank's column slice and the peers' (value, index)
+        pairs (``muk_tp_greedy``)."""
+        if rows > self.pair_rows:
+            raise ValueError(f"greedy_: {rows} rows > pair capacity {self.pair_rows}")
+        _lib.call("muk_tp_greedy", logits.data_ptr(), logits.stride(0), rows, col0, cols,
+                  None if rep_penalty is None else rep_penalty.data_ptr(),
+                  None if seen_bits is None else seen_bits.data_ptr(),
+                  0 if seen_bits is None else seen_bits.stride(0),
+                  None if seen_rows is None else seen_rows.data_ptr(),
+                  ctypes.addressof(self._prs), self.pair_rows, ctypes.addressof(self._flags),
+                  self.rank, self.world, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
 
     def residual_norm_(self, part: torch.Tensor, resid: torch.Tensor, norm_w, eps: float,
                        x: torch.Tensor, clamp, clamp_delta: bool, clamp_sum: bool,

@@ -107,7 +107,13 @@ class Workspace:
         self.part = comm.view(n) if self.shared_part else torch.empty(n, device=dev, dtype=f32)
         self.act = torch.empty(T, model.act_width(), device=dev, dtype=bf)
         self.xl = torch.empty(max_seqs, H, device=dev, dtype=bf)
-        self.logits = torch.empty(max_seqs, cfg.vocab_size, device=dev, dtype=f32)
+        # under a vocabulary-parallel LM head the logits live in the peer
+        # buffer (each rank writes its columns, the samplers combine them)
+        lg = comm.logits_view(max_seqs, cfg.vocab_size) \
+            if comm is not None and model.vocab_parallel_ok() else None
+        self.shared_logits = lg is not None
+        self.logits = lg if lg is not None else torch.empty(max_seqs, cfg.vocab_size, device=dev,
+                                                            dtype=f32)
         nbytes = K.decode_attn_workspace_size(max_seqs, Hq, D, max_seq_len)
         self.attn_ws = torch.empty(max(nbytes // 4, 4), device=dev, dtype=f32)
         model.extra_workspace(self, T)
@@ -151,6 +157,27 @@ class MuModelBase:
 
     def extra_workspace(self, ws: Workspace, T: int) -> None:
         pass
+
+    def vocab_parallel_ok(self) -> bool:
+        """Whether the LM head can run vocabulary-parallel: peer-memory tensor
+        parallelism and V a multiple of 4 x ranks (MU_TP_VOCAB=0: every rank
+        computes the full head)."""
+        if self.tp_group is None or os.environ.get("MU_TP_COMM", "peer") != "peer":
+            return False
+        if os.environ.get("MU_TP_VOCAB", "1") == "0":
+            return False
+        import torch.distributed as dist
+
+        return self.config.vocab_size % (4 * dist.get_world_size(self.tp_group)) == 0
+
+    def vocab_slice(self):
+        """(col0, cols) of this rank's vocabulary columns when the LM head is
+        vocabulary-parallel, else None."""
+        ws = self.ws
+        if self.comm is None or ws is None or not ws.shared_logits:
+            return None
+        cols = self.config.vocab_size // self.comm.world
+        return self.comm.rank * cols, cols
 
     def peer_x_elems(self, max_tokens: int) -> int:
         """bf16 elements of the activation rows kept in peer memory under
@@ -263,7 +290,19 @@ class MuModelBase:
         ws, B = self.ws, batch.num_seqs
         K.rmsnorm_rows(ws.resid, batch.last_token_idx[:B], final_norm_w, self.config.rms_norm_eps,
                        ws.xl, self.clamp)
-        K.gemm(ws.xl, lm_w, ws.logits, K.MUK_EPI_F32, M=B)
+        return self.lm_gemm(lm_w, B)
+
+    def lm_gemm(self, lm_w: torch.Tensor, B: int) -> torch.Tensor:
+        """logits = xl · lm_wᵀ; under a vocabulary-parallel head only this
+        rank's columns (rows [col0, col0 + cols) of lm_w) are computed, into
+        the same columns of the shared [B, V] buffer, which is returned."""
+        ws = self.ws
+        vs = self.vocab_slice()
+        if vs is None:
+            K.gemm(ws.xl, lm_w, ws.logits, K.MUK_EPI_F32, M=B)
+        else:
+            c0, n = vs
+            K.gemm(ws.xl, lm_w[c0:c0 + n], ws.logits[:, c0:c0 + n], K.MUK_EPI_F32, M=B)
         return ws.logits[:B]
 
     def forward_step(self, batch, cache) -> torch.Tensor:

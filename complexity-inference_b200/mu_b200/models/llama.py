@@ -137,7 +137,7 @@ class LlamaForCausalLM(MuModelBase):
         ws, cfg = self.ws, self.config
         key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
                self.fused_rope(), self._tp_fused, self.fused_norm(), self.fused_norm_min_rows,
-               self.tp_norm())
+               self.tp_norm(), self.vocab_slice())
         if key == self._native_key:
             return self._native_model
         layers = (_lib.MukLlamaLayer * len(self.layers))()
@@ -153,8 +153,9 @@ class LlamaForCausalLM(MuModelBase):
         m.eps = cfg.rms_norm_eps
         m.clamp, m.mu, m.clamp_min, m.clamp_max = int(cl.enabled), cl.mu, cl.clamp_min, cl.clamp_max
         m.layers = layers
-        m.embed, m.final_norm, m.lm_head = (self.embed.data_ptr(), self.norm_w.data_ptr(),
-                                            self.lm_w.data_ptr())
+        vs = self.vocab_slice()
+        m.embed, m.final_norm = self.embed.data_ptr(), self.norm_w.data_ptr()
+        m.lm_head = self.lm_w.data_ptr() + (0 if vs is None else vs[0] * self.lm_w.stride(0) * 2)
         m.rope_cos, m.rope_sin, m.rope_len = (self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
                                               self.rope_cos.shape[0])
         m.kv_pool, m.num_blocks, m.block_size = (cache.block_pool.data_ptr(), cache.max_num_blocks,
@@ -163,6 +164,12 @@ class LlamaForCausalLM(MuModelBase):
         m.qkv, m.attn, m.act = ws.qkv.data_ptr(), ws.attn.data_ptr(), ws.act.data_ptr()
         m.part, m.part_rows = ws.part.data_ptr(), ws.part_rows
         m.xl, m.logits = ws.xl.data_ptr(), ws.logits.data_ptr()
+        m.lm_rows, m.logits_ld = cfg.vocab_size, ws.logits.stride(0)
+        vs = self.vocab_slice()
+        if vs is not None:  # this rank's vocabulary columns only
+            c0, n = vs
+            m.lm_rows = n
+            m.logits = ws.logits.data_ptr() + 4 * c0
         m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
         m.fused_rope = int(self.fused_rope())
         m.tp_fused = int(self._tp_fused)
@@ -242,8 +249,7 @@ class LlamaForCausalLM(MuModelBase):
                              self.norm_w if last else self.layers[l + 1]["w_in"], True)
             B = batch.num_seqs
             K.gather_rows(x, batch.last_token_idx[:B], ws.xl, num_rows=B)
-            K.gemm(ws.xl, self.lm_w, ws.logits, K.MUK_EPI_F32, M=B)
-            return ws.logits[:B]
+            return self.lm_gemm(self.lm_w, B)
         if self.fused_norm() and T >= max(1, self.fused_norm_min_rows):
             # x holds bf16(w * h); the GEMM that reads it scales each row by
             # rsqrt(mean(h^2) + eps) from the producer's partial sums

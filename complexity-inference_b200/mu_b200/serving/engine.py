@@ -132,6 +132,7 @@ class StepEngine:
                                     2 * max(config.cache.max_num_seqs,
                                             config.scheduler.max_batch_size),
                                     worker.device)
+        self.sampler.tp = self._sampling_tp()
         self.eos_token_id = eos_token_id
         self.overlap = overlap
         self.requests: Dict[str, Request] = {}
@@ -143,6 +144,11 @@ class StepEngine:
         self._closing: set = set()   # last token in flight and length limit reached
 
     # ---- requests ------------------------------------------------------------
+    def _sampling_tp(self):
+        """The worker's vocabulary-parallel sampling context (None without one)."""
+        f = getattr(self.worker, "sampling_tp", None)
+        return f() if f is not None else None
+
     def add_request(self, prompt_token_ids: Sequence[int], sampling_params: SamplingParams,
                     request_id: Optional[str] = None) -> str:
         rid = request_id or uuid.uuid4().hex[:16]
@@ -292,6 +298,7 @@ class StepEngine:
         T = sum(len(s.token_ids) for s in seqs)
         reqs = [self.requests[s.request_id] for s in seqs]
         ids = [s.request_id for s in seqs]
+        self.sampler.tp = self._sampling_tp()  # follows workspace reallocations
         handle = self.sampler.launch(logits, ids, [r.sampling_params for r in reqs],
                                      [r.num_generated_tokens for r in reqs],
                                      batch.token_rows, batch.input_ids, T)

@@ -213,8 +213,12 @@ class MuWorker:
             # may round T up to a CUDA-graph bucket)
             rows = max(max_tokens, _bucket(max_seqs))
             cap = self.model.part_elems(rows)
-            self.model.comm = PeerAllReduce(self.model.tp_group, cap, self.device,
-                                            x_elems=self.model.peer_x_elems(rows))
+            lg_rows = max(max_seqs, _bucket(max_seqs))
+            vp = self.model.vocab_parallel_ok()
+            self.model.comm = PeerAllReduce(
+                self.model.tp_group, cap, self.device, x_elems=self.model.peer_x_elems(rows),
+                logits_elems=lg_rows * mc.vocab_size if vp else 0,
+                pair_rows=lg_rows if vp else 0)
         self.packer = StepPacker(self.device, max_tokens, max_seqs, max_blocks)
         self.model.ensure_workspace(max_tokens, max_seqs, max_blocks * cc.block_size)
         self._graphs.clear()
@@ -356,6 +360,9 @@ class MuWorker:
             nd = sum(1 for r in dec if r.request_id in ok_ids)
             if seqs:
                 logits, _ = self.run_step(seqs, nd)
+                vs = self.model.vocab_slice()
+                if vs is not None:  # each rank computed its vocabulary columns
+                    self.model.comm.allgather_cols_(self.model.ws.logits, len(seqs), *vs)
                 logits = logits.clone()
                 for i, s in enumerate(seqs):
                     out[s.request_id] = WorkerOutput(s.request_id, logits[i:i + 1])
@@ -367,6 +374,12 @@ class MuWorker:
                 if r.request_id not in out or out[r.request_id].error is None:
                     out[r.request_id] = WorkerOutput(r.request_id, torch.zeros(1, V), True, str(e))
         return [out[r.request_id] for r in requests]
+
+    def sampling_tp(self):
+        """(comm, col0, cols) when the LM head is vocabulary-parallel (the
+        sampler then combines the ranks' columns), else None."""
+        vs = self.model.vocab_slice() if self.model is not None else None
+        return None if vs is None else (self.model.comm, vs[0], vs[1])
 
     def close(self) -> None:
         """Release CUDA graphs and peer mappings (before the process group goes)."""

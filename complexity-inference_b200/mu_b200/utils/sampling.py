@@ -62,6 +62,9 @@ class BatchSampler:
         self.free_rows: List[int] = list(range(max_rows - 1, -1, -1))
         self.row_of: Dict[str, int] = {}
         self._seed_of: Dict[str, int] = {}
+        # (comm, col0, cols) under a vocabulary-parallel LM head: the logits
+        # buffer holds only this rank's columns until they are combined
+        self.tp = None
         self._cap = 0
         self._alloc(256)
 
@@ -152,8 +155,7 @@ class BatchSampler:
         self._blob_ev[k] = ev
         if token_rows is not None and num_tokens > 0:
             self.mark_inputs(token_rows, input_ids, num_tokens)
-        K.sample(logits, self.d_temp, self.d_topk, self.d_topp, self.d_rep, self.seen,
-                 self.d_seed, self.d_off, self.d_out, num_rows=B, seen_rows=self.d_rows)
+        self.device_sample(logits, B, all(p.temperature <= 0 for p in params))
         host = self._out_h[k][:B]
         host.copy_(self.d_out[:B], non_blocking=True)
         err = self._err_h[k]
@@ -162,6 +164,20 @@ class BatchSampler:
         done.record(stream)
         self._cur ^= 1
         return SampleHandle(self.d_out[:B], host, done, err)
+
+    def device_sample(self, logits: torch.Tensor, B: int, greedy: bool) -> None:
+        """The sampling launches of one step (parameters already in the
+        device blob) into d_out.  Under a vocabulary-parallel head, an
+        all-greedy step exchanges one (value, index) pair per row and rank;
+        any other step all-gathers the columns first."""
+        if self.tp is not None:
+            comm, c0, n = self.tp
+            if greedy:
+                comm.greedy_(logits, B, c0, n, self.d_rep, self.seen, self.d_rows, self.d_out)
+                return
+            comm.allgather_cols_(logits, B, c0, n)
+        K.sample(logits, self.d_temp, self.d_topk, self.d_topp, self.d_rep, self.seen,
+                 self.d_seed, self.d_off, self.d_out, num_rows=B, seen_rows=self.d_rows)
 
     def sample(self, logits: torch.Tensor, request_ids: Sequence[str],
                params: Sequence[SamplingParams], steps: Sequence[int],

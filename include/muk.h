@@ -492,6 +492,32 @@ int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B, int64_t ld
                            int K, float* const* bufs, float* const* scratch,
                            uint32_t* const* flags, int rank, int world, void* stream);
 
+/* Vocabulary-parallel LM head under tensor parallelism (the vocab-parallel
+ * head of the tensor-parallel Llama step; the reference computes the full
+ * head in one process, mu_inference/models/llama.py:237).  Rank r holds
+ * the logits of columns [col0, col0 + cols) in its [rows][ld] f32 buffer
+ * (peer-mapped, same layout on every rank; bufs[s] = rank s's buffer as
+ * mapped here).
+ *
+ * muk_tp_allgather_cols: every rank stores its column slice into every
+ * peer's buffer, so each ends with all V columns (for sampling that needs
+ * the full rows).  col0, cols and ld are multiples of 4. */
+int muk_tp_allgather_cols(float* const* bufs, uint32_t* const* flags, int rank, int world,
+                          int rows, int64_t ld, int col0, int cols, void* stream);
+
+/* Greedy sampling over the vocabulary slices: per row, the argmax of this
+ * rank's columns of `logits` after the repetition penalty (the sampler's
+ * greedy rule: a seen token's logit is divided by the penalty when positive,
+ * multiplied otherwise; lowest index on ties); the (value, index) pairs are
+ * exchanged through pair_bufs (each rank's [2][world][rows_cap] 8-byte
+ * pairs) and every rank writes the winning index to out[row] — the argmax of
+ * the full row.  Replaces the greedy branch of sample_token
+ * (mu_inference/utils/sampling.py:90-120) for a vocabulary-sharded head. */
+int muk_tp_greedy(const float* logits, int64_t ld, int rows, int col0, int cols,
+                  const float* rep_penalty, const int32_t* seen_bits, int64_t seen_stride,
+                  const int32_t* seen_rows, void* const* pair_bufs, int rows_cap,
+                  uint32_t* const* flags, int rank, int world, int32_t* out, void* stream);
+
 /* Tensor-parallel "h += all-reduce(partials); x = norm(h)" as reduce-scatter
  * + residual/RMSNorm on this rank's rows + all-gather of the bf16 rows, over
  * NVLink peer memory (replaces muk_allreduce_f32 + muk_residual_rmsnorm
@@ -579,6 +605,8 @@ typedef struct {
   int tp_norm;    /* 1 (tp_world > 1): reduce-scatter + residual/RMSNorm on owned rows +
                      all-gather of x (muk_tp_residual_norm); x must be x_peer[tp_rank] */
   void* x_peer[8]; /* every rank's x buffer as mapped here (tp_norm) */
+  int lm_rows;      /* rows of lm_head computed here (vocab, or this rank's vocabulary slice) */
+  int64_t logits_ld; /* row stride of logits (vocab unless the slice sits in a wider buffer) */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */

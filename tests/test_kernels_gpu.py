@@ -879,3 +879,42 @@ def test_reduce_bias_silu(cuda):
     ref = torch.nn.functional.silu(A.float() @ W.float().t() + b)
     torch.testing.assert_close(out[:T, :N].float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
     assert torch.isnan(out[T:].float()).all() and torch.isnan(out[:, N:].float()).all()
+
+
+def test_tp_greedy_single_rank_slice(cuda):
+    """muk_tp_greedy with one rank over a column slice: the argmax of the
+    penalised slice (divide positive logits of seen tokens by the penalty,
+    multiply the others; lowest index on ties), with global indices."""
+    import ctypes
+
+    from mu_b200 import _lib
+
+    B, V, c0, n = 37, 4096, 1024, 2048
+    g = torch.Generator(device="cuda").manual_seed(31)
+    logits = torch.randn(B, V, device=cuda, generator=g)
+    logits[3, c0 + 7] = logits[3, c0 + 900] = 50.0          # tie: lowest index wins
+    logits[4, c0:c0 + n] = float("-inf")                      # all -inf: index 0
+    words = (V + 31) // 32
+    seen = torch.randint(-2**31, 2**31 - 1, (B, words), device=cuda, generator=g, dtype=torch.int32)
+    rep = torch.full((B,), 1.3, device=cuda)
+    rep[::2] = 1.0
+    pairs = torch.zeros(2 * 1 * B * 2, device=cuda, dtype=torch.int32)
+    flags = torch.zeros(int(_lib.load().muk_allreduce_flag_bytes()) // 4, device=cuda,
+                        dtype=torch.int32)
+    out = torch.full((B,), -1, device=cuda, dtype=torch.int32)
+    pb = (ctypes.c_void_p * 1)(pairs.data_ptr())
+    fb = (ctypes.c_void_p * 1)(flags.data_ptr())
+    for _ in range(3):  # the pair buffer alternates by call; the result must not
+        out.fill_(-1)
+        _lib.call("muk_tp_greedy", logits.data_ptr(), V, B, c0, n, rep.data_ptr(), seen.data_ptr(),
+                  words, None, ctypes.addressof(pb), B, ctypes.addressof(fb), 0, 1,
+                  out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        idx = torch.arange(V, device=cuda)
+        bit = ((seen[:, idx >> 5] >> (idx & 31)) & 1).bool()
+        pen = torch.where(bit & (rep[:, None] != 1.0),
+                          torch.where(logits > 0, logits / rep[:, None], logits * rep[:, None]),
+                          logits)[:, c0:c0 + n]
+        ref = pen.argmax(-1) + c0                              # first maximum = lowest index
+        ref[4] = 0
+        assert torch.equal(out.long(), ref), (out, ref)
+    assert _lib.device_error() == 0

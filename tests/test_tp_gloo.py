@@ -504,3 +504,69 @@ def test_ep_combine_bookkeeping_matches_unsharded():
         np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-5)
         assert np.array_equal(e, O.route_experts(ids, mu, p["layers.0.mlp.mu_router.weight"], E, V))
     assert len(np.unique(got[0][1])) > 1   # tokens really spread over both ranks' experts
+
+
+def _greedy_combine_worker(rank, world, port, q):
+    """Each rank holds the columns [r V/P, (r+1) V/P) of the same logits rows;
+    it reduces them to one (value, index) pair per row with the sampler's
+    penalty rule, the pairs are all-gathered and the best pair is taken
+    (largest value, lowest index): muk_tp_greedy's arithmetic."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        B, V = 9, 64
+        rng = np.random.default_rng(5)                      # the same rows on every rank
+        x = rng.standard_normal((B, V)).astype(np.float32)
+        x[1, 3] = x[1, 40] = 9.0                            # a tie across the two slices
+        x[2, 17] = x[2, 21] = 9.0                           # a tie inside one slice
+        x[3] = -np.inf
+        seen = rng.random((B, V)) < 0.3
+        seen[1, [3, 40]] = seen[2, [17, 21]] = False        # keep the planted ties exact
+        rp = np.where(np.arange(B) % 2 == 0, 1.3, 1.0).astype(np.float32)
+        pen = np.where(seen & (rp[:, None] != 1.0),
+                       np.where(x > 0, x / rp[:, None], x * rp[:, None]), x)
+        n = V // world
+        c0 = rank * n
+        loc = pen[:, c0:c0 + n]
+        vals, idxs = [], []
+        for b in range(B):
+            best, bi = -np.inf, 2**31 - 1
+            for i in range(n):                              # first maximum of the slice
+                if loc[b, i] > best:
+                    best, bi = loc[b, i], c0 + i
+            vals.append(best)
+            idxs.append(bi)
+        mine = torch.tensor([vals, idxs], dtype=torch.float64)
+        allp = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allp, mine)
+        out = []
+        for b in range(B):
+            best, bi = -np.inf, 2**31 - 1
+            for p in allp:                                  # rank order = vocabulary order
+                v, i = float(p[0, b]), int(p[1, b])
+                if v > best or (v == best and i < bi):
+                    best, bi = v, i
+            out.append(0 if bi == 2**31 - 1 else bi)
+        ref = [int(np.argmax(pen[b])) if np.isfinite(pen[b]).any() else 0 for b in range(B)]
+        q.put((rank, out == ref and out[1] == 3 and out[2] == 17))
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+
+
+def test_vocab_parallel_greedy_combine():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_greedy_combine_worker, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert got == {0: True, 1: True}, got

@@ -181,6 +181,8 @@ def main():
         w.use_graphs = graphs
         if form.startswith("rs-norm"):
             assert w.model.tp_norm(), "peer-memory TP should take the reduce-scatter + norm path"
+        if comm != "nccl":
+            assert w.model.vocab_slice() is not None, "peer-memory TP: vocabulary-parallel head"
         toks = d["tokens"]
         R, n = toks.shape
         steps = list(d["logit_steps"])
@@ -221,6 +223,27 @@ def main():
         for g in allg:
             if not torch.equal(g, allg[0]):
                 failures.append((name, graphs, rank, "ranks generated different tokens"))
+        # greedy tokens equal the reference's up to its first near tie
+        for r in range(R):
+            for i, t in enumerate(gen[r].tolist()):
+                if t != int(toks[r, i]):
+                    if d["top2_gap"][r, i] > 0.05:
+                        failures.append((name, graphs, rank, f"greedy token r{r} step {i}"))
+                    break
+        # sampled generation (temperature 0.8, top-p 0.9, seeded): the ranks
+        # combine the vocabulary columns before sampling and draw the same tokens
+        for r in range(R):
+            eng.add_request(prompts[r], SamplingParams(temperature=0.8, top_k=0, top_p=0.9,
+                                                       repetition_penalty=1.1, max_tokens=8,
+                                                       seed=1234 + r), f"s{r}")
+        eng.run_to_completion()
+        smp = torch.tensor([eng.requests[f"s{r}"].output_token_ids for r in range(R)],
+                           device="cuda")
+        alls = [torch.empty_like(smp) for _ in range(world)]
+        dist.all_gather(alls, smp)
+        for g in alls:
+            if not torch.equal(g, alls[0]):
+                failures.append((name, graphs, rank, "ranks sampled different tokens"))
         w.close()  # graphs (which may hold NCCL calls) and peer mappings go before the group
         del eng, w
     from mu_b200 import _lib
