@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 #include <stdio.h>
 
 #include "../../include/muk.h"
@@ -62,6 +63,28 @@ int launch_tp_norm_finish(float* const* bufs, float* const* scratch, uint32_t* c
                           int64_t ld_resid, const float* norm_w, float eps, void* const* x_bufs,
                           int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm, float mu,
                           float cmin, float cmax, cudaStream_t stream);
+
+// Kernels are launched as programmatic dependents of the previous kernel on
+// the stream (MUK_PDL=0: fully serialised; 2: GEMMs only).  A kernel launched this way must
+// execute griddepcontrol.wait (grid_dep_wait) before it reads or writes
+// anything an earlier kernel touches.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace muk
 

@@ -71,6 +71,10 @@ __global__ void __launch_bounds__(kDecWarps * 32)
                         const int32_t* __restrict__ seq_lens, int num_q_heads, int num_kv_heads,
                         int num_blocks, float scale_log2, int blocks_per_split, int max_splits,
                         float* __restrict__ part_o, float* __restrict__ part_ml) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   constexpr int kChunks = D / 8;            // 16-byte chunks per row
   constexpr int kTile = kBlockSize * D * 2; // bytes of one K (or V) tile
   constexpr int kKS = D / 16;               // k-slices of QK
@@ -288,6 +292,10 @@ __global__ void decode_merge_kernel(__nv_bfloat16* __restrict__ out, int64_t out
                                     int blocks_per_split, int max_splits,
                                     const float* __restrict__ part_o,
                                     const float* __restrict__ part_ml) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.y, h = blockIdx.x;
   const int ctx = seq_lens[b];
   const int nblk = (ctx + kBlockSize - 1) / kBlockSize;
@@ -324,6 +332,10 @@ __global__ void __launch_bounds__(G * WR * 32)
                          const int32_t* __restrict__ block_tables, int bt_stride,
                          const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ cu_q,
                          int num_q_heads, int num_kv_heads, int num_blocks, float scale_log2) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   constexpr int kChunks = D / 8;
   constexpr int kKS = D / 16;
   constexpr int kDT = D / 8;
@@ -598,7 +610,7 @@ static int launch_decode(const void* q, int64_t q_stride, void* out, int64_t out
     return MUK_ERR_CUDA;
   }
   dim3 grid(p.max_splits, num_kv_heads, num_seqs);
-  paged_decode_kernel<D><<<grid, kDecWarps * 32, smem, stream>>>(
+  launch_pdl(paged_decode_kernel<D>, dim3(grid), dim3(kDecWarps * 32), smem, stream,
       reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<__nv_bfloat16*>(out),
       out_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
       reinterpret_cast<const __nv_bfloat16*>(v_cache), block_tables, bt_stride, seq_lens,
@@ -607,7 +619,7 @@ static int launch_decode(const void* q, int64_t q_stride, void* out, int64_t out
   int rc = check_launch("muk_paged_decode_attn");
   if (rc != MUK_OK || p.max_splits <= 1) return rc;
   dim3 mgrid(num_q_heads, num_seqs);
-  decode_merge_kernel<D><<<mgrid, D >= 128 ? 128 : 64, 0, stream>>>(
+  launch_pdl(decode_merge_kernel<D>, dim3(mgrid), dim3(D >= 128 ? 128 : 64), 0, stream,
       reinterpret_cast<__nv_bfloat16*>(out), out_stride, seq_lens, num_q_heads,
       p.blocks_per_split, p.max_splits, part_o, part_ml);
   return check_launch("muk_paged_decode_attn(merge)");
@@ -661,7 +673,7 @@ static int launch_prefill_g(const void* q, int64_t q_stride, void* out, int64_t 
     return MUK_ERR_CUDA;
   }
   dim3 grid((max_q_len + 16 * WR - 1) / (16 * WR), num_q_heads / G, num_seqs);
-  paged_prefill_kernel<D, G, WR><<<grid, G * WR * 32, smem, stream>>>(
+  launch_pdl(paged_prefill_kernel<D, G, WR>, dim3(grid), dim3(G * WR * 32), smem, stream,
       reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<__nv_bfloat16*>(out),
       out_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
       reinterpret_cast<const __nv_bfloat16*>(v_cache), block_tables, bt_stride, seq_lens, cu_q,

@@ -73,13 +73,17 @@ static bool g_pair_enabled = true;
 // stream (prologue and the first weight tiles overlap its tail); MUK_PDL=0
 // launches them fully serialised.
 static int g_pdl = -1;
-static bool pdl_enabled() {
+static int pdl_mode() {  // 0 none, 1 every kernel, 2 GEMMs only
   if (g_pdl < 0) {
     const char* e = getenv("MUK_PDL");
-    g_pdl = (e && e[0] == '0') ? 0 : 1;
+    g_pdl = (e && (e[0] == '0' || e[0] == '2')) ? e[0] - '0' : 1;
   }
-  return g_pdl != 0;
+  return g_pdl;
 }
+}  // namespace muk
+bool muk::pdl_enabled() { return pdl_mode() == 1; }
+namespace muk {
+static bool gemm_pdl_enabled() { return pdl_mode() != 0; }
 static double g_pair128_cost = [] {
   const char* e = getenv("MUK_GEMM_PAIR128_COST");
   return e ? atof(e) : 0.67;
@@ -1505,7 +1509,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const T
   attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = gemm_pdl_enabled() ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, kern, ma, mb, C, a);
   if (e != cudaSuccess) {
     set_last_error("%s: launch failed: %s", GROUPED ? "muk_grouped_gemm_bf16" : "muk_gemm_bf16",
@@ -1579,7 +1583,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, co
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.numAttrs = gemm_pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, C, a);
   if (e != cudaSuccess) {
     set_last_error("muk_gemm_bf16(pair): launch failed: %s", cudaGetErrorString(e));

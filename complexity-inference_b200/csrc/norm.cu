@@ -60,6 +60,10 @@ __global__ void residual_rmsnorm_kernel(float* __restrict__ resid, const DT* __r
                                         __nv_bfloat16* __restrict__ out, int64_t out_stride,
                                         int hidden, int clamp_delta, int clamp_sum,
                                         ClampParams cp_norm, ClampParams cp) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   extern __shared__ float srow[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -122,6 +126,10 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 4 : (VPT <= 8 ? 2 : 1))
                                 __nv_bfloat16* __restrict__ out, int64_t out_stride, int hidden,
                                 int clamp_delta, int clamp_sum, ClampParams cp_norm,
                                 ClampParams cp) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int src = delta_rows ? delta_rows[t] : t;
@@ -196,6 +204,10 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ resid, const int32
                                     const float* __restrict__ norm_w, float eps,
                                     __nv_bfloat16* __restrict__ out, int64_t out_stride, int hidden,
                                     ClampParams cp) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   __shared__ float red[32];
   const int i = blockIdx.x;
   const float* rrow = resid + (int64_t)rows[i] * hidden;
@@ -212,6 +224,10 @@ __global__ void reduce_clamp_kernel(const float* __restrict__ partials, int64_t 
                                     int num_partials, float* __restrict__ dst,
                                     __nv_bfloat16* __restrict__ dst_bf16, int64_t dst_bf16_stride,
                                     int hidden, int64_t total, ClampParams cp) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
@@ -231,6 +247,10 @@ __global__ void reduce_bias_silu_kernel(const float* __restrict__ partials, int6
                                         int num_partials, const float* __restrict__ bias,
                                         __nv_bfloat16* __restrict__ out, int64_t out_stride,
                                         int cols, int64_t total) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / cols;
@@ -262,6 +282,10 @@ __global__ void inl_dynamics_kernel(const float* __restrict__ h, const float* __
                                     const __nv_bfloat16* __restrict__ router_w, int num_experts,
                                     int vocab, int32_t* __restrict__ expert_ids, int hidden,
                                     ClampParams cp_norm) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   extern __shared__ float srow[];
   __shared__ float red[32];
   __shared__ float dots[kMaxExperts];
@@ -360,6 +384,10 @@ __global__ void __launch_bounds__(256, VPT <= 4 ? 3 : 1)
                             const int32_t* __restrict__ token_ids,
                             const __nv_bfloat16* __restrict__ router_w, int num_experts, int vocab,
                             int32_t* __restrict__ expert_ids, int hidden, ClampParams cp_norm) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   constexpr int NV = 1 + kInlMaxVecExperts;      // squared sum + router dots
   __shared__ float red[32 * NV];
   const int t = blockIdx.x;
@@ -507,7 +535,8 @@ static int launch_residual_rmsnorm(float* resid, const DT* partials, int64_t par
                       (partial_row_stride % 4 == 0) && (out == nullptr || ((uintptr_t)out & 7) == 0);
   cudaStream_t st = as_stream(stream);
 #define MUK_RRN(V, THREADS)                                                                     \
-  residual_rmsnorm_vec_kernel<V, DT><<<num_tokens, THREADS, 0, st>>>(                          \
+  launch_pdl(residual_rmsnorm_vec_kernel<V, DT>,                                                   \
+      dim3(num_tokens), dim3(THREADS), 0, st,                                                      \
       resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps, \
       o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp)
   bool done = false;
@@ -524,7 +553,8 @@ static int launch_residual_rmsnorm(float* resid, const DT* partials, int64_t par
     }
   }
   if (!done)
-    residual_rmsnorm_kernel<DT><<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+    launch_pdl(residual_rmsnorm_kernel<DT>,
+               dim3(num_tokens), dim3(kRowThreads), hidden * sizeof(float), st,
         resid, partials, partial_stride, partial_row_stride, num_partials, delta_rows, norm_w, eps,
         o, out_stride, hidden, clamp_delta, clamp_sum, cpn, cp);
 #undef MUK_RRN
@@ -562,7 +592,7 @@ extern "C" int muk_rmsnorm_rows(const float* resid, const int32_t* rows, int num
   MUK_REQUIRE(resid && rows && norm_w && out && hidden > 0 && out_stride >= hidden,
               "muk_rmsnorm_rows: bad arguments");
   if (num_rows <= 0) return MUK_OK;
-  rmsnorm_rows_kernel<<<num_rows, kRowThreads, 0, as_stream(stream)>>>(
+  launch_pdl(rmsnorm_rows_kernel, dim3(num_rows), dim3(kRowThreads), 0, as_stream(stream),
       resid, rows, norm_w, eps, reinterpret_cast<__nv_bfloat16*>(out), out_stride, hidden,
       make_clamp(clamp, mu, clamp_min, clamp_max));
   return check_launch("muk_rmsnorm_rows");
@@ -579,7 +609,7 @@ extern "C" int muk_reduce_clamp(const float* partials, int64_t partial_stride, i
   if (total == 0) return MUK_OK;
   int blocks = (int)((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  reduce_clamp_kernel<<<blocks, 256, 0, as_stream(stream)>>>(
+  launch_pdl(reduce_clamp_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
       partials, partial_stride, num_partials, dst_f32, reinterpret_cast<__nv_bfloat16*>(dst_bf16),
       dst_bf16_stride, hidden, total, make_clamp(clamp, mu, clamp_min, clamp_max));
   return check_launch("muk_reduce_clamp");
@@ -596,7 +626,7 @@ extern "C" int muk_reduce_bias_silu(const float* partials, int64_t partial_strid
   const int64_t total = (int64_t)rows * cols;
   int blocks = (int)((total + 255) / 256);
   if (blocks > 4 * 148) blocks = 4 * 148;
-  reduce_bias_silu_kernel<<<blocks, 256, 0, as_stream(stream)>>>(
+  launch_pdl(reduce_bias_silu_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
       partials, partial_stride, num_partials, bias, reinterpret_cast<__nv_bfloat16*>(out),
       out_stride, cols, total);
   return check_launch("muk_reduce_bias_silu");
@@ -637,12 +667,13 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
                       (mu_out == nullptr || (mu_out_stride % 4 == 0 && ((uintptr_t)mu_out & 7) == 0)) &&
                       (router_w == nullptr || ((uintptr_t)router_w & 7) == 0);
 #define MUK_INL(V, THREADS)                                                                      \
-  inl_dynamics_vec_kernel<V><<<num_tokens, THREADS, 0, st>>>(                                   \
+  launch_pdl(inl_dynamics_vec_kernel<V>,                                                           \
+      dim3(num_tokens), dim3(THREADS), 0, st,                                                      \
       h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,            \
       mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,        \
       expert_ids, hidden, cpn)
   if (router_w != nullptr && num_experts > kInlMaxVecExperts) {
-    inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+    launch_pdl(inl_dynamics_kernel, dim3(num_tokens), dim3(kRowThreads), hidden * sizeof(float), st,
         h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,
         mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
         expert_ids, hidden, cpn);
@@ -655,7 +686,7 @@ extern "C" int muk_inl_dynamics(const float* h, const float* ctrl_raw, const flo
   } else if (vec_ok && vpt == 4) {
     MUK_INL(4, 256);
   } else {
-    inl_dynamics_kernel<<<num_tokens, kRowThreads, hidden * sizeof(float), st>>>(
+    launch_pdl(inl_dynamics_kernel, dim3(num_tokens), dim3(kRowThreads), hidden * sizeof(float), st,
         h, ctrl_raw, ctrl_bias, muproj, mu_param, dt, v, v_zero, vb, v_bf16_stride, resid, mo,
         mu_out_stride, norm_w, eps, no, norm_out_stride, token_ids, rw, num_experts, vocab,
         expert_ids, hidden, cpn);

@@ -95,6 +95,10 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const TcArgs a) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -480,7 +484,7 @@ int launch_prefill_tc(const void* q, int64_t q_stride, void* out, int64_t out_st
   const int P = kTcRows / a.group;
   a.q_tiles = (max_q_len + P - 1) / P;
   dim3 grid(a.q_tiles, num_kv_heads, num_seqs);
-  prefill_tc_kernel<<<grid, kTcThreads, TcLayout::kBytes, stream>>>(mk, mv, a);
+  launch_pdl(prefill_tc_kernel, dim3(grid), dim3(kTcThreads), TcLayout::kBytes, stream, mk, mv, a);
   return check_launch("muk_paged_prefill_attn(tc)");
 }
 

@@ -20,6 +20,10 @@ __global__ void __launch_bounds__(kRouteThreads)
     route_permute_kernel(const int32_t* __restrict__ expert_ids, int T, int E,
                          int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
                          int32_t* __restrict__ inv_perm) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   __shared__ int hist[kRouteMaxExperts];
   __shared__ int running[kRouteMaxExperts];
   __shared__ int wcount[kRouteThreads / 32][kRouteMaxExperts];
@@ -79,6 +83,10 @@ __global__ void __launch_bounds__(kRouteThreads)
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t src_stride,
                                    const int32_t* __restrict__ rows, __nv_bfloat16* __restrict__ dst,
                                    int64_t dst_stride, int width, int vec) {
+  // programmatic dependent launch: let the next kernel launch once every CTA
+  // of this one runs, and wait for the previous kernel before touching memory
+  grid_dep_launch();
+  grid_dep_wait();
   const int i = blockIdx.x;
   const __nv_bfloat16* s = src + (int64_t)rows[i] * src_stride;
   __nv_bfloat16* d = dst + (int64_t)i * dst_stride;
@@ -121,7 +129,7 @@ extern "C" int muk_route_permute(const int32_t* expert_ids, int num_tokens, int 
               "muk_route_permute: null pointer");
   MUK_REQUIRE(num_experts >= 1 && num_experts <= kRouteMaxExperts && num_tokens >= 0,
               "muk_route_permute: E=%d must be in [1, %d]", num_experts, kRouteMaxExperts);
-  route_permute_kernel<<<1, kRouteThreads, 0, as_stream(stream)>>>(
+  launch_pdl(route_permute_kernel, dim3(1), dim3(kRouteThreads), 0, as_stream(stream),
       expert_ids, num_tokens, num_experts, expert_offsets, perm, inv_perm);
   return check_launch("muk_route_permute");
 }
@@ -136,7 +144,7 @@ extern "C" int muk_gather_rows_bf16(const void* src, int64_t src_stride, const i
                    MUK_ALIGNED16(src) && MUK_ALIGNED16(dst))
                       ? 1
                       : 0;
-  gather_rows_kernel<<<num_rows, 256, 0, as_stream(stream)>>>(
+  launch_pdl(gather_rows_kernel, dim3(num_rows), dim3(256), 0, as_stream(stream),
       reinterpret_cast<const __nv_bfloat16*>(src), src_stride, rows,
       reinterpret_cast<__nv_bfloat16*>(dst), dst_stride, width, vec);
   return check_launch("muk_gather_rows_bf16");
