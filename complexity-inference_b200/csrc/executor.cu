@@ -93,9 +93,8 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
 
   // Sum a row-parallel projection over the tensor-parallel ranks; returns the
   // number of slices the consumer reads.
-  // GEMM + reduce-scatter in one kernel while the step has few rows (see
-  // FUSED_TP_MAX_ROWS in mu_b200/models/base.py: 512)
-  const bool fused_tp = m->tp_world > 1 && m->tp_fused && T <= 512;
+  // GEMM + reduce-scatter in one kernel for steps of up to tp_fused rows
+  const bool fused_tp = m->tp_world > 1 && m->tp_fused > 0 && T <= m->tp_fused;
   auto reduce = [&](int slices) -> int {
     if (m->tp_world == 1) return slices;
     int rc = muk_allreduce_f32(m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world,

@@ -29,7 +29,13 @@ PAD_MULT = 64  # SwiGLU weights are interleaved in 64-row gate/up groups
 # GEMM has few rows (decode steps: 68 vs 79 us at 256 x 4096 x 2048 on 2
 # GPUs); with more rows the epilogue's row-per-lane NVLink stores lose to a
 # local GEMM plus the coalesced push kernel (117 vs 91 us at 1000 rows).
-FUSED_TP_MAX_ROWS = 512
+# Steps of at most this many rows run a row-parallel projection under
+# peer-memory TP as one GEMM whose epilogue pushes rows to their owners
+# (MU_TP_FUSED_MAX_ROWS overrides); larger steps run split-K, then a push
+# kernel.  With the epilogue's stores staged through shared memory (whole
+# 128-byte rows per NVLink store) the fused form wins at every C3 step size
+# (2 GPUs: 16,842 vs 16,316-16,396 tokens/s with a 512-row limit).
+FUSED_TP_MAX_ROWS = int(os.environ.get("MU_TP_FUSED_MAX_ROWS", str(1 << 20)))
 
 
 @dataclass

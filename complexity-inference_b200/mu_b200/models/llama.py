@@ -172,7 +172,7 @@ class LlamaForCausalLM(MuModelBase):
             m.logits = ws.logits.data_ptr() + 4 * c0
         m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
         m.fused_rope = int(self.fused_rope())
-        m.tp_fused = int(self._tp_fused)
+        m.tp_fused = FUSED_TP_MAX_ROWS if self._tp_fused else 0
         m.fused_norm = max(1, self.fused_norm_min_rows) if self.fused_norm() else 0
         m.sumsq = ws.sumsq.data_ptr()
         m.tp_norm = int(self.tp_norm())
@@ -202,10 +202,10 @@ class LlamaForCausalLM(MuModelBase):
         if m.tp_world > 1 and m.tp_norm:
             # q|k|v (+RoPE), attention, 2 x (projection + finish [+ push]), SwiGLU
             per_layer = (1 if m.fused_rope else 2) + attn + 1 + \
-                (4 if (m.tp_fused and T <= 512) else 6)
+                (4 if (m.tp_fused and T <= m.tp_fused) else 6)
             n = 2 + per_layer * m.num_layers + 2
         else:
-            tp = (2 if (m.tp_fused and T <= 512) else 4) if m.tp_world > 1 else 0
+            tp = (2 if (m.tp_fused and T <= m.tp_fused) else 4) if m.tp_world > 1 else 0
             fused = m.fused_norm > 0 and T >= m.fused_norm
             per_layer = (4 if fused else 6 if m.fused_rope else 7) + attn + tp
             n = 4 + per_layer * m.num_layers

@@ -596,7 +596,8 @@ typedef struct {
   float* ar_scratch[8];
   uint32_t* ar_flags[8];
   int fused_rope; /* 1: RoPE + KV append in the q|k|v GEMM epilogue (muk_gemm_qkv_rope) */
-  int tp_fused;   /* 1: O / down projections as muk_gemm_allreduce_f32 under TP */
+  int tp_fused;   /* > 0: under TP, steps of at most this many rows run the O / down
+                     projections with the row push in the GEMM epilogue */
   int fused_norm; /* > 0: steps of at least this many tokens split residual + RMSNorm across
                      the GEMMs (muk_gemm_residual_norm and the _rownorm consumers; needs
                      tp_world 1, clamp 0, hidden % 128 == 0, fused_rope); smaller steps keep
