@@ -12,7 +12,7 @@
 // (r / G, r % G)), so every K/V byte staged serves the whole group.  Keys are
 // walked in tiles of 128 (eight 16-token paged blocks).
 //
-// Warp roles (6 warps):
+// Warp roles (10 warps):
 //   warp 0    TMA producer: K_0, V_0, K_1, V_1, ... each 16 two-kilobyte
 //             boxes (8 blocks x 2 column panels) from the layer's pool into a
 //             5-slot ring, 128-byte swizzled, completion on the slot's
@@ -23,9 +23,14 @@
 //               O   += P_j · V_j   (A = P from shared memory, B = V MN-major)
 //             issued as S_0, S_1, [P_0] O_0, S_2, [P_1] O_1, ... so the tensor
 //             core computes S_{j+1} while the softmax warps work on S_j.
-//   warps 2-5 softmax, one query row per thread (its TMEM lane): read S_j,
-//             mask, online softmax in the log2 domain, P_j as bf16 into shared
-//             memory for the second MMA, final O / l to global.
+//   warps 2-9 softmax, two threads per query row (its TMEM lane; warps w and
+//             w + 4 share lane quarter w % 4 and take key columns 0-63 and
+//             64-127 of each tile): read S_j, mask, online softmax in the log2
+//             domain (the two halves agree on the row max through shared memory
+//             and a 64-thread named barrier), P_j as bf16 into its shared-memory
+//             panel for the second MMA, final O / l to global.  One softmax
+//             warp per SM sub-partition spent ~3x the tile's MMA time on the
+//             128 exponentials of its row; split in two it overlaps them.
 // TMEM: two S buffers (columns 0-127, 128-255) and O (256-383) of 512.
 //
 // Online softmax with lazy rescaling: the running max m used for the
@@ -50,7 +55,7 @@ constexpr int kTcRows = 128;        // query rows per CTA
 constexpr int kTcKeys = 128;        // keys per tile
 constexpr int kTcBlk = 16;          // tokens per paged block
 constexpr int kTcSlots = 5;         // ring of K / V tiles (K_0 V_0 K_1 V_1 ...)
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;
 constexpr int kTcPanel = 128 * 128;  // [128 rows][64 bf16] = 16 KB, one swizzled column panel
 
 struct TcLayout {
@@ -59,7 +64,8 @@ struct TcLayout {
   static constexpr int kKV = kP + 2 * kTcPanel;         // slot s: one K or V tile (2 panels)
   static constexpr int kSlot = 2 * kTcPanel;
   static constexpr int kBar = kKV + kTcSlots * kSlot;
-  static constexpr int kBytes = kBar + 192 + 1024;      // barriers + slot, 1024-B alignment slack
+  static constexpr int kRed = kBar + 256;               // [2 halves][128 rows] f32 row max / sum
+  static constexpr int kBytes = kRed + 1024 + 1024;     // + 1024-B alignment slack
 };
 static_assert(TcLayout::kBytes <= 232448, "prefill tile exceeds 227 KB of shared memory");
 
@@ -82,6 +88,23 @@ struct TcArgs {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int code) {
   const bool ok = mbar_wait(bar, parity, code);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Named barrier of the two softmax warps sharing a TMEM lane quarter (ids
+// 1-4; 0 is __syncthreads), and its AND-reduction over both warps' flags so
+// that both leave a loop together.
+__device__ __forceinline__ void pair_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ bool pair_all(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id)
+      : "memory");
+  return r != 0;
 }
 
 // 2^x with one MUFU op (PTX ex2.approx, ~2 ulp); the probabilities are rounded
@@ -140,8 +163,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(q_full, 4);
-    mbar_init(p_full, 4);
+    mbar_init(q_full, 8);
+    mbar_init(p_full, 8);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -260,8 +283,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---- softmax / epilogue: one query row per thread ------------------------
+    // ---- softmax / epilogue: two threads per query row -------------------------
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
+    const int hf = warp >= 6 ? 1 : 0;             // key / output columns 64*hf .. +63
+    const int bid = 1 + quarter;                  // named barrier of this warp pair
     const int r = quarter * 32 + lane;            // query row of this thread
     const int pos = p0 + r / G;                   // query index within the sequence
     const int h = kvh * G + r % G;
@@ -269,15 +294,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int limit = past + pos;                 // last key this row may see
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const uint32_t swz = (uint32_t)(r & 7);
-    // Q row -> shared memory (swizzled, zeros for rows past the sequence)
+    float* red = reinterpret_cast<float*>(basep + TcLayout::kRed);  // [2][128]
+    // this half of the Q row -> its panel (swizzled, zeros for rows past the sequence)
     {
       const uint4* src = reinterpret_cast<const uint4*>(
           a.q + (int64_t)(q_begin + (row_ok ? pos : 0)) * a.q_stride + (int64_t)h * kTcD);
-      uint8_t* qrow = basep + TcLayout::kQ + r * 128;
+      uint8_t* qrow = basep + TcLayout::kQ + hf * kTcPanel + r * 128;
 #pragma unroll
-      for (int c = 0; c < kTcD / 8; ++c) {
-        const uint4 v = row_ok ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(qrow + (c >> 3) * kTcPanel + (((uint32_t)(c & 7) ^ swz) << 4)) = v;
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = row_ok ? src[hf * 8 + c] : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(qrow + (((uint32_t)c ^ swz) << 4)) = v;
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -287,31 +313,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int t = 0; t < nt; ++t) {
-      if (!warp_wait(&s_full[t & 1], (t >> 1) & 1u, kDevTimeoutAccum)) {
-        ok = false;
-        break;
-      }
+      ok = pair_all(bid, warp_wait(&s_full[t & 1], (t >> 1) & 1u, kDevTimeoutAccum));
+      if (!ok) break;
       tc_fence_after();
-      // raw scores of this row: four 32-column loads, one wait
-      float sv[kTcKeys];
+      // this half's raw scores: two 32-column loads, one wait
+      float sv[64];
       {
-        uint32_t (&r4)[4][32] = *reinterpret_cast<uint32_t(*)[4][32]>(sv);
-        const uint32_t ta = lane_base + (uint32_t)((t & 1) * kTcKeys);
+        uint32_t (&r4)[2][32] = *reinterpret_cast<uint32_t(*)[2][32]>(sv);
+        const uint32_t ta = lane_base + (uint32_t)((t & 1) * kTcKeys + hf * 64);
         tmem_ld_32x32b_x32(ta, r4[0]);
         tmem_ld_32x32b_x32(ta + 32, r4[1]);
-        tmem_ld_32x32b_x32(ta + 64, r4[2]);
-        tmem_ld_32x32b_x32(ta + 96, r4[3]);
         tmem_ld_wait();
       }
-      const int k0 = t * kTcKeys;
-      if (k0 + kTcKeys - 1 > row_min_limit) {     // the tile reaches past some row's limit
+      const int k0 = t * kTcKeys + hf * 64;
+      if (k0 + 63 > row_min_limit) {              // the half-tile reaches past some row's limit
 #pragma unroll
-        for (int i = 0; i < kTcKeys; ++i)
+        for (int i = 0; i < 64; ++i)
           if (k0 + i > limit) sv[i] = -INFINITY;
       }
-      float mraw = -INFINITY;
+      float mh = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kTcKeys; ++i) mraw = fmaxf(mraw, sv[i]);
+      for (int i = 0; i < 64; ++i) mh = fmaxf(mh, sv[i]);
+      red[hf * kTcRows + r] = mh;                 // the row max of both halves
+      pair_sync(bid);
+      const float mraw = fmaxf(red[r], red[kTcRows + r]);
       const float mt = mraw * a.scale_log2;       // scale > 0: max commutes with it
       float corr = 1.f;
       if (mt > m_used + 8.f) {                    // also true on the first unmasked tile
@@ -321,24 +346,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float mu = m_used == -INFINITY ? 0.f : m_used;
       float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < kTcKeys; ++i) {
+      for (int i = 0; i < 64; ++i) {
         sv[i] = fast_exp2(fmaf(sv[i], a.scale_log2, -mu));
         sum += sv[i];
       }
-      l = l * corr + sum;
+      l = l * corr + sum;                         // this half's part of the row sum
       // P_t may only overwrite P_{t-1} once O += P_{t-1} V_{t-1} has run, and
       // a rescale must see that O too
       if (t > 0) {
-        if (!warp_wait(o_done, (t - 1) & 1u, kDevTimeoutAccum)) {
-          ok = false;
-          break;
-        }
+        ok = pair_all(bid, warp_wait(o_done, (t - 1) & 1u, kDevTimeoutAccum));
+        if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, corr != 1.f)) {
+        if (__any_sync(0xffffffffu, corr != 1.f)) {  // this half's 64 O columns
           uint32_t rr[32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t ta = lane_base + (uint32_t)(2 * kTcKeys + c * 32);
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t ta = lane_base + (uint32_t)(2 * kTcKeys + hf * 64 + c * 32);
             tmem_ld_32x32b_x32(ta, rr);
             tmem_ld_wait();
 #pragma unroll
@@ -348,30 +371,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tmem_st_wait();
         }
       }
-      uint8_t* prow = basep + TcLayout::kP + r * 128;
+      uint8_t* prow = basep + TcLayout::kP + hf * kTcPanel + r * 128;
 #pragma unroll
-      for (int c = 0; c < kTcKeys / 8; ++c) {
+      for (int c = 0; c < 8; ++c) {
         uint4 v;
         v.x = pack_bf16x2(sv[c * 8 + 0], sv[c * 8 + 1]);
         v.y = pack_bf16x2(sv[c * 8 + 2], sv[c * 8 + 3]);
         v.z = pack_bf16x2(sv[c * 8 + 4], sv[c * 8 + 5]);
         v.w = pack_bf16x2(sv[c * 8 + 6], sv[c * 8 + 7]);
-        *reinterpret_cast<uint4*>(prow + (c >> 3) * kTcPanel + (((uint32_t)(c & 7) ^ swz) << 4)) = v;
+        *reinterpret_cast<uint4*>(prow + (((uint32_t)c ^ swz) << 4)) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && warp_wait(o_done, (nt - 1) & 1u, kDevTimeoutAccum)) {
+    if (ok) ok = pair_all(bid, warp_wait(o_done, (nt - 1) & 1u, kDevTimeoutAccum));
+    if (ok) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      // the two halves' row sums (the max exchange is over: red is free again)
+      pair_sync(bid);
+      red[hf * kTcRows + r] = l;
+      pair_sync(bid);
+      const float lt = red[r] + red[kTcRows + r];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(
           a.out + (int64_t)(q_begin + (row_ok ? pos : 0)) * a.out_stride + (int64_t)h * kTcD);
       uint32_t rr[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(2 * kTcKeys + c * 32), rr);
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)(2 * kTcKeys + hf * 64 + c * 32), rr);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
@@ -381,7 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             v.y = pack_bf16x2(__uint_as_float(rr[j * 8 + 2]) * inv, __uint_as_float(rr[j * 8 + 3]) * inv);
             v.z = pack_bf16x2(__uint_as_float(rr[j * 8 + 4]) * inv, __uint_as_float(rr[j * 8 + 5]) * inv);
             v.w = pack_bf16x2(__uint_as_float(rr[j * 8 + 6]) * inv, __uint_as_float(rr[j * 8 + 7]) * inv);
-            dst[c * 4 + j] = v;
+            dst[hf * 8 + c * 4 + j] = v;
           }
         }
       }
