@@ -59,7 +59,8 @@ int launch_allreduce_finish(float* const* bufs, float* const* scratch, uint32_t*
 // bf16 rows into every rank's x buffer; ends with the "done" barrier.
 int launch_tp_norm_finish(float* const* bufs, float* const* scratch, uint32_t* const* flags,
                           int rank, int world, int T, int H, int share_rows, int slices,
-                          int64_t slice_stride, bool own_in_scratch, float* resid,
+                          int64_t slice_stride, bool own_in_scratch, bool scratch_bf16,
+                          float* resid,
                           int64_t ld_resid, const float* norm_w, float eps, void* const* x_bufs,
                           int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm, float mu,
                           float cmin, float cmax, cudaStream_t stream);

@@ -202,6 +202,7 @@ struct TpNormArgs {
   int64_t ldx8;  // row stride of x in 16-byte units
   int clamp_delta, clamp_sum;
   ClampParams cp, cp_norm;
+  int scratch_bf16;  // the pushed rows are bf16 (uint2 = 4 values per float4 slot)
 };
 
 constexpr int kTpNormThreads = 256;
@@ -231,8 +232,16 @@ __global__ void __launch_bounds__(kTpNormThreads) tp_norm_finish_kernel(const Tp
 #pragma unroll
         for (int s = 0; s < kMaxRanks; ++s)
           if (s < ar.world) {
-            const float4 v = (s == ar.rank && !ar.own_in_scratch) ? folded(ar, own, i)
-                                                                   : scr[(int64_t)s * ar.share + k];
+            float4 v;
+            if (s == ar.rank && !ar.own_in_scratch) {
+              v = folded(ar, own, i);
+            } else if (a.scratch_bf16) {
+              const uint2 q = reinterpret_cast<const uint2*>(scr)[(int64_t)s * ar.share + k];
+              const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
+              v = make_float4(lo.x, lo.y, hi.x, hi.y);
+            } else {
+              v = scr[(int64_t)s * ar.share + k];
+            }
             d.x += v.x;
             d.y += v.y;
             d.z += v.z;
@@ -278,6 +287,111 @@ __global__ void __launch_bounds__(kTpNormThreads) tp_norm_finish_kernel(const Tp
 #pragma unroll
         for (int s = 0; s < kMaxRanks; ++s)
           if (s < ar.world) a.x[s][(int64_t)row * a.ldx8 + j] = pk;
+      }
+    }
+  }
+  if (last_cta(my + kFlagArrive2)) {
+    for (int s = 0; s < ar.world; ++s) st_release_sys(ar.flags[s] + kFlagB + ar.rank, epoch);
+    wait_all(my, kFlagB, ar.world, epoch);
+    *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) = epoch;
+  }
+}
+
+// The same finish with each row in registers (VPT float4 per thread, H =
+// 1024 VPT): every load of a row is issued before the first use and the
+// normalised row is written from registers, where the loop above serialises
+// load, store and the re-read of the residual.  Same sums in the same order.
+// 2 GPUs, projection + exchange at 1,000 rows: 68.3 -> 64.5 us; 2,000 rows:
+// 99.4 -> 90.1 us.
+template <int VPT>
+__global__ void __launch_bounds__(kTpNormThreads) tp_norm_finish_vec_kernel(const TpNormArgs a) {
+  const ArArgs& ar = a.ar;
+  uint32_t* my = ar.flags[ar.rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my + kFlagEpoch) + 1u;
+  __shared__ int ok;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) ok = wait_all(my, kFlagA, ar.world, epoch);
+  __syncthreads();
+  if (ok) {
+    const int row0 = ar.rank * a.share_rows;
+    const int rows = min(a.T, row0 + a.share_rows) - row0;
+    const int h4 = a.H >> 2;
+    const float4* own = ar.data[ar.rank];
+    const float4* scr = ar.scratch[ar.rank];
+    const float4* w4 = reinterpret_cast<const float4*>(a.w);
+    for (int rl = blockIdx.x; rl < rows; rl += gridDim.x) {
+      const int row = row0 + rl;
+      float4* rrow = reinterpret_cast<float4*>(a.resid + (int64_t)row * a.ld_resid);
+      float4 d[VPT], r[VPT];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        d[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        r[v] = rrow[threadIdx.x + v * kTpNormThreads];
+      }
+      for (int s = 0; s < ar.world; ++s) {  // rank order: the all-reduce's sum
+        float4 t[VPT];
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int j = threadIdx.x + v * kTpNormThreads;
+          const int64_t k = (int64_t)rl * h4 + j;
+          if (s == ar.rank && !ar.own_in_scratch) {
+            t[v] = folded(ar, own, (int64_t)row * h4 + j);
+          } else if (a.scratch_bf16) {
+            const uint2 q = reinterpret_cast<const uint2*>(scr)[(int64_t)s * ar.share + k];
+            const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
+            t[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
+          } else {
+            t[v] = scr[(int64_t)s * ar.share + k];
+          }
+        }
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          d[v].x += t[v].x;
+          d[v].y += t[v].y;
+          d[v].z += t[v].z;
+          d[v].w += t[v].w;
+        }
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        float4 q = d[v];
+        if (a.clamp_delta) {
+          q.x = mu_clamp(q.x, a.cp);
+          q.y = mu_clamp(q.y, a.cp);
+          q.z = mu_clamp(q.z, a.cp);
+          q.w = mu_clamp(q.w, a.cp);
+        }
+        float4 o = r[v];
+        o.x += q.x;
+        o.y += q.y;
+        o.z += q.z;
+        o.w += q.w;
+        if (a.clamp_sum) {
+          o.x = mu_clamp(o.x, a.cp);
+          o.y = mu_clamp(o.y, a.cp);
+          o.z = mu_clamp(o.z, a.cp);
+          o.w = mu_clamp(o.w, a.cp);
+        }
+        r[v] = o;
+        rrow[threadIdx.x + v * kTpNormThreads] = o;
+        ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+      }
+      if (a.w == nullptr) continue;
+      const float inv = rsqrtf(block_sum(ss, red) / (float)a.H + a.eps);
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int j = threadIdx.x + v * kTpNormThreads;
+        const float4 w = w4[j];
+        uint2 pk;
+        pk.x = pack_bf16x2(mu_clamp(w.x * (r[v].x * inv), a.cp_norm),
+                           mu_clamp(w.y * (r[v].y * inv), a.cp_norm));
+        pk.y = pack_bf16x2(mu_clamp(w.z * (r[v].z * inv), a.cp_norm),
+                           mu_clamp(w.w * (r[v].w * inv), a.cp_norm));
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+          if (s < ar.world)
+            reinterpret_cast<uint2*>(a.x[s])[(int64_t)row * (a.ldx8 * 2) + j] = pk;
       }
     }
   }
@@ -579,13 +693,16 @@ int launch_allreduce_finish(float* const* bufs, float* const* scratch, uint32_t*
   a.own_in_scratch = own_in_scratch ? 1 : 0;
   int grid = (int)((a.share + kArThreads - 1) / kArThreads);
   grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
-  allreduce_finish_kernel<<<grid, kArThreads, 0, stream>>>(a);
+  // after the push GEMM: synchronised by the "pushed" flags alone (see
+  // launch_tp_norm_finish)
+  launch_pdl(allreduce_finish_kernel, dim3(grid), dim3(kArThreads), 0, stream, a);
   return check_launch("allreduce finish");
 }
 
 int launch_tp_norm_finish(float* const* bufs, float* const* scratch, uint32_t* const* flags,
                           int rank, int world, int T, int H, int share_rows, int slices,
-                          int64_t slice_stride, bool own_in_scratch, float* resid,
+                          int64_t slice_stride, bool own_in_scratch, bool scratch_bf16,
+                          float* resid,
                           int64_t ld_resid, const float* norm_w, float eps, void* const* x_bufs,
                           int64_t ldx, int clamp_delta, int clamp_sum, int clamp_norm, float mu,
                           float cmin, float cmax, cudaStream_t stream) {
@@ -615,8 +732,35 @@ int launch_tp_norm_finish(float* const* bufs, float* const* scratch, uint32_t* c
   a.clamp_sum = clamp_sum;
   a.cp = make_clamp(clamp_delta || clamp_sum, mu, cmin, cmax);
   a.cp_norm = make_clamp(clamp_norm, mu, cmin, cmax);
-  int grid = share_rows < 1 ? 1 : (share_rows > 1184 ? 1184 : share_rows);
-  tp_norm_finish_kernel<<<grid, kTpNormThreads, 0, stream>>>(a);
+  a.scratch_bf16 = scratch_bf16 ? 1 : 0;
+  // two CTAs per SM, each looping over rows: fewer CTAs polling the peers'
+  // flags and counting arrivals than one CTA per row (measured 82 -> 69 us
+  // per exchange at 1,000 rows on 2 GPUs).
+  int grid = share_rows < 1 ? 1 : (share_rows > 296 ? 296 : share_rows);
+  // A programmatic dependent of the push (GEMM or push kernel) without
+  // griddepcontrol.wait: everything it reads from this call (every rank's
+  // pushed rows, this rank's included) is released by the "pushed" flags it
+  // waits for; the residual rows it updates were last written by the
+  // previous exchange's finish, which completed before this layer's first
+  // GEMM launched (a plain launch is never a programmatic primary).  Its
+  // small CTAs sit beside the GEMM's and start as soon as the rows are in.
+  const int vpt = (H % (4 * kTpNormThreads) == 0) ? H / (4 * kTpNormThreads) : 0;
+  switch (vpt) {
+    case 1:
+      launch_pdl(tp_norm_finish_vec_kernel<1>, dim3(grid), dim3(kTpNormThreads), 0, stream, a);
+      break;
+    case 2:
+      launch_pdl(tp_norm_finish_vec_kernel<2>, dim3(grid), dim3(kTpNormThreads), 0, stream, a);
+      break;
+    case 4:
+      launch_pdl(tp_norm_finish_vec_kernel<4>, dim3(grid), dim3(kTpNormThreads), 0, stream, a);
+      break;
+    case 8:
+      launch_pdl(tp_norm_finish_vec_kernel<8>, dim3(grid), dim3(kTpNormThreads), 0, stream, a);
+      break;
+    default:
+      launch_pdl(tp_norm_finish_kernel, dim3(grid), dim3(kTpNormThreads), 0, stream, a);
+  }
   return check_launch("tp residual norm (finish)");
 }
 
@@ -807,7 +951,7 @@ extern "C" int muk_tp_residual_norm(float* const* bufs, float* const* scratch,
     if (rc) return rc;
   }
   return launch_tp_norm_finish(bufs, scratch, flags, rank, world, T, H, share_rows, slices,
-                               slice_stride, false, resid, H, norm_w, eps, x_bufs, ldx,
+                               slice_stride, false, false, resid, H, norm_w, eps, x_bufs, ldx,
                                clamp_delta, clamp_sum, clamp_norm, mu, cmin, cmax, st);
 }
 

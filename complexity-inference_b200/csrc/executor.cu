@@ -162,7 +162,7 @@ extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, 
         return muk_gemm_tp_residual_norm(A, lda, W, K, T, H, K, m->ar_data, m->ar_scratch,
                                          m->ar_flags, m->tp_rank, m->tp_world, m->resid, norm_w,
                                          m->eps, m->x_peer, m->x_stride, cl, clamp_sum, cl, mu,
-                                         cmin, cmax, stream);
+                                         cmin, cmax, m->tp_push_bf16, stream);
       const int s = choose_split(T, H, K, m->part_rows);
       MUK_TRY(muk_gemm_bf16(A, lda, W, K, m->part, H, T, H, K, kEpiF32, s, nullptr, stream));
       return muk_tp_residual_norm(m->ar_data, m->ar_scratch, m->ar_flags, m->tp_rank, m->tp_world,

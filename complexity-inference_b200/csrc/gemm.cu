@@ -126,6 +126,7 @@ struct PushArgs {
   float* scratch[kArMaxRanks];
   uint32_t* flags[kArMaxRanks];
   int rank, world, share_rows;
+  int bf16;  // store the rows as bf16 (same element offsets, half the bytes)
 };
 
 // RMSNorm split across two GEMMs (dense, one GPU, no mu_clamp on the norm):
@@ -269,8 +270,12 @@ __device__ __forceinline__ void store_push(const TileArgs& a, int row, int row_e
     if (r >= row_end) break;
     const int owner = r / p.share_rows;
     const int rr = r - owner * p.share_rows;
-    float* dst = p.scratch[owner] + ((int64_t)p.rank * p.share_rows + rr) * a.ldc + cx;
-    put4_f32(dst, pc[i], cx, a.N, (a.ldc & 3) == 0);
+    const int64_t off = ((int64_t)p.rank * p.share_rows + rr) * a.ldc + cx;
+    if (p.bf16)
+      put4_bf16(reinterpret_cast<__nv_bfloat16*>(p.scratch[owner]) + off, pc[i], cx, a.N,
+                (a.ldc & 3) == 0);
+    else
+      put4_f32(p.scratch[owner] + off, pc[i], cx, a.N, (a.ldc & 3) == 0);
   }
 }
 
@@ -2008,6 +2013,7 @@ extern "C" int muk_gemm_allreduce_f32(const void* A, int64_t lda, const void* B,
   p.rank = rank;
   p.world = world;
   p.share_rows = (M + world - 1) / world;
+  p.bf16 = 0;
   cudaStream_t st = as_stream(stream);
   int rc = run_gemm(false, A, lda, B, ldb, bufs[rank], N, M, N, K, kEpiF32Push, 1, nullptr,
                     nullptr, 0, (M + kBM - 1) / kBM, st, nullptr, &p);
@@ -2022,7 +2028,7 @@ extern "C" int muk_gemm_tp_residual_norm(const void* A, int64_t lda, const void*
                                          int world, float* resid, const float* norm_w, float eps,
                                          void* const* x_bufs, int64_t ldx, int clamp_delta,
                                          int clamp_sum, int clamp_norm, float mu, float cmin,
-                                         float cmax, void* stream) {
+                                         float cmax, int push_bf16, void* stream) {
   MUK_REQUIRE(A && B && bufs && scratch && flags && world >= 1 && world <= kArMaxRanks &&
                   rank >= 0 && rank < world,
               "muk_gemm_tp_residual_norm: rank %d of %d", rank, world);
@@ -2048,11 +2054,12 @@ extern "C" int muk_gemm_tp_residual_norm(const void* A, int64_t lda, const void*
   p.rank = rank;
   p.world = world;
   p.share_rows = (M + world - 1) / world;
+  p.bf16 = push_bf16 ? 1 : 0;
   cudaStream_t st = as_stream(stream);
   int rc = run_gemm(false, A, lda, B, ldb, bufs[rank], N, M, N, K, kEpiF32Push, 1, nullptr,
                     nullptr, 0, (M + kBM - 1) / kBM, st, nullptr, &p);
   if (rc) return rc;
   return launch_tp_norm_finish(bufs, scratch, flags, rank, world, M, N, p.share_rows, 1, 0, true,
-                               resid, N, norm_w, eps, x_bufs, ldx, clamp_delta, clamp_sum,
-                               clamp_norm, mu, cmin, cmax, st);
+                               p.bf16 != 0, resid, N, norm_w, eps, x_bufs, ldx, clamp_delta,
+                               clamp_sum, clamp_norm, mu, cmin, cmax, st);
 }

@@ -87,7 +87,7 @@ SIGNATURES = {
                                      c_float, c_float, _P]),
     "muk_gemm_tp_residual_norm": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P,
                                           _P, c_int, c_int, _P, _P, c_float, _P, c_int64, c_int,
-                                          c_int, c_int, c_float, c_float, c_float, _P]),
+                                          c_int, c_int, c_float, c_float, c_float, c_int, _P]),
     "muk_tp_allgather_cols": (c_int, [_P, _P, c_int, c_int, c_int, c_int64, c_int, c_int, _P]),
     "muk_tp_greedy": (c_int, [_P, c_int64, c_int, c_int, c_int, _P, _P, c_int64, _P, _P, c_int,
                               _P, c_int, c_int, _P, _P]),
@@ -141,7 +141,7 @@ class MukLlamaModel(ctypes.Structure):
                 ("ar_scratch", c_void_p * 8), ("ar_flags", c_void_p * 8), ("fused_rope", c_int),
                 ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p),
                 ("tp_norm", c_int), ("x_peer", c_void_p * 8), ("lm_rows", c_int),
-                ("logits_ld", c_int64)]
+                ("logits_ld", c_int64), ("tp_push_bf16", c_int)]
 
 
 class MukStepBatch(ctypes.Structure):

@@ -176,6 +176,7 @@ class LlamaForCausalLM(MuModelBase):
         m.fused_norm = max(1, self.fused_norm_min_rows) if self.fused_norm() else 0
         m.sumsq = ws.sumsq.data_ptr()
         m.tp_norm = int(self.tp_norm())
+        m.tp_push_bf16 = int(self.comm.push_bf16) if self.comm is not None else 0
         m.tp_world, m.tp_rank = 1, 0
         if self.comm is not None:
             c = self.comm

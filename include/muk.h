@@ -536,15 +536,16 @@ int muk_tp_residual_norm(float* const* bufs, float* const* scratch, uint32_t* co
                          float cmin, float cmax, void* stream);
 
 /* The same with the projection GEMM (A [M][K] · B [N][K]ᵀ, this rank's
- * K-slice) in front: its epilogue stores each f32 output row straight into
- * the owner rank's scratch (muk_gemm_allreduce_f32's push), then the finish
- * above. */
+ * K-slice) in front: its epilogue stores each output row straight into the
+ * owner rank's scratch (muk_gemm_allreduce_f32's push), then the finish
+ * above.  push_bf16: the pushed rows are rounded to bf16 (half the NVLink
+ * bytes; the sum over the ranks stays f32), else f32. */
 int muk_gemm_tp_residual_norm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
                               int K, float* const* bufs, float* const* scratch,
                               uint32_t* const* flags, int rank, int world, float* resid,
                               const float* norm_w, float eps, void* const* x_bufs, int64_t ldx,
                               int clamp_delta, int clamp_sum, int clamp_norm, float mu, float cmin,
-                              float cmax, void* stream);
+                              float cmax, int push_bf16, void* stream);
 
 /* ---- Native step executor (dense Llama family) ----------------------------- */
 
@@ -608,6 +609,7 @@ typedef struct {
   void* x_peer[8]; /* every rank's x buffer as mapped here (tp_norm) */
   int lm_rows;      /* rows of lm_head computed here (vocab, or this rank's vocabulary slice) */
   int64_t logits_ld; /* row stride of logits (vocab unless the slice sits in a wider buffer) */
+  int tp_push_bf16; /* tp_norm: the projection rows travel to their owners as bf16 */
 } MukLlamaModel;
 
 /* The packed step (StepPacker layout; device pointers). */
