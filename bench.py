@@ -881,7 +881,7 @@ def run_micro(args):
     elif args.micro == "grouped_gemm":
         # a Deep step's expert gate|up GEMM (SwiGLU epilogue): T rows spread evenly over
         # E experts, per-expert width args.n (gate + up), K = args.k
-        T, E, N2, Kd = args.m, 8, args.n, args.k
+        T, E, N2, Kd = args.m, args.experts, args.n, args.k
         counts = [T // E + (1 if e < T % E else 0) for e in range(E)]
         offs = torch.tensor(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32),
                             device="cuda")
@@ -967,6 +967,7 @@ def main():
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--experts", type=int, default=8, help="grouped_gemm micro: experts")
     ap.add_argument("--prompts", default="600", help="prefill_attn micro: comma-separated prompt lengths")
     ap.add_argument("--streamk", type=int, choices=[0, 1, 2], default=None,
                     help="GEMM micro cases: stream-K planning mode (0 off, 1 on, 2 auto)")

@@ -87,7 +87,22 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Split-K factor for an f32-output projection, bounded by the rows of the
+// partial buffer (same rule as mu_b200.models.base.choose_split).
+inline int choose_split(int M, int N, int K, int64_t max_rows) {
+  int64_t s = max_rows / (M > 0 ? M : 1);
+  if (s > 16) s = 16;
+  if (s < 1) s = 1;
+  return muk_gemm_plan_split(M, N, K, MUK_EPI_F32, (int)s);
+}
+
 }  // namespace muk
+
+#define MUK_TRY(expr)              \
+  do {                             \
+    int rc_ = (expr);              \
+    if (rc_ != MUK_OK) return rc_; \
+  } while (0)
 
 #define MUK_REQUIRE(cond, ...)            \
   do {                                    \

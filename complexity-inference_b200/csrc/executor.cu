@@ -23,21 +23,6 @@ constexpr int kEpiBf16 = MUK_EPI_BF16;
 constexpr int kEpiF32 = MUK_EPI_F32;
 constexpr int kEpiSwiglu = MUK_EPI_SWIGLU;
 
-// Split-K factor for an f32-output projection, bounded by the rows of the
-// partial buffer (same rule as mu_b200.models.base.choose_split).
-int choose_split(int M, int N, int K, int64_t max_rows) {
-  int64_t s = max_rows / (M > 0 ? M : 1);
-  if (s > 16) s = 16;
-  if (s < 1) s = 1;
-  return muk_gemm_plan_split(M, N, K, kEpiF32, (int)s);
-}
-
-#define MUK_TRY(expr)         \
-  do {                        \
-    int rc_ = (expr);         \
-    if (rc_ != MUK_OK) return rc_; \
-  } while (0)
-
 }  // namespace
 
 extern "C" int muk_llama_forward(const MukLlamaModel* m, const MukStepBatch* b, void* stream) {

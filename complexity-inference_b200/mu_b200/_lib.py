@@ -93,6 +93,7 @@ SIGNATURES = {
                               _P, c_int, c_int, _P, _P]),
     "muk_ep_gather_bf16": (c_int, [_P, _P, c_int, c_int, _P, c_int, c_int, c_int, _P]),
     "muk_llama_forward": (c_int, [_P, _P, _P]),
+    "muk_deep_forward": (c_int, [_P, _P, _P, _P]),
     "muk_gemm_allreduce_scratch_elems": (c_int64, [c_int, c_int, c_int]),
     "muk_gemm_allreduce_f32": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, _P, _P,
                                        c_int, c_int, _P]),
@@ -142,6 +143,35 @@ class MukLlamaModel(ctypes.Structure):
                 ("tp_fused", c_int), ("fused_norm", c_int), ("sumsq", c_void_p),
                 ("tp_norm", c_int), ("x_peer", c_void_p * 8), ("lm_rows", c_int),
                 ("logits_ld", c_int64), ("tp_push_bf16", c_int)]
+
+
+class MukDeepLayer(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("in_norm", "wcat", "wo", "post_norm", "wci", "bci", "wco",
+                                        "bco", "wmu", "mu_param", "q_norm", "k_norm", "wgu", "wd",
+                                        "router")]
+
+
+class MukDeepModel(ctypes.Structure):
+    _fields_ = [("num_layers", c_int), ("hidden", c_int), ("num_q_heads", c_int),
+                ("num_kv_heads", c_int), ("head_dim", c_int), ("inter_pad", c_int),
+                ("vocab", c_int), ("ctrl_hidden", c_int), ("num_experts", c_int),
+                ("local_experts", c_int), ("expert_lo", c_int), ("ep_gather", c_int),
+                ("eps", c_float), ("dt", c_float), ("clamp", c_int), ("mu", c_float),
+                ("clamp_min", c_float), ("clamp_max", c_float),
+                ("layers", ctypes.POINTER(MukDeepLayer)), ("embed", c_void_p),
+                ("final_norm", c_void_p), ("lm_head", c_void_p), ("rope_cos", c_void_p),
+                ("rope_sin", c_void_p), ("rope_len", c_int), ("kv_pool", c_void_p),
+                ("num_blocks", c_int), ("block_size", c_int), ("resid", c_void_p),
+                ("x", c_void_p), ("x_stride", c_int64), ("qkv", c_void_p), ("attn", c_void_p),
+                ("act", c_void_p), ("part", c_void_p), ("part_rows", c_int64), ("h", c_void_p),
+                ("hv", c_void_p), ("v", c_void_p), ("ch", c_void_p), ("ctrl", c_void_p),
+                ("mp", c_void_p), ("x2", c_void_p), ("xs", c_void_p), ("dpart", c_void_p),
+                ("eids", c_void_p), ("offs", c_void_p), ("perm", c_void_p), ("inv", c_void_p),
+                ("xl", c_void_p), ("logits", c_void_p), ("logits_ld", c_int64),
+                ("lm_rows", c_int), ("attn_ws", c_void_p), ("attn_ws_bytes", c_size_t),
+                ("fused_rope", c_int), ("tp_world", c_int), ("tp_rank", c_int),
+                ("tp_fused", c_int), ("ar_data", c_void_p * 8), ("ar_scratch", c_void_p * 8),
+                ("ar_flags", c_void_p * 8)]
 
 
 class MukStepBatch(ctypes.Structure):
@@ -220,6 +250,18 @@ def call_counted(name: str, launches: int, *args) -> None:
     if rc != MUK_OK:
         raise MukError(name, rc, last_error())
     launch_count += launches
+
+
+def call_native(name: str, *args) -> None:
+    """Call a native step executor whose last argument before the stream is
+    an ``int*`` receiving its kernel launch count."""
+    global launch_count
+    n = ctypes.c_int(0)
+    fn = getattr(load(), name)
+    rc = fn(*args[:-1], ctypes.byref(n), args[-1])
+    launch_count += n.value
+    if rc != MUK_OK:
+        raise MukError(name, rc, last_error())
 
 
 def call_status(name: str, *args) -> None:

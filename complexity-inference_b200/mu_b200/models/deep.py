@@ -20,6 +20,7 @@ K-major ([E·2I, H] interleaved gate/up, [E·H, I]).
 
 from __future__ import annotations
 
+import ctypes
 import os
 from typing import Dict, List, Optional
 
@@ -28,7 +29,8 @@ import torch
 from .. import _lib
 from .. import kernels as K
 from ..core.config import ModelConfig, MuConfig
-from .base import PAD_MULT, MuModelBase, choose_split, interleave_gate_up, pad_cols, pad_to
+from .base import (FUSED_TP_MAX_ROWS, PAD_MULT, MuModelBase, choose_split, interleave_gate_up,
+                   pad_cols, pad_to)
 from .registry import register_model
 from .weights import expert_intermediate, is_routed
 
@@ -52,6 +54,11 @@ class DeepForCausalLM(MuModelBase):
         # peer-memory collectives: "gather" (each GPU's expert rows in bf16,
         # muk_ep_gather_bf16) or "allreduce" (full-width f32 all-reduce)
         self.ep_combine = os.environ.get("MU_EP_COMBINE", "gather")
+        # whole step issued by libmuk's native executor (muk_deep_forward);
+        # MU_NATIVE_STEP=0 (or native = False) issues it kernel by kernel
+        self.native = os.environ.get("MU_NATIVE_STEP", "1") != "0"
+        self._native_key = None
+        self._native_model = None
 
     def act_width(self) -> int:
         return self.i_pad
@@ -145,7 +152,95 @@ class DeepForCausalLM(MuModelBase):
         cap = (3 * self.config.hidden_size) // max(N, 1)
         return int(_lib.load().muk_gemm_plan_split(T, N, K, _lib.MUK_EPI_F32, max(1, min(16, cap))))
 
+    def _native_ok(self) -> bool:
+        if not self.native:
+            return False
+        if self.tp_group is None:
+            return True
+        return self.comm is not None and self.ws.shared_part  # peer all-reduce only
+
+    def _native(self, cache) -> "_lib.MukDeepModel":
+        """The executor's model struct (rebuilt when a buffer moves)."""
+        ws, cfg, cl = self.ws, self.config, self.clamp
+        key = (id(ws), cache.block_pool.data_ptr(), self.rope_cos.data_ptr(), id(self.comm),
+               self.fused_rope(), self._tp_fused, self.vocab_slice(), self.expert_lo,
+               self.ep_combine)
+        if key == self._native_key:
+            return self._native_model
+        H = cfg.hidden_size
+
+        def p(t):
+            return 0 if t is None else t.data_ptr()
+
+        layers = (_lib.MukDeepLayer * len(self.layers))()
+        for i, L in enumerate(self.layers):
+            # the executor assumes the fused layouts from_state_dict builds
+            assert L["wcat"].stride(0) == 2 * H and L["wci"].stride(0) == 2 * H
+            layers[i] = _lib.MukDeepLayer(
+                p(L["w_in"]), p(L["wcat"]), p(L["wo"]), p(L["w_post"]), p(L["wci"]),
+                p(L["bci"]), p(L["wco"]), p(L["bco"]), p(L["wmu"]), p(L["mu"]), p(L.get("qn")),
+                p(L.get("kn")), p(L["wgu"]), p(L["wd"]), p(L.get("router")))
+        m = _lib.MukDeepModel()
+        m.num_layers, m.hidden = len(self.layers), H
+        m.num_q_heads, m.num_kv_heads = cfg.num_attention_heads, cfg.num_key_value_heads
+        m.head_dim, m.inter_pad, m.vocab = cfg.head_dim, self.i_pad, cfg.vocab_size
+        m.ctrl_hidden = self.layers[0]["wci"].shape[0]
+        m.num_experts = cfg.num_experts if self.routed else 0
+        m.local_experts, m.expert_lo = self.local_experts, self.expert_lo
+        m.ep_gather = int(self.ep_combine == "gather")
+        m.eps, m.dt = cfg.rms_norm_eps, cfg.dynamics_dt
+        m.clamp, m.mu, m.clamp_min, m.clamp_max = int(cl.enabled), cl.mu, cl.clamp_min, cl.clamp_max
+        m.layers = layers
+        m.embed, m.final_norm = self.embed.data_ptr(), self.norm_w.data_ptr()
+        vs = self.vocab_slice()
+        m.lm_head = self.lm_w.data_ptr() + (0 if vs is None else vs[0] * self.lm_w.stride(0) * 2)
+        m.rope_cos, m.rope_sin, m.rope_len = (self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+                                              self.rope_cos.shape[0])
+        m.kv_pool, m.num_blocks, m.block_size = (cache.block_pool.data_ptr(), cache.max_num_blocks,
+                                                 cache.block_size)
+        m.resid, m.x, m.x_stride = ws.resid.data_ptr(), ws.x.data_ptr(), ws.x.stride(0)
+        m.qkv, m.attn, m.act = ws.qkv.data_ptr(), ws.attn.data_ptr(), ws.act.data_ptr()
+        m.part, m.part_rows = ws.part.data_ptr(), ws.part_rows
+        m.h, m.hv, m.v, m.ch = ws.h.data_ptr(), ws.hv.data_ptr(), ws.v.data_ptr(), ws.ch.data_ptr()
+        m.ctrl, m.mp, m.x2, m.xs = (ws.ctrl.data_ptr(), ws.mp.data_ptr(), ws.x2.data_ptr(),
+                                    ws.xs.data_ptr())
+        m.dpart, m.eids, m.offs = ws.dpart.data_ptr(), ws.eids.data_ptr(), ws.offs.data_ptr()
+        m.perm, m.inv = ws.perm.data_ptr(), ws.inv.data_ptr()
+        m.xl, m.logits = ws.xl.data_ptr(), ws.logits.data_ptr()
+        m.lm_rows, m.logits_ld = cfg.vocab_size, ws.logits.stride(0)
+        if vs is not None:  # this rank's vocabulary columns only
+            c0, n = vs
+            m.lm_rows = n
+            m.logits = ws.logits.data_ptr() + 4 * c0
+        m.attn_ws, m.attn_ws_bytes = ws.attn_ws.data_ptr(), ws.attn_ws.numel() * 4
+        m.fused_rope = int(self.fused_rope())
+        m.tp_world, m.tp_rank = 1, 0
+        m.tp_fused = FUSED_TP_MAX_ROWS if self._tp_fused else 0
+        if self.comm is not None:
+            c = self.comm
+            m.tp_world, m.tp_rank = c.world, c.rank
+            for r in range(c.world):
+                m.ar_data[r], m.ar_scratch[r], m.ar_flags[r] = (c.ptrs[r], c.scratch_ptrs[r],
+                                                                 c.flag_ptrs[r])
+        m._keep = layers  # the layer array must outlive the struct
+        self._native_key, self._native_model = key, m
+        return m
+
+    def _forward_native(self, batch, cache) -> torch.Tensor:
+        m = self._native(cache)
+        b = _lib.MukStepBatch(batch.num_tokens, batch.num_seqs, batch.num_decode,
+                              batch.max_q_len, batch.decode_len_bound,
+                              batch.input_ids.data_ptr(), batch.positions.data_ptr(),
+                              batch.slot_mapping.data_ptr(), batch.seq_lens.data_ptr(),
+                              batch.prefill_cu.data_ptr(), batch.last_token_idx.data_ptr(),
+                              batch.block_tables.data_ptr(), batch.block_tables.stride(0))
+        _lib.call_native("muk_deep_forward", ctypes.byref(m), ctypes.byref(b),
+                         torch.cuda.current_stream().cuda_stream)
+        return self.ws.logits[:batch.num_seqs]
+
     def forward_step(self, batch, cache) -> torch.Tensor:
+        if self._native_ok():
+            return self._forward_native(batch, cache)
         cfg, ws, cl = self.config, self.ws, self.clamp
         T, H, eps = batch.num_tokens, cfg.hidden_size, cfg.rms_norm_eps
         E, V = cfg.num_experts, cfg.vocab_size

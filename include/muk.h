@@ -633,6 +633,108 @@ typedef struct {
  * (mu_inference/models/llama.py:184-245) for a flat step. */
 int muk_llama_forward(const MukLlamaModel* model, const MukStepBatch* batch, void* stream);
 
+/* ---- Native step executor (DeepForCausalLM) -------------------------------- */
+
+/* One Deep decoder layer: f32 norm / bias / mu vectors, bf16 K-major
+ * matrices.  wcat is [q|k|v ; mu_to_q|k|v] fused along K ([(Hq+2Hkv)D][2H]);
+ * wci is [ctrl_hidden][2H] (the [h | v] controller input), wco [3H][ctrl],
+ * wmu [H][H].  Routed: wgu [E_local * 2 inter_pad][H] (per expert, gate/up
+ * interleaved in 64-row groups), wd [E_local * H][inter_pad], router
+ * [E][H]; dense: wgu [2 inter_pad][H], wd [H][inter_pad], router NULL.
+ * q_norm / k_norm (QK-norm weights) may be NULL. */
+typedef struct {
+  const float* in_norm;
+  const void* wcat;
+  const void* wo;
+  const float* post_norm;
+  const void* wci;
+  const float* bci;
+  const void* wco;
+  const float* bco;
+  const void* wmu;
+  const float* mu_param;
+  const float* q_norm;
+  const float* k_norm;
+  const void* wgu;
+  const void* wd;
+  const void* router;
+} MukDeepLayer;
+
+/* Model, workspace and (optional) tensor / expert-parallel peer buffers; all
+ * device pointers, every buffer row-contiguous.  x is [rows][x_stride] bf16
+ * holding [x | mu_prev] (x_stride >= 2 hidden); h, v, mp are [rows][hidden]
+ * f32, hv [rows][2 hidden] bf16 ([h | v]), ch [rows][ctrl_hidden] bf16, ctrl
+ * [rows][3 hidden] f32 (also the controller input's split-K partials), x2 /
+ * xs [rows][hidden] bf16, act [rows][inter_pad] bf16; eids / perm / inv
+ * [rows] int32 and offs [num_experts + 1] int32 (routing).  dpart holds the
+ * routed MLP's f32 output (the start of part under peer-memory TP). */
+typedef struct {
+  int num_layers, hidden, num_q_heads, num_kv_heads, head_dim, inter_pad, vocab;
+  int ctrl_hidden;
+  int num_experts;   /* routed experts over all ranks (0: dense MLP) */
+  int local_experts; /* experts held here: [expert_lo, expert_lo + local_experts) */
+  int expert_lo;
+  int ep_gather;     /* expert parallel: 1 combine by the bf16 row gather, 0 by the f32 all-reduce */
+  float eps, dt;
+  int clamp;
+  float mu, clamp_min, clamp_max;
+  const MukDeepLayer* layers;
+  const void* embed;
+  const float* final_norm;
+  const void* lm_head;
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_len;
+  void* kv_pool;
+  int num_blocks, block_size;
+  float* resid;
+  void* x;
+  int64_t x_stride;
+  void* qkv;
+  void* attn;
+  void* act;
+  float* part;
+  int64_t part_rows;
+  float* h;
+  void* hv;
+  float* v;
+  void* ch;
+  float* ctrl;
+  float* mp;
+  void* x2;
+  void* xs;
+  float* dpart;
+  int32_t* eids;
+  int32_t* offs;
+  int32_t* perm;
+  int32_t* inv;
+  void* xl;
+  float* logits;
+  int64_t logits_ld;
+  int lm_rows;
+  void* attn_ws;
+  size_t attn_ws_bytes;
+  int fused_rope;
+  int tp_world, tp_rank;
+  int tp_fused;
+  float* ar_data[8];
+  float* ar_scratch[8];
+  uint32_t* ar_flags[8];
+} MukDeepModel;
+
+/* The whole forward step of a DeepForCausalLM (embedding; per layer the
+ * fused q|k|v|mu projection with QK-norm + RoPE + KV append, attention, the
+ * clamped O projection, the INL controller, mu projection and dynamics with
+ * the post-attention norm and mu-guided routing, the token-routed or dense
+ * MLP and the clamped residual + next norm; the tensor / expert-parallel
+ * exchanges when tp_world > 1; final norm of each sequence's last token and
+ * LM head -> logits) issued in one call: the same kernels with the same
+ * arguments as the per-kernel step.  *launches (may be NULL) receives the
+ * number of kernels launched.  Replaces DeepForCausalLM.forward
+ * (mu_inference/models/deep.py:232-333) for a flat step. */
+int muk_deep_forward(const MukDeepModel* model, const MukStepBatch* batch, int* launches,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

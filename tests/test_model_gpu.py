@@ -309,15 +309,17 @@ def test_device_error_fails_the_step_not_the_engine(cuda):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("name", ["llama_tiny", "deep_tiny"])
 @pytest.mark.parametrize("graphs", [False, True])
-def test_native_executor_matches_python_step(cuda, graphs):
-    """muk_llama_forward launches the same kernels with the same arguments as
-    the per-kernel Python step: logits must be bit-identical."""
+def test_native_executor_matches_python_step(cuda, name, graphs):
+    """The native executors (muk_llama_forward, muk_deep_forward) launch the
+    same kernels with the same arguments as the per-kernel Python step:
+    logits must be bit-identical."""
     from mu_b200.serving.worker import WorkerRequest
 
     outs = []
     for native in (False, True):
-        w, shape, d, prompts, _ = _worker("llama_tiny", cuda, graphs)
+        w, shape, d, prompts, _ = _worker(name, cuda, graphs)
         w.model.native = native
         toks = d["tokens"]
         R = toks.shape[0]

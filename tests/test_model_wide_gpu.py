@@ -49,7 +49,9 @@ PROMPT_LENS = {
 }
 
 
-def _build(name):
+def _worker(name):
+    """MuWorker with a 2-layer slice of the workload's model (the benchmark's
+    seeded bf16 weights); returns (workload, worker, cpu state dict, config)."""
     import bench
     from mu_b200.core.config import CacheConfig, EngineConfig, MuConfig, SchedulerConfig
     from mu_b200.models.weights import random_state_dict
@@ -69,6 +71,16 @@ def _build(name):
     w = MuWorker(ec, "cuda")
     w.load_state_dict(wl["arch"], cfg, sd)
     w.use_graphs = False  # expert ids are read from eager launches
+    return wl, w, sd, cfg
+
+
+def _build(name):
+    wl, w, sd, cfg = _worker(name)
+    if wl["arch"] == "deep":
+        # expert ids are traced through the per-kernel Python step's INL call;
+        # test_wide_native_matches_python ties the native executor to that step
+        w.model.native = False
+    lens = PROMPT_LENS[name]
     shape = O.ModelShape(arch=wl["arch"], hidden=wl["hidden"], layers=2, heads=wl["heads"],
                          kv_heads=wl["kv"], head_dim=wl["head_dim"], vocab=wl["vocab"],
                          eps=wl["eps"], theta=wl["theta"],
@@ -168,3 +180,51 @@ def test_wide_model_teacher_forced(cuda, name, monkeypatch):
     print(f"{name}: worst logit max-abs {worst:.4g} (bf16 floor {float(floor.max()):.4g}, worst "
           f"GPU/floor ratio {ratio:.3g}) over {R} requests x {N_DECODE} steps; "
           f"{flips} near-tie argmax flips")
+
+
+@pytest.mark.parametrize("name", ["c2", "c5"])
+def test_wide_native_matches_python(cuda, name):
+    """At the Deep workloads' widths the native executor (muk_deep_forward)
+    launches the same kernels with the same arguments as the per-kernel
+    Python step that the oracle test above pins: the logits of a prefill
+    step and of decode steps, and the last layer's expert ids, must be
+    bit-identical."""
+    from mu_b200.serving.worker import WorkerRequest
+
+    prompts = None
+    runs = []
+    for native in (False, True):
+        wl, w, sd, _ = _worker(name)
+        del sd
+        w.model.native = native
+        if prompts is None:
+            rng = np.random.default_rng(100 + wl["seed"])
+            prompts = [rng.integers(0, wl["vocab"], n).tolist() for n in PROMPT_LENS[name]]
+        R = len(prompts)
+        for r in range(R):
+            assert w.allocate_request(f"r{r}")
+        got, eids = [], []
+        toks = None
+        for i in range(4):
+            if i == 0:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([prompts[r]]), is_prefill=True)
+                        for r in range(R)]
+                T = sum(len(p) for p in prompts)
+            else:
+                reqs = [WorkerRequest(f"r{r}", torch.tensor([[int(toks[r])]]), is_prefill=False)
+                        for r in range(R)]
+                T = R
+            outs = w.execute(reqs)
+            assert all(o.error is None for o in outs)
+            lg = torch.cat([o.logits.reshape(1, -1) for o in outs]).float().cpu()
+            got.append(lg)
+            eids.append(w.model.ws.eids[:T].cpu().clone())
+            toks = lg.argmax(-1).tolist()
+        runs.append((got, eids))
+        del w
+        torch.cuda.empty_cache()
+    (pl, pe), (nl, ne) = runs
+    for i, (a, b) in enumerate(zip(pl, nl)):
+        assert torch.equal(a, b), (name, i, float((a - b).abs().max()))
+    for i, (a, b) in enumerate(zip(pe, ne)):
+        assert torch.equal(a, b), (name, i)

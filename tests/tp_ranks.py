@@ -154,7 +154,9 @@ def main():
     # ("gather", the default) or the f32 all-reduce ("allreduce").
     # Llama steps under peer memory: "rs-norm" (default: reduce-scatter, residual
     # + norm on the owned rows, all-gather of x) from the native executor or the
-    # Python step, or "allreduce" (all-reduce, then the replicated residual/norm)
+    # Python step, or "allreduce" (all-reduce, then the replicated residual/norm).
+    # Deep steps under peer memory run the native executor ("python": the
+    # per-kernel step)
     for name, graphs, ep, comm, combine, form in (
             ("llama_tiny", False, False, "nccl", "-", "-"),
             ("llama_tiny", True, False, "peer", "-", "rs-norm"),
@@ -165,12 +167,13 @@ def main():
             ("deep_tiny", False, False, "nccl", "-", "-"),
             ("deep_tiny", True, False, "peer", "-", "-"),
             ("deep_tiny", True, True, "peer-split", "gather", "-"),
-            ("deep_tiny", False, True, "peer", "allreduce", "-")):
+            ("deep_tiny", False, True, "peer", "allreduce", "-"),
+            ("deep_tiny", False, True, "peer", "gather", "python")):
         os.environ["MU_TP_COMM"] = "nccl" if comm == "nccl" else "peer"
         os.environ["MU_TP_FUSED"] = "0" if comm == "peer-split" else "1"
         os.environ["MU_EP_COMBINE"] = "allreduce" if combine == "allreduce" else "gather"
         os.environ["MU_TP_NORM"] = "0" if form == "allreduce" else "1"
-        os.environ["MU_NATIVE_STEP"] = "0" if form == "rs-norm-python" else "1"
+        os.environ["MU_NATIVE_STEP"] = "0" if form in ("rs-norm-python", "python") else "1"
         shape, cfg, sd, d, prompts = load_tiny(name)
         ec = EngineConfig(model=cfg, mu=MuConfig(enabled=True), tensor_parallel_size=world,
                           expert_parallel=ep,
