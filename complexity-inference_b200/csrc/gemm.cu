@@ -1563,6 +1563,24 @@ static int pick_bn(long m_tiles, int N, int splits, int sms) {
   return wave_eff(t128, sms) > wave_eff(t256, sms) + 0.15 ? 128 : 256;
 }
 
+// Tile width of a grouped SwiGLU launch.  BN = 256 halves the A traffic per
+// flop, but when the (expert, row-tile) x 256-column tiles cannot cover the
+// SMs (few rows per expert: decode-sized steps) the launch streams the
+// expert weights through a fraction of the GPU; 128-wide tiles double the
+// SMs that stream.  The row tiles are estimated for balanced routing
+// (max_rows / E rows per expert).  MUK_GROUPED_BN=128 / 256 forces a width.
+static int grouped_swiglu_bn(int max_rows, int N, int num_experts, int sms) {
+  static int forced = [] {
+    const char* e = getenv("MUK_GROUPED_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (N % 256 != 0 || forced == 128) return 128;
+  if (forced == 256) return 256;
+  const long per_expert = ((long)max_rows + num_experts - 1) / num_experts;
+  const long m_est = (long)num_experts * ((per_expert + kBM - 1) / kBM);
+  return m_est * (N / 256) < sms ? 128 : 256;
+}
+
 template <int EPI, int PBN>
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, const TileArgs& a,
                        int sms, cudaStream_t stream) {
@@ -1693,7 +1711,7 @@ static int run_gemm(bool grouped, const void* A, int64_t lda, const void* B, int
     bn = best.bn;
     sk = best.sk;
   } else {
-    bn = epilogue == MUK_EPI_SWIGLU ? (N % 256 == 0 ? 256 : 128)
+    bn = epilogue == MUK_EPI_SWIGLU ? grouped_swiglu_bn(M, N, num_experts, sms)
                                     : pick_bn(m_tiles, N, split_k, sms);
   }
   CUtensorMap ma, mb;
