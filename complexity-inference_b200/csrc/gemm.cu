@@ -404,6 +404,90 @@ __device__ __forceinline__ void sk_sum_chunk(const SkFix& f, int chunk, uint32_t
   for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(acc[j]);
 }
 
+// Stream-K fix-up on the CTA's last unit: the TMA ring is idle then, and each
+// epilogue warp stages the other shares' partials of its 32 rows in a
+// private part of it (two chunk buffers x up to kSkPrefetchSrc shares x
+// 32 rows x 32 f32), so the copies of two chunks are in flight at once
+// instead of one warp-load group per share and chunk.
+constexpr int kSkPrefetchSrc = 4;
+constexpr int kSkWarpScratch = 2 * kSkPrefetchSrc * 4096;
+
+// cp.async copies of chunk `chunk` of every other share's partial (this
+// lane's row) into buf, laid out [share k][float4 j][lane]; one commit group.
+__device__ __forceinline__ void sk_prefetch_chunk(const SkFix& f, int chunk, uint32_t buf,
+                                                  int lane) {
+  int k = 0;
+  for (int c = f.wf; c <= f.wl; ++c) {
+    if (c == f.self) continue;
+    const int which = sk_begin(*f.a, c) >= f.tile_begin ? 0 : 1;
+    const float4* p = sk_slot(c, which, f.rank, f.ranks) + (size_t)(chunk * 8) * kBM + f.row_local;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      cp_async_16(buf + (uint32_t)(((k * 8 + j) * 32 + lane) * 16), p + (size_t)j * kBM);
+    ++k;
+  }
+  cp_async_commit();
+}
+
+// Replaces this warp's accumulator rows in TMEM by the sum of all stream-K
+// shares of the tile, in the fixed share order (bit-identical whoever
+// finishes).  `scratch` (shared-memory address of kSkWarpScratch bytes, 0:
+// none) stages the other shares' partials; without it they are read chunk by
+// chunk.  The epilogue then reads the finished accumulator.  Warp-collective.
+template <int BN>
+__device__ __forceinline__ void sk_fix_tmem(const SkFix& f, uint32_t lane_addr, uint32_t scratch) {
+  constexpr int kChunks = BN / 32;
+  const int lane = threadIdx.x & 31;
+  const bool pre = scratch != 0 && f.wl - f.wf <= kSkPrefetchSrc;
+  constexpr uint32_t kHalf = kSkWarpScratch / 2;
+  if (pre) {
+    fence_proxy_async_smem();  // the ring was last written by TMA (async proxy)
+    sk_prefetch_chunk(f, 0, scratch, lane);
+    sk_prefetch_chunk(f, 1, scratch + kHalf, lane);
+  }
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(lane_addr + c * 32, v);
+    tmem_ld_wait();
+    if (pre) {
+      if (c + 1 < kChunks)
+        cp_async_wait<1>();
+      else
+        cp_async_wait<0>();
+      const uint32_t buf = scratch + (uint32_t)(c & 1) * kHalf;
+      float acc[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+      int k = 0;
+      for (int s = f.wf; s <= f.wl; ++s) {
+        if (s == f.self) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(v[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = ld_shared_f4(buf + (uint32_t)(((k * 8 + j) * 32 + lane) * 16));
+            acc[4 * j] += x.x;
+            acc[4 * j + 1] += x.y;
+            acc[4 * j + 2] += x.z;
+            acc[4 * j + 3] += x.w;
+          }
+          ++k;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(acc[j]);
+    } else {
+      sk_sum_chunk(f, c, v);
+    }
+    tmem_st_32x32b_x32(lane_addr + c * 32, v);
+    // this lane's reads of the buffer are done (their sums were stored)
+    if (pre && c + 2 < kChunks) sk_prefetch_chunk(f, c + 2, scratch + (uint32_t)(c & 1) * kHalf, lane);
+  }
+  tmem_st_wait();
+}
+
 struct Tile {
   int row0, row_end, brow0, n0, split, kt0, nk;
   bool valid;
@@ -510,13 +594,11 @@ __device__ __forceinline__ void store_chunk(void* C, int64_t ldc, int64_t split_
   }
 }
 
-// One 32-column chunk of this lane's accumulator row (+ the other stream-K
-// shares when `fix`).  Warp-collective: every lane must call it.
-__device__ __forceinline__ void acc_chunk(uint32_t lane_addr, int c, uint32_t (&v)[32],
-                                          const SkFix* fix) {
+// One 32-column chunk of this lane's accumulator row.  Warp-collective:
+// every lane must call it.
+__device__ __forceinline__ void acc_chunk(uint32_t lane_addr, int c, uint32_t (&v)[32]) {
   tmem_ld_32x32b_x32(lane_addr + c * 32, v);
   tmem_ld_wait();
-  if (fix) sk_sum_chunk(*fix, c, v);
 }
 
 // MUK_EPI_ROPE_KV: the tile's columns are whole heads of the q|k|v
@@ -530,7 +612,7 @@ __device__ __forceinline__ void acc_chunk(uint32_t lane_addr, int c, uint32_t (&
 // stores are per lane.
 template <int BN>
 __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int row, int row_end,
-                                              int n0, uint32_t lane_addr, const SkFix* fix) {
+                                              int n0, uint32_t lane_addr) {
   const RopeArgs& r = a.rope;
   const int D = r.head_dim, half = D >> 1, cph = D >> 5;
   const bool valid = row < row_end;
@@ -568,7 +650,7 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
     if (!is_q && !is_k) {  // v: straight to the cache
       for (int c = 0; c < cph; ++c) {
         uint32_t v[32];
-        acc_chunk(lane_addr, c0 + c, v, fix);
+        acc_chunk(lane_addr, c0 + c, v);
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
@@ -582,7 +664,7 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
       float ss = 0.f;
       for (int c = 0; c < cph; ++c) {
         uint32_t v[32];
-        acc_chunk(lane_addr, c0 + c, v, fix);
+        acc_chunk(lane_addr, c0 + c, v);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float x = __uint_as_float(v[j]) * rs;
@@ -594,8 +676,8 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
     const int p = pos < 0 ? 0 : pos;
     for (int c = 0; c < cph / 2; ++c) {  // chunk c of the first half with its partner
       uint32_t lo[32], hi[32];
-      acc_chunk(lane_addr, c0 + c, lo, fix);
-      acc_chunk(lane_addr, c0 + c + cph / 2, hi, fix);
+      acc_chunk(lane_addr, c0 + c, lo);
+      acc_chunk(lane_addr, c0 + c + cph / 2, hi);
       const int i0 = c * 32;
       const float4* cs = reinterpret_cast<const float4*>(r.cos + (int64_t)p * half + i0);
       const float4* sn = reinterpret_cast<const float4*>(r.sin + (int64_t)p * half + i0);
@@ -625,14 +707,14 @@ __device__ __forceinline__ void epilogue_rope(void* C, const TileArgs& a, int ro
 }
 
 // Epilogue of one accumulator (this warp's 32 rows): TMEM -> registers ->
-// fused epilogue -> global.  With `fix`, each chunk is first replaced by the
-// sum of all stream-K shares of the tile.
+// fused epilogue -> global.  A stream-K tile's accumulator has been replaced
+// by the sum of its shares first (sk_fix_tmem).
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int row, int row_end,
                                               int n0, int64_t split_off, uint32_t lane_addr,
-                                              const SkFix* fix, float* stage, bool last_unit) {
+                                              float* stage, bool last_unit) {
   if (EPI == MUK_EPI_ROPE_KV) {
-    epilogue_rope<BN>(C, args, row, row_end, n0, lane_addr, fix);
+    epilogue_rope<BN>(C, args, row, row_end, n0, lane_addr);
   } else if (EPI == kEpiResidNorm) {
     // resid += acc; x~ = bf16(w * resid); one partial sum of resid^2 per 128
     // columns.  Staged: lane holds 4 columns of rows rb + 4i (i = 0..7).
@@ -647,7 +729,6 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
       uint32_t v[32];
       tmem_ld_32x32b_x32(lane_addr + c * 32, v);
       tmem_ld_wait();
-      if (fix) sk_sum_chunk(*fix, c, v);
       float f[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
@@ -709,7 +790,6 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
       uint32_t v[32];
       tmem_ld_32x32b_x32(lane_addr + c * 32, v);
       tmem_ld_wait();
-      if (fix) sk_sum_chunk(*fix, c, v);
       float f[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) f[j] = mu_clamp(__uint_as_float(v[j]), du.cp);
@@ -738,10 +818,6 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
         tmem_ld_32x32b_x32(lane_addr + grp * 128 + c * 32, gv);
         tmem_ld_32x32b_x32(lane_addr + grp * 128 + 64 + c * 32, uv);
         tmem_ld_wait();
-        if (fix) {
-          sk_sum_chunk(*fix, grp * 4 + c, gv);
-          sk_sum_chunk(*fix, grp * 4 + 2 + c, uv);
-        }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           gv[j] = __float_as_uint(silu(__uint_as_float(gv[j]) * rs) * (__uint_as_float(uv[j]) * rs));
@@ -755,7 +831,6 @@ __device__ __forceinline__ void epilogue_rows(void* C, const TileArgs& args, int
       uint32_t v[32];
       tmem_ld_32x32b_x32(lane_addr + c * 32, v);
       tmem_ld_wait();
-      if (fix) sk_sum_chunk(*fix, c, v);
       if (EPI == kEpiF32Push)
         store_push(args, row, row_end, n0 + c * 32, v, stage);
       else
@@ -987,12 +1062,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else if (u.part >= 0) {
         const SkFix f = make_fix(args, u, w, 0, 1, quarter * 32 + lane);
-        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
-          epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, &f, stage,
+        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr)) {
+          sk_fix_tmem<BN>(f, lane_addr,
+                          last_unit ? base + (uint32_t)(quarter * kSkWarpScratch) : 0u);
+          epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, stage,
                                  last_unit);
+        }
       } else {
-        epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, nullptr,
-                               stage, last_unit);
+        epilogue_rows<EPI, BN>(C, args, row, tl.row_end, tl.n0, split_off, lane_addr, stage,
+                               last_unit);
       }
       tc_fence_before();
       __syncwarp();
@@ -1215,11 +1293,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else if (u.part >= 0) {
         const SkFix f = make_fix(args, u, pair, (int)rank, 2, quarter * 32 + lane);
-        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr))
-          epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, &f, stage,
+        if (sk_arrive<BN>(f, u, quarter, lane, lane_addr)) {
+          sk_fix_tmem<BN>(f, lane_addr,
+                          last_unit ? base + (uint32_t)(quarter * kSkWarpScratch) : 0u);
+          epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, stage,
                                  last_unit);
+        }
       } else {
-        epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, nullptr, stage,
+        epilogue_rows<EPI, BN>(C, args, row, args.M, n0, split_off, lane_addr, stage,
                                last_unit);
       }
       tc_fence_before();

@@ -685,13 +685,30 @@ def test_decode_workspace_covers_smaller_batches(cuda):
 
 
 # q|k|v projection with RoPE (+QK-norm) and the KV append in the GEMM epilogue:
-# 1-SM and CTA-pair kernels, head_dim 64 and 128, padding slots (-1)
-@pytest.mark.parametrize("M,Hq,Hkv,D,qk_norm", [(37, 4, 2, 64, True), (300, 32, 8, 128, False),
-                                                (600, 32, 8, 128, True), (130, 16, 8, 128, False)])
-def test_gemm_qkv_rope(cuda, M, Hq, Hkv, D, qk_norm):
+# 1-SM and CTA-pair kernels, head_dim 64 and 128, padding slots (-1); the
+# last two cases run stream-K schedules (1-SM and pair), whose shares are
+# summed into the accumulator before the RoPE epilogue reads it
+@pytest.mark.parametrize("M,Hq,Hkv,D,qk_norm,sk", [(37, 4, 2, 64, True, 0),
+                                                   (300, 32, 8, 128, False, 0),
+                                                   (600, 32, 8, 128, True, 0),
+                                                   (130, 16, 8, 128, False, 0),
+                                                   (64, 16, 8, 128, True, 1),
+                                                   (200, 32, 8, 128, False, 1)])
+def test_gemm_qkv_rope(cuda, M, Hq, Hkv, D, qk_norm, sk):
     k = _kern()
-    K_, NB, bs = 512, 64, 16
+    prev = k.gemm_set_stream_k(sk)
+    try:
+        _check_qkv_rope(k, cuda, M, Hq, Hkv, D, qk_norm, sk)
+    finally:
+        k.gemm_set_stream_k(prev)
+
+
+def _check_qkv_rope(k, cuda, M, Hq, Hkv, D, qk_norm, sk):
+    K_, NB, bs = (4096 if sk else 512), 64, 16  # stream-K pays over a long K
     N = (Hq + 2 * Hkv) * D
+    if sk:
+        plan = k.gemm_plan_info(M, N, K_, 4)  # MUK_EPI_ROPE_KV
+        assert plan["stream_k"] == 1 and plan["sk_tiles"] > 0, plan
     g = torch.Generator(device="cuda").manual_seed(M + D)
     A = torch.randn(M, K_, device=cuda, generator=g).bfloat16()
     W = (torch.randn(N, K_, device=cuda, generator=g) * 0.05).bfloat16()
